@@ -1,0 +1,344 @@
+#!/usr/bin/env python
+"""Benchmark of the Gemma-3-1B Q4_0 forward pass (BASELINE.json's metric).
+
+A step is one greedy decode token of BASELINE config 1's model (26 layers,
+Q4_0, seed-0 random init, batch 1 per GPU after a 32-token prefill), through
+the C ABI.  `value` is decode tokens/s over all ranks with the inputs resident
+(steps enqueued back to back); `e2e` is the same through the public step API
+with each step's 16-byte record read back to the host before the next;
+`prefill_tokens_per_s` times the 32-token prefill; `roofline` times the
+dominant kernel, the 262144 x 1152 Q4_0 head matvec, alone.
+
+N > 1 (torchrun): independent sequences, one per GPU (a 1B model has no
+tensor-parallel split), with a final NCCL gather of each rank's last logits;
+weak scaling.  `--impl reference` times the CPU restatement of the
+reference's arithmetic (the WGSL path needs a WebGPU device, unavailable here).
+"""
+import argparse
+import ctypes as C
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Gemma-3-1B q4_0 decode tok/s, prefill tok/s; q4 matvec HBM GB/s vs peak"
+PROMPT = 32
+HEAD_N, HEAD_K = 262144, 1152
+LAUNCHES_PER_DECODE_STEP = 1 + 26 * 5 + 1 + 2   # embed, 26 x (qkv, attention, o, gate/up, down), head, select x2
+DECODE_BYTES = 562_360_320 + 537_088           # Q4_0 weights + F32 gains a decode token reads
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, ordinal):
+        self.ordinal = ordinal
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.ordinal), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx.append(float(f[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        except OSError:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU legs
+
+def cpu_decode_sample(path, decode_tokens=2, prefill=4):
+    """The oracle's decode tokens/s on this host's cores: a `prefill`-token prompt,
+    then `decode_tokens` timed decode steps of the full model."""
+    import numpy as np
+    import oracle
+    from frizzle_b200 import synth
+    orc = oracle.OracleModel(path, context=256)
+    ids = np.random.default_rng(0).integers(2, synth.GEMMA3_1B.vocab, size=prefill).astype(np.uint32)
+    logits, _ = orc.step(0, ids, logits=True)
+    t0 = time.perf_counter()
+    for i in range(decode_tokens):
+        tok = int(np.argmax(logits))
+        logits, _ = orc.step(prefill + i, [tok], logits=True)
+    dt = time.perf_counter() - t0
+    threads = oracle.lib().oracle_threads()
+    orc.close()
+    return decode_tokens / dt, threads, f"{decode_tokens} greedy decode tokens of the 26-layer model after a " \
+                                        f"{prefill}-token prompt, oracle port on {threads} host threads"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from frizzle_b200 import synth
+    path = synth.model_path(synth.GEMMA3_1B, 0)
+    steps, warmup = max(1, args.steps), max(0, args.warmup)
+    # Bounded: the whole arm is a handful of CPU decode tokens.
+    decode = min(steps, 3)
+    value, threads, sample = cpu_decode_sample(path, decode_tokens=decode)
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
+            "warmup": warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init Q4_0 weights, seeded ids)",
+            "config": config(args.gpus), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "the reference's WGSL forward pass needs a WebGPU device (Dawn), unavailable on this box; "
+                    "this is the oracle's C restatement of its arithmetic"}
+    print(json.dumps(line))
+    return 0
+
+
+def config(n):
+    return {"workload": "BASELINE config 1: Gemma-3-1B-shaped Q4_0 model (26 layers, hidden 1152, vocab 262144, "
+                        "seed 0), batch-1 greedy decode after a 32-token prefill, one sequence per GPU",
+            "batch_per_gpu": 1, "prompt_tokens": PROMPT,
+            "l2": "inputs larger than L2: each decode step streams 562.9 MB of weights (L2 is 126 MB)",
+            "parallelism": f"independent sequences x{n}, final NCCL gather of logits" if n > 1 else "single GPU"}
+
+
+# ------------------------------------------------------------------ GPU leg
+
+def head_roofline(torch, lib, native, reps=20):
+    """The dominant kernel (262144 x 1152 Q4_0 head, M = 1) timed alone with CUDA
+    events on its stream; two weight copies alternate so L2 holds neither."""
+    import numpy as np
+    n, k = HEAD_N, HEAD_K
+    rng = np.random.default_rng(1)
+    mats = []
+    for c in range(2):
+        blocks = np.empty((n * k // 32, 18), dtype=np.uint8)
+        d = np.abs(rng.standard_normal(n * k // 32).astype(np.float32) * np.float32(0.005)).astype(np.float16)
+        blocks[:, :2] = d.view(np.uint8).reshape(-1, 2)
+        blocks[:, 2:] = rng.integers(0, 256, size=(n * k // 32, 16), dtype=np.uint8)
+        src = torch.from_numpy(blocks.reshape(-1)).cuda()
+        codes = torch.empty(lib.fz_q4_0_codes_bytes(n, k), dtype=torch.uint8, device="cuda")
+        scales = torch.empty(lib.fz_q4_0_scales_bytes(n, k), dtype=torch.uint8, device="cuda")
+        native.check(lib.fz_q4_0_repack(src.data_ptr(), n, k, codes.data_ptr(), scales.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream))
+        del src
+        mats.append((codes, scales))
+    x = torch.randn(1, k, device="cuda")
+    logits = torch.empty(1, n, device="cuda")
+    am = torch.zeros(1, dtype=torch.int64, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for i in range(4):
+        c, sc = mats[i % 2]
+        native.check(lib.fz_q4_0_head(c.data_ptr(), sc.data_ptr(), n, k, x.data_ptr(), 1, logits.data_ptr(),
+                                      am.data_ptr(), s))
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(reps):
+        c, sc = mats[i % 2]
+        native.check(lib.fz_q4_0_head(c.data_ptr(), sc.data_ptr(), n, k, x.data_ptr(), 1, logits.data_ptr(),
+                                      am.data_ptr(), s))
+    end.record()
+    torch.cuda.synchronize()
+    secs = start.elapsed_time(end) / 1000.0 / reps
+    bytes_ = n * k * 9 // 16 + 4 * k + 4 * n
+    del mats
+    torch.cuda.empty_cache()
+    return bytes_, secs
+
+
+def traffic_from_profile():
+    p = os.path.join(ROOT, "profiles", "head_matvec_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("dram_bytes_per_launch")
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from frizzle_b200 import _native, engine, synth
+    if rank == 0:
+        path = synth.model_path(synth.GEMMA3_1B, 0)
+    if dist:
+        dist.barrier()
+    path = synth.model_path(synth.GEMMA3_1B, 0)
+    dev = engine.Device(local)
+    model = engine.Model.from_file(dev, path)
+    batch = engine.Batch(model, 1, 4096)
+    lib = _native.load()
+    stream = torch.cuda.ExternalStream(dev.stream)
+    ids = np.random.default_rng([rank, PROMPT]).integers(2, synth.GEMMA3_1B.vocab, size=PROMPT).astype(np.uint32)
+
+    def prefill():
+        for pos in range(0, PROMPT, 16):
+            batch.step(pos, ids[pos:pos + 16], tokens=16, logits=pos + 16 == PROMPT)
+
+    # Prefill timing (two blocks of 16 tokens), after a warm-up prefill.
+    prefill()
+    batch.wait()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    with torch.cuda.stream(stream):
+        ev[0].record()
+    prefill()
+    with torch.cuda.stream(stream):
+        ev[1].record()
+    batch.wait()
+    prefill_s = ev[0].elapsed_time(ev[1]) / 1000.0
+
+    pos = PROMPT
+    for _ in range(args.warmup):
+        batch.step(pos, fed=True, tokens=1, logits=True)
+        batch.wait()
+        pos += 1
+    K = args.steps
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local)
+    with clocks:
+        with torch.cuda.stream(stream):
+            ev[2].record()
+        for i in range(K):
+            batch.step(pos + i, fed=True, tokens=1, logits=True)
+        with torch.cuda.stream(stream):
+            ev[3].record()
+        batch.wait()
+        torch.cuda.synchronize()
+        pos += K
+        # End to end: each step's record read back to the host before the next.
+        with torch.cuda.stream(stream):
+            ev[4].record()
+        for i in range(K):
+            batch.step(pos + i, fed=True, tokens=1, logits=True)
+            batch.wait()
+        with torch.cuda.stream(stream):
+            ev[5].record()
+        torch.cuda.synchronize()
+        pos += K
+    dec_s = ev[2].elapsed_time(ev[3]) / 1000.0
+    e2e_s = ev[4].elapsed_time(ev[5]) / 1000.0
+    if dist:
+        # The job's final exchange: rank 0 gathers every sequence's last logits.
+        last = torch.from_numpy(batch.logits(0)).cuda()
+        gathered = [torch.empty_like(last) for _ in range(world)] if rank == 0 else None
+        dist.gather(last, gathered, dst=0)
+        t = torch.tensor([dec_s, e2e_s, prefill_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dec_s, e2e_s, prefill_s = [float(v) for v in t.cpu()]
+    value = world * K / dec_s
+    e2e = world * K / e2e_s
+    line = None
+    if rank == 0:
+        head_bytes, head_secs = head_roofline(torch, lib, _native)
+        hbm, _, which = peaks()
+        achieved = head_bytes / head_secs / 1e9
+        line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K,
+                "warmup": args.warmup, "ms_per_step": 1000.0 * dec_s / K, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded random-init Q4_0 weights, seeded prompt ids)",
+                "config": config(world),
+                "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 64 + 8, "d2h_bytes_per_step": 16},
+                "gpu_launches": LAUNCHES_PER_DECODE_STEP * K,
+                "prefill_tokens_per_s": world * PROMPT / prefill_s,
+                "decode_step_hbm_gbs": DECODE_BYTES / (dec_s / K) / 1e9,
+                "decode_step_hbm_frac": DECODE_BYTES / (dec_s / K) / 1e9 / hbm,
+                "roofline": {"bound": "hbm", "kernel": "q4_0 head matvec 262144 x 1152, M=1",
+                             "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                             "peak_source": which, "algorithmic_bytes": head_bytes,
+                             "launch_us": head_secs * 1e6, "traffic": traffic_from_profile()},
+                "clocks": clocks.summary()}
+        if world == 1 and not args.no_cpu_baseline:
+            v, threads, sample = cpu_decode_sample(path)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
+    batch.free()
+    model.free()
+    dev.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line:
+        print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,987 @@
+// The engine behind the C ABI (include/frizzle_b200.h): device, load with
+// on-device repack, batches of sequences with their KV rings, and the step's
+// launch chain (embed, 26 x [QKV+RoPE, attention, O, gate/up+GELU+edits,
+// down], head+argmax, selection+draw) captured once per step shape into a
+// CUDA graph whose kernels read the position from device memory.
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "frizzle_b200.h"
+#include "gguf_index.h"
+#include "kernels.cuh"
+#include "q4_matvec.cuh"
+
+using fz::DeviceStep;
+using fz::GgufIndex;
+using fz::Q4Matrix;
+
+namespace {
+
+thread_local std::string g_error;
+thread_local uint64_t g_index_needed = 0;
+
+fz_status fail(fz_status s, const std::string& msg) {
+  g_error = msg;
+  return s;
+}
+
+#define FZ_CUDA(x)                                                                           \
+  do {                                                                                       \
+    cudaError_t e_ = (x);                                                                    \
+    if (e_ != cudaSuccess) return fail(FZ_ERR_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr uint32_t kMaxEdits = 4096;  // edit::kMaxEdits
+constexpr uint32_t kSplitKeys = 512;  // keys an attention CTA takes
+
+}  // namespace
+
+struct fz_device {
+  int ordinal = 0;
+  cudaStream_t stream = nullptr;
+  cudaStream_t capture = nullptr;
+};
+
+namespace {
+
+struct DevMatrix {
+  uint4* codes = nullptr;
+  uint2* scales = nullptr;
+  uint32_t n = 0, k = 0;
+  Q4Matrix view() const { return Q4Matrix{codes, scales, n, k}; }
+};
+
+struct Layer {
+  DevMatrix qkv, o, gate, up, down;
+  float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn_norm = nullptr,
+        *ffn_norm = nullptr, *post_ffw_norm = nullptr;
+  float* turns = nullptr;
+  bool global = false;
+  uint32_t window = 0;
+  float rope_base = 0.f;
+};
+
+struct Shape {
+  uint32_t layers = 0, hidden = 0, ffn = 0, heads = 0, kv_heads = 0, head_dim = 0, vocab = 0, window = 0,
+           pattern = 6, context = 0;
+  float eps = 0.f, rope_global = 0.f, rope_local = 0.f;
+};
+
+// Per-layer capture layout (floats): residual, query, attention addition,
+// neurons, feed-forward addition.
+struct CaptureLayout {
+  uint64_t residual, query, attn_added, neurons, mlp_added, per_layer;
+};
+CaptureLayout capture_layout(const Shape& s) {
+  CaptureLayout c{};
+  c.residual = 0;
+  c.query = s.hidden;
+  c.attn_added = c.query + (uint64_t)s.heads * s.head_dim;
+  c.neurons = c.attn_added + s.hidden;
+  c.mlp_added = c.neurons + s.ffn;
+  c.per_layer = c.mlp_added + s.hidden;
+  return c;
+}
+
+}  // namespace
+
+struct fz_model {
+  fz_device* dev = nullptr;
+  GgufIndex index;
+  Shape shape;
+  uint64_t file_bytes = 0;
+  uint8_t* staging = nullptr;
+  uint64_t staging_bytes = 0;
+  std::vector<std::pair<uint64_t, uint64_t>> written;  // merged ranges within the data section
+  std::vector<Layer> layers;
+  DevMatrix embd;
+  float* output_norm = nullptr;
+  bool finished = false;
+  uint64_t weight_bytes = 0;
+  std::vector<void*> allocations;
+
+  ~fz_model() {
+    for (void* p : allocations) cudaFree(p);
+    if (staging) cudaFree(staging);
+  }
+  template <typename T>
+  fz_status alloc(T** p, size_t bytes) {
+    void* v = nullptr;
+    cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
+    if (e != cudaSuccess) return fail(FZ_ERR_FIT, "device allocation of " + std::to_string(bytes) + " bytes: " +
+                                                     cudaGetErrorString(e));
+    allocations.push_back(v);
+    *p = static_cast<T*>(v);
+    weight_bytes += bytes;
+    return FZ_OK;
+  }
+};
+
+namespace {
+
+struct GraphKey {
+  uint32_t tokens, logits, capture, edits;
+  bool operator<(const GraphKey& o) const {
+    return std::tie(tokens, logits, capture, edits) < std::tie(o.tokens, o.logits, o.capture, o.edits);
+  }
+};
+
+}  // namespace
+
+struct fz_batch {
+  fz_model* model = nullptr;
+  uint32_t S = 0, context = 0, rollback = 0;
+  std::vector<uint16_t*> kc, vc;
+  std::vector<uint32_t> slots;
+  std::vector<uint64_t> seq_stride;
+  float *hidden_a = nullptr, *hidden_b = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr,
+        *y_attn = nullptr, *y_mlp = nullptr, *act = nullptr, *logits = nullptr;
+  float *partial_o = nullptr, *partial_ml = nullptr;
+  uint32_t* counters = nullptr;   // per layer: 1 QKV + M*kv attention counters
+  uint32_t counters_per_layer = 0;
+  uint32_t splits_max = 0;
+  unsigned long long* argmax = nullptr;
+  unsigned long long* tile_best = nullptr;
+  uint32_t *records = nullptr, *candidates = nullptr;
+  DeviceStep* dstep = nullptr;
+  uint32_t *dids = nullptr, *dseeds = nullptr;
+  uint32_t* edit_tables = nullptr;
+  uint32_t table_words = 0;
+  std::vector<bool> has_edits;
+  float* captures = nullptr;
+  uint64_t capture_floats = 0;
+  // Host staging, two slots (at most two steps in flight, kernels/order.h:70).
+  struct Slot {
+    DeviceStep* step = nullptr;
+    uint32_t* ids = nullptr;
+    uint32_t* seeds = nullptr;
+    uint32_t* records = nullptr;
+    cudaEvent_t copied = nullptr;  // the H2D copy of this slot has run
+    cudaEvent_t done = nullptr;    // the step's records are home
+    bool used = false;
+  } slot[2];
+  int next_slot = 0;
+  int last_slot = -1;
+  std::map<GraphKey, cudaGraphExec_t> graphs;
+  std::vector<void*> allocations;
+
+  ~fz_batch() {
+    for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    for (void* p : allocations) cudaFree(p);
+    for (auto& s : slot) {
+      if (s.step) cudaFreeHost(s.step);
+      if (s.ids) cudaFreeHost(s.ids);
+      if (s.seeds) cudaFreeHost(s.seeds);
+      if (s.records) cudaFreeHost(s.records);
+      if (s.copied) cudaEventDestroy(s.copied);
+      if (s.done) cudaEventDestroy(s.done);
+    }
+  }
+  template <typename T>
+  fz_status alloc(T** p, size_t bytes) {
+    void* v = nullptr;
+    cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+      return fail(FZ_ERR_FIT, "device allocation of " + std::to_string(bytes) + " bytes: " + cudaGetErrorString(e));
+    allocations.push_back(v);
+    *p = static_cast<T*>(v);
+    return cudaMemset(v, 0, bytes ? bytes : 16) == cudaSuccess ? FZ_OK : fail(FZ_ERR_CUDA, "memset");
+  }
+};
+
+namespace {
+
+// ------------------------------------------------------------ describe
+
+fz_status describe(fz_model& m) {
+  const GgufIndex& ix = m.index;
+  auto it = ix.metadata.find("general.architecture");
+  if (it == ix.metadata.end() || it->second.s != "gemma3")
+    return fail(FZ_ERR_ARCHITECTURE, "general.architecture is not gemma3");
+  Shape& s = m.shape;
+  const std::string a = "gemma3.";
+  struct Req { const char* key; uint32_t* v; } req[] = {
+      {"block_count", &s.layers}, {"context_length", &s.context}, {"embedding_length", &s.hidden},
+      {"feed_forward_length", &s.ffn}, {"attention.head_count", &s.heads},
+      {"attention.head_count_kv", &s.kv_heads}};
+  for (auto& r : req)
+    if (!ix.get_u32(a + r.key, *r.v) || *r.v == 0) return fail(FZ_ERR_ARCHITECTURE, a + r.key + " missing or zero");
+  if (!ix.get_f32(a + "attention.layer_norm_rms_epsilon", s.eps))
+    return fail(FZ_ERR_ARCHITECTURE, a + "attention.layer_norm_rms_epsilon missing");
+  if (!ix.get_f32(a + "rope.freq_base", s.rope_global)) return fail(FZ_ERR_ARCHITECTURE, a + "rope.freq_base missing");
+  s.rope_local = 10000.f;
+  ix.get_f32(a + "rope.freq_base_swa", s.rope_local);
+  s.head_dim = s.hidden / s.heads;
+  ix.get_u32(a + "attention.key_length", s.head_dim);
+  uint32_t vlen = s.head_dim;
+  ix.get_u32(a + "attention.value_length", vlen);
+  if (vlen != s.head_dim) return fail(FZ_ERR_ARCHITECTURE, "value length differs from key length");
+  s.window = 0;
+  ix.get_u32(a + "attention.sliding_window", s.window);
+  s.pattern = 6;
+  ix.get_u32(a + "attention.sliding_window_pattern", s.pattern);
+  if (s.pattern == 0) return fail(FZ_ERR_ARCHITECTURE, "sliding window pattern 0");
+  float cap = 0.f;
+  if ((ix.get_f32(a + "attn_logit_softcapping", cap) && cap != 0.f) ||
+      (ix.get_f32(a + "final_logit_softcapping", cap) && cap != 0.f))
+    return fail(FZ_ERR_ARCHITECTURE, "logit softcapping is not run");
+  if (s.heads % s.kv_heads) return fail(FZ_ERR_ARCHITECTURE, "head_count_kv does not divide head_count");
+  if (s.head_dim != 256) return fail(FZ_ERR_NOT_SUPPORTED, "head dimension other than 256");
+  if (s.heads / s.kv_heads > 8) return fail(FZ_ERR_NOT_SUPPORTED, "more than 8 query heads a KV head");
+  if (s.hidden % 64 || s.ffn % 64 || (s.heads * s.head_dim) % 64 || s.hidden > 8192)
+    return fail(FZ_ERR_NOT_SUPPORTED, "widths must be multiples of 64 (hidden at most 8192)");
+  const fz::GgufTensor* embd = ix.find("token_embd.weight");
+  if (!embd || embd->type != 2 || embd->dims.size() != 2 || embd->dims[0] != s.hidden)
+    return fail(FZ_ERR_ARCHITECTURE, "token_embd.weight missing or not Q4_0 [hidden, vocab]");
+  s.vocab = (uint32_t)embd->dims[1];
+  if (s.vocab % 16) return fail(FZ_ERR_NOT_SUPPORTED, "vocabulary not a multiple of 16");
+  if (ix.find("output.weight")) return fail(FZ_ERR_NOT_SUPPORTED, "an untied output head");
+  auto need = [&](const std::string& name, uint32_t type, uint64_t d0, uint64_t d1) -> fz_status {
+    const fz::GgufTensor* t = ix.find(name);
+    if (!t) return fail(FZ_ERR_ARCHITECTURE, "missing tensor " + name);
+    if (t->type != type) return fail(FZ_ERR_NOT_SUPPORTED, name + ": type " + std::to_string(t->type));
+    if (t->dims[0] != d0 || (d1 && (t->dims.size() != 2 || t->dims[1] != d1)))
+      return fail(FZ_ERR_ARCHITECTURE, name + ": unexpected shape");
+    return FZ_OK;
+  };
+  fz_status st;
+  if ((st = need("output_norm.weight", 0, s.hidden, 0))) return st;
+  const uint32_t Q = s.heads * s.head_dim, KV = s.kv_heads * s.head_dim;
+  for (uint32_t l = 0; l < s.layers; l++) {
+    const std::string p = "blk." + std::to_string(l) + ".";
+    if ((st = need(p + "attn_norm.weight", 0, s.hidden, 0)) || (st = need(p + "attn_q.weight", 2, s.hidden, Q)) ||
+        (st = need(p + "attn_k.weight", 2, s.hidden, KV)) || (st = need(p + "attn_v.weight", 2, s.hidden, KV)) ||
+        (st = need(p + "attn_q_norm.weight", 0, s.head_dim, 0)) ||
+        (st = need(p + "attn_k_norm.weight", 0, s.head_dim, 0)) ||
+        (st = need(p + "attn_output.weight", 2, Q, s.hidden)) ||
+        (st = need(p + "post_attention_norm.weight", 0, s.hidden, 0)) ||
+        (st = need(p + "ffn_norm.weight", 0, s.hidden, 0)) || (st = need(p + "ffn_gate.weight", 2, s.hidden, s.ffn)) ||
+        (st = need(p + "ffn_up.weight", 2, s.hidden, s.ffn)) || (st = need(p + "ffn_down.weight", 2, s.ffn, s.hidden)) ||
+        (st = need(p + "post_ffw_norm.weight", 0, s.hidden, 0)))
+      return st;
+  }
+  return FZ_OK;
+}
+
+fz_status place_matrix(fz_model& m, DevMatrix& d, uint32_t n, uint32_t k) {
+  d.n = n;
+  d.k = k;
+  fz_status st;
+  if ((st = m.alloc(&d.codes, fz::q4_codes_bytes(n, k)))) return st;
+  return m.alloc(&d.scales, fz::q4_scales_bytes(n, k));
+}
+
+fz_status repack_into(fz_model& m, const std::string& name, DevMatrix& d, uint32_t row0) {
+  const fz::GgufTensor* t = m.index.find(name);
+  const uint32_t k = (uint32_t)t->dims[0], n = (uint32_t)t->dims[1];
+  uint4* codes = d.codes + (size_t)(row0 / 16) * (k / 64) * 32;
+  uint2* scales = d.scales + (size_t)(row0 / 16) * (k / 64) * 8;
+  FZ_CUDA(fz::launch_repack(m.staging + t->offset, n, k, codes, scales, m.dev->stream));
+  return FZ_OK;
+}
+
+fz_status copy_gain(fz_model& m, const std::string& name, float** out) {
+  const fz::GgufTensor* t = m.index.find(name);
+  fz_status st;
+  if ((st = m.alloc(out, t->bytes))) return st;
+  FZ_CUDA(cudaMemcpyAsync(*out, m.staging + t->offset, t->bytes, cudaMemcpyDeviceToDevice, m.dev->stream));
+  return FZ_OK;
+}
+
+bool covered(const fz_model& m, uint64_t a, uint64_t b) {
+  for (auto& r : m.written)
+    if (r.first <= a && b <= r.second) return true;
+  return false;
+}
+
+// ------------------------------------------------------------ launch configs
+
+struct Split {
+  uint32_t rg, ks, cluster;
+};
+
+Split split_for(uint32_t n, uint32_t k, uint32_t m, int epi) {
+  const uint32_t nbp = k / 64;
+  if (epi == fz::kEpilogueGated) return {2, std::min<uint32_t>(4, std::max<uint32_t>(1, nbp / 2)), 1};
+  if (epi == fz::kEpilogueHead) return {8, 1, 1};
+  Split s{1, std::min<uint32_t>(8, std::max<uint32_t>(1, nbp / 2)), 1};
+  const uint32_t mq = (m + 3) / 4;
+  // Keep each CTA's share of X fragments under ~110 KB of shared memory, and
+  // give narrow products with long rows enough CTAs.
+  while ((size_t)2 * ((nbp + s.cluster - 1) / s.cluster) * 2 * mq * 32 * 8 > 110 * 1024 && s.cluster < 8)
+    s.cluster *= 2;
+  if (n / 16 < 100 && nbp >= 64 && s.cluster < 2) s.cluster = 2;
+  return s;
+}
+
+fz_status run_matvec(fz::MatvecArgs a, int pro, int epi, cudaStream_t stream, bool pdl) {
+  const Split s = split_for(a.mat[0].n, a.mat[0].k, a.m, epi);
+  a.rg_per_cta = s.rg;
+  a.k_split = s.ks;
+  a.cluster = s.cluster;
+  FZ_CUDA(fz::launch_matvec(a, pro, epi, stream, pdl));
+  return FZ_OK;
+}
+
+// ------------------------------------------------------------ the step chain
+
+fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
+  fz_model& m = *b.model;
+  const Shape& s = m.shape;
+  const uint32_t T = key.tokens, M = b.S * T;
+  const bool pdl = true;
+  const CaptureLayout cl = capture_layout(s);
+  float* cap = key.capture ? b.captures : nullptr;
+  const uint32_t QW = s.heads * s.head_dim;
+  fz_status stt;
+  {
+    fz::EmbedArgs e{};
+    e.step = b.dstep;
+    e.table = m.embd.view();
+    e.ids = b.dids;
+    e.records = b.records;
+    e.seq_tokens = T;
+    e.m = M;
+    e.scale = std::sqrt((float)s.hidden);
+    e.hidden = b.hidden_a;
+    e.argmax = b.argmax;
+    e.seqs = b.S;
+    FZ_CUDA(fz::launch_embed(e, st, pdl));
+  }
+  for (uint32_t l = 0; l < s.layers; l++) {
+    const Layer& L = m.layers[l];
+    uint32_t* lc = b.counters + (size_t)l * b.counters_per_layer;
+    // QKV with the attention norm before it and QK-norm/RoPE/KV append after.
+    fz::MatvecArgs a{};
+    a.step = b.dstep;
+    a.mat[0] = L.qkv.view();
+    a.m = M;
+    a.seq_tokens = T;
+    a.capture_stride = cl.per_layer * s.layers;
+    a.norm.hidden_in = b.hidden_a;
+    a.norm.y = l ? b.y_mlp : nullptr;
+    a.norm.post_gain = l ? m.layers[l - 1].post_ffw_norm : nullptr;
+    a.norm.gain = L.attn_norm;
+    a.norm.hidden_out = b.hidden_b;
+    a.norm.eps = s.eps;
+    a.norm.width = s.hidden;
+    a.norm.row_of_token_stride = 1;
+    a.norm.capture_residual = cap ? cap + l * cl.per_layer + cl.residual : nullptr;
+    a.norm.capture_added = (cap && l) ? cap + (l - 1) * cl.per_layer + cl.mlp_added : nullptr;
+    a.out = b.qkv;
+    a.out_stride = L.qkv.n;
+    a.rope.q_gain = L.q_norm;
+    a.rope.k_gain = L.k_norm;
+    a.rope.turns = L.turns;
+    a.rope.eps = s.eps;
+    a.rope.heads = s.heads;
+    a.rope.kv_heads = s.kv_heads;
+    a.rope.head_dim = s.head_dim;
+    a.rope.key_cache = b.kc[l];
+    a.rope.value_cache = b.vc[l];
+    a.rope.slots = b.slots[l];
+    a.rope.seq_stride = b.seq_stride[l];
+    a.rope.query_out = b.q;
+    a.rope.capture_query = cap ? cap + l * cl.per_layer + cl.query : nullptr;
+    a.counter = lc;
+    if ((stt = run_matvec(a, fz::kPrologueNorm, fz::kEpilogueQkv, st, pdl))) return stt;
+    // Attention.
+    fz::AttentionArgs at{};
+    at.step = b.dstep;
+    at.q = b.q;
+    at.key_cache = b.kc[l];
+    at.value_cache = b.vc[l];
+    at.seq_stride = b.seq_stride[l];
+    at.slots = b.slots[l];
+    at.heads = s.heads;
+    at.kv_heads = s.kv_heads;
+    at.head_dim = s.head_dim;
+    at.window = L.window;
+    at.seq_tokens = T;
+    at.m = M;
+    at.scale_log2e = (float)((double)(1.0f / std::sqrt((float)s.head_dim)) * 1.4426950408889634);
+    at.split_keys = kSplitKeys;
+    at.splits = (std::min(L.window, b.context) + kSplitKeys - 1) / kSplitKeys;
+    at.partial_o = b.partial_o;
+    at.partial_ml = b.partial_ml;
+    at.counters = lc + 1;
+    at.out = b.attn;
+    FZ_CUDA(fz::launch_attention(at, st, pdl));
+    // Output projection.
+    fz::MatvecArgs o{};
+    o.step = b.dstep;
+    o.mat[0] = L.o.view();
+    o.m = M;
+    o.seq_tokens = T;
+    o.x = b.attn;
+    o.out = b.y_attn;
+    o.out_stride = s.hidden;
+    if ((stt = run_matvec(o, fz::kPrologueInput, fz::kEpilogueWrite, st, pdl))) return stt;
+    // Gate and up with the feed-forward norm before and GELU and edits after.
+    fz::MatvecArgs g{};
+    g.step = b.dstep;
+    g.mat[0] = L.gate.view();
+    g.mat[1] = L.up.view();
+    g.m = M;
+    g.seq_tokens = T;
+    g.capture_stride = cl.per_layer * s.layers;
+    g.norm.hidden_in = b.hidden_b;
+    g.norm.y = b.y_attn;
+    g.norm.post_gain = L.post_attn_norm;
+    g.norm.gain = L.ffn_norm;
+    g.norm.hidden_out = b.hidden_a;
+    g.norm.eps = s.eps;
+    g.norm.width = s.hidden;
+    g.norm.row_of_token_stride = 1;
+    g.norm.capture_added = cap ? cap + l * cl.per_layer + cl.attn_added : nullptr;
+    g.out = b.act;
+    g.out_stride = s.ffn;
+    g.edit.table = key.edits ? b.edit_tables : nullptr;
+    g.edit.table_stride = b.table_words;
+    g.edit.layer = l;
+    g.edit.capture_neurons = cap ? cap + l * cl.per_layer + cl.neurons : nullptr;
+    if ((stt = run_matvec(g, fz::kPrologueNorm, fz::kEpilogueGated, st, pdl))) return stt;
+    // Down projection.
+    fz::MatvecArgs d{};
+    d.step = b.dstep;
+    d.mat[0] = L.down.view();
+    d.m = M;
+    d.seq_tokens = T;
+    d.x = b.act;
+    d.out = b.y_mlp;
+    d.out_stride = s.hidden;
+    if ((stt = run_matvec(d, fz::kPrologueInput, fz::kEpilogueWrite, st, pdl))) return stt;
+  }
+  (void)QW;
+  if (key.logits) {
+    fz::MatvecArgs h{};
+    h.step = b.dstep;
+    h.mat[0] = m.embd.view();
+    h.m = b.S;
+    h.seq_tokens = T;
+    h.capture_stride = cl.per_layer * s.layers;
+    h.norm.hidden_in = b.hidden_a;
+    h.norm.y = b.y_mlp;
+    h.norm.post_gain = m.layers[s.layers - 1].post_ffw_norm;
+    h.norm.gain = m.output_norm;
+    h.norm.hidden_out = nullptr;
+    h.norm.eps = s.eps;
+    h.norm.width = s.hidden;
+    h.norm.row_of_token_stride = T;
+    h.norm.row_of_token_offset = T - 1;
+    h.norm.capture_added = cap ? cap + (s.layers - 1) * cl.per_layer + cl.mlp_added : nullptr;
+    h.out = b.logits;
+    h.out_stride = s.vocab;
+    h.head.argmax = b.argmax;
+    if ((stt = run_matvec(h, fz::kPrologueNorm, fz::kEpilogueHead, st, pdl))) return stt;
+    fz::SelectArgs se{};
+    se.step = b.dstep;
+    se.logits = b.logits;
+    se.vocab = s.vocab;
+    se.seqs = b.S;
+    se.argmax = b.argmax;
+    se.seeds = b.dseeds;
+    se.tile_best = b.tile_best;
+    se.candidates = b.candidates;
+    se.records = b.records;
+    FZ_CUDA(fz::launch_select(se, st, pdl));
+  }
+  return FZ_OK;
+}
+
+fz_status graph_for(fz_batch& b, const GraphKey& key, cudaGraphExec_t* out) {
+  auto it = b.graphs.find(key);
+  if (it != b.graphs.end()) {
+    *out = it->second;
+    return FZ_OK;
+  }
+  cudaStream_t cs = b.model->dev->capture;
+  FZ_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  fz_status st = enqueue_step(b, key, cs);
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(cs, &graph);
+  if (st) {
+    if (graph) cudaGraphDestroy(graph);
+    return st;
+  }
+  if (e != cudaSuccess) return fail(FZ_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return fail(FZ_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+  b.graphs[key] = exec;
+  *out = exec;
+  return FZ_OK;
+}
+
+bool direct_launch() {
+  const char* v = std::getenv("FRIZZLE_B200_NO_GRAPH");
+  return v && *v && *v != '0';
+}
+
+}  // namespace
+
+// ================================================================== C ABI
+
+extern "C" {
+
+const char* fz_last_error(void) { return g_error.c_str(); }
+
+fz_status fz_device_open(int ordinal, fz_device** out) {
+  if (!out) return fail(FZ_ERR_ARGUMENT, "null output");
+  int count = 0;
+  FZ_CUDA(cudaGetDeviceCount(&count));
+  if (ordinal < 0 || ordinal >= count) return fail(FZ_ERR_ARGUMENT, "no device " + std::to_string(ordinal));
+  FZ_CUDA(cudaSetDevice(ordinal));
+  cudaDeviceProp prop{};
+  FZ_CUDA(cudaGetDeviceProperties(&prop, ordinal));
+  if (prop.major != 10) return fail(FZ_ERR_NOT_SUPPORTED, std::string("not an sm_100 device: ") + prop.name);
+  auto d = std::make_unique<fz_device>();
+  d->ordinal = ordinal;
+  FZ_CUDA(fz::configure_kernels());
+  FZ_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+  FZ_CUDA(cudaStreamCreateWithFlags(&d->capture, cudaStreamNonBlocking));
+  *out = d.release();
+  return FZ_OK;
+}
+
+fz_status fz_device_close(fz_device* d) {
+  if (!d) return FZ_OK;
+  cudaSetDevice(d->ordinal);
+  cudaStreamSynchronize(d->stream);
+  cudaStreamDestroy(d->stream);
+  cudaStreamDestroy(d->capture);
+  delete d;
+  return FZ_OK;
+}
+
+void* fz_device_stream(fz_device* d) { return d ? (void*)d->stream : nullptr; }
+
+uint64_t fz_model_index_needed(void) { return g_index_needed; }
+
+fz_status fz_model_index_check(const void* head, uint64_t head_bytes, uint64_t file_bytes, fz_model_info* o) {
+  if (!head || !o) return fail(FZ_ERR_ARGUMENT, "null argument");
+  fz_model m;
+  uint64_t needed = 0;
+  std::string msg;
+  const fz::GgufError e = fz::parse_gguf_index(static_cast<const uint8_t*>(head), head_bytes, m.index, needed, msg);
+  if (e == fz::GgufError::Truncated) {
+    g_index_needed = needed;
+    return fail(FZ_ERR_TRUNCATED, msg);
+  }
+  if (e != fz::GgufError::Ok) return fail(FZ_ERR_INDEX, msg);
+  uint64_t end = 0;
+  for (auto& t : m.index.tensors) end = std::max(end, t.offset + t.bytes);
+  if (m.index.data_offset + end > file_bytes) return fail(FZ_ERR_INDEX, "tensor data runs past the end of the file");
+  fz_status st;
+  if ((st = describe(m))) return st;
+  const Shape& s = m.shape;
+  uint64_t bytes = 0;
+  for (auto& t : m.index.tensors) bytes += t.bytes;
+  *o = fz_model_info{s.layers, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim, s.vocab, s.window, s.pattern,
+                     s.context, s.eps, s.rope_global, s.rope_local, bytes};
+  return FZ_OK;
+}
+
+fz_status fz_model_load_begin(fz_device* dev, const void* head, uint64_t head_bytes, uint64_t file_bytes,
+                              fz_model** out) {
+  if (!dev || !head || !out) return fail(FZ_ERR_ARGUMENT, "null argument");
+  FZ_CUDA(cudaSetDevice(dev->ordinal));
+  auto m = std::make_unique<fz_model>();
+  m->dev = dev;
+  m->file_bytes = file_bytes;
+  uint64_t needed = 0;
+  std::string msg;
+  const fz::GgufError e =
+      fz::parse_gguf_index(static_cast<const uint8_t*>(head), head_bytes, m->index, needed, msg);
+  if (e == fz::GgufError::Truncated) {
+    g_index_needed = needed;
+    return fail(FZ_ERR_TRUNCATED, msg);
+  }
+  if (e != fz::GgufError::Ok) return fail(FZ_ERR_INDEX, msg);
+  uint64_t end = 0;
+  for (auto& t : m->index.tensors) end = std::max(end, t.offset + t.bytes);
+  if (m->index.data_offset + end > file_bytes) return fail(FZ_ERR_INDEX, "tensor data runs past the end of the file");
+  fz_status st;
+  if ((st = describe(*m))) return st;
+  m->staging_bytes = end;
+  cudaError_t ce = cudaMalloc(&m->staging, end);
+  if (ce != cudaSuccess) return fail(FZ_ERR_FIT, std::string("staging: ") + cudaGetErrorString(ce));
+  *out = m.release();
+  return FZ_OK;
+}
+
+fz_status fz_model_load_write(fz_model* m, uint64_t offset, const void* chunk, uint64_t bytes) {
+  if (!m || (!chunk && bytes)) return fail(FZ_ERR_ARGUMENT, "null argument");
+  if (m->finished || !m->staging) return fail(FZ_ERR_STATE, "the load is finished");
+  if (offset > m->file_bytes || bytes > m->file_bytes - offset)
+    return fail(FZ_ERR_UPLOAD, "chunk past the end of the file");
+  FZ_CUDA(cudaSetDevice(m->dev->ordinal));
+  const uint64_t d0 = m->index.data_offset, d1 = d0 + m->staging_bytes;
+  const uint64_t a = std::max(offset, d0), b = std::min(offset + bytes, d1);
+  if (a < b) {
+    FZ_CUDA(cudaMemcpy(m->staging + (a - d0), static_cast<const uint8_t*>(chunk) + (a - offset), b - a,
+                       cudaMemcpyHostToDevice));
+    // Merge [a-d0, b-d0) into the written set.
+    std::pair<uint64_t, uint64_t> r{a - d0, b - d0};
+    std::vector<std::pair<uint64_t, uint64_t>> merged;
+    for (auto& w : m->written) {
+      if (w.second < r.first || r.second < w.first) merged.push_back(w);
+      else r = {std::min(r.first, w.first), std::max(r.second, w.second)};
+    }
+    merged.push_back(r);
+    std::sort(merged.begin(), merged.end());
+    m->written.swap(merged);
+  }
+  return FZ_OK;
+}
+
+fz_status fz_model_load_finish(fz_model* m) {
+  if (!m) return fail(FZ_ERR_ARGUMENT, "null model");
+  if (m->finished) return fail(FZ_ERR_STATE, "the load is finished");
+  FZ_CUDA(cudaSetDevice(m->dev->ordinal));
+  for (auto& t : m->index.tensors)
+    if (!covered(*m, t.offset, t.offset + t.bytes)) return fail(FZ_ERR_UPLOAD, "tensor " + t.name + " was not written");
+  const Shape& s = m->shape;
+  const uint32_t Q = s.heads * s.head_dim, KV = s.kv_heads * s.head_dim;
+  fz_status st;
+  m->weight_bytes = 0;
+  if ((st = place_matrix(*m, m->embd, s.vocab, s.hidden)) || (st = repack_into(*m, "token_embd.weight", m->embd, 0)) ||
+      (st = copy_gain(*m, "output_norm.weight", &m->output_norm)))
+    return st;
+  m->layers.resize(s.layers);
+  for (uint32_t l = 0; l < s.layers; l++) {
+    Layer& L = m->layers[l];
+    const std::string p = "blk." + std::to_string(l) + ".";
+    if ((st = place_matrix(*m, L.qkv, Q + 2 * KV, s.hidden)) || (st = repack_into(*m, p + "attn_q.weight", L.qkv, 0)) ||
+        (st = repack_into(*m, p + "attn_k.weight", L.qkv, Q)) ||
+        (st = repack_into(*m, p + "attn_v.weight", L.qkv, Q + KV)) || (st = place_matrix(*m, L.o, s.hidden, Q)) ||
+        (st = repack_into(*m, p + "attn_output.weight", L.o, 0)) || (st = place_matrix(*m, L.gate, s.ffn, s.hidden)) ||
+        (st = repack_into(*m, p + "ffn_gate.weight", L.gate, 0)) || (st = place_matrix(*m, L.up, s.ffn, s.hidden)) ||
+        (st = repack_into(*m, p + "ffn_up.weight", L.up, 0)) || (st = place_matrix(*m, L.down, s.hidden, s.ffn)) ||
+        (st = repack_into(*m, p + "ffn_down.weight", L.down, 0)) ||
+        (st = copy_gain(*m, p + "attn_norm.weight", &L.attn_norm)) ||
+        (st = copy_gain(*m, p + "attn_q_norm.weight", &L.q_norm)) ||
+        (st = copy_gain(*m, p + "attn_k_norm.weight", &L.k_norm)) ||
+        (st = copy_gain(*m, p + "post_attention_norm.weight", &L.post_attn_norm)) ||
+        (st = copy_gain(*m, p + "ffn_norm.weight", &L.ffn_norm)) ||
+        (st = copy_gain(*m, p + "post_ffw_norm.weight", &L.post_ffw_norm)))
+      return st;
+    // Window layers: every pattern-th layer attends globally (gemma3.cpp:79-85).
+    L.global = s.window == 0 || l % s.pattern == s.pattern - 1;
+    L.window = L.global ? s.context : s.window;
+    L.rope_base = L.global ? s.rope_global : s.rope_local;
+    // theta_k / 2 pi in f64, rounded once (rope.cpp:95-107).
+    std::vector<float> turns(s.head_dim / 2);
+    for (uint32_t k = 0; k < s.head_dim / 2; k++) {
+      const double theta = std::pow((double)L.rope_base, -2.0 * (double)k / (double)s.head_dim);
+      turns[k] = (float)(theta / (2.0 * 3.14159265358979323846));
+    }
+    if ((st = m->alloc(&L.turns, turns.size() * 4))) return st;
+    FZ_CUDA(cudaMemcpy(L.turns, turns.data(), turns.size() * 4, cudaMemcpyHostToDevice));
+  }
+  FZ_CUDA(cudaStreamSynchronize(m->dev->stream));
+  FZ_CUDA(cudaFree(m->staging));
+  m->staging = nullptr;
+  m->finished = true;
+  return FZ_OK;
+}
+
+fz_status fz_model_info_get(const fz_model* m, fz_model_info* o) {
+  if (!m || !o) return fail(FZ_ERR_ARGUMENT, "null argument");
+  const Shape& s = m->shape;
+  *o = fz_model_info{s.layers, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim, s.vocab, s.window, s.pattern,
+                     s.context, s.eps, s.rope_global, s.rope_local, m->weight_bytes};
+  return FZ_OK;
+}
+
+fz_status fz_model_free(fz_model* m) {
+  if (m) {
+    cudaSetDevice(m->dev->ordinal);
+    delete m;
+  }
+  return FZ_OK;
+}
+
+fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uint32_t rollback, fz_batch** out) {
+  if (!m || !out) return fail(FZ_ERR_ARGUMENT, "null argument");
+  if (!m->finished) return fail(FZ_ERR_STATE, "the model is not loaded");
+  if (sequences == 0 || sequences > (uint32_t)fz::kMaxTokens)
+    return fail(FZ_ERR_NOT_SUPPORTED, "1 to 16 sequences a batch");
+  if (context == 0 || context > m->shape.context) return fail(FZ_ERR_ARGUMENT, "context outside 1 .. trained context");
+  FZ_CUDA(cudaSetDevice(m->dev->ordinal));
+  const Shape& s = m->shape;
+  auto b = std::make_unique<fz_batch>();
+  b->model = m;
+  b->S = sequences;
+  b->context = context;
+  b->rollback = rollback;
+  const uint32_t M = sequences * fz::kMaxTokens;
+  fz_status st;
+  for (uint32_t l = 0; l < s.layers; l++) {
+    const Layer& L = m->layers[l];
+    const uint64_t ring = (uint64_t)L.window + 512 + rollback;  // plan.cpp:335-336
+    const uint32_t slots = (uint32_t)std::min<uint64_t>(context, ring);
+    const uint64_t per_seq = (uint64_t)slots * s.kv_heads * s.head_dim;
+    uint16_t *k = nullptr, *v = nullptr;
+    if ((st = b->alloc(&k, per_seq * sequences * 2)) || (st = b->alloc(&v, per_seq * sequences * 2))) return st;
+    b->kc.push_back(k);
+    b->vc.push_back(v);
+    b->slots.push_back(slots);
+    b->seq_stride.push_back(per_seq);
+    b->splits_max = std::max<uint32_t>(b->splits_max, (std::min(L.window, context) + kSplitKeys - 1) / kSplitKeys);
+  }
+  const uint32_t Q = s.heads * s.head_dim, KV = s.kv_heads * s.head_dim;
+  b->counters_per_layer = 1 + M * s.kv_heads;
+  b->table_words = 2 * s.layers + 5 * kMaxEdits;
+  b->capture_floats = capture_layout(s).per_layer * s.layers;
+  const uint32_t tiles = fz::select_tiles(s.vocab);
+  if ((st = b->alloc(&b->hidden_a, (size_t)M * s.hidden * 4)) || (st = b->alloc(&b->hidden_b, (size_t)M * s.hidden * 4)) ||
+      (st = b->alloc(&b->qkv, (size_t)M * (Q + 2 * KV) * 4)) || (st = b->alloc(&b->q, (size_t)M * Q * 4)) ||
+      (st = b->alloc(&b->attn, (size_t)M * Q * 4)) || (st = b->alloc(&b->y_attn, (size_t)M * s.hidden * 4)) ||
+      (st = b->alloc(&b->y_mlp, (size_t)M * s.hidden * 4)) || (st = b->alloc(&b->act, (size_t)M * s.ffn * 4)) ||
+      (st = b->alloc(&b->logits, (size_t)sequences * s.vocab * 4)) ||
+      (st = b->alloc(&b->partial_o, (size_t)M * s.heads * b->splits_max * s.head_dim * 4)) ||
+      (st = b->alloc(&b->partial_ml, (size_t)M * s.heads * b->splits_max * 2 * 4)) ||
+      (st = b->alloc(&b->counters, (size_t)s.layers * b->counters_per_layer * 4)) ||
+      (st = b->alloc(&b->argmax, (size_t)sequences * 8)) ||
+      (st = b->alloc(&b->tile_best, (size_t)sequences * tiles * 64 * 8)) ||
+      (st = b->alloc(&b->candidates, (size_t)sequences * 128 * 4)) || (st = b->alloc(&b->records, (size_t)sequences * 16)) ||
+      (st = b->alloc(&b->dstep, sizeof(DeviceStep))) || (st = b->alloc(&b->dids, (size_t)M * 4)) ||
+      (st = b->alloc(&b->dseeds, (size_t)sequences * 8)) ||
+      (st = b->alloc(&b->edit_tables, (size_t)sequences * b->table_words * 4)) ||
+      (st = b->alloc(&b->captures, (size_t)sequences * b->capture_floats * 4)))
+    return st;
+  b->has_edits.assign(sequences, false);
+  for (auto& sl : b->slot) {
+    FZ_CUDA(cudaMallocHost(&sl.step, sizeof(DeviceStep)));
+    FZ_CUDA(cudaMallocHost(&sl.ids, (size_t)M * 4));
+    FZ_CUDA(cudaMallocHost(&sl.seeds, (size_t)sequences * 8));
+    FZ_CUDA(cudaMallocHost(&sl.records, (size_t)sequences * 16));
+    FZ_CUDA(cudaEventCreateWithFlags(&sl.copied, cudaEventDisableTiming));
+    FZ_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+  }
+  FZ_CUDA(cudaDeviceSynchronize());
+  *out = b.release();
+  return FZ_OK;
+}
+
+fz_status fz_batch_free(fz_batch* b) {
+  if (b) {
+    cudaSetDevice(b->model->dev->ordinal);
+    cudaStreamSynchronize(b->model->dev->stream);
+    delete b;
+  }
+  return FZ_OK;
+}
+
+fz_status fz_batch_set_edits(fz_batch* b, uint32_t sequence, const uint32_t* words, size_t count) {
+  if (!b || sequence >= b->S) return fail(FZ_ERR_ARGUMENT, "no such sequence");
+  const Shape& s = b->model->shape;
+  std::vector<uint32_t> table(b->table_words, 0u);
+  if (words && count) {
+    if (count > b->table_words || count < 2 * (size_t)s.layers)
+      return fail(FZ_ERR_EDITS, "table size outside 2 x layers .. 2 x layers + 5 x 4096 words");
+    for (uint32_t l = 0; l < s.layers; l++) {
+      const uint64_t first = words[2 * l], n = words[2 * l + 1];
+      if (n && (first < 2ull * s.layers || first + 5 * n > count))
+        return fail(FZ_ERR_EDITS, "layer " + std::to_string(l) + "'s edits lie outside the table");
+      for (uint64_t i = 0; i < n; i++) {
+        const uint32_t* e = words + first + 5 * i;
+        if (e[0] >= s.ffn) return fail(FZ_ERR_EDITS, "an edit's neuron is past the layer's width");
+        if (e[1] > 2) return fail(FZ_ERR_EDITS, "an edit's kind is not Set, Scale or Zero");
+        if (i && words[first + 5 * (i - 1)] > e[0])
+          return fail(FZ_ERR_EDITS, "a layer's edits are not sorted by neuron (edit::table's order)");
+      }
+    }
+    std::memcpy(table.data(), words, count * 4);
+  }
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  FZ_CUDA(cudaStreamSynchronize(b->model->dev->stream));
+  FZ_CUDA(cudaMemcpy(b->edit_tables + (size_t)sequence * b->table_words, table.data(), table.size() * 4,
+                     cudaMemcpyHostToDevice));
+  b->has_edits[sequence] = words && count;
+  return FZ_OK;
+}
+
+fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, const uint32_t* seeds) {
+  if (!b || !step) return fail(FZ_ERR_ARGUMENT, "null argument");
+  const Shape& s = b->model->shape;
+  const uint32_t T = step->tokens;
+  if (T < 1 || T * b->S > (uint32_t)fz::kMaxTokens) return fail(FZ_ERR_NOT_SUPPORTED, "sequences x tokens above 16");
+  if (step->fed && T != 1) return fail(FZ_ERR_ARGUMENT, "a fed step is one token");
+  if ((uint64_t)step->position + T > b->context) return fail(FZ_ERR_ARGUMENT, "the step runs past the context");
+  if ((uint64_t)step->position + T > (1u << 24)) return fail(FZ_ERR_ARGUMENT, "position past 2^24 (interface.h:220)");
+  if (!step->fed && !ids) return fail(FZ_ERR_ARGUMENT, "no token identifiers");
+  if (!step->fed)
+    for (uint32_t i = 0; i < T * b->S; i++)
+      if (ids[i] >= s.vocab) return fail(FZ_ERR_ARGUMENT, "a token identifier past the vocabulary");
+  if (step->logits && step->temperature > 0.f && step->top_k == 0) return fail(FZ_ERR_ARGUMENT, "top_k 0");
+  cudaStream_t st = b->model->dev->stream;
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  auto& sl = b->slot[b->next_slot];
+  if (sl.used) FZ_CUDA(cudaEventSynchronize(sl.copied));
+  std::memcpy(sl.step, step, sizeof(DeviceStep));
+  if (!step->fed) std::memcpy(sl.ids, ids, (size_t)T * b->S * 4);
+  for (uint32_t i = 0; i < b->S; i++) {
+    sl.seeds[2 * i] = seeds ? seeds[2 * i] : step->seed[0];
+    sl.seeds[2 * i + 1] = seeds ? seeds[2 * i + 1] : step->seed[1];
+  }
+  FZ_CUDA(cudaMemcpyAsync(b->dstep, sl.step, sizeof(DeviceStep), cudaMemcpyHostToDevice, st));
+  if (!step->fed) FZ_CUDA(cudaMemcpyAsync(b->dids, sl.ids, (size_t)T * b->S * 4, cudaMemcpyHostToDevice, st));
+  FZ_CUDA(cudaMemcpyAsync(b->dseeds, sl.seeds, (size_t)b->S * 8, cudaMemcpyHostToDevice, st));
+  FZ_CUDA(cudaEventRecord(sl.copied, st));
+  bool edits = false;
+  for (bool e : b->has_edits) edits = edits || e;
+  const GraphKey key{T, step->logits ? 1u : 0u, step->capture ? 1u : 0u, edits ? 1u : 0u};
+  fz_status stt;
+  if (direct_launch()) {
+    if ((stt = enqueue_step(*b, key, st))) return stt;
+  } else {
+    cudaGraphExec_t exec = nullptr;
+    if ((stt = graph_for(*b, key, &exec))) return stt;
+    FZ_CUDA(cudaGraphLaunch(exec, st));
+  }
+  FZ_CUDA(cudaMemcpyAsync(sl.records, b->records, (size_t)b->S * 16, cudaMemcpyDeviceToHost, st));
+  FZ_CUDA(cudaEventRecord(sl.done, st));
+  sl.used = true;
+  b->last_slot = b->next_slot;
+  b->next_slot ^= 1;
+  return FZ_OK;
+}
+
+fz_status fz_batch_wait(fz_batch* b, fz_record* records) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  if (b->last_slot < 0) return fail(FZ_ERR_STATE, "no step was run");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  auto& sl = b->slot[b->last_slot];
+  cudaError_t e = cudaEventSynchronize(sl.done);
+  if (e != cudaSuccess) {
+    const bool lost = e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure || e == cudaErrorECCUncorrectable;
+    return fail(lost ? FZ_ERR_DEVICE_LOST : FZ_ERR_CUDA, std::string("step: ") + cudaGetErrorString(e));
+  }
+  if (records) std::memcpy(records, sl.records, (size_t)b->S * 16);
+  return FZ_OK;
+}
+
+fz_status fz_batch_read_logits(fz_batch* b, uint32_t sequence, float* out, size_t count) {
+  if (!b || !out || sequence >= b->S) return fail(FZ_ERR_ARGUMENT, "bad argument");
+  const uint32_t V = b->model->shape.vocab;
+  if (count < V) return fail(FZ_ERR_ARGUMENT, "the output holds fewer than vocab floats");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  FZ_CUDA(cudaStreamSynchronize(b->model->dev->stream));
+  FZ_CUDA(cudaMemcpy(out, b->logits + (size_t)sequence * V, (size_t)V * 4, cudaMemcpyDeviceToHost));
+  return FZ_OK;
+}
+
+size_t fz_capture_floats(const fz_model* m) { return m ? capture_layout(m->shape).per_layer * m->shape.layers : 0; }
+
+fz_status fz_batch_read_capture(fz_batch* b, uint32_t sequence, float* out, size_t count) {
+  if (!b || !out || sequence >= b->S) return fail(FZ_ERR_ARGUMENT, "bad argument");
+  if (count < b->capture_floats) return fail(FZ_ERR_ARGUMENT, "the output holds fewer than fz_capture_floats floats");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  FZ_CUDA(cudaStreamSynchronize(b->model->dev->stream));
+  FZ_CUDA(cudaMemcpy(out, b->captures + (size_t)sequence * b->capture_floats, b->capture_floats * 4,
+                     cudaMemcpyDeviceToHost));
+  return FZ_OK;
+}
+
+fz_status fz_batch_cache(fz_batch* b, uint32_t sequence, uint32_t layer, int values, void** ptr, uint32_t* slots) {
+  if (!b || !ptr || sequence >= b->S || layer >= b->model->shape.layers) return fail(FZ_ERR_ARGUMENT, "bad argument");
+  *ptr = (values ? b->vc[layer] : b->kc[layer]) + (size_t)sequence * b->seq_stride[layer];
+  if (slots) *slots = b->slots[layer];
+  return FZ_OK;
+}
+
+// ------------------------------------------------------------------ kernel level
+
+size_t fz_q4_0_codes_bytes(uint32_t n, uint32_t k) { return fz::q4_codes_bytes(n, k); }
+size_t fz_q4_0_scales_bytes(uint32_t n, uint32_t k) { return fz::q4_scales_bytes(n, k); }
+
+static fz_status check_shape(uint32_t n, uint32_t k) {
+  if (n == 0 || k == 0 || n % 16 || k % 64) return fail(FZ_ERR_ARGUMENT, "n must be a multiple of 16 and k of 64");
+  return FZ_OK;
+}
+
+fz_status fz_q4_0_repack(const void* file_blocks, uint32_t n, uint32_t k, void* codes, void* scales, void* stream) {
+  fz_status st;
+  if ((st = check_shape(n, k))) return st;
+  if (!file_blocks || !codes || !scales) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  FZ_CUDA(fz::launch_repack(static_cast<const uint8_t*>(file_blocks), n, k, static_cast<uint4*>(codes),
+                            static_cast<uint2*>(scales), static_cast<cudaStream_t>(stream)));
+  return FZ_OK;
+}
+
+fz_status fz_q4_0_rows(const void* codes, const void* scales, uint32_t n, uint32_t k, const uint32_t* rows,
+                       uint32_t count, float scale, float* out, void* stream) {
+  fz_status st;
+  if ((st = check_shape(n, k))) return st;
+  if (!codes || !scales || !rows || !out) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  const Q4Matrix mat{static_cast<const uint4*>(codes), static_cast<const uint2*>(scales), n, k};
+  FZ_CUDA(fz::launch_dequant_rows(mat, rows, count, scale, out, static_cast<cudaStream_t>(stream)));
+  return FZ_OK;
+}
+
+fz_status fz_q4_0_matvec(const void* codes, const void* scales, uint32_t n, uint32_t k, const float* x, uint32_t m,
+                         float* y, void* stream) {
+  fz_status st;
+  if ((st = check_shape(n, k))) return st;
+  if (!codes || !scales || !x || !y) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  if (m < 1 || m > (uint32_t)fz::kMaxTokens) return fail(FZ_ERR_ARGUMENT, "m outside 1 .. 16");
+  fz::MatvecArgs a{};
+  a.mat[0] = Q4Matrix{static_cast<const uint4*>(codes), static_cast<const uint2*>(scales), n, k};
+  a.m = m;
+  a.seq_tokens = m;
+  a.x = x;
+  a.out = y;
+  a.out_stride = n;
+  return run_matvec(a, fz::kPrologueInput, fz::kEpilogueWrite, static_cast<cudaStream_t>(stream), false);
+}
+
+fz_status fz_q4_0_gated(const void* gate_codes, const void* gate_scales, const void* up_codes, const void* up_scales,
+                        uint32_t f, uint32_t k, const float* x, uint32_t m, const uint32_t* table, uint32_t layer,
+                        uint32_t position, float* act, void* stream) {
+  fz_status st;
+  if ((st = check_shape(f, k))) return st;
+  if (!gate_codes || !gate_scales || !up_codes || !up_scales || !x || !act) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  if (m < 1 || m > (uint32_t)fz::kMaxTokens) return fail(FZ_ERR_ARGUMENT, "m outside 1 .. 16");
+  fz::MatvecArgs a{};
+  a.mat[0] = Q4Matrix{static_cast<const uint4*>(gate_codes), static_cast<const uint2*>(gate_scales), f, k};
+  a.mat[1] = Q4Matrix{static_cast<const uint4*>(up_codes), static_cast<const uint2*>(up_scales), f, k};
+  a.m = m;
+  a.seq_tokens = m;
+  a.position = position;
+  a.x = x;
+  a.out = act;
+  a.out_stride = f;
+  a.edit.table = table;
+  a.edit.layer = layer;
+  return run_matvec(a, fz::kPrologueInput, fz::kEpilogueGated, static_cast<cudaStream_t>(stream), false);
+}
+
+fz_status fz_q4_0_head(const void* codes, const void* scales, uint32_t n, uint32_t k, const float* x, uint32_t m,
+                       float* logits, unsigned long long* argmax, void* stream) {
+  fz_status st;
+  if ((st = check_shape(n, k))) return st;
+  if (!codes || !scales || !x || !logits || !argmax) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  if (m < 1 || m > (uint32_t)fz::kMaxTokens) return fail(FZ_ERR_ARGUMENT, "m outside 1 .. 16");
+  fz::MatvecArgs a{};
+  a.mat[0] = Q4Matrix{static_cast<const uint4*>(codes), static_cast<const uint2*>(scales), n, k};
+  a.m = m;
+  a.seq_tokens = m;
+  a.x = x;
+  a.out = logits;
+  a.out_stride = n;
+  a.head.argmax = argmax;
+  return run_matvec(a, fz::kPrologueInput, fz::kEpilogueHead, static_cast<cudaStream_t>(stream), false);
+}
+
+}  // extern "C"

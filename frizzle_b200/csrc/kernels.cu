@@ -1,0 +1,375 @@
+// Attention (split-K flash-decode with an in-kernel combine), the embedding
+// gather, and top-64 selection with the draw.
+#include <algorithm>
+
+#include "kernels.cuh"
+
+namespace fz {
+namespace {
+
+constexpr int kHeadDim = 256;    // Gemma 3's d: one thread a dimension
+constexpr int kMaxGroup = 8;     // query heads sharing a KV head
+
+// ------------------------------------------------------------ attention
+//
+// softmax(q . k_j / sqrt(d)) . v_j over keys j in [p - W + 1, p]
+// (attention.h:18-30), in log2 units: q is staged times scale*log2(e) and
+// exp2 replaces exp (attention.wgsl:198-215).  A CTA takes one row, one KV
+// head (the G query heads that share it, so each key and value is read once
+// per group) and one split of `split_keys` keys.  Rows whose keys span
+// several splits leave (m, l, O) partials; the last of their CTAs folds them
+// in split order and divides (the combine, attention.wgsl:403-438).  The
+// fold factors keep the side holding the maximum at exactly 1
+// (fold_factors, attention.wgsl:135-151).
+__global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
+  __shared__ float sc[kMaxGroup][512];      // scores, then weights
+  __shared__ float red[kMaxGroup][8];
+  __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
+  __shared__ uint32_t s_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t row = blockIdx.z, kvh = blockIdx.y, split = blockIdx.x;
+  const int G = (int)(a.heads / a.kv_heads);
+  pdl_wait();
+  const uint32_t p = (a.step ? a.step->position : a.position) + row % a.seq_tokens;
+  const uint32_t seq = row / a.seq_tokens;
+  const uint32_t earliest = p + 1 > a.window ? p + 1 - a.window : 0;
+  const uint32_t nkeys = p + 1 - earliest;
+  const uint32_t nsplits = (nkeys + a.split_keys - 1) / a.split_keys;
+  if (split >= nsplits) return;
+  const uint32_t j0 = earliest + split * a.split_keys;
+  const uint32_t j1 = min(j0 + a.split_keys, p + 1);
+  const int n = (int)(j1 - j0);
+  const uint16_t* kc = a.key_cache + seq * a.seq_stride;
+  const uint16_t* vc = a.value_cache + seq * a.seq_stride;
+
+  // q for the group, dims 8*lane .. 8*lane+7, times scale*log2(e).
+  float qv[kMaxGroup][8];
+  for (int h = 0; h < G; h++) {
+    const float* q = a.q + ((size_t)row * a.heads + kvh * G + h) * kHeadDim + 8 * lane;
+    const float4 x0 = reinterpret_cast<const float4*>(q)[0], x1 = reinterpret_cast<const float4*>(q)[1];
+    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int i = 0; i < 8; i++) qv[h][i] = mul(v[i], a.scale_log2e);
+  }
+  // Scores: warp w takes keys w, w + 8, ...
+  for (int jj = warp; jj < n; jj += 8) {
+    const uint32_t j = j0 + jj;
+    const uint4 kw = *reinterpret_cast<const uint4*>(kc + ((size_t)(j % a.slots) * a.kv_heads + kvh) * kHeadDim +
+                                                     8 * lane);
+    const uint32_t w4[4] = {kw.x, kw.y, kw.z, kw.w};
+    float k[8];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+      k[2 * i] = f.x;
+      k[2 * i + 1] = f.y;
+    }
+    for (int h = 0; h < G; h++) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; i++) s = __fmaf_rn(qv[h][i], k[i], s);
+      s = warp_sum(s);
+      if (lane == 0) sc[h][jj] = s;
+    }
+  }
+  __syncthreads();
+  // Per head: maximum, weights exp2(s - m), sum.
+  for (int h = 0; h < G; h++) {
+    float m = -INFINITY;
+    for (int jj = tid; jj < n; jj += 256) m = fmaxf(m, sc[h][jj]);
+    m = warp_max(m);
+    if (lane == 0) red[h][warp] = m;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float m = red[tid][0];
+    for (int w = 1; w < 8; w++) m = fmaxf(m, red[tid][w]);
+    s_m[tid] = m;
+  }
+  __syncthreads();
+  for (int h = 0; h < G; h++) {
+    float l = 0.f;
+    for (int jj = tid; jj < n; jj += 256) {
+      const float e = exp2f(sc[h][jj] - s_m[h]);
+      sc[h][jj] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) red[h][warp] = l;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float l = 0.f;
+    for (int w = 0; w < 8; w++) l += red[tid][w];
+    s_l[tid] = l;
+  }
+  __syncthreads();
+  // O = sum_j w_j v_j, thread tid the dimension tid.
+  float o[kMaxGroup];
+  for (int h = 0; h < G; h++) o[h] = 0.f;
+  for (int jj = 0; jj < n; jj++) {
+    const uint32_t j = j0 + jj;
+    const float v = f16_unpack(vc[((size_t)(j % a.slots) * a.kv_heads + kvh) * kHeadDim + tid]);
+    for (int h = 0; h < G; h++) o[h] = __fmaf_rn(sc[h][jj], v, o[h]);
+  }
+  pdl_launch_dependents();
+  if (nsplits == 1) {
+    for (int h = 0; h < G; h++)
+      a.out[((size_t)row * a.heads + kvh * G + h) * kHeadDim + tid] = __fdiv_rn(o[h], s_l[h]);
+    return;
+  }
+  for (int h = 0; h < G; h++) {
+    const size_t at = ((size_t)row * a.heads + kvh * G + h) * a.splits + split;
+    a.partial_o[at * kHeadDim + tid] = o[h];
+    if (tid == 0) {
+      a.partial_ml[at * 2] = s_m[h];
+      a.partial_ml[at * 2 + 1] = s_l[h];
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(a.counters + row * a.kv_heads + kvh, 1u) == nsplits - 1 ? 1u : 0u;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int h = 0; h < G; h++) {
+    const size_t base = ((size_t)row * a.heads + kvh * G + h) * a.splits;
+    float m = -INFINITY;
+    for (uint32_t s = 0; s < nsplits; s++) m = fmaxf(m, __ldcg(a.partial_ml + (base + s) * 2));
+    float l = 0.f, acc = 0.f;
+    for (uint32_t s = 0; s < nsplits; s++) {
+      const float ms = __ldcg(a.partial_ml + (base + s) * 2);
+      const float f = ms == m ? 1.0f : exp2f(ms - m);
+      l = __fmaf_rn(__ldcg(a.partial_ml + (base + s) * 2 + 1), f, l);
+      acc = __fmaf_rn(__ldcg(a.partial_o + (base + s) * kHeadDim + tid), f, acc);
+    }
+    a.out[((size_t)row * a.heads + kvh * G + h) * kHeadDim + tid] = __fdiv_rn(acc, l);
+  }
+  if (tid == 0) a.counters[row * a.kv_heads + kvh] = 0u;
+}
+
+// ------------------------------------------------------------ embed
+
+__global__ void embed_kernel(const EmbedArgs a) {
+  const uint32_t i = blockIdx.x;
+  pdl_wait();
+  if (i == 0 && threadIdx.x < a.seqs) a.argmax[threadIdx.x] = 0ull;
+  const uint32_t seq = i / a.seq_tokens;
+  const uint32_t token = a.step->fed ? a.records[seq * 4] : a.ids[i];
+  const Q4Matrix& mat = a.table;
+  if (token >= mat.n) return;
+  const uint32_t NBP = mat.k / 64, KB = mat.k / 32;
+  const uint32_t rg = token / 16, rr = token % 16, g = rr % 8, hsel = rr / 8;
+  for (uint32_t j = threadIdx.x; j < KB * 8; j += blockDim.x) {
+    const uint32_t kb = j / 8, h = (j / 4) % 2, t = j % 4;
+    const uint32_t bp = kb / 2, kbi = kb % 2;
+    const uint4 c = mat.codes[((size_t)rg * NBP + bp) * 32 + g * 4 + t];
+    const uint32_t wi = kbi * 2 + h;
+    const uint32_t w = wi == 0 ? c.x : wi == 1 ? c.y : wi == 2 ? c.z : c.w;
+    const uint2 sc = mat.scales[((size_t)rg * NBP + bp) * 8 + g];
+    const uint32_t sw = kbi ? sc.y : sc.x;
+    const float d = __half2float(__ushort_as_half((unsigned short)(hsel ? sw >> 16 : sw & 0xffffu)));
+    const uint32_t q0 = (w >> (8 * hsel)) & 0xffu, q1 = (w >> (16 + 8 * hsel)) & 0xffu;
+    const uint32_t k0 = 32 * kb + 8 * h + 2 * t;
+    float* o = a.hidden + (size_t)i * mat.k;
+    o[k0] = mul(mul((float)(q0 & 0xF) - 8.0f, d), a.scale);
+    o[k0 + 1] = mul(mul((float)(q1 & 0xF) - 8.0f, d), a.scale);
+    o[k0 + 16] = mul(mul((float)(q0 >> 4) - 8.0f, d), a.scale);
+    o[k0 + 17] = mul(mul((float)(q1 >> 4) - 8.0f, d), a.scale);
+  }
+  pdl_launch_dependents();
+}
+
+// ------------------------------------------------------------ selection
+
+constexpr int kTile = 4096;      // logits a selection CTA sorts
+constexpr int kCandidates = 64;  // kernels::kCandidates
+
+FZ_DEV unsigned long long packed_key(float v, uint32_t id) {
+  return ((unsigned long long)topk_key(__float_as_uint(v)) << 32) | (0xFFFFFFFFu - id);
+}
+
+// Descending bitonic sort of n (a power of two) keys in shared memory.
+FZ_DEV void bitonic_desc(unsigned long long* k, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const unsigned long long x = k[lo], y = k[hi];
+        if ((x < y) == desc) {
+          k[lo] = y;
+          k[hi] = x;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+FZ_DEV float temperature_of(const SelectArgs& a) { return a.step->temperature; }
+
+// Each CTA keeps the top 64 of its tile of logits (topk.wgsl first/merge:
+// the same set and order, by a sort of the tile).
+__global__ void __launch_bounds__(512) select_tiles_kernel(const SelectArgs a) {
+  __shared__ unsigned long long keys[kTile];
+  pdl_wait();
+  if (!(temperature_of(a) > 0.0f)) return;
+  const uint32_t seq = blockIdx.y, tile = blockIdx.x, tiles = gridDim.x;
+  const float* l = a.logits + (size_t)seq * a.vocab;
+  for (int i = threadIdx.x; i < kTile; i += blockDim.x) {
+    const uint32_t id = tile * kTile + i;
+    keys[i] = id < a.vocab ? packed_key(l[id], id) : 0ull;
+  }
+  __syncthreads();
+  bitonic_desc(keys, kTile);
+  if (threadIdx.x < kCandidates)
+    a.tile_best[((size_t)seq * tiles + tile) * kCandidates + threadIdx.x] = keys[threadIdx.x];
+}
+
+FZ_DEV float unit_interval(uint32_t w) {
+  return __fadd_rn(__fmul_rn((float)(w >> 9), 1.0f / 8388608.0f), 1.0f / 16777216.0f);
+}
+
+// Merge the tiles' candidates and draw (draw.wgsl:78-170); at temperature 0
+// the record is the head's greedy maximum.
+__global__ void __launch_bounds__(512) select_draw_kernel(const SelectArgs a, uint32_t tiles) {
+  __shared__ unsigned long long keys[kTile];
+  __shared__ float tempered[kCandidates], weight[kCandidates], running[kCandidates];
+  __shared__ uint32_t above[kCandidates];
+  pdl_wait();
+  const uint32_t seq = blockIdx.x;
+  const DeviceStep& st = *a.step;
+  const uint2 seed = a.seeds ? make_uint2(a.seeds[2 * seq], a.seeds[2 * seq + 1]) : make_uint2(st.seed[0], st.seed[1]);
+  const uint4 rnd = philox(make_uint4(st.position + st.tokens, 0u, 0u, 0u), seed);
+  const float u = unit_interval(rnd.x);
+  uint32_t* rec = a.records + seq * 4;
+  if (!(st.temperature > 0.0f)) {
+    if (threadIdx.x == 0) {
+      const unsigned long long best = a.argmax[seq];
+      const uint32_t bits = topk_bits((uint32_t)(best >> 32));
+      const bool failed = (bits & 0x7F800000u) == 0x7F800000u;
+      rec[0] = failed ? 0u : 0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu);
+      rec[1] = failed ? 1u : 0u;
+      rec[2] = __float_as_uint(u);
+      rec[3] = 0u;
+    }
+    return;
+  }
+  const int n = (int)(tiles * kCandidates);
+  int padded = 64;
+  while (padded < n) padded <<= 1;
+  for (int i = threadIdx.x; i < padded; i += blockDim.x)
+    keys[i] = i < n ? a.tile_best[(size_t)seq * tiles * kCandidates + i] : 0ull;
+  __syncthreads();
+  bitonic_desc(keys, padded);
+  uint32_t* cand = a.candidates + seq * kCandidates * 2;
+  if (threadIdx.x < kCandidates) {
+    const unsigned long long k = keys[threadIdx.x];
+    cand[2 * threadIdx.x] = k ? topk_bits((uint32_t)(k >> 32)) : 0u;
+    cand[2 * threadIdx.x + 1] = k ? 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu) : 0xFFFFFFFFu;
+  }
+  __syncthreads();
+  const uint32_t k = min(st.top_k, (uint32_t)kCandidates);
+  const bool use_top_p = st.top_p < 1.0f;
+  const uint32_t first_bits = cand[0];
+  const bool failed = (first_bits & 0x7F800000u) == 0x7F800000u;
+  const uint32_t t = threadIdx.x;
+  if (t < k) {
+    const uint32_t mine_bits = cand[2 * t];
+    weight[t] = 0.f;
+    tempered[t] = 0.f;
+    above[t] = 0u;
+    if (!failed && mine_bits != 0xFF800000u) {
+      const float first = __uint_as_float(first_bits), mine = __uint_as_float(mine_bits);
+      if (use_top_p) weight[t] = expf(sub(mine, first));
+      tempered[t] = expf(__fdiv_rn(sub(mine, first), st.temperature));
+      above[t] = (st.min_p == 0.0f || mine >= add(first, st.log_min_p)) ? 1u : 0u;
+    }
+  }
+  __syncthreads();
+  if (t != 0) return;
+  if (use_top_p) {
+    float sum = 0.f;
+    for (uint32_t i = 0; i < k; i++) sum = add(sum, weight[i]);
+    if (!failed)
+      for (uint32_t i = 0; i < k; i++) weight[i] = __fdiv_rn(weight[i], sum);
+  }
+  uint32_t kept = k;
+  float cumulative = 0.f, tsum = 0.f;
+  for (uint32_t i = 0; i < k; i++) {
+    tsum = add(tsum, tempered[i]);
+    running[i] = tsum;
+    if (use_top_p) {
+      cumulative = add(cumulative, weight[i]);
+      if (cumulative >= st.top_p) {
+        kept = i + 1;
+        break;
+      }
+    }
+  }
+  uint32_t survivors = 1;
+  while (survivors < kept && above[survivors] == 1u) survivors++;
+  const float goal = mul(u, running[survivors - 1]);
+  uint32_t chosen = survivors - 1;
+  for (uint32_t i = 0; i < survivors; i++)
+    if (running[i] > goal) {
+      chosen = i;
+      break;
+    }
+  rec[0] = failed ? 0u : cand[2 * chosen + 1];
+  rec[1] = failed ? 1u : 0u;
+  rec[2] = __float_as_uint(u);
+  rec[3] = 0u;
+}
+
+cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.head_dim != kHeadDim || a.heads % a.kv_heads || a.heads / a.kv_heads > kMaxGroup || a.split_keys > 512 ||
+      a.split_keys == 0)
+    return cudaErrorInvalidValue;
+  AttentionArgs copy = a;
+  void* args[] = {&copy};
+  return launch((const void*)attention_kernel, dim3(a.splits, a.kv_heads, a.m), dim3(256), 0, stream, pdl, args);
+}
+
+cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.seqs > 256) return cudaErrorInvalidValue;
+  EmbedArgs copy = a;
+  void* args[] = {&copy};
+  return launch((const void*)embed_kernel, dim3(a.m), dim3(256), 0, stream, pdl, args);
+}
+
+uint32_t select_tiles(uint32_t vocab) { return (vocab + kTile - 1) / kTile; }
+
+cudaError_t launch_select(const SelectArgs& a, cudaStream_t stream, bool pdl) {
+  const uint32_t tiles = select_tiles(a.vocab);
+  if (tiles * kCandidates > (uint32_t)kTile) return cudaErrorInvalidValue;
+  SelectArgs copy = a;
+  void* args1[] = {&copy};
+  cudaError_t e = launch((const void*)select_tiles_kernel, dim3(tiles, a.seqs), dim3(512), 0, stream, pdl, args1);
+  if (e != cudaSuccess) return e;
+  uint32_t t = tiles;
+  void* args2[] = {&copy, &t};
+  return launch((const void*)select_draw_kernel, dim3(a.seqs), dim3(512), 0, stream, pdl, args2);
+}
+
+}  // namespace fz

@@ -1,0 +1,63 @@
+// Attention, embedding gather, selection and draw kernels (launch side).
+#pragma once
+
+#include "fz_common.cuh"
+#include "q4_matvec.cuh"
+
+namespace fz {
+
+struct AttentionArgs {
+  const DeviceStep* step;          // or null for `position`
+  uint32_t position;
+  const float* q;                  // [m][heads][d], after rope
+  const uint16_t* key_cache;       // [seqs][slots][kv_heads][d]
+  const uint16_t* value_cache;
+  uint64_t seq_stride;
+  uint32_t slots;
+  uint32_t heads, kv_heads, head_dim;
+  uint32_t window;
+  uint32_t seq_tokens;             // T
+  uint32_t m;                      // rows
+  float scale_log2e;
+  uint32_t split_keys;             // keys a split
+  uint32_t splits;                 // grid.x: the most splits any row needs
+  float* partial_o;                // [m][heads][splits][d]
+  float* partial_ml;               // [m][heads][splits][2]
+  uint32_t* counters;              // [m][kv_heads], zero between launches
+  float* out;                      // [m][heads][d]
+};
+
+cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl);
+
+// The embedding rows of the step's tokens (or, for a fed step, the last draw)
+// times `scale`, into hidden [m][width]; also clears the argmax slots.
+struct EmbedArgs {
+  const DeviceStep* step;
+  Q4Matrix table;
+  const uint32_t* ids;             // [m]
+  const uint32_t* records;         // [seqs][4], the last step's draws (fed)
+  uint32_t seq_tokens;
+  uint32_t m;
+  float scale;
+  float* hidden;
+  unsigned long long* argmax;      // [seqs] cleared
+  uint32_t seqs;
+};
+cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t stream, bool pdl);
+
+// Selection and the draw (topk.wgsl, draw.wgsl) over each sequence's logits.
+struct SelectArgs {
+  const DeviceStep* step;
+  const float* logits;             // [seqs][vocab]
+  uint32_t vocab;
+  uint32_t seqs;
+  const unsigned long long* argmax;  // [seqs], the head's greedy maximum
+  const uint32_t* seeds;           // [seqs][2], or null for the step's seed
+  unsigned long long* tile_best;   // [seqs][tiles][64] scratch
+  uint32_t* candidates;            // [seqs][64][2] (logit bits, token)
+  uint32_t* records;               // [seqs][4] {token, failed, u bits, 0}
+};
+uint32_t select_tiles(uint32_t vocab);
+cudaError_t launch_select(const SelectArgs& a, cudaStream_t stream, bool pdl);
+
+}  // namespace fz

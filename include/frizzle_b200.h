@@ -1,0 +1,198 @@
+/*
+ * frizzle_b200: the Gemma 3 1B Q4_0 forward pass and neuron-steering hook of
+ * plainsight-systems/frizzle, as hand-written sm_100a CUDA kernels behind a
+ * plain C ABI.  No torch or CUDA types appear in the signatures: device
+ * buffers are `void*`/typed pointers, streams are `void*` (a cudaStream_t or
+ * NULL for the library's own stream), sizes are explicit.
+ *
+ * Two levels:
+ *   - Engine level: device, model load (GGUF bytes in chunks), sequences
+ *     ("batch" of sequences stepped together), steps, readback.  This replaces
+ *     the WebGPU Program/Upload/Device layer under Frizzle's C++ engine.
+ *   - Kernel level: each hot kernel over caller-owned device buffers, for a
+ *     host that drives its own launch list (as kernels::Program does) and for
+ *     parity tests.
+ *
+ * Every call returns an fz_status; on failure fz_last_error() (thread-local)
+ * names what was refused and why.  Calls on one fz_device are not
+ * thread-safe against each other; distinct devices may be driven from
+ * distinct threads.
+ */
+#ifndef FRIZZLE_B200_H
+#define FRIZZLE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Mirrors ProgramError (src/core/kernels/program.h:264-278), LoadError
+ * (src/core/runtime/engine.h:150-165) and EditError (src/core/edit/edit.h:140-150)
+ * folded into one code space. */
+typedef enum fz_status {
+  FZ_OK = 0,
+  FZ_ERR_ARGUMENT = 1,       /* a pointer, size or value outside the contract */
+  FZ_ERR_CUDA = 2,           /* a CUDA call failed (ProgramError::Step) */
+  FZ_ERR_INDEX = 3,          /* not a GGUF index this engine reads (LoadError::Index) */
+  FZ_ERR_ARCHITECTURE = 4,   /* not a Gemma 3 file this engine runs (LoadError::Architecture) */
+  FZ_ERR_FIT = 5,            /* does not fit device memory (LoadError::Fit) */
+  FZ_ERR_UPLOAD = 6,         /* bytes outside the file, or missing at finish (LoadError::Upload) */
+  FZ_ERR_STATE = 7,          /* called in the wrong load/run state (LoadError::Busy/NotLoading) */
+  FZ_ERR_EDITS = 8,          /* an edit table that is not well formed (OperationError::Edits) */
+  FZ_ERR_TRUNCATED = 9,      /* more index bytes are needed: see fz_model_index_needed */
+  FZ_ERR_DEVICE_LOST = 10,   /* the context is unusable (ProgramError::DeviceLost) */
+  FZ_ERR_NOT_SUPPORTED = 11  /* a shape this build does not run */
+} fz_status;
+
+typedef struct fz_device fz_device;
+typedef struct fz_model fz_model;
+typedef struct fz_batch fz_batch;
+
+/* The step's parameters: kernels::Step's 64-byte head
+ * (src/core/kernels/interface.h:163-185), the token identifiers passed beside
+ * it.  `capture` (a padding word in the reference) asks for the per-layer
+ * activation capture of each sequence's last row. */
+typedef struct fz_step {
+  uint32_t position;      /* the first token's position in the context */
+  uint32_t tokens;        /* tokens a sequence this step, 1 .. 16 */
+  uint32_t logits;        /* 1: the last row's logits, selection and draw */
+  uint32_t fed;           /* 1: the one token is each sequence's last draw, read on the device */
+  uint32_t seed[2];       /* the draw's seed, low word first */
+  uint32_t top_k;
+  float temperature;      /* 0: greedy */
+  float top_p;
+  float min_p;
+  float log_min_p;        /* ln min_p (sampler::apply, src/core/sampler/sampler.cpp:51-62) */
+  uint32_t capture;
+  uint32_t padding[4];
+} fz_step;
+
+/* What the draw writes per sequence: SampledRecord (src/core/sampler/sampler.h:187-193). */
+typedef struct fz_record {
+  uint32_t token;
+  uint32_t failed;        /* 1 when the top logit was not finite */
+  float u;                /* the uniform the draw used */
+  uint32_t padding;
+} fz_record;
+
+typedef struct fz_model_info {
+  uint32_t layers, hidden, ffn, heads, kv_heads, head_dim, vocab, window, pattern, context;
+  float eps, rope_global, rope_local;
+  uint64_t weight_bytes;  /* device bytes of the repacked weights */
+} fz_model_info;
+
+/* ------------------------------------------------------------------ errors */
+
+/* The message of the calling thread's last failed call. */
+const char *fz_last_error(void);
+
+/* ------------------------------------------------------------------ device
+ * Replaces gpu::Device (src/core/gpu/device.h:132): a CUDA device and the
+ * stream the engine runs on. */
+fz_status fz_device_open(int ordinal, fz_device **out);
+fz_status fz_device_close(fz_device *device);
+/* The device's stream as a cudaStream_t (for hosts that order their own work after it). */
+void *fz_device_stream(fz_device *device);
+
+/* ------------------------------------------------------------------ load
+ * Replaces Upload::begin/write/finish (src/core/residency/upload.h:263-337)
+ * with the describe (src/core/arch/describe.cpp:205-320) and residency plan
+ * (src/core/residency/plan.h:319-324) it depends on.
+ *
+ * begin: `head` holds the file's first `head_bytes` bytes, at least through
+ * its tensor infos; FZ_ERR_TRUNCATED asks for fz_model_index_needed() bytes.
+ * write: any chunk of the file by its absolute offset, each byte once; bytes
+ * outside tensor data are ignored.  finish: repacks every weight on the
+ * device into the kernels' layout and frees the staging copy. */
+/* Parses and describes a file's index without a device: the checks
+ * fz_model_load_begin makes before it allocates (LoadError::Index and
+ * ::Architecture), and the shape it would load. */
+fz_status fz_model_index_check(const void *head, uint64_t head_bytes, uint64_t file_bytes, fz_model_info *out);
+fz_status fz_model_load_begin(fz_device *device, const void *head, uint64_t head_bytes, uint64_t file_bytes,
+                              fz_model **out);
+uint64_t fz_model_index_needed(void);
+fz_status fz_model_load_write(fz_model *model, uint64_t offset, const void *chunk, uint64_t bytes);
+fz_status fz_model_load_finish(fz_model *model);
+fz_status fz_model_info_get(const fz_model *model, fz_model_info *out);
+fz_status fz_model_free(fz_model *model);
+
+/* ------------------------------------------------------------------ sequences
+ * A batch is `sequences` independent sequences stepped together at the same
+ * positions, each with its own KV cache (cache/kv.h), edit table and seed.
+ * Window layers keep rings of window + 512 + rollback slots
+ * (src/core/residency/plan.cpp:335-336); global layers keep `context`. */
+fz_status fz_batch_create(fz_model *model, uint32_t sequences, uint32_t context, uint32_t rollback,
+                          fz_batch **out);
+fz_status fz_batch_free(fz_batch *batch);
+
+/* The run's edits for one sequence, as edit::table lays them out
+ * (src/core/edit/edit.h:50-60, edit.cpp:147-170): per layer [first, count],
+ * then 5 words an edit {neuron, kind, value bits, first position, end}.
+ * NULL/0 clears them.  Checked for shape (offsets inside the table, neurons
+ * inside the layer, kinds 0..2); edit::check's semantic checks stay the
+ * caller's, as in the reference (engine.cpp:706-708 writes a checked table). */
+fz_status fz_batch_set_edits(fz_batch *batch, uint32_t sequence, const uint32_t *words, size_t count);
+
+/* One step over every sequence: replaces Program::run (src/core/kernels/program.h:380-388).
+ * `ids` holds sequences x step->tokens identifiers (ignored when fed);
+ * `seeds` 2 words a sequence or NULL for step->seed.  Enqueued on the
+ * device's stream; fz_batch_wait returns the records. */
+fz_status fz_batch_step(fz_batch *batch, const fz_step *step, const uint32_t *ids, const uint32_t *seeds);
+fz_status fz_batch_wait(fz_batch *batch, fz_record *records);
+
+/* Readback: each sequence's last logits row (vocab floats), and its capture
+ * store of the last row of the step that asked for it (fz_capture_floats
+ * floats: per layer the residual entering the layer, the query after rope,
+ * the attention block's addition, the neurons after edits, the feed-forward
+ * block's addition; the capture of src/core/capture/capture.h:217-255). */
+fz_status fz_batch_read_logits(fz_batch *batch, uint32_t sequence, float *out, size_t count);
+size_t fz_capture_floats(const fz_model *model);
+fz_status fz_batch_read_capture(fz_batch *batch, uint32_t sequence, float *out, size_t count);
+/* Device pointer of sequence s's key or value cache for `layer` ([slots][kv_heads][d] f16). */
+fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int values, void **ptr,
+                         uint32_t *slots);
+
+/* ------------------------------------------------------------------ kernel level
+ * Device pointers throughout; `stream` is a cudaStream_t or NULL (the legacy
+ * default stream). */
+
+/* Bytes of the fragment-native layout of an n x k Q4_0 matrix (n % 16 == 0, k % 64 == 0). */
+size_t fz_q4_0_codes_bytes(uint32_t n, uint32_t k);
+size_t fz_q4_0_scales_bytes(uint32_t n, uint32_t k);
+
+/* GGUF Q4_0 blocks (18 bytes each, row-major) into the layout
+ * (PieceWriter's transpose, src/core/residency/piece_writer.h:165-245). */
+fz_status fz_q4_0_repack(const void *file_blocks, uint32_t n, uint32_t k, void *codes, void *scales,
+                         void *stream);
+
+/* Rows of a repacked matrix back to f32, times `scale` (the gather,
+ * src/core/kernels/gather/gather.wgsl:25-48). */
+fz_status fz_q4_0_rows(const void *codes, const void *scales, uint32_t n, uint32_t k, const uint32_t *rows,
+                       uint32_t count, float scale, float *out, void *stream);
+
+/* y[m][n] = sum_k W[n][k] x[m][k], m <= 16 (matmul_launches with the Write
+ * epilogue, src/core/kernels/matmul/matmul.cpp:258-312). */
+fz_status fz_q4_0_matvec(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
+                         uint32_t m, float *y, void *stream);
+
+/* act[m][f] = gelu_tanh(gate . x) * (up . x), then the edit table applied to
+ * rows at positions position + r (the GatedActivation epilogue,
+ * matmul.wgsl:247-270, and the edit launch, src/core/edit/edit.wgsl:55-76);
+ * `table` may be NULL. */
+fz_status fz_q4_0_gated(const void *gate_codes, const void *gate_scales, const void *up_codes,
+                        const void *up_scales, uint32_t f, uint32_t k, const float *x, uint32_t m,
+                        const uint32_t *table, uint32_t layer, uint32_t position, float *act, void *stream);
+
+/* The head: logits[m][n] and, per row, the greedy choice (largest logit,
+ * ties to the lower id; topk.wgsl:32-61) packed as (key << 32) | ~id into
+ * argmax[m] (max-reduced: clear it first). */
+fz_status fz_q4_0_head(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
+                       uint32_t m, float *logits, unsigned long long *argmax, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRIZZLE_B200_H */

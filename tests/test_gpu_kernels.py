@@ -1,0 +1,134 @@
+"""Kernel-level parity through the C ABI on the GPU: each hot kernel against the
+CPU oracle on the same seeded inputs (BASELINE config 2's Q4_0 sweep shapes).
+
+Bars: the Q4_0 decode and repack bit-exact; products within 1e-5 relative RMS
+and 1e-4 x max|y| of the oracle's f32 (the hi/lo split keeps them f32-exact
+to ~2^-22; the sum order differs from the reference's 32 ranges); argmax
+identical to the argmax of the kernel's own logits."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import oracle
+from frizzle_b200 import _native, synth
+from frizzle_b200.edits import Edit, check, table, SET, SCALE, ZERO
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(1152, 1024), (1152, 256), (1024, 1152), (1152, 6912), (6912, 1152)]  # (K, N)
+
+
+def torch_cuda():
+    import torch
+    assert torch.cuda.is_available(), "the GPU tests need a CUDA device"
+    return torch
+
+
+def dev(arr):
+    torch = torch_cuda()
+    return torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+
+
+def stream():
+    return torch_cuda().cuda.current_stream().cuda_stream
+
+
+def repacked(blocks, n, k):
+    torch = torch_cuda()
+    lib = _native.load()
+    src = dev(blocks)
+    codes = torch.empty(lib.fz_q4_0_codes_bytes(n, k), dtype=torch.uint8, device="cuda")
+    scales = torch.empty(lib.fz_q4_0_scales_bytes(n, k), dtype=torch.uint8, device="cuda")
+    _native.check(lib.fz_q4_0_repack(src.data_ptr(), n, k, codes.data_ptr(), scales.data_ptr(), stream()))
+    return codes, scales
+
+
+def test_repack_and_rows_bit_exact():
+    torch = torch_cuda()
+    lib = _native.load()
+    n, k = 96, 1152
+    blocks = synth.random_q4_0(n, k, seed=11)
+    codes, scales = repacked(blocks, n, k)
+    rows = dev(np.arange(n, dtype=np.uint32).astype(np.int32)).to(torch.int32)
+    out = torch.empty(n * k, dtype=torch.float32, device="cuda")
+    _native.check(lib.fz_q4_0_rows(codes.data_ptr(), scales.data_ptr(), n, k, rows.data_ptr(), n, 1.0,
+                                   out.data_ptr(), stream()))
+    got = out.cpu().numpy()
+    want = oracle.dequant(blocks)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    # And the gather's scaling: (code - 8) * d, then * sqrt(width), in f32.
+    s = np.float32(np.sqrt(np.float32(k)))
+    _native.check(lib.fz_q4_0_rows(codes.data_ptr(), scales.data_ptr(), n, k, rows.data_ptr(), n, float(s),
+                                   out.data_ptr(), stream()))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), (want * s).view(np.uint32))
+
+
+@pytest.mark.parametrize("k,n", SHAPES)
+@pytest.mark.parametrize("m", [1, 4, 8, 16])
+def test_matvec_sweep_shapes(k, n, m):
+    torch = torch_cuda()
+    lib = _native.load()
+    blocks = synth.random_q4_0(n, k, seed=k * 7 + n)
+    x = np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)
+    codes, scales = repacked(blocks, n, k)
+    xd = dev(x)
+    y = torch.empty((m, n), dtype=torch.float32, device="cuda")
+    _native.check(lib.fz_q4_0_matvec(codes.data_ptr(), scales.data_ptr(), n, k, xd.data_ptr(), m, y.data_ptr(),
+                                     stream()))
+    got = y.cpu().numpy()
+    want = oracle.matmul(blocks, n, k, x)
+    err = np.sqrt(np.mean((got.astype(np.float64) - want) ** 2)) / np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    assert err < 1e-5
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
+
+
+def test_head_shape_and_argmax():
+    torch = torch_cuda()
+    lib = _native.load()
+    n, k = 262144, 1152
+    blocks = synth.random_q4_0(n, k, seed=5)
+    codes, scales = repacked(blocks, n, k)
+    x = np.random.default_rng(3).standard_normal((2, k)).astype(np.float32)
+    xd = dev(x)
+    logits = torch.empty((2, n), dtype=torch.float32, device="cuda")
+    am = torch.zeros(2, dtype=torch.int64, device="cuda")
+    _native.check(lib.fz_q4_0_head(codes.data_ptr(), scales.data_ptr(), n, k, xd.data_ptr(), 2, logits.data_ptr(),
+                                   am.data_ptr(), stream()))
+    got = logits.cpu().numpy()
+    want = oracle.matmul(blocks, n, k, x)
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
+    packed = am.cpu().numpy().view(np.uint64)
+    for r in range(2):
+        token = 0xFFFFFFFF - int(packed[r] & 0xFFFFFFFF)
+        assert token == int(np.argmax(got[r]))
+
+
+@pytest.mark.parametrize("m,position", [(5, 36), (5, 40), (1, 45), (1, 46), (16, 30)])
+def test_gated_with_edits(m, position):
+    torch = torch_cuda()
+    lib = _native.load()
+    f, k = 6912, 1152
+    gate = synth.random_q4_0(f, k, seed=1)
+    up = synth.random_q4_0(f, k, seed=2)
+    x = np.random.default_rng(4).standard_normal((m, k)).astype(np.float32) * np.float32(0.05)
+    gc, gs = repacked(gate, f, k)
+    uc, us = repacked(up, f, k)
+    edits = [Edit(1, n, [SET, SCALE, ZERO][n % 3], [n * 0.5, -1.75, 0.0][n % 3], 0, 6) for n in range(10, 160)]
+    edits += [Edit(1, 7, SCALE, 1.0, 0, 6), Edit(1, 6911, SET, 10.0, 2, 4), Edit(0, 3, SET, 999.0)]
+    assert check(edits, 3, f).ok
+    words = np.array(table(edits, 3, 40), dtype=np.uint32)
+    td = dev(words.view(np.int32))
+    xd = dev(x)
+    act = torch.empty((m, f), dtype=torch.float32, device="cuda")
+    _native.check(lib.fz_q4_0_gated(gc.data_ptr(), gs.data_ptr(), uc.data_ptr(), us.data_ptr(), f, k, xd.data_ptr(),
+                                    m, td.data_ptr(), 1, position, act.data_ptr(), stream()))
+    got = act.cpu().numpy()
+    want = oracle.edit_apply(words, 1, position, oracle.gated(gate, up, f, k, x))
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
+    # Set and Zero edits land exactly.
+    for e in edits:
+        if e.layer == 1 and e.kind in (SET, ZERO):
+            for r in range(m):
+                if 40 + e.start <= position + r < 40 + e.until:
+                    assert got[r, e.neuron] == np.float32(e.value)

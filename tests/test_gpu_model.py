@@ -1,0 +1,117 @@
+"""Model-level parity through the C ABI on the GPU against the CPU oracle.
+
+The north-star bar: per-layer activations and logits within 1e-2 max-abs and
+1e-3 relative RMS of the oracle's f32, and identical greedy tokens over the
+whole run, unsteered and steered.  BASELINE config 1 is the 26-layer
+Gemma-3-1B-shaped Q4_0 model (seed 0) with 32 prompt tokens, 32-token prefill
+then 32 greedy decode steps; the tiny model runs the same path in seconds."""
+import numpy as np
+import pytest
+
+import oracle
+from frizzle_b200 import engine, synth
+from frizzle_b200.edits import Edit, SET, SCALE, ZERO, check, table
+
+from conftest import max_abs, rel_rms
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, REL_RMS = 1e-2, 1e-3
+
+
+def prompt(shape, n, seed=0):
+    return np.random.default_rng([seed, n]).integers(2, shape.vocab, size=n).astype(np.uint32)
+
+
+def run_both(path, shape, n_prompt, steps, edits=None, capture=True, context=4096):
+    """Greedy decode on the GPU and the oracle; returns per-step comparisons."""
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, path)
+    batch = engine.Batch(model, 1, context)
+    orc = oracle.OracleModel(path, context=context)
+    ids = prompt(shape, n_prompt)
+    words = None
+    if edits:
+        assert check(edits, shape.layers, shape.ffn).ok
+        words = np.array(table(edits, shape.layers, n_prompt - 1), dtype=np.uint32)
+        batch.set_edits(0, words)
+    out = {"tokens_gpu": [], "tokens_cpu": [], "logit_rms": [], "logit_abs": [], "cap_rms": [], "cap_abs": []}
+    # Prefill in blocks of 16 (the skinny path's rows), the last asking for logits.
+    pos = 0
+    while pos < n_prompt:
+        t = min(16, n_prompt - pos)
+        last = pos + t == n_prompt
+        batch.step(pos, ids[pos:pos + t], tokens=t, logits=last, capture=capture and last)
+        pos += t
+    want_logits, want_cap = orc.step(0, ids, logits=True, edit_table=words, capture=capture)
+    for i in range(steps):
+        tok = batch.tokens()[0]
+        got = batch.logits(0)
+        out["tokens_gpu"].append(tok)
+        out["tokens_cpu"].append(int(np.argmax(want_logits)))
+        out["logit_rms"].append(rel_rms(got, want_logits))
+        out["logit_abs"].append(max_abs(got, want_logits))
+        if capture and i == 0:
+            cap = batch.capture(0)
+            out["cap_rms"].append(rel_rms(cap, want_cap))
+            out["cap_abs"].append(max_abs(cap, want_cap))
+            out["cap_layers"] = (cap, want_cap)
+        if i + 1 < steps:
+            nxt = out["tokens_cpu"][-1]
+            batch.step(n_prompt + i, fed=True, tokens=1, logits=True)
+            want_logits, _ = orc.step(n_prompt + i, [nxt], logits=True, edit_table=words)
+    kv = []
+    for layer in (0, shape.pattern - 1):
+        ptr, slots = batch.cache(0, layer)
+        kv.append((layer, ptr, slots))
+    orc.close()
+    batch.free()
+    model.free()
+    dev.close()
+    return out
+
+
+def assert_parity(out):
+    assert out["tokens_gpu"] == out["tokens_cpu"], (out["tokens_gpu"], out["tokens_cpu"])
+    assert max(out["logit_rms"]) < REL_RMS, max(out["logit_rms"])
+    assert max(out["logit_abs"]) < MAX_ABS, max(out["logit_abs"])
+    if out["cap_rms"]:
+        assert max(out["cap_rms"]) < REL_RMS
+        assert max(out["cap_abs"]) < MAX_ABS
+
+
+def test_tiny_model_greedy(tiny_model_path):
+    assert_parity(run_both(tiny_model_path, synth.TINY, 21, 12))
+
+
+def test_tiny_model_steered(tiny_model_path):
+    s = synth.TINY
+    edits = [Edit(3, 5, SET, 8.0, 0), Edit(3, 100, SCALE, -2.5, 1), Edit(3, 900, ZERO, 0.0, 0, 3),
+             Edit(6, 17, SET, -10.0, 2, 5)]
+    out = run_both(tiny_model_path, s, 9, 8, edits=edits)
+    assert_parity(out)
+    cap, _ = out["cap_layers"]
+    per = 3 * s.hidden + s.heads * s.head_dim + s.ffn
+    neurons = cap[3 * per + 2 * s.hidden + s.heads * s.head_dim:][:s.ffn]
+    assert neurons[5] == np.float32(8.0) and neurons[900] == 0.0
+
+
+def test_tiny_model_long_prompt_wraps_window(tiny_model_path):
+    # 70 prompt tokens: the window layers (16 keys) read a sliding range and the
+    # prefill crosses several 16-token blocks.
+    assert_parity(run_both(tiny_model_path, synth.TINY, 70, 6))
+
+
+def test_gemma_1b_config1_greedy(gemma_model_path):
+    out = run_both(gemma_model_path, synth.GEMMA3_1B, 32, 32, capture=True)
+    assert_parity(out)
+
+
+def test_gemma_1b_config1_steered(gemma_model_path):
+    s = synth.GEMMA3_1B
+    rng = np.random.default_rng(13)
+    idx = rng.choice(s.ffn, size=8, replace=False)
+    vals = rng.uniform(-10, 10, size=8).astype(np.float32)
+    edits = [Edit(13, int(i), SET, float(v), 0) for i, v in zip(idx, vals)]
+    out = run_both(gemma_model_path, s, 32, 32, edits=edits, capture=True)
+    assert_parity(out)
