@@ -319,6 +319,7 @@ Split split_for(uint32_t n, uint32_t k, uint32_t m, int epi) {
   while ((size_t)2 * ((nbp + s.cluster - 1) / s.cluster) * 2 * mq * 32 * 8 > 110 * 1024 && s.cluster < 8)
     s.cluster *= 2;
   if (n / 16 < 100 && nbp >= 64 && s.cluster < 2) s.cluster = 2;
+  if (const char* v = std::getenv("FRIZZLE_B200_CLUSTER")) s.cluster = (uint32_t)std::max(1, std::atoi(v));
   return s;
 }
 
