@@ -337,7 +337,9 @@ cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStrea
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelExC(&cfg, fn, args);
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return e;
 }
 
 }  // namespace

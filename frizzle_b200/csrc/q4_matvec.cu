@@ -13,6 +13,8 @@
 // not bit for bit.
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "q4_matvec.cuh"
 
 namespace cg = cooperative_groups;
@@ -570,7 +572,9 @@ cudaError_t launch_one(const MatvecArgs& a, cudaStream_t stream, bool pdl) {
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, matvec_kernel<MQ, PRO, EPI>, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, matvec_kernel<MQ, PRO, EPI>, a);
+  if (e != cudaSuccess) (void)cudaGetLastError();  // the error is returned, not left behind
+  return e;
 }
 
 template <int MQ, int PRO, int EPI>
@@ -612,8 +616,25 @@ cudaError_t configure_kernels() {
   return configure_mq<kPrologueNorm, kEpilogueHead>();
 }
 
+// Raises the shared-memory limits once per device, on first use there.
+cudaError_t ensure_configured() {
+  static std::mutex mu;
+  static bool done[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev]) return cudaSuccess;
+  e = configure_kernels();
+  if (e == cudaSuccess) done[dev] = true;
+  return e;
+}
+
 cudaError_t launch_matvec(const MatvecArgs& a, int prologue, int epilogue, cudaStream_t stream, bool pdl) {
   if (a.m < 1 || a.m > (uint32_t)kMaxTokens) return cudaErrorInvalidValue;
+  cudaError_t ce = ensure_configured();
+  if (ce != cudaSuccess) return ce;
   if (prologue == kPrologueInput) {
     switch (epilogue) {
       case kEpilogueWrite: return launch_mq<kPrologueInput, kEpilogueWrite>(a, stream, pdl);
@@ -637,6 +658,7 @@ cudaError_t launch_repack(const uint8_t* file_blocks, uint32_t n, uint32_t k, ui
   if (n % 16 || k % 64) return cudaErrorInvalidValue;
   const size_t total = (size_t)(n / 16) * (k / 64) * 32;
   const int blocks = (int)std::min<size_t>((total + 255) / 256, 148 * 16);
+  (void)cudaGetLastError();
   repack_kernel<<<blocks, 256, 0, stream>>>(file_blocks, n, k, codes, scales);
   return cudaGetLastError();
 }
@@ -644,6 +666,7 @@ cudaError_t launch_repack(const uint8_t* file_blocks, uint32_t n, uint32_t k, ui
 cudaError_t launch_dequant_rows(const Q4Matrix& mat, const uint32_t* rows, uint32_t count, float scale, float* out,
                                 cudaStream_t stream) {
   if (count == 0) return cudaSuccess;
+  (void)cudaGetLastError();
   dequant_rows_kernel<<<count, 256, 0, stream>>>(mat, rows, count, scale, out);
   return cudaGetLastError();
 }

@@ -115,7 +115,7 @@ def test_gated_with_edits(m, position):
     gc, gs = repacked(gate, f, k)
     uc, us = repacked(up, f, k)
     edits = [Edit(1, n, [SET, SCALE, ZERO][n % 3], [n * 0.5, -1.75, 0.0][n % 3], 0, 6) for n in range(10, 160)]
-    edits += [Edit(1, 7, SCALE, 1.0, 0, 6), Edit(1, 6911, SET, 10.0, 2, 4), Edit(0, 3, SET, 999.0)]
+    edits += [Edit(1, 7, SCALE, 1.0, 0, 6), Edit(1, 6911, SET, 10.0, 2, 4), Edit(0, 3, SET, 999.0, 0)]
     assert check(edits, 3, f).ok
     words = np.array(table(edits, 3, 40), dtype=np.uint32)
     td = dev(words.view(np.int32))
