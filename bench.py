@@ -254,6 +254,19 @@ def run_ours(args):
         batch.step(pos, fed=True, tokens=1, logits=True)
         batch.wait()
         pos += 1
+    if args.profile_steps:
+        # Only the decode steps run between the profiler marks (for ncu --profile-from-start off).
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        for i in range(args.profile_steps):
+            batch.step(pos + i, fed=True, tokens=1, logits=True)
+        batch.wait()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        batch.free()
+        model.free()
+        dev.close()
+        return 0
     K = args.steps
     if dist:
         dist.barrier()
@@ -332,6 +345,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
