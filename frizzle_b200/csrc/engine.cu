@@ -310,9 +310,11 @@ struct Split {
 
 Split split_for(uint32_t n, uint32_t k, uint32_t m, int epi) {
   const uint32_t nbp = k / 64;
-  if (epi == fz::kEpilogueGated) return {2, std::min<uint32_t>(4, std::max<uint32_t>(1, nbp / 2)), 1};
+  // Eight warps a CTA: a gated pair splits K four ways; the head streams
+  // whole row groups, one a warp; everything else splits K eight ways.
+  if (epi == fz::kEpilogueGated) return {2, 4, 1};
   if (epi == fz::kEpilogueHead) return {8, 1, 1};
-  Split s{1, std::min<uint32_t>(8, std::max<uint32_t>(1, nbp / 2)), 1};
+  Split s{1, 8, 1};
   const uint32_t mq = (m + 3) / 4;
   // Keep each CTA's share of X fragments under ~110 KB of shared memory, and
   // give narrow products with long rows enough CTAs.

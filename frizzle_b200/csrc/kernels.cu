@@ -8,7 +8,6 @@ namespace fz {
 namespace {
 
 constexpr int kHeadDim = 256;    // Gemma 3's d: one thread a dimension
-constexpr int kMaxGroup = 8;     // query heads sharing a KV head
 
 // ------------------------------------------------------------ attention
 //
@@ -21,14 +20,14 @@ constexpr int kMaxGroup = 8;     // query heads sharing a KV head
 // in split order and divides (the combine, attention.wgsl:403-438).  The
 // fold factors keep the side holding the maximum at exactly 1
 // (fold_factors, attention.wgsl:135-151).
+template <int G>
 __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
-  __shared__ float sc[kMaxGroup][512];      // scores, then weights
-  __shared__ float red[kMaxGroup][8];
-  __shared__ float s_m[kMaxGroup], s_l[kMaxGroup];
+  __shared__ float sc[G][512];      // scores, then weights
+  __shared__ float red[G][8];
+  __shared__ float s_m[G], s_l[G];
   __shared__ uint32_t s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t row = blockIdx.z, kvh = blockIdx.y, split = blockIdx.x;
-  const int G = (int)(a.heads / a.kv_heads);
   pdl_wait();
   const uint32_t p = (a.step ? a.step->position : a.position) + row % a.seq_tokens;
   const uint32_t seq = row / a.seq_tokens;
@@ -41,9 +40,11 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
   const int n = (int)(j1 - j0);
   const uint16_t* kc = a.key_cache + seq * a.seq_stride;
   const uint16_t* vc = a.value_cache + seq * a.seq_stride;
+  auto slot_of = [&](int jj) { return (size_t)((j0 + (uint32_t)jj) % a.slots) * a.kv_heads + kvh; };
 
   // q for the group, dims 8*lane .. 8*lane+7, times scale*log2(e).
-  float qv[kMaxGroup][8];
+  float qv[G][8];
+#pragma unroll
   for (int h = 0; h < G; h++) {
     const float* q = a.q + ((size_t)row * a.heads + kvh * G + h) * kHeadDim + 8 * lane;
     const float4 x0 = reinterpret_cast<const float4*>(q)[0], x1 = reinterpret_cast<const float4*>(q)[1];
@@ -51,29 +52,38 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
 #pragma unroll
     for (int i = 0; i < 8; i++) qv[h][i] = mul(v[i], a.scale_log2e);
   }
-  // Scores: warp w takes keys w, w + 8, ...
-  for (int jj = warp; jj < n; jj += 8) {
-    const uint32_t j = j0 + jj;
-    const uint4 kw = *reinterpret_cast<const uint4*>(kc + ((size_t)(j % a.slots) * a.kv_heads + kvh) * kHeadDim +
-                                                     8 * lane);
-    const uint32_t w4[4] = {kw.x, kw.y, kw.z, kw.w};
-    float k[8];
+  // Scores: each warp takes four keys at a time, loads first.
+  constexpr int KU = 4;
+  for (int base = warp * KU; base < n; base += 8 * KU) {
+    uint4 kw[KU];
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
-      k[2 * i] = f.x;
-      k[2 * i + 1] = f.y;
-    }
-    for (int h = 0; h < G; h++) {
-      float s = 0.f;
+    for (int u = 0; u < KU; u++)
+      if (base + u < n) kw[u] = *reinterpret_cast<const uint4*>(kc + slot_of(base + u) * kHeadDim + 8 * lane);
 #pragma unroll
-      for (int i = 0; i < 8; i++) s = __fmaf_rn(qv[h][i], k[i], s);
-      s = warp_sum(s);
-      if (lane == 0) sc[h][jj] = s;
+    for (int u = 0; u < KU; u++) {
+      if (base + u < n) {
+        const uint32_t w4[4] = {kw[u].x, kw[u].y, kw[u].z, kw[u].w};
+        float k[8];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w4[i]));
+          k[2 * i] = f.x;
+          k[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; i++) s = __fmaf_rn(qv[h][i], k[i], s);
+          s = warp_sum(s);
+          if (lane == 0) sc[h][base + u] = s;
+        }
+      }
     }
   }
   __syncthreads();
   // Per head: maximum, weights exp2(s - m), sum.
+#pragma unroll
   for (int h = 0; h < G; h++) {
     float m = -INFINITY;
     for (int jj = tid; jj < n; jj += 256) m = fmaxf(m, sc[h][jj]);
@@ -87,6 +97,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
     s_m[tid] = m;
   }
   __syncthreads();
+#pragma unroll
   for (int h = 0; h < G; h++) {
     float l = 0.f;
     for (int jj = tid; jj < n; jj += 256) {
@@ -104,20 +115,29 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
     s_l[tid] = l;
   }
   __syncthreads();
-  // O = sum_j w_j v_j, thread tid the dimension tid.
-  float o[kMaxGroup];
+  // O = sum_j w_j v_j, thread tid the dimension tid, eight keys' loads at a time.
+  float o[G];
+#pragma unroll
   for (int h = 0; h < G; h++) o[h] = 0.f;
-  for (int jj = 0; jj < n; jj++) {
-    const uint32_t j = j0 + jj;
-    const float v = f16_unpack(vc[((size_t)(j % a.slots) * a.kv_heads + kvh) * kHeadDim + tid]);
-    for (int h = 0; h < G; h++) o[h] = __fmaf_rn(sc[h][jj], v, o[h]);
+  constexpr int VU = 8;
+  for (int base = 0; base < n; base += VU) {
+    float v[VU];
+#pragma unroll
+    for (int u = 0; u < VU; u++) v[u] = base + u < n ? f16_unpack(vc[slot_of(base + u) * kHeadDim + tid]) : 0.f;
+#pragma unroll
+    for (int u = 0; u < VU; u++)
+      if (base + u < n)
+#pragma unroll
+        for (int h = 0; h < G; h++) o[h] = __fmaf_rn(sc[h][base + u], v[u], o[h]);
   }
   pdl_launch_dependents();
   if (nsplits == 1) {
+#pragma unroll
     for (int h = 0; h < G; h++)
       a.out[((size_t)row * a.heads + kvh * G + h) * kHeadDim + tid] = __fdiv_rn(o[h], s_l[h]);
     return;
   }
+#pragma unroll
   for (int h = 0; h < G; h++) {
     const size_t at = ((size_t)row * a.heads + kvh * G + h) * a.splits + split;
     a.partial_o[at * kHeadDim + tid] = o[h];
@@ -134,6 +154,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();
+#pragma unroll
   for (int h = 0; h < G; h++) {
     const size_t base = ((size_t)row * a.heads + kvh * G + h) * a.splits;
     float m = -INFINITY;
@@ -345,12 +366,19 @@ cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStrea
 }  // namespace
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.head_dim != kHeadDim || a.heads % a.kv_heads || a.heads / a.kv_heads > kMaxGroup || a.split_keys > 512 ||
+  if (a.head_dim != kHeadDim || a.heads % a.kv_heads || a.heads / a.kv_heads > 8 || a.split_keys > 512 ||
       a.split_keys == 0)
     return cudaErrorInvalidValue;
   AttentionArgs copy = a;
   void* args[] = {&copy};
-  return launch((const void*)attention_kernel, dim3(a.splits, a.kv_heads, a.m), dim3(256), 0, stream, pdl, args);
+  const dim3 grid(a.splits, a.kv_heads, a.m);
+  switch (a.heads / a.kv_heads) {
+    case 1: return launch((const void*)attention_kernel<1>, grid, dim3(256), 0, stream, pdl, args);
+    case 2: return launch((const void*)attention_kernel<2>, grid, dim3(256), 0, stream, pdl, args);
+    case 4: return launch((const void*)attention_kernel<4>, grid, dim3(256), 0, stream, pdl, args);
+    case 8: return launch((const void*)attention_kernel<8>, grid, dim3(256), 0, stream, pdl, args);
+  }
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t stream, bool pdl) {

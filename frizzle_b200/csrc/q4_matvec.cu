@@ -13,6 +13,7 @@
 // not bit for bit.
 #include <cooperative_groups.h>
 
+#include <map>
 #include <mutex>
 
 #include "q4_matvec.cuh"
@@ -57,10 +58,6 @@ FZ_DEV uint2 ld_stream2(const uint2* p) {
   asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
 }
-FZ_DEV void prefetch_l2(const void* p, uint32_t bytes) {
-  if (bytes) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // hi/lo f16 pair of an f32 value.
 FZ_DEV void split_hi_lo(float v, __half& hi, __half& lo) {
   hi = __float2half_rn(v);
@@ -105,99 +102,171 @@ FZ_DEV void build_fragments(uint2* xf, int MQ, int row, const float* src, int kb
   }
 }
 
-// One warp's sums for its row group over block pairs [bp0, bp1): lane (g, t)
-// ends with acc[q][0] = row g and acc[q][1] = row g + 8 against X row 4q + t.
+constexpr int kThreads = 256;   // every matvec CTA: 8 warps, the norm's 256 invocations
+constexpr int kWarps = kThreads / 32;
+constexpr int kU = 4;           // block pairs a warp loads at once
+
+// A warp's registers for kU block pairs of one row group.
+struct Batch {
+  uint4 c[kU];
+  uint2 s[kU];
+};
+
+FZ_DEV void load_batch(const uint4* codes, const uint2* scales, int bp, int bp1, int lane, Batch& b) {
+  const int g = lane >> 2;
+#pragma unroll
+  for (int u = 0; u < kU; u++) {
+    if (bp + u < bp1) {
+      b.c[u] = ld_stream(codes + (size_t)(bp + u) * 32 + lane);
+      b.s[u] = ld_stream2(scales + (size_t)(bp + u) * 8 + g);
+    }
+  }
+}
+
+// The batch's products into acc: lane (g, t) accumulates rows g (acc[q][0])
+// and g + 8 (acc[q][1]) against X row 4q + t.
 template <int MQ>
-FZ_DEV void rowgroup_dot(const uint4* codes, const uint2* scales, int bp0, int bp1, const uint2* xf,
-                         int kb_base, int lane, float acc[MQ][2]) {
+FZ_DEV void compute_batch(const Batch& b, int bp, int bp1, const uint2* xf, int kb_base, int lane, float acc[MQ][2]) {
   const int g = lane >> 2, t = lane & 3;
   const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-  constexpr int U = 4;
-  for (int bp = bp0; bp < bp1; bp += U) {
-    uint4 c[U];
-    uint2 s[U];
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      if (bp + u < bp1) {
-        c[u] = ld_stream(codes + (size_t)(bp + u) * 32 + lane);
-        s[u] = ld_stream2(scales + (size_t)(bp + u) * 8 + g);
-      }
-    }
+  for (int u = 0; u < kU; u++) {
+    if (bp + u < bp1) {
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      if (bp + u < bp1) {
+      for (int kbi = 0; kbi < 2; kbi++) {
+        const int kb_rel = 2 * (bp + u) + kbi - kb_base;
+        uint32_t a0[4], a1[4];
+        dequant_word(kbi ? b.c[u].z : b.c[u].x, a0);
+        dequant_word(kbi ? b.c[u].w : b.c[u].y, a1);
+        const uint32_t sw = kbi ? b.s[u].y : b.s[u].x;
+        const float dg = __half2float(__ushort_as_half((unsigned short)(sw & 0xffffu)));
+        const float dg8 = __half2float(__ushort_as_half((unsigned short)(sw >> 16)));
 #pragma unroll
-        for (int kbi = 0; kbi < 2; kbi++) {
-          const int kb_rel = 2 * (bp + u) + kbi - kb_base;
-          uint32_t a0[4], a1[4];
-          dequant_word(kbi ? c[u].z : c[u].x, a0);
-          dequant_word(kbi ? c[u].w : c[u].y, a1);
-          const uint32_t sw = kbi ? s[u].y : s[u].x;
-          const float dg = __half2float(__ushort_as_half((unsigned short)(sw & 0xffffu)));
-          const float dg8 = __half2float(__ushort_as_half((unsigned short)(sw >> 16)));
-#pragma unroll
-          for (int q = 0; q < MQ; q++) {
-            const uint2 b0 = xf[xf_index(kb_rel, 0, q, MQ, t, g)];
-            const uint2 b1 = xf[xf_index(kb_rel, 1, q, MQ, t, g)];
-            float d[4];
-            mma16816(d, a0, b0, zero);
-            mma16816(d, a1, b1, d);
-            acc[q][0] = __fmaf_rn(dg, d[0] + d[1], acc[q][0]);
-            acc[q][1] = __fmaf_rn(dg8, d[2] + d[3], acc[q][1]);
-          }
+        for (int q = 0; q < MQ; q++) {
+          const uint2 b0 = xf[xf_index(kb_rel, 0, q, MQ, t, g)];
+          const uint2 b1 = xf[xf_index(kb_rel, 1, q, MQ, t, g)];
+          float d[4];
+          mma16816(d, a0, b0, zero);
+          mma16816(d, a1, b1, d);
+          acc[q][0] = __fmaf_rn(dg, d[0] + d[1], acc[q][0]);
+          acc[q][1] = __fmaf_rn(dg8, d[2] + d[3], acc[q][1]);
         }
       }
     }
   }
 }
 
-// The norm of one row by one warp into `buf` (norm.wgsl:97-198): y through
-// its post-norm added into x, then (x * r) * gain.  `buf` ends holding the
-// normed row; `xout` and `xcap` (if non-null) receive x after the add, `yadd`
-// y as added.
-FZ_DEV void norm_row_warp(const NormArgs& n, int row, float* buf, float* xout, float* xcap, float* yadd,
-                          int lane) {
-  const int W = n.width, V = W / 4;
-  float4* b4 = reinterpret_cast<float4*>(buf);
-  const float inv_n = (float)W;
-  if (n.y) {
-    const float4* y4 = reinterpret_cast<const float4*>(n.y + (size_t)row * W);
-    for (int v = lane; v < V; v += 32) b4[v] = y4[v];
-    __syncwarp();
-    if (n.post_gain) {
-      const float r = inverse_sqrt(add(__fdiv_rn(norm_sum_squares_warp(b4, V, lane), inv_n), n.eps));
-      const float4* pg = reinterpret_cast<const float4*>(n.post_gain);
-      __syncwarp();
-      for (int v = lane; v < V; v += 32) {
-        float4 y = b4[v], p = pg[v];
-        b4[v] = make_float4(mul(mul(y.x, r), p.x), mul(mul(y.y, r), p.y), mul(mul(y.z, r), p.z),
-                            mul(mul(y.w, r), p.w));
+// One warp's sums for its row group over block pairs [bp0, bp1), two register
+// batches in flight: `first` already holds the batch at bp0.
+template <int MQ>
+FZ_DEV void rowgroup_dot(const uint4* codes, const uint2* scales, int bp0, int bp1, const uint2* xf, int kb_base,
+                         int lane, Batch& first, float acc[MQ][2]) {
+  Batch second;
+  for (int bp = bp0; bp < bp1; bp += 2 * kU) {
+    if (bp + kU < bp1) load_batch(codes, scales, bp + kU, bp1, lane, second);
+    compute_batch<MQ>(first, bp, bp1, xf, kb_base, lane, acc);
+    if (bp + kU < bp1) {
+      if (bp + 2 * kU < bp1) load_batch(codes, scales, bp + 2 * kU, bp1, lane, first);
+      compute_batch<MQ>(second, bp + kU, bp1, xf, kb_base, lane, acc);
+    }
+  }
+}
+
+// The reference norm's fixed-order tree over the CTA's 256 invocations, for
+// `rows` rows at once (norm.wgsl:75-85): part[r][i] holds invocation i's sum;
+// halving levels 128, 64, 32 in shared memory, the last five inside a warp.
+// Leaves each row's total in total[r].
+FZ_DEV void tree_reduce(float* part, int rows, float* total) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __syncthreads();
+  for (int stride = 128; stride >= 32; stride >>= 1) {
+    for (int idx = tid; idx < rows * stride; idx += kThreads) {
+      const int r = idx / stride, i = idx % stride;
+      part[r * kThreads + i] = add(part[r * kThreads + i], part[r * kThreads + i + stride]);
+    }
+    __syncthreads();
+  }
+  for (int r = warp; r < rows; r += kWarps) {
+    float s = part[r * kThreads + lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float other = __shfl_down_sync(0xffffffffu, s, o);
+      if (lane < o) s = add(s, other);
+    }
+    if (lane == 0) total[r] = s;
+  }
+  __syncthreads();
+}
+
+// The norm launch over the step's rows, by the whole CTA (norm.wgsl:97-198):
+// invocation i of the reference is thread i, holding vec4s i, i + 256, ...
+// Leaves the normed rows in `rowbuf` [rows][width]; CTA 0 writes X after the
+// add to hidden_out and the captures of each sequence's last row.
+FZ_DEV void norm_rows_cta(const MatvecArgs& a, int rows, float* rowbuf, float* part, float* stat) {
+  const NormArgs& n = a.norm;
+  const int tid = threadIdx.x, W = (int)n.width, V = W / 4;
+  const float wf = (float)W;
+  const bool writer = blockIdx.x == 0;
+  float* ry = stat;
+  float* rx = stat + kMaxTokens;
+  auto hrow_of = [&](int r) { return r * (int)n.row_of_token_stride + (int)n.row_of_token_offset; };
+  if (n.y && n.post_gain) {
+    for (int r = 0; r < rows; r++) {
+      const float4* y4 = reinterpret_cast<const float4*>(n.y + (size_t)hrow_of(r) * W);
+      float p = 0.f;
+      for (int v = tid; v < V; v += kThreads) p = add(p, dot_self(y4[v]));
+      part[r * kThreads + tid] = p;
+    }
+    tree_reduce(part, rows, ry);
+    if (tid < rows) ry[tid] = inverse_sqrt(add(__fdiv_rn(ry[tid], wf), n.eps));
+    __syncthreads();
+  }
+  for (int r = 0; r < rows; r++) {
+    const int hrow = hrow_of(r);
+    const uint32_t seq = (uint32_t)hrow / a.seq_tokens;
+    const bool last = (uint32_t)hrow % a.seq_tokens == a.seq_tokens - 1;
+    const float4* x4 = reinterpret_cast<const float4*>(n.hidden_in + (size_t)hrow * W);
+    const float4* y4 = n.y ? reinterpret_cast<const float4*>(n.y + (size_t)hrow * W) : nullptr;
+    const float4* pg4 = reinterpret_cast<const float4*>(n.post_gain);
+    float4* out4 = writer && n.hidden_out ? reinterpret_cast<float4*>(n.hidden_out + (size_t)hrow * W) : nullptr;
+    float4* xcap = writer && last && n.capture_residual
+                       ? reinterpret_cast<float4*>(n.capture_residual + seq * a.capture_stride) : nullptr;
+    float4* ycap = writer && last && n.capture_added
+                       ? reinterpret_cast<float4*>(n.capture_added + seq * a.capture_stride) : nullptr;
+    float4* buf = reinterpret_cast<float4*>(rowbuf + (size_t)r * W);
+    float p = 0.f;
+    for (int v = tid; v < V; v += kThreads) {
+      float4 x = x4[v];
+      if (y4) {
+        float4 y = y4[v];
+        if (n.post_gain) {
+          const float s = ry[r];
+          const float4 g = pg4[v];
+          y = make_float4(mul(mul(y.x, s), g.x), mul(mul(y.y, s), g.y), mul(mul(y.z, s), g.z), mul(mul(y.w, s), g.w));
+        }
+        if (ycap) ycap[v] = y;
+        x = make_float4(add(x.x, y.x), add(x.y, y.y), add(x.z, y.z), add(x.w, y.w));
       }
+      if (out4) out4[v] = x;
+      if (xcap) xcap[v] = x;
+      buf[v] = x;
+      p = add(p, dot_self(x));
     }
-    const float4* x4 = reinterpret_cast<const float4*>(n.hidden_in + (size_t)row * W);
-    for (int v = lane; v < V; v += 32) {
-      float4 y = b4[v], x = x4[v];
-      if (yadd) reinterpret_cast<float4*>(yadd)[v] = y;
-      b4[v] = make_float4(add(x.x, y.x), add(x.y, y.y), add(x.z, y.z), add(x.w, y.w));
-    }
-  } else {
-    const float4* x4 = reinterpret_cast<const float4*>(n.hidden_in + (size_t)row * W);
-    for (int v = lane; v < V; v += 32) b4[v] = x4[v];
+    part[r * kThreads + tid] = p;
   }
-  __syncwarp();
-  if (xout)
-    for (int v = lane; v < V; v += 32) reinterpret_cast<float4*>(xout)[v] = b4[v];
-  if (xcap)
-    for (int v = lane; v < V; v += 32) reinterpret_cast<float4*>(xcap)[v] = b4[v];
-  const float r = inverse_sqrt(add(__fdiv_rn(norm_sum_squares_warp(b4, V, lane), inv_n), n.eps));
-  __syncwarp();
+  tree_reduce(part, rows, rx);
+  if (tid < rows) rx[tid] = inverse_sqrt(add(__fdiv_rn(rx[tid], wf), n.eps));
+  __syncthreads();
   const float4* g4 = reinterpret_cast<const float4*>(n.gain);
-  for (int v = lane; v < V; v += 32) {
-    float4 x = b4[v], gg = g4[v];
-    b4[v] = make_float4(mul(mul(x.x, r), gg.x), mul(mul(x.y, r), gg.y), mul(mul(x.z, r), gg.z),
-                        mul(mul(x.w, r), gg.w));
+  for (int r = 0; r < rows; r++) {
+    float4* buf = reinterpret_cast<float4*>(rowbuf + (size_t)r * W);
+    const float s = rx[r];
+    for (int v = tid; v < V; v += kThreads) {
+      const float4 x = buf[v], g = g4[v];
+      buf[v] = make_float4(mul(mul(x.x, s), g.x), mul(mul(x.y, s), g.y), mul(mul(x.z, s), g.z), mul(mul(x.w, s), g.w));
+    }
   }
-  __syncwarp();
+  __syncthreads();
 }
 
 // QK-norm, RoPE and the f16 KV append for one (row, head) by one warp
@@ -282,170 +351,240 @@ FZ_DEV float apply_edits(const uint32_t* table, uint32_t layer, uint32_t neuron,
   return v;
 }
 
+// Shared memory of one CTA, carved from the dynamic allocation.
 struct Smem {
-  uint2* xf;
-  float* red;
-  float* rowbuf;
-  float* cred;
+  uint2* xf;       // X fragments of the CTA's K range
+  float* red;      // [RG][KS][16 rows][16 tokens] K-split partials
+  float* rowbuf;   // [m][width] normed rows (norm prologue)
+  float* part;     // [m][256] the norm tree's partials
+  float* stat;     // 2 x kMaxTokens reciprocal RMS values
+  float* cred;     // [C][outs] cluster partials (rank 0's is the one read)
 };
 
+struct Geometry {
+  uint32_t C, KS, RG, rank, NBP, nrowsets;
+  int kb_base, nkb, nkb_max;
+};
+
+template <int MQ, int PRO>
+FZ_DEV Smem carve(unsigned char* raw, const MatvecArgs& a, const Geometry& geo) {
+  Smem s;
+  s.xf = reinterpret_cast<uint2*>(raw);
+  s.red = reinterpret_cast<float*>(s.xf + (size_t)geo.nkb_max * 2 * MQ * 32);
+  s.rowbuf = s.red + geo.RG * geo.KS * 256;
+  s.part = s.rowbuf + (PRO == kPrologueNorm ? (size_t)a.m * a.norm.width : 0);
+  s.stat = s.part + (PRO == kPrologueNorm ? (size_t)a.m * kThreads : 0);
+  s.cred = s.stat + 2 * kMaxTokens;
+  return s;
+}
+
+// X rows as B fragments for the CTA's blocks [kb_base, kb_base + nkb): from
+// the input rows, or through the norm.
+template <int MQ, int PRO>
+FZ_DEV void prologue(const MatvecArgs& a, const Smem& sm, const Geometry& geo) {
+  const int M = (int)a.m, K = (int)a.mat[0].k;
+  const float* rows = a.x;
+  if (PRO == kPrologueNorm) {
+    norm_rows_cta(a, M, sm.rowbuf, sm.part, sm.stat);
+    rows = sm.rowbuf;
+  }
+  for (int r = 0; r < 4 * MQ; r++)
+    build_fragments(sm.xf, MQ, r, r < M ? rows + (size_t)r * K : nullptr, geo.kb_base, geo.nkb, threadIdx.x,
+                    kThreads);
+  __syncthreads();
+}
+
+// Writes one finished output (row n of the product, X row `tok`).
+template <int EPI>
+FZ_DEV void write_out(const MatvecArgs& a, uint32_t n, int tok, float v) {
+  a.out[(size_t)tok * a.out_stride + n] = v;
+}
+
+FZ_DEV unsigned long long head_key(float v, uint32_t n) {
+  return ((unsigned long long)topk_key(__float_as_uint(v)) << 32) | (0xFFFFFFFFu - n);
+}
+
 template <int MQ, int PRO, int EPI>
-__global__ void __launch_bounds__(256) matvec_kernel(const MatvecArgs a) {
+__global__ void __launch_bounds__(kThreads) matvec_kernel(const MatvecArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ uint32_t s_last;
   __shared__ unsigned long long s_best[kMaxTokens];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
-  const uint32_t C = a.cluster, KS = a.k_split, RG = a.rg_per_cta;
-  uint32_t rank = 0;
-  if (C > 1) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
-  const uint32_t rowset = blockIdx.x / C;
-  const uint32_t K = a.mat[0].k, NBP = K / 64;
-  const uint32_t rgl = warp / KS, ks = warp % KS;
-  const uint32_t S = KS * C, slice = rank * KS + ks;
-  const int bp0 = (int)(slice * NBP / S), bp1 = (int)((slice + 1) * NBP / S);
-  const int cta_bp0 = (int)(rank * NBP / C), cta_bp1 = (int)((rank + 1) * NBP / C);
-  const int kb_base = 2 * cta_bp0, nkb = 2 * (cta_bp1 - cta_bp0);
+  const int g = lane >> 2, t = lane & 3;
   const int M = (int)a.m;
+  Geometry geo;
+  geo.C = a.cluster;
+  geo.KS = a.k_split;
+  geo.RG = a.rg_per_cta;
+  geo.rank = 0;
+  if (geo.C > 1) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(geo.rank));
+  geo.NBP = a.mat[0].k / 64;
+  geo.nrowsets = EPI == kEpilogueGated ? a.mat[0].n / 16 : (a.mat[0].n / 16 + geo.RG - 1) / geo.RG;
+  const int cta_bp0 = (int)(geo.rank * geo.NBP / geo.C), cta_bp1 = (int)((geo.rank + 1) * geo.NBP / geo.C);
+  geo.kb_base = 2 * cta_bp0;
+  geo.nkb = 2 * (cta_bp1 - cta_bp0);
+  geo.nkb_max = 2 * (int)((geo.NBP + geo.C - 1) / geo.C);
+  const Smem sm = carve<MQ, PRO>(smem_raw, a, geo);
+  if (threadIdx.x < kMaxTokens) s_best[threadIdx.x] = 0ull;
 
-  const Q4Matrix& mat = (EPI == kEpilogueGated) ? a.mat[rgl & 1] : a.mat[0];
-  const uint32_t rg = (EPI == kEpilogueGated) ? rowset : rowset * RG + rgl;
-  const bool live = rgl < RG && rg < mat.n / 16;
-  const uint4* codes = mat.codes + (size_t)rg * NBP * 32;
-  const uint2* scales = mat.scales + (size_t)rg * NBP * 8;
-
-  // Smem carve-up.
-  const int nkb_max = 2 * (int)((NBP + C - 1) / C);
-  Smem sm;
-  sm.xf = reinterpret_cast<uint2*>(smem_raw);
-  sm.red = reinterpret_cast<float*>(sm.xf + nkb_max * 2 * MQ * 32);
-  sm.rowbuf = sm.red + RG * KS * 256;
-  const int norm_warps = PRO == kPrologueNorm ? min(nwarps, M) : 0;
-  sm.cred = sm.rowbuf + norm_warps * (int)a.norm.width;
-
-  // Weights do not depend on the previous kernel: start them toward L2 now.
-  if (live && lane == 0) {
-    prefetch_l2(codes + (size_t)bp0 * 32, (uint32_t)(bp1 - bp0) * 512u);
-    prefetch_l2(scales + (size_t)bp0 * 8, (uint32_t)(bp1 - bp0) * 64u);
-  }
-  pdl_wait();
-
-  // X rows as B fragments.
-  const int rows_padded = 4 * MQ;
-  if (PRO == kPrologueInput) {
-    for (int r = 0; r < rows_padded; r++)
-      build_fragments(sm.xf, MQ, r, r < M ? a.x + (size_t)r * K : nullptr, kb_base, nkb, threadIdx.x,
-                      blockDim.x);
-  } else {
-    const NormArgs& n = a.norm;
-    const bool writer = blockIdx.x == 0;
-    for (int r0 = 0; r0 < rows_padded; r0 += norm_warps) {
-      if (warp < norm_warps && r0 + warp < M) {
-        const int r = r0 + warp;
-        const int hrow = r * (int)n.row_of_token_stride + (int)n.row_of_token_offset;
-        const uint32_t seq = (uint32_t)hrow / a.seq_tokens;
-        const bool last_row = (uint32_t)hrow % a.seq_tokens == a.seq_tokens - 1;
-        float* xout = writer && n.hidden_out ? n.hidden_out + (size_t)hrow * K : nullptr;
-        float* yadd = writer && last_row && n.capture_added ? n.capture_added + seq * a.capture_stride : nullptr;
-        float* xcap =
-            writer && last_row && n.capture_residual ? n.capture_residual + seq * a.capture_stride : nullptr;
-        norm_row_warp(n, hrow, sm.rowbuf + warp * K, xout, xcap, yadd, lane);
-      }
-      __syncthreads();
-      for (int w = 0; w < norm_warps && r0 + w < rows_padded; w++) {
-        const int r = r0 + w;
-        build_fragments(sm.xf, MQ, r, r < M ? sm.rowbuf + w * K : nullptr, kb_base, nkb, threadIdx.x,
-                        blockDim.x);
-      }
-      __syncthreads();
-    }
-    if (norm_warps == 0) {
-      for (int r = 0; r < rows_padded; r++)
-        build_fragments(sm.xf, MQ, r, nullptr, kb_base, nkb, threadIdx.x, blockDim.x);
-    }
-  }
-  __syncthreads();
-
+  const bool warp_mode = geo.KS == 1 && geo.C == 1 && EPI != kEpilogueGated;
+  Batch first;
   float acc[MQ][2];
-#pragma unroll
-  for (int q = 0; q < MQ; q++) acc[q][0] = acc[q][1] = 0.f;
-  if (live) rowgroup_dot<MQ>(codes, scales, bp0, bp1, sm.xf, kb_base, lane, acc);
-  pdl_launch_dependents();
 
-  // Reduce the K split inside the CTA: red[rgl][ks][row][token].
-  if (rgl < RG) {
-    const int g = lane >> 2, t = lane & 3;
-    float* red = sm.red + (rgl * KS + ks) * 256;
+  if (warp_mode) {
+    // Each warp streams whole row groups on its own; no CTA barrier in the loop.
+    const uint32_t nrg = a.mat[0].n / 16, NBP = geo.NBP;
+    const uint32_t total = gridDim.x * kWarps;
+    uint32_t rg = blockIdx.x * kWarps + warp;
+    const Q4Matrix& mat = a.mat[0];
+    if (rg < nrg) {
+      const uint4* codes = mat.codes + (size_t)rg * NBP * 32;
+      const uint2* scales = mat.scales + (size_t)rg * NBP * 8;
+      load_batch(codes, scales, 0, (int)NBP, lane, first);
+    }
+    pdl_wait();
+    prologue<MQ, PRO>(a, sm, geo);
+    unsigned long long best[MQ];
 #pragma unroll
-    for (int q = 0; q < MQ; q++) {
-      red[g * 16 + 4 * q + t] = acc[q][0];
-      red[(g + 8) * 16 + 4 * q + t] = acc[q][1];
-    }
-  }
-  __syncthreads();
-  const int outs = (int)RG * 16 * rows_padded;
-  if (C > 1) {
-    cg::cluster_group cluster = cg::this_cluster();
-    float* dst = cluster.map_shared_rank(sm.cred, 0);
-    for (int i = threadIdx.x; i < outs; i += blockDim.x) {
-      const int rr = i / (16 * rows_padded), rest = i % (16 * rows_padded);
-      const int row = rest / rows_padded, tok = rest % rows_padded;
-      float v = 0.f;
-      for (uint32_t k2 = 0; k2 < KS; k2++) v = add(v, sm.red[(rr * KS + k2) * 256 + row * 16 + tok]);
-      dst[rank * outs + i] = v;
-    }
-    cluster.sync();
-    if (rank != 0) return;
-  }
-  // Final values: vals[rr][row][tok] in red's first slots (re-used after a sync).
-  auto final_value = [&](int rr, int row, int tok) -> float {
-    float v = 0.f;
-    if (C > 1) {
-      const int i = (rr * 16 + row) * rows_padded + tok;
-      for (uint32_t c2 = 0; c2 < C; c2++) v = add(v, sm.cred[c2 * outs + i]);
-    } else {
-      for (uint32_t k2 = 0; k2 < KS; k2++) v = add(v, sm.red[(rr * KS + k2) * 256 + row * 16 + tok]);
-    }
-    return v;
-  };
-
-  if (EPI == kEpilogueWrite || EPI == kEpilogueQkv) {
-    for (int i = threadIdx.x; i < (int)RG * 16 * M; i += blockDim.x) {
-      const int rr = i / (16 * M), rest = i % (16 * M), tok = rest / 16, row = rest % 16;
-      const uint32_t rgi = rowset * RG + rr;
-      if (rgi < mat.n / 16) a.out[(size_t)tok * a.out_stride + rgi * 16 + row] = final_value(rr, row, tok);
-    }
-  } else if (EPI == kEpilogueGated) {
-    const uint32_t F = a.mat[0].n;
-    for (int i = threadIdx.x; i < 16 * M; i += blockDim.x) {
-      const int tok = i / 16, row = i % 16;
-      const uint32_t neuron = rowset * 16 + row;
-      const float gate = final_value(0, row, tok), up = final_value(1, row, tok);
-      float v = mul(gelu_tanh(gate), up);
-      const uint32_t seq = (uint32_t)tok / a.seq_tokens;
-      const uint32_t pos = (a.step ? a.step->position : a.position) + (uint32_t)tok % a.seq_tokens;
-      if (a.edit.table) v = apply_edits(a.edit.table + seq * a.edit.table_stride, a.edit.layer, neuron, pos, v);
-      a.out[(size_t)tok * a.out_stride + neuron] = v;
-      if (a.edit.capture_neurons && (uint32_t)tok % a.seq_tokens == a.seq_tokens - 1)
-        a.edit.capture_neurons[seq * a.capture_stride + neuron] = v;
-    }
-    (void)F;
-  } else if (EPI == kEpilogueHead) {
-    if (threadIdx.x < kMaxTokens) s_best[threadIdx.x] = 0ull;
-    __syncthreads();
-    for (int i = threadIdx.x; i < (int)RG * 16 * M; i += blockDim.x) {
-      const int tok = i / (RG * 16), rest = i % (RG * 16), rr = rest / 16, row = rest % 16;
-      const uint32_t n = (rowset * RG + rr) * 16 + row;
-      if (n < mat.n) {
-        const float v = final_value(rr, row, tok);
-        a.out[(size_t)tok * a.out_stride + n] = v;
-        const unsigned long long key =
-            ((unsigned long long)topk_key(__float_as_uint(v)) << 32) | (0xFFFFFFFFu - n);
-        atomicMax(&s_best[tok], key);
+    for (int q = 0; q < MQ; q++) best[q] = 0ull;
+    for (; rg < nrg; rg += total) {
+      const uint4* codes = mat.codes + (size_t)rg * NBP * 32;
+      const uint2* scales = mat.scales + (size_t)rg * NBP * 8;
+#pragma unroll
+      for (int q = 0; q < MQ; q++) acc[q][0] = acc[q][1] = 0.f;
+      rowgroup_dot<MQ>(codes, scales, 0, (int)NBP, sm.xf, 0, lane, first, acc);
+      if (rg + total < nrg)
+        load_batch(mat.codes + (size_t)(rg + total) * NBP * 32, mat.scales + (size_t)(rg + total) * NBP * 8, 0,
+                   (int)NBP, lane, first);
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        const int tok = 4 * q + t;
+        if (tok < M) {
+          const uint32_t n0 = rg * 16 + g, n8 = n0 + 8;
+          a.out[(size_t)tok * a.out_stride + n0] = acc[q][0];
+          a.out[(size_t)tok * a.out_stride + n8] = acc[q][1];
+          if (EPI == kEpilogueHead) {
+            const unsigned long long k0 = head_key(acc[q][0], n0), k8 = head_key(acc[q][1], n8);
+            best[q] = max(best[q], max(k0, k8));
+          }
+        }
       }
     }
-    __syncthreads();
-    if (threadIdx.x < M) atomicMax(a.head.argmax + threadIdx.x, s_best[threadIdx.x]);
+    pdl_launch_dependents();
+    if (EPI == kEpilogueHead) {
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        unsigned long long b = best[q];
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+        const int tok = 4 * q + t;
+        if (g == 0 && tok < M && b) atomicMax(a.head.argmax + tok, b);
+      }
+    }
+  } else {
+    // CTA mode: the CTA's warps split K (and, with a cluster, so do its CTAs);
+    // partials meet in shared memory, in a fixed order.
+    const uint32_t rgl = warp / geo.KS, ks = warp % geo.KS;
+    const uint32_t S = geo.KS * geo.C, slice = geo.rank * geo.KS + ks;
+    const int bp0 = (int)(slice * geo.NBP / S), bp1 = (int)((slice + 1) * geo.NBP / S);
+    const Q4Matrix& mat = EPI == kEpilogueGated ? a.mat[rgl & 1] : a.mat[0];
+    const uint32_t stride = gridDim.x / geo.C;
+    uint32_t rowset = blockIdx.x / geo.C;
+    auto rg_of = [&](uint32_t rs) { return EPI == kEpilogueGated ? rs : rs * geo.RG + rgl; };
+    auto live_of = [&](uint32_t rs) { return rgl < geo.RG && rs < geo.nrowsets && rg_of(rs) < mat.n / 16 && bp0 < bp1; };
+    if (live_of(rowset)) {
+      const uint32_t rg = rg_of(rowset);
+      load_batch(mat.codes + (size_t)rg * geo.NBP * 32, mat.scales + (size_t)rg * geo.NBP * 8, bp0, bp1, lane, first);
+    }
+    pdl_wait();
+    prologue<MQ, PRO>(a, sm, geo);
+    const int rows_padded = 4 * MQ;
+    const int outs = (int)geo.RG * 16 * rows_padded;
+    for (; rowset < geo.nrowsets; rowset += stride) {
+#pragma unroll
+      for (int q = 0; q < MQ; q++) acc[q][0] = acc[q][1] = 0.f;
+      if (live_of(rowset)) {
+        const uint32_t rg = rg_of(rowset);
+        rowgroup_dot<MQ>(mat.codes + (size_t)rg * geo.NBP * 32, mat.scales + (size_t)rg * geo.NBP * 8, bp0, bp1, sm.xf,
+                         geo.kb_base, lane, first, acc);
+      }
+      if (live_of(rowset + stride)) {
+        const uint32_t rg = rg_of(rowset + stride);
+        load_batch(mat.codes + (size_t)rg * geo.NBP * 32, mat.scales + (size_t)rg * geo.NBP * 8, bp0, bp1, lane, first);
+      }
+      if (rgl < geo.RG) {
+        float* red = sm.red + (rgl * geo.KS + ks) * 256;
+#pragma unroll
+        for (int q = 0; q < MQ; q++) {
+          red[g * 16 + 4 * q + t] = acc[q][0];
+          red[(g + 8) * 16 + 4 * q + t] = acc[q][1];
+        }
+      }
+      __syncthreads();
+      if (geo.C > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        float* dst = cluster.map_shared_rank(sm.cred, 0);
+        for (int i = threadIdx.x; i < outs; i += kThreads) {
+          const int rr = i / (16 * rows_padded), rest = i % (16 * rows_padded);
+          const int row = rest / rows_padded, tok = rest % rows_padded;
+          float v = 0.f;
+          for (uint32_t k2 = 0; k2 < geo.KS; k2++) v = add(v, sm.red[(rr * geo.KS + k2) * 256 + row * 16 + tok]);
+          dst[geo.rank * outs + i] = v;
+        }
+        cluster.sync();
+      }
+      auto final_value = [&](int rr, int row, int tok) -> float {
+        float v = 0.f;
+        if (geo.C > 1) {
+          const int i = (rr * 16 + row) * rows_padded + tok;
+          for (uint32_t c2 = 0; c2 < geo.C; c2++) v = add(v, sm.cred[c2 * outs + i]);
+        } else {
+          for (uint32_t k2 = 0; k2 < geo.KS; k2++) v = add(v, sm.red[(rr * geo.KS + k2) * 256 + row * 16 + tok]);
+        }
+        return v;
+      };
+      if (geo.rank == 0) {
+        if (EPI == kEpilogueWrite || EPI == kEpilogueQkv) {
+          for (int i = threadIdx.x; i < (int)geo.RG * 16 * M; i += kThreads) {
+            const int rr = i / (16 * M), rest = i % (16 * M), tok = rest / 16, row = rest % 16;
+            const uint32_t rgi = rowset * geo.RG + rr;
+            if (rgi < mat.n / 16) a.out[(size_t)tok * a.out_stride + rgi * 16 + row] = final_value(rr, row, tok);
+          }
+        } else if (EPI == kEpilogueGated) {
+          for (int i = threadIdx.x; i < 16 * M; i += kThreads) {
+            const int tok = i / 16, row = i % 16;
+            const uint32_t neuron = rowset * 16 + row;
+            const float gate = final_value(0, row, tok), up = final_value(1, row, tok);
+            float v = mul(gelu_tanh(gate), up);
+            const uint32_t seq = (uint32_t)tok / a.seq_tokens;
+            const uint32_t pos = (a.step ? a.step->position : a.position) + (uint32_t)tok % a.seq_tokens;
+            if (a.edit.table) v = apply_edits(a.edit.table + seq * a.edit.table_stride, a.edit.layer, neuron, pos, v);
+            a.out[(size_t)tok * a.out_stride + neuron] = v;
+            if (a.edit.capture_neurons && (uint32_t)tok % a.seq_tokens == a.seq_tokens - 1)
+              a.edit.capture_neurons[seq * a.capture_stride + neuron] = v;
+          }
+        } else if (EPI == kEpilogueHead) {
+          for (int i = threadIdx.x; i < (int)geo.RG * 16 * M; i += kThreads) {
+            const int tok = i / (geo.RG * 16), rest = i % (geo.RG * 16), rr = rest / 16, row = rest % 16;
+            const uint32_t n = (rowset * geo.RG + rr) * 16 + row;
+            if (n < mat.n) {
+              const float v = final_value(rr, row, tok);
+              a.out[(size_t)tok * a.out_stride + n] = v;
+              atomicMax(&s_best[tok], head_key(v, n));
+            }
+          }
+        }
+      }
+      // The partials are rewritten by the next rowset.
+      if (geo.C > 1) cg::this_cluster().sync();
+      else __syncthreads();
+    }
+    pdl_launch_dependents();
+    if (EPI == kEpilogueHead) {
+      __syncthreads();
+      if (geo.rank == 0 && threadIdx.x < M && s_best[threadIdx.x]) atomicMax(a.head.argmax + threadIdx.x, s_best[threadIdx.x]);
+    }
+    if (geo.C > 1 && geo.rank != 0) return;
   }
 
   if (EPI == kEpilogueQkv) {
@@ -454,7 +593,7 @@ __global__ void __launch_bounds__(256) matvec_kernel(const MatvecArgs a) {
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence();
-      const uint32_t writers = gridDim.x / C;
+      const uint32_t writers = gridDim.x / geo.C;
       s_last = atomicAdd(a.counter, 1u) == writers - 1 ? 1u : 0u;
     }
     __syncthreads();
@@ -462,7 +601,7 @@ __global__ void __launch_bounds__(256) matvec_kernel(const MatvecArgs a) {
     __threadfence();
     const RopeArgs& r = a.rope;
     const int heads = (int)(r.heads + 2 * r.kv_heads);
-    for (int item = warp; item < M * heads; item += nwarps) {
+    for (int item = warp; item < M * heads; item += kWarps) {
       const int row = item / heads, head = item % heads;
       const uint32_t seq = (uint32_t)row / a.seq_tokens;
       const uint32_t pos = (a.step ? a.step->position : a.position) + (uint32_t)row % a.seq_tokens;
@@ -539,21 +678,56 @@ __global__ void dequant_rows_kernel(Q4Matrix mat, const uint32_t* rows, uint32_t
   }
 }
 
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int MQ, int PRO, int EPI>
+int blocks_per_sm(size_t smem) {
+  static std::mutex mu;
+  static std::map<size_t, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(smem);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, matvec_kernel<MQ, PRO, EPI>, kThreads, smem) != cudaSuccess ||
+      n < 1) {
+    (void)cudaGetLastError();
+    n = 1;
+  }
+  cache[smem] = n;
+  return n;
+}
+
 template <int MQ, int PRO, int EPI>
 cudaError_t launch_one(const MatvecArgs& a, cudaStream_t stream, bool pdl) {
   const uint32_t NBP = a.mat[0].k / 64;
   const uint32_t C = a.cluster, RG = a.rg_per_cta, KS = a.k_split;
-  const int threads = (int)(RG * KS * 32);
-  const int norm_warps = PRO == kPrologueNorm ? (int)std::min<uint32_t>(RG * KS, a.m) : 0;
+  if (RG * KS != (uint32_t)kWarps || (EPI == kEpilogueGated && RG != 2) || C < 1 || C > 8) return cudaErrorInvalidValue;
   const size_t nkb_max = 2 * ((NBP + C - 1) / C);
-  size_t smem = nkb_max * 2 * MQ * 32 * sizeof(uint2) + (size_t)RG * KS * 256 * 4 +
-                (size_t)norm_warps * a.norm.width * 4 + (C > 1 ? (size_t)C * RG * 16 * 4 * MQ * 4 : 0);
-  uint32_t rowsets;
-  if (EPI == kEpilogueGated) rowsets = a.mat[0].n / 16;
-  else rowsets = (a.mat[0].n / 16 + RG - 1) / RG;
+  const size_t outs = (size_t)RG * 16 * 4 * MQ;
+  const size_t smem = nkb_max * 2 * MQ * 32 * sizeof(uint2) + (size_t)RG * KS * 256 * 4 +
+                      (PRO == kPrologueNorm ? (size_t)a.m * a.norm.width * 4 + (size_t)a.m * kThreads * 4 : 0) +
+                      2 * kMaxTokens * 4 + (C > 1 ? C * outs * 4 : 0);
+  const bool warp_mode = KS == 1 && C == 1 && EPI != kEpilogueGated;
+  const uint32_t cap = (uint32_t)(sm_count() * blocks_per_sm<MQ, PRO, EPI>(smem));
+  uint32_t grid;
+  if (warp_mode) {
+    grid = std::min<uint32_t>((a.mat[0].n / 16 + kWarps - 1) / kWarps, cap);
+  } else {
+    const uint32_t rowsets = EPI == kEpilogueGated ? a.mat[0].n / 16 : (a.mat[0].n / 16 + RG - 1) / RG;
+    grid = std::min<uint32_t>(rowsets, std::max<uint32_t>(1, cap / C)) * C;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(rowsets * C);
-  cfg.blockDim = dim3(threads);
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
