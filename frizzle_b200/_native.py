@@ -77,6 +77,8 @@ SIGNATURES = {
     "fz_q4_0_matvec": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP]),
     "fz_q4_0_gated": (C.c_int, [VP, VP, VP, VP, U32, U32, VP, U32, VP, U32, U32, VP, VP]),
     "fz_q4_0_head": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP, VP]),
+    "fz_attention": (C.c_int, [VP, VP, VP, U32, U32, U32, U32, U32, U32, U32, VP, VP, VP, VP, VP]),
+    "fz_attention_splits": (U32, [U32, U32, U32]),
 }
 
 

@@ -987,4 +987,45 @@ fz_status fz_q4_0_head(const void* codes, const void* scales, uint32_t n, uint32
   return run_matvec(a, fz::kPrologueInput, fz::kEpilogueHead, static_cast<cudaStream_t>(stream), false);
 }
 
+uint32_t fz_attention_splits(uint32_t window, uint32_t position, uint32_t rows) {
+  const uint64_t keys = std::min<uint64_t>(window, (uint64_t)position + rows);
+  return (uint32_t)((keys + kSplitKeys - 1) / kSplitKeys);
+}
+
+fz_status fz_attention(const float* q, const void* key_cache, const void* value_cache, uint32_t slots, uint32_t heads,
+                       uint32_t kv_heads, uint32_t head_dim, uint32_t window, uint32_t position, uint32_t rows,
+                       float* partial_o, float* partial_ml, uint32_t* counters, float* out, void* stream) {
+  if (!q || !key_cache || !value_cache || !out) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  if (head_dim != 256) return fail(FZ_ERR_NOT_SUPPORTED, "head dimension other than 256");
+  if (kv_heads == 0 || heads % kv_heads || heads / kv_heads > 8) return fail(FZ_ERR_ARGUMENT, "heads per KV head 1..8");
+  if (rows == 0 || window == 0 || slots == 0) return fail(FZ_ERR_ARGUMENT, "rows, window and slots must be nonzero");
+  if ((uint64_t)position + rows > (1u << 24)) return fail(FZ_ERR_ARGUMENT, "position past 2^24");
+  const uint32_t splits = fz_attention_splits(window, position, rows);
+  if (splits > 1 && (!partial_o || !partial_ml || !counters))
+    return fail(FZ_ERR_ARGUMENT, "more than one split needs partial and counter scratch");
+  fz::AttentionArgs at{};
+  at.step = nullptr;
+  at.position = position;
+  at.q = q;
+  at.key_cache = static_cast<const uint16_t*>(key_cache);
+  at.value_cache = static_cast<const uint16_t*>(value_cache);
+  at.seq_stride = 0;
+  at.slots = slots;
+  at.heads = heads;
+  at.kv_heads = kv_heads;
+  at.head_dim = head_dim;
+  at.window = window;
+  at.seq_tokens = rows;
+  at.m = rows;
+  at.scale_log2e = (float)((double)(1.0f / std::sqrt((float)head_dim)) * 1.4426950408889634);
+  at.split_keys = kSplitKeys;
+  at.splits = splits;
+  at.partial_o = partial_o;
+  at.partial_ml = partial_ml;
+  at.counters = counters;
+  at.out = out;
+  FZ_CUDA(fz::launch_attention(at, static_cast<cudaStream_t>(stream), false));
+  return FZ_OK;
+}
+
 }  // extern "C"

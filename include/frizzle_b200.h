@@ -191,6 +191,22 @@ fz_status fz_q4_0_gated(const void *gate_codes, const void *gate_scales, const v
 fz_status fz_q4_0_head(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
                        uint32_t m, float *logits, unsigned long long *argmax, void *stream);
 
+/* Attention of `rows` consecutive query rows (positions position .. position +
+ * rows - 1, one sequence) over a KV cache: softmax(q . k / sqrt(d)) . v over
+ * keys in [p - window + 1, p], keys read from slot j mod slots (the attention
+ * launch and its combine, src/core/kernels/attention/attention.cpp:36-102).
+ * q, out: [rows][heads][256] f32; key_cache, value_cache: [slots][kv_heads][256]
+ * f16.  Keys split into CTAs of 512; rows whose keys span several splits leave
+ * partials in caller scratch: partial_o rows x heads x splits x 256 floats,
+ * partial_ml rows x heads x splits x 2 floats, counters rows x kv_heads words
+ * that start at zero (the kernel leaves them zero), with
+ * splits = ceil(min(window, position + rows) / 512). */
+fz_status fz_attention(const float *q, const void *key_cache, const void *value_cache, uint32_t slots,
+                       uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t window, uint32_t position,
+                       uint32_t rows, float *partial_o, float *partial_ml, uint32_t *counters, float *out,
+                       void *stream);
+uint32_t fz_attention_splits(uint32_t window, uint32_t position, uint32_t rows);
+
 #ifdef __cplusplus
 }
 #endif

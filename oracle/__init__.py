@@ -63,6 +63,8 @@ def _declare(L):
     L.oracle_gelu.argtypes = [C.c_float]; L.oracle_gelu.restype = C.c_float
     L.oracle_norm_row.argtypes = [F32P, P, P, F32P, C.c_int, C.c_float, F32P, P]
     L.oracle_rope_turns.argtypes = [C.c_float, C.c_int, F32P]
+    L.oracle_attention.argtypes = [F32P, P, P, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_uint32, C.c_float,
+                                   C.c_uint32, C.c_int, F32P]
     L.oracle_edit_apply.argtypes = [P, C.c_uint32, C.c_uint32, C.c_int, C.c_int, F32P]
     L.oracle_topk_key.argtypes = [C.c_uint32]; L.oracle_topk_key.restype = C.c_uint32
     L.oracle_topk64.argtypes = [F32P, C.c_int64, U32P]
@@ -123,6 +125,18 @@ def draw(candidates: np.ndarray, top_k: int, temperature: float, top_p: float, m
     lib().oracle_draw(np.ascontiguousarray(candidates, dtype=np.uint32), top_k, temperature, top_p, min_p,
                       log_min_p, np.asarray(seed, dtype=np.uint32), counter, rec)
     return rec
+
+
+def attention(q, kc, vc, slots, kv_heads, window, scale_log2e, position):
+    """q [rows][heads][d] f32; kc, vc [slots][kv_heads][d] uint16 (f16 bits)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    rows, heads, d = q.shape
+    kc = np.ascontiguousarray(kc, dtype=np.uint16)
+    vc = np.ascontiguousarray(vc, dtype=np.uint16)
+    out = np.empty_like(q)
+    lib().oracle_attention(q, kc.ctypes.data, vc.ctypes.data, slots, heads, kv_heads, d, window, scale_log2e,
+                           position, rows, out)
+    return out
 
 
 def edit_apply(table, layer: int, position: int, activation: np.ndarray) -> np.ndarray:

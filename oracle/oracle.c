@@ -349,6 +349,21 @@ static void attend_query(const float *q_in, const uint16_t *kc, const uint16_t *
     if (stats_out) { stats_out[0] = run_m; stats_out[1] = run_l; }
 }
 
+/* Attention over a KV cache for `rows` consecutive query rows at positions
+ * position + r, every query head (the attention launch with its combine,
+ * attention.wgsl:166-438): q [rows][heads][d], caches [slots][kv_heads][d]
+ * f16 words, out [rows][heads][d]. */
+EXPORT void oracle_attention(const float *q, const uint16_t *kc, const uint16_t *vc, uint32_t slots, int heads,
+                             int kv_heads, int d, uint32_t window, float scale_log2e, uint32_t position, int rows,
+                             float *out) {
+    int G = heads / kv_heads;
+#pragma omp parallel for collapse(2)
+    for (int r = 0; r < rows; r++)
+        for (int h = 0; h < heads; h++)
+            attend_query(q + ((size_t)r * heads + h) * d, kc, vc, slots, kv_heads, h / G, d, window, scale_log2e,
+                         position + (uint32_t)r, out + ((size_t)r * heads + h) * d, NULL, 0, NULL);
+}
+
 /* ------------------------------------------------------------ edits */
 
 /* The edit launch over a step's rows (edit.wgsl:55-76): for each of the

@@ -132,3 +132,41 @@ def test_gated_with_edits(m, position):
             for r in range(m):
                 if 40 + e.start <= position + r < 40 + e.until:
                     assert got[r, e.neuron] == np.float32(e.value)
+
+
+ATTN_CASES = [
+    # (rows, position, window, slots): decode and prefill rows, one and several 512-key splits,
+    # a sliding window, and a ring smaller than the positions (keys at slot j mod slots).
+    (1, 35, 512, 5120),
+    (1, 1500, 32768, 4096),
+    (4, 1020, 32768, 2048),
+    (16, 100, 16, 48),
+    (1, 3000, 512, 1100),
+    (2, 5000, 32768, 8192),
+]
+
+
+@pytest.mark.parametrize("rows,position,window,slots", ATTN_CASES)
+def test_attention_vs_oracle(rows, position, window, slots):
+    torch = torch_cuda()
+    lib = _native.load()
+    heads, kv, d = 4, 1, 256
+    rng = np.random.default_rng([rows, position, window])
+    q = rng.standard_normal((rows, heads, d)).astype(np.float32)
+    kc = (rng.standard_normal((slots, kv, d)) * 0.5).astype(np.float16).view(np.uint16)
+    vc = rng.standard_normal((slots, kv, d)).astype(np.float16).view(np.uint16)
+    scale = float(np.float32(np.float64(np.float32(1.0) / np.sqrt(np.float32(d))) * 1.4426950408889634))
+    want = oracle.attention(q, kc, vc, slots, kv, window, scale, position)
+    splits = lib.fz_attention_splits(window, position, rows)
+    qd, kd, vd = dev(q), dev(kc.view(np.int16)), dev(vc.view(np.int16))
+    po = torch.empty(rows * heads * splits * d, dtype=torch.float32, device="cuda")
+    pml = torch.empty(rows * heads * splits * 2, dtype=torch.float32, device="cuda")
+    cnt = torch.zeros(rows * kv, dtype=torch.int32, device="cuda")
+    out = torch.empty((rows, heads, d), dtype=torch.float32, device="cuda")
+    _native.check(lib.fz_attention(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), slots, heads, kv, d, window, position,
+                                   rows, po.data_ptr(), pml.data_ptr(), cnt.data_ptr(), out.data_ptr(), stream()))
+    got = out.cpu().numpy()
+    err = np.sqrt(np.mean((got.astype(np.float64) - want) ** 2)) / np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    assert err < 1e-5, err
+    assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
+    assert int(cnt.abs().sum()) == 0  # the counters are left at zero for the next launch
