@@ -79,6 +79,7 @@ SIGNATURES = {
     "fz_q4_0_head": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP, VP]),
     "fz_attention": (C.c_int, [VP, VP, VP, U32, U32, U32, U32, U32, U32, U32, VP, VP, VP, VP, VP]),
     "fz_attention_splits": (U32, [U32, U32, U32]),
+    "fz_attention_static": (C.c_int, [VP, VP, VP, U32, U32, U32, U32, U32, U32, U32, VP, VP]),
 }
 
 

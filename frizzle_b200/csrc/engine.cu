@@ -17,6 +17,7 @@
 #include "frizzle_b200.h"
 #include "gguf_index.h"
 #include "kernels.cuh"
+#include "last_error.h"
 #include "q4_matvec.cuh"
 
 using fz::DeviceStep;
@@ -32,6 +33,12 @@ fz_status fail(fz_status s, const std::string& msg) {
   g_error = msg;
   return s;
 }
+
+}  // namespace
+
+void fz::set_last_error(const char* message) { g_error = message; }
+
+namespace {
 
 #define FZ_CUDA(x)                                                                           \
   do {                                                                                       \

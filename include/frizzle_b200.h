@@ -207,6 +207,26 @@ fz_status fz_attention(const float *q, const void *key_cache, const void *value_
                        void *stream);
 uint32_t fz_attention_splits(uint32_t window, uint32_t position, uint32_t rows);
 
+/* fz_attention for callers that cannot allocate device memory: no
+ * counterpart in the reference.  Some hosts own no device allocator (a
+ * runtime that hands out only pre-registered buffers, a memory pool fixed
+ * before plugins load, a caller recording work that must stay free of
+ * allocation), so this entry point takes only inputs and outputs and keeps
+ * the split scratch in a static device array the library holds on every
+ * device that loads it, until the process exits: 2 MiB + 16 KiB + 512 B.
+ * Limits: rows x heads x key splits <= FZ_ATTENTION_STATIC_MAX_PARTIALS and
+ * rows x kv_heads <= FZ_ATTENTION_STATIC_MAX_COUNTERS; larger calls are
+ * refused with FZ_ERR_ARGUMENT.  It calls no cudaMalloc or cudaFree: the
+ * first call on a device looks up the array's device address there
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * Every call shares the one array and clears its split counters before the
+ * launch; calls whose launches overlap on the GPU race on the scratch. */
+#define FZ_ATTENTION_STATIC_MAX_PARTIALS 2048u
+#define FZ_ATTENTION_STATIC_MAX_COUNTERS 128u
+fz_status fz_attention_static(const float *q, const void *key_cache, const void *value_cache, uint32_t slots,
+                              uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t window,
+                              uint32_t position, uint32_t rows, float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
