@@ -115,3 +115,36 @@ def test_gemma_1b_config1_steered(gemma_model_path):
     edits = [Edit(13, int(i), SET, float(v), 0) for i, v in zip(idx, vals)]
     out = run_both(gemma_model_path, s, 32, 32, edits=edits, capture=True)
     assert_parity(out)
+
+
+def test_tiny_model_sampled_draw(tiny_model_path):
+    """Temperature 1, top-k 64 (config 4's sampling): the GPU's top-64 selection
+    and Philox draw against the oracle's on the oracle's own logits; the uniform
+    must be the same bits (Philox is integer arithmetic) and the token the same
+    unless the uniform falls within float rounding of a cumulative boundary."""
+    s = synth.TINY
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, tiny_model_path)
+    batch = engine.Batch(model, 1, 512)
+    orc = oracle.OracleModel(tiny_model_path, context=512)
+    samp = engine.Sampling(temperature=1.0, top_k=64, top_p=1.0, min_p=0.0, seed=(7, 9))
+    ids = prompt(s, 12, seed=3)
+    batch.step(0, ids, tokens=12, logits=True, sampling=samp)
+    want_logits, _ = orc.step(0, ids, logits=True)
+    agree = 0
+    for i in range(10):
+        rec = batch.wait()[0]
+        tok, failed, u = int(rec[0]), int(rec[1]), float(rec[2])
+        cand = oracle.topk64(want_logits)
+        want = oracle.draw(cand, 64, 1.0, 1.0, 0.0, (7, 9), 12 + i)
+        assert failed == 0
+        assert np.float32(u).view(np.uint32) == want[2]
+        agree += tok == int(want[0])
+        batch.step(12 + i, fed=True, tokens=1, logits=True, sampling=samp)
+        want_logits, _ = orc.step(12 + i, [tok], logits=True)
+    batch.wait()
+    assert agree >= 9
+    orc.close()
+    batch.free()
+    model.free()
+    dev.close()
