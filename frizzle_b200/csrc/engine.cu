@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "frizzle_b200.h"
+#include "gemm_tc.cuh"
 #include "gguf_index.h"
 #include "kernels.cuh"
 #include "last_error.h"
@@ -992,6 +993,57 @@ fz_status fz_q4_0_head(const void* codes, const void* scales, uint32_t n, uint32
   a.out_stride = n;
   a.head.argmax = argmax;
   return run_matvec(a, fz::kPrologueInput, fz::kEpilogueHead, static_cast<cudaStream_t>(stream), false);
+}
+
+fz_status fz_q4_0_gemm(const void* codes, const void* scales, uint32_t n, uint32_t k, const void* x_hi, const void* x_lo,
+                       uint32_t m, float* y, uint32_t* error, void* stream) {
+  fz_status st;
+  if ((st = check_shape(n, k))) return st;
+  if (!codes || !scales || !x_hi || !y || !error || m == 0) return fail(FZ_ERR_ARGUMENT, "null pointer or m = 0");
+  fz::GemmArgs a{};
+  a.w[0] = Q4Matrix{static_cast<const uint4*>(codes), static_cast<const uint2*>(scales), n, k};
+  a.m = m;
+  a.x_hi = static_cast<const __half*>(x_hi);
+  a.x_lo = static_cast<const __half*>(x_lo);
+  a.out = y;
+  a.out_stride = n;
+  a.seq_tokens = m;
+  a.error = error;
+  FZ_CUDA(fz::launch_gemm(a, fz::kGemmWrite, static_cast<cudaStream_t>(stream), false));
+  return FZ_OK;
+}
+
+fz_status fz_q4_0_gemm_gated(const void* gate_codes, const void* gate_scales, const void* up_codes,
+                             const void* up_scales, uint32_t f, uint32_t k, const void* x_hi, const void* x_lo,
+                             uint32_t m, const uint32_t* table, uint32_t layer, uint32_t position, float* act,
+                             void* act_hi, void* act_lo, uint32_t* error, void* stream) {
+  fz_status st;
+  if ((st = check_shape(f, k))) return st;
+  if (!gate_codes || !gate_scales || !up_codes || !up_scales || !x_hi || !act_hi || !error || m == 0)
+    return fail(FZ_ERR_ARGUMENT, "null pointer or m = 0");
+  fz::GemmArgs a{};
+  a.w[0] = Q4Matrix{static_cast<const uint4*>(gate_codes), static_cast<const uint2*>(gate_scales), f, k};
+  a.w[1] = Q4Matrix{static_cast<const uint4*>(up_codes), static_cast<const uint2*>(up_scales), f, k};
+  a.m = m;
+  a.position = position;
+  a.x_hi = static_cast<const __half*>(x_hi);
+  a.x_lo = static_cast<const __half*>(x_lo);
+  a.out = act;
+  a.out_stride = f;
+  a.act_hi = static_cast<__half*>(act_hi);
+  a.act_lo = static_cast<__half*>(act_lo);
+  a.edit_table = table;
+  a.layer = layer;
+  a.seq_tokens = m;
+  a.error = error;
+  FZ_CUDA(fz::launch_gemm(a, fz::kGemmGated, static_cast<cudaStream_t>(stream), false));
+  return FZ_OK;
+}
+
+fz_status fz_split_f16(const float* x, size_t n, void* hi, void* lo, void* stream) {
+  if (!x || !hi) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  FZ_CUDA(fz::launch_split_f16(x, n, static_cast<__half*>(hi), static_cast<__half*>(lo), static_cast<cudaStream_t>(stream)));
+  return FZ_OK;
 }
 
 uint32_t fz_attention_splits(uint32_t window, uint32_t position, uint32_t rows) {

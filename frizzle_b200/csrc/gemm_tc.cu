@@ -1,0 +1,481 @@
+// tcgen05/TMEM product over Q4_0 weights (gemm_tc.cuh).
+//
+// A CTA computes a 128-row x BN-column tile of Y (128 rows of X: tokens; BN
+// weight rows).  K is walked 64 columns (one Q4_0 block pair) a stage through
+// a ring of shared-memory stages:
+//   - warp 0 (one lane) loads the 128 x 64 f16 tile of X with TMA
+//     (SWIZZLE_128B, K-major), and of X's remainder for two passes;
+//   - warps 2..9 dequantize the BN x 64 weight tile from the fragment-native
+//     Q4_0 layout, (code - 8) x d rounded once to f16, into the same
+//     swizzled K-major layout;
+//   - warp 1 (one lane) issues tcgen05.mma kind::f16 (M = 128, N = BN,
+//     K = 16) into an f32 accumulator in tensor memory and commits each stage
+//     back to its producers;
+//   - warps 2..5 read the accumulator (tcgen05.ld 32x32b) and write Y, or,
+//     for a gated product, gelu(gate) * up with the steering edits.
+// Every mbarrier wait is bounded: on timeout the kernel records an error,
+// stops waiting, and still releases its tensor memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "gemm_tc.cuh"
+
+namespace fz {
+namespace {
+
+constexpr int kBM = 128;              // rows of X a tile (the MMA's M)
+constexpr int kBK = 64;               // columns a stage: 128 B of f16 a row
+constexpr int kProducers = 8;         // weight-dequant warps (warps 2..9)
+constexpr int kThreadsG = 32 * (2 + kProducers);
+constexpr uint32_t kSpinLimit = 1u << 24;
+
+FZ_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+FZ_DEV void mbar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(n) : "memory");
+}
+FZ_DEV void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+FZ_DEV void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+FZ_DEV bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase of parity `parity` to complete, at most kSpinLimit
+// polls; gives up early once another warp has recorded an error.
+FZ_DEV bool mbar_wait(uint64_t* b, uint32_t parity, uint32_t* err, uint32_t code) {
+  for (uint32_t i = 0; i < kSpinLimit; i++) {
+    if (mbar_try(b, parity)) return true;
+    if ((i & 1023u) == 1023u && *reinterpret_cast<volatile uint32_t*>(err)) return false;
+  }
+  atomicExch(err, code);
+  return false;
+}
+
+FZ_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 bytes stacked along M/N (stride byte offset 1024), tile base 1024-aligned.
+FZ_DEV uint64_t smem_desc(const void* p) {
+  const uint32_t a = smem_u32(p);
+  uint64_t d = (uint64_t)((a & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;              // leading byte offset (unused by swizzled K-major): 16 B
+  d |= (uint64_t)(1024 >> 4) << 32;    // stride byte offset
+  d |= (uint64_t)1 << 46;              // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;              // SWIZZLE_128B
+  return d;
+}
+
+template <int BN>
+__host__ __device__ constexpr uint32_t instr_desc() {
+  // kind::f16: D f32, A and B f16, both K-major, M = 128, N = BN.
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
+}
+
+FZ_DEV void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+FZ_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+FZ_DEV void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+FZ_DEV void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+FZ_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+FZ_DEV void tmem_ld32(uint32_t taddr, uint32_t r[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+FZ_DEV uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+FZ_DEV __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Byte offset of element (n, k) in a K-major 128B-swizzled tile of 64 f16 columns.
+FZ_DEV uint32_t swz(uint32_t n, uint32_t k) { return n * 128u + ((((k >> 3) ^ (n & 7u)) & 7u) << 4) + (k & 7u) * 2u; }
+
+// A row group's codes and scales for one block pair, in registers.
+struct Codes {
+  uint4 c;
+  uint2 s;
+};
+
+FZ_DEV Codes load_codes(const Q4Matrix& w, uint32_t rg, uint32_t bp, bool live, int lane) {
+  Codes x;
+  x.c = make_uint4(0, 0, 0, 0);
+  x.s = make_uint2(0, 0);
+  if (live) {
+    const uint32_t nbp = w.k / 64;
+    x.c = w.codes[((size_t)rg * nbp + bp) * 32 + lane];
+    x.s = w.scales[((size_t)rg * nbp + bp) * 8 + (lane >> 2)];
+  }
+  return x;
+}
+
+// One row group's 16 x 64 weights (one block pair) into the stage's B tile at
+// rows [row0, row0 + 16).  Lane (g, t) holds rows g and g + 8 of both blocks;
+// each of its four code words gives, per row, the f16 pairs at columns
+// (2t, 2t+1) and (16 + 2t, 17 + 2t) of half h of block kb.  A row group past
+// the matrix is written as zeros (its codes were never loaded).
+FZ_DEV void dequant_tile(unsigned char* tile, uint32_t row0, const Codes& x, bool live, int lane) {
+  const uint32_t g = lane >> 2, t = lane & 3;
+  const uint32_t kMask = 0x000F000Fu, kMagic = 0x64006400u;
+  const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408u));
+  const uint32_t words[4] = {x.c.x, x.c.y, x.c.z, x.c.w};
+#pragma unroll
+  for (int wi = 0; wi < 4; wi++) {
+    const uint32_t kb = wi >> 1, h = wi & 1;
+    const uint32_t wd = words[wi];
+    const uint32_t sw = kb ? x.s.y : x.s.x;
+    const __half2 dg = __half2half2(__ushort_as_half((unsigned short)(sw & 0xffffu)));
+    const __half2 dg8 = __half2half2(__ushort_as_half((unsigned short)(sw >> 16)));
+    const uint32_t k0 = 32 * kb + 8 * h + 2 * t;
+    const __half2 g_lo = __hmul2(__hsub2(u2h((wd & kMask) | kMagic), bias), dg);
+    const __half2 g_hi = __hmul2(__hsub2(u2h(((wd >> 4) & kMask) | kMagic), bias), dg);
+    const __half2 e_lo = __hmul2(__hsub2(u2h(((wd >> 8) & kMask) | kMagic), bias), dg8);
+    const __half2 e_hi = __hmul2(__hsub2(u2h(((wd >> 12) & kMask) | kMagic), bias), dg8);
+    const uint32_t r0 = row0 + g, r8 = row0 + g + 8;
+    *reinterpret_cast<uint32_t*>(tile + swz(r0, k0)) = live ? h2u(g_lo) : 0u;
+    *reinterpret_cast<uint32_t*>(tile + swz(r0, k0 + 16)) = live ? h2u(g_hi) : 0u;
+    *reinterpret_cast<uint32_t*>(tile + swz(r8, k0)) = live ? h2u(e_lo) : 0u;
+    *reinterpret_cast<uint32_t*>(tile + swz(r8, k0 + 16)) = live ? h2u(e_hi) : 0u;
+  }
+}
+
+FZ_DEV float apply_edit_table(const uint32_t* table, uint32_t layer, uint32_t neuron, uint32_t pos, float v) {
+  const uint32_t first = table[2 * layer], count = table[2 * layer + 1];
+  uint32_t lo = 0, hi = count;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (table[first + 5 * mid] < neuron) lo = mid + 1; else hi = mid;
+  }
+  for (uint32_t i = lo; i < count; i++) {
+    const uint32_t* e = table + first + 5 * i;
+    if (e[0] != neuron) break;
+    if (pos < e[3] || pos >= e[4]) continue;
+    const float value = __uint_as_float(e[2]);
+    float edited = value;
+    if (e[1] == 1u) edited = value == 1.0f ? v : __fmul_rn(v, value);
+    v = edited;
+  }
+  return v;
+}
+
+template <int BN, int PASSES>
+struct Layout {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes * PASSES + kBBytes;
+  static constexpr int kStages = (196 * 1024) / kStageBytes > 6 ? 6 : (196 * 1024) / kStageBytes;
+  static constexpr int kSmem = kStages * kStageBytes + 1024;  // + alignment slack
+};
+
+template <int BN, int PASSES, int EPI>
+__global__ void __launch_bounds__(kThreadsG, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
+                const GemmArgs a) {
+  using L = Layout<BN, PASSES>;
+  constexpr int S = L::kStages;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t full[S];
+  __shared__ __align__(8) uint64_t empty[S];
+  __shared__ __align__(8) uint64_t accum_full;
+  __shared__ uint32_t tmem_base;
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  auto a_tile = [&](int s, int p) { return smem + s * L::kStageBytes + p * L::kABytes; };
+  auto b_tile = [&](int s) { return smem + s * L::kStageBytes + PASSES * L::kABytes; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t m0 = blockIdx.y * kBM;
+  const uint32_t K = a.w[0].k, nkt = K / kBK;
+  const uint32_t half_bn = BN / 2;
+  // Weight rows of this tile: n0.. for Write; neurons nn0.. of gate and up for Gated.
+  const uint32_t n0 = EPI == kGemmGated ? blockIdx.x * half_bn : blockIdx.x * BN;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < S; s++) {
+      mbar_init(&full[s], 1 + kProducers);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&accum_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                 "r"((uint32_t)BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // X tiles by TMA; X is the previous kernel's output.  The whole warp runs
+    // the loop and waits, lane 0 issues.
+    pdl_wait();
+    for (uint32_t kt = 0; kt < nkt; kt++) {
+      const int s = (int)(kt % S);
+      const uint32_t round = kt / S;
+      if (!mbar_wait(&empty[s], (round + 1) & 1u, a.error, 1)) break;
+      if (lane == 0) {
+        mbar_expect_tx(&full[s], (uint32_t)(L::kABytes * PASSES));
+        tma_load_2d(a_tile(s, 0), &map_hi, &full[s], (int)(kt * kBK), (int)m0);
+        if (PASSES == 2) tma_load_2d(a_tile(s, 1), &map_lo, &full[s], (int)(kt * kBK), (int)m0);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // The MMA issuer: the whole warp waits, lane 0 issues and commits.
+    constexpr uint32_t idesc = instr_desc<BN>();
+    for (uint32_t kt = 0; kt < nkt; kt++) {
+      const int s = (int)(kt % S);
+      const uint32_t round = kt / S;
+      if (!mbar_wait(&full[s], round & 1u, a.error, 2)) break;
+      fence_after_sync();
+      if (lane == 0) {
+        const uint64_t db = smem_desc(b_tile(s));
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; kk++) {
+#pragma unroll
+          for (int p = 0; p < PASSES; p++) {
+            const uint64_t da = smem_desc(a_tile(s, p));
+            // 16 columns of f16 = 32 bytes along K: +2 in the 16-byte address field.
+            umma(tmem, da + 2 * kk, db + 2 * kk, idesc, (kt | kk | p) != 0 ? 1u : 0u);
+          }
+        }
+        umma_commit(&empty[s]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) umma_commit(&accum_full);
+    __syncwarp();
+  } else {
+    // Weight producers: warps 2..9 dequantize BN / 16 row groups a stage, the
+    // codes of the next two stages already in flight.
+    const int pw = warp - 2;
+    constexpr int kRgs = BN / 16;
+    constexpr int kMine = kRgs / kProducers;       // row groups a warp, a stage
+    static_assert(kRgs % kProducers == 0, "row groups split evenly over the producers");
+    auto rg_of = [&](int j) {
+      const int r = pw + j * kProducers;
+      return EPI == kGemmGated ? (n0 / 16 + (uint32_t)(r % (kRgs / 2))) : (n0 / 16 + (uint32_t)r);
+    };
+    auto mat_of = [&](int j) -> const Q4Matrix& {
+      const int r = pw + j * kProducers;
+      return (EPI == kGemmGated && r >= kRgs / 2) ? a.w[1] : a.w[0];
+    };
+    Codes A[kMine], B[kMine], C[kMine];
+    bool stop = false;
+    // One stage: stage kt's codes are in `cur`; stage kt + 2's load into `later`.
+    auto step = [&](uint32_t kt, Codes (&cur)[kMine], Codes (&later)[kMine]) {
+      const int s = (int)(kt % S);
+      const uint32_t round = kt / S;
+      if (kt + 2 < nkt)
+#pragma unroll
+        for (int j = 0; j < kMine; j++)
+          later[j] = load_codes(mat_of(j), rg_of(j), kt + 2, rg_of(j) < mat_of(j).n / 16, lane);
+      if (!mbar_wait(&empty[s], (round + 1) & 1u, a.error, 3)) {
+        stop = true;
+        return;
+      }
+      unsigned char* tile = b_tile(s);
+#pragma unroll
+      for (int j = 0; j < kMine; j++)
+        dequant_tile(tile, (uint32_t)(pw + j * kProducers) * 16, cur[j], rg_of(j) < mat_of(j).n / 16, lane);
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+    };
+#pragma unroll
+    for (int j = 0; j < kMine; j++) {
+      A[j] = load_codes(mat_of(j), rg_of(j), 0, rg_of(j) < mat_of(j).n / 16, lane);
+      if (nkt > 1) B[j] = load_codes(mat_of(j), rg_of(j), 1, rg_of(j) < mat_of(j).n / 16, lane);
+    }
+    for (uint32_t kt = 0; kt < nkt && !stop; kt += 3) {
+      step(kt, A, C);
+      if (kt + 1 < nkt && !stop) step(kt + 1, B, A);
+      if (kt + 2 < nkt && !stop) step(kt + 2, C, B);
+    }
+    // Epilogue: warps 2..5, TMEM lanes 32 * (warp % 4) .. + 31.
+    if (warp < 6) {
+      const bool ok = mbar_wait(&accum_full, 0, a.error, 4);
+      fence_after_sync();
+      const uint32_t quarter = (uint32_t)warp & 3u;
+      const uint32_t row = m0 + quarter * 32 + lane;
+      const uint32_t lane_addr = tmem + ((quarter * 32u) << 16);
+      if (ok) {
+        if (EPI == kGemmWrite) {
+          const uint32_t N = a.w[0].n;
+          for (int c0 = 0; c0 < BN; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(lane_addr + (uint32_t)c0, r);
+            if (row < a.m) {
+              float* o = a.out + (size_t)row * a.out_stride + n0 + c0;
+              if (n0 + c0 + 32 <= N) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4)
+                  *reinterpret_cast<float4*>(o + i) = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                                                                  __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+              } else {
+                for (int i = 0; i < 32; i++)
+                  if (n0 + c0 + i < N) o[i] = __uint_as_float(r[i]);
+              }
+            }
+          }
+        } else {
+          const uint32_t F = a.w[0].n;
+          const uint32_t seq = row / a.seq_tokens;
+          const uint32_t pos = (a.step ? a.step->position : a.position) + row % a.seq_tokens;
+          const bool last = row % a.seq_tokens == a.seq_tokens - 1;
+          for (int c0 = 0; c0 < (int)half_bn; c0 += 32) {
+            uint32_t gr[32], ur[32];
+            tmem_ld32(lane_addr + (uint32_t)c0, gr);
+            tmem_ld32(lane_addr + half_bn + (uint32_t)c0, ur);
+            if (row < a.m) {
+#pragma unroll
+              for (int i = 0; i < 32; i++) {
+                const uint32_t neuron = n0 + c0 + i;
+                if (neuron >= F) continue;
+                float v = __fmul_rn(gelu_tanh(__uint_as_float(gr[i])), __uint_as_float(ur[i]));
+                if (a.edit_table) v = apply_edit_table(a.edit_table + seq * a.table_stride, a.layer, neuron, pos, v);
+                const size_t at = (size_t)row * F + neuron;
+                if (a.out) a.out[(size_t)row * a.out_stride + neuron] = v;
+                const __half hi = __float2half_rn(v);
+                a.act_hi[at] = hi;
+                if (a.act_lo) a.act_lo[at] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
+                if (a.capture_neurons && last) a.capture_neurons[seq * a.capture_stride + neuron] = v;
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+  pdl_launch_dependents();
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after_sync();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+  }
+}
+
+__global__ void split_f16_kernel(const float* __restrict__ x, size_t n, __half* hi, __half* lo) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    const __half h = __float2half_rn(v);
+    hi[i] = h;
+    if (lo) lo[i] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A 2D tensor map over an [rows][cols] f16 matrix: boxes of 128 rows x 64
+// columns, 128-byte swizzle, rows past `rows` read as zeros.
+bool make_map(CUtensorMap* map, const __half* base, uint32_t rows, uint32_t cols) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  const cuuint32_t estride[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int PASSES, int EPI>
+cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
+  using L = Layout<BN, PASSES>;
+  static std::once_flag once;
+  static cudaError_t configured = cudaSuccess;
+  std::call_once(once, [] {
+    configured = cudaFuncSetAttribute(gemm_kernel<BN, PASSES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      L::kSmem);
+  });
+  if (configured != cudaSuccess) return configured;
+  CUtensorMap map_hi, map_lo;
+  if (!make_map(&map_hi, a.x_hi, a.m, a.w[0].k)) return cudaErrorInvalidValue;
+  if (!make_map(&map_lo, PASSES == 2 ? a.x_lo : a.x_hi, a.m, a.w[0].k)) return cudaErrorInvalidValue;
+  const uint32_t cols = EPI == kGemmGated ? BN / 2 : BN;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.w[0].n + cols - 1) / cols, (a.m + kBM - 1) / kBM);
+  cfg.blockDim = dim3(kThreadsG);
+  cfg.dynamicSmemBytes = L::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, PASSES, EPI>, map_hi, map_lo, a);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return e;
+}
+
+}  // namespace
+
+cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bool pdl) {
+  if (a.m == 0 || a.w[0].k % 64 || a.w[0].n % 16 || !a.x_hi || !a.error) return cudaErrorInvalidValue;
+  // TMA wants 16-byte aligned rows: K f16 values a row, K a multiple of 64.
+  if ((reinterpret_cast<uintptr_t>(a.x_hi) & 15) || (a.x_lo && (reinterpret_cast<uintptr_t>(a.x_lo) & 15)))
+    return cudaErrorInvalidValue;
+  const bool two = a.x_lo != nullptr;
+  if (epilogue == kGemmGated) {
+    if (!a.act_hi || a.w[1].n != a.w[0].n || a.w[1].k != a.w[0].k) return cudaErrorInvalidValue;
+    return two ? launch_tiles<256, 2, kGemmGated>(a, stream, pdl) : launch_tiles<256, 1, kGemmGated>(a, stream, pdl);
+  }
+  if (!a.out) return cudaErrorInvalidValue;
+  return two ? launch_tiles<256, 2, kGemmWrite>(a, stream, pdl) : launch_tiles<256, 1, kGemmWrite>(a, stream, pdl);
+}
+
+cudaError_t launch_split_f16(const float* x, size_t n, __half* hi, __half* lo, cudaStream_t stream) {
+  if (!n) return cudaSuccess;
+  const int blocks = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
+  (void)cudaGetLastError();
+  split_f16_kernel<<<blocks, 256, 0, stream>>>(x, n, hi, lo);
+  return cudaGetLastError();
+}
+
+}  // namespace fz

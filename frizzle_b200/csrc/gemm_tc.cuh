@@ -1,0 +1,42 @@
+// Prefill products on the 5th-generation tensor cores: Y[m][n] = sum_k W[n][k] X[m][k]
+// for many rows of X (prefill blocks, wide batches), W in the fragment-native
+// Q4_0 layout (q4_matvec.cuh), X as f16 (optionally f16 hi + lo of an f32).
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include "fz_common.cuh"
+#include "q4_matvec.cuh"
+
+namespace fz {
+
+enum GemmEpilogue : int { kGemmWrite = 0, kGemmGated = 1 };
+
+struct GemmArgs {
+  const DeviceStep* step;     // position of row 0, or null for `position`
+  uint32_t position;
+  Q4Matrix w[2];              // w[1]: the up projection of a gated product
+  uint32_t m;                 // rows of X
+  const __half* x_hi;         // [m][k] f16
+  const __half* x_lo;         // [m][k] f16 remainder, or null (one pass)
+  float* out;                 // [m][out_stride] f32 (Write; Gated: optional)
+  uint32_t out_stride;
+  // Gated epilogue: act = gelu(gate) * up, edits, then f16 hi/lo for the next product.
+  __half* act_hi;             // [m][f]
+  __half* act_lo;             // [m][f] or null
+  const uint32_t* edit_table; // or null
+  uint64_t table_stride;
+  uint32_t layer;
+  uint32_t seq_tokens;        // rows a sequence holds
+  float* capture_neurons;     // sequence 0's capture slot, or null
+  uint64_t capture_stride;
+  uint32_t* error;            // set nonzero when a bounded wait gives up
+};
+
+// Launches the product; `passes` is 1 (x_hi only) or 2 (x_hi + x_lo).
+cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bool pdl);
+
+// x -> f16 hi = f16(x), lo = f16(x - hi) (lo may be null).
+cudaError_t launch_split_f16(const float* x, size_t n, __half* hi, __half* lo, cudaStream_t stream);
+
+}  // namespace fz

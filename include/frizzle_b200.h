@@ -191,6 +191,27 @@ fz_status fz_q4_0_gated(const void *gate_codes, const void *gate_scales, const v
 fz_status fz_q4_0_head(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
                        uint32_t m, float *logits, unsigned long long *argmax, void *stream);
 
+/* Y[m][n] = sum_k W[n][k] X[m][k] for many rows on the tensor cores
+ * (tcgen05.mma into tensor memory; the reference's prefill form,
+ * src/core/kernels/matmul/matmul.wgsl:287-485): X as f16 `x_hi` [m][k] and,
+ * for f32-level accuracy, its f16 remainder `x_lo` (two passes; NULL for one).
+ * Weights are rounded once to f16 as they are dequantized.  `error` is a
+ * device word the caller zeroes; nonzero after the call completes means a
+ * bounded wait inside the kernel gave up (no result). */
+fz_status fz_q4_0_gemm(const void *codes, const void *scales, uint32_t n, uint32_t k, const void *x_hi,
+                       const void *x_lo, uint32_t m, float *y, uint32_t *error, void *stream);
+
+/* The gated product for many rows: act = gelu_tanh(gate . x) * (up . x), the
+ * edit table applied to rows at positions position + r, written as f32 `act`
+ * (may be NULL) and as f16 hi/lo (`act_lo` may be NULL) for the next product. */
+fz_status fz_q4_0_gemm_gated(const void *gate_codes, const void *gate_scales, const void *up_codes,
+                             const void *up_scales, uint32_t f, uint32_t k, const void *x_hi, const void *x_lo,
+                             uint32_t m, const uint32_t *table, uint32_t layer, uint32_t position, float *act,
+                             void *act_hi, void *act_lo, uint32_t *error, void *stream);
+
+/* x -> f16 hi = f16(x) and lo = f16(x - hi) (`lo` may be NULL). */
+fz_status fz_split_f16(const float *x, size_t n, void *hi, void *lo, void *stream);
+
 /* Attention of `rows` consecutive query rows (positions position .. position +
  * rows - 1, one sequence) over a KV cache: softmax(q . k / sqrt(d)) . v over
  * keys in [p - window + 1, p], keys read from slot j mod slots (the attention

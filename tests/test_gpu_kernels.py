@@ -170,3 +170,79 @@ def test_attention_vs_oracle(rows, position, window, slots):
     assert err < 1e-5, err
     assert np.abs(got - want).max() <= 1e-4 * np.abs(want).max()
     assert int(cnt.abs().sum()) == 0  # the counters are left at zero for the next launch
+
+
+def split_dev(x):
+    torch = torch_cuda()
+    lib = _native.load()
+    xd = dev(x)
+    hi = torch.empty(x.shape, dtype=torch.float16, device="cuda")
+    lo = torch.empty(x.shape, dtype=torch.float16, device="cuda")
+    _native.check(lib.fz_split_f16(xd.data_ptr(), x.size, hi.data_ptr(), lo.data_ptr(), stream()))
+    return hi, lo
+
+
+GEMM_SHAPES = [(1152, 1536), (1024, 1152), (6912, 1152), (1152, 6912)]  # (K, N)
+
+
+@pytest.mark.parametrize("k,n", GEMM_SHAPES)
+@pytest.mark.parametrize("m", [64, 200, 512])
+@pytest.mark.parametrize("passes", [1, 2])
+def test_tensor_core_gemm(k, n, m, passes):
+    """The tcgen05 product against the oracle's f32: weights rounded once to
+    f16 (and X to f16, or f16 hi + lo for two passes), f32 accumulation."""
+    torch = torch_cuda()
+    lib = _native.load()
+    blocks = synth.random_q4_0(n, k, seed=k + n)
+    x = np.random.default_rng(m).standard_normal((m, k)).astype(np.float32)
+    codes, scales = repacked(blocks, n, k)
+    hi, lo = split_dev(x)
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _native.check(lib.fz_q4_0_gemm(codes.data_ptr(), scales.data_ptr(), n, k, hi.data_ptr(),
+                                   lo.data_ptr() if passes == 2 else None, m, y.data_ptr(), err.data_ptr(), stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = y.cpu().numpy()
+    want = oracle.matmul(blocks, n, k, x)
+    rel = np.sqrt(np.mean((got.astype(np.float64) - want) ** 2)) / np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    print(f"gemm k={k} n={n} m={m} passes={passes} rel_rms={rel:.3e}")
+    assert np.isfinite(got).all()
+    assert rel < (5e-4 if passes == 2 else 1e-3), rel
+
+
+@pytest.mark.parametrize("m,position", [(128, 30), (300, 0)])
+def test_tensor_core_gated_with_edits(m, position):
+    torch = torch_cuda()
+    lib = _native.load()
+    f, k = 6912, 1152
+    gate = synth.random_q4_0(f, k, seed=1)
+    up = synth.random_q4_0(f, k, seed=2)
+    x = np.random.default_rng(4).standard_normal((m, k)).astype(np.float32) * np.float32(0.05)
+    gc, gs = repacked(gate, f, k)
+    uc, us = repacked(up, f, k)
+    edits = [Edit(1, nn, [SET, SCALE, ZERO][nn % 3], [nn * 0.5, -1.75, 0.0][nn % 3], 0, 6) for nn in range(10, 160)]
+    edits += [Edit(1, 7, SCALE, 1.0, 0, 6), Edit(1, 6911, SET, 10.0, 2, 4), Edit(0, 3, SET, 999.0, 0)]
+    words = np.array(table(edits, 3, 40), dtype=np.uint32)
+    td = dev(words.view(np.int32))
+    hi, lo = split_dev(x)
+    act = torch.empty((m, f), dtype=torch.float32, device="cuda")
+    ahi = torch.empty((m, f), dtype=torch.float16, device="cuda")
+    alo = torch.empty((m, f), dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _native.check(lib.fz_q4_0_gemm_gated(gc.data_ptr(), gs.data_ptr(), uc.data_ptr(), us.data_ptr(), f, k,
+                                         hi.data_ptr(), lo.data_ptr(), m, td.data_ptr(), 1, position, act.data_ptr(),
+                                         ahi.data_ptr(), alo.data_ptr(), err.data_ptr(), stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = act.cpu().numpy()
+    want = oracle.edit_apply(words, 1, position, oracle.gated(gate, up, f, k, x))
+    rel = np.sqrt(np.mean((got.astype(np.float64) - want) ** 2)) / np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    assert rel < 1e-3, rel
+    split = ahi.float().cpu().numpy() + alo.float().cpu().numpy()
+    assert np.abs(split - got).max() <= 1e-6 * max(1.0, np.abs(got).max())
+    for e in edits:
+        if e.layer == 1 and e.kind in (SET, ZERO):
+            for r in range(m):
+                if 40 + e.start <= position + r < 40 + e.until:
+                    assert got[r, e.neuron] == np.float32(e.value)
