@@ -29,7 +29,7 @@ constexpr int kBM = 128;              // rows of X a tile (the MMA's M)
 constexpr int kBK = 64;               // columns a stage: 128 B of f16 a row
 constexpr int kProducers = 8;         // weight-dequant warps (warps 2..9)
 constexpr int kThreadsG = 32 * (2 + kProducers);
-constexpr uint32_t kSpinLimit = 1u << 24;
+constexpr uint32_t kSpinLimit = 1u << 20;
 
 FZ_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
