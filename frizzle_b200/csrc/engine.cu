@@ -166,12 +166,20 @@ struct fz_batch {
   std::vector<bool> has_edits;
   float* captures = nullptr;
   uint64_t capture_floats = 0;
+  // Rows the per-row scratch holds (sequences x tokens of the widest step so
+  // far); grown on demand, which drops the captured graphs.
+  uint32_t rows_cap = 0;
+  __half *x16_hi = nullptr, *x16_lo = nullptr, *act16_hi = nullptr, *act16_lo = nullptr;
+  uint32_t* gemm_error = nullptr;  // set by a tensor-core product whose bounded wait gave up
+  uint32_t passes = 2;             // f16 passes over X in the tensor-core products (1 or 2)
+  std::vector<void*> row_allocs;
   // Host staging, two slots (at most two steps in flight, kernels/order.h:70).
   struct Slot {
     DeviceStep* step = nullptr;
     uint32_t* ids = nullptr;
     uint32_t* seeds = nullptr;
     uint32_t* records = nullptr;
+    uint32_t* error = nullptr;     // the tensor-core products' error word, read back
     cudaEvent_t copied = nullptr;  // the H2D copy of this slot has run
     cudaEvent_t done = nullptr;    // the step's records are home
     bool used = false;
@@ -184,11 +192,13 @@ struct fz_batch {
   ~fz_batch() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     for (void* p : allocations) cudaFree(p);
+    for (void* p : row_allocs) cudaFree(p);
     for (auto& s : slot) {
       if (s.step) cudaFreeHost(s.step);
       if (s.ids) cudaFreeHost(s.ids);
       if (s.seeds) cudaFreeHost(s.seeds);
       if (s.records) cudaFreeHost(s.records);
+      if (s.error) cudaFreeHost(s.error);
       if (s.copied) cudaEventDestroy(s.copied);
       if (s.done) cudaEventDestroy(s.done);
     }
@@ -200,6 +210,16 @@ struct fz_batch {
     if (e != cudaSuccess)
       return fail(FZ_ERR_FIT, "device allocation of " + std::to_string(bytes) + " bytes: " + cudaGetErrorString(e));
     allocations.push_back(v);
+    *p = static_cast<T*>(v);
+    return cudaMemset(v, 0, bytes ? bytes : 16) == cudaSuccess ? FZ_OK : fail(FZ_ERR_CUDA, "memset");
+  }
+  template <typename T>
+  fz_status alloc_row(T** p, size_t bytes) {
+    void* v = nullptr;
+    cudaError_t e = cudaMalloc(&v, bytes ? bytes : 16);
+    if (e != cudaSuccess)
+      return fail(FZ_ERR_FIT, "device allocation of " + std::to_string(bytes) + " bytes: " + cudaGetErrorString(e));
+    row_allocs.push_back(v);
     *p = static_cast<T*>(v);
     return cudaMemset(v, 0, bytes ? bytes : 16) == cudaSuccess ? FZ_OK : fail(FZ_ERR_CUDA, "memset");
   }
@@ -342,6 +362,42 @@ fz_status run_matvec(fz::MatvecArgs a, int pro, int epi, cudaStream_t stream, bo
   return FZ_OK;
 }
 
+// ------------------------------------------------------------ per-row scratch
+
+// (Re)allocates every buffer sized by the step's rows for `rows` rows.
+fz_status alloc_rows(fz_batch& b, uint32_t rows) {
+  const Shape& s = b.model->shape;
+  FZ_CUDA(cudaStreamSynchronize(b.model->dev->stream));
+  for (auto& kv : b.graphs) cudaGraphExecDestroy(kv.second);
+  b.graphs.clear();
+  for (void* p : b.row_allocs) cudaFree(p);
+  b.row_allocs.clear();
+  for (auto& sl : b.slot)
+    if (sl.ids) {
+      cudaFreeHost(sl.ids);
+      sl.ids = nullptr;
+    }
+  const uint32_t Q = s.heads * s.head_dim, KV = s.kv_heads * s.head_dim;
+  const size_t M = rows, X = std::max(s.hidden, Q);
+  b.counters_per_layer = 1 + rows * s.kv_heads;
+  fz_status st;
+  if ((st = b.alloc_row(&b.hidden_a, M * s.hidden * 4)) || (st = b.alloc_row(&b.hidden_b, M * s.hidden * 4)) ||
+      (st = b.alloc_row(&b.qkv, M * (Q + 2 * KV) * 4)) || (st = b.alloc_row(&b.q, M * Q * 4)) ||
+      (st = b.alloc_row(&b.attn, M * Q * 4)) || (st = b.alloc_row(&b.y_attn, M * s.hidden * 4)) ||
+      (st = b.alloc_row(&b.y_mlp, M * s.hidden * 4)) || (st = b.alloc_row(&b.act, M * s.ffn * 4)) ||
+      (st = b.alloc_row(&b.partial_o, M * s.heads * b.splits_max * s.head_dim * 4)) ||
+      (st = b.alloc_row(&b.partial_ml, M * s.heads * b.splits_max * 2 * 4)) ||
+      (st = b.alloc_row(&b.counters, (size_t)s.layers * b.counters_per_layer * 4)) ||
+      (st = b.alloc_row(&b.dids, M * 4)) || (st = b.alloc_row(&b.x16_hi, M * X * 2)) ||
+      (st = b.alloc_row(&b.x16_lo, M * X * 2)) || (st = b.alloc_row(&b.act16_hi, M * s.ffn * 2)) ||
+      (st = b.alloc_row(&b.act16_lo, M * s.ffn * 2)))
+    return st;
+  for (auto& sl : b.slot) FZ_CUDA(cudaMallocHost(&sl.ids, M * 4));
+  FZ_CUDA(cudaDeviceSynchronize());
+  b.rows_cap = rows;
+  return FZ_OK;
+}
+
 // ------------------------------------------------------------ the step chain
 
 fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
@@ -367,6 +423,105 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     e.seqs = b.S;
     FZ_CUDA(fz::launch_embed(e, st, pdl));
   }
+  if (M > (uint32_t)fz::kMaxTokens) {
+    // Wide step: per-row norms into f16, the products on the tensor cores.
+    __half* xlo = b.passes == 2 ? b.x16_lo : nullptr;
+    __half* alo = b.passes == 2 ? b.act16_lo : nullptr;
+    auto gemm = [&](const DevMatrix& w, const DevMatrix* up, const __half* xh, const __half* xl, float* out,
+                    uint32_t stride, int epi, uint32_t layer) -> fz_status {
+      fz::GemmArgs g{};
+      g.step = b.dstep;
+      g.w[0] = w.view();
+      if (up) g.w[1] = up->view();
+      g.m = M;
+      g.x_hi = xh;
+      g.x_lo = xl;
+      g.out = out;
+      g.out_stride = stride;
+      g.act_hi = b.act16_hi;
+      g.act_lo = alo;
+      g.edit_table = key.edits ? b.edit_tables : nullptr;
+      g.table_stride = b.table_words;
+      g.layer = layer;
+      g.seq_tokens = T;
+      g.capture_neurons = (cap && epi == fz::kGemmGated) ? cap + layer * cl.per_layer + cl.neurons : nullptr;
+      g.capture_stride = cl.per_layer * s.layers;
+      g.error = b.gemm_error;
+      FZ_CUDA(fz::launch_gemm(g, epi, st, pdl));
+      return FZ_OK;
+    };
+    for (uint32_t l = 0; l < s.layers; l++) {
+      const Layer& L = m.layers[l];
+      uint32_t* lc = b.counters + (size_t)l * b.counters_per_layer;
+      fz::MatvecArgs a{};
+      a.step = b.dstep;
+      a.m = M;
+      a.seq_tokens = T;
+      a.capture_stride = cl.per_layer * s.layers;
+      a.norm.hidden_in = b.hidden_a;
+      a.norm.y = l ? b.y_mlp : nullptr;
+      a.norm.post_gain = l ? m.layers[l - 1].post_ffw_norm : nullptr;
+      a.norm.gain = L.attn_norm;
+      a.norm.hidden_out = b.hidden_b;
+      a.norm.eps = s.eps;
+      a.norm.width = s.hidden;
+      a.norm.capture_residual = cap ? cap + l * cl.per_layer + cl.residual : nullptr;
+      a.norm.capture_added = (cap && l) ? cap + (l - 1) * cl.per_layer + cl.mlp_added : nullptr;
+      FZ_CUDA(fz::launch_norm_f16(a, b.x16_hi, xlo, st, pdl));
+      if ((stt = gemm(L.qkv, nullptr, b.x16_hi, xlo, b.qkv, L.qkv.n, fz::kGemmWrite, l))) return stt;
+      a.out = b.qkv;
+      a.out_stride = L.qkv.n;
+      a.rope.q_gain = L.q_norm;
+      a.rope.k_gain = L.k_norm;
+      a.rope.turns = L.turns;
+      a.rope.eps = s.eps;
+      a.rope.heads = s.heads;
+      a.rope.kv_heads = s.kv_heads;
+      a.rope.head_dim = s.head_dim;
+      a.rope.key_cache = b.kc[l];
+      a.rope.value_cache = b.vc[l];
+      a.rope.slots = b.slots[l];
+      a.rope.seq_stride = b.seq_stride[l];
+      a.rope.query_out = b.q;
+      a.rope.capture_query = cap ? cap + l * cl.per_layer + cl.query : nullptr;
+      FZ_CUDA(fz::launch_rope_rows(a, st, pdl));
+      fz::AttentionArgs at{};
+      at.step = b.dstep;
+      at.q = b.q;
+      at.key_cache = b.kc[l];
+      at.value_cache = b.vc[l];
+      at.seq_stride = b.seq_stride[l];
+      at.slots = b.slots[l];
+      at.heads = s.heads;
+      at.kv_heads = s.kv_heads;
+      at.head_dim = s.head_dim;
+      at.window = L.window;
+      at.seq_tokens = T;
+      at.m = M;
+      at.scale_log2e = (float)((double)(1.0f / std::sqrt((float)s.head_dim)) * 1.4426950408889634);
+      at.split_keys = kSplitKeys;
+      at.splits = (std::min(L.window, b.context) + kSplitKeys - 1) / kSplitKeys;
+      at.partial_o = b.partial_o;
+      at.partial_ml = b.partial_ml;
+      at.counters = lc + 1;
+      at.out = b.attn;
+      at.out_hi = b.x16_hi;
+      at.out_lo = xlo;
+      FZ_CUDA(fz::launch_attention(at, st, pdl));
+      if ((stt = gemm(L.o, nullptr, b.x16_hi, xlo, b.y_attn, s.hidden, fz::kGemmWrite, l))) return stt;
+      fz::MatvecArgs g = a;
+      g.norm.hidden_in = b.hidden_b;
+      g.norm.y = b.y_attn;
+      g.norm.post_gain = L.post_attn_norm;
+      g.norm.gain = L.ffn_norm;
+      g.norm.hidden_out = b.hidden_a;
+      g.norm.capture_residual = nullptr;
+      g.norm.capture_added = cap ? cap + l * cl.per_layer + cl.attn_added : nullptr;
+      FZ_CUDA(fz::launch_norm_f16(g, b.x16_hi, xlo, st, pdl));
+      if ((stt = gemm(L.gate, &L.up, b.x16_hi, xlo, nullptr, s.ffn, fz::kGemmGated, l))) return stt;
+      if ((stt = gemm(L.down, nullptr, b.act16_hi, alo, b.y_mlp, s.hidden, fz::kGemmWrite, l))) return stt;
+    }
+  } else
   for (uint32_t l = 0; l < s.layers; l++) {
     const Layer& L = m.layers[l];
     uint32_t* lc = b.counters + (size_t)l * b.counters_per_layer;
@@ -750,32 +905,23 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     b->seq_stride.push_back(per_seq);
     b->splits_max = std::max<uint32_t>(b->splits_max, (std::min(L.window, context) + kSplitKeys - 1) / kSplitKeys);
   }
-  const uint32_t Q = s.heads * s.head_dim, KV = s.kv_heads * s.head_dim;
-  b->counters_per_layer = 1 + M * s.kv_heads;
   b->table_words = 2 * s.layers + 5 * kMaxEdits;
   b->capture_floats = capture_layout(s).per_layer * s.layers;
   const uint32_t tiles = fz::select_tiles(s.vocab);
-  if ((st = b->alloc(&b->hidden_a, (size_t)M * s.hidden * 4)) || (st = b->alloc(&b->hidden_b, (size_t)M * s.hidden * 4)) ||
-      (st = b->alloc(&b->qkv, (size_t)M * (Q + 2 * KV) * 4)) || (st = b->alloc(&b->q, (size_t)M * Q * 4)) ||
-      (st = b->alloc(&b->attn, (size_t)M * Q * 4)) || (st = b->alloc(&b->y_attn, (size_t)M * s.hidden * 4)) ||
-      (st = b->alloc(&b->y_mlp, (size_t)M * s.hidden * 4)) || (st = b->alloc(&b->act, (size_t)M * s.ffn * 4)) ||
-      (st = b->alloc(&b->logits, (size_t)sequences * s.vocab * 4)) ||
-      (st = b->alloc(&b->partial_o, (size_t)M * s.heads * b->splits_max * s.head_dim * 4)) ||
-      (st = b->alloc(&b->partial_ml, (size_t)M * s.heads * b->splits_max * 2 * 4)) ||
-      (st = b->alloc(&b->counters, (size_t)s.layers * b->counters_per_layer * 4)) ||
-      (st = b->alloc(&b->argmax, (size_t)sequences * 8)) ||
+  if ((st = b->alloc(&b->logits, (size_t)sequences * s.vocab * 4)) || (st = b->alloc(&b->argmax, (size_t)sequences * 8)) ||
       (st = b->alloc(&b->tile_best, (size_t)sequences * tiles * 64 * 8)) ||
       (st = b->alloc(&b->candidates, (size_t)sequences * 128 * 4)) || (st = b->alloc(&b->records, (size_t)sequences * 16)) ||
-      (st = b->alloc(&b->dstep, sizeof(DeviceStep))) || (st = b->alloc(&b->dids, (size_t)M * 4)) ||
-      (st = b->alloc(&b->dseeds, (size_t)sequences * 8)) ||
+      (st = b->alloc(&b->dstep, sizeof(DeviceStep))) || (st = b->alloc(&b->dseeds, (size_t)sequences * 8)) ||
+      (st = b->alloc(&b->gemm_error, 16)) ||
       (st = b->alloc(&b->edit_tables, (size_t)sequences * b->table_words * 4)) ||
-      (st = b->alloc(&b->captures, (size_t)sequences * b->capture_floats * 4)))
+      (st = b->alloc(&b->captures, (size_t)sequences * b->capture_floats * 4)) || (st = alloc_rows(*b, M)))
     return st;
+  if (const char* v = std::getenv("FRIZZLE_B200_PASSES")) b->passes = std::atoi(v) == 1 ? 1u : 2u;
   b->has_edits.assign(sequences, false);
   for (auto& sl : b->slot) {
     FZ_CUDA(cudaMallocHost(&sl.step, sizeof(DeviceStep)));
-    FZ_CUDA(cudaMallocHost(&sl.ids, (size_t)M * 4));
     FZ_CUDA(cudaMallocHost(&sl.seeds, (size_t)sequences * 8));
+    FZ_CUDA(cudaMallocHost(&sl.error, 16));
     FZ_CUDA(cudaMallocHost(&sl.records, (size_t)sequences * 16));
     FZ_CUDA(cudaEventCreateWithFlags(&sl.copied, cudaEventDisableTiming));
     FZ_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
@@ -827,7 +973,7 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   if (!b || !step) return fail(FZ_ERR_ARGUMENT, "null argument");
   const Shape& s = b->model->shape;
   const uint32_t T = step->tokens;
-  if (T < 1 || T * b->S > (uint32_t)fz::kMaxTokens) return fail(FZ_ERR_NOT_SUPPORTED, "sequences x tokens above 16");
+  if (T < 1 || (uint64_t)T * b->S > (1u << 16)) return fail(FZ_ERR_NOT_SUPPORTED, "sequences x tokens above 65536");
   if (step->fed && T != 1) return fail(FZ_ERR_ARGUMENT, "a fed step is one token");
   if ((uint64_t)step->position + T > b->context) return fail(FZ_ERR_ARGUMENT, "the step runs past the context");
   if ((uint64_t)step->position + T > (1u << 24)) return fail(FZ_ERR_ARGUMENT, "position past 2^24 (interface.h:220)");
@@ -838,6 +984,13 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   if (step->logits && step->temperature > 0.f && step->top_k == 0) return fail(FZ_ERR_ARGUMENT, "top_k 0");
   cudaStream_t st = b->model->dev->stream;
   FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  if (T * b->S > b->rows_cap) {
+    uint32_t cap = 16;
+    while (cap < T * b->S) cap <<= 1;
+    fz_status gs;
+    if ((gs = alloc_rows(*b, cap))) return gs;
+    for (auto& x : b->slot) x.used = false;
+  }
   auto& sl = b->slot[b->next_slot];
   if (sl.used) FZ_CUDA(cudaEventSynchronize(sl.copied));
   std::memcpy(sl.step, step, sizeof(DeviceStep));
@@ -862,6 +1015,7 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
     FZ_CUDA(cudaGraphLaunch(exec, st));
   }
   FZ_CUDA(cudaMemcpyAsync(sl.records, b->records, (size_t)b->S * 16, cudaMemcpyDeviceToHost, st));
+  FZ_CUDA(cudaMemcpyAsync(sl.error, b->gemm_error, 4, cudaMemcpyDeviceToHost, st));
   FZ_CUDA(cudaEventRecord(sl.done, st));
   sl.used = true;
   b->last_slot = b->next_slot;
@@ -878,6 +1032,11 @@ fz_status fz_batch_wait(fz_batch* b, fz_record* records) {
   if (e != cudaSuccess) {
     const bool lost = e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure || e == cudaErrorECCUncorrectable;
     return fail(lost ? FZ_ERR_DEVICE_LOST : FZ_ERR_CUDA, std::string("step: ") + cudaGetErrorString(e));
+  }
+  if (*sl.error) {
+    const uint32_t code = *sl.error;
+    FZ_CUDA(cudaMemsetAsync(b->gemm_error, 0, 4, b->model->dev->stream));
+    return fail(FZ_ERR_CUDA, "a tensor-core product gave up waiting (code " + std::to_string(code) + ")");
   }
   if (records) std::memcpy(records, sl.records, (size_t)b->S * 16);
   return FZ_OK;

@@ -133,8 +133,16 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
   pdl_launch_dependents();
   if (nsplits == 1) {
 #pragma unroll
-    for (int h = 0; h < G; h++)
-      a.out[((size_t)row * a.heads + kvh * G + h) * kHeadDim + tid] = __fdiv_rn(o[h], s_l[h]);
+    for (int h = 0; h < G; h++) {
+      const size_t at = ((size_t)row * a.heads + kvh * G + h) * kHeadDim + tid;
+      const float v = __fdiv_rn(o[h], s_l[h]);
+      a.out[at] = v;
+      if (a.out_hi) {
+        const __half hh = __float2half_rn(v);
+        a.out_hi[at] = hh;
+        if (a.out_lo) a.out_lo[at] = __float2half_rn(__fsub_rn(v, __half2float(hh)));
+      }
+    }
     return;
   }
 #pragma unroll
@@ -166,7 +174,14 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttentionArgs a) {
       l = __fmaf_rn(__ldcg(a.partial_ml + (base + s) * 2 + 1), f, l);
       acc = __fmaf_rn(__ldcg(a.partial_o + (base + s) * kHeadDim + tid), f, acc);
     }
-    a.out[((size_t)row * a.heads + kvh * G + h) * kHeadDim + tid] = __fdiv_rn(acc, l);
+    const size_t at = ((size_t)row * a.heads + kvh * G + h) * kHeadDim + tid;
+    const float v = __fdiv_rn(acc, l);
+    a.out[at] = v;
+    if (a.out_hi) {
+      const __half hh = __float2half_rn(v);
+      a.out_hi[at] = hh;
+      if (a.out_lo) a.out_lo[at] = __float2half_rn(__fsub_rn(v, __half2float(hh)));
+    }
   }
   if (tid == 0) a.counters[row * a.kv_heads + kvh] = 0u;
 }

@@ -25,6 +25,8 @@ struct AttentionArgs {
   float* partial_ml;               // [m][heads][splits][2]
   uint32_t* counters;              // [m][kv_heads], zero between launches
   float* out;                      // [m][heads][d]
+  __half* out_hi;                  // [m][heads][d] f16 of out, or null
+  __half* out_lo;                  // its f16 remainder, or null
 };
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl);

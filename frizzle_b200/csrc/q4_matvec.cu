@@ -202,11 +202,10 @@ FZ_DEV void tree_reduce(float* part, int rows, float* total) {
 // invocation i of the reference is thread i, holding vec4s i, i + 256, ...
 // Leaves the normed rows in `rowbuf` [rows][width]; CTA 0 writes X after the
 // add to hidden_out and the captures of each sequence's last row.
-FZ_DEV void norm_rows_cta(const MatvecArgs& a, int rows, float* rowbuf, float* part, float* stat) {
-  const NormArgs& n = a.norm;
+FZ_DEV void norm_rows_cta(const MatvecArgs& a, const NormArgs& n, int rows, float* rowbuf, float* part, float* stat,
+                          bool writer) {
   const int tid = threadIdx.x, W = (int)n.width, V = W / 4;
   const float wf = (float)W;
-  const bool writer = blockIdx.x == 0;
   float* ry = stat;
   float* rx = stat + kMaxTokens;
   auto hrow_of = [&](int r) { return r * (int)n.row_of_token_stride + (int)n.row_of_token_offset; };
@@ -385,7 +384,7 @@ FZ_DEV void prologue(const MatvecArgs& a, const Smem& sm, const Geometry& geo) {
   const int M = (int)a.m, K = (int)a.mat[0].k;
   const float* rows = a.x;
   if (PRO == kPrologueNorm) {
-    norm_rows_cta(a, M, sm.rowbuf, sm.part, sm.stat);
+    norm_rows_cta(a, a.norm, M, sm.rowbuf, sm.part, sm.stat, blockIdx.x == 0);
     rows = sm.rowbuf;
   }
   for (int r = 0; r < 4 * MQ; r++)
@@ -614,6 +613,51 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(const MatvecArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- wide steps
+
+// The norm launch for many rows, one CTA a row (norm.wgsl:97-198): X after
+// the add to hidden_out, the normed row as f16 hi (and lo) for the tensor-core
+// products, the captures of each sequence's last row.
+__global__ void __launch_bounds__(kThreads) norm_f16_kernel(const MatvecArgs a, __half* out_hi, __half* out_lo) {
+  __shared__ __align__(16) float rowbuf[8192];
+  __shared__ float part[kThreads];
+  __shared__ float stat[2 * kMaxTokens];
+  pdl_wait();
+  NormArgs n = a.norm;
+  n.row_of_token_stride = 1;
+  n.row_of_token_offset = blockIdx.x;
+  norm_rows_cta(a, n, 1, rowbuf, part, stat, true);
+  const int W = (int)n.width;
+  __half* hi = out_hi + (size_t)blockIdx.x * W;
+  __half* lo = out_lo ? out_lo + (size_t)blockIdx.x * W : nullptr;
+  for (int i = threadIdx.x; i < W; i += kThreads) {
+    const float v = rowbuf[i];
+    const __half h = __float2half_rn(v);
+    hi[i] = h;
+    if (lo) lo[i] = __float2half_rn(__fsub_rn(v, __half2float(h)));
+  }
+  pdl_launch_dependents();
+}
+
+// QK-norm, RoPE and the KV append for many rows: one warp a (row, head).
+__global__ void __launch_bounds__(kThreads) rope_rows_kernel(const MatvecArgs a) {
+  pdl_wait();
+  const RopeArgs& r = a.rope;
+  const int heads = (int)(r.heads + 2 * r.kv_heads);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int item = blockIdx.x * kWarps + warp;
+  if (item < (int)a.m * heads) {
+    const int row = item / heads, head = item % heads;
+    const uint32_t seq = (uint32_t)row / a.seq_tokens;
+    const uint32_t pos = (a.step ? a.step->position : a.position) + (uint32_t)row % a.seq_tokens;
+    float* cq = (r.capture_query && (uint32_t)row % a.seq_tokens == a.seq_tokens - 1)
+                    ? r.capture_query + seq * a.capture_stride
+                    : nullptr;
+    rope_head_warp(r, a.out, a.out_stride, row, head, seq, pos, cq, lane);
+  }
+  pdl_launch_dependents();
+}
+
 // ---------------------------------------------------------------- repack
 
 __global__ void repack_kernel(const uint8_t* __restrict__ file, uint32_t n, uint32_t k, uint4* codes,
@@ -825,6 +869,39 @@ cudaError_t launch_matvec(const MatvecArgs& a, int prologue, int epilogue, cudaS
     }
   }
   return cudaErrorInvalidValue;
+}
+
+namespace {
+cudaError_t launch_plain(const void* fn, dim3 grid, dim3 block, cudaStream_t stream, bool pdl, void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, fn, args);
+  if (e != cudaSuccess) (void)cudaGetLastError();
+  return e;
+}
+}  // namespace
+
+cudaError_t launch_norm_f16(const MatvecArgs& a, __half* out_hi, __half* out_lo, cudaStream_t stream, bool pdl) {
+  if (a.norm.width > 8192 || a.norm.width % 4 || a.m == 0) return cudaErrorInvalidValue;
+  MatvecArgs copy = a;
+  void* args[] = {&copy, &out_hi, &out_lo};
+  return launch_plain((const void*)norm_f16_kernel, dim3(a.m), dim3(kThreads), stream, pdl, args);
+}
+
+cudaError_t launch_rope_rows(const MatvecArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.rope.head_dim != 256 || a.m == 0) return cudaErrorInvalidValue;
+  const uint32_t items = a.m * (a.rope.heads + 2 * a.rope.kv_heads);
+  MatvecArgs copy = a;
+  void* args[] = {&copy};
+  return launch_plain((const void*)rope_rows_kernel, dim3((items + kWarps - 1) / kWarps), dim3(kThreads), stream, pdl,
+                      args);
 }
 
 cudaError_t launch_repack(const uint8_t* file_blocks, uint32_t n, uint32_t k, uint4* codes, uint2* scales,

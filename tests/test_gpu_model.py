@@ -23,8 +23,10 @@ def prompt(shape, n, seed=0):
     return np.random.default_rng([seed, n]).integers(2, shape.vocab, size=n).astype(np.uint32)
 
 
-def run_both(path, shape, n_prompt, steps, edits=None, capture=True, context=4096):
-    """Greedy decode on the GPU and the oracle; returns per-step comparisons."""
+def run_both(path, shape, n_prompt, steps, edits=None, capture=True, context=4096, block=16):
+    """Greedy decode on the GPU and the oracle; returns per-step comparisons.
+    The prompt is prefilled in steps of `block` tokens: up to 16 rows run the
+    skinny tensor-core matvec, more rows the tcgen05 GEMM path."""
     dev = engine.Device(0)
     model = engine.Model.from_file(dev, path)
     batch = engine.Batch(model, 1, context)
@@ -36,10 +38,10 @@ def run_both(path, shape, n_prompt, steps, edits=None, capture=True, context=409
         words = np.array(table(edits, shape.layers, n_prompt - 1), dtype=np.uint32)
         batch.set_edits(0, words)
     out = {"tokens_gpu": [], "tokens_cpu": [], "logit_rms": [], "logit_abs": [], "cap_rms": [], "cap_abs": []}
-    # Prefill in blocks of 16 (the skinny path's rows), the last asking for logits.
+    # Prefill in blocks, the last asking for logits.
     pos = 0
     while pos < n_prompt:
-        t = min(16, n_prompt - pos)
+        t = min(block, n_prompt - pos)
         last = pos + t == n_prompt
         batch.step(pos, ids[pos:pos + t], tokens=t, logits=last, capture=capture and last)
         pos += t
@@ -148,3 +150,33 @@ def test_tiny_model_sampled_draw(tiny_model_path):
     batch.free()
     model.free()
     dev.close()
+
+
+def test_tiny_model_wide_prefill(tiny_model_path):
+    # A 40-token prompt in one step: every product on the tcgen05 GEMM path.
+    assert_parity(run_both(tiny_model_path, synth.TINY, 40, 8, block=40))
+
+
+def test_tiny_model_wide_prefill_steered(tiny_model_path):
+    edits = [Edit(3, 5, SET, 8.0, 0), Edit(3, 100, SCALE, -2.5, 0), Edit(4, 900, ZERO, 0.0, 0, 3)]
+    out = run_both(tiny_model_path, synth.TINY, 33, 6, edits=edits, block=33)
+    assert_parity(out)
+
+
+def test_gemma_1b_config1_one_step_prefill(gemma_model_path):
+    # Config 1's 32-token prompt as one step (32 rows: the GEMM path), then decode.
+    assert_parity(run_both(gemma_model_path, synth.GEMMA3_1B, 32, 32, block=32))
+
+
+def test_gemma_1b_config1_one_step_prefill_steered(gemma_model_path):
+    s = synth.GEMMA3_1B
+    rng = np.random.default_rng(13)
+    idx = rng.choice(s.ffn, size=8, replace=False)
+    vals = rng.uniform(-10, 10, size=8).astype(np.float32)
+    edits = [Edit(13, int(i), SET, float(v), 0) for i, v in zip(idx, vals)]
+    assert_parity(run_both(gemma_model_path, s, 32, 32, edits=edits, block=32))
+
+
+def test_gemma_1b_256_token_prefill(gemma_model_path):
+    # A 256-token prompt in one step, two 128-row tiles of the GEMM, then decode.
+    assert_parity(run_both(gemma_model_path, synth.GEMMA3_1B, 256, 8, block=256))
