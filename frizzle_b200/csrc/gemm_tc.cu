@@ -144,7 +144,8 @@ FZ_DEV Codes load_codes(const Q4Matrix& w, uint32_t rg, uint32_t bp, bool live, 
 // each of its four code words gives, per row, the f16 pairs at columns
 // (2t, 2t+1) and (16 + 2t, 17 + 2t) of half h of block kb.  A row group past
 // the matrix is written as zeros (its codes were never loaded).
-FZ_DEV void dequant_tile(unsigned char* tile, uint32_t row0, const Codes& x, bool live, int lane) {
+FZ_DEV void dequant_tile(unsigned char* tile, unsigned char* tile_lo, uint32_t row0, const Codes& x, bool live,
+                         int lane) {
   const uint32_t g = lane >> 2, t = lane & 3;
   const uint32_t kMask = 0x000F000Fu, kMagic = 0x64006400u;
   const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408u));
@@ -154,18 +155,29 @@ FZ_DEV void dequant_tile(unsigned char* tile, uint32_t row0, const Codes& x, boo
     const uint32_t kb = wi >> 1, h = wi & 1;
     const uint32_t wd = words[wi];
     const uint32_t sw = kb ? x.s.y : x.s.x;
-    const __half2 dg = __half2half2(__ushort_as_half((unsigned short)(sw & 0xffffu)));
-    const __half2 dg8 = __half2half2(__ushort_as_half((unsigned short)(sw >> 16)));
     const uint32_t k0 = 32 * kb + 8 * h + 2 * t;
-    const __half2 g_lo = __hmul2(__hsub2(u2h((wd & kMask) | kMagic), bias), dg);
-    const __half2 g_hi = __hmul2(__hsub2(u2h(((wd >> 4) & kMask) | kMagic), bias), dg);
-    const __half2 e_lo = __hmul2(__hsub2(u2h(((wd >> 8) & kMask) | kMagic), bias), dg8);
-    const __half2 e_hi = __hmul2(__hsub2(u2h(((wd >> 12) & kMask) | kMagic), bias), dg8);
     const uint32_t r0 = row0 + g, r8 = row0 + g + 8;
-    *reinterpret_cast<uint32_t*>(tile + swz(r0, k0)) = live ? h2u(g_lo) : 0u;
-    *reinterpret_cast<uint32_t*>(tile + swz(r0, k0 + 16)) = live ? h2u(g_hi) : 0u;
-    *reinterpret_cast<uint32_t*>(tile + swz(r8, k0)) = live ? h2u(e_lo) : 0u;
-    *reinterpret_cast<uint32_t*>(tile + swz(r8, k0 + 16)) = live ? h2u(e_hi) : 0u;
+    // (code - 8) exactly, as f16 pairs: rows g and g + 8, columns k0 (+1) and k0 + 16 (+1).
+    const __half2 c4[4] = {__hsub2(u2h((wd & kMask) | kMagic), bias), __hsub2(u2h(((wd >> 4) & kMask) | kMagic), bias),
+                           __hsub2(u2h(((wd >> 8) & kMask) | kMagic), bias),
+                           __hsub2(u2h(((wd >> 12) & kMask) | kMagic), bias)};
+    const uint32_t rows[4] = {r0, r0, r8, r8};
+    const uint32_t cols[4] = {k0, k0 + 16, k0, k0 + 16};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float d = __half2float(__ushort_as_half((unsigned short)(j < 2 ? (sw & 0xffffu) : (sw >> 16))));
+      const float2 q = __half22float2(c4[j]);
+      // (code - 8) * d is exact in f32; hi is it rounded once to f16, lo the
+      // remainder (exact in f32, rounded once to f16).
+      const float w0 = __fmul_rn(q.x, d), w1 = __fmul_rn(q.y, d);
+      const __half2 hi = __floats2half2_rn(w0, w1);
+      *reinterpret_cast<uint32_t*>(tile + swz(rows[j], cols[j])) = live ? h2u(hi) : 0u;
+      if (tile_lo) {
+        const float2 hf = __half22float2(hi);
+        const __half2 lo = __floats2half2_rn(__fsub_rn(w0, hf.x), __fsub_rn(w1, hf.y));
+        *reinterpret_cast<uint32_t*>(tile_lo + swz(rows[j], cols[j])) = live ? h2u(lo) : 0u;
+      }
+    }
   }
 }
 
@@ -188,20 +200,24 @@ FZ_DEV float apply_edit_table(const uint32_t* table, uint32_t layer, uint32_t ne
   return v;
 }
 
-template <int BN, int PASSES>
+template <int BN, int XP, int WP>
 struct Layout {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
-  static constexpr int kStageBytes = kABytes * PASSES + kBBytes;
+  static constexpr int kStageBytes = kABytes * XP + kBBytes * WP;
   static constexpr int kStages = (196 * 1024) / kStageBytes > 6 ? 6 : (196 * 1024) / kStageBytes;
   static constexpr int kSmem = kStages * kStageBytes + 1024;  // + alignment slack
 };
 
-template <int BN, int PASSES, int EPI>
+// XP: passes over X (f16 hi, + lo); WP: passes over W (f16 hi, + lo).  The
+// MMAs per 16 columns: X_hi.W_hi, X_lo.W_hi (XP = 2), X_hi.W_lo (WP = 2); the
+// dropped X_lo.W_lo term is below 2^-22 relative.
+template <int BN, int XP, int WP, int EPI>
 __global__ void __launch_bounds__(kThreadsG, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
                 const GemmArgs a) {
-  using L = Layout<BN, PASSES>;
+  constexpr int PASSES = XP;
+  using L = Layout<BN, XP, WP>;
   constexpr int S = L::kStages;
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full[S];
@@ -210,7 +226,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   __shared__ uint32_t tmem_base;
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   auto a_tile = [&](int s, int p) { return smem + s * L::kStageBytes + p * L::kABytes; };
-  auto b_tile = [&](int s) { return smem + s * L::kStageBytes + PASSES * L::kABytes; };
+  auto b_tile = [&](int s) { return smem + s * L::kStageBytes + XP * L::kABytes; };
+  auto b_tile_lo = [&](int s) { return smem + s * L::kStageBytes + XP * L::kABytes + L::kBBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t m0 = blockIdx.y * kBM;
@@ -263,14 +280,15 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       fence_after_sync();
       if (lane == 0) {
         const uint64_t db = smem_desc(b_tile(s));
+        const uint64_t db_lo = smem_desc(b_tile_lo(s));
+        const uint64_t da = smem_desc(a_tile(s, 0));
+        const uint64_t da_lo = smem_desc(a_tile(s, XP - 1));
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; kk++) {
-#pragma unroll
-          for (int p = 0; p < PASSES; p++) {
-            const uint64_t da = smem_desc(a_tile(s, p));
-            // 16 columns of f16 = 32 bytes along K: +2 in the 16-byte address field.
-            umma(tmem, da + 2 * kk, db + 2 * kk, idesc, (kt | kk | p) != 0 ? 1u : 0u);
-          }
+          // 16 columns of f16 = 32 bytes along K: +2 in the 16-byte address field.
+          umma(tmem, da + 2 * kk, db + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
+          if (XP == 2) umma(tmem, da_lo + 2 * kk, db + 2 * kk, idesc, 1u);
+          if (WP == 2) umma(tmem, da + 2 * kk, db_lo + 2 * kk, idesc, 1u);
         }
         umma_commit(&empty[s]);
       }
@@ -310,7 +328,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       unsigned char* tile = b_tile(s);
 #pragma unroll
       for (int j = 0; j < kMine; j++)
-        dequant_tile(tile, (uint32_t)(pw + j * kProducers) * 16, cur[j], rg_of(j) < mat_of(j).n / 16, lane);
+        dequant_tile(tile, WP == 2 ? b_tile_lo(s) : nullptr, (uint32_t)(pw + j * kProducers) * 16, cur[j],
+                     rg_of(j) < mat_of(j).n / 16, lane);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[s]);
@@ -425,13 +444,14 @@ bool make_map(CUtensorMap* map, const __half* base, uint32_t rows, uint32_t cols
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int PASSES, int EPI>
+template <int BN, int XP, int WP, int EPI>
 cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
-  using L = Layout<BN, PASSES>;
+  constexpr int PASSES = XP;
+  using L = Layout<BN, XP, WP>;
   static std::once_flag once;
   static cudaError_t configured = cudaSuccess;
   std::call_once(once, [] {
-    configured = cudaFuncSetAttribute(gemm_kernel<BN, PASSES, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    configured = cudaFuncSetAttribute(gemm_kernel<BN, XP, WP, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       L::kSmem);
   });
   if (configured != cudaSuccess) return configured;
@@ -449,7 +469,7 @@ cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, PASSES, EPI>, map_hi, map_lo, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, XP, WP, EPI>, map_hi, map_lo, a);
   if (e != cudaSuccess) (void)cudaGetLastError();
   return e;
 }
@@ -461,13 +481,14 @@ cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bo
   // TMA wants 16-byte aligned rows: K f16 values a row, K a multiple of 64.
   if ((reinterpret_cast<uintptr_t>(a.x_hi) & 15) || (a.x_lo && (reinterpret_cast<uintptr_t>(a.x_lo) & 15)))
     return cudaErrorInvalidValue;
+  // Exact weights (WP = 2) go with both halves of X: the f32-level product.
   const bool two = a.x_lo != nullptr;
   if (epilogue == kGemmGated) {
     if (!a.act_hi || a.w[1].n != a.w[0].n || a.w[1].k != a.w[0].k) return cudaErrorInvalidValue;
-    return two ? launch_tiles<256, 2, kGemmGated>(a, stream, pdl) : launch_tiles<256, 1, kGemmGated>(a, stream, pdl);
+    return two ? launch_tiles<128, 2, 2, kGemmGated>(a, stream, pdl) : launch_tiles<256, 1, 1, kGemmGated>(a, stream, pdl);
   }
   if (!a.out) return cudaErrorInvalidValue;
-  return two ? launch_tiles<256, 2, kGemmWrite>(a, stream, pdl) : launch_tiles<256, 1, kGemmWrite>(a, stream, pdl);
+  return two ? launch_tiles<128, 2, 2, kGemmWrite>(a, stream, pdl) : launch_tiles<256, 1, 1, kGemmWrite>(a, stream, pdl);
 }
 
 cudaError_t launch_split_f16(const float* x, size_t n, __half* hi, __half* lo, cudaStream_t stream) {
