@@ -198,6 +198,53 @@ def head_roofline(torch, lib, native, reps=20):
     return bytes_, secs
 
 
+def gemm_roofline(torch, lib, native, m=4096, reps=10):
+    """The prefill's dominant product (gate and up, 1152 -> 2 x 6912, GELU and
+    the f16 hand-off) on the tensor cores at m rows, timed alone."""
+    import numpy as np
+    from frizzle_b200 import synth
+    f, k = 6912, 1152
+    mats = []
+    for seed in (1, 2):
+        blocks = synth.random_q4_0(f, k, seed=seed)
+        src = torch.from_numpy(blocks).cuda()
+        codes = torch.empty(lib.fz_q4_0_codes_bytes(f, k), dtype=torch.uint8, device="cuda")
+        scales = torch.empty(lib.fz_q4_0_scales_bytes(f, k), dtype=torch.uint8, device="cuda")
+        native.check(lib.fz_q4_0_repack(src.data_ptr(), f, k, codes.data_ptr(), scales.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream))
+        mats.append((codes, scales))
+    x = torch.randn(m, k, device="cuda") * 0.05
+    hi = torch.empty(m, k, dtype=torch.float16, device="cuda")
+    lo = torch.empty(m, k, dtype=torch.float16, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    native.check(lib.fz_split_f16(x.data_ptr(), m * k, hi.data_ptr(), lo.data_ptr(), s))
+    ahi = torch.empty(m, f, dtype=torch.float16, device="cuda")
+    alo = torch.empty(m, f, dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    (gc, gs), (uc, us) = mats
+    out = {}
+    for passes in (2, 1):
+        def run():
+            native.check(lib.fz_q4_0_gemm_gated(gc.data_ptr(), gs.data_ptr(), uc.data_ptr(), us.data_ptr(), f, k,
+                                                hi.data_ptr(), lo.data_ptr() if passes == 2 else None, m, None, 0, 0,
+                                                None, ahi.data_ptr(), alo.data_ptr() if passes == 2 else None,
+                                                err.data_ptr(), s))
+        for _ in range(3):
+            run()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            run()
+        b.record()
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        secs = a.elapsed_time(b) / 1000.0 / reps
+        out[passes] = secs
+    flops = 2.0 * m * (2 * f) * k
+    return flops, out
+
+
 def traffic_from_profile():
     p = os.path.join(ROOT, "profiles", "head_matvec_traffic.json")
     if os.path.exists(p):
@@ -324,6 +371,34 @@ def run_ours(args):
                              "peak_source": which, "algorithmic_bytes": head_bytes,
                              "launch_us": head_secs * 1e6, "traffic": traffic_from_profile()},
                 "clocks": clocks.summary()}
+        # a 4096-token prompt prefilled in one step (the tcgen05 path).
+        pre = engine.Batch(model, 1, 8192)
+        ids4k = np.random.default_rng([rank, 4096]).integers(2, synth.GEMMA3_1B.vocab, size=4096).astype(np.uint32)
+        pre.step(0, ids4k, tokens=4096, logits=True)
+        pre.wait()
+        pstream = torch.cuda.ExternalStream(dev.stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(pstream):
+            e0.record()
+        pre.step(0, ids4k, tokens=4096, logits=True)
+        with torch.cuda.stream(pstream):
+            e1.record()
+        pre.wait()
+        p4k = e0.elapsed_time(e1) / 1000.0
+        pre.free()
+        gflops, gsecs = gemm_roofline(torch, lib, _native)
+        _, bf16, _ = peaks()
+        line["prefill_4096"] = {"tokens_per_s": 4096 / p4k, "ms": 1000.0 * p4k,
+                                "workload": "BASELINE config 3: 4096 seeded ids in one step, 26 layers, "
+                                            "f32-level products (three tcgen05 MMAs a k-slice)",
+                                "tflops_algorithmic": 6.03e12 / p4k / 1e12}
+        line["prefill_gemm_roofline"] = {
+            "bound": "tensor", "kernel": "tcgen05 gated product 1152 -> 2 x 6912 at M = 4096",
+            "unit": "TFLOP/s", "peak": bf16, "algorithmic_flops": gflops,
+            "f32_level": {"achieved": gflops / gsecs[2] / 1e12, "frac": gflops / gsecs[2] / 1e12 / bf16,
+                          "us": gsecs[2] * 1e6, "mmas_per_k_slice": 3},
+            "f16_one_pass": {"achieved": gflops / gsecs[1] / 1e12, "frac": gflops / gsecs[1] / 1e12 / bf16,
+                             "us": gsecs[1] * 1e6, "mmas_per_k_slice": 1}}
         if world == 1 and not args.no_cpu_baseline:
             v, threads, sample = cpu_decode_sample(path)
             line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
