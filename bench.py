@@ -420,6 +420,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-only", action="store_true",
+                    help="time only the tensor-core gated product at M = 4096 and print its numbers")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
     args = ap.parse_args()
@@ -427,6 +429,16 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.gemm_only:
+        import torch
+        from frizzle_b200 import _native
+        flops, secs = gemm_roofline(torch, _native.load(), _native, reps=args.steps)
+        _, bf16, _ = peaks()
+        print(json.dumps({"kernel": "tcgen05 gated product 1152 -> 2 x 6912, M = 4096",
+                          "tflops": {p: flops / t / 1e12 for p, t in secs.items()},
+                          "frac": {p: flops / t / 1e12 / bf16 for p, t in secs.items()},
+                          "us": {p: t * 1e6 for p, t in secs.items()}}))
+        return 0
     return run_ours(args)
 
 

@@ -351,24 +351,25 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       const uint32_t quarter = (uint32_t)warp & 3u;
       const uint32_t row = m0 + quarter * 32 + lane;
       const uint32_t lane_addr = tmem + ((quarter * 32u) << 16);
+      // The stages are idle once the accumulator is full: each epilogue warp
+      // turns its 32 rows x 32 columns around through shared memory, so every
+      // global store covers consecutive columns of one row.
+      float* stage = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * 33;
       if (ok) {
         if (EPI == kGemmWrite) {
           const uint32_t N = a.w[0].n;
           for (int c0 = 0; c0 < BN; c0 += 32) {
             uint32_t r[32];
             tmem_ld32(lane_addr + (uint32_t)c0, r);
-            if (row < a.m) {
-              float* o = a.out + (size_t)row * a.out_stride + n0 + c0;
-              if (n0 + c0 + 32 <= N) {
 #pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                  *reinterpret_cast<float4*>(o + i) = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
-                                                                  __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-              } else {
-                for (int i = 0; i < 32; i++)
-                  if (n0 + c0 + i < N) o[i] = __uint_as_float(r[i]);
-              }
+            for (int i = 0; i < 32; i++) stage[lane * 33 + i] = __uint_as_float(r[i]);
+            __syncwarp();
+            const uint32_t n = n0 + (uint32_t)c0 + lane;
+            for (int rr = 0; rr < 32; rr++) {
+              const uint32_t orow = m0 + quarter * 32 + rr;
+              if (orow < a.m && n < N) a.out[(size_t)orow * a.out_stride + n] = stage[rr * 33 + lane];
             }
+            __syncwarp();
           }
         } else {
           const uint32_t F = a.w[0].n;
@@ -379,21 +380,30 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             uint32_t gr[32], ur[32];
             tmem_ld32(lane_addr + (uint32_t)c0, gr);
             tmem_ld32(lane_addr + half_bn + (uint32_t)c0, ur);
-            if (row < a.m) {
 #pragma unroll
-              for (int i = 0; i < 32; i++) {
-                const uint32_t neuron = n0 + c0 + i;
-                if (neuron >= F) continue;
-                float v = __fmul_rn(gelu_tanh(__uint_as_float(gr[i])), __uint_as_float(ur[i]));
-                if (a.edit_table) v = apply_edit_table(a.edit_table + seq * a.table_stride, a.layer, neuron, pos, v);
-                const size_t at = (size_t)row * F + neuron;
-                if (a.out) a.out[(size_t)row * a.out_stride + neuron] = v;
+            for (int i = 0; i < 32; i++) {
+              const uint32_t neuron = n0 + c0 + i;
+              float v = __fmul_rn(gelu_tanh(__uint_as_float(gr[i])), __uint_as_float(ur[i]));
+              if (a.edit_table && row < a.m && neuron < F)
+                v = apply_edit_table(a.edit_table + seq * a.table_stride, a.layer, neuron, pos, v);
+              if (a.capture_neurons && last && row < a.m && neuron < F)
+                a.capture_neurons[seq * a.capture_stride + neuron] = v;
+              stage[lane * 33 + i] = v;
+            }
+            __syncwarp();
+            const uint32_t n = n0 + (uint32_t)c0 + lane;
+            for (int rr = 0; rr < 32; rr++) {
+              const uint32_t orow = m0 + quarter * 32 + rr;
+              if (orow < a.m && n < F) {
+                const float v = stage[rr * 33 + lane];
+                const size_t at = (size_t)orow * F + n;
+                if (a.out) a.out[(size_t)orow * a.out_stride + n] = v;
                 const __half hi = __float2half_rn(v);
                 a.act_hi[at] = hi;
                 if (a.act_lo) a.act_lo[at] = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-                if (a.capture_neurons && last) a.capture_neurons[seq * a.capture_stride + neuron] = v;
               }
             }
+            __syncwarp();
           }
         }
       }
