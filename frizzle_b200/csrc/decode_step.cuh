@@ -1,0 +1,82 @@
+// The whole decode step (one token for each of up to 8 sequences) as one
+// persistent kernel: every layer's norms, products, QK-norm/RoPE, attention
+// and steering, then the final norm and the tied head, in one launch.
+//
+// Frizzle runs the step as ~300 dispatches (graph/graph.h:189-199); at batch 1
+// the separate launches cost more than the 563 MB the step reads.  Here one
+// CTA per SM walks the step's phases in order; a phase that needs another
+// phase's whole output (the product's input vector) waits on a counter in
+// global memory that the producing CTAs raise, and each CTA's weight tiles
+// stream into a shared-memory ring by bulk copies (cp.async.bulk) issued by a
+// producer warp that runs ahead of the phases, so the weights of the next
+// phases arrive while the current phase waits.
+#pragma once
+
+#include "q4_matvec.cuh"
+
+namespace fz {
+
+// One layer as the decode kernel reads it (a device array of these).
+struct DecodeLayer {
+  Q4Matrix qkv, o, gate, up, down;
+  const float *attn_norm, *q_norm, *k_norm, *post_attn_norm, *ffn_norm, *post_ffw_norm;
+  const float* turns;              // RoPE theta_k / 2 pi, [d/2]
+  uint16_t *key_cache, *value_cache;
+  uint64_t seq_stride;             // cache elements between sequences
+  uint32_t slots, window;
+};
+
+constexpr uint32_t kDecodeMaxRows = 8;      // sequences one decode launch takes
+constexpr uint32_t kDecodeOSlices = 2;      // K slices of the output projection
+constexpr uint32_t kDecodeDownSlices = 4;   // K slices of the down projection
+constexpr uint32_t kDecodeSyncFixed = 8;    // per-layer phase counters
+constexpr uint32_t kDecodeMaxGroup = 6;     // query heads a KV head may serve
+
+struct DecodeArgs {
+  const DeviceStep* step;          // position (every row is one sequence's next token)
+  const DecodeLayer* layers;       // [n_layers], device memory
+  uint32_t n_layers;
+  uint32_t m;                      // sequences = rows
+  uint32_t hidden, ffn, heads, kv_heads;
+  float eps, scale_log2e;
+  float* hidden_a;                 // [m][hidden]: the embedding rows in, the residual stream
+  float* hidden_b;                 // [m][hidden]
+  float* qkv;                      // [m][(heads + 2 kv_heads) 256] raw products
+  float* attn;                     // [m][heads 256]
+  float* y_attn;                   // [kDecodeOSlices][m][hidden] output-projection partials
+  float* act;                      // [m][ffn]
+  float* y_mlp;                    // [kDecodeDownSlices][m][hidden] down-projection partials
+  float* partial_o;                // [m][heads][max_splits][256] attention split partials
+  float* partial_ml;               // [m][heads][max_splits][2]
+  uint32_t max_splits;
+  uint32_t* sync;                  // decode_sync_words(...) words, zero at launch
+  const uint32_t* edit_table;      // sequence 0's edit table, or null
+  uint64_t table_stride;           // words between sequences' tables
+  float* capture;                  // sequence 0's capture store, or null
+  uint64_t capture_stride;         // floats between sequences' stores
+  uint64_t cap_residual, cap_query, cap_attn_added, cap_neurons, cap_mlp_added, cap_per_layer;
+  Q4Matrix head;                   // tied embedding
+  const float* output_norm;
+  float* logits;                   // [m][vocab], or null for no head
+  unsigned long long* argmax;      // [m], cleared before the launch
+  uint32_t* error;                 // nonzero when a bounded wait gave up
+};
+
+inline size_t decode_sync_words(uint32_t layers, uint32_t rows, uint32_t kv_heads) {
+  return (size_t)layers * (kDecodeSyncFixed + (size_t)rows * kv_heads);
+}
+
+// Whether the decode kernel takes this shape (head_dim 256, the grouping,
+// hidden/ffn multiples of the slices, at most kDecodeMaxRows rows).
+bool decode_supported(uint32_t rows, uint32_t hidden, uint32_t ffn, uint32_t heads, uint32_t kv_heads,
+                      uint32_t head_dim);
+
+// Raises the kernel's shared-memory limit on the current device for this
+// shape (both row counts); call before the first launch and outside stream
+// capture.
+cudaError_t prepare_decode(uint32_t hidden, uint32_t ffn, uint32_t heads, uint32_t kv_heads);
+
+// Cooperative launch, one CTA per SM.
+cudaError_t launch_decode(const DecodeArgs& a, cudaStream_t stream);
+
+}  // namespace fz

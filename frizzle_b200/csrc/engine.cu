@@ -15,6 +15,7 @@
 #include <vector>
 
 #include "frizzle_b200.h"
+#include "decode_step.cuh"
 #include "gemm_tc.cuh"
 #include "gguf_index.h"
 #include "kernels.cuh"
@@ -170,7 +171,12 @@ struct fz_batch {
   // far); grown on demand, which drops the captured graphs.
   uint32_t rows_cap = 0;
   __half *x16_hi = nullptr, *x16_lo = nullptr, *act16_hi = nullptr, *act16_lo = nullptr;
-  uint32_t* gemm_error = nullptr;  // set by a tensor-core product whose bounded wait gave up
+  uint32_t* gemm_error = nullptr;  // set by a device wait (tensor-core product, decode step) that gave up
+  // The persistent decode step: its per-layer view, K-slice partials, phase counters.
+  fz::DecodeLayer* dlayers = nullptr;
+  float* y_parts = nullptr;        // [O slices + down slices][rows][hidden]
+  uint32_t* dsync = nullptr;
+  size_t dsync_words = 0;
   uint32_t passes = 2;             // f16 passes over X in the tensor-core products (1 or 2)
   std::vector<void*> row_allocs;
   // Host staging, two slots (at most two steps in flight, kernels/order.h:70).
@@ -392,6 +398,10 @@ fz_status alloc_rows(fz_batch& b, uint32_t rows) {
       (st = b.alloc_row(&b.x16_lo, M * X * 2)) || (st = b.alloc_row(&b.act16_hi, M * s.ffn * 2)) ||
       (st = b.alloc_row(&b.act16_lo, M * s.ffn * 2)))
     return st;
+  b.dsync_words = fz::decode_sync_words(s.layers, rows, s.kv_heads);
+  if ((st = b.alloc_row(&b.y_parts, (fz::kDecodeOSlices + fz::kDecodeDownSlices) * M * s.hidden * 4)) ||
+      (st = b.alloc_row(&b.dsync, b.dsync_words * 4)))
+    return st;
   for (auto& sl : b.slot) FZ_CUDA(cudaMallocHost(&sl.ids, M * 4));
   FZ_CUDA(cudaDeviceSynchronize());
   b.rows_cap = rows;
@@ -399,6 +409,13 @@ fz_status alloc_rows(fz_batch& b, uint32_t rows) {
 }
 
 // ------------------------------------------------------------ the step chain
+
+// The persistent decode kernel serves one-token steps unless
+// FRIZZLE_B200_LAYERED=1 asks for the per-operation launches.
+bool decode_step_enabled() {
+  const char* v = std::getenv("FRIZZLE_B200_LAYERED");
+  return !(v && *v && *v != '0');
+}
 
 fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
   fz_model& m = *b.model;
@@ -422,6 +439,63 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     e.argmax = b.argmax;
     e.seqs = b.S;
     FZ_CUDA(fz::launch_embed(e, st, pdl));
+  }
+  if (T == 1 && decode_step_enabled() &&
+      fz::decode_supported(b.S, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim)) {
+    // One token for each sequence: the whole step in one persistent kernel.
+    FZ_CUDA(cudaMemsetAsync(b.dsync, 0, b.dsync_words * 4, st));
+    fz::DecodeArgs d{};
+    d.step = b.dstep;
+    d.layers = b.dlayers;
+    d.n_layers = s.layers;
+    d.m = b.S;
+    d.hidden = s.hidden;
+    d.ffn = s.ffn;
+    d.heads = s.heads;
+    d.kv_heads = s.kv_heads;
+    d.eps = s.eps;
+    d.scale_log2e = (float)((double)(1.0f / std::sqrt((float)s.head_dim)) * 1.4426950408889634);
+    d.hidden_a = b.hidden_a;
+    d.hidden_b = b.hidden_b;
+    d.qkv = b.qkv;
+    d.attn = b.attn;
+    d.y_attn = b.y_parts;
+    d.act = b.act;
+    d.y_mlp = b.y_parts + (size_t)fz::kDecodeOSlices * b.S * s.hidden;
+    d.partial_o = b.partial_o;
+    d.partial_ml = b.partial_ml;
+    d.max_splits = b.splits_max;
+    d.sync = b.dsync;
+    d.edit_table = key.edits ? b.edit_tables : nullptr;
+    d.table_stride = b.table_words;
+    d.capture = cap;
+    d.capture_stride = cl.per_layer * s.layers;
+    d.cap_residual = cl.residual;
+    d.cap_query = cl.query;
+    d.cap_attn_added = cl.attn_added;
+    d.cap_neurons = cl.neurons;
+    d.cap_mlp_added = cl.mlp_added;
+    d.cap_per_layer = cl.per_layer;
+    d.head = m.embd.view();
+    d.output_norm = m.output_norm;
+    d.logits = key.logits ? b.logits : nullptr;
+    d.argmax = b.argmax;
+    d.error = b.gemm_error;
+    FZ_CUDA(fz::launch_decode(d, st));
+    if (key.logits) {
+      fz::SelectArgs se{};
+      se.step = b.dstep;
+      se.logits = b.logits;
+      se.vocab = s.vocab;
+      se.seqs = b.S;
+      se.argmax = b.argmax;
+      se.seeds = b.dseeds;
+      se.tile_best = b.tile_best;
+      se.candidates = b.candidates;
+      se.records = b.records;
+      FZ_CUDA(fz::launch_select(se, st, pdl));
+    }
+    return FZ_OK;
   }
   if (M > (uint32_t)fz::kMaxTokens) {
     // Wide step: per-row norms into f16, the products on the tensor cores.
@@ -905,6 +979,34 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     b->seq_stride.push_back(per_seq);
     b->splits_max = std::max<uint32_t>(b->splits_max, (std::min(L.window, context) + kSplitKeys - 1) / kSplitKeys);
   }
+  {
+    std::vector<fz::DecodeLayer> dl(s.layers);
+    for (uint32_t l = 0; l < s.layers; l++) {
+      const Layer& L = m->layers[l];
+      fz::DecodeLayer& d = dl[l];
+      d.qkv = L.qkv.view();
+      d.o = L.o.view();
+      d.gate = L.gate.view();
+      d.up = L.up.view();
+      d.down = L.down.view();
+      d.attn_norm = L.attn_norm;
+      d.q_norm = L.q_norm;
+      d.k_norm = L.k_norm;
+      d.post_attn_norm = L.post_attn_norm;
+      d.ffn_norm = L.ffn_norm;
+      d.post_ffw_norm = L.post_ffw_norm;
+      d.turns = L.turns;
+      d.key_cache = b->kc[l];
+      d.value_cache = b->vc[l];
+      d.seq_stride = b->seq_stride[l];
+      d.slots = b->slots[l];
+      d.window = L.window;
+    }
+    if ((st = b->alloc(&b->dlayers, dl.size() * sizeof(fz::DecodeLayer)))) return st;
+    if (fz::decode_supported(1, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim))
+      FZ_CUDA(fz::prepare_decode(s.hidden, s.ffn, s.heads, s.kv_heads));
+    FZ_CUDA(cudaMemcpy(b->dlayers, dl.data(), dl.size() * sizeof(fz::DecodeLayer), cudaMemcpyHostToDevice));
+  }
   b->table_words = 2 * s.layers + 5 * kMaxEdits;
   b->capture_floats = capture_layout(s).per_layer * s.layers;
   const uint32_t tiles = fz::select_tiles(s.vocab);
@@ -1036,7 +1138,7 @@ fz_status fz_batch_wait(fz_batch* b, fz_record* records) {
   if (*sl.error) {
     const uint32_t code = *sl.error;
     FZ_CUDA(cudaMemsetAsync(b->gemm_error, 0, 4, b->model->dev->stream));
-    return fail(FZ_ERR_CUDA, "a tensor-core product gave up waiting (code " + std::to_string(code) + ")");
+    return fail(FZ_ERR_CUDA, "a device wait gave up (code " + std::to_string(code) + ")");
   }
   if (records) std::memcpy(records, sl.records, (size_t)b->S * 16);
   return FZ_OK;

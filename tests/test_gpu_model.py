@@ -180,3 +180,78 @@ def test_gemma_1b_config1_one_step_prefill_steered(gemma_model_path):
 def test_gemma_1b_256_token_prefill(gemma_model_path):
     # A 256-token prompt in one step, two 128-row tiles of the GEMM, then decode.
     assert_parity(run_both(gemma_model_path, synth.GEMMA3_1B, 256, 8, block=256))
+
+
+def run_batch(path, shape, S, n_prompt, steps, edit_sets=None, context=4096):
+    """S sequences stepped together (one decode launch serves them all), each
+    against its own oracle run; prompts differ per sequence."""
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, path)
+    batch = engine.Batch(model, S, context)
+    prompts = [prompt(shape, n_prompt, seed=11 + s) for s in range(S)]
+    words = []
+    for s in range(S):
+        es = (edit_sets or [None] * S)[s]
+        w = np.array(table(es, shape.layers, n_prompt - 1), dtype=np.uint32) if es else None
+        batch.set_edits(s, w)
+        words.append(w)
+    block = max(1, 16 // S)
+    pos = 0
+    while pos < n_prompt:
+        t = min(block, n_prompt - pos)
+        ids = np.array([p[pos:pos + t] for p in prompts], dtype=np.uint32)
+        batch.step(pos, ids, tokens=t, logits=pos + t == n_prompt)
+        pos += t
+    got_tokens, got_logits = [], []
+    for i in range(steps):
+        got_tokens.append(batch.tokens())
+        got_logits.append([batch.logits(s) for s in range(S)])
+        if i + 1 < steps:
+            batch.step(n_prompt + i, fed=True, tokens=1, logits=True)
+    batch.free()
+    model.free()
+    dev.close()
+    worst_rms = worst_abs = 0.0
+    for s in range(S):
+        orc = oracle.OracleModel(path, context=context)
+        want, _ = orc.step(0, prompts[s], logits=True, edit_table=words[s])
+        for i in range(steps):
+            tok = int(np.argmax(want))
+            assert got_tokens[i][s] == tok, (s, i, got_tokens[i][s], tok)
+            worst_rms = max(worst_rms, rel_rms(got_logits[i][s], want))
+            worst_abs = max(worst_abs, max_abs(got_logits[i][s], want))
+            if i + 1 < steps:
+                want, _ = orc.step(n_prompt + i, [tok], logits=True, edit_table=words[s])
+        orc.close()
+    assert worst_rms < REL_RMS, worst_rms
+    assert worst_abs < MAX_ABS, worst_abs
+
+
+@pytest.mark.parametrize("S", [3, 6])
+def test_tiny_model_batch_decode(tiny_model_path, S):
+    # 3 sequences: one column quad of the decode kernel's fragments; 6: two.
+    edit_sets = [None] * S
+    edit_sets[1] = [Edit(3, 5, SET, 8.0, 0), Edit(4, 900, ZERO, 0.0, 0, 3)]
+    run_batch(tiny_model_path, synth.TINY, S, 12, 8, edit_sets=edit_sets)
+
+
+def test_tiny_model_layered_decode(tiny_model_path, monkeypatch):
+    # The per-operation launches (FRIZZLE_B200_LAYERED=1) stay a working path.
+    monkeypatch.setenv("FRIZZLE_B200_LAYERED", "1")
+    assert_parity(run_both(tiny_model_path, synth.TINY, 21, 8))
+
+
+def test_tiny_model_decode_attention_splits(tiny_model_path):
+    # 700 prompt tokens: the global layer's decode attention spans two
+    # 512-key splits, folded by the last CTA.
+    assert_parity(run_both(tiny_model_path, synth.TINY, 700, 4, block=700))
+
+
+def test_gemma_1b_steered_pair_decode(gemma_model_path):
+    # A steered sequence and its unsteered twin stepped together (config 4's pairing).
+    s = synth.GEMMA3_1B
+    rng = np.random.default_rng(4)
+    idx = rng.choice(s.ffn, size=5, replace=False)
+    vals = rng.uniform(-10, 10, size=5).astype(np.float32)
+    edits = [Edit(13, int(i), SET, float(v), 0) for i, v in zip(idx, vals)]
+    run_batch(gemma_model_path, s, 2, 32, 8, edit_sets=[edits, None])
