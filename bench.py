@@ -424,6 +424,8 @@ def main():
                     help="time only the tensor-core gated product at M = 4096 and print its numbers")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
+    ap.add_argument("--trace", action="store_true",
+                    help="print the decode kernel's phase timeline (device timestamps), averaged over steps")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -439,7 +441,92 @@ def main():
                           "frac": {p: flops / t / 1e12 / bf16 for p, t in secs.items()},
                           "us": {p: t * 1e6 for p, t in secs.items()}}))
         return 0
+    if args.trace:
+        return run_trace(args)
     return run_ours(args)
+
+
+PHASES = ("qkv", "attention", "o", "gate_up", "down", "head")
+
+
+def run_trace(args):
+    """The persistent decode kernel's timeline: per phase, the time from the
+    previous phase's last CTA finishing to this phase's last CTA having its
+    inputs (hand-off: counter, wait, prologue) and from then to its last CTA
+    finishing (work), in microseconds, the mean over layers and steps."""
+    import ctypes as C
+    import numpy as np
+    from frizzle_b200 import engine, synth
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, synth.model_path(synth.GEMMA3_1B, 0))
+    batch = engine.Batch(model, 1, 4096)
+    ids = np.random.default_rng([0, PROMPT]).integers(2, synth.GEMMA3_1B.vocab, size=PROMPT).astype(np.uint32)
+    for pos in range(0, PROMPT, 16):
+        batch.step(pos, ids[pos:pos + 16], tokens=16, logits=pos + 16 == PROMPT)
+    batch.wait()
+    lib = batch.lib
+    engine.check(lib.fz_batch_trace(batch.handle, 1))
+    ctas, events = C.c_uint32(), C.c_uint32()
+    engine.check(lib.fz_batch_read_trace(batch.handle, None, 0, C.byref(ctas), C.byref(events)))
+    L = synth.GEMMA3_1B.layers
+    hand = np.zeros((L, 6)), np.zeros((L, 6))
+    spread = [{k: [] for k in ("work_median", "work_max", "ready_first", "ready_last", "counter_seen_last",
+                               "prologue_median", "compute_median", "finish_median")} for _ in range(6)]
+    totals = []
+    tails = []
+    pos, n = PROMPT, 0
+    for i in range(args.warmup + args.steps):
+        batch.step(pos, fed=True, tokens=1, logits=True)
+        batch.wait()
+        pos += 1
+        if i < args.warmup:
+            continue
+        buf = np.zeros(ctas.value * events.value, dtype=np.uint64)
+        engine.check(lib.fz_batch_read_trace(batch.handle, buf.ctypes.data, buf.size, None, None))
+        body = L * 6 * 5
+        tail = buf.reshape(ctas.value, events.value)[:, body:].astype(np.float64)
+        tails.append(tail)
+        t = buf.reshape(ctas.value, events.value)[:, :body].reshape(ctas.value, L, 6, 5).astype(np.float64)
+        t[t == 0] = np.nan
+        t0 = np.nanmin(t)
+        t = (t - t0) / 1000.0
+        prev = 0.0
+        for l in range(L):
+            for ph in range(6):
+                if ph == 5 and l != L - 1:
+                    continue
+                seen = np.nanmax(t[:, l, ph, 1])
+                ready = np.nanmax(t[:, l, ph, 2])
+                done = np.nanmax(t[:, l, ph, 4])
+                per = t[:, l, ph, 4] - t[:, l, ph, 2]
+                spread[ph]["compute_median"].append(np.nanmedian(t[:, l, ph, 3] - t[:, l, ph, 2]))
+                spread[ph]["finish_median"].append(np.nanmedian(t[:, l, ph, 4] - t[:, l, ph, 3]))
+                spread[ph]["counter_seen_last"].append(seen - prev)
+                spread[ph]["prologue_median"].append(np.nanmedian(t[:, l, ph, 2] - t[:, l, ph, 1]))
+                spread[ph]["work_median"].append(np.nanmedian(per))
+                spread[ph]["work_max"].append(np.nanmax(per))
+                spread[ph]["ready_first"].append(np.nanmin(t[:, l, ph, 2]) - prev)
+                spread[ph]["ready_last"].append(ready - prev)
+                hand[0][l, ph] += ready - prev
+                hand[1][l, ph] += done - ready
+                prev = done
+        totals.append(prev)
+        n += 1
+    out = {"steps": n, "kernel_us": float(np.mean(totals)), "phases": {}}
+    tl = np.mean(np.stack(tails), axis=0)  # [ctas][9], ns
+    out["tile_wait_us_per_cta"] = {name: float(np.mean(tl[:, i]) / 1000.0) for i, name in enumerate(PHASES)}
+    out["issuer"] = {"wait_us": float(np.mean(tl[:, 6]) / 1000.0), "issue_us": float(np.mean(tl[:, 7]) / 1000.0),
+                     "tiles": float(np.mean(tl[:, 8]))}
+    for ph, name in enumerate(PHASES):
+        rows = range(L - 1, L) if ph == 5 else range(L)
+        out["phases"][name] = {"handoff_us": float(np.mean([hand[0][l, ph] for l in rows]) / n),
+                               "work_us": float(np.mean([hand[1][l, ph] for l in rows]) / n)}
+        out["phases"][name].update({k: float(np.mean(v)) for k, v in spread[ph].items()})
+    print(json.dumps(out))
+    batch.free()
+    model.free()
+    dev.close()
+    return 0
 
 
 if __name__ == "__main__":

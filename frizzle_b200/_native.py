@@ -70,6 +70,8 @@ SIGNATURES = {
     "fz_capture_floats": (C.c_size_t, [VP]),
     "fz_batch_read_capture": (C.c_int, [VP, U32, VP, C.c_size_t]),
     "fz_batch_cache": (C.c_int, [VP, U32, U32, C.c_int, C.POINTER(VP), C.POINTER(U32)]),
+    "fz_batch_trace": (C.c_int, [VP, C.c_int]),
+    "fz_batch_read_trace": (C.c_int, [VP, VP, C.c_size_t, C.POINTER(U32), C.POINTER(U32)]),
     "fz_q4_0_codes_bytes": (C.c_size_t, [U32, U32]),
     "fz_q4_0_scales_bytes": (C.c_size_t, [U32, U32]),
     "fz_q4_0_repack": (C.c_int, [VP, U32, U32, VP, VP, VP]),

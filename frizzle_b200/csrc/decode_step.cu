@@ -2,7 +2,7 @@
 //
 // Grid: one CTA per SM, launched cooperatively so every CTA is resident.
 // Block: 8 consumer warps (the norm's 256 invocations, the products, the
-// attention) and one producer warp whose lane 0 streams weight tiles.
+// attention) and a producer warp whose lane 0 issues the weight copies.
 //
 // Every CTA walks the same sequence of phases:
 //   for each layer: QKV (norm prologue) -> attention (QK-norm, RoPE, KV
@@ -17,16 +17,19 @@
 // depend on timing.
 //
 // Weight tiles (a row group's block pairs, codes then scales) move from HBM to
-// a ring of shared-memory slots by cp.async.bulk, completing on the slot's
-// full mbarrier; the consumers release a slot on its empty mbarrier.  The
-// producer walks the same phase sequence without waiting on counters, so it
-// runs up to a ring ahead of the consumers, across phase and layer bounds.
+// a ring of S shared-memory slots by cp.async.bulk, completing on the slot's
+// full mbarrier; each consumer warp releases a slot on its empty mbarrier
+// when it has used the tile.  The producer follows the CTA's tile sequence
+// with a cursor (TileCursor) and refills each slot as soon as it is released,
+// without waiting on phase counters, so the weights of the next phases arrive
+// while the current phase waits.  The norm and the attention run in
+// functions of their own, so their registers do not add to the products'.
 //
 // Every wait is bounded (2 s by the global timer, and an iteration cap); a
 // wait that gives up records an error word for the host and the CTA abandons
 // the step; other CTAs see the error word in their own waits.  Consumer
 // barriers that follow a possible give-up are barrier reductions, so all
-// consumer warps leave together.
+// consumer warps leave together; copies in flight land before the CTA exits.
 #include <algorithm>
 #include <mutex>
 
@@ -47,14 +50,17 @@ constexpr uint32_t kHd = 256;           // head dimension
 constexpr uint32_t kKeysPerSplit = 512;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint32_t kWaitIters = 1u << 30;
+constexpr int kNormVec = 3;             // vec4s of a row an invocation holds (hidden <= 3072)
+// Tasks whose partials are reduced together.
+__host__ __device__ constexpr uint32_t red_slots(int MQ) { return MQ == 1 ? 4u : 2u; }
 
 enum : uint32_t { kPhQkv = 0, kPhO = 1, kPhGate = 2, kPhDown = 3, kPhHead = 4 };
 enum : uint32_t { kSyncQkv = 0, kSyncAttn = 1, kSyncO = 2, kSyncGate = 3, kSyncDown = 4 };
-enum : uint32_t { kErrCounter = 0x100u, kErrFull = 0x200u, kErrEmpty = 0x400u, kErrDrain = 0x800u };
+enum : uint32_t { kErrCounter = 0x100u, kErrFull = 0x200u, kErrEmpty = 0x400u, kErrDrain = 0x800u, kErrTile = 0x1000u };
 
 template <int MQ>
 __host__ __device__ constexpr uint32_t ring_slots() {
-  return MQ == 1 ? 8u : 6u;
+  return MQ == 1 ? 8u : 5u;
 }
 
 __host__ __device__ inline uint32_t slice_kb(uint32_t k, uint32_t D) { return 2u * ((k / 64u + D - 1u) / D); }
@@ -72,10 +78,7 @@ __host__ __device__ inline uint32_t active_ctas(uint32_t nrg, uint32_t D, uint32
   return D * (P < nrg ? P : nrg);
 }
 
-// Shared memory of one CTA (byte offsets).
-struct DLayout {
-  uint32_t codes, scales, full, empty, uni, xf, rowbuf, part, stat, red, best, flags, total;
-};
+using DLayout = DecodeLayout;
 
 __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t hidden, uint32_t group,
                                               uint32_t nkb) {
@@ -103,13 +106,32 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   L.stat = o;
   o += 2u * kDecodeMaxRows * 4u;
   L.red = o;
-  o += kCW * 2u * 16u * 4u * MQ * 4u;
+  o += red_slots(MQ) * kCW * 2u * 16u * 4u * MQ * 4u;
+  L.task_rg = o;
+  o += red_slots(MQ) * 4u;
+  o = (o + 7u) & ~7u;
   L.best = o;
   o += kDecodeMaxRows * 8u;
   L.flags = o;
   o += 16u;
+  o = (o + 15u) & ~15u;
+  L.gains = o;
+  o += 2u * hidden * 4u;
+  L.tags = o;
+  o += slots * 4u;
+  L.uses = o;
+  o += slots * 4u;
   L.total = o;
   return L;
+}
+
+// Every region at the alignment its accesses need: bulk-copy destinations
+// 128 bytes, vector and cp.async accesses 16, mbarriers and 64-bit words 8.
+__host__ __device__ inline bool layout_aligned(const DLayout& L) {
+  return L.codes % 128 == 0 && L.scales % 128 == 0 && L.full % 8 == 0 && L.empty % 8 == 0 && L.uni % 128 == 0 &&
+         L.xf % 16 == 0 && L.rowbuf % 16 == 0 && L.part % 16 == 0 && L.stat % 16 == 0 && L.red % 16 == 0 &&
+         L.task_rg % 4 == 0 && L.best % 8 == 0 && L.flags % 4 == 0 && L.gains % 16 == 0 && L.tags % 4 == 0 &&
+         L.uses % 4 == 0;
 }
 
 // ------------------------------------------------------------ primitives
@@ -164,6 +186,12 @@ FZ_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
                : "memory");
 }
 
+// 16 bytes global -> shared without registers (waited for by cp_async_wait).
+FZ_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+FZ_DEV void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Consumer-warp barriers (named barrier 1; the producer warp never joins).
 FZ_DEV void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 FZ_DEV bool cbar_or(bool p) {
@@ -194,9 +222,11 @@ FZ_DEV bool wait_counter(const uint32_t* ctr, uint32_t target, uint32_t* err) {
   atomicOr(err, kErrCounter);
   return false;
 }
+// Raised by one thread after a barrier of the CTA's consumers: the release
+// orders every consumer's earlier stores before the count (the arrive of a
+// generic grid barrier; the waiter's acquire pairs with it).
 FZ_DEV void raise_counter(uint32_t* ctr) {
-  __threadfence();
-  atomicAdd(ctr, 1u);
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
 }
 
 FZ_DEV float2 h2f2(uint32_t u) { return __half22float2(bits_h2(u)); }
@@ -206,452 +236,394 @@ FZ_DEV float4 scale4(float4 v, float s, float4 g) {
   return make_float4(mul(mul(v.x, s), g.x), mul(mul(v.y, s), g.y), mul(mul(v.z, s), g.z), mul(mul(v.w, s), g.w));
 }
 
+// The CTA's dynamic shared memory (regions at the offsets in DecodeArgs::lay).
+extern __shared__ __align__(1024) unsigned char g_smem[];
+
 // ------------------------------------------------------------ the walk
 
-// Both roles walk this sequence; the producer issues each tile, the consumers
-// wait for it, use it and release it.
+// One phase's products for CTA c: its row groups rg0, rg0 + rstep, ... < rend
+// over block pairs [bp0, bp1) of w (and of w2, the up projection, after w's
+// tiles of each task).  ph: 0 QKV, 1 O, 2 gate/up, 3 down, 4 head.
+struct PhaseGeo {
+  const Q4Matrix* w;
+  const Q4Matrix* w2;
+  uint32_t bp0, bp1, rg0, rstep, rend, d;
+  bool has;
+};
+
+FZ_DEV PhaseGeo phase_geo(const DecodeArgs& a, uint32_t l, uint32_t ph, uint32_t c, uint32_t G) {
+  PhaseGeo g;
+  if (ph == 4) {
+    const uint32_t nrg = a.head.n / 16;
+    g.w = &a.head;
+    g.w2 = nullptr;
+    g.bp0 = 0;
+    g.bp1 = a.head.k / 64;
+    g.rg0 = (uint32_t)((uint64_t)c * nrg / G);
+    g.rend = (uint32_t)((uint64_t)(c + 1) * nrg / G);
+    g.rstep = 1;
+    g.d = 0;
+    g.has = a.logits != nullptr && g.rg0 < g.rend;
+    return g;
+  }
+  const DecodeLayer& L = a.layers[l];
+  const uint32_t D = ph == 1 ? kDecodeOSlices : ph == 3 ? kDecodeDownSlices : 1u;
+  g.w = ph == 0 ? &L.qkv : ph == 1 ? &L.o : ph == 2 ? &L.gate : &L.down;
+  g.w2 = ph == 2 ? &L.up : nullptr;
+  const uint32_t P = G / D, nrg = g.w->n / 16, nbp = g.w->k / 64;
+  g.d = c % D;
+  g.bp0 = g.d * nbp / D;
+  g.bp1 = (g.d + 1) * nbp / D;
+  g.rg0 = c / D;
+  g.rstep = P;
+  g.rend = nrg;
+  g.has = g.rg0 < P && g.rg0 < nrg && g.bp0 < g.bp1;
+  return g;
+}
+
 template <class V>
-FZ_DEV void matvec_phase(V& v, uint32_t kind, uint32_t l, const Q4Matrix& w, const Q4Matrix* w2, uint32_t D,
-                         uint32_t c, uint32_t G) {
-  const uint32_t P = G / D, d = c % D, i0 = c / D;
-  const uint32_t nrg = w.n / 16, nbp = w.k / 64;
-  const uint32_t bp0 = d * nbp / D, bp1 = (d + 1) * nbp / D;
-  const bool has = i0 < P && i0 < nrg && bp0 < bp1;
-  if (!v.phase_begin(kind, l, has, 2 * bp0, 2 * (bp1 - bp0))) return;
-  if (has) {
-    for (uint32_t rg = i0; rg < nrg; rg += P) {
-      for (uint32_t b = bp0; b < bp1; b += kSlotBp) v.tile(w, rg, b, min(kSlotBp, bp1 - b), 0u);
-      if (w2)
-        for (uint32_t b = bp0; b < bp1; b += kSlotBp) v.tile(*w2, rg, b, min(kSlotBp, bp1 - b), 1u);
-      v.task_end(kind, l, rg, d);
+FZ_DEV void matvec_phase(const DecodeArgs& a, V& v, uint32_t kind, uint32_t l) {
+  const PhaseGeo g = phase_geo(a, l, kind, blockIdx.x, gridDim.x);
+  if (!v.phase_begin(kind, l, g.has, 2 * g.bp0, 2 * (g.bp1 - g.bp0))) return;
+  if (g.has) {
+#pragma unroll 1
+    for (uint32_t rg = g.rg0; rg < g.rend; rg += g.rstep) {
+#pragma unroll 1
+      for (uint32_t b = g.bp0; b < g.bp1; b += kSlotBp) v.tile(rg, b, min(kSlotBp, g.bp1 - b), 0u);
+      if (g.w2) {
+#pragma unroll 1
+        for (uint32_t b = g.bp0; b < g.bp1; b += kSlotBp) v.tile(rg, b, min(kSlotBp, g.bp1 - b), 1u);
+      }
+      v.task_end(kind, l, rg, g.d);
       if (v.aborted()) return;
     }
   }
-  v.phase_end(kind, l, has);
+  v.phase_end(kind, l, g.has);
 }
 
 template <class V>
 FZ_DEV void walk(const DecodeArgs& a, V& v) {
-  const uint32_t G = gridDim.x, c = blockIdx.x;
+#pragma unroll 1
   for (uint32_t l = 0; l < a.n_layers; l++) {
-    const DecodeLayer& L = a.layers[l];
-    matvec_phase(v, kPhQkv, l, L.qkv, nullptr, 1, c, G);
+    matvec_phase(a, v, kPhQkv, l);
     v.attention(l);
-    matvec_phase(v, kPhO, l, L.o, nullptr, kDecodeOSlices, c, G);
-    matvec_phase(v, kPhGate, l, L.gate, &L.up, 1, c, G);
-    matvec_phase(v, kPhDown, l, L.down, nullptr, kDecodeDownSlices, c, G);
+    matvec_phase(a, v, kPhO, l);
+    matvec_phase(a, v, kPhGate, l);
+    matvec_phase(a, v, kPhDown, l);
     if (v.aborted()) return;
   }
-  if (!a.logits) return;
-  // The head: a contiguous range of row groups a CTA, whole row groups a warp.
-  const Q4Matrix& w = a.head;
-  const uint32_t nrg = w.n / 16, nbp = w.k / 64;
-  const uint32_t r0 = (uint32_t)((uint64_t)c * nrg / G), r1 = (uint32_t)((uint64_t)(c + 1) * nrg / G);
-  if (!v.phase_begin(kPhHead, a.n_layers, r0 < r1, 0, 2 * nbp)) return;
-  for (uint32_t rg = r0; rg < r1; rg++) {
-    for (uint32_t b = 0; b < nbp; b += kSlotBp)
-      v.head_tile(w, rg, b, min(kSlotBp, nbp - b), rg - r0, b == 0, b + kSlotBp >= nbp);
-    if (v.aborted()) return;
-  }
-  v.phase_end(kPhHead, a.n_layers, r0 < r1);
+  if (a.logits) matvec_phase(a, v, kPhHead, a.n_layers - 1);
 }
 
-// ------------------------------------------------------------ producer
-
-template <int MQ>
-struct Producer {
-  static constexpr uint32_t S = ring_slots<MQ>();
-  const DecodeArgs& a;
-  unsigned char* codes;
-  unsigned char* scales;
-  uint64_t* full;
-  uint64_t* empty;
-  volatile uint32_t* flags;
-  uint32_t idx;
-  bool dead;
-
-  FZ_DEV bool aborted() {
-    if (!dead && flags[0]) dead = true;
-    return dead;
-  }
-  FZ_DEV bool phase_begin(uint32_t, uint32_t, bool, uint32_t, uint32_t) { return !aborted(); }
-  FZ_DEV void tile(const Q4Matrix& w, uint32_t rg, uint32_t b, uint32_t nb, uint32_t) {
-    if (aborted()) return;
-    const uint32_t slot = idx % S, use = idx / S;
-    if (use > 0 && !mb_wait(empty + slot, (use - 1) & 1u, a.error, flags)) {
-      if (!flags[0] && !error_word(a.error)) atomicOr(a.error, kErrEmpty);
-      dead = true;
-      return;
-    }
-    const size_t at = (size_t)rg * (w.k / 64) + b;
-    mb_expect_tx(full + slot, nb * 576u);
-    bulk_g2s(codes + (size_t)slot * kSlotCodes, reinterpret_cast<const unsigned char*>(w.codes) + at * 512, nb * 512u,
-             full + slot);
-    bulk_g2s(scales + (size_t)slot * kSlotScales, reinterpret_cast<const unsigned char*>(w.scales) + at * 64,
-             nb * 64u, full + slot);
-    idx++;
-  }
-  FZ_DEV void head_tile(const Q4Matrix& w, uint32_t rg, uint32_t b, uint32_t nb, uint32_t, bool, bool) {
-    tile(w, rg, b, nb, 0);
-  }
-  FZ_DEV void task_end(uint32_t, uint32_t, uint32_t, uint32_t) {}
-  FZ_DEV void phase_end(uint32_t, uint32_t, bool) {}
-  FZ_DEV void attention(uint32_t) {}
-  // Copies in flight must land before the CTA exits: every slot's last fill.
-  FZ_DEV void drain() {
-    const uint32_t n = idx < S ? idx : S;
-    for (uint32_t k = idx - n; k < idx; k++)
-      if (!mb_wait(full + k % S, (k / S) & 1u, nullptr, nullptr)) atomicOr(a.error, kErrDrain);
-  }
+// The CTA's tile sequence as walk() consumes it, one tile at a time: the
+// copies run ahead of the consumers by following this cursor.
+struct TileCursor {
+  PhaseGeo g;
+  uint32_t l, ph, rg, b, which;
+  bool end;
 };
 
-// ------------------------------------------------------------ consumers
+FZ_DEV uint32_t tile_tag(uint32_t l, uint32_t ph, uint32_t rg, uint32_t b, uint32_t which) {
+  return (rg * 64u + b) ^ (which << 23) ^ (ph << 24) ^ (l << 27);
+}
 
-template <int MQ>
-struct Consumer {
-  static constexpr uint32_t S = ring_slots<MQ>();
-  static constexpr int R = 4 * MQ;  // rows of X the fragments carry
-  const DecodeArgs& a;
-  unsigned char* sm;
-  DLayout ly;
-  const uint4* codes;
-  const uint2* scales;
-  uint64_t* full;
-  uint64_t* empty;
-  uint2* xf;
-  float* rowbuf;
-  float* part;
-  float* stat;
-  float* red;
-  unsigned long long* best;
-  volatile uint32_t* flags;
-  uint32_t idx, kb_base, M, pos, W;
-  int tid, warp, lane, g, t;
-  bool fail, dead;
-  float acc[2][MQ][2];
-  unsigned long long hbest[MQ];
-
-  FZ_DEV bool aborted() const { return dead; }
-  // A barrier that also agrees on whether any consumer thread gave up.
-  FZ_DEV bool sync_dead() {
-    dead = cbar_or(fail);
-    if (dead && tid == 0) flags[0] = 1u;
-    return dead;
-  }
-  FZ_DEV uint32_t* sync_of(uint32_t l) { return a.sync + (size_t)l * W; }
-  FZ_DEV void zero_acc() {
-#pragma unroll
-    for (int w = 0; w < 2; w++)
-#pragma unroll
-      for (int q = 0; q < MQ; q++) acc[w][q][0] = acc[w][q][1] = 0.f;
-  }
-
-  // The norm's fixed-order tree over the 256 invocations (norm.wgsl:75-85).
-  FZ_DEV void tree(int rows, float* total) {
-    cbar();
-    for (int stride = 128; stride >= 32; stride >>= 1) {
-      for (int i = tid; i < rows * stride; i += kCT) {
-        const int r = i / stride, j = i % stride;
-        part[r * kCT + j] = add(part[r * kCT + j], part[r * kCT + j + stride]);
-      }
-      cbar();
+// Moves to the first phase at or after (l, ph) that gives this CTA tiles.
+FZ_DEV void cursor_seek(const DecodeArgs& a, TileCursor& k) {
+  const uint32_t c = blockIdx.x, G = gridDim.x;
+#pragma unroll 1
+  while (!k.end) {
+    k.g = phase_geo(a, k.l, k.ph, c, G);
+    if (k.g.has) {
+      k.rg = k.g.rg0;
+      k.b = k.g.bp0;
+      k.which = 0;
+      return;
     }
-    for (int r = warp; r < rows; r += kCW) {
-      float s = part[r * kCT + lane];
+    if (k.ph == 4) {
+      k.end = true;
+    } else if (k.ph == 3) {
+      k.l++;
+      if (k.l == a.n_layers) {
+        k.l = a.n_layers - 1;
+        k.ph = 4;
+      } else {
+        k.ph = 0;
+      }
+    } else {
+      k.ph++;
+    }
+  }
+}
+
+FZ_DEV void cursor_start(const DecodeArgs& a, TileCursor& k) {
+  k.l = 0;
+  k.ph = 0;
+  k.end = false;
+  cursor_seek(a, k);
+}
+
+FZ_DEV void cursor_advance(const DecodeArgs& a, TileCursor& k) {
+  if (k.end) return;
+  k.b += kSlotBp;
+  if (k.b < k.g.bp1) return;
+  k.b = k.g.bp0;
+  if (k.g.w2 && k.which == 0) {
+    k.which = 1;
+    return;
+  }
+  k.which = 0;
+  k.rg += k.g.rstep;
+  if (k.rg < k.g.rend) return;
+  if (k.ph == 4) {
+    k.end = true;
+    return;
+  }
+  if (k.ph == 3) {
+    k.l++;
+    if (k.l == a.n_layers) {
+      k.l = a.n_layers - 1;
+      k.ph = 4;
+    } else {
+      k.ph = 0;
+    }
+  } else {
+    k.ph++;
+  }
+  cursor_seek(a, k);
+}
+
+// Issues the cursor's tile into `slot` (one thread).
+FZ_DEV void issue_tile(const TileCursor& k, uint32_t slot, uint64_t* full, unsigned char* codes,
+                       unsigned char* scales, uint32_t* tags) {
+  const Q4Matrix& w = k.which ? *k.g.w2 : *k.g.w;
+  const uint32_t nb = min(kSlotBp, k.g.bp1 - k.b);
+  const size_t at = (size_t)k.rg * (w.k / 64) + k.b;
+  tags[slot] = tile_tag(k.l, k.ph, k.rg, k.b, k.which);
+  mb_expect_tx(full + slot, nb * 576u);
+  bulk_g2s(codes + (size_t)slot * kSlotCodes, reinterpret_cast<const unsigned char*>(w.codes) + at * 512, nb * 512u,
+           full + slot);
+  bulk_g2s(scales + (size_t)slot * kSlotScales, reinterpret_cast<const unsigned char*>(w.scales) + at * 64, nb * 64u,
+           full + slot);
+}
+
+// ------------------------------------------------------------ norm, fragments
+
+FZ_DEV float* smem_f(uint32_t off) { return reinterpret_cast<float*>(g_smem + off); }
+
+// The norm's fixed-order tree over the 256 invocations (norm.wgsl:75-85),
+// row r by warp r after one barrier: halving levels 128, 64 and 32 give
+// lane l ((a_l + a_l+128) + (a_l+64 + a_l+192)) + ((a_l+32 + a_l+160) +
+// (a_l+96 + a_l+224)), the last five levels are shuffles.  Leaves each
+// row's reciprocal RMS, 1 / sqrt(total / width + eps), in rms[r].
+FZ_DEV void tree_rms(const DecodeArgs& a, int rows, float* rms, float width) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* part = smem_f(a.lay.part);
+  cbar();
+#pragma unroll 1
+  for (int r = warp; r < rows; r += kCW) {
+    const float* p = part + r * kCT;
+    const float b0 = add(p[lane], p[lane + 128]), b1 = add(p[lane + 64], p[lane + 192]);
+    const float b2 = add(p[lane + 32], p[lane + 160]), b3 = add(p[lane + 96], p[lane + 224]);
+    float s = add(add(b0, b1), add(b2, b3));
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float other = __shfl_down_sync(0xffffffffu, s, o);
-        if (lane < o) s = add(s, other);
-      }
-      if (lane == 0) total[r] = s;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float other = __shfl_down_sync(0xffffffffu, s, o);
+      if (lane < o) s = add(s, other);
     }
-    cbar();
+    if (lane == 0) rms[r] = inverse_sqrt(add(__fdiv_rn(s, width), a.eps));
   }
+  cbar();
+}
 
-  // y of row r at vec4 v: the sum of its K-slice partials, in slice order.
-  FZ_DEV float4 y_at(const float* y, uint32_t ny, int r, int v) {
-    const int Wd = (int)a.hidden;
-    float4 s = ldcg4(y + (size_t)r * Wd + 4 * v);
-    for (uint32_t k = 1; k < ny; k++) s = add4(s, ldcg4(y + ((size_t)k * M + r) * Wd + 4 * v));
-    return s;
-  }
-
-  // The norm launch (norm.wgsl:97-198) over the M rows into rowbuf: X plus
-  // the post-normed block output, written back by CTA 0 with the captures;
-  // then X's RMS norm times `gain`.
-  FZ_DEV void norm(const float* xin, const float* y, uint32_t ny, const float* pg, const float* gain, float* xout,
-                   uint64_t cap_x, uint64_t cap_y) {
-    const int Wd = (int)a.hidden, V = Wd / 4;
-    const float wf = (float)Wd;
-    float* ry = stat;
-    float* rx = stat + kDecodeMaxRows;
-    const bool writer = blockIdx.x == 0;
-    if (y) {
-      for (int r = 0; r < (int)M; r++) {
-        float p = 0.f;
-        for (int v = tid; v < V; v += kCT) p = add(p, dot_self(y_at(y, ny, r, v)));
-        part[r * kCT + tid] = p;
-      }
-      tree((int)M, ry);
-      if (tid < (int)M) ry[tid] = inverse_sqrt(add(__fdiv_rn(ry[tid], wf), a.eps));
-      cbar();
-    }
-    const float4* pg4 = reinterpret_cast<const float4*>(pg);
-    for (int r = 0; r < (int)M; r++) {
-      float* capbase = (writer && a.capture) ? a.capture + (size_t)r * a.capture_stride : nullptr;
-      float4* xc = capbase && cap_x != ~0ull ? reinterpret_cast<float4*>(capbase + cap_x) : nullptr;
-      float4* yc = capbase && cap_y != ~0ull ? reinterpret_cast<float4*>(capbase + cap_y) : nullptr;
-      float4* out4 = writer && xout ? reinterpret_cast<float4*>(xout + (size_t)r * Wd) : nullptr;
-      float4* buf = reinterpret_cast<float4*>(rowbuf + (size_t)r * Wd);
-      float p = 0.f;
-      for (int v = tid; v < V; v += kCT) {
-        float4 x = ldcg4(xin + (size_t)r * Wd + 4 * v);
+// The norm launch (norm.wgsl:97-198) over the M rows into rowbuf: X plus
+// the post-normed block output (y: the sum of ny K-slice partials, in slice
+// order), written back by CTA 0 with the captures; then X's RMS norm times
+// the gain.  Invocation i (thread i) holds vec4s i, i + 256, ...  The gains
+// were copied to shared memory (gain, then post gain) before the wait; the
+// rows are staged in shared memory with every load in flight at once.
+__device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const float* xin, const float* y,
+                                       uint32_t ny, float* xout, uint64_t cap_x, uint64_t cap_y) {
+  const int tid = threadIdx.x;
+  const int Wd = (int)a.hidden, V = Wd / 4, items = (int)M * V;
+  const float wf = (float)Wd;
+  float4* xs = reinterpret_cast<float4*>(smem_f(a.lay.rowbuf));
+  float4* ys = reinterpret_cast<float4*>(smem_f(a.lay.xf));  // scratch until the fragments are built
+  const float4* g4 = reinterpret_cast<const float4*>(smem_f(a.lay.gains));
+  const float4* pg4 = g4 + V;
+  float* part = smem_f(a.lay.part);
+  float* ry = smem_f(a.lay.stat);
+  float* rx = ry + kDecodeMaxRows;
+#pragma unroll 1
+  for (int base = 0; base < items; base += 2 * kCT) {
+    float4 xa[2], ya[2][kDecodeDownSlices];
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      const int i = base + k * kCT + tid;
+      if (i < items) {
+        const int r = i / V, v = i % V;
+        xa[k] = ldcg4(xin + (size_t)r * Wd + 4 * v);
         if (y) {
-          const float4 yy = scale4(y_at(y, ny, r, v), ry[r], pg4[v]);
+#pragma unroll
+          for (uint32_t sl = 0; sl < kDecodeDownSlices; sl++)
+            if (sl < ny) ya[k][sl] = ldcg4(y + ((size_t)sl * M + r) * Wd + 4 * v);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 2; k++) {
+      const int i = base + k * kCT + tid;
+      if (i < items) {
+        xs[i] = xa[k];
+        if (y) {
+          float4 sum = ya[k][0];
+#pragma unroll
+          for (uint32_t sl = 1; sl < kDecodeDownSlices; sl++)
+            if (sl < ny) sum = add4(sum, ya[k][sl]);
+          ys[i] = sum;
+        }
+      }
+    }
+  }
+  cp_async_wait();
+  const bool writer = blockIdx.x == 0;
+  if (y) {
+    cbar();
+#pragma unroll 1
+    for (int r = 0; r < (int)M; r++) {
+      float p = 0.f;
+#pragma unroll
+      for (int k = 0; k < kNormVec; k++) {
+        const int v = tid + k * kCT;
+        if (v < V) p = add(p, dot_self(ys[r * V + v]));
+      }
+      part[r * kCT + tid] = p;
+    }
+    tree_rms(a, (int)M, ry, wf);
+  } else {
+    cbar();
+  }
+#pragma unroll 1
+  for (int r = 0; r < (int)M; r++) {
+    float* capbase = (writer && a.capture) ? a.capture + (size_t)r * a.capture_stride : nullptr;
+    float4* xc = capbase && cap_x != ~0ull ? reinterpret_cast<float4*>(capbase + cap_x) : nullptr;
+    float4* yc = capbase && cap_y != ~0ull ? reinterpret_cast<float4*>(capbase + cap_y) : nullptr;
+    float4* out4 = writer && xout ? reinterpret_cast<float4*>(xout + (size_t)r * Wd) : nullptr;
+    float p = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormVec; k++) {
+      const int v = tid + k * kCT;
+      if (v < V) {
+        float4 x = xs[r * V + v];
+        if (y) {
+          const float4 yy = scale4(ys[r * V + v], ry[r], pg4[v]);
           if (yc) yc[v] = yy;
           x = add4(x, yy);
         }
         if (out4) out4[v] = x;
         if (xc) xc[v] = x;
-        buf[v] = x;
+        xs[r * V + v] = x;
         p = add(p, dot_self(x));
       }
-      part[r * kCT + tid] = p;
     }
-    tree((int)M, rx);
-    if (tid < (int)M) rx[tid] = inverse_sqrt(add(__fdiv_rn(rx[tid], wf), a.eps));
-    cbar();
-    const float4* g4 = reinterpret_cast<const float4*>(gain);
-    for (int r = 0; r < (int)M; r++) {
-      float4* buf = reinterpret_cast<float4*>(rowbuf + (size_t)r * Wd);
-      for (int v = tid; v < V; v += kCT) buf[v] = scale4(buf[v], rx[r], g4[v]);
-    }
-    cbar();
+    part[r * kCT + tid] = p;
   }
+  tree_rms(a, (int)M, rx, wf);
+#pragma unroll 1
+  for (int r = 0; r < (int)M; r++) {
+#pragma unroll
+    for (int k = 0; k < kNormVec; k++) {
+      const int v = tid + k * kCT;
+      if (v < V) xs[r * V + v] = scale4(xs[r * V + v], rx[r], g4[v]);
+    }
+  }
+  cbar();
+}
 
-  // B fragments of the rows (src [M][K]) for blocks [kb0, kb0 + nkb); rows
-  // past M are zero.  `global` rows were written by other CTAs this launch.
-  template <bool kGlobal>
-  FZ_DEV void fragments(const float* src, uint32_t K, uint32_t kb0, uint32_t nkb) {
-    for (int r = 0; r < R; r++) {
-      const int q = r >> 2, gp = r & 3;
-      for (int i = tid; i < (int)nkb * 8; i += kCT) {
-        const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
-        uint2 hi = make_uint2(0, 0), lo = make_uint2(0, 0);
-        if (r < (int)M) {
-          const float* row = src + (size_t)r * K + 32 * (kb0 + kb_rel) + 8 * h + 2 * tq;
-          float2 v01, v23;
-          if (kGlobal) {
-            v01 = __ldcg(reinterpret_cast<const float2*>(row));
-            v23 = __ldcg(reinterpret_cast<const float2*>(row + 16));
-          } else {
-            v01 = *reinterpret_cast<const float2*>(row);
-            v23 = *reinterpret_cast<const float2*>(row + 16);
-          }
-          __half h0, h1, h2, h3, l0, l1, l2, l3;
-          split_hi_lo(v01.x, h0, l0);
-          split_hi_lo(v01.y, h1, l1);
-          split_hi_lo(v23.x, h2, l2);
-          split_hi_lo(v23.y, h3, l3);
-          hi = pack4(h0, h1, h2, h3);
-          lo = pack4(l0, l1, l2, l3);
+// B fragments of the rows (src [M][K]) for blocks [kb0, kb0 + nkb); rows
+// past M are zero.  kGlobal rows were written by other CTAs this launch.
+template <int MQ, bool kGlobal>
+__device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const float* src, uint32_t K, uint32_t kb0,
+                                       uint32_t nkb) {
+  const int tid = threadIdx.x;
+  uint2* xf = reinterpret_cast<uint2*>(g_smem + a.lay.xf);
+#pragma unroll 1
+  for (int r = 0; r < 4 * MQ; r++) {
+    const int q = r >> 2, gp = r & 3;
+#pragma unroll 1
+    for (int i = tid; i < (int)nkb * 8; i += kCT) {
+      const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
+      uint2 hi = make_uint2(0, 0), lo = make_uint2(0, 0);
+      if (r < (int)M) {
+        const float* row = src + (size_t)r * K + 32 * (kb0 + kb_rel) + 8 * h + 2 * tq;
+        float2 v01, v23;
+        if (kGlobal) {
+          v01 = __ldcg(reinterpret_cast<const float2*>(row));
+          v23 = __ldcg(reinterpret_cast<const float2*>(row + 16));
+        } else {
+          v01 = *reinterpret_cast<const float2*>(row);
+          v23 = *reinterpret_cast<const float2*>(row + 16);
         }
-        xf[xf_index(kb_rel, h, q, MQ, tq, 2 * gp)] = hi;
-        xf[xf_index(kb_rel, h, q, MQ, tq, 2 * gp + 1)] = lo;
+        __half h0, h1, h2, h3, l0, l1, l2, l3;
+        split_hi_lo(v01.x, h0, l0);
+        split_hi_lo(v01.y, h1, l1);
+        split_hi_lo(v23.x, h2, l2);
+        split_hi_lo(v23.y, h3, l3);
+        hi = pack4(h0, h1, h2, h3);
+        lo = pack4(l0, l1, l2, l3);
       }
+      xf[xf_index(kb_rel, h, q, MQ, tq, 2 * gp)] = hi;
+      xf[xf_index(kb_rel, h, q, MQ, tq, 2 * gp + 1)] = lo;
     }
   }
+}
 
-  FZ_DEV bool phase_begin(uint32_t kind, uint32_t l, bool has, uint32_t kb0, uint32_t nkb) {
-    if (dead) return false;
-    if (!has) return true;
-    const uint32_t G = gridDim.x, Ln = a.n_layers;
-    const uint32_t* ctr = nullptr;
-    uint32_t target = 0;
-    const DecodeLayer& L = a.layers[l < Ln ? l : Ln - 1];
-    if (kind == kPhQkv && l > 0) {
-      ctr = sync_of(l - 1) + kSyncDown;
-      target = active_ctas(a.layers[l - 1].down.n / 16, kDecodeDownSlices, G);
-    } else if (kind == kPhO) {
-      ctr = sync_of(l) + kSyncAttn;
-      target = M * a.kv_heads;
-    } else if (kind == kPhGate) {
-      ctr = sync_of(l) + kSyncO;
-      target = active_ctas(L.o.n / 16, kDecodeOSlices, G);
-    } else if (kind == kPhDown) {
-      ctr = sync_of(l) + kSyncGate;
-      target = active_ctas(L.gate.n / 16, 1, G);
-    } else if (kind == kPhHead) {
-      ctr = sync_of(Ln - 1) + kSyncDown;
-      target = active_ctas(L.down.n / 16, kDecodeDownSlices, G);
-    }
-    if (tid == 0 && ctr && !wait_counter(ctr, target, a.error)) fail = true;
-    if (sync_dead()) return false;
-    kb_base = kb0;
-    const uint64_t none = ~0ull, per = a.cap_per_layer;
-    if (kind == kPhQkv) {
-      norm(a.hidden_a, l > 0 ? a.y_mlp : nullptr, kDecodeDownSlices, l > 0 ? a.layers[l - 1].post_ffw_norm : nullptr,
-           L.attn_norm, a.hidden_b, l * per + a.cap_residual, l > 0 ? (l - 1) * per + a.cap_mlp_added : none);
-      fragments<false>(rowbuf, a.hidden, kb0, nkb);
-    } else if (kind == kPhGate) {
-      norm(a.hidden_b, a.y_attn, kDecodeOSlices, L.post_attn_norm, L.ffn_norm, a.hidden_a, none,
-           l * per + a.cap_attn_added);
-      fragments<false>(rowbuf, a.hidden, kb0, nkb);
-    } else if (kind == kPhHead) {
-      norm(a.hidden_a, a.y_mlp, kDecodeDownSlices, a.layers[Ln - 1].post_ffw_norm, a.output_norm, nullptr, none,
-           (Ln - 1) * per + a.cap_mlp_added);
-      fragments<false>(rowbuf, a.hidden, kb0, nkb);
-#pragma unroll
-      for (int q = 0; q < MQ; q++) hbest[q] = 0ull;
-    } else if (kind == kPhO) {
-      fragments<true>(a.attn, a.heads * kHd, kb0, nkb);
-    } else {
-      fragments<true>(a.act, a.ffn, kb0, nkb);
-    }
-    cbar();
-    zero_acc();
-    return true;
+// ------------------------------------------------------------ attention
+
+// The step's attention for one layer: the CTAs with work items wait for the
+// layer's QKV counter.  Run in a function of its own (attention_layer), so
+// its registers do not add to the products'.
+template <int GH>
+struct Attn {
+  const DecodeArgs& a;
+  uint32_t M, pos, W;
+  int tid, warp, lane;
+  bool fail, dead;
+
+  FZ_DEV volatile uint32_t* flags() const { return reinterpret_cast<volatile uint32_t*>(g_smem + a.lay.flags); }
+  FZ_DEV uint32_t* sync_of(uint32_t l) { return a.sync + (size_t)l * W; }
+  FZ_DEV void stamp(uint32_t l, uint32_t ph, uint32_t k) {
+    if (a.trace && tid == 0)
+      a.trace[(size_t)blockIdx.x * a.trace_stride + (l * kDecodeTracePhases + ph) * kDecodeTraceStamps + k] = now_ns();
   }
-
-  // One block pair's products into acc (rows g, g + 8 against X rows 4q + t).
-  FZ_DEV void bp_dot(uint4 c, uint2 sc, int kb_rel0, float ac[MQ][2]) {
-    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kbi = 0; kbi < 2; kbi++) {
-      uint32_t a0[4], a1[4];
-      dequant_word(kbi ? c.z : c.x, a0);
-      dequant_word(kbi ? c.w : c.y, a1);
-      const uint32_t sw = kbi ? sc.y : sc.x;
-      const float dg = __half2float(__ushort_as_half((unsigned short)(sw & 0xffffu)));
-      const float dg8 = __half2float(__ushort_as_half((unsigned short)(sw >> 16)));
-#pragma unroll
-      for (int q = 0; q < MQ; q++) {
-        const uint2 b0 = xf[xf_index(kb_rel0 + kbi, 0, q, MQ, t, g)];
-        const uint2 b1 = xf[xf_index(kb_rel0 + kbi, 1, q, MQ, t, g)];
-        float d[4];
-        mma16816(d, a0, b0, zero);
-        mma16816(d, a1, b1, d);
-        ac[q][0] = __fmaf_rn(dg, d[0] + d[1], ac[q][0]);
-        ac[q][1] = __fmaf_rn(dg8, d[2] + d[3], ac[q][1]);
-      }
-    }
-  }
-
-  // A tile shared by the 8 warps: warp w takes block pairs w, w + 8, ...
-  FZ_DEV void tile(const Q4Matrix&, uint32_t, uint32_t b, uint32_t nb, uint32_t which) {
-    if (dead) return;
-    const uint32_t slot = idx % S, use = idx / S;
-    idx++;
-    if (!fail && !mb_wait(full + slot, use & 1u, a.error, flags)) fail = true;
-    if (!fail) {
-      const uint4* cs = codes + (size_t)slot * (kSlotCodes / 16);
-      const uint2* ss = scales + (size_t)slot * (kSlotScales / 8);
-      // (two calls, so that acc stays in registers)
-      if (which)
-        for (uint32_t j = warp; j < nb; j += kCW) bp_dot(cs[j * 32 + lane], ss[j * 8 + g], (int)(2 * (b + j) - kb_base), acc[1]);
-      else
-        for (uint32_t j = warp; j < nb; j += kCW) bp_dot(cs[j * 32 + lane], ss[j * 8 + g], (int)(2 * (b + j) - kb_base), acc[0]);
-    }
-    __syncwarp();
-    if (lane == 0) mb_arrive(empty + slot, 1u);
-  }
-
-  // A head tile: the warp that owns the row group takes all of it.
-  FZ_DEV void head_tile(const Q4Matrix& w, uint32_t rg, uint32_t b, uint32_t nb, uint32_t k, bool first, bool last) {
-    if (dead) return;
-    const uint32_t slot = idx % S, use = idx / S;
-    idx++;
-    if ((int)(k % kCW) != warp) return;
-    if (first) {
-#pragma unroll
-      for (int q = 0; q < MQ; q++) acc[0][q][0] = acc[0][q][1] = 0.f;
-    }
-    if (!fail && !mb_wait(full + slot, use & 1u, a.error, flags)) fail = true;
-    if (!fail) {
-      const uint4* cs = codes + (size_t)slot * (kSlotCodes / 16);
-      const uint2* ss = scales + (size_t)slot * (kSlotScales / 8);
-      for (uint32_t j = 0; j < nb; j++) bp_dot(cs[j * 32 + lane], ss[j * 8 + g], (int)(2 * (b + j)), acc[0]);
-    }
-    __syncwarp();
-    if (lane == 0) mb_arrive(empty + slot, (uint32_t)kCW);
-    if (last && !fail) {
-#pragma unroll
-      for (int q = 0; q < MQ; q++) {
-        const int tok = 4 * q + t;
-        if (tok < (int)M) {
-          const uint32_t n0 = rg * 16 + g, n8 = n0 + 8;
-          a.logits[(size_t)tok * w.n + n0] = acc[0][q][0];
-          a.logits[(size_t)tok * w.n + n8] = acc[0][q][1];
-          const unsigned long long k0 = head_key(acc[0][q][0], n0), k8 = head_key(acc[0][q][1], n8);
-          hbest[q] = max(hbest[q], max(k0, k8));
-        }
-      }
-    }
-  }
-
-  FZ_DEV void task_end(uint32_t kind, uint32_t l, uint32_t rg, uint32_t d) {
-    if (dead) return;
-    constexpr int C = 4 * MQ;
-    float* rw = red + warp * (2 * 16 * C);
-#pragma unroll
-    for (int q = 0; q < MQ; q++) {
-      rw[g * C + 4 * q + t] = acc[0][q][0];
-      rw[(g + 8) * C + 4 * q + t] = acc[0][q][1];
-      if (kind == kPhGate) {
-        rw[16 * C + g * C + 4 * q + t] = acc[1][q][0];
-        rw[16 * C + (g + 8) * C + 4 * q + t] = acc[1][q][1];
-      }
-    }
-    cbar();
-    const uint32_t Hd = a.hidden;
-    for (int i = tid; i < 16 * (int)M; i += kCT) {
-      const int tok = i / 16, row = i % 16;
-      const uint32_t n = rg * 16 + row;
-      float v = 0.f;
-      for (int w = 0; w < kCW; w++) v = add(v, red[w * (2 * 16 * C) + row * C + tok]);
-      if (kind == kPhQkv) {
-        a.qkv[(size_t)tok * ((a.heads + 2 * a.kv_heads) * kHd) + n] = v;
-      } else if (kind == kPhO) {
-        a.y_attn[((size_t)d * M + tok) * Hd + n] = v;
-      } else if (kind == kPhDown) {
-        a.y_mlp[((size_t)d * M + tok) * Hd + n] = v;
-      } else {
-        float up = 0.f;
-        for (int w = 0; w < kCW; w++) up = add(up, red[w * (2 * 16 * C) + 16 * C + row * C + tok]);
-        v = mul(gelu_tanh(v), up);
-        if (a.edit_table) v = apply_edits(a.edit_table + (size_t)tok * a.table_stride, l, n, pos, v);
-        a.act[(size_t)tok * a.ffn + n] = v;
-        if (a.capture) a.capture[(size_t)tok * a.capture_stride + l * a.cap_per_layer + a.cap_neurons + n] = v;
-      }
-    }
-    sync_dead();
-    zero_acc();
-  }
-
-  FZ_DEV void phase_end(uint32_t kind, uint32_t l, bool has) {
-    if (dead || !has) return;
-    if (kind == kPhHead) {
-#pragma unroll
-      for (int q = 0; q < MQ; q++) {
-        unsigned long long b = hbest[q];
-#pragma unroll
-        for (int o = 4; o < 32; o <<= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
-        const int tok = 4 * q + t;
-        if (g == 0 && tok < (int)M && b) atomicMax(best + tok, b);
-      }
-      if (sync_dead()) return;
-      if (tid < (int)M && best[tid]) atomicMax(a.argmax + tid, best[tid]);
-      return;
-    }
-    // The last task's barrier has ordered every consumer's stores.
-    const uint32_t which = kind == kPhQkv ? kSyncQkv : kind == kPhO ? kSyncO : kind == kPhGate ? kSyncGate : kSyncDown;
-    if (tid == 0) raise_counter(sync_of(l) + which);
+  FZ_DEV bool sync_dead() {
+    dead = cbar_or(fail);
+    if (dead && tid == 0) flags()[0] = 1u;
+    return dead;
   }
 
   // ---------------------------------------------------------- attention
 
-  FZ_DEV void attention(uint32_t l) {
-    if (dead) return;
+  static constexpr int KU = 4;   // keys a warp loads at once
+
+  // The split's keys j0 + warp + 8u (u < KU) of one (row, KV head), K and V
+  // together; the new position's (not yet in the cache) is left to the caller.
+  FZ_DEV void load_keys(const DecodeLayer& L, uint32_t row, uint32_t kvh, uint32_t jb, uint32_t j1, uint4 (&kw)[KU],
+                        uint4 (&vw)[KU]) {
+    const uint16_t* kc = L.key_cache + row * L.seq_stride;
+    const uint16_t* vc = L.value_cache + row * L.seq_stride;
+#pragma unroll
+    for (int u = 0; u < KU; u++) {
+      const uint32_t j = jb + kCW * u;
+      kw[u] = vw[u] = make_uint4(0, 0, 0, 0);
+      if (j < j1 && j != pos) {
+        const size_t at = ((size_t)(j % L.slots) * a.kv_heads + kvh) * kHd;
+        kw[u] = __ldcg(reinterpret_cast<const uint4*>(kc + at) + lane);
+        vw[u] = __ldcg(reinterpret_cast<const uint4*>(vc + at) + lane);
+      }
+    }
+  }
+
+  FZ_DEV void run(uint32_t l) {
     const DecodeLayer& L = a.layers[l];
     const uint32_t G = gridDim.x;
     const uint32_t earliest = pos + 1 > L.window ? pos + 1 - L.window : 0;
@@ -659,16 +631,34 @@ struct Consumer {
     const uint32_t KV = a.kv_heads, items = M * KV * nsplit;
     uint32_t item = G - 1 - blockIdx.x;
     if (item >= items) return;
+    // Before waiting for this step's q, k, v: the layer's QK-norm gains and
+    // RoPE turns, and the first batch of the first item's cached keys.
+    float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga, tt = ga;
+    if (warp <= GH) {
+      const float* gain = warp < GH ? L.q_norm : L.k_norm;
+      ga = reinterpret_cast<const float4*>(gain)[lane];
+      gb = reinterpret_cast<const float4*>(gain + kHd / 2)[lane];
+      tt = reinterpret_cast<const float4*>(L.turns)[lane];
+    }
+    uint4 kw[KU], vw[KU];
+    {
+      const uint32_t row = item / (KV * nsplit), kvh = (item / nsplit) % KV, split = item % nsplit;
+      const uint32_t j0 = earliest + split * kKeysPerSplit, j1 = min(j0 + kKeysPerSplit, pos + 1);
+      load_keys(L, row, kvh, j0 + warp, j1, kw, vw);
+    }
+    stamp(l, 1, 0);
     if (tid == 0 && !wait_counter(sync_of(l) + kSyncQkv, active_ctas(L.qkv.n / 16, 1, G), a.error)) fail = true;
     if (sync_dead()) return;
-    const uint32_t group = a.heads / KV;
+    stamp(l, 1, 1);
+    bool have = true;
+    #pragma unroll 1
     for (; item < items; item += G) {
       const uint32_t row = item / (KV * nsplit), kvh = (item / nsplit) % KV, split = item % nsplit;
-      if (group == 4) attend<4>(L, l, row, kvh, split, nsplit, earliest);
-      else if (group == 2) attend<2>(L, l, row, kvh, split, nsplit, earliest);
-      else attend<1>(L, l, row, kvh, split, nsplit, earliest);
+      attend(L, l, row, kvh, split, nsplit, earliest, ga, gb, tt, kw, vw, have);
+      have = false;
       if (dead) return;
     }
+    stamp(l, 1, 4);
   }
 
   // One (row, KV head, key split): QK-norm and RoPE of the group's queries
@@ -677,10 +667,10 @@ struct Consumer {
   // the split's keys: warp w takes keys w, w + 8, ..., K and V loaded
   // together, an online softmax per warp, the warps folded in order; several
   // splits fold in split order in the last CTA (attention.wgsl:403-438).
-  template <int GH>
   FZ_DEV void attend(const DecodeLayer& L, uint32_t l, uint32_t row, uint32_t kvh, uint32_t split, uint32_t nsplit,
-                     uint32_t earliest) {
-    float* qs = reinterpret_cast<float*>(sm + ly.uni);         // [GH][256], times scale * log2(e)
+                     uint32_t earliest, float4 ga, float4 gb, float4 tt, uint4 (&kw)[KU], uint4 (&vw)[KU],
+                     bool have) {
+    float* qs = reinterpret_cast<float*>(g_smem + a.lay.uni);         // [GH][256], times scale * log2(e)
     uint16_t* kvs = reinterpret_cast<uint16_t*>(qs + GH * kHd);  // [2][256] the new key and value
     float* pm = reinterpret_cast<float*>(kvs + 2 * kHd);       // [8][GH]
     float* pl = pm + kCW * GH;                                 // [8][GH]
@@ -690,17 +680,11 @@ struct Consumer {
     const uint32_t j1 = min(j0 + kKeysPerSplit, pos + 1);
     const bool last = j1 == pos + 1;
     if (warp < GH + 2) {
-      RopeArgs r{};
-      r.q_gain = L.q_norm;
-      r.k_gain = L.k_norm;
-      r.turns = L.turns;
-      r.eps = a.eps;
-      r.heads = H;
-      r.kv_heads = KV;
-      r.head_dim = kHd;
       const int head = warp < GH ? (int)(kvh * GH) + warp : (warp == GH ? (int)(H + kvh) : (int)(H + KV + kvh));
-      float4 va, vb;
-      rope_values(r, a.qkv, (H + 2 * KV) * kHd, (int)row, head, pos, lane, va, vb);
+      const float* src = a.qkv + (size_t)row * ((H + 2 * KV) * kHd) + head * kHd;
+      float4 va = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+      float4 vb = __ldcg(reinterpret_cast<const float4*>(src + kHd / 2) + lane);
+      if (warp <= GH) rope_apply(va, vb, ga, gb, tt, a.eps, (int)kHd, pos, lane);
       if (warp < GH) {
         if (last && a.capture) {
           float* cq = a.capture + (size_t)row * a.capture_stride + l * a.cap_per_layer + a.cap_query + head * kHd;
@@ -727,15 +711,10 @@ struct Consumer {
       }
     }
     cbar();
-    // Keys: lane holds dimensions 8 lane .. 8 lane + 7.
-    float q[GH][8];
-#pragma unroll
-    for (int h = 0; h < GH; h++) {
-      const float4 x0 = reinterpret_cast<const float4*>(qs + h * kHd + 8 * lane)[0];
-      const float4 x1 = reinterpret_cast<const float4*>(qs + h * kHd + 8 * lane)[1];
-      q[h][0] = x0.x; q[h][1] = x0.y; q[h][2] = x0.z; q[h][3] = x0.w;
-      q[h][4] = x1.x; q[h][5] = x1.y; q[h][6] = x1.z; q[h][7] = x1.w;
-    }
+    stamp(l, 1, 2);
+    // Keys: lane holds dimensions 8 lane .. 8 lane + 7 (the queries stay in
+    // shared memory, read per key, to leave registers to the loads in flight).
+    const float4* q4 = reinterpret_cast<const float4*>(qs) + 2 * lane;
     float m[GH], ls[GH], o[GH][8];
 #pragma unroll
     for (int h = 0; h < GH; h++) {
@@ -744,26 +723,16 @@ struct Consumer {
 #pragma unroll
       for (int i = 0; i < 8; i++) o[h][i] = 0.f;
     }
-    const uint16_t* kc = L.key_cache + row * L.seq_stride;
-    const uint16_t* vc = L.value_cache + row * L.seq_stride;
-    constexpr int KU = 4;
+    #pragma unroll 1
     for (uint32_t jb = j0 + warp; jb < j1; jb += kCW * KU) {
-      uint4 kw[KU], vw[KU];
+      if (!have) load_keys(L, row, kvh, jb, j1, kw, vw);
+      have = false;
 #pragma unroll
-      for (int u = 0; u < KU; u++) {
-        const uint32_t j = jb + kCW * u;
-        kw[u] = vw[u] = make_uint4(0, 0, 0, 0);
-        if (j < j1) {
-          if (j == pos) {
-            kw[u] = reinterpret_cast<const uint4*>(kvs)[lane];
-            vw[u] = reinterpret_cast<const uint4*>(kvs + kHd)[lane];
-          } else {
-            const size_t at = ((size_t)(j % L.slots) * KV + kvh) * kHd;
-            kw[u] = __ldcg(reinterpret_cast<const uint4*>(kc + at) + lane);
-            vw[u] = __ldcg(reinterpret_cast<const uint4*>(vc + at) + lane);
-          }
+      for (int u = 0; u < KU; u++)
+        if (jb + kCW * u == pos) {
+          kw[u] = reinterpret_cast<const uint4*>(kvs)[lane];
+          vw[u] = reinterpret_cast<const uint4*>(kvs + kHd)[lane];
         }
-      }
       float sc[KU][GH];
 #pragma unroll
       for (int u = 0; u < KU; u++) {
@@ -775,9 +744,11 @@ struct Consumer {
         }
 #pragma unroll
         for (int h = 0; h < GH; h++) {
+          const float4 x0 = q4[h * (kHd / 4)], x1 = q4[h * (kHd / 4) + 1];
+          const float qv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
           float s = 0.f;
 #pragma unroll
-          for (int i = 0; i < 8; i++) s = __fmaf_rn(q[h][i], k[i], s);
+          for (int i = 0; i < 8; i++) s = __fmaf_rn(qv[i], k[i], s);
           s = warp_sum(s);
           sc[u][h] = jb + kCW * u < j1 ? s : -INFINITY;
         }
@@ -843,15 +814,16 @@ struct Consumer {
         }
       }
     }
+    stamp(l, 1, 3);
     bool final_cta = nsplit == 1;
     if (!final_cta) {
       cbar();
       if (tid == 0) {
         __threadfence();
-        flags[1] = atomicAdd(sync_of(l) + kDecodeSyncFixed + row * KV + kvh, 1u) == nsplit - 1 ? 1u : 0u;
+        flags()[1] = atomicAdd(sync_of(l) + kDecodeSyncFixed + row * KV + kvh, 1u) == nsplit - 1 ? 1u : 0u;
       }
       cbar();
-      final_cta = flags[1] != 0;
+      final_cta = flags()[1] != 0;
       if (final_cta) {
         __threadfence();
 #pragma unroll
@@ -859,8 +831,10 @@ struct Consumer {
           const uint32_t head = kvh * GH + h;
           const size_t base = ((size_t)row * H + head) * a.max_splits;
           float mm = -INFINITY;
+          #pragma unroll 1
           for (uint32_t s = 0; s < nsplit; s++) mm = fmaxf(mm, __ldcg(a.partial_ml + (base + s) * 2));
           float lsum = 0.f, acc_o = 0.f;
+          #pragma unroll 1
           for (uint32_t s = 0; s < nsplit; s++) {
             const float ms = __ldcg(a.partial_ml + (base + s) * 2);
             const float f = ms == mm ? 1.0f : exp2f(ms - mm);
@@ -879,21 +853,355 @@ struct Consumer {
   }
 };
 
-// ------------------------------------------------------------ kernel
+// Returns bit 0: this thread gave up waiting; bit 1: the step is abandoned.
+template <int GH>
+__device__ __noinline__ uint32_t attention_layer(const DecodeArgs& a, uint32_t l, uint32_t pos, bool fail) {
+  Attn<GH> s{a};
+  s.M = a.m;
+  s.pos = pos;
+  s.W = kDecodeSyncFixed + a.m * a.kv_heads;
+  s.tid = threadIdx.x;
+  s.warp = threadIdx.x >> 5;
+  s.lane = threadIdx.x & 31;
+  s.fail = fail;
+  s.dead = false;
+  s.run(l);
+  return (s.fail ? 1u : 0u) | (s.dead ? 2u : 0u);
+}
+
+// ------------------------------------------------------------ consumers
 
 template <int MQ>
-__global__ void __launch_bounds__(kDT, 1) decode_kernel(const DecodeArgs a) {
-  extern __shared__ __align__(1024) unsigned char sm[];
-  const uint32_t group = a.heads / a.kv_heads;
-  const DLayout ly = layout_for(MQ, ring_slots<MQ>(), a.hidden, group, nkb_max(a.hidden, a.heads, a.ffn));
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + ly.full);
-  uint64_t* empty = reinterpret_cast<uint64_t*>(sm + ly.empty);
-  volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(sm + ly.flags);
-  unsigned long long* best = reinterpret_cast<unsigned long long*>(sm + ly.best);
+struct Consumer {
+  static constexpr uint32_t S = ring_slots<MQ>();
+  static constexpr int R = 4 * MQ;        // rows of X the fragments carry
+  static constexpr int C = 4 * MQ;        // columns of a warp's partial block
+  static constexpr int kRedBlock = kCW * 2 * 16 * C;  // floats one task's partials take
+  const DecodeArgs& a;
+  uint32_t idx, kb_base, M, pos, W, pending, task_d, ph_kind, ph_l;
+  unsigned long long wait_ns;   // thread 0: time waiting for tiles (trace)
+  // Shared-memory regions (offsets from the launch, so no registers hold them).
+  FZ_DEV const uint4* codes() const { return reinterpret_cast<const uint4*>(g_smem + a.lay.codes); }
+  FZ_DEV const uint2* scales() const { return reinterpret_cast<const uint2*>(g_smem + a.lay.scales); }
+  FZ_DEV uint64_t* full() const { return reinterpret_cast<uint64_t*>(g_smem + a.lay.full); }
+  FZ_DEV uint64_t* empty() const { return reinterpret_cast<uint64_t*>(g_smem + a.lay.empty); }
+  FZ_DEV uint2* xf() const { return reinterpret_cast<uint2*>(g_smem + a.lay.xf); }
+  FZ_DEV float* rowbuf() const { return reinterpret_cast<float*>(g_smem + a.lay.rowbuf); }
+  FZ_DEV float* part() const { return reinterpret_cast<float*>(g_smem + a.lay.part); }
+  FZ_DEV float* stat() const { return reinterpret_cast<float*>(g_smem + a.lay.stat); }
+  FZ_DEV float* red() const { return reinterpret_cast<float*>(g_smem + a.lay.red); }
+  FZ_DEV uint32_t* task_rg() const { return reinterpret_cast<uint32_t*>(g_smem + a.lay.task_rg); }
+  FZ_DEV unsigned long long* best() const { return reinterpret_cast<unsigned long long*>(g_smem + a.lay.best); }
+  FZ_DEV volatile uint32_t* flags() const { return reinterpret_cast<volatile uint32_t*>(g_smem + a.lay.flags); }
+  FZ_DEV uint32_t* tags() const { return reinterpret_cast<uint32_t*>(g_smem + a.lay.tags); }
+  FZ_DEV uint32_t* uses() const { return reinterpret_cast<uint32_t*>(g_smem + a.lay.uses); }
+  int tid, warp, lane, g, t;
+  bool fail, dead;
+  float acc[2][MQ][2];
+
+  FZ_DEV bool aborted() const { return dead; }
+  FZ_DEV void stamp(uint32_t l, uint32_t ph, uint32_t k) {
+    if (a.trace && tid == 0)
+      a.trace[(size_t)blockIdx.x * a.trace_stride + (l * kDecodeTracePhases + ph) * kDecodeTraceStamps + k] = now_ns();
+  }
+  FZ_DEV static uint32_t trace_phase(uint32_t kind) {
+    return kind == kPhQkv ? 0u : kind == kPhO ? 2u : kind == kPhGate ? 3u : kind == kPhDown ? 4u : 5u;
+  }
+  // A barrier that also agrees on whether any consumer thread gave up.
+  FZ_DEV bool sync_dead() {
+    dead = cbar_or(fail);
+    if (dead && tid == 0) flags()[0] = 1u;
+    return dead;
+  }
+  FZ_DEV uint32_t* sync_of(uint32_t l) { return a.sync + (size_t)l * W; }
+  FZ_DEV void zero_acc() {
+#pragma unroll
+    for (int w = 0; w < 2; w++)
+#pragma unroll
+      for (int q = 0; q < MQ; q++) acc[w][q][0] = acc[w][q][1] = 0.f;
+  }
+
+  FZ_DEV bool phase_begin(uint32_t kind, uint32_t l, bool has, uint32_t kb0, uint32_t nkb) {
+    if (dead) return false;
+    if (!has) return true;
+    const uint32_t G = gridDim.x, Ln = a.n_layers;
+    const uint32_t* ctr = nullptr;
+    uint32_t target = 0;
+    const DecodeLayer& L = a.layers[l < Ln ? l : Ln - 1];
+    const float* pg = nullptr;
+    const float* gain = nullptr;
+    if (kind == kPhQkv) {
+      if (l > 0) {
+        ctr = sync_of(l - 1) + kSyncDown;
+        target = active_ctas(a.layers[l - 1].down.n / 16, kDecodeDownSlices, G);
+        pg = a.layers[l - 1].post_ffw_norm;
+      }
+      gain = L.attn_norm;
+    } else if (kind == kPhO) {
+      ctr = sync_of(l) + kSyncAttn;
+      target = M * a.kv_heads;
+    } else if (kind == kPhGate) {
+      ctr = sync_of(l) + kSyncO;
+      target = active_ctas(L.o.n / 16, kDecodeOSlices, G);
+      pg = L.post_attn_norm;
+      gain = L.ffn_norm;
+    } else if (kind == kPhDown) {
+      ctr = sync_of(l) + kSyncGate;
+      target = active_ctas(L.gate.n / 16, 1, G);
+    } else {
+      ctr = sync_of(Ln - 1) + kSyncDown;
+      target = active_ctas(L.down.n / 16, kDecodeDownSlices, G);
+      pg = L.post_ffw_norm;
+      gain = a.output_norm;
+    }
+    // The norm's gains do not depend on the step: copy them before waiting.
+    if (gain) {
+      const int V = (int)a.hidden / 4;
+      float* gs = smem_f(a.lay.gains);
+#pragma unroll 1
+      for (int v = tid; v < V; v += kCT) {
+        cp_async16(gs + 4 * v, gain + 4 * v);
+        if (pg) cp_async16(gs + 4 * (V + v), pg + 4 * v);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    const uint32_t tl = kind == kPhHead ? Ln - 1 : l;
+    stamp(tl, trace_phase(kind), 0);
+    if (tid == 0 && ctr && !wait_counter(ctr, target, a.error)) fail = true;
+    if (sync_dead()) return false;
+    stamp(tl, trace_phase(kind), 1);
+    kb_base = kb0;
+    pending = 0;
+    ph_kind = kind;
+    ph_l = l;
+    const uint64_t none = ~0ull, per = a.cap_per_layer;
+    if (kind == kPhQkv) {
+      norm_rows(a, M, a.hidden_a, l > 0 ? a.y_mlp : nullptr, kDecodeDownSlices, a.hidden_b, l * per + a.cap_residual,
+                l > 0 ? (l - 1) * per + a.cap_mlp_added : none);
+      fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+    } else if (kind == kPhGate) {
+      norm_rows(a, M, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, none, l * per + a.cap_attn_added);
+      fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+    } else if (kind == kPhHead) {
+      norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, none, (Ln - 1) * per + a.cap_mlp_added);
+      fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+    } else if (kind == kPhO) {
+      fragments<MQ, true>(a, M, a.attn, a.heads * kHd, kb0, nkb);
+    } else {
+      fragments<MQ, true>(a, M, a.act, a.ffn, kb0, nkb);
+    }
+    cbar();
+    stamp(tl, trace_phase(kind), 2);
+    zero_acc();
+    return true;
+  }
+
+  // One block pair's products into ac (rows g, g + 8 against X rows 4q + t).
+  FZ_DEV void bp_dot(uint4 c, uint2 sc, int kb_rel0, float ac[MQ][2]) {
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kbi = 0; kbi < 2; kbi++) {
+      uint32_t a0[4], a1[4];
+      dequant_word(kbi ? c.z : c.x, a0);
+      dequant_word(kbi ? c.w : c.y, a1);
+      const uint32_t sw = kbi ? sc.y : sc.x;
+      const float dg = __half2float(__ushort_as_half((unsigned short)(sw & 0xffffu)));
+      const float dg8 = __half2float(__ushort_as_half((unsigned short)(sw >> 16)));
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        const uint2 b0 = xf()[xf_index(kb_rel0 + kbi, 0, q, MQ, t, g)];
+        const uint2 b1 = xf()[xf_index(kb_rel0 + kbi, 1, q, MQ, t, g)];
+        float d[4];
+        mma16816(d, a0, b0, zero);
+        mma16816(d, a1, b1, d);
+        ac[q][0] = __fmaf_rn(dg, d[0] + d[1], ac[q][0]);
+        ac[q][1] = __fmaf_rn(dg8, d[2] + d[3], ac[q][1]);
+      }
+    }
+  }
+
+  // A tile shared by the 8 warps: warp w takes block pairs w, w + 8, ...
+  FZ_DEV void tile(uint32_t rg, uint32_t b, uint32_t nb, uint32_t which) {
+    if (dead) return;
+    const uint32_t slot = idx % S, use = idx / S;
+    const uint64_t t0 = a.trace && tid == 0 ? now_ns() : 0;
+    if (!fail && !mb_wait(full() + slot, use & 1u, a.error, flags())) fail = true;
+    if (a.trace && tid == 0) wait_ns += now_ns() - t0;
+    if (!fail && tags()[slot] != tile_tag(ph_l, ph_kind, rg, b, which)) {
+      fail = true;
+      if (lane == 0) atomicOr(a.error, kErrTile);
+    }
+    if (!fail) {
+      const uint4* cs = codes() + (size_t)slot * (kSlotCodes / 16);
+      const uint2* ss = scales() + (size_t)slot * (kSlotScales / 8);
+      // (two calls, so that acc stays in registers)
+      if (which) {
+#pragma unroll 1
+        for (uint32_t j = warp; j < nb; j += kCW) bp_dot(cs[j * 32 + lane], ss[j * 8 + g], (int)(2 * (b + j) - kb_base), acc[1]);
+      } else {
+#pragma unroll 1
+        for (uint32_t j = warp; j < nb; j += kCW) bp_dot(cs[j * 32 + lane], ss[j * 8 + g], (int)(2 * (b + j) - kb_base), acc[0]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mb_arrive(empty() + slot, 1u);
+    idx++;
+  }
+
+  // A task's per-warp partials wait in their slot; the slots are reduced and
+  // finished together (one barrier pair for up to red_slots(MQ) tasks).
+  FZ_DEV void task_end(uint32_t kind, uint32_t l, uint32_t rg, uint32_t d) {
+    if (dead) return;
+    float* rw = red() + pending * kRedBlock + warp * (2 * 16 * C);
+#pragma unroll
+    for (int q = 0; q < MQ; q++) {
+      rw[g * C + 4 * q + t] = acc[0][q][0];
+      rw[(g + 8) * C + 4 * q + t] = acc[0][q][1];
+      if (kind == kPhGate) {
+        rw[16 * C + g * C + 4 * q + t] = acc[1][q][0];
+        rw[16 * C + (g + 8) * C + 4 * q + t] = acc[1][q][1];
+      }
+    }
+    if (tid == 0) task_rg()[pending] = rg;
+    task_d = d;
+    pending++;
+    zero_acc();
+    if (pending == red_slots(MQ)) flush(kind, l);
+  }
+
+  FZ_DEV void flush(uint32_t kind, uint32_t l) {
+    cbar();
+    stamp(kind == kPhHead ? a.n_layers - 1 : l, trace_phase(kind), 3);
+    const uint32_t Hd = a.hidden;
+    const int per_task = 16 * (int)M, total = (int)pending * per_task;
+#pragma unroll 1
+    for (int base = 0; base < total; base += kCT) {
+      const int i = base + tid;
+      const bool live = i < total;
+      const int slot = i / per_task, rest = i % per_task, tok = rest / 16, row = rest % 16;
+      unsigned long long key = 0ull;
+      if (live) {
+        const float* rs = red() + slot * kRedBlock;
+        const uint32_t n = task_rg()[slot] * 16 + row;
+        float v = 0.f;
+        for (int w = 0; w < kCW; w++) v = add(v, rs[w * (2 * 16 * C) + row * C + tok]);
+        if (kind == kPhQkv) {
+          a.qkv[(size_t)tok * ((a.heads + 2 * a.kv_heads) * kHd) + n] = v;
+        } else if (kind == kPhO) {
+          a.y_attn[((size_t)task_d * M + tok) * Hd + n] = v;
+        } else if (kind == kPhDown) {
+          a.y_mlp[((size_t)task_d * M + tok) * Hd + n] = v;
+        } else if (kind == kPhHead) {
+          a.logits[(size_t)tok * a.head.n + n] = v;
+          key = head_key(v, n);
+        } else {
+          float up = 0.f;
+          for (int w = 0; w < kCW; w++) up = add(up, rs[w * (2 * 16 * C) + 16 * C + row * C + tok]);
+          v = mul(gelu_tanh(v), up);
+          if (a.edit_table) v = apply_edits(a.edit_table + (size_t)tok * a.table_stride, l, n, pos, v);
+          a.act[(size_t)tok * a.ffn + n] = v;
+          if (a.capture) a.capture[(size_t)tok * a.capture_stride + l * a.cap_per_layer + a.cap_neurons + n] = v;
+        }
+      }
+      if (kind == kPhHead) {
+        // Lanes 16h .. 16h + 15 hold one (row group, row) block of a token.
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+        if ((lane & 15) == 0 && key) atomicMax(best() + tok, key);
+      }
+    }
+    pending = 0;
+    sync_dead();
+  }
+
+  FZ_DEV void phase_end(uint32_t kind, uint32_t l, bool has) {
+    if (dead || !has) return;
+    if (pending) flush(kind, l);
+    if (dead) return;
+    if (a.trace && tid == 0) {
+      a.trace[(size_t)blockIdx.x * a.trace_stride + a.n_layers * kDecodeTracePhases * kDecodeTraceStamps +
+              trace_phase(kind)] += wait_ns;
+      wait_ns = 0;
+    }
+    if (kind == kPhHead) {
+      if (tid < (int)M && best()[tid]) atomicMax(a.argmax + tid, best()[tid]);
+      stamp(a.n_layers - 1, 5, 4);
+      return;
+    }
+    // The flush's barrier has ordered every consumer's stores.
+    const uint32_t which = kind == kPhQkv ? kSyncQkv : kind == kPhO ? kSyncO : kind == kPhGate ? kSyncGate : kSyncDown;
+    if (tid == 0) raise_counter(sync_of(l) + which);
+    stamp(l, trace_phase(kind), 4);
+  }
+
+  // The attention of layer l, in its own function (own registers).
+  FZ_DEV void attention(uint32_t l) {
+    if (dead) return;
+    const uint32_t group = a.heads / a.kv_heads;
+    const uint32_t r = group == 4 ? attention_layer<4>(a, l, pos, fail)
+                                  : group == 2 ? attention_layer<2>(a, l, pos, fail) : attention_layer<1>(a, l, pos, fail);
+    fail = (r & 1u) != 0;
+    dead = (r & 2u) != 0;
+  }
+};
+
+// ------------------------------------------------------------ kernel
+
+// The producer (one thread): every tile of the CTA's sequence into its slot
+// as soon as the slot's last use is released.
+template <int MQ>
+FZ_DEV void produce(const DecodeArgs& a) {
+  constexpr uint32_t S = ring_slots<MQ>();
+  uint64_t* full = reinterpret_cast<uint64_t*>(g_smem + a.lay.full);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(g_smem + a.lay.empty);
+  volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(g_smem + a.lay.flags);
+  uint32_t* tags = reinterpret_cast<uint32_t*>(g_smem + a.lay.tags);
+  uint32_t* uses = reinterpret_cast<uint32_t*>(g_smem + a.lay.uses);
+  TileCursor k;
+  cursor_start(a, k);
+  unsigned long long waited = 0, issuing = 0;
+  uint32_t n = 0;
+#pragma unroll 1
+  for (; !k.end; n++) {
+    const uint32_t slot = n % S, use = n / S;
+    const uint64_t t0 = a.trace ? now_ns() : 0;
+    if (use > 0 && !mb_wait(empty + slot, (use - 1) & 1u, a.error, flags)) {
+      if (!flags[0] && !error_word(a.error)) atomicOr(a.error, kErrEmpty);
+      break;
+    }
+    if (flags[0]) break;
+    const uint64_t t1 = a.trace ? now_ns() : 0;
+    issue_tile(k, slot, full, g_smem + a.lay.codes, g_smem + a.lay.scales, tags);
+    uses[slot] = use + 1;
+    cursor_advance(a, k);
+    if (a.trace) {
+      waited += t1 - t0;
+      issuing += now_ns() - t1;
+    }
+  }
+  if (a.trace) {
+    unsigned long long* tail =
+        a.trace + (size_t)blockIdx.x * a.trace_stride + a.n_layers * kDecodeTracePhases * kDecodeTraceStamps;
+    tail[6] = waited;
+    tail[7] = issuing;
+    tail[8] = n;
+  }
+}
+
+template <int MQ>
+__global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ DecodeArgs a) {
+  constexpr uint32_t S = ring_slots<MQ>();
+  const DLayout& ly = a.lay;
+  uint64_t* full = reinterpret_cast<uint64_t*>(g_smem + ly.full);
+  uint64_t* empty = reinterpret_cast<uint64_t*>(g_smem + ly.empty);
+  volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(g_smem + ly.flags);
+  unsigned long long* best = reinterpret_cast<unsigned long long*>(g_smem + ly.best);
+  uint32_t* uses = reinterpret_cast<uint32_t*>(g_smem + ly.uses);
   if (threadIdx.x == 0) {
-    for (uint32_t s = 0; s < ring_slots<MQ>(); s++) {
+    for (uint32_t s = 0; s < S; s++) {
       mb_init(full + s, 1);
       mb_init(empty + s, kCW);
+      uses[s] = 0;
     }
     flags[0] = 0u;
     flags[1] = 0u;
@@ -903,29 +1211,18 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const DecodeArgs a) {
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == kCW) {
-    if (lane == 0) {
-      Producer<MQ> p{a, sm + ly.codes, sm + ly.scales, full, empty, flags, 0u, false};
-      walk(a, p);
-      p.drain();
-    }
+    if (lane == 0) produce<MQ>(a);
   } else {
-    Consumer<MQ> c{a, sm, ly};
-    c.codes = reinterpret_cast<const uint4*>(sm + ly.codes);
-    c.scales = reinterpret_cast<const uint2*>(sm + ly.scales);
-    c.full = full;
-    c.empty = empty;
-    c.xf = reinterpret_cast<uint2*>(sm + ly.xf);
-    c.rowbuf = reinterpret_cast<float*>(sm + ly.rowbuf);
-    c.part = reinterpret_cast<float*>(sm + ly.part);
-    c.stat = reinterpret_cast<float*>(sm + ly.stat);
-    c.red = reinterpret_cast<float*>(sm + ly.red);
-    c.best = best;
-    c.flags = flags;
+    Consumer<MQ> c{a};
     c.idx = 0;
     c.kb_base = 0;
     c.M = a.m;
     c.pos = a.step->position;
     c.W = kDecodeSyncFixed + a.m * a.kv_heads;
+    c.pending = 0;
+    c.task_d = 0;
+    c.ph_kind = 0;
+    c.ph_l = 0;
     c.tid = threadIdx.x;
     c.warp = warp;
     c.lane = lane;
@@ -933,9 +1230,15 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const DecodeArgs a) {
     c.t = lane & 3;
     c.fail = false;
     c.dead = false;
+    c.wait_ns = 0;
     walk(a, c);
   }
+  // Copies in flight (a step abandoned early) land before the CTA exits.
   __syncthreads();
+  if (threadIdx.x == 0) {
+    for (uint32_t s = 0; s < S; s++)
+      if (uses[s] && !mb_wait(full + s, (uses[s] - 1) & 1u, nullptr, nullptr)) atomicOr(a.error, kErrDrain);
+  }
 }
 
 // Per device: the dynamic shared memory each instantiation was configured
@@ -978,6 +1281,8 @@ cudaError_t launch_mq(const DecodeArgs& a, cudaStream_t stream) {
     if (g_configured[MQ - 1][dev] < ly.total) return cudaErrorNotReady;  // prepare_decode first
     sms = g_sms[dev];
   }
+  DecodeArgs args = a;
+  args.lay = ly;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sms);
   cfg.blockDim = dim3(kDT);
@@ -988,7 +1293,7 @@ cudaError_t launch_mq(const DecodeArgs& a, cudaStream_t stream) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, decode_kernel<MQ>, a);
+  return cudaLaunchKernelEx(&cfg, decode_kernel<MQ>, args);
 }
 
 }  // namespace
@@ -998,11 +1303,11 @@ bool decode_supported(uint32_t rows, uint32_t hidden, uint32_t ffn, uint32_t hea
   if (rows == 0 || rows > kDecodeMaxRows || head_dim != kHd || kv_heads == 0 || heads % kv_heads) return false;
   const uint32_t group = heads / kv_heads;
   if (group != 1 && group != 2 && group != 4) return false;
-  if (hidden % 64 || ffn % 64 || hidden > 8192) return false;
+  if (hidden % 64 || ffn % 64 || hidden > (uint32_t)(kNormVec * kCT * 4)) return false;
   const int MQ = rows <= 4 ? 1 : 2;
   const DLayout ly = layout_for(MQ, MQ == 1 ? ring_slots<1>() : ring_slots<2>(), hidden, group,
                                 nkb_max(hidden, heads, ffn));
-  return ly.total <= 227u * 1024u;
+  return ly.total <= 227u * 1024u && layout_aligned(ly);
 }
 
 cudaError_t prepare_decode(uint32_t hidden, uint32_t ffn, uint32_t heads, uint32_t kv_heads) {

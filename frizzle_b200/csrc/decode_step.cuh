@@ -32,6 +32,12 @@ constexpr uint32_t kDecodeDownSlices = 4;   // K slices of the down projection
 constexpr uint32_t kDecodeSyncFixed = 8;    // per-layer phase counters
 constexpr uint32_t kDecodeMaxGroup = 6;     // query heads a KV head may serve
 
+// Byte offsets of the decode kernel's shared-memory regions (set by the launch).
+struct DecodeLayout {
+  uint32_t codes, scales, full, empty, uni, xf, rowbuf, part, stat, red, task_rg, best, flags, gains, tags, uses,
+      total;
+};
+
 struct DecodeArgs {
   const DeviceStep* step;          // position (every row is one sequence's next token)
   const DecodeLayer* layers;       // [n_layers], device memory
@@ -60,7 +66,22 @@ struct DecodeArgs {
   float* logits;                   // [m][vocab], or null for no head
   unsigned long long* argmax;      // [m], cleared before the launch
   uint32_t* error;                 // nonzero when a bounded wait gave up
+  // Optional phase timeline (global timer, ns): CTA c's event e at
+  // trace[c * trace_stride + e], e = (layer * 6 + phase) * 5 + k with phase
+  // 0 QKV, 1 attention, 2 O, 3 gate/up, 4 down, 5 head (in the last layer's
+  // slots) and k 0 began waiting, 1 counter reached, 2 inputs staged (after
+  // the prologue; attention: queries roped), 3 products done (attention:
+  // keys folded), 4 done.  Then kDecodeTraceTail words: per phase the
+  // time thread 0 waited for weight tiles (ns), the producer's time waiting
+  // for free slots and issuing copies (ns), and its tile count.  Null: no trace.
+  unsigned long long* trace;
+  uint32_t trace_stride;
+  DecodeLayout lay;                // filled by launch_decode
 };
+
+constexpr uint32_t kDecodeTracePhases = 6;
+constexpr uint32_t kDecodeTraceStamps = 5;
+constexpr uint32_t kDecodeTraceTail = 9;
 
 inline size_t decode_sync_words(uint32_t layers, uint32_t rows, uint32_t kv_heads) {
   return (size_t)layers * (kDecodeSyncFixed + (size_t)rows * kv_heads);

@@ -177,6 +177,8 @@ struct fz_batch {
   float* y_parts = nullptr;        // [O slices + down slices][rows][hidden]
   uint32_t* dsync = nullptr;
   size_t dsync_words = 0;
+  unsigned long long* trace = nullptr;  // phase timeline, when enabled
+  uint32_t trace_ctas = 0, trace_events = 0;
   uint32_t passes = 2;             // f16 passes over X in the tensor-core products (1 or 2)
   std::vector<void*> row_allocs;
   // Host staging, two slots (at most two steps in flight, kernels/order.h:70).
@@ -197,6 +199,7 @@ struct fz_batch {
 
   ~fz_batch() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+    if (trace) cudaFree(trace);
     for (void* p : allocations) cudaFree(p);
     for (void* p : row_allocs) cudaFree(p);
     for (auto& s : slot) {
@@ -481,6 +484,11 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     d.logits = key.logits ? b.logits : nullptr;
     d.argmax = b.argmax;
     d.error = b.gemm_error;
+    if (b.trace) {
+      FZ_CUDA(cudaMemsetAsync(b.trace, 0, (size_t)b.trace_ctas * b.trace_events * 8, st));
+      d.trace = b.trace;
+      d.trace_stride = b.trace_events;
+    }
     FZ_CUDA(fz::launch_decode(d, st));
     if (key.logits) {
       fz::SelectArgs se{};
@@ -1030,6 +1038,41 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
   }
   FZ_CUDA(cudaDeviceSynchronize());
   *out = b.release();
+  return FZ_OK;
+}
+
+fz_status fz_batch_trace(fz_batch* b, int enable) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  FZ_CUDA(cudaStreamSynchronize(b->model->dev->stream));
+  for (auto& kv : b->graphs) cudaGraphExecDestroy(kv.second);
+  b->graphs.clear();
+  if (b->trace) {
+    cudaFree(b->trace);
+    b->trace = nullptr;
+  }
+  if (!enable) return FZ_OK;
+  int sms = 0;
+  FZ_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, b->model->dev->ordinal));
+  b->trace_ctas = (uint32_t)sms;
+  b->trace_events = b->model->shape.layers * fz::kDecodeTracePhases * fz::kDecodeTraceStamps + fz::kDecodeTraceTail;
+  const size_t bytes = (size_t)b->trace_ctas * b->trace_events * 8;
+  FZ_CUDA(cudaMalloc(&b->trace, bytes));
+  FZ_CUDA(cudaMemset(b->trace, 0, bytes));
+  return FZ_OK;
+}
+
+fz_status fz_batch_read_trace(fz_batch* b, uint64_t* out, size_t count, uint32_t* ctas, uint32_t* events) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  if (!b->trace) return fail(FZ_ERR_STATE, "tracing is off (fz_batch_trace)");
+  if (ctas) *ctas = b->trace_ctas;
+  if (events) *events = b->trace_events;
+  if (!out) return FZ_OK;
+  const size_t n = (size_t)b->trace_ctas * b->trace_events;
+  if (count < n) return fail(FZ_ERR_ARGUMENT, "the output holds fewer than ctas x events values");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  FZ_CUDA(cudaStreamSynchronize(b->model->dev->stream));
+  FZ_CUDA(cudaMemcpy(out, b->trace, n * 8, cudaMemcpyDeviceToHost));
   return FZ_OK;
 }
 

@@ -87,9 +87,40 @@ FZ_DEV void build_fragments(uint2* xf, int MQ, int row, const float* src, int kb
   }
 }
 
-// QK-norm, RoPE and the f16 KV append for one (row, head) by one warp
-// (rope.wgsl:40-138, rope_cache.wgsl:16-91, d = 256: lane l holds the head's
-// elements 4l..4l+3 and 128+4l..128+4l+3).
+// QK-norm and RoPE of one head held by a warp (rope.wgsl:40-138, d = 256:
+// lane l holds elements 4l..4l+3 in a and 128+4l..128+4l+3 in b), given the
+// lane's gains ga, gb and its four theta/2pi turns.
+FZ_DEV void rope_apply(float4& a, float4& b, float4 ga, float4 gb, float4 turns, float eps, int d, uint32_t pos,
+                       int lane) {
+  float s = add(dot_self(a), dot_self(b));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float other = __shfl_down_sync(0xffffffffu, s, o);
+    if (lane < o) s = add(s, other);
+  }
+  s = __shfl_sync(0xffffffffu, s, 0);
+  const float rr = inverse_sqrt(add(__fdiv_rn(s, (float)d), eps));
+  a = make_float4(mul(mul(a.x, rr), ga.x), mul(mul(a.y, rr), ga.y), mul(mul(a.z, rr), ga.z), mul(mul(a.w, rr), ga.w));
+  b = make_float4(mul(mul(b.x, rr), gb.x), mul(mul(b.y, rr), gb.y), mul(mul(b.z, rr), gb.z), mul(mul(b.w, rr), gb.w));
+  // The angle is 2 pi times the turns' fraction (rope.wgsl:120-127 reduces the
+  // same way); sincospi of twice the fraction has no large-argument path.
+  const float tv[4] = {turns.x, turns.y, turns.z, turns.w};
+  float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const float tt = mul((float)pos, tv[c]);
+    float sn, cs;
+    sincospif(mul(2.0f, sub(tt, rintf(tt))), &sn, &cs);
+    const float x = av[c], y = bv[c];
+    av[c] = sub(mul(x, cs), mul(y, sn));
+    bv[c] = add(mul(x, sn), mul(y, cs));
+  }
+  a = make_float4(av[0], av[1], av[2], av[3]);
+  b = make_float4(bv[0], bv[1], bv[2], bv[3]);
+}
+
+// The raw q, k or v of one (row, head), with QK-norm and RoPE applied to q
+// and k (rope_cache.wgsl:16-91 reads the same columns).
 FZ_DEV void rope_values(const RopeArgs& r, const float* raw, uint32_t raw_stride, int row, int head, uint32_t pos,
                        int lane, float4& a, float4& b) {
   const int d = (int)r.head_dim, H = (int)r.heads, KV = (int)r.kv_heads;
@@ -100,35 +131,9 @@ FZ_DEV void rope_values(const RopeArgs& r, const float* raw, uint32_t raw_stride
   a = __ldcg(reinterpret_cast<const float4*>(src) + lane);
   b = __ldcg(reinterpret_cast<const float4*>(src + d / 2) + lane);
   if (!is_value) {
-    float s = add(dot_self(a), dot_self(b));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      float other = __shfl_down_sync(0xffffffffu, s, o);
-      if (lane < o) s = add(s, other);
-    }
-    s = __shfl_sync(0xffffffffu, s, 0);
-    const float rr = inverse_sqrt(add(__fdiv_rn(s, (float)d), r.eps));
     const float* gain = is_query ? r.q_gain : r.k_gain;
-    const float4 ga = reinterpret_cast<const float4*>(gain)[lane];
-    const float4 gb = reinterpret_cast<const float4*>(gain + d / 2)[lane];
-    a = make_float4(mul(mul(a.x, rr), ga.x), mul(mul(a.y, rr), ga.y), mul(mul(a.z, rr), ga.z),
-                    mul(mul(a.w, rr), ga.w));
-    b = make_float4(mul(mul(b.x, rr), gb.x), mul(mul(b.y, rr), gb.y), mul(mul(b.z, rr), gb.z),
-                    mul(mul(b.w, rr), gb.w));
-    const float tau = (float)6.283185307179586;
-    float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-      const float tt = mul((float)pos, r.turns[4 * lane + c]);
-      const float angle = mul(tau, sub(tt, rintf(tt)));
-      float sn, cs;
-      sincosf(angle, &sn, &cs);
-      const float x = av[c], y = bv[c];
-      av[c] = sub(mul(x, cs), mul(y, sn));
-      bv[c] = add(mul(x, sn), mul(y, cs));
-    }
-    a = make_float4(av[0], av[1], av[2], av[3]);
-    b = make_float4(bv[0], bv[1], bv[2], bv[3]);
+    rope_apply(a, b, reinterpret_cast<const float4*>(gain)[lane], reinterpret_cast<const float4*>(gain + d / 2)[lane],
+               reinterpret_cast<const float4*>(r.turns)[lane], r.eps, d, pos, lane);
   }
 }
 

@@ -153,6 +153,21 @@ fz_status fz_batch_read_capture(fz_batch *batch, uint32_t sequence, float *out, 
 /* Device pointer of sequence s's key or value cache for `layer` ([slots][kv_heads][d] f16). */
 fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int values, void **ptr,
                          uint32_t *slots);
+/* Phase timeline of one-token steps (the GPU timestamps of Frizzle's profiled
+ * step, one after each launch, src/core/kernels/program.h:142-168; here the
+ * step is one launch, so the stamps are taken inside it): when enabled, each decode
+ * step records, per CTA of the persistent decode kernel, the GPU global timer
+ * (ns) when each phase began waiting, saw its inputs complete, had them
+ * staged, had its products and finished. fz_batch_read_trace copies the last
+ * step's record: `ctas` x `events` values, event e = (layer * 6 + phase) * 5
+ * + k (phase 0 QKV, 1 attention, 2 output projection, 3 gate/up, 4 down,
+ * 5 head in the last layer's slots; k 0 began waiting, 1 inputs complete,
+ * 2 inputs staged, 3 products done, 4 done), 0 where a CTA had no work;
+ * then 9 totals: per phase the ns spent waiting for weight tiles, the ns the
+ * copy issuer waited for free slots, the ns it spent issuing, its tile count.
+ * With out = NULL it only reports the shape. */
+fz_status fz_batch_trace(fz_batch *batch, int enable);
+fz_status fz_batch_read_trace(fz_batch *batch, uint64_t *out, size_t count, uint32_t *ctas, uint32_t *events);
 
 /* ------------------------------------------------------------------ kernel level
  * Device pointers throughout; `stream` is a cudaStream_t or NULL (the legacy
