@@ -32,7 +32,7 @@ sys.path.insert(0, ROOT)
 METRIC = "Gemma-3-1B q4_0 decode tok/s, prefill tok/s; q4 matvec HBM GB/s vs peak"
 PROMPT = 32
 HEAD_N, HEAD_K = 262144, 1152
-LAUNCHES_PER_DECODE_STEP = 1 + 26 * 5 + 1 + 2   # embed, 26 x (qkv, attention, o, gate/up, down), head, select x2
+LAUNCHES_PER_DECODE_STEP = 5   # embed, the persistent decode step (26 layers), head, select x2
 DECODE_BYTES = 562_360_320 + 537_088           # Q4_0 weights + F32 gains a decode token reads
 
 
@@ -495,6 +495,8 @@ def run_trace(args):
             for ph in range(6):
                 if ph == 5 and l != L - 1:
                     continue
+                if np.all(np.isnan(t[:, l, ph, 4])):
+                    continue
                 seen = np.nanmax(t[:, l, ph, 1])
                 ready = np.nanmax(t[:, l, ph, 2])
                 done = np.nanmax(t[:, l, ph, 4])
@@ -519,6 +521,8 @@ def run_trace(args):
                      "tiles": float(np.mean(tl[:, 8]))}
     for ph, name in enumerate(PHASES):
         rows = range(L - 1, L) if ph == 5 else range(L)
+        if not spread[ph]["work_max"]:
+            continue
         out["phases"][name] = {"handoff_us": float(np.mean([hand[0][l, ph] for l in rows]) / n),
                                "work_us": float(np.mean([hand[1][l, ph] for l in rows]) / n)}
         out["phases"][name].update({k: float(np.mean(v)) for k, v in spread[ph].items()})

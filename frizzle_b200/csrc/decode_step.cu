@@ -51,8 +51,10 @@ constexpr uint32_t kKeysPerSplit = 512;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint32_t kWaitIters = 1u << 30;
 constexpr int kNormVec = 3;             // vec4s of a row an invocation holds (hidden <= 3072)
-// Tasks whose partials are reduced together.
-__host__ __device__ constexpr uint32_t red_slots(int MQ) { return MQ == 1 ? 4u : 2u; }
+// Task partials reduced together: half-slots of [warps][16 rows][4 MQ
+// columns]; a gate/up task takes two.
+__host__ __device__ constexpr uint32_t red_half_slots(int MQ) { return MQ == 1 ? 8u : 4u; }
+constexpr uint32_t kAttnChunk = 32;     // keys an attention chunk
 
 enum : uint32_t { kPhQkv = 0, kPhO = 1, kPhGate = 2, kPhDown = 3, kPhHead = 4 };
 enum : uint32_t { kSyncQkv = 0, kSyncAttn = 1, kSyncO = 2, kSyncGate = 3, kSyncDown = 4 };
@@ -93,30 +95,35 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   L.empty = o;
   o += slots * 8;
   o = (o + 127u) & ~127u;
+  // One region, two uses: the products' fragments, norm rows and partials,
+  // or the attention's queries and key/value chunks.
   L.uni = o;
-  const uint32_t xf = nkb * 512u * (uint32_t)MQ;
-  const uint32_t rows = 4u * (uint32_t)MQ * hidden * 4u;
-  const uint32_t att = (group * kHd + 2u * kCW * group + kCW * group * kHd) * 4u + 2u * kHd * 2u;
-  L.xf = o;
-  L.rowbuf = o + xf;
-  o += (xf + rows > att ? xf + rows : att);
+  uint32_t m = o;
+  L.xf = m;
+  m += nkb * 512u * (uint32_t)MQ;
+  L.rowbuf = m;
+  m += 4u * (uint32_t)MQ * hidden * 4u;
+  m = (m + 15u) & ~15u;
+  L.part = m;
+  m += 4u * MQ * kCT * 4u;
+  L.red = m;
+  m += red_half_slots(MQ) * kCW * 16u * 4u * MQ * 4u;
+  m = (m + 15u) & ~15u;
+  L.gains = m;
+  m += 2u * hidden * 4u;
+  const uint32_t att = 8u * (kHd + 8u) * 2u + 2u * 2u * kAttnChunk * kHd * 2u + group * kAttnChunk * 4u +
+                       8u * (kAttnChunk + 8u) * 2u + 2u * group * 4u;
+  o = m > o + att ? m : o + att;
   o = (o + 15u) & ~15u;
-  L.part = o;
-  o += 4u * MQ * kCT * 4u;
   L.stat = o;
   o += 2u * kDecodeMaxRows * 4u;
-  L.red = o;
-  o += red_slots(MQ) * kCW * 2u * 16u * 4u * MQ * 4u;
   L.task_rg = o;
-  o += red_slots(MQ) * 4u;
+  o += red_half_slots(MQ) * 4u;
   o = (o + 7u) & ~7u;
   L.best = o;
   o += kDecodeMaxRows * 8u;
   L.flags = o;
   o += 16u;
-  o = (o + 15u) & ~15u;
-  L.gains = o;
-  o += 2u * hidden * 4u;
   L.tags = o;
   o += slots * 4u;
   L.uses = o;
@@ -156,6 +163,18 @@ FZ_DEV bool mb_try(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// As mb_try, but a thread whose phase is not complete sleeps (up to about
+// 1 us) until it completes, instead of spinning on issue slots the
+// product warps on its scheduler need.
+FZ_DEV bool mb_try_sleep(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity), "r"(1000u)
+      : "memory");
+  return ok != 0;
+}
 FZ_DEV uint64_t now_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -169,8 +188,8 @@ FZ_DEV bool mb_wait(uint64_t* b, uint32_t parity, const uint32_t* err, const vol
   if (mb_try(b, parity)) return true;
   const uint64_t t0 = now_ns();
   for (uint32_t i = 1; i < kWaitIters; i++) {
-    if (mb_try(b, parity)) return true;
-    if ((i & 63u) == 0) {
+    if (mb_try_sleep(b, parity)) return true;
+    if ((i & 3u) == 0) {
       if ((abort && *abort) || (err && error_word(err))) return false;
       if (now_ns() - t0 > kWaitNs) return false;
     }
@@ -211,6 +230,7 @@ FZ_DEV bool wait_counter(const uint32_t* ctr, uint32_t target, uint32_t* err) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
     if (v >= target) return true;
+    __nanosleep(32);
     if ((i & 15u) == 15u) {
       if (error_word(err)) return false;
       if (now_ns() - t0 > kWaitNs) {
@@ -545,34 +565,45 @@ template <int MQ, bool kGlobal>
 __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const float* src, uint32_t K, uint32_t kb0,
                                        uint32_t nkb) {
   const int tid = threadIdx.x;
-  uint2* xf = reinterpret_cast<uint2*>(g_smem + a.lay.xf);
+  uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
+  // Thread i: block kb_rel, half h, lane quad tq; for each quad of rows q it
+  // writes the eight columns (rows 4q..4q+3, hi and lo) of slot tq * 8 as one
+  // contiguous 64 bytes.
 #pragma unroll 1
-  for (int r = 0; r < 4 * MQ; r++) {
-    const int q = r >> 2, gp = r & 3;
-#pragma unroll 1
-    for (int i = tid; i < (int)nkb * 8; i += kCT) {
-      const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
-      uint2 hi = make_uint2(0, 0), lo = make_uint2(0, 0);
-      if (r < (int)M) {
-        const float* row = src + (size_t)r * K + 32 * (kb0 + kb_rel) + 8 * h + 2 * tq;
-        float2 v01, v23;
-        if (kGlobal) {
-          v01 = __ldcg(reinterpret_cast<const float2*>(row));
-          v23 = __ldcg(reinterpret_cast<const float2*>(row + 16));
-        } else {
-          v01 = *reinterpret_cast<const float2*>(row);
-          v23 = *reinterpret_cast<const float2*>(row + 16);
+  for (int i = tid; i < (int)nkb * 8; i += kCT) {
+    const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
+#pragma unroll
+    for (int q = 0; q < MQ; q++) {
+      uint2 col[8];
+#pragma unroll
+      for (int gp = 0; gp < 4; gp++) {
+        const int r = 4 * q + gp;
+        uint2 hi = make_uint2(0, 0), lo = make_uint2(0, 0);
+        if (r < (int)M) {
+          const float* row = src + (size_t)r * K + 32 * (kb0 + kb_rel) + 8 * h + 2 * tq;
+          float2 v01, v23;
+          if (kGlobal) {
+            v01 = __ldcg(reinterpret_cast<const float2*>(row));
+            v23 = __ldcg(reinterpret_cast<const float2*>(row + 16));
+          } else {
+            v01 = *reinterpret_cast<const float2*>(row);
+            v23 = *reinterpret_cast<const float2*>(row + 16);
+          }
+          __half h0, h1, h2, h3, l0, l1, l2, l3;
+          split_hi_lo(v01.x, h0, l0);
+          split_hi_lo(v01.y, h1, l1);
+          split_hi_lo(v23.x, h2, l2);
+          split_hi_lo(v23.y, h3, l3);
+          hi = pack4(h0, h1, h2, h3);
+          lo = pack4(l0, l1, l2, l3);
         }
-        __half h0, h1, h2, h3, l0, l1, l2, l3;
-        split_hi_lo(v01.x, h0, l0);
-        split_hi_lo(v01.y, h1, l1);
-        split_hi_lo(v23.x, h2, l2);
-        split_hi_lo(v23.y, h3, l3);
-        hi = pack4(h0, h1, h2, h3);
-        lo = pack4(l0, l1, l2, l3);
+        col[2 * gp] = hi;
+        col[2 * gp + 1] = lo;
       }
-      xf[xf_index(kb_rel, h, q, MQ, tq, 2 * gp)] = hi;
-      xf[xf_index(kb_rel, h, q, MQ, tq, 2 * gp + 1)] = lo;
+      // xf_index(kb_rel, h, q, MQ, tq, g) = ((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8 + g
+      uint4* dst = xf + (((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8) / 2;
+#pragma unroll
+      for (int k = 0; k < 4; k++) dst[k] = make_uint4(col[2 * k].x, col[2 * k].y, col[2 * k + 1].x, col[2 * k + 1].y);
     }
   }
 }
@@ -602,25 +633,53 @@ struct Attn {
   }
 
   // ---------------------------------------------------------- attention
+  //
+  // Keys are taken C at a time: their K and V rows are copied into shared
+  // memory (cp.async, 16 bytes a copy; the 16-byte pieces of a row
+  // XOR-swizzled by the row, so that eight rows read together hit all
+  // banks).  Both contractions run on the tensor cores (mma.m16n8k16, f16 in,
+  // f32 accumulate): scores = Q K^T with the queries split into f16 parts
+  // and remainders (rows 0..GH-1 and GH..2GH-1 of A), so each product is
+  // exact; warp h keeps head h's online softmax; out = P V with the weights
+  // split the same way, V's fragments loaded by ldmatrix.trans.
 
-  static constexpr int KU = 4;   // keys a warp loads at once
+  static constexpr int C = kAttnChunk;    // keys a chunk (two chunk buffers)
 
-  // The split's keys j0 + warp + 8u (u < KU) of one (row, KV head), K and V
-  // together; the new position's (not yet in the cache) is left to the caller.
-  FZ_DEV void load_keys(const DecodeLayer& L, uint32_t row, uint32_t kvh, uint32_t jb, uint32_t j1, uint4 (&kw)[KU],
-                        uint4 (&vw)[KU]) {
+  static constexpr int QS = kHd + 8;      // row stride (halves) of the split queries
+  static constexpr int PS = C + 8;        // row stride (halves) of the split weights
+  // Split rows: r < GH the f16 part of head r's query (or weights), GH <= r <
+  // 2 GH the f16 remainder of head r - GH's, the rest zero (the mma's A rows).
+  FZ_DEV uint16_t* qh() const { return reinterpret_cast<uint16_t*>(g_smem + a.lay.uni); }  // [8][QS]
+  FZ_DEV uint16_t* ks() const { return qh() + 8 * QS; }                                      // [2C][256] swizzled
+  FZ_DEV uint16_t* vs() const { return ks() + 2 * C * kHd; }                                 // [2C][256] swizzled
+  FZ_DEV float* sc() const { return reinterpret_cast<float*>(vs() + 2 * C * kHd); }         // [GH][C] scores
+  FZ_DEV uint16_t* ph() const { return reinterpret_cast<uint16_t*>(sc() + GH * C); }        // [8][PS] weights
+  FZ_DEV float* hstat() const { return reinterpret_cast<float*>(ph() + 8 * PS); }           // [GH] corr or m, [GH] l
+
+  // Copies keys [jc, jc + n) of (row, kvh) into chunk buffer `buf` (one
+  // cp.async group).
+  FZ_DEV void stage(const DecodeLayer& L, uint32_t row, uint32_t kvh, uint32_t jc, uint32_t n, uint32_t buf) {
     const uint16_t* kc = L.key_cache + row * L.seq_stride;
     const uint16_t* vc = L.value_cache + row * L.seq_stride;
-#pragma unroll
-    for (int u = 0; u < KU; u++) {
-      const uint32_t j = jb + kCW * u;
-      kw[u] = vw[u] = make_uint4(0, 0, 0, 0);
-      if (j < j1 && j != pos) {
-        const size_t at = ((size_t)(j % L.slots) * a.kv_heads + kvh) * kHd;
-        kw[u] = __ldcg(reinterpret_cast<const uint4*>(kc + at) + lane);
-        vw[u] = __ldcg(reinterpret_cast<const uint4*>(vc + at) + lane);
-      }
+    const uint32_t KV = a.kv_heads, r0 = buf * C;
+#pragma unroll 1
+    for (uint32_t i = tid; i < n * 64; i += kCT) {
+      const bool isv = i >= n * 32;
+      const uint32_t ii = isv ? i - n * 32 : i, r = ii / 32, c = ii % 32;
+      const size_t at = ((size_t)((jc + r) % L.slots) * KV + kvh) * kHd + c * 8;
+      cp_async16((isv ? vs() : ks()) + (r0 + r) * kHd + ((c ^ (r & 7u)) * 8), (isv ? vc : kc) + at);
     }
+    // A short chunk's missing value rows are zero (their weights are zero, and
+    // 0 x NaN would not be).
+#pragma unroll 1
+    for (uint32_t i = tid; i < (C - n) * 32; i += kCT)
+      *reinterpret_cast<uint4*>(vs() + (r0 + n + i / 32) * kHd + (i % 32) * 8) = make_uint4(0, 0, 0, 0);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  // The split's first two chunks.
+  FZ_DEV void stage_first(const DecodeLayer& L, uint32_t row, uint32_t kvh, uint32_t j0, uint32_t j1) {
+    stage(L, row, kvh, j0, min((uint32_t)C, j1 - j0), 0);
+    if (j0 + C < j1) stage(L, row, kvh, j0 + C, min((uint32_t)C, j1 - j0 - C), 1);
   }
 
   FZ_DEV void run(uint32_t l) {
@@ -631,8 +690,8 @@ struct Attn {
     const uint32_t KV = a.kv_heads, items = M * KV * nsplit;
     uint32_t item = G - 1 - blockIdx.x;
     if (item >= items) return;
-    // Before waiting for this step's q, k, v: the layer's QK-norm gains and
-    // RoPE turns, and the first batch of the first item's cached keys.
+    // Before waiting for this step's q, k, v: the first chunk of the first
+    // item's cached keys and the layer's QK-norm gains and RoPE turns.
     float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga, tt = ga;
     if (warp <= GH) {
       const float* gain = warp < GH ? L.q_norm : L.k_norm;
@@ -640,22 +699,24 @@ struct Attn {
       gb = reinterpret_cast<const float4*>(gain + kHd / 2)[lane];
       tt = reinterpret_cast<const float4*>(L.turns)[lane];
     }
-    uint4 kw[KU], vw[KU];
     {
       const uint32_t row = item / (KV * nsplit), kvh = (item / nsplit) % KV, split = item % nsplit;
       const uint32_t j0 = earliest + split * kKeysPerSplit, j1 = min(j0 + kKeysPerSplit, pos + 1);
-      load_keys(L, row, kvh, j0 + warp, j1, kw, vw);
+      stage_first(L, row, kvh, j0, j1);
     }
     stamp(l, 1, 0);
     if (tid == 0 && !wait_counter(sync_of(l) + kSyncQkv, active_ctas(L.qkv.n / 16, 1, G), a.error)) fail = true;
-    if (sync_dead()) return;
+    if (sync_dead()) {
+      cp_async_wait();
+      return;
+    }
     stamp(l, 1, 1);
-    bool have = true;
-    #pragma unroll 1
+    bool staged = true;
+#pragma unroll 1
     for (; item < items; item += G) {
       const uint32_t row = item / (KV * nsplit), kvh = (item / nsplit) % KV, split = item % nsplit;
-      attend(L, l, row, kvh, split, nsplit, earliest, ga, gb, tt, kw, vw, have);
-      have = false;
+      attend(L, l, row, kvh, split, nsplit, earliest, ga, gb, tt, staged);
+      staged = false;
       if (dead) return;
     }
     stamp(l, 1, 4);
@@ -663,27 +724,24 @@ struct Attn {
 
   // One (row, KV head, key split): QK-norm and RoPE of the group's queries
   // and of the new key (rope.wgsl:40-138), the KV append by the split that
-  // holds the new position (rope_cache.wgsl:16-91), then flash decode over
-  // the split's keys: warp w takes keys w, w + 8, ..., K and V loaded
-  // together, an online softmax per warp, the warps folded in order; several
-  // splits fold in split order in the last CTA (attention.wgsl:403-438).
+  // holds the new position (rope_cache.wgsl:16-91), then the split's keys a
+  // chunk at a time with an online softmax per head; several splits fold in
+  // split order in the last CTA (attention.wgsl:403-438).  `staged`: the
+  // first chunk's copies were issued before the wait.
   FZ_DEV void attend(const DecodeLayer& L, uint32_t l, uint32_t row, uint32_t kvh, uint32_t split, uint32_t nsplit,
-                     uint32_t earliest, float4 ga, float4 gb, float4 tt, uint4 (&kw)[KU], uint4 (&vw)[KU],
-                     bool have) {
-    float* qs = reinterpret_cast<float*>(g_smem + a.lay.uni);         // [GH][256], times scale * log2(e)
-    uint16_t* kvs = reinterpret_cast<uint16_t*>(qs + GH * kHd);  // [2][256] the new key and value
-    float* pm = reinterpret_cast<float*>(kvs + 2 * kHd);       // [8][GH]
-    float* pl = pm + kCW * GH;                                 // [8][GH]
-    float* po = pl + kCW * GH;                                 // [8][GH][256]
+                     uint32_t earliest, float4 ga, float4 gb, float4 tt, bool staged) {
     const uint32_t H = a.heads, KV = a.kv_heads;
     const uint32_t j0 = earliest + split * kKeysPerSplit;
     const uint32_t j1 = min(j0 + kKeysPerSplit, pos + 1);
     const bool last = j1 == pos + 1;
+    if (!staged) stage_first(L, row, kvh, j0, j1);
+    // QK-norm and RoPE: warps 0..GH-1 the queries, warp GH the key, GH+1 the value.
+    float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
     if (warp < GH + 2) {
       const int head = warp < GH ? (int)(kvh * GH) + warp : (warp == GH ? (int)(H + kvh) : (int)(H + KV + kvh));
       const float* src = a.qkv + (size_t)row * ((H + 2 * KV) * kHd) + head * kHd;
-      float4 va = __ldcg(reinterpret_cast<const float4*>(src) + lane);
-      float4 vb = __ldcg(reinterpret_cast<const float4*>(src + kHd / 2) + lane);
+      va = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+      vb = __ldcg(reinterpret_cast<const float4*>(src + kHd / 2) + lane);
       if (warp <= GH) rope_apply(va, vb, ga, gb, tt, a.eps, (int)kHd, pos, lane);
       if (warp < GH) {
         if (last && a.capture) {
@@ -691,130 +749,162 @@ struct Attn {
           reinterpret_cast<float4*>(cq)[lane] = va;
           reinterpret_cast<float4*>(cq + kHd / 2)[lane] = vb;
         }
-        float* q = qs + warp * kHd;
         const float s = a.scale_log2e;
-        reinterpret_cast<float4*>(q)[lane] = make_float4(mul(va.x, s), mul(va.y, s), mul(va.z, s), mul(va.w, s));
-        reinterpret_cast<float4*>(q + kHd / 2)[lane] =
-            make_float4(mul(vb.x, s), mul(vb.y, s), mul(vb.z, s), mul(vb.w, s));
-      } else {
+        const float qv[8] = {mul(va.x, s), mul(va.y, s), mul(va.z, s), mul(va.w, s),
+                             mul(vb.x, s), mul(vb.y, s), mul(vb.z, s), mul(vb.w, s)};
+        __half hi[8], lo[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) split_hi_lo(qv[i], hi[i], lo[i]);
+        uint16_t* qa = qh() + warp * QS;
+        uint16_t* qb = qh() + (GH + warp) * QS;
+        *reinterpret_cast<uint2*>(qa + 4 * lane) = pack4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint2*>(qa + kHd / 2 + 4 * lane) = pack4(hi[4], hi[5], hi[6], hi[7]);
+        *reinterpret_cast<uint2*>(qb + 4 * lane) = pack4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint2*>(qb + kHd / 2 + 4 * lane) = pack4(lo[4], lo[5], lo[6], lo[7]);
+      } else if (last) {
+        uint16_t* cache = (warp == GH ? L.key_cache : L.value_cache) + row * L.seq_stride +
+                          ((size_t)(pos % L.slots) * KV + kvh) * kHd;
+        reinterpret_cast<ushort4*>(cache)[lane] =
+            make_ushort4(f16_pack(va.x), f16_pack(va.y), f16_pack(va.z), f16_pack(va.w));
+        reinterpret_cast<ushort4*>(cache + kHd / 2)[lane] =
+            make_ushort4(f16_pack(vb.x), f16_pack(vb.y), f16_pack(vb.z), f16_pack(vb.w));
+      }
+    }
+    // The unused split rows of the mma's A operands are zero.
+    if (2 * GH < 8 && warp >= GH + 2) {
+      for (int i = tid - (GH + 2) * 32; i < (8 - 2 * GH) * QS; i += (kCW - GH - 2) * 32) qh()[2 * GH * QS + i] = 0;
+      for (int i = tid - (GH + 2) * 32; i < (8 - 2 * GH) * PS; i += (kCW - GH - 2) * 32) ph()[2 * GH * PS + i] = 0;
+    }
+    stamp(l, 1, 2);
+    float m_h = -INFINITY, l_h = 0.f;  // warp h < GH: head h's running max and sum
+    const int g = lane >> 2, t = lane & 3;
+    // Lane (g, t) of warp w: split row g, dimensions 32 w + 8 i + 2 t + {0, 1}.
+    float acc[4][2];
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = 0.f;
+#pragma unroll 1
+    for (uint32_t jc = j0, ci = 0; jc < j1; jc += C, ci++) {
+      const uint32_t n = min((uint32_t)C, j1 - jc), rb = (ci & 1u) * C;
+      // Chunk ci's copies: the next chunk's may still be in flight.
+      if (jc + C < j1) asm volatile("cp.async.wait_group 1;" ::: "memory");
+      else asm volatile("cp.async.wait_group 0;" ::: "memory");
+      cbar();
+      // The new position's key and value are not in the cache yet: from the rope warps.
+      if (pos >= jc && pos < jc + n && (warp == GH || warp == GH + 1)) {
+        const uint32_t r = pos - jc, rr = rb + r;
         const ushort4 pa = make_ushort4(f16_pack(va.x), f16_pack(va.y), f16_pack(va.z), f16_pack(va.w));
         const ushort4 pb = make_ushort4(f16_pack(vb.x), f16_pack(vb.y), f16_pack(vb.z), f16_pack(vb.w));
-        uint16_t* kv = kvs + (warp - GH) * kHd;
-        reinterpret_cast<ushort4*>(kv)[lane] = pa;
-        reinterpret_cast<ushort4*>(kv + kHd / 2)[lane] = pb;
-        if (last) {
-          uint16_t* cache = (warp == GH ? L.key_cache : L.value_cache) + row * L.seq_stride +
-                            ((size_t)(pos % L.slots) * KV + kvh) * kHd;
-          reinterpret_cast<ushort4*>(cache)[lane] = pa;
-          reinterpret_cast<ushort4*>(cache + kHd / 2)[lane] = pb;
+        // elements 4 lane .. 4 lane + 3 and 128 + 4 lane ..: pieces lane / 2 and 16 + lane / 2
+        const uint32_t c0 = (uint32_t)lane / 2, c1 = 16u + (uint32_t)lane / 2, off = (lane & 1) * 4;
+        uint16_t* base = (warp == GH ? ks() : vs()) + rr * kHd + off;
+        uint16_t* dst0 = base + ((c0 ^ (r & 7u)) * 8);
+        uint16_t* dst1 = base + ((c1 ^ (r & 7u)) * 8);
+        *reinterpret_cast<ushort4*>(dst0) = pa;
+        *reinterpret_cast<ushort4*>(dst1) = pb;
+      }
+      cbar();
+      // Scores: warp w < 4 takes keys 8 w .. 8 w + 7 (one n-tile), all 16 k-steps.
+      if (warp < 4) {
+        const uint16_t* qrow = qh() + g * QS + 2 * t;
+        const uint32_t key = rb + 8 * warp + g;
+        const uint16_t* krow = ks() + key * kHd + 2 * t;
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+          const uint32_t af[4] = {*reinterpret_cast<const uint32_t*>(qrow + 16 * k), 0u,
+                                  *reinterpret_cast<const uint32_t*>(qrow + 16 * k + 8), 0u};
+          const uint2 bf = make_uint2(*reinterpret_cast<const uint32_t*>(krow + (((2 * k) ^ (key & 7u)) * 8)),
+                                      *reinterpret_cast<const uint32_t*>(krow + (((2 * k + 1) ^ (key & 7u)) * 8)));
+          mma16816(d, af, bf, d);
+        }
+        // Row g < GH: head g's part; row g + GH its remainder, GH lanes-of-4 down.
+        const float r0 = __shfl_down_sync(0xffffffffu, d[0], 4 * GH);
+        const float r1 = __shfl_down_sync(0xffffffffu, d[1], 4 * GH);
+        if (g < GH) {
+          sc()[g * C + 8 * warp + 2 * t] = add(d[0], r0);
+          sc()[g * C + 8 * warp + 2 * t + 1] = add(d[1], r1);
         }
       }
-    }
-    cbar();
-    stamp(l, 1, 2);
-    // Keys: lane holds dimensions 8 lane .. 8 lane + 7 (the queries stay in
-    // shared memory, read per key, to leave registers to the loads in flight).
-    const float4* q4 = reinterpret_cast<const float4*>(qs) + 2 * lane;
-    float m[GH], ls[GH], o[GH][8];
-#pragma unroll
-    for (int h = 0; h < GH; h++) {
-      m[h] = -INFINITY;
-      ls[h] = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; i++) o[h][i] = 0.f;
-    }
-    #pragma unroll 1
-    for (uint32_t jb = j0 + warp; jb < j1; jb += kCW * KU) {
-      if (!have) load_keys(L, row, kvh, jb, j1, kw, vw);
-      have = false;
-#pragma unroll
-      for (int u = 0; u < KU; u++)
-        if (jb + kCW * u == pos) {
-          kw[u] = reinterpret_cast<const uint4*>(kvs)[lane];
-          vw[u] = reinterpret_cast<const uint4*>(kvs + kHd)[lane];
-        }
-      float sc[KU][GH];
-#pragma unroll
-      for (int u = 0; u < KU; u++) {
-        float k[8];
-        {
-          const float2 f0 = h2f2(kw[u].x), f1 = h2f2(kw[u].y), f2 = h2f2(kw[u].z), f3 = h2f2(kw[u].w);
-          k[0] = f0.x; k[1] = f0.y; k[2] = f1.x; k[3] = f1.y;
-          k[4] = f2.x; k[5] = f2.y; k[6] = f3.x; k[7] = f3.y;
-        }
-#pragma unroll
-        for (int h = 0; h < GH; h++) {
-          const float4 x0 = q4[h * (kHd / 4)], x1 = q4[h * (kHd / 4) + 1];
-          const float qv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-          float s = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; i++) s = __fmaf_rn(qv[i], k[i], s);
-          s = warp_sum(s);
-          sc[u][h] = jb + kCW * u < j1 ? s : -INFINITY;
-        }
+      cbar();
+      // Online softmax: warp h takes head h.
+      if (warp < GH) {
+        const float s = (uint32_t)lane < n ? sc()[warp * C + lane] : -INFINITY;
+        const float mx = fmaxf(m_h, warp_max(s));
+        const float corr = exp2f(m_h - mx);
+        const float e = (uint32_t)lane < n ? exp2f(s - mx) : 0.f;
+        l_h = __fmaf_rn(l_h, corr, warp_sum(e));
+        m_h = mx;
+        __half ehi, elo;
+        split_hi_lo(e, ehi, elo);
+        ph()[warp * PS + lane] = __half_as_ushort(ehi);
+        ph()[(GH + warp) * PS + lane] = __half_as_ushort(elo);
+        if (lane == 0) hstat()[warp] = corr;
       }
+      cbar();
+      // Values: warp w takes dimensions 32 w .. 32 w + 31 (four n-tiles), keys in two k-steps.
+      {
+        const float corr = g < 2 * GH ? hstat()[g < GH ? g : g - GH] : 0.f;
+        uint32_t af[2][4];
 #pragma unroll
-      for (int h = 0; h < GH; h++) {
-        float mx = m[h];
+        for (int k = 0; k < 2; k++) {
+          af[k][0] = *reinterpret_cast<const uint32_t*>(ph() + g * PS + 16 * k + 2 * t);
+          af[k][1] = 0u;
+          af[k][2] = *reinterpret_cast<const uint32_t*>(ph() + g * PS + 16 * k + 8 + 2 * t);
+          af[k][3] = 0u;
+        }
 #pragma unroll
-        for (int u = 0; u < KU; u++) mx = fmaxf(mx, sc[u][h]);
-        const float corr = exp2f(m[h] - mx);
-        ls[h] = mul(ls[h], corr);
+        for (int i = 0; i < 4; i++) {
+          const uint32_t nt = 4 * warp + i;
+          float d[4] = {mul(acc[i][0], corr), mul(acc[i][1], corr), 0.f, 0.f};
 #pragma unroll
-        for (int i = 0; i < 8; i++) o[h][i] = mul(o[h][i], corr);
-#pragma unroll
-        for (int u = 0; u < KU; u++) {
-          if (jb + kCW * u < j1) {
-            const float e = exp2f(sc[u][h] - mx);
-            ls[h] = add(ls[h], e);
-            const float2 f[4] = {h2f2(vw[u].x), h2f2(vw[u].y), h2f2(vw[u].z), h2f2(vw[u].w)};
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-              o[h][2 * i] = __fmaf_rn(e, f[i].x, o[h][2 * i]);
-              o[h][2 * i + 1] = __fmaf_rn(e, f[i].y, o[h][2 * i + 1]);
-            }
+          for (int k = 0; k < 2; k++) {
+            // Lanes 0..15 address the 16 key rows of this k-step's two 8 x 8 tiles.
+            const uint32_t key = rb + 16 * k + (lane & 15);
+            const uint16_t* src = vs() + key * kHd + ((nt ^ (key & 7u)) * 8);
+            uint2 bf;
+            asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+                         : "=r"(bf.x), "=r"(bf.y)
+                         : "r"(su32(src)));
+            mma16816(d, af[k], bf, d);
           }
+          acc[i][0] = d[0];
+          acc[i][1] = d[1];
         }
-        m[h] = mx;
       }
+      cbar();
+      if (jc + 2 * C < j1) stage(L, row, kvh, jc + 2 * C, min((uint32_t)C, j1 - jc - 2 * C), ci & 1u);
     }
-#pragma unroll
-    for (int h = 0; h < GH; h++) {
-      if (lane == 0) {
-        pm[warp * GH + h] = m[h];
-        pl[warp * GH + h] = ls[h];
-      }
-      float4* dst = reinterpret_cast<float4*>(po + (warp * GH + h) * kHd + 8 * lane);
-      dst[0] = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
-      dst[1] = make_float4(o[h][4], o[h][5], o[h][6], o[h][7]);
+    // Each head's max and sum from warp h.
+    if (warp < GH && lane == 0) {
+      hstat()[warp] = m_h;
+      hstat()[GH + warp] = l_h;
     }
     cbar();
-    // Fold the warps in order; thread tid is dimension tid.
-    const uint32_t dim = (uint32_t)tid;
+    stamp(l, 1, 3);
+    // Row g < GH: head g's output, plus its remainder row g + GH.
 #pragma unroll
-    for (int h = 0; h < GH; h++) {
-      float mm = -INFINITY;
-      for (int w = 0; w < kCW; w++) mm = fmaxf(mm, pm[w * GH + h]);
-      float lsum = 0.f, acc_o = 0.f;
-      for (int w = 0; w < kCW; w++) {
-        const float mw = pm[w * GH + h];
-        const float f = mw == mm ? 1.0f : exp2f(mw - mm);
-        lsum = __fmaf_rn(pl[w * GH + h], f, lsum);
-        acc_o = __fmaf_rn(po[(w * GH + h) * kHd + dim], f, acc_o);
-      }
-      const uint32_t head = kvh * GH + h;
-      if (nsplit == 1) {
-        a.attn[((size_t)row * H + head) * kHd + dim] = __fdiv_rn(acc_o, lsum);
-      } else {
-        const size_t at = ((size_t)row * H + head) * a.max_splits + split;
-        a.partial_o[at * kHd + dim] = acc_o;
-        if (dim == 0) {
-          a.partial_ml[at * 2] = mm;
-          a.partial_ml[at * 2 + 1] = lsum;
+    for (int i = 0; i < 4; i++) {
+      const float r0 = __shfl_down_sync(0xffffffffu, acc[i][0], 4 * GH);
+      const float r1 = __shfl_down_sync(0xffffffffu, acc[i][1], 4 * GH);
+      if (g < GH) {
+        const uint32_t head = kvh * GH + g, dim = 32 * warp + 8 * i + 2 * t;
+        const float o0 = add(acc[i][0], r0), o1 = add(acc[i][1], r1);
+        if (nsplit == 1) {
+          const float lsum = hstat()[GH + g];
+          *reinterpret_cast<float2*>(a.attn + ((size_t)row * H + head) * kHd + dim) =
+              make_float2(__fdiv_rn(o0, lsum), __fdiv_rn(o1, lsum));
+        } else {
+          const size_t at = ((size_t)row * H + head) * a.max_splits + split;
+          *reinterpret_cast<float2*>(a.partial_o + at * kHd + dim) = make_float2(o0, o1);
         }
       }
     }
-    stamp(l, 1, 3);
+    if (nsplit > 1 && tid < GH) {
+      const size_t at = ((size_t)row * H + kvh * GH + tid) * a.max_splits + split;
+      a.partial_ml[at * 2] = hstat()[tid];
+      a.partial_ml[at * 2 + 1] = hstat()[GH + tid];
+    }
+    const uint32_t dim = (uint32_t)tid;
     bool final_cta = nsplit == 1;
     if (!final_cta) {
       cbar();
@@ -831,10 +921,8 @@ struct Attn {
           const uint32_t head = kvh * GH + h;
           const size_t base = ((size_t)row * H + head) * a.max_splits;
           float mm = -INFINITY;
-          #pragma unroll 1
           for (uint32_t s = 0; s < nsplit; s++) mm = fmaxf(mm, __ldcg(a.partial_ml + (base + s) * 2));
           float lsum = 0.f, acc_o = 0.f;
-          #pragma unroll 1
           for (uint32_t s = 0; s < nsplit; s++) {
             const float ms = __ldcg(a.partial_ml + (base + s) * 2);
             const float f = ms == mm ? 1.0f : exp2f(ms - mm);
@@ -876,9 +964,8 @@ struct Consumer {
   static constexpr uint32_t S = ring_slots<MQ>();
   static constexpr int R = 4 * MQ;        // rows of X the fragments carry
   static constexpr int C = 4 * MQ;        // columns of a warp's partial block
-  static constexpr int kRedBlock = kCW * 2 * 16 * C;  // floats one task's partials take
   const DecodeArgs& a;
-  uint32_t idx, kb_base, M, pos, W, pending, task_d, ph_kind, ph_l;
+  uint32_t idx, kb_base, M, pos, W, pending, pslots, task_d, ph_kind, ph_l;
   unsigned long long wait_ns;   // thread 0: time waiting for tiles (trace)
   // Shared-memory regions (offsets from the launch, so no registers hold them).
   FZ_DEV const uint4* codes() const { return reinterpret_cast<const uint4*>(g_smem + a.lay.codes); }
@@ -972,6 +1059,7 @@ struct Consumer {
     stamp(tl, trace_phase(kind), 1);
     kb_base = kb0;
     pending = 0;
+    pslots = 0;
     ph_kind = kind;
     ph_l = l;
     const uint64_t none = ~0ull, per = a.cap_per_layer;
@@ -1048,31 +1136,35 @@ struct Consumer {
     idx++;
   }
 
-  // A task's per-warp partials wait in their slot; the slots are reduced and
-  // finished together (one barrier pair for up to red_slots(MQ) tasks).
+  // A task's per-warp partials wait in shared memory; the waiting tasks are
+  // reduced and finished together (one barrier pair for several tasks).
+  static constexpr int kRedHalf = kCW * 16 * C;   // floats of one half-slot
   FZ_DEV void task_end(uint32_t kind, uint32_t l, uint32_t rg, uint32_t d) {
     if (dead) return;
-    float* rw = red() + pending * kRedBlock + warp * (2 * 16 * C);
+    const uint32_t need = kind == kPhGate ? 2u : 1u;
+    if (pslots + need > red_half_slots(MQ)) flush(kind, l);
+    if (dead) return;
+    float* rw = red() + pslots * kRedHalf + warp * (16 * C);
 #pragma unroll
     for (int q = 0; q < MQ; q++) {
       rw[g * C + 4 * q + t] = acc[0][q][0];
       rw[(g + 8) * C + 4 * q + t] = acc[0][q][1];
       if (kind == kPhGate) {
-        rw[16 * C + g * C + 4 * q + t] = acc[1][q][0];
-        rw[16 * C + (g + 8) * C + 4 * q + t] = acc[1][q][1];
+        rw[kRedHalf + g * C + 4 * q + t] = acc[1][q][0];
+        rw[kRedHalf + (g + 8) * C + 4 * q + t] = acc[1][q][1];
       }
     }
     if (tid == 0) task_rg()[pending] = rg;
     task_d = d;
     pending++;
+    pslots += need;
     zero_acc();
-    if (pending == red_slots(MQ)) flush(kind, l);
   }
 
   FZ_DEV void flush(uint32_t kind, uint32_t l) {
     cbar();
     stamp(kind == kPhHead ? a.n_layers - 1 : l, trace_phase(kind), 3);
-    const uint32_t Hd = a.hidden;
+    const uint32_t Hd = a.hidden, need = kind == kPhGate ? 2u : 1u;
     const int per_task = 16 * (int)M, total = (int)pending * per_task;
 #pragma unroll 1
     for (int base = 0; base < total; base += kCT) {
@@ -1081,10 +1173,10 @@ struct Consumer {
       const int slot = i / per_task, rest = i % per_task, tok = rest / 16, row = rest % 16;
       unsigned long long key = 0ull;
       if (live) {
-        const float* rs = red() + slot * kRedBlock;
+        const float* rs = red() + slot * need * kRedHalf;
         const uint32_t n = task_rg()[slot] * 16 + row;
         float v = 0.f;
-        for (int w = 0; w < kCW; w++) v = add(v, rs[w * (2 * 16 * C) + row * C + tok]);
+        for (int w = 0; w < kCW; w++) v = add(v, rs[w * (16 * C) + row * C + tok]);
         if (kind == kPhQkv) {
           a.qkv[(size_t)tok * ((a.heads + 2 * a.kv_heads) * kHd) + n] = v;
         } else if (kind == kPhO) {
@@ -1096,7 +1188,7 @@ struct Consumer {
           key = head_key(v, n);
         } else {
           float up = 0.f;
-          for (int w = 0; w < kCW; w++) up = add(up, rs[w * (2 * 16 * C) + 16 * C + row * C + tok]);
+          for (int w = 0; w < kCW; w++) up = add(up, rs[kRedHalf + w * (16 * C) + row * C + tok]);
           v = mul(gelu_tanh(v), up);
           if (a.edit_table) v = apply_edits(a.edit_table + (size_t)tok * a.table_stride, l, n, pos, v);
           a.act[(size_t)tok * a.ffn + n] = v;
@@ -1111,6 +1203,7 @@ struct Consumer {
       }
     }
     pending = 0;
+    pslots = 0;
     sync_dead();
   }
 
@@ -1220,6 +1313,7 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
     c.pos = a.step->position;
     c.W = kDecodeSyncFixed + a.m * a.kv_heads;
     c.pending = 0;
+    c.pslots = 0;
     c.task_d = 0;
     c.ph_kind = 0;
     c.ph_l = 0;

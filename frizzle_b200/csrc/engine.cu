@@ -481,7 +481,8 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     d.cap_per_layer = cl.per_layer;
     d.head = m.embd.view();
     d.output_norm = m.output_norm;
-    d.logits = key.logits ? b.logits : nullptr;
+    // The head runs as its own streaming launch (below), not inside the step.
+    d.logits = nullptr;
     d.argmax = b.argmax;
     d.error = b.gemm_error;
     if (b.trace) {
@@ -491,6 +492,28 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     }
     FZ_CUDA(fz::launch_decode(d, st));
     if (key.logits) {
+      // Final norm (X plus the last down projection's K-slice partials) and the tied head.
+      fz::MatvecArgs h{};
+      h.step = b.dstep;
+      h.mat[0] = m.embd.view();
+      h.m = b.S;
+      h.seq_tokens = 1;
+      h.capture_stride = cl.per_layer * s.layers;
+      h.norm.hidden_in = b.hidden_a;
+      h.norm.y = d.y_mlp;
+      h.norm.y_parts = fz::kDecodeDownSlices;
+      h.norm.y_part_stride = (uint64_t)b.S * s.hidden;
+      h.norm.post_gain = m.layers[s.layers - 1].post_ffw_norm;
+      h.norm.gain = m.output_norm;
+      h.norm.hidden_out = nullptr;
+      h.norm.eps = s.eps;
+      h.norm.width = s.hidden;
+      h.norm.row_of_token_stride = 1;
+      h.norm.capture_added = cap ? cap + (s.layers - 1) * cl.per_layer + cl.mlp_added : nullptr;
+      h.out = b.logits;
+      h.out_stride = s.vocab;
+      h.head.argmax = b.argmax;
+      if ((stt = run_matvec(h, fz::kPrologueNorm, fz::kEpilogueHead, st, pdl))) return stt;
       fz::SelectArgs se{};
       se.step = b.dstep;
       se.logits = b.logits;

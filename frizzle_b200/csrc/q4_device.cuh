@@ -11,15 +11,21 @@ namespace q4dev {
 FZ_DEV uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 FZ_DEV __half2 bits_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
-// Four A registers (rows g, g+8 x the permuted columns) from one code word:
-// 0x6400 | n is the half 1024 + n, less 1032 gives n - 8 exactly.
+// Four A registers (rows g, g+8 x the permuted columns) from one code word.
+// A nibble n at bits 0-3 of a half: (n | 0x6400) is the half 1024 + n, less
+// 1032 gives n - 8 exactly.  A nibble at bits 4-7: (16 n | 0x6400) is
+// 1024 + 16 n, and 1/16 of it less 72 (one fused multiply-add) is n - 8,
+// exactly; so one shift serves the word's upper two nibbles of each half.
 FZ_DEV void dequant_word(uint32_t w, uint32_t a[4]) {
-  const uint32_t kMask = 0x000F000Fu, kMagic = 0x64006400u;
-  const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408u));
-  a[0] = h2_bits(__hsub2(bits_h2((w & kMask) | kMagic), bias));
-  a[1] = h2_bits(__hsub2(bits_h2(((w >> 8) & kMask) | kMagic), bias));
-  a[2] = h2_bits(__hsub2(bits_h2(((w >> 4) & kMask) | kMagic), bias));
-  a[3] = h2_bits(__hsub2(bits_h2(((w >> 12) & kMask) | kMagic), bias));
+  const uint32_t kLow = 0x000F000Fu, kHigh = 0x00F000F0u, kMagic = 0x64006400u;
+  const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408u));       // 1032
+  const __half2 sixteenth = __half2half2(__ushort_as_half((unsigned short)0x2C00u));  // 1/16
+  const __half2 bias16 = __half2half2(__ushort_as_half((unsigned short)0xD480u));     // -72
+  const uint32_t w8 = w >> 8;
+  a[0] = h2_bits(__hsub2(bits_h2((w & kLow) | kMagic), bias));
+  a[1] = h2_bits(__hsub2(bits_h2((w8 & kLow) | kMagic), bias));
+  a[2] = h2_bits(__hfma2(bits_h2((w & kHigh) | kMagic), sixteenth, bias16));
+  a[3] = h2_bits(__hfma2(bits_h2((w8 & kHigh) | kMagic), sixteenth, bias16));
 }
 
 FZ_DEV void mma16816(float d[4], const uint32_t a[4], uint2 b, const float c[4]) {

@@ -122,6 +122,17 @@ FZ_DEV void tree_reduce(float* part, int rows, float* total) {
   __syncthreads();
 }
 
+// vec4 v of the block output y for one row: y itself, or the sum of its
+// n.y_parts K-slice partials (n.y_part_stride floats apart), in slice order.
+FZ_DEV float4 y_sum(const NormArgs& n, const float* yr, int v) {
+  float4 y = __ldcg(reinterpret_cast<const float4*>(yr) + v);
+  for (uint32_t k = 1; k < n.y_parts; k++) {
+    const float4 z = __ldcg(reinterpret_cast<const float4*>(yr + k * n.y_part_stride) + v);
+    y = make_float4(add(y.x, z.x), add(y.y, z.y), add(y.z, z.z), add(y.w, z.w));
+  }
+  return y;
+}
+
 // The norm launch over the step's rows, by the whole CTA (norm.wgsl:97-198):
 // invocation i of the reference is thread i, holding vec4s i, i + 256, ...
 // Leaves the normed rows in `rowbuf` [rows][width]; CTA 0 writes X after the
@@ -135,9 +146,9 @@ FZ_DEV void norm_rows_cta(const MatvecArgs& a, const NormArgs& n, int rows, floa
   auto hrow_of = [&](int r) { return r * (int)n.row_of_token_stride + (int)n.row_of_token_offset; };
   if (n.y && n.post_gain) {
     for (int r = 0; r < rows; r++) {
-      const float4* y4 = reinterpret_cast<const float4*>(n.y + (size_t)hrow_of(r) * W);
+      const float* yr = n.y + (size_t)hrow_of(r) * W;
       float p = 0.f;
-      for (int v = tid; v < V; v += kThreads) p = add(p, dot_self(y4[v]));
+      for (int v = tid; v < V; v += kThreads) p = add(p, dot_self(y_sum(n, yr, v)));
       part[r * kThreads + tid] = p;
     }
     tree_reduce(part, rows, ry);
@@ -149,7 +160,7 @@ FZ_DEV void norm_rows_cta(const MatvecArgs& a, const NormArgs& n, int rows, floa
     const uint32_t seq = (uint32_t)hrow / a.seq_tokens;
     const bool last = (uint32_t)hrow % a.seq_tokens == a.seq_tokens - 1;
     const float4* x4 = reinterpret_cast<const float4*>(n.hidden_in + (size_t)hrow * W);
-    const float4* y4 = n.y ? reinterpret_cast<const float4*>(n.y + (size_t)hrow * W) : nullptr;
+    const float* yr = n.y ? n.y + (size_t)hrow * W : nullptr;
     const float4* pg4 = reinterpret_cast<const float4*>(n.post_gain);
     float4* out4 = writer && n.hidden_out ? reinterpret_cast<float4*>(n.hidden_out + (size_t)hrow * W) : nullptr;
     float4* xcap = writer && last && n.capture_residual
@@ -160,8 +171,8 @@ FZ_DEV void norm_rows_cta(const MatvecArgs& a, const NormArgs& n, int rows, floa
     float p = 0.f;
     for (int v = tid; v < V; v += kThreads) {
       float4 x = x4[v];
-      if (y4) {
-        float4 y = y4[v];
+      if (yr) {
+        float4 y = y_sum(n, yr, v);
         if (n.post_gain) {
           const float s = ry[r];
           const float4 g = pg4[v];

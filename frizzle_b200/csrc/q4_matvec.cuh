@@ -51,6 +51,8 @@ struct NormArgs {
   uint32_t row_of_token_offset;  // added to the row index
   float* capture_residual;  // [m][width] X after the add, or null
   float* capture_added;     // [m][width] y as added, or null
+  uint32_t y_parts;         // y is the sum of this many K-slice partials (0 or 1: y itself)
+  uint64_t y_part_stride;   // floats between the partials
 };
 
 struct RopeArgs {
