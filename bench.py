@@ -341,6 +341,40 @@ def run_ours(args):
         pos += K
     dec_s = ev[2].elapsed_time(ev[3]) / 1000.0
     e2e_s = ev[4].elapsed_time(ev[5]) / 1000.0
+    sweep_line = None
+    if not args.no_sweep:
+        # 64 steered/unsteered pairs over one 256-token prompt, 128 sampled tokens each
+        # (temperature 1, top-k 64), pairs sharded across the ranks; device-timed, max over ranks.
+        from frizzle_b200 import sweep
+        n_pairs, s_steps, s_layer = 64, 128, 13
+        pairs = sweep.make_pairs(n_pairs, synth.GEMMA3_1B.ffn, seed=0)
+        mine = [pairs[i] for i in sweep.shard(n_pairs, world, rank)]
+        s_prompt = np.random.default_rng([0, 256]).integers(2, synth.GEMMA3_1B.vocab, size=256).astype(np.uint32)
+        if dist:
+            dist.barrier()
+        sv = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        with torch.cuda.stream(stream):
+            sv[0].record()
+        res = sweep.run(model, s_prompt, mine, s_steps, s_layer, batch_seqs=8, context=1024, temperature=1.0)
+        with torch.cuda.stream(stream):
+            sv[1].record()
+        torch.cuda.synchronize()
+        sweep_s = sv[0].elapsed_time(sv[1]) / 1000.0
+        full = sweep.gather(res, n_pairs, s_steps, dist, device=torch.device("cuda", local)) if dist else None
+        if dist:
+            t = torch.tensor([sweep_s], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            sweep_s = float(t.item())
+        else:
+            full = np.stack([res[i] for i in range(n_pairs)])
+        if rank == 0:
+            differ = float(np.mean(np.any(full[:, 0] != full[:, 1], axis=1)))
+            sweep_line = {"workload": "BASELINE config 4: 64 steered + 64 unsteered twins (same seed), one 256-token "
+                                      "prompt, layer-13 pins (k in 1..8, values in [-10, 10]), 128 tokens each at "
+                                      "temperature 1, top-k 64; 8 sequences a batch; pairs sharded over the GPUs",
+                          "sequences": 2 * n_pairs, "tokens_per_sequence": s_steps, "seconds": sweep_s,
+                          "tokens_per_s": 2 * n_pairs * s_steps / sweep_s, "scaling": "strong",
+                          "pairs_whose_twins_differ": differ}
     if dist:
         # The job's final exchange: rank 0 gathers every sequence's last logits.
         last = torch.from_numpy(batch.logits(0)).cuda()
@@ -371,6 +405,8 @@ def run_ours(args):
                              "peak_source": which, "algorithmic_bytes": head_bytes,
                              "launch_us": head_secs * 1e6, "traffic": traffic_from_profile()},
                 "clocks": clocks.summary()}
+        if sweep_line:
+            line["steering_sweep"] = sweep_line
         # a 4096-token prompt prefilled in one step (the tcgen05 path).
         pre = engine.Batch(model, 1, 8192)
         ids4k = np.random.default_rng([rank, 4096]).integers(2, synth.GEMMA3_1B.vocab, size=4096).astype(np.uint32)
@@ -424,6 +460,7 @@ def main():
                     help="time only the tensor-core gated product at M = 4096 and print its numbers")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config-4 steering sweep")
     ap.add_argument("--trace", action="store_true",
                     help="print the decode kernel's phase timeline (device timestamps), averaged over steps")
     args = ap.parse_args()
