@@ -415,6 +415,12 @@ fz_status alloc_rows(fz_batch& b, uint32_t rows) {
 
 // The persistent decode kernel serves one-token steps unless
 // FRIZZLE_B200_LAYERED=1 asks for the per-operation launches.
+// Wide steps use the tensor-core attention unless FRIZZLE_B200_SCALAR_ATTENTION=1.
+bool prefill_attention_enabled() {
+  const char* v = std::getenv("FRIZZLE_B200_SCALAR_ATTENTION");
+  return !(v && *v && *v != '0');
+}
+
 bool decode_step_enabled() {
   const char* v = std::getenv("FRIZZLE_B200_LAYERED");
   return !(v && *v && *v != '0');
@@ -612,7 +618,10 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       at.out = b.attn;
       at.out_hi = b.x16_hi;
       at.out_lo = xlo;
-      FZ_CUDA(fz::launch_attention(at, st, pdl));
+      if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim) && prefill_attention_enabled())
+        FZ_CUDA(fz::launch_attention_prefill(at, st, pdl));
+      else
+        FZ_CUDA(fz::launch_attention(at, st, pdl));
       if ((stt = gemm(L.o, nullptr, b.x16_hi, xlo, b.y_attn, s.hidden, fz::kGemmWrite, l))) return stt;
       fz::MatvecArgs g = a;
       g.norm.hidden_in = b.hidden_b;
@@ -1036,6 +1045,7 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     if ((st = b->alloc(&b->dlayers, dl.size() * sizeof(fz::DecodeLayer)))) return st;
     if (fz::decode_supported(1, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim))
       FZ_CUDA(fz::prepare_decode(s.hidden, s.ffn, s.heads, s.kv_heads));
+    if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) FZ_CUDA(fz::configure_attention_prefill());
     FZ_CUDA(cudaMemcpy(b->dlayers, dl.data(), dl.size() * sizeof(fz::DecodeLayer), cudaMemcpyHostToDevice));
   }
   b->table_words = 2 * s.layers + 5 * kMaxEdits;

@@ -147,34 +147,38 @@ FZ_DEV Codes load_codes(const Q4Matrix& w, uint32_t rg, uint32_t bp, bool live, 
 FZ_DEV void dequant_tile(unsigned char* tile, unsigned char* tile_lo, uint32_t row0, const Codes& x, bool live,
                          int lane) {
   const uint32_t g = lane >> 2, t = lane & 3;
-  const uint32_t kMask = 0x000F000Fu, kMagic = 0x64006400u;
-  const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408u));
+  const uint32_t kLow = 0x000F000Fu, kHigh = 0x00F000F0u, kMagic = 0x64006400u;
+  const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408u));       // 1032
+  const __half2 sixteenth = __half2half2(__ushort_as_half((unsigned short)0x2C00u));  // 1/16
+  const __half2 bias16 = __half2half2(__ushort_as_half((unsigned short)0xD480u));     // -72
   const uint32_t words[4] = {x.c.x, x.c.y, x.c.z, x.c.w};
 #pragma unroll
   for (int wi = 0; wi < 4; wi++) {
     const uint32_t kb = wi >> 1, h = wi & 1;
-    const uint32_t wd = words[wi];
+    const uint32_t wd = words[wi], w8 = wd >> 8;
     const uint32_t sw = kb ? x.s.y : x.s.x;
+    // The block's scale for rows g and g + 8, each as a half2 pair.
+    const __half2 dg = u2h(__byte_perm(sw, 0, 0x1010)), dg8 = u2h(__byte_perm(sw, 0, 0x3232));
     const uint32_t k0 = 32 * kb + 8 * h + 2 * t;
     const uint32_t r0 = row0 + g, r8 = row0 + g + 8;
-    // (code - 8) exactly, as f16 pairs: rows g and g + 8, columns k0 (+1) and k0 + 16 (+1).
-    const __half2 c4[4] = {__hsub2(u2h((wd & kMask) | kMagic), bias), __hsub2(u2h(((wd >> 4) & kMask) | kMagic), bias),
-                           __hsub2(u2h(((wd >> 8) & kMask) | kMagic), bias),
-                           __hsub2(u2h(((wd >> 12) & kMask) | kMagic), bias)};
+    // (code - 8) exactly, as f16 pairs: rows g and g + 8, columns k0 (+1) and k0 + 16 (+1); a nibble
+    // at bits 0-3 of a half is 1024 + n less 1032, at bits 4-7 it is (1024 + 16 n) / 16 less 72.
+    const __half2 c4[4] = {__hsub2(u2h((wd & kLow) | kMagic), bias),
+                           __hfma2(u2h((wd & kHigh) | kMagic), sixteenth, bias16),
+                           __hsub2(u2h((w8 & kLow) | kMagic), bias),
+                           __hfma2(u2h((w8 & kHigh) | kMagic), sixteenth, bias16)};
     const uint32_t rows[4] = {r0, r0, r8, r8};
     const uint32_t cols[4] = {k0, k0 + 16, k0, k0 + 16};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const float d = __half2float(__ushort_as_half((unsigned short)(j < 2 ? (sw & 0xffffu) : (sw >> 16))));
-      const float2 q = __half22float2(c4[j]);
-      // (code - 8) * d is exact in f32; hi is it rounded once to f16, lo the
-      // remainder (exact in f32, rounded once to f16).
-      const float w0 = __fmul_rn(q.x, d), w1 = __fmul_rn(q.y, d);
-      const __half2 hi = __floats2half2_rn(w0, w1);
+      // (code - 8) * d is exact as a real product; hi is it rounded once to f16 (one f16 multiply), lo
+      // the remainder rounded once (one fused multiply-add): the f32 split of the product, without
+      // leaving f16.
+      const __half2 d = j < 2 ? dg : dg8;
+      const __half2 hi = __hmul2(c4[j], d);
       *reinterpret_cast<uint32_t*>(tile + swz(rows[j], cols[j])) = live ? h2u(hi) : 0u;
       if (tile_lo) {
-        const float2 hf = __half22float2(hi);
-        const __half2 lo = __floats2half2_rn(__fsub_rn(w0, hf.x), __fsub_rn(w1, hf.y));
+        const __half2 lo = __hfma2(c4[j], d, __hneg2(hi));
         *reinterpret_cast<uint32_t*>(tile_lo + swz(rows[j], cols[j])) = live ? h2u(lo) : 0u;
       }
     }

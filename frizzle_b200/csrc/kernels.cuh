@@ -31,6 +31,14 @@ struct AttentionArgs {
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl);
 
+// The tensor-core form for steps of many rows (attention_prefill.cu): head
+// dimension 256, 1, 2 or 4 query heads a KV head; every row of a sequence at
+// consecutive positions from the step's.  configure_attention_prefill raises
+// its shared-memory limit on the current device (call outside stream capture).
+bool attention_prefill_supported(uint32_t heads, uint32_t kv_heads, uint32_t head_dim);
+cudaError_t configure_attention_prefill();
+cudaError_t launch_attention_prefill(const AttentionArgs& a, cudaStream_t stream, bool pdl);
+
 // The embedding rows of the step's tokens (or, for a fed step, the last draw)
 // times `scale`, into hidden [m][width]; also clears the argmax slots.
 struct EmbedArgs {

@@ -66,11 +66,16 @@ def run(model, prompt, pairs: list, steps: int, layer: int, batch_seqs: int = 8,
     out = {p.index: np.zeros((2, steps), dtype=np.int32) for p in pairs}
     n = len(prompt)
     sampling = engine.Sampling(temperature=temperature, top_k=top_k, top_p=1.0, min_p=0.0)
-    for b0 in range(0, len(seqs), batch_seqs):
-        group = seqs[b0:b0 + batch_seqs]
-        S = len(group)
-        batch = engine.Batch(model, S, context)
-        try:
+    # One batch serves every group of the same size (a new group's prefill rewrites its caches from
+    # position 0, and the step graphs captured for the first group are reused).
+    batches = {}
+    try:
+        for b0 in range(0, len(seqs), batch_seqs):
+            group = seqs[b0:b0 + batch_seqs]
+            S = len(group)
+            if S not in batches:
+                batches[S] = engine.Batch(model, S, context)
+            batch = batches[S]
             seeds = np.array([p.seed for p, _ in group], dtype=np.uint32)
             for s, (p, steered) in enumerate(group):
                 words = E.table(p.edits(layer), model.info.layers, n - 1) if steered else None
@@ -84,8 +89,9 @@ def run(model, prompt, pairs: list, steps: int, layer: int, batch_seqs: int = 8,
                     out[p.index][0 if steered else 1, i] = toks[s]
                 if i + 1 < steps:
                     batch.step(n + i, fed=True, tokens=1, logits=True, sampling=sampling, seeds=seeds)
-        finally:
-            batch.free()
+    finally:
+        for b in batches.values():
+            b.free()
     return out
 
 
