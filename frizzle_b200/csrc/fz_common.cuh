@@ -105,6 +105,14 @@ FZ_DEV uint32_t topk_bits(uint32_t key) {
   return ~key;
 }
 
+// p * 2^k for k in [-149, 0], rounded once, as ldexp: a normal result is an
+// exact product with 2^k; below 2^-126 the product with 2^(k + 64) is exact and
+// the one with 2^-64 rounds once.
+FZ_DEV float scale_pow2(float p, int k) {
+  if (k >= -126) return __fmul_rn(p, __int_as_float((127 + k) << 23));
+  return __fmul_rn(__fmul_rn(p, __int_as_float((127 + k + 64) << 23)), 5.421010862427522e-20f);
+}
+
 // e^x for x <= 0 (matmul.wgsl:122-138) and GELU's tanh form from it
 // (matmul.wgsl:140-152): the same fma chain, so the same bits as the shader
 // on an IEEE target.
@@ -120,13 +128,13 @@ FZ_DEV float exp_nonpositive(float x) {
   p = __fmaf_rn(p, r, 0.5f);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  return ldexpf(p, (int)k);
+  return scale_pow2(p, (int)k);
 }
 FZ_DEV float gelu_tanh(float g) {
   float z = mul(0.7978845608028654f, __fmaf_rn(mul(mul(0.044715f, g), g), g, g));
   float e = exp_nonpositive(mul(-2.0f, fabsf(z)));
   float s = z > 0.0f ? 1.0f : (z < 0.0f ? -1.0f : 0.0f);
-  float t = mul(s, mul(sub(1.0f, e), __fdiv_rn(1.0f, add(1.0f, e))));
+  float t = mul(s, mul(sub(1.0f, e), __frcp_rn(add(1.0f, e))));  // 1 / (1 + e), rounded once
   float half_g = mul(0.5f, g);
   return __fmaf_rn(half_g, t, half_g);
 }

@@ -348,11 +348,13 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       if (kt + 1 < nkt && !stop) step(kt + 1, B, A);
       if (kt + 2 < nkt && !stop) step(kt + 2, C, B);
     }
-    // Epilogue: warps 2..5, TMEM lanes 32 * (warp % 4) .. + 31.
-    if (warp < 6) {
+    // Epilogue: all eight producer warps; warp w reads TMEM lanes 32 * (w % 4)
+    // .. + 31, warps 2..5 the first half of the columns, warps 6..9 the second.
+    {
       const bool ok = mbar_wait(&accum_full, 0, a.error, 4);
       fence_after_sync();
       const uint32_t quarter = (uint32_t)warp & 3u;
+      const int side = warp < 6 ? 0 : 1;
       const uint32_t row = m0 + quarter * 32 + lane;
       const uint32_t lane_addr = tmem + ((quarter * 32u) << 16);
       // The stages are idle once the accumulator is full: each epilogue warp
@@ -362,7 +364,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       if (ok) {
         if (EPI == kGemmWrite) {
           const uint32_t N = a.w[0].n;
-          for (int c0 = 0; c0 < BN; c0 += 32) {
+          for (int c0 = side * (BN / 2); c0 < (side + 1) * (BN / 2); c0 += 32) {
             uint32_t r[32];
             tmem_ld32(lane_addr + (uint32_t)c0, r);
 #pragma unroll
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           const uint32_t seq = row / a.seq_tokens;
           const uint32_t pos = (a.step ? a.step->position : a.position) + row % a.seq_tokens;
           const bool last = row % a.seq_tokens == a.seq_tokens - 1;
-          for (int c0 = 0; c0 < (int)half_bn; c0 += 32) {
+          for (int c0 = side * (int)(half_bn / 2); c0 < (side + 1) * (int)(half_bn / 2); c0 += 32) {
             uint32_t gr[32], ur[32];
             tmem_ld32(lane_addr + (uint32_t)c0, gr);
             tmem_ld32(lane_addr + half_bn + (uint32_t)c0, ur);
