@@ -11,13 +11,18 @@
 //   - warp 1 (one lane) issues tcgen05.mma kind::f16 (M = 128, N = BN,
 //     K = 16) into an f32 accumulator in tensor memory and commits each stage
 //     back to its producers;
-//   - warps 2..5 read the accumulator (tcgen05.ld 32x32b) and write Y, or,
+//   - warps 10..17 read the accumulator (tcgen05.ld 32x32b) and write Y, or,
 //     for a gated product, gelu(gate) * up with the steering edits.
+// CTAs are persistent (one per SM) and walk tiles t = blockIdx.x, + gridDim.x,
+// ...; the accumulator is double-buffered in TMEM (2 x BN columns), so the
+// epilogue of one tile runs while the next tile's MMAs fill the other buffer,
+// and the stage ring runs on across tile bounds.
 // Every mbarrier wait is bounded: on timeout the kernel records an error,
 // stops waiting, and still releases its tensor memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "gemm_tc.cuh"
@@ -28,7 +33,9 @@ namespace {
 constexpr int kBM = 128;              // rows of X a tile (the MMA's M)
 constexpr int kBK = 64;               // columns a stage: 128 B of f16 a row
 constexpr int kProducers = 8;         // weight-dequant warps (warps 2..9)
-constexpr int kThreadsG = 32 * (2 + kProducers);
+constexpr int kEpilogue = 8;          // epilogue warps (warps 10..17)
+constexpr int kThreadsG = 32 * (2 + kProducers + kEpilogue);
+constexpr int kStageCols = 16;        // accumulator columns an epilogue warp turns around at once
 constexpr uint32_t kSpinLimit = 1u << 20;
 
 FZ_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -209,8 +216,9 @@ struct Layout {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes * XP + kBBytes * WP;
-  static constexpr int kStages = (196 * 1024) / kStageBytes > 6 ? 6 : (196 * 1024) / kStageBytes;
-  static constexpr int kSmem = kStages * kStageBytes + 1024;  // + alignment slack
+  static constexpr int kStages = (200 * 1024) / kStageBytes > 6 ? 6 : (200 * 1024) / kStageBytes;
+  static constexpr int kEpiBytes = kEpilogue * 32 * (kStageCols + 1) * 4;   // epilogue turn-around
+  static constexpr int kSmem = kStages * kStageBytes + kEpiBytes + 1024;  // + alignment slack
 };
 
 // XP: passes over X (f16 hi, + lo); WP: passes over W (f16 hi, + lo).  The
@@ -226,31 +234,39 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   extern __shared__ unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full[S];
   __shared__ __align__(8) uint64_t empty[S];
-  __shared__ __align__(8) uint64_t accum_full;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base;
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   auto a_tile = [&](int s, int p) { return smem + s * L::kStageBytes + p * L::kABytes; };
   auto b_tile = [&](int s) { return smem + s * L::kStageBytes + XP * L::kABytes; };
   auto b_tile_lo = [&](int s) { return smem + s * L::kStageBytes + XP * L::kABytes + L::kBBytes; };
+  float* epi_stage = reinterpret_cast<float*>(smem + S * L::kStageBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t m0 = blockIdx.y * kBM;
   const uint32_t K = a.w[0].k, nkt = K / kBK;
   const uint32_t half_bn = BN / 2;
-  // Weight rows of this tile: n0.. for Write; neurons nn0.. of gate and up for Gated.
-  const uint32_t n0 = EPI == kGemmGated ? blockIdx.x * half_bn : blockIdx.x * BN;
+  const uint32_t cols = EPI == kGemmGated ? half_bn : BN;       // weight rows (neurons) a tile
+  const uint32_t mtiles = (a.m + kBM - 1) / kBM, ntiles = (a.w[0].n + cols - 1) / cols;
+  const uint32_t tiles = mtiles * ntiles;
+  // Tile t: rows m0 = (t % mtiles) * 128 of X, weight rows n0 = (t / mtiles) * cols.
+  auto m0_of = [&](uint32_t tile) { return (tile % mtiles) * kBM; };
+  auto n0_of = [&](uint32_t tile) { return (tile / mtiles) * cols; };
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < S; s++) {
       mbar_init(&full[s], 1 + kProducers);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&accum_full, 1);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpilogue);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
-                 "r"((uint32_t)BN)
+                 "r"((uint32_t)(2 * BN))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -263,51 +279,77 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     // X tiles by TMA; X is the previous kernel's output.  The whole warp runs
     // the loop and waits, lane 0 issues.
     pdl_wait();
-    for (uint32_t kt = 0; kt < nkt; kt++) {
-      const int s = (int)(kt % S);
-      const uint32_t round = kt / S;
-      if (!mbar_wait(&empty[s], (round + 1) & 1u, a.error, 1)) break;
-      if (lane == 0) {
-        mbar_expect_tx(&full[s], (uint32_t)(L::kABytes * PASSES));
-        tma_load_2d(a_tile(s, 0), &map_hi, &full[s], (int)(kt * kBK), (int)m0);
-        if (PASSES == 2) tma_load_2d(a_tile(s, 1), &map_lo, &full[s], (int)(kt * kBK), (int)m0);
+    uint32_t it = 0;
+    bool stop = false;
+    for (uint32_t tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x) {
+      const uint32_t m0 = m0_of(tile);
+      for (uint32_t kt = 0; kt < nkt; kt++, it++) {
+        const int s = (int)(it % S);
+        const uint32_t round = it / S;
+        if (!mbar_wait(&empty[s], (round + 1) & 1u, a.error, 1)) {
+          stop = true;
+          break;
+        }
+        if (lane == 0) {
+          mbar_expect_tx(&full[s], (uint32_t)(L::kABytes * PASSES));
+          tma_load_2d(a_tile(s, 0), &map_hi, &full[s], (int)(kt * kBK), (int)m0);
+          if (PASSES == 2) tma_load_2d(a_tile(s, 1), &map_lo, &full[s], (int)(kt * kBK), (int)m0);
+        }
+        __syncwarp();
       }
-      __syncwarp();
     }
   } else if (warp == 1) {
     // The MMA issuer: the whole warp waits, lane 0 issues and commits.
     constexpr uint32_t idesc = instr_desc<BN>();
-    for (uint32_t kt = 0; kt < nkt; kt++) {
-      const int s = (int)(kt % S);
-      const uint32_t round = kt / S;
-      if (!mbar_wait(&full[s], round & 1u, a.error, 2)) break;
+    uint32_t it = 0, tl = 0;
+    bool stop = false;
+    for (uint32_t tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x, tl++) {
+      const uint32_t buf = tl & 1u, use = tl >> 1;
+      // The epilogue has drained this accumulator (its previous use).
+      if (!mbar_wait(&acc_empty[buf], (use + 1) & 1u, a.error, 5)) break;
       fence_after_sync();
-      if (lane == 0) {
-        const uint64_t db = smem_desc(b_tile(s));
-        const uint64_t db_lo = smem_desc(b_tile_lo(s));
-        const uint64_t da = smem_desc(a_tile(s, 0));
-        const uint64_t da_lo = smem_desc(a_tile(s, XP - 1));
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; kk++) {
-          // 16 columns of f16 = 32 bytes along K: +2 in the 16-byte address field.
-          umma(tmem, da + 2 * kk, db + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
-          if (XP == 2) umma(tmem, da_lo + 2 * kk, db + 2 * kk, idesc, 1u);
-          if (WP == 2) umma(tmem, da + 2 * kk, db_lo + 2 * kk, idesc, 1u);
+      const uint32_t acc = tmem + buf * BN;
+      for (uint32_t kt = 0; kt < nkt; kt++, it++) {
+        const int s = (int)(it % S);
+        const uint32_t round = it / S;
+        if (!mbar_wait(&full[s], round & 1u, a.error, 2)) {
+          stop = true;
+          break;
         }
-        umma_commit(&empty[s]);
+        fence_after_sync();
+        if (lane == 0) {
+          const uint64_t db = smem_desc(b_tile(s));
+          const uint64_t db_lo = smem_desc(b_tile_lo(s));
+          const uint64_t da = smem_desc(a_tile(s, 0));
+          const uint64_t da_lo = smem_desc(a_tile(s, XP - 1));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; kk++) {
+            // 16 columns of f16 = 32 bytes along K: +2 in the 16-byte address field.
+            umma(acc, da + 2 * kk, db + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
+            if (XP == 2) umma(acc, da_lo + 2 * kk, db + 2 * kk, idesc, 1u);
+            if (WP == 2) umma(acc, da + 2 * kk, db_lo + 2 * kk, idesc, 1u);
+          }
+          umma_commit(&empty[s]);
+        }
+        __syncwarp();
       }
-      __syncwarp();
+      if (!stop) {
+        if (lane == 0) umma_commit(&acc_full[buf]);
+        __syncwarp();
+      }
     }
-    if (lane == 0) umma_commit(&accum_full);
-    __syncwarp();
-  } else {
+  } else if (warp < 2 + kProducers) {
     // Weight producers: warps 2..9 dequantize BN / 16 row groups a stage, the
-    // codes of the next two stages already in flight.
+    // codes of the next two stages already in flight; the stages run on
+    // across tiles (flat index q over this CTA's tiles x k-slices).
     const int pw = warp - 2;
     constexpr int kRgs = BN / 16;
     constexpr int kMine = kRgs / kProducers;       // row groups a warp, a stage
     static_assert(kRgs % kProducers == 0, "row groups split evenly over the producers");
-    auto rg_of = [&](int j) {
+    const uint32_t my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const uint32_t total = my_tiles * nkt;
+    auto rg_of = [&](uint32_t q, int j) {
+      const uint32_t n0 = n0_of(blockIdx.x + (q / nkt) * gridDim.x);
       const int r = pw + j * kProducers;
       return EPI == kGemmGated ? (n0 / 16 + (uint32_t)(r % (kRgs / 2))) : (n0 / 16 + (uint32_t)r);
     };
@@ -315,93 +357,104 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       const int r = pw + j * kProducers;
       return (EPI == kGemmGated && r >= kRgs / 2) ? a.w[1] : a.w[0];
     };
+    auto load_q = [&](uint32_t q, Codes (&dst)[kMine]) {
+#pragma unroll
+      for (int j = 0; j < kMine; j++) {
+        const uint32_t rg = rg_of(q, j);
+        dst[j] = load_codes(mat_of(j), rg, q % nkt, rg < mat_of(j).n / 16, lane);
+      }
+    };
     Codes A[kMine], B[kMine], C[kMine];
     bool stop = false;
-    // One stage: stage kt's codes are in `cur`; stage kt + 2's load into `later`.
-    auto step = [&](uint32_t kt, Codes (&cur)[kMine], Codes (&later)[kMine]) {
-      const int s = (int)(kt % S);
-      const uint32_t round = kt / S;
-      if (kt + 2 < nkt)
-#pragma unroll
-        for (int j = 0; j < kMine; j++)
-          later[j] = load_codes(mat_of(j), rg_of(j), kt + 2, rg_of(j) < mat_of(j).n / 16, lane);
+    // One stage: stage q's codes are in `cur`; stage q + 2's load into `later`.
+    auto step = [&](uint32_t q, Codes (&cur)[kMine], Codes (&later)[kMine]) {
+      const int s = (int)(q % S);
+      const uint32_t round = q / S;
+      if (q + 2 < total) load_q(q + 2, later);
       if (!mbar_wait(&empty[s], (round + 1) & 1u, a.error, 3)) {
         stop = true;
         return;
       }
       unsigned char* tile = b_tile(s);
 #pragma unroll
-      for (int j = 0; j < kMine; j++)
+      for (int j = 0; j < kMine; j++) {
+        const uint32_t rg = rg_of(q, j);
         dequant_tile(tile, WP == 2 ? b_tile_lo(s) : nullptr, (uint32_t)(pw + j * kProducers) * 16, cur[j],
-                     rg_of(j) < mat_of(j).n / 16, lane);
+                     rg < mat_of(j).n / 16, lane);
+      }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(&full[s]);
     };
-#pragma unroll
-    for (int j = 0; j < kMine; j++) {
-      A[j] = load_codes(mat_of(j), rg_of(j), 0, rg_of(j) < mat_of(j).n / 16, lane);
-      if (nkt > 1) B[j] = load_codes(mat_of(j), rg_of(j), 1, rg_of(j) < mat_of(j).n / 16, lane);
+    if (total > 0) load_q(0, A);
+    if (total > 1) load_q(1, B);
+    for (uint32_t q = 0; q < total && !stop; q += 3) {
+      step(q, A, C);
+      if (q + 1 < total && !stop) step(q + 1, B, A);
+      if (q + 2 < total && !stop) step(q + 2, C, B);
     }
-    for (uint32_t kt = 0; kt < nkt && !stop; kt += 3) {
-      step(kt, A, C);
-      if (kt + 1 < nkt && !stop) step(kt + 1, B, A);
-      if (kt + 2 < nkt && !stop) step(kt + 2, C, B);
-    }
-    // Epilogue: all eight producer warps; warp w reads TMEM lanes 32 * (w % 4)
-    // .. + 31, warps 2..5 the first half of the columns, warps 6..9 the second.
-    {
-      const bool ok = mbar_wait(&accum_full, 0, a.error, 4);
+  } else {
+    // Epilogue: warps 10..17; warp w reads TMEM lanes 32 * (w % 4) .. + 31,
+    // warps 10..13 the first half of the columns, warps 14..17 the second.
+    const int ew = warp - 2 - kProducers;
+    const uint32_t quarter = (uint32_t)warp & 3u;
+    const int side = ew < 4 ? 0 : 1;
+    float* stage = epi_stage + ew * 32 * (kStageCols + 1);
+    uint32_t tl = 0;
+    for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, tl++) {
+      const uint32_t buf = tl & 1u, use = tl >> 1;
+      if (!mbar_wait(&acc_full[buf], use & 1u, a.error, 4)) break;
       fence_after_sync();
-      const uint32_t quarter = (uint32_t)warp & 3u;
-      const int side = warp < 6 ? 0 : 1;
+      const uint32_t m0 = m0_of(tile), n0 = n0_of(tile);
       const uint32_t row = m0 + quarter * 32 + lane;
-      const uint32_t lane_addr = tmem + ((quarter * 32u) << 16);
-      // The stages are idle once the accumulator is full: each epilogue warp
-      // turns its 32 rows x 32 columns around through shared memory, so every
-      // global store covers consecutive columns of one row.
-      float* stage = reinterpret_cast<float*>(smem) + (warp - 2) * 32 * 33;
-      if (ok) {
-        if (EPI == kGemmWrite) {
-          const uint32_t N = a.w[0].n;
-          for (int c0 = side * (BN / 2); c0 < (side + 1) * (BN / 2); c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(lane_addr + (uint32_t)c0, r);
+      const uint32_t lane_addr = tmem + buf * BN + ((quarter * 32u) << 16);
+      if (EPI == kGemmWrite) {
+        const uint32_t N = a.w[0].n;
+        for (int c0 = side * (BN / 2); c0 < (side + 1) * (BN / 2); c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(lane_addr + (uint32_t)c0, r);
 #pragma unroll
-            for (int i = 0; i < 32; i++) stage[lane * 33 + i] = __uint_as_float(r[i]);
+          for (int h = 0; h < 2; h++) {
+#pragma unroll
+            for (int i = 0; i < kStageCols; i++) stage[lane * (kStageCols + 1) + i] = __uint_as_float(r[h * kStageCols + i]);
             __syncwarp();
-            const uint32_t n = n0 + (uint32_t)c0 + lane;
-            for (int rr = 0; rr < 32; rr++) {
+            // 16 consecutive columns of two rows a store instruction.
+            const uint32_t n = n0 + (uint32_t)c0 + h * kStageCols + (lane & 15);
+            for (int rr = lane >> 4; rr < 32; rr += 2) {
               const uint32_t orow = m0 + quarter * 32 + rr;
-              if (orow < a.m && n < N) a.out[(size_t)orow * a.out_stride + n] = stage[rr * 33 + lane];
+              if (orow < a.m && n < N) a.out[(size_t)orow * a.out_stride + n] = stage[rr * (kStageCols + 1) + (lane & 15)];
             }
             __syncwarp();
           }
-        } else {
-          const uint32_t F = a.w[0].n;
-          const uint32_t seq = row / a.seq_tokens;
-          const uint32_t pos = (a.step ? a.step->position : a.position) + row % a.seq_tokens;
-          const bool last = row % a.seq_tokens == a.seq_tokens - 1;
-          for (int c0 = side * (int)(half_bn / 2); c0 < (side + 1) * (int)(half_bn / 2); c0 += 32) {
-            uint32_t gr[32], ur[32];
-            tmem_ld32(lane_addr + (uint32_t)c0, gr);
-            tmem_ld32(lane_addr + half_bn + (uint32_t)c0, ur);
+        }
+      } else {
+        const uint32_t F = a.w[0].n;
+        const uint32_t seq = row / a.seq_tokens;
+        const uint32_t pos = (a.step ? a.step->position : a.position) + row % a.seq_tokens;
+        const bool last = row % a.seq_tokens == a.seq_tokens - 1;
+        for (int c0 = side * (int)(half_bn / 2); c0 < (side + 1) * (int)(half_bn / 2); c0 += 32) {
+          uint32_t gr[32], ur[32];
+          tmem_ld32(lane_addr + (uint32_t)c0, gr);
+          tmem_ld32(lane_addr + half_bn + (uint32_t)c0, ur);
 #pragma unroll
-            for (int i = 0; i < 32; i++) {
-              const uint32_t neuron = n0 + c0 + i;
-              float v = __fmul_rn(gelu_tanh(__uint_as_float(gr[i])), __uint_as_float(ur[i]));
+          for (int h = 0; h < 2; h++) {
+#pragma unroll
+            for (int i = 0; i < kStageCols; i++) {
+              const uint32_t neuron = n0 + c0 + h * kStageCols + i;
+              float v = __fmul_rn(gelu_tanh(__uint_as_float(gr[h * kStageCols + i])),
+                                  __uint_as_float(ur[h * kStageCols + i]));
               if (a.edit_table && row < a.m && neuron < F)
                 v = apply_edit_table(a.edit_table + seq * a.table_stride, a.layer, neuron, pos, v);
               if (a.capture_neurons && last && row < a.m && neuron < F)
                 a.capture_neurons[seq * a.capture_stride + neuron] = v;
-              stage[lane * 33 + i] = v;
+              stage[lane * (kStageCols + 1) + i] = v;
             }
             __syncwarp();
-            const uint32_t n = n0 + (uint32_t)c0 + lane;
-            for (int rr = 0; rr < 32; rr++) {
+            const uint32_t n = n0 + (uint32_t)c0 + h * kStageCols + (lane & 15);
+            for (int rr = lane >> 4; rr < 32; rr += 2) {
               const uint32_t orow = m0 + quarter * 32 + rr;
               if (orow < a.m && n < F) {
-                const float v = stage[rr * 33 + lane];
+                const float v = stage[rr * (kStageCols + 1) + (lane & 15)];
                 const size_t at = (size_t)orow * F + n;
                 if (a.out) a.out[(size_t)orow * a.out_stride + n] = v;
                 const __half hi = __float2half_rn(v);
@@ -413,6 +466,10 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           }
         }
       }
+      // This accumulator may take the tile after next.
+      fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   pdl_launch_dependents();
@@ -420,7 +477,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   __syncthreads();
   if (warp == 0) {
     fence_after_sync();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN)) : "memory");
   }
 }
 
@@ -475,8 +532,16 @@ cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
   if (!make_map(&map_hi, a.x_hi, a.m, a.w[0].k)) return cudaErrorInvalidValue;
   if (!make_map(&map_lo, PASSES == 2 ? a.x_lo : a.x_hi, a.m, a.w[0].k)) return cudaErrorInvalidValue;
   const uint32_t cols = EPI == kGemmGated ? BN / 2 : BN;
+  const uint32_t tiles = ((a.w[0].n + cols - 1) / cols) * ((a.m + kBM - 1) / kBM);
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.w[0].n + cols - 1) / cols, (a.m + kBM - 1) / kBM);
+  cfg.gridDim = dim3(std::min<uint32_t>(tiles, (uint32_t)sms));
   cfg.blockDim = dim3(kThreadsG);
   cfg.dynamicSmemBytes = L::kSmem;
   cfg.stream = stream;
