@@ -34,6 +34,7 @@ PROMPT = 32
 HEAD_N, HEAD_K = 262144, 1152
 LAUNCHES_PER_DECODE_STEP = 5   # embed, the persistent decode step (26 layers), head, select x2
 DECODE_BYTES = 562_360_320 + 537_088           # Q4_0 weights + F32 gains a decode token reads
+LAYER_BYTES = 392_491_008 + 532_480            # the 26 layers' Q4_0 weights + their norm gains (no head)
 
 
 def peaks():
@@ -281,8 +282,8 @@ def run_ours(args):
     ids = np.random.default_rng([rank, PROMPT]).integers(2, synth.GEMMA3_1B.vocab, size=PROMPT).astype(np.uint32)
 
     def prefill():
-        for pos in range(0, PROMPT, 16):
-            batch.step(pos, ids[pos:pos + 16], tokens=16, logits=pos + 16 == PROMPT)
+        # The 32-token prompt in one step (more than 16 rows: the tensor-core path).
+        batch.step(0, ids, tokens=PROMPT, logits=True)
 
     # Prefill timing (two blocks of 16 tokens), after a warm-up prefill.
     prefill()
@@ -341,6 +342,26 @@ def run_ours(args):
         pos += K
     dec_s = ev[2].elapsed_time(ev[3]) / 1000.0
     e2e_s = ev[4].elapsed_time(ev[5]) / 1000.0
+    # The persistent decode kernel's own duration, from its device timestamps (first phase start
+    # to last phase end, fz_batch_trace), over a few traced steps after the timed region.
+    decode_kernel_us = None
+    if rank == 0:
+        import ctypes as C
+        engine.check(lib.fz_batch_trace(batch.handle, 1))
+        ctas, events = C.c_uint32(), C.c_uint32()
+        engine.check(lib.fz_batch_read_trace(batch.handle, None, 0, C.byref(ctas), C.byref(events)))
+        spans = []
+        for i in range(4):
+            batch.step(pos + i, fed=True, tokens=1, logits=True)
+            batch.wait()
+            buf = np.zeros(ctas.value * events.value, dtype=np.uint64)
+            engine.check(lib.fz_batch_read_trace(batch.handle, buf.ctypes.data, buf.size, None, None))
+            body = buf.reshape(ctas.value, events.value)[:, :synth.GEMMA3_1B.layers * 6 * 5].astype(np.float64)
+            body[body == 0] = np.nan
+            spans.append((np.nanmax(body) - np.nanmin(body)) / 1000.0)
+        engine.check(lib.fz_batch_trace(batch.handle, 0))
+        pos += 4
+        decode_kernel_us = float(np.median(spans[1:]))
     sweep_line = None
     if not args.no_sweep:
         # 64 steered/unsteered pairs over one 256-token prompt, 128 sampled tokens each
@@ -404,6 +425,13 @@ def run_ours(args):
                              "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                              "peak_source": which, "algorithmic_bytes": head_bytes,
                              "launch_us": head_secs * 1e6, "traffic": traffic_from_profile()},
+                "decode_kernel": {
+                    "kernel": "persistent decode step (26 layers), the step's dominant launch by time",
+                    "us": decode_kernel_us, "algorithmic_bytes": LAYER_BYTES,
+                    "achieved_gbs": LAYER_BYTES / (decode_kernel_us * 1e-6) / 1e9 if decode_kernel_us else None,
+                    "frac": LAYER_BYTES / (decode_kernel_us * 1e-6) / 1e9 / hbm if decode_kernel_us else None,
+                    "bound": "hbm (latency-bound in practice: 130 dependent phases)",
+                    "timing": "device global timer inside the kernel (fz_batch_trace), median of 3 steps"},
                 "clocks": clocks.summary()}
         if sweep_line:
             line["steering_sweep"] = sweep_line
@@ -461,6 +489,9 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-4 steering sweep")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="run one config-3 4096-token prefill step between cudaProfilerStart/Stop (after a warm-up one)")
+    ap.add_argument("--seqs", type=int, default=1, help="sequences a batch in --trace")
     ap.add_argument("--trace", action="store_true",
                     help="print the decode kernel's phase timeline (device timestamps), averaged over steps")
     args = ap.parse_args()
@@ -480,6 +511,26 @@ def main():
         return 0
     if args.trace:
         return run_trace(args)
+    if args.profile_prefill:
+        import numpy as np
+        import torch
+        from frizzle_b200 import engine, synth
+        dev = engine.Device(0)
+        model = engine.Model.from_file(dev, synth.model_path(synth.GEMMA3_1B, 0))
+        b = engine.Batch(model, 1, 8192)
+        ids = np.random.default_rng([0, 4096]).integers(2, synth.GEMMA3_1B.vocab, size=4096).astype(np.uint32)
+        b.step(0, ids, tokens=4096, logits=True)
+        b.wait()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        b.step(0, ids, tokens=4096, logits=True)
+        b.wait()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        b.free()
+        model.free()
+        dev.close()
+        return 0
     return run_ours(args)
 
 
@@ -496,10 +547,10 @@ def run_trace(args):
     from frizzle_b200 import engine, synth
     dev = engine.Device(0)
     model = engine.Model.from_file(dev, synth.model_path(synth.GEMMA3_1B, 0))
-    batch = engine.Batch(model, 1, 4096)
+    S = args.seqs
+    batch = engine.Batch(model, S, 4096)
     ids = np.random.default_rng([0, PROMPT]).integers(2, synth.GEMMA3_1B.vocab, size=PROMPT).astype(np.uint32)
-    for pos in range(0, PROMPT, 16):
-        batch.step(pos, ids[pos:pos + 16], tokens=16, logits=pos + 16 == PROMPT)
+    batch.step(0, np.tile(ids, (S, 1)), tokens=PROMPT, logits=True)
     batch.wait()
     lib = batch.lib
     engine.check(lib.fz_batch_trace(batch.handle, 1))
