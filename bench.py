@@ -362,6 +362,48 @@ def run_ours(args):
         engine.check(lib.fz_batch_trace(batch.handle, 0))
         pos += 4
         decode_kernel_us = float(np.median(spans[1:]))
+    long_line = None
+    if not args.no_long:
+        # 8 sequences, each a seeded prompt prefilled into the KV cache, then 256 greedy
+        # decode steps; sequences sharded across the ranks.  The prompt is 32,512 tokens so that the last
+        # step's position is the model's 32,768-token trained context.
+        from frizzle_b200 import sweep as _sw
+        n_seq, p_len, l_steps, chunk = 8, 32768 - 256, 256, 4096
+        mine = list(_sw.shard(n_seq, world, rank))
+        lb = engine.Batch(model, len(mine), 32768) if mine else None
+        prompts = np.stack([np.random.default_rng([s, 32768]).integers(2, synth.GEMMA3_1B.vocab, size=p_len)
+                            for s in mine]).astype(np.uint32) if mine else None
+        if dist:
+            dist.barrier()
+        lv = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        with torch.cuda.stream(stream):
+            lv[0].record()
+        if lb:
+            for p0 in range(0, p_len, chunk):
+                t = min(chunk, p_len - p0)
+                lb.step(p0, np.ascontiguousarray(prompts[:, p0:p0 + t]), tokens=t, logits=p0 + t == p_len)
+        with torch.cuda.stream(stream):
+            lv[1].record()
+        if lb:
+            for i in range(l_steps - 1):
+                lb.step(p_len + i, fed=True, tokens=1, logits=True)
+            lb.wait()
+        with torch.cuda.stream(stream):
+            lv[2].record()
+        torch.cuda.synchronize()
+        l_pre, l_dec = lv[0].elapsed_time(lv[1]) / 1000.0, lv[1].elapsed_time(lv[2]) / 1000.0
+        if lb:
+            lb.free()
+        if dist:
+            t = torch.tensor([l_pre, l_dec], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            l_pre, l_dec = [float(v) for v in t.cpu()]
+        long_line = {"workload": "BASELINE config 5: 8 sequences x 32,512-token seeded prompt (prefilled in 4096-token "
+                                 "steps), then 256 greedy decode steps each (the last at the 32,768 trained context); "
+                                 "sequences sharded over the GPUs",
+                     "prefill_tokens_per_s": n_seq * p_len / l_pre, "prefill_s": l_pre,
+                     "decode_tokens_per_s": n_seq * (l_steps - 1) / l_dec, "decode_s": l_dec,
+                     "sequences_per_gpu": len(mine), "scaling": "strong"}
     sweep_line = None
     if not args.no_sweep:
         # 64 steered/unsteered pairs over one 256-token prompt, 128 sampled tokens each
@@ -435,6 +477,8 @@ def run_ours(args):
                 "clocks": clocks.summary()}
         if sweep_line:
             line["steering_sweep"] = sweep_line
+        if long_line:
+            line["long_context"] = long_line
         # a 4096-token prompt prefilled in one step (the tcgen05 path).
         pre = engine.Batch(model, 1, 8192)
         ids4k = np.random.default_rng([rank, 4096]).integers(2, synth.GEMMA3_1B.vocab, size=4096).astype(np.uint32)
@@ -489,9 +533,12 @@ def main():
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-4 steering sweep")
+    ap.add_argument("--no-long", action="store_true", help="skip the config-5 long-context run")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="run one config-3 4096-token prefill step between cudaProfilerStart/Stop (after a warm-up one)")
     ap.add_argument("--seqs", type=int, default=1, help="sequences a batch in --trace")
+    ap.add_argument("--trace-prompt", type=int, default=PROMPT,
+                    help="prompt tokens a sequence before the traced steps (prefilled in 4096-token steps)")
     ap.add_argument("--trace", action="store_true",
                     help="print the decode kernel's phase timeline (device timestamps), averaged over steps")
     args = ap.parse_args()
@@ -547,10 +594,13 @@ def run_trace(args):
     from frizzle_b200 import engine, synth
     dev = engine.Device(0)
     model = engine.Model.from_file(dev, synth.model_path(synth.GEMMA3_1B, 0))
-    S = args.seqs
-    batch = engine.Batch(model, S, 4096)
-    ids = np.random.default_rng([0, PROMPT]).integers(2, synth.GEMMA3_1B.vocab, size=PROMPT).astype(np.uint32)
-    batch.step(0, np.tile(ids, (S, 1)), tokens=PROMPT, logits=True)
+    S, P = args.seqs, args.trace_prompt
+    context = max(4096, P + args.warmup + args.steps + 1)
+    batch = engine.Batch(model, S, context)
+    ids = np.random.default_rng([0, P]).integers(2, synth.GEMMA3_1B.vocab, size=P).astype(np.uint32)
+    for p0 in range(0, P, 4096):
+        t = min(4096, P - p0)
+        batch.step(p0, np.ascontiguousarray(np.tile(ids[p0:p0 + t], (S, 1))), tokens=t, logits=p0 + t == P)
     batch.wait()
     lib = batch.lib
     engine.check(lib.fz_batch_trace(batch.handle, 1))
@@ -562,7 +612,7 @@ def run_trace(args):
                                "prologue_median", "compute_median", "finish_median")} for _ in range(6)]
     totals = []
     tails = []
-    pos, n = PROMPT, 0
+    pos, n = P, 0
     for i in range(args.warmup + args.steps):
         batch.step(pos, fed=True, tokens=1, logits=True)
         batch.wait()

@@ -47,7 +47,7 @@ constexpr int kDT = kCT + 32;           // + the producer warp
 constexpr uint32_t kSlotBp = 32;        // block pairs a ring slot holds
 constexpr uint32_t kSlotCodes = kSlotBp * 512, kSlotScales = kSlotBp * 64;
 constexpr uint32_t kHd = 256;           // head dimension
-constexpr uint32_t kKeysPerSplit = 512;
+constexpr uint32_t kMinSplitKeys = kDecodeSplitKeys;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint32_t kWaitIters = 1u << 30;
 constexpr int kNormVec = 3;             // vec4s of a row an invocation holds (hidden <= 3072)
@@ -616,7 +616,7 @@ __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const fl
 template <int GH>
 struct Attn {
   const DecodeArgs& a;
-  uint32_t M, pos, W;
+  uint32_t M, pos, W, kps;
   int tid, warp, lane;
   bool fail, dead;
 
@@ -686,8 +686,14 @@ struct Attn {
     const DecodeLayer& L = a.layers[l];
     const uint32_t G = gridDim.x;
     const uint32_t earliest = pos + 1 > L.window ? pos + 1 - L.window : 0;
-    const uint32_t nkeys = pos + 1 - earliest, nsplit = (nkeys + kKeysPerSplit - 1) / kKeysPerSplit;
-    const uint32_t KV = a.kv_heads, items = M * KV * nsplit;
+    const uint32_t KV = a.kv_heads, nkeys = pos + 1 - earliest;
+    // Splits of whole chunks, at least kMinSplitKeys keys each, as many as
+    // give every (row, KV head) its share of the CTAs (at most max_splits).
+    const uint32_t share = max(1u, G / (M * KV));
+    kps = max(kMinSplitKeys, (nkeys + share - 1) / share);
+    if ((nkeys + kps - 1) / kps > a.max_splits) kps = (nkeys + a.max_splits - 1) / a.max_splits;
+    kps = (kps + C - 1) / C * C;
+    const uint32_t nsplit = (nkeys + kps - 1) / kps, items = M * KV * nsplit;
     uint32_t item = G - 1 - blockIdx.x;
     if (item >= items) return;
     // Before waiting for this step's q, k, v: the first chunk of the first
@@ -701,7 +707,7 @@ struct Attn {
     }
     {
       const uint32_t row = item / (KV * nsplit), kvh = (item / nsplit) % KV, split = item % nsplit;
-      const uint32_t j0 = earliest + split * kKeysPerSplit, j1 = min(j0 + kKeysPerSplit, pos + 1);
+      const uint32_t j0 = earliest + split * kps, j1 = min(j0 + kps, pos + 1);
       stage_first(L, row, kvh, j0, j1);
     }
     stamp(l, 1, 0);
@@ -731,8 +737,8 @@ struct Attn {
   FZ_DEV void attend(const DecodeLayer& L, uint32_t l, uint32_t row, uint32_t kvh, uint32_t split, uint32_t nsplit,
                      uint32_t earliest, float4 ga, float4 gb, float4 tt, bool staged) {
     const uint32_t H = a.heads, KV = a.kv_heads;
-    const uint32_t j0 = earliest + split * kKeysPerSplit;
-    const uint32_t j1 = min(j0 + kKeysPerSplit, pos + 1);
+    const uint32_t j0 = earliest + split * kps;
+    const uint32_t j1 = min(j0 + kps, pos + 1);
     const bool last = j1 == pos + 1;
     if (!staged) stage_first(L, row, kvh, j0, j1);
     // QK-norm and RoPE: warps 0..GH-1 the queries, warp GH the key, GH+1 the value.
@@ -904,7 +910,6 @@ struct Attn {
       a.partial_ml[at * 2] = hstat()[tid];
       a.partial_ml[at * 2 + 1] = hstat()[GH + tid];
     }
-    const uint32_t dim = (uint32_t)tid;
     bool final_cta = nsplit == 1;
     if (!final_cta) {
       cbar();
@@ -916,21 +921,7 @@ struct Attn {
       final_cta = flags()[1] != 0;
       if (final_cta) {
         __threadfence();
-#pragma unroll
-        for (int h = 0; h < GH; h++) {
-          const uint32_t head = kvh * GH + h;
-          const size_t base = ((size_t)row * H + head) * a.max_splits;
-          float mm = -INFINITY;
-          for (uint32_t s = 0; s < nsplit; s++) mm = fmaxf(mm, __ldcg(a.partial_ml + (base + s) * 2));
-          float lsum = 0.f, acc_o = 0.f;
-          for (uint32_t s = 0; s < nsplit; s++) {
-            const float ms = __ldcg(a.partial_ml + (base + s) * 2);
-            const float f = ms == mm ? 1.0f : exp2f(ms - mm);
-            lsum = __fmaf_rn(__ldcg(a.partial_ml + (base + s) * 2 + 1), f, lsum);
-            acc_o = __fmaf_rn(__ldcg(a.partial_o + (base + s) * kHd + dim), f, acc_o);
-          }
-          a.attn[((size_t)row * H + head) * kHd + dim] = __fdiv_rn(acc_o, lsum);
-        }
+        combine(row, kvh, nsplit);
       }
     }
     if (final_cta) {
@@ -938,6 +929,64 @@ struct Attn {
       if (tid == 0) raise_counter(sync_of(l) + kSyncAttn);
     }
     sync_dead();
+  }
+
+  // The last split of (row, kvh) to finish folds all of them (the key
+  // buffer, drained by now, holds the weights): warp h < GH takes head h's
+  // maxima and sums (lanes stride the splits, then a fixed-order shuffle
+  // tree), then each thread one head's four dimensions, its split loads in
+  // flight together.
+  FZ_DEV void combine(uint32_t row, uint32_t kvh, uint32_t nsplit) {
+    const uint32_t H = a.heads;
+    float* fac = reinterpret_cast<float*>(ks());   // [GH][nsplit] weights, then [GH] sums
+    float* lsum = fac + GH * nsplit;
+    if (warp < GH) {
+      const size_t base = ((size_t)row * H + kvh * GH + warp) * a.max_splits;
+      float mm = -INFINITY;
+      for (uint32_t s = lane; s < nsplit; s += 32) mm = fmaxf(mm, __ldcg(a.partial_ml + (base + s) * 2));
+      mm = warp_max(mm);
+      float ls = 0.f;
+      for (uint32_t s = lane; s < nsplit; s += 32) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.partial_ml + (base + s) * 2));
+        const float f = ml.x == mm ? 1.0f : exp2f(ml.x - mm);
+        fac[warp * nsplit + s] = f;
+        ls = __fmaf_rn(ml.y, f, ls);
+      }
+      ls = warp_sum(ls);
+      if (lane == 0) lsum[warp] = ls;
+    }
+    cbar();
+#pragma unroll 1
+    for (int i = tid; i < GH * (int)(kHd / 4); i += kCT) {
+      const int h = i / (kHd / 4), d4 = i % (kHd / 4);
+      const size_t base = ((size_t)row * H + kvh * GH + h) * a.max_splits;
+      const float4* po = reinterpret_cast<const float4*>(a.partial_o + base * kHd) + d4;
+      const float* fh = fac + h * nsplit;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      uint32_t s = 0;
+#pragma unroll 1
+      for (; s + 4 <= nsplit; s += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) v[u] = __ldcg(po + (size_t)(s + u) * (kHd / 4));
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const float f = fh[s + u];
+          acc = make_float4(__fmaf_rn(v[u].x, f, acc.x), __fmaf_rn(v[u].y, f, acc.y), __fmaf_rn(v[u].z, f, acc.z),
+                            __fmaf_rn(v[u].w, f, acc.w));
+        }
+      }
+#pragma unroll 1
+      for (; s < nsplit; s++) {
+        const float4 v = __ldcg(po + (size_t)s * (kHd / 4));
+        const float f = fh[s];
+        acc = make_float4(__fmaf_rn(v.x, f, acc.x), __fmaf_rn(v.y, f, acc.y), __fmaf_rn(v.z, f, acc.z),
+                          __fmaf_rn(v.w, f, acc.w));
+      }
+      const float ls = lsum[h];
+      reinterpret_cast<float4*>(a.attn + ((size_t)row * H + kvh * GH + h) * kHd)[d4] =
+          make_float4(__fdiv_rn(acc.x, ls), __fdiv_rn(acc.y, ls), __fdiv_rn(acc.z, ls), __fdiv_rn(acc.w, ls));
+    }
   }
 };
 

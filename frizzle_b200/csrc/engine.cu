@@ -388,14 +388,19 @@ fz_status alloc_rows(fz_batch& b, uint32_t rows) {
     }
   const uint32_t Q = s.heads * s.head_dim, KV = s.kv_heads * s.head_dim;
   const size_t M = rows, X = std::max(s.hidden, Q);
+  // Attention split partials serve steps of at most 16 rows (and the decode
+  // kernel's); wider steps use the tensor-core attention, which needs none.
+  const size_t PM = fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)
+                        ? std::min<size_t>(rows, (size_t)fz::kMaxTokens)
+                        : M;
   b.counters_per_layer = 1 + rows * s.kv_heads;
   fz_status st;
   if ((st = b.alloc_row(&b.hidden_a, M * s.hidden * 4)) || (st = b.alloc_row(&b.hidden_b, M * s.hidden * 4)) ||
       (st = b.alloc_row(&b.qkv, M * (Q + 2 * KV) * 4)) || (st = b.alloc_row(&b.q, M * Q * 4)) ||
       (st = b.alloc_row(&b.attn, M * Q * 4)) || (st = b.alloc_row(&b.y_attn, M * s.hidden * 4)) ||
       (st = b.alloc_row(&b.y_mlp, M * s.hidden * 4)) || (st = b.alloc_row(&b.act, M * s.ffn * 4)) ||
-      (st = b.alloc_row(&b.partial_o, M * s.heads * b.splits_max * s.head_dim * 4)) ||
-      (st = b.alloc_row(&b.partial_ml, M * s.heads * b.splits_max * 2 * 4)) ||
+      (st = b.alloc_row(&b.partial_o, PM * s.heads * b.splits_max * s.head_dim * 4)) ||
+      (st = b.alloc_row(&b.partial_ml, PM * s.heads * b.splits_max * 2 * 4)) ||
       (st = b.alloc_row(&b.counters, (size_t)s.layers * b.counters_per_layer * 4)) ||
       (st = b.alloc_row(&b.dids, M * 4)) || (st = b.alloc_row(&b.x16_hi, M * X * 2)) ||
       (st = b.alloc_row(&b.x16_lo, M * X * 2)) || (st = b.alloc_row(&b.act16_hi, M * s.ffn * 2)) ||
@@ -415,12 +420,6 @@ fz_status alloc_rows(fz_batch& b, uint32_t rows) {
 
 // The persistent decode kernel serves one-token steps unless
 // FRIZZLE_B200_LAYERED=1 asks for the per-operation launches.
-// Wide steps use the tensor-core attention unless FRIZZLE_B200_SCALAR_ATTENTION=1.
-bool prefill_attention_enabled() {
-  const char* v = std::getenv("FRIZZLE_B200_SCALAR_ATTENTION");
-  return !(v && *v && *v != '0');
-}
-
 bool decode_step_enabled() {
   const char* v = std::getenv("FRIZZLE_B200_LAYERED");
   return !(v && *v && *v != '0');
@@ -618,7 +617,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       at.out = b.attn;
       at.out_hi = b.x16_hi;
       at.out_lo = xlo;
-      if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim) && prefill_attention_enabled())
+      if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim))
         FZ_CUDA(fz::launch_attention_prefill(at, st, pdl));
       else
         FZ_CUDA(fz::launch_attention(at, st, pdl));
@@ -1017,7 +1016,12 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     b->vc.push_back(v);
     b->slots.push_back(slots);
     b->seq_stride.push_back(per_seq);
-    b->splits_max = std::max<uint32_t>(b->splits_max, (std::min(L.window, context) + kSplitKeys - 1) / kSplitKeys);
+    // The per-op attention splits its keys kSplitKeys at a time; the decode
+    // kernel into up to one split a CTA (kDecodeSplitKeys keys at least).
+    const uint32_t keys = std::min(L.window, context);
+    b->splits_max = std::max<uint32_t>({b->splits_max, (keys + kSplitKeys - 1) / kSplitKeys,
+                                        std::min<uint32_t>((keys + fz::kDecodeSplitKeys - 1) / fz::kDecodeSplitKeys,
+                                                           fz::kDecodeMaxSplits)});
   }
   {
     std::vector<fz::DecodeLayer> dl(s.layers);

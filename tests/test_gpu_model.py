@@ -182,9 +182,10 @@ def test_gemma_1b_256_token_prefill(gemma_model_path):
     assert_parity(run_both(gemma_model_path, synth.GEMMA3_1B, 256, 8, block=256))
 
 
-def run_batch(path, shape, S, n_prompt, steps, edit_sets=None, context=4096):
+def run_batch(path, shape, S, n_prompt, steps, edit_sets=None, context=4096, block=None):
     """S sequences stepped together (one decode launch serves them all), each
-    against its own oracle run; prompts differ per sequence."""
+    against its own oracle run; prompts differ per sequence.  The prompt goes in
+    steps of `block` tokens a sequence (default: 16 rows a step)."""
     dev = engine.Device(0)
     model = engine.Model.from_file(dev, path)
     batch = engine.Batch(model, S, context)
@@ -195,7 +196,7 @@ def run_batch(path, shape, S, n_prompt, steps, edit_sets=None, context=4096):
         w = np.array(table(es, shape.layers, n_prompt - 1), dtype=np.uint32) if es else None
         batch.set_edits(s, w)
         words.append(w)
-    block = max(1, 16 // S)
+    block = block or max(1, 16 // S)
     pos = 0
     while pos < n_prompt:
         t = min(block, n_prompt - pos)
@@ -225,6 +226,17 @@ def run_batch(path, shape, S, n_prompt, steps, edit_sets=None, context=4096):
         orc.close()
     assert worst_rms < REL_RMS, worst_rms
     assert worst_abs < MAX_ABS, worst_abs
+
+
+@pytest.mark.parametrize("S", [2, 8])
+def test_tiny_model_chunked_wide_prefill(tiny_model_path, S):
+    # Config 5 in small: S sequences whose 700-token prompts go in 256-token
+    # steps (GEMM and tensor-core attention reading the keys of earlier steps
+    # from the cache, the window layers sliding), then batched decode whose
+    # global layers split 700+ keys over many CTAs and fold the splits.
+    s = synth.TINY
+    edits = [[Edit(3, 5, SET, 8.0, 0)]] + [None] * (S - 1)
+    run_batch(tiny_model_path, s, S, 700, 6, edit_sets=edits, block=256)
 
 
 @pytest.mark.parametrize("S", [3, 6])

@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 
 def test_tiny_sweep_matches_oracle(tiny_model_path):
     s = synth.TINY
-    pairs = sweep.make_pairs(3, s.ffn, seed=5)
+    pairs = sweep.make_pairs(5, s.ffn, seed=5)   # 10 sequences: groups of 4, 4 (batch reused) and 2
     prompt = np.random.default_rng([5, 20]).integers(2, s.vocab, size=20).astype(np.uint32)
     steps, layer = 5, 3
     dev = engine.Device(0)
