@@ -30,6 +30,9 @@
 // the step; other CTAs see the error word in their own waits.  Consumer
 // barriers that follow a possible give-up are barrier reductions, so all
 // consumer warps leave together; copies in flight land before the CTA exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
 #include <mutex>
 
@@ -64,6 +67,13 @@ template <int MQ>
 __host__ __device__ constexpr uint32_t ring_slots() {
   return MQ == 1 ? 8u : 5u;
 }
+// Attention key/value chunk buffers (as many as the shared region between
+// the products' views leaves room for).
+__host__ __device__ constexpr uint32_t kv_bufs(int MQ) { return MQ == 1 ? 2u : 3u; }
+// A chunk buffer: keys then values, each four 32-key x 64-dimension boxes of
+// 4 KB (rows of 128 bytes, 16-byte units swizzled by the row).
+constexpr uint32_t kKvBox = kAttnChunk * 128u;
+constexpr uint32_t kKvBuf = 8u * kKvBox;
 
 __host__ __device__ inline uint32_t slice_kb(uint32_t k, uint32_t D) { return 2u * ((k / 64u + D - 1u) / D); }
 
@@ -111,9 +121,12 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   m = (m + 15u) & ~15u;
   L.gains = m;
   m += 2u * hidden * 4u;
-  const uint32_t att = 8u * (kHd + 8u) * 2u + 2u * 2u * kAttnChunk * kHd * 2u + group * kAttnChunk * 4u +
-                       8u * (kAttnChunk + 8u) * 2u + 2u * group * 4u;
-  o = m > o + att ? m : o + att;
+  // Attention view: the split queries, then (1024-aligned, for the 128-byte
+  // swizzle) the chunk buffers, then scores, weights and head statistics.
+  L.kvbuf = (o + 8u * (kHd + 8u) * 2u + 1023u) & ~1023u;
+  const uint32_t att_end = L.kvbuf + kv_bufs(MQ) * kKvBuf + 2u * group * kAttnChunk * 4u +
+                           8u * (kAttnChunk + 8u) * 2u + 2u * group * 4u;
+  o = m > att_end ? m : att_end;
   o = (o + 15u) & ~15u;
   L.stat = o;
   o += 2u * kDecodeMaxRows * 4u;
@@ -128,6 +141,11 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   o += slots * 4u;
   L.uses = o;
   o += slots * 4u;
+  o = (o + 7u) & ~7u;
+  L.kvbar = o;
+  o += 4u * 8u;
+  L.kvstate = o;
+  o += 2u * 4u;
   L.total = o;
   return L;
 }
@@ -138,7 +156,7 @@ __host__ __device__ inline bool layout_aligned(const DLayout& L) {
   return L.codes % 128 == 0 && L.scales % 128 == 0 && L.full % 8 == 0 && L.empty % 8 == 0 && L.uni % 128 == 0 &&
          L.xf % 16 == 0 && L.rowbuf % 16 == 0 && L.part % 16 == 0 && L.stat % 16 == 0 && L.red % 16 == 0 &&
          L.task_rg % 4 == 0 && L.best % 8 == 0 && L.flags % 4 == 0 && L.gains % 16 == 0 && L.tags % 4 == 0 &&
-         L.uses % 4 == 0;
+         L.uses % 4 == 0 && L.kvbar % 8 == 0 && L.kvstate % 4 == 0 && L.kvbuf % 1024 == 0;
 }
 
 // ------------------------------------------------------------ primitives
@@ -210,6 +228,9 @@ FZ_DEV void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
 }
 FZ_DEV void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory accesses before later
+// bulk copies into the same bytes.
+FZ_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Consumer-warp barriers (named barrier 1; the producer warp never joins).
 FZ_DEV void cbar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
@@ -613,12 +634,16 @@ __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const fl
 // The step's attention for one layer: the CTAs with work items wait for the
 // layer's QKV counter.  Run in a function of its own (attention_layer), so
 // its registers do not add to the products'.
-template <int GH>
+template <int GH, int NB>
 struct Attn {
   const DecodeArgs& a;
   uint32_t M, pos, W, kps;
+  uint32_t kvp, kvf;   // per chunk buffer: bit b the parity its next completion has, bit b a copy in flight
+  const unsigned char* kmap;  // the layer's key cache tensor map (the value map follows)
+  unsigned long long wait_ns; // traced: thread 0's time waiting for chunks
+  uint32_t slots, row;
   int tid, warp, lane;
-  bool fail, dead;
+  bool fail, dead, wrote;    // wrote: generic stores into a chunk buffer since its last refill
 
   FZ_DEV volatile uint32_t* flags() const { return reinterpret_cast<volatile uint32_t*>(g_smem + a.lay.flags); }
   FZ_DEV uint32_t* sync_of(uint32_t l) { return a.sync + (size_t)l * W; }
@@ -634,59 +659,102 @@ struct Attn {
 
   // ---------------------------------------------------------- attention
   //
-  // Keys are taken C at a time: their K and V rows are copied into shared
-  // memory (cp.async, 16 bytes a copy; the 16-byte pieces of a row
-  // XOR-swizzled by the row, so that eight rows read together hit all
-  // banks).  Both contractions run on the tensor cores (mma.m16n8k16, f16 in,
-  // f32 accumulate): scores = Q K^T with the queries split into f16 parts
-  // and remainders (rows 0..GH-1 and GH..2GH-1 of A), so each product is
-  // exact; warp h keeps head h's online softmax; out = P V with the weights
-  // split the same way, V's fragments loaded by ldmatrix.trans.
+  // Keys are taken C at a time, in chunks aligned to multiples of C in the
+  // sequence: a chunk's keys and values arrive by eight TMA tensor copies
+  // (32 keys x 64 dimensions each, 128-byte swizzle) completing on the chunk
+  // buffer's mbarrier, NB buffers in flight.  Both contractions run on the
+  // tensor cores (mma.m16n8k16, f16 in, f32 accumulate): scores = Q K^T with
+  // the queries split into f16 parts and remainders (rows 0..GH-1 and
+  // GH..2GH-1 of A), so each product is exact; warp h keeps head h's online
+  // softmax; out = P V with the weights split the same way, K's fragments
+  // loaded by ldmatrix and V's by ldmatrix.trans.
 
-  static constexpr int C = kAttnChunk;    // keys a chunk (two chunk buffers)
-
+  static constexpr int C = kAttnChunk;    // keys a chunk
   static constexpr int QS = kHd + 8;      // row stride (halves) of the split queries
   static constexpr int PS = C + 8;        // row stride (halves) of the split weights
   // Split rows: r < GH the f16 part of head r's query (or weights), GH <= r <
   // 2 GH the f16 remainder of head r - GH's, the rest zero (the mma's A rows).
   FZ_DEV uint16_t* qh() const { return reinterpret_cast<uint16_t*>(g_smem + a.lay.uni); }  // [8][QS]
-  FZ_DEV uint16_t* ks() const { return qh() + 8 * QS; }                                      // [2C][256] swizzled
-  FZ_DEV uint16_t* vs() const { return ks() + 2 * C * kHd; }                                 // [2C][256] swizzled
-  FZ_DEV float* sc() const { return reinterpret_cast<float*>(vs() + 2 * C * kHd); }         // [GH][C] scores
-  FZ_DEV uint16_t* ph() const { return reinterpret_cast<uint16_t*>(sc() + GH * C); }        // [8][PS] weights
+  FZ_DEV unsigned char* ks(uint32_t b) const { return g_smem + a.lay.kvbuf + b * kKvBuf; }  // 4 boxes
+  FZ_DEV unsigned char* vs(uint32_t b) const { return ks(b) + 4 * kKvBox; }                 // 4 boxes
+  FZ_DEV float* sc() const { return reinterpret_cast<float*>(ks(NB)); }                     // [2][GH][C] scores
+  FZ_DEV uint16_t* ph() const { return reinterpret_cast<uint16_t*>(sc() + 2 * GH * C); }    // [8][PS] weights
   FZ_DEV float* hstat() const { return reinterpret_cast<float*>(ph() + 8 * PS); }           // [GH] corr or m, [GH] l
-
-  // Copies keys [jc, jc + n) of (row, kvh) into chunk buffer `buf` (one
-  // cp.async group).
-  FZ_DEV void stage(const DecodeLayer& L, uint32_t row, uint32_t kvh, uint32_t jc, uint32_t n, uint32_t buf) {
-    const uint16_t* kc = L.key_cache + row * L.seq_stride;
-    const uint16_t* vc = L.value_cache + row * L.seq_stride;
-    const uint32_t KV = a.kv_heads, r0 = buf * C;
-#pragma unroll 1
-    for (uint32_t i = tid; i < n * 64; i += kCT) {
-      const bool isv = i >= n * 32;
-      const uint32_t ii = isv ? i - n * 32 : i, r = ii / 32, c = ii % 32;
-      const size_t at = ((size_t)((jc + r) % L.slots) * KV + kvh) * kHd + c * 8;
-      cp_async16((isv ? vs() : ks()) + (r0 + r) * kHd + ((c ^ (r & 7u)) * 8), (isv ? vc : kc) + at);
-    }
-    // A short chunk's missing value rows are zero (their weights are zero, and
-    // 0 x NaN would not be).
-#pragma unroll 1
-    for (uint32_t i = tid; i < (C - n) * 32; i += kCT)
-      *reinterpret_cast<uint4*>(vs() + (r0 + n + i / 32) * kHd + (i % 32) * 8) = make_uint4(0, 0, 0, 0);
-    asm volatile("cp.async.commit_group;" ::: "memory");
+  // Byte offset of (key r, dimensions d .. d + 7) in a K or V half-buffer:
+  // box d / 64, row r of 128 bytes, 16-byte unit (d / 8) % 8 XOR r % 8.
+  FZ_DEV static uint32_t at(uint32_t r, uint32_t d) {
+    return (d >> 6) * kKvBox + r * 128u + ((((d >> 3) & 7u) ^ (r & 7u)) << 4);
   }
-  // The split's first two chunks.
-  FZ_DEV void stage_first(const DecodeLayer& L, uint32_t row, uint32_t kvh, uint32_t j0, uint32_t j1) {
-    stage(L, row, kvh, j0, min((uint32_t)C, j1 - j0), 0);
-    if (j0 + C < j1) stage(L, row, kvh, j0 + C, min((uint32_t)C, j1 - j0 - C), 1);
+
+  FZ_DEV uint64_t* kvbar() const { return reinterpret_cast<uint64_t*>(g_smem + a.lay.kvbar); }
+
+  // Copies the chunk of C keys from jc (a multiple of C) of (row, kvh) into
+  // chunk buffer b: lanes 0..7 of warp 0 issue one tensor copy a box (four
+  // of keys, four of values), completing on the buffer's mbarrier.  Every
+  // consumer thread calls it (the buffer state stays uniform), after a
+  // barrier that follows their last generic access to the buffer and their
+  // proxy fence.  The slots of a chunk never wrap (the ring holds whole
+  // chunks); slots past a cache shorter than a chunk read as zeros.
+  FZ_DEV void stage(uint32_t kvh, uint32_t jc, uint32_t b) {
+    if (warp == 0) {
+      if (lane == 0) mb_expect_tx(kvbar() + b, kKvBuf);
+      __syncwarp();
+      if (lane < 8) {
+        const uint32_t q = lane & 3u;
+        unsigned char* dst = (lane < 4 ? ks(b) : vs(b)) + q * kKvBox;
+        const unsigned char* map = kmap + (lane < 4 ? 0 : 128);
+        asm volatile(
+            "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+            "%5}], [%6];" ::"r"(su32(dst)),
+            "l"(map), "r"(64u * q), "r"(kvh), "r"(jc % slots), "r"(row), "r"(su32(kvbar() + b))
+            : "memory");
+      }
+    }
+    kvf |= 1u << b;
+  }
+  // The item's cache and its split's first NB chunks.
+  FZ_DEV void stage_first(uint32_t l, uint32_t item_row, uint32_t kvh, uint32_t j0, uint32_t j1) {
+    kmap = a.kv_maps[l].map[0];
+    slots = a.layers[l].slots;
+    row = item_row;
+#pragma unroll
+    for (uint32_t b = 0; b < (uint32_t)NB; b++)
+      if (j0 + b * C < j1) stage(kvh, j0 + b * C, b);
+  }
+  // Waits for chunk buffer b's copies (bounded).
+  FZ_DEV void wait_chunk(uint32_t b) {
+    const uint64_t t0 = a.trace && tid == 0 ? now_ns() : 0;
+    if (!fail && !mb_wait(kvbar() + b, (kvp >> b) & 1u, a.error, flags())) fail = true;
+    if (a.trace && tid == 0) wait_ns += now_ns() - t0;
+    if (!fail) {
+      kvp ^= 1u << b;
+      kvf &= ~(1u << b);
+    }
+  }
+  // After giving up: thread 0 waits (bounded) for the copies still in flight,
+  // so that none lands after the CTA has moved on.
+  FZ_DEV void drain() {
+    if (tid == 0) {
+#pragma unroll 1
+      for (uint32_t b = 0; b < (uint32_t)NB; b++)
+        if ((kvf >> b) & 1u) {
+          if (mb_wait(kvbar() + b, (kvp >> b) & 1u, nullptr, nullptr)) {
+            kvp ^= 1u << b;
+            kvf &= ~(1u << b);
+          } else {
+            atomicOr(a.error, kErrDrain);
+          }
+        }
+    }
   }
 
   FZ_DEV void run(uint32_t l) {
     const DecodeLayer& L = a.layers[l];
     const uint32_t G = gridDim.x;
     const uint32_t earliest = pos + 1 > L.window ? pos + 1 - L.window : 0;
-    const uint32_t KV = a.kv_heads, nkeys = pos + 1 - earliest;
+    // Keys from a0 (earliest rounded down to a chunk; the keys before
+    // earliest are masked).
+    const uint32_t KV = a.kv_heads, a0 = earliest / C * C, nkeys = pos + 1 - a0;
     // Splits of whole chunks, at least kMinSplitKeys keys each, as many as
     // give every (row, KV head) its share of the CTAs (at most max_splits).
     const uint32_t share = max(1u, G / (M * KV));
@@ -696,7 +764,10 @@ struct Attn {
     const uint32_t nsplit = (nkeys + kps - 1) / kps, items = M * KV * nsplit;
     uint32_t item = G - 1 - blockIdx.x;
     if (item >= items) return;
-    // Before waiting for this step's q, k, v: the first chunk of the first
+    // The region held the products' rows and fragments (generic stores).
+    fence_proxy_async();
+    cbar();
+    // Before waiting for this step's q, k, v: the first chunks of the first
     // item's cached keys and the layer's QK-norm gains and RoPE turns.
     float4 ga = make_float4(0.f, 0.f, 0.f, 0.f), gb = ga, tt = ga;
     if (warp <= GH) {
@@ -707,13 +778,13 @@ struct Attn {
     }
     {
       const uint32_t row = item / (KV * nsplit), kvh = (item / nsplit) % KV, split = item % nsplit;
-      const uint32_t j0 = earliest + split * kps, j1 = min(j0 + kps, pos + 1);
-      stage_first(L, row, kvh, j0, j1);
+      const uint32_t j0 = a0 + split * kps, j1 = min(j0 + kps, pos + 1);
+      stage_first(l, row, kvh, j0, j1);
     }
     stamp(l, 1, 0);
     if (tid == 0 && !wait_counter(sync_of(l) + kSyncQkv, active_ctas(L.qkv.n / 16, 1, G), a.error)) fail = true;
     if (sync_dead()) {
-      cp_async_wait();
+      drain();
       return;
     }
     stamp(l, 1, 1);
@@ -721,7 +792,7 @@ struct Attn {
 #pragma unroll 1
     for (; item < items; item += G) {
       const uint32_t row = item / (KV * nsplit), kvh = (item / nsplit) % KV, split = item % nsplit;
-      attend(L, l, row, kvh, split, nsplit, earliest, ga, gb, tt, staged);
+      attend(L, l, row, kvh, split, nsplit, earliest, ga, gb, tt, staged, item + G < items);
       staged = false;
       if (dead) return;
     }
@@ -735,12 +806,12 @@ struct Attn {
   // split order in the last CTA (attention.wgsl:403-438).  `staged`: the
   // first chunk's copies were issued before the wait.
   FZ_DEV void attend(const DecodeLayer& L, uint32_t l, uint32_t row, uint32_t kvh, uint32_t split, uint32_t nsplit,
-                     uint32_t earliest, float4 ga, float4 gb, float4 tt, bool staged) {
+                     uint32_t earliest, float4 ga, float4 gb, float4 tt, bool staged, bool more) {
     const uint32_t H = a.heads, KV = a.kv_heads;
-    const uint32_t j0 = earliest + split * kps;
+    const uint32_t j0 = earliest / C * C + split * kps;
     const uint32_t j1 = min(j0 + kps, pos + 1);
     const bool last = j1 == pos + 1;
-    if (!staged) stage_first(L, row, kvh, j0, j1);
+    if (!staged) stage_first(l, row, kvh, j0, j1);
     // QK-norm and RoPE: warps 0..GH-1 the queries, warp GH the key, GH+1 the value.
     float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
     if (warp < GH + 2) {
@@ -788,56 +859,68 @@ struct Attn {
     float acc[4][2];
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[i][0] = acc[i][1] = 0.f;
+    wrote = false;
 #pragma unroll 1
-    for (uint32_t jc = j0, ci = 0; jc < j1; jc += C, ci++) {
-      const uint32_t n = min((uint32_t)C, j1 - jc), rb = (ci & 1u) * C;
-      // Chunk ci's copies: the next chunk's may still be in flight.
-      if (jc + C < j1) asm volatile("cp.async.wait_group 1;" ::: "memory");
-      else asm volatile("cp.async.wait_group 0;" ::: "memory");
-      cbar();
+    for (uint32_t jc = j0, b = 0; jc < j1; jc += C, b = b + 1 == (uint32_t)NB ? 0u : b + 1) {
+      // Keys lo .. n - 1 of the chunk are the split's.
+      const uint32_t n = min((uint32_t)C, j1 - jc), lo = earliest > jc ? earliest - jc : 0u;
+      // Chunk's copies (the next chunks' may still be in flight).
+      wait_chunk(b);
       // The new position's key and value are not in the cache yet: from the rope warps.
       if (pos >= jc && pos < jc + n && (warp == GH || warp == GH + 1)) {
-        const uint32_t r = pos - jc, rr = rb + r;
-        const ushort4 pa = make_ushort4(f16_pack(va.x), f16_pack(va.y), f16_pack(va.z), f16_pack(va.w));
-        const ushort4 pb = make_ushort4(f16_pack(vb.x), f16_pack(vb.y), f16_pack(vb.z), f16_pack(vb.w));
-        // elements 4 lane .. 4 lane + 3 and 128 + 4 lane ..: pieces lane / 2 and 16 + lane / 2
-        const uint32_t c0 = (uint32_t)lane / 2, c1 = 16u + (uint32_t)lane / 2, off = (lane & 1) * 4;
-        uint16_t* base = (warp == GH ? ks() : vs()) + rr * kHd + off;
-        uint16_t* dst0 = base + ((c0 ^ (r & 7u)) * 8);
-        uint16_t* dst1 = base + ((c1 ^ (r & 7u)) * 8);
-        *reinterpret_cast<ushort4*>(dst0) = pa;
-        *reinterpret_cast<ushort4*>(dst1) = pb;
+        const uint32_t r = pos - jc, d = 4u * (uint32_t)lane;
+        unsigned char* half = warp == GH ? ks(b) : vs(b);
+        *reinterpret_cast<ushort4*>(half + at(r, d) + (d & 7u) * 2u) =
+            make_ushort4(f16_pack(va.x), f16_pack(va.y), f16_pack(va.z), f16_pack(va.w));
+        *reinterpret_cast<ushort4*>(half + at(r, d + kHd / 2) + (d & 7u) * 2u) =
+            make_ushort4(f16_pack(vb.x), f16_pack(vb.y), f16_pack(vb.z), f16_pack(vb.w));
+        wrote = true;
       }
-      cbar();
-      // Scores: warp w < 4 takes keys 8 w .. 8 w + 7 (one n-tile), all 16 k-steps.
-      if (warp < 4) {
-        const uint16_t* qrow = qh() + g * QS + 2 * t;
-        const uint32_t key = rb + 8 * warp + g;
-        const uint16_t* krow = ks() + key * kHd + 2 * t;
+      // Keys outside lo .. n - 1 get zero weights; their value rows are
+      // finite (the caches are zeroed at creation and the copy fills slots
+      // past a short cache with zeros), so 0 x V adds nothing.
+      if (cbar_or(fail)) {
+        dead = true;
+        break;
+      }
+      // Scores: warp w takes keys 8 (w % 4) .. + 7 (one n-tile) over dimensions
+      // 128 (w / 4) .. + 127 (eight k-steps; K fragments by ldmatrix, two
+      // k-steps a load); the two halves meet in shared memory.
+      {
+        const int nt = warp & 3, kh = warp >> 2;
+        const uint16_t* qrow = qh() + g * QS + 2 * t + 128 * kh;
+        const uint32_t key = 8 * nt + (lane & 7), d0 = 128 * kh + 8 * (lane >> 3);
         float d[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-          const uint32_t af[4] = {*reinterpret_cast<const uint32_t*>(qrow + 16 * k), 0u,
-                                  *reinterpret_cast<const uint32_t*>(qrow + 16 * k + 8), 0u};
-          const uint2 bf = make_uint2(*reinterpret_cast<const uint32_t*>(krow + (((2 * k) ^ (key & 7u)) * 8)),
-                                      *reinterpret_cast<const uint32_t*>(krow + (((2 * k + 1) ^ (key & 7u)) * 8)));
-          mma16816(d, af, bf, d);
+        for (int kp = 0; kp < 4; kp++) {
+          const uint32_t af0[4] = {*reinterpret_cast<const uint32_t*>(qrow + 32 * kp), 0u,
+                                   *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 8), 0u};
+          const uint32_t af1[4] = {*reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 16), 0u,
+                                   *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 24), 0u};
+          uint32_t r0, r1, r2, r3;
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                       : "r"(su32(ks(b) + at(key, d0 + 32 * kp))));
+          mma16816(d, af0, make_uint2(r0, r1), d);
+          mma16816(d, af1, make_uint2(r2, r3), d);
         }
         // Row g < GH: head g's part; row g + GH its remainder, GH lanes-of-4 down.
         const float r0 = __shfl_down_sync(0xffffffffu, d[0], 4 * GH);
         const float r1 = __shfl_down_sync(0xffffffffu, d[1], 4 * GH);
         if (g < GH) {
-          sc()[g * C + 8 * warp + 2 * t] = add(d[0], r0);
-          sc()[g * C + 8 * warp + 2 * t + 1] = add(d[1], r1);
+          float* dst = sc() + (kh * GH + g) * C + 8 * nt + 2 * t;
+          dst[0] = add(d[0], r0);
+          dst[1] = add(d[1], r1);
         }
       }
       cbar();
-      // Online softmax: warp h takes head h.
+      // Online softmax: warp h takes head h (lane l: key l).
       if (warp < GH) {
-        const float s = (uint32_t)lane < n ? sc()[warp * C + lane] : -INFINITY;
+        const bool ok = (uint32_t)lane >= lo && (uint32_t)lane < n;
+        const float s = ok ? add(sc()[warp * C + lane], sc()[(GH + warp) * C + lane]) : -INFINITY;
         const float mx = fmaxf(m_h, warp_max(s));
         const float corr = exp2f(m_h - mx);
-        const float e = (uint32_t)lane < n ? exp2f(s - mx) : 0.f;
+        const float e = ok ? exp2f(s - mx) : 0.f;
         l_h = __fmaf_rn(l_h, corr, warp_sum(e));
         m_h = mx;
         __half ehi, elo;
@@ -847,7 +930,8 @@ struct Attn {
         if (lane == 0) hstat()[warp] = corr;
       }
       cbar();
-      // Values: warp w takes dimensions 32 w .. 32 w + 31 (four n-tiles), keys in two k-steps.
+      // Values: warp w takes dimensions 32 w .. 32 w + 31 (four n-tiles), the
+      // chunk's two k-steps from one ldmatrix.x4.trans (lane l: key row l).
       {
         const float corr = g < 2 * GH ? hstat()[g < GH ? g : g - GH] : 0.f;
         uint32_t af[2][4];
@@ -858,27 +942,34 @@ struct Attn {
           af[k][2] = *reinterpret_cast<const uint32_t*>(ph() + g * PS + 16 * k + 8 + 2 * t);
           af[k][3] = 0u;
         }
-#pragma unroll
+#pragma unroll 2
         for (int i = 0; i < 4; i++) {
           const uint32_t nt = 4 * warp + i;
+          uint32_t r0, r1, r2, r3;
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                       : "r"(su32(vs(b) + at((uint32_t)lane, nt * 8))));
           float d[4] = {mul(acc[i][0], corr), mul(acc[i][1], corr), 0.f, 0.f};
-#pragma unroll
-          for (int k = 0; k < 2; k++) {
-            // Lanes 0..15 address the 16 key rows of this k-step's two 8 x 8 tiles.
-            const uint32_t key = rb + 16 * k + (lane & 15);
-            const uint16_t* src = vs() + key * kHd + ((nt ^ (key & 7u)) * 8);
-            uint2 bf;
-            asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
-                         : "=r"(bf.x), "=r"(bf.y)
-                         : "r"(su32(src)));
-            mma16816(d, af[k], bf, d);
-          }
+          mma16816(d, af[0], make_uint2(r0, r1), d);
+          mma16816(d, af[1], make_uint2(r2, r3), d);
           acc[i][0] = d[0];
           acc[i][1] = d[1];
         }
       }
+      // Buffer b is read: its next chunk (after a proxy fence by the threads
+      // that stored the new key into it).
+      const bool refill = jc + NB * C < j1;
+      if (wrote && refill) {
+        fence_proxy_async();
+        wrote = false;
+      }
       cbar();
-      if (jc + 2 * C < j1) stage(L, row, kvh, jc + 2 * C, min((uint32_t)C, j1 - jc - 2 * C), ci & 1u);
+      if (refill) stage(kvh, jc + NB * C, b);
+    }
+    if (dead) {
+      if (tid == 0) flags()[0] = 1u;
+      drain();
+      return;
     }
     // Each head's max and sum from warp h.
     if (warp < GH && lane == 0) {
@@ -928,6 +1019,9 @@ struct Attn {
       cbar();
       if (tid == 0) raise_counter(sync_of(l) + kSyncAttn);
     }
+    // Another item's copies follow: order this item's generic stores into
+    // the buffers (the new key, the fold's weights) before them.
+    if (more && wrote) fence_proxy_async();
     sync_dead();
   }
 
@@ -938,9 +1032,10 @@ struct Attn {
   // flight together.
   FZ_DEV void combine(uint32_t row, uint32_t kvh, uint32_t nsplit) {
     const uint32_t H = a.heads;
-    float* fac = reinterpret_cast<float*>(ks());   // [GH][nsplit] weights, then [GH] sums
+    float* fac = reinterpret_cast<float*>(ks(0));  // [GH][nsplit] weights, then [GH] sums
     float* lsum = fac + GH * nsplit;
     if (warp < GH) {
+      wrote = true;
       const size_t base = ((size_t)row * H + kvh * GH + warp) * a.max_splits;
       float mm = -INFINITY;
       for (uint32_t s = lane; s < nsplit; s += 32) mm = fmaxf(mm, __ldcg(a.partial_ml + (base + s) * 2));
@@ -991,9 +1086,12 @@ struct Attn {
 };
 
 // Returns bit 0: this thread gave up waiting; bit 1: the step is abandoned.
-template <int GH>
+template <int GH, int NB>
 __device__ __noinline__ uint32_t attention_layer(const DecodeArgs& a, uint32_t l, uint32_t pos, bool fail) {
-  Attn<GH> s{a};
+  Attn<GH, NB> s{a};
+  uint32_t* kvstate = reinterpret_cast<uint32_t*>(g_smem + a.lay.kvstate);
+  s.kvp = kvstate[0];
+  s.kvf = kvstate[1];
   s.M = a.m;
   s.pos = pos;
   s.W = kDecodeSyncFixed + a.m * a.kv_heads;
@@ -1002,7 +1100,19 @@ __device__ __noinline__ uint32_t attention_layer(const DecodeArgs& a, uint32_t l
   s.lane = threadIdx.x & 31;
   s.fail = fail;
   s.dead = false;
+  s.wait_ns = 0;
   s.run(l);
+  // Traced: the time thread 0 waited for key/value chunks (the attention
+  // phase's tile-wait total).
+  if (a.trace && threadIdx.x == 0 && s.wait_ns)
+    a.trace[(size_t)blockIdx.x * a.trace_stride + a.n_layers * kDecodeTracePhases * kDecodeTraceStamps + 1] +=
+        s.wait_ns;
+  // Every thread read the state before run()'s first barrier; thread 0's
+  // copy (it waited for or drained each buffer) carries on.
+  if (threadIdx.x == 0) {
+    kvstate[0] = s.kvp;
+    kvstate[1] = s.kvf;
+  }
   return (s.fail ? 1u : 0u) | (s.dead ? 2u : 0u);
 }
 
@@ -1280,8 +1390,10 @@ struct Consumer {
   FZ_DEV void attention(uint32_t l) {
     if (dead) return;
     const uint32_t group = a.heads / a.kv_heads;
-    const uint32_t r = group == 4 ? attention_layer<4>(a, l, pos, fail)
-                                  : group == 2 ? attention_layer<2>(a, l, pos, fail) : attention_layer<1>(a, l, pos, fail);
+    constexpr int NB = (int)kv_bufs(MQ);
+    const uint32_t r = group == 4   ? attention_layer<4, NB>(a, l, pos, fail)
+                       : group == 2 ? attention_layer<2, NB>(a, l, pos, fail)
+                                    : attention_layer<1, NB>(a, l, pos, fail);
     fail = (r & 1u) != 0;
     dead = (r & 2u) != 0;
   }
@@ -1347,6 +1459,10 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
     }
     flags[0] = 0u;
     flags[1] = 0u;
+    uint64_t* kvbar = reinterpret_cast<uint64_t*>(g_smem + ly.kvbar);
+    uint32_t* kvstate = reinterpret_cast<uint32_t*>(g_smem + ly.kvstate);
+    for (uint32_t b = 0; b < kv_bufs(MQ); b++) mb_init(kvbar + b, 1);
+    kvstate[0] = kvstate[1] = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x < kDecodeMaxRows) best[threadIdx.x] = 0ull;
@@ -1381,6 +1497,8 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < S; s++)
       if (uses[s] && !mb_wait(full + s, (uses[s] - 1) & 1u, nullptr, nullptr)) atomicOr(a.error, kErrDrain);
+    // (Key/value chunk copies are drained by the attention itself: only a
+    // drain that timed out leaves one in flight, and it reported kErrDrain.)
   }
 }
 
@@ -1440,6 +1558,33 @@ cudaError_t launch_mq(const DecodeArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+bool make_kv_maps(DecodeKvMaps& m, const DecodeLayer& d, uint32_t kv_heads, uint32_t sequences) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) return false;
+  static_assert(sizeof(CUtensorMap) == sizeof(m.map[0]), "tensor map size");
+  // Element (x, h, j, s): dimension x of KV head h at slot j of sequence s.
+  const cuuint64_t dims[4] = {kHd, kv_heads, d.slots, sequences};
+  const cuuint64_t strides[3] = {(cuuint64_t)kHd * 2, (cuuint64_t)kv_heads * kHd * 2, d.seq_stride * 2};
+  const cuuint32_t box[4] = {64, 1, kAttnChunk, 1};
+  const cuuint32_t estride[4] = {1, 1, 1, 1};
+  for (int w = 0; w < 2; w++) {
+    void* base = w ? d.value_cache : d.key_cache;
+    if (fn(reinterpret_cast<CUtensorMap*>(m.map[w]), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, base, dims, strides, box,
+           estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  return true;
+}
 
 bool decode_supported(uint32_t rows, uint32_t hidden, uint32_t ffn, uint32_t heads, uint32_t kv_heads,
                       uint32_t head_dim) {

@@ -26,6 +26,17 @@ struct DecodeLayer {
   uint32_t slots, window;
 };
 
+// A layer's TMA tensor maps (CUtensorMap) of its key and value caches, 4D
+// [sequence][slot][KV head][256]: boxes of 32 slots x 64 dimensions,
+// 128-byte swizzle.
+struct alignas(64) DecodeKvMaps {
+  unsigned char map[2][128];
+};
+
+// Encodes m from d's caches (slots, seq_stride) for `sequences` sequences of
+// kv_heads heads; false when the driver refuses.
+bool make_kv_maps(DecodeKvMaps& m, const DecodeLayer& d, uint32_t kv_heads, uint32_t sequences);
+
 constexpr uint32_t kDecodeMaxRows = 8;      // sequences one decode launch takes
 constexpr uint32_t kDecodeOSlices = 2;      // K slices of the output projection
 constexpr uint32_t kDecodeDownSlices = 4;   // K slices of the down projection
@@ -37,12 +48,13 @@ constexpr uint32_t kDecodeMaxSplits = 256;  // key splits the partial buffers ar
 // Byte offsets of the decode kernel's shared-memory regions (set by the launch).
 struct DecodeLayout {
   uint32_t codes, scales, full, empty, uni, xf, rowbuf, part, stat, red, task_rg, best, flags, gains, tags, uses,
-      total;
+      kvbuf, kvbar, kvstate, total;
 };
 
 struct DecodeArgs {
   const DeviceStep* step;          // position (every row is one sequence's next token)
   const DecodeLayer* layers;       // [n_layers], device memory
+  const DecodeKvMaps* kv_maps;     // [n_layers], device memory
   uint32_t n_layers;
   uint32_t m;                      // sequences = rows
   uint32_t hidden, ffn, heads, kv_heads;

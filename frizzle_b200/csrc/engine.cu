@@ -174,6 +174,7 @@ struct fz_batch {
   uint32_t* gemm_error = nullptr;  // set by a device wait (tensor-core product, decode step) that gave up
   // The persistent decode step: its per-layer view, K-slice partials, phase counters.
   fz::DecodeLayer* dlayers = nullptr;
+  fz::DecodeKvMaps* kv_maps = nullptr;   // the decode kernel's key/value tensor maps
   float* y_parts = nullptr;        // [O slices + down slices][rows][hidden]
   uint32_t* dsync = nullptr;
   size_t dsync_words = 0;
@@ -455,6 +456,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     fz::DecodeArgs d{};
     d.step = b.dstep;
     d.layers = b.dlayers;
+    d.kv_maps = b.kv_maps;
     d.n_layers = s.layers;
     d.m = b.S;
     d.hidden = s.hidden;
@@ -1007,7 +1009,9 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
   fz_status st;
   for (uint32_t l = 0; l < s.layers; l++) {
     const Layer& L = m->layers[l];
-    const uint64_t ring = (uint64_t)L.window + 512 + rollback;  // plan.cpp:335-336
+    // plan.cpp:335-336, rounded up to whole 32-slot chunks (the decode
+    // kernel's tensor-map boxes never wrap).
+    const uint64_t ring = ((uint64_t)L.window + 512 + rollback + 31) / 32 * 32;
     const uint32_t slots = (uint32_t)std::min<uint64_t>(context, ring);
     const uint64_t per_seq = (uint64_t)slots * s.kv_heads * s.head_dim;
     uint16_t *k = nullptr, *v = nullptr;
@@ -1025,6 +1029,7 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
   }
   {
     std::vector<fz::DecodeLayer> dl(s.layers);
+    std::vector<fz::DecodeKvMaps> maps(s.layers);
     for (uint32_t l = 0; l < s.layers; l++) {
       const Layer& L = m->layers[l];
       fz::DecodeLayer& d = dl[l];
@@ -1045,12 +1050,17 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
       d.seq_stride = b->seq_stride[l];
       d.slots = b->slots[l];
       d.window = L.window;
+      if (s.head_dim == 256 && !fz::make_kv_maps(maps[l], d, s.kv_heads, sequences))
+        return fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled refused the key/value cache maps");
     }
-    if ((st = b->alloc(&b->dlayers, dl.size() * sizeof(fz::DecodeLayer)))) return st;
+    if ((st = b->alloc(&b->dlayers, dl.size() * sizeof(fz::DecodeLayer))) ||
+        (st = b->alloc(&b->kv_maps, maps.size() * sizeof(fz::DecodeKvMaps))))
+      return st;
     if (fz::decode_supported(1, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim))
       FZ_CUDA(fz::prepare_decode(s.hidden, s.ffn, s.heads, s.kv_heads));
     if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) FZ_CUDA(fz::configure_attention_prefill());
     FZ_CUDA(cudaMemcpy(b->dlayers, dl.data(), dl.size() * sizeof(fz::DecodeLayer), cudaMemcpyHostToDevice));
+    FZ_CUDA(cudaMemcpy(b->kv_maps, maps.data(), maps.size() * sizeof(fz::DecodeKvMaps), cudaMemcpyHostToDevice));
   }
   b->table_words = 2 * s.layers + 5 * kMaxEdits;
   b->capture_floats = capture_layout(s).per_layer * s.layers;
