@@ -330,12 +330,16 @@ def run_ours(args):
         batch.wait()
         torch.cuda.synchronize()
         pos += K
-        # End to end: each step's record read back to the host before the next.
+        # End to end: every step's inputs copied in and its records read back, two steps in
+        # flight (the next enqueued before the previous one's records are read, as the
+        # reference's step order keeps two outstanding), records reported in order.
         with torch.cuda.stream(stream):
             ev[4].record()
+        batch.step(pos, fed=True, tokens=1, logits=True)
         for i in range(K):
-            batch.step(pos + i, fed=True, tokens=1, logits=True)
-            batch.wait()
+            if i + 1 < K:
+                batch.step(pos + i + 1, fed=True, tokens=1, logits=True)
+            batch.wait_oldest()
         with torch.cuda.stream(stream):
             ev[5].record()
         torch.cuda.synchronize()

@@ -66,6 +66,7 @@ SIGNATURES = {
     "fz_batch_set_edits": (C.c_int, [VP, U32, VP, C.c_size_t]),
     "fz_batch_step": (C.c_int, [VP, C.POINTER(Step), VP, VP]),
     "fz_batch_wait": (C.c_int, [VP, VP]),
+    "fz_batch_wait_oldest": (C.c_int, [VP, VP]),
     "fz_batch_read_logits": (C.c_int, [VP, U32, VP, C.c_size_t]),
     "fz_capture_floats": (C.c_size_t, [VP]),
     "fz_batch_read_capture": (C.c_int, [VP, U32, VP, C.c_size_t]),

@@ -61,7 +61,9 @@ constexpr uint32_t kAttnChunk = 32;     // keys an attention chunk
 
 enum : uint32_t { kPhQkv = 0, kPhO = 1, kPhGate = 2, kPhDown = 3, kPhHead = 4 };
 enum : uint32_t { kSyncQkv = 0, kSyncAttn = 1, kSyncO = 2, kSyncGate = 3, kSyncDown = 4 };
-enum : uint32_t { kErrCounter = 0x100u, kErrFull = 0x200u, kErrEmpty = 0x400u, kErrDrain = 0x800u, kErrTile = 0x1000u };
+enum : uint32_t {
+  kErrCounter = 0x100u, kErrFull = 0x200u, kErrEmpty = 0x400u, kErrDrain = 0x800u, kErrTile = 0x1000u, kErrNorm = 0x2000u
+};
 
 template <int MQ>
 __host__ __device__ constexpr uint32_t ring_slots() {
@@ -109,10 +111,11 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   // or the attention's queries and key/value chunks.
   L.uni = o;
   uint32_t m = o;
-  L.xf = m;
-  m += nkb * 512u * (uint32_t)MQ;
   L.rowbuf = m;
   m += 4u * (uint32_t)MQ * hidden * 4u;
+  m = (m + 15u) & ~15u;
+  L.xf = m;
+  m += nkb * 512u * (uint32_t)MQ;
   m = (m + 15u) & ~15u;
   L.part = m;
   m += 4u * MQ * kCT * 4u;
@@ -145,7 +148,7 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   L.kvbar = o;
   o += 4u * 8u;
   L.kvstate = o;
-  o += 2u * 4u;
+  o += 4u * 4u;
   L.total = o;
   return L;
 }
@@ -226,6 +229,9 @@ FZ_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) 
 // 16 bytes global -> shared without registers (waited for by cp_async_wait).
 FZ_DEV void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+FZ_DEV void cp_async16_cg(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(su32(dst)), "l"(src) : "memory");
 }
 FZ_DEV void cp_async_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // Orders this thread's generic-proxy shared-memory accesses before later
@@ -494,38 +500,42 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
   float* part = smem_f(a.lay.part);
   float* ry = smem_f(a.lay.stat);
   float* rx = ry + kDecodeMaxRows;
-#pragma unroll 1
-  for (int base = 0; base < items; base += 2 * kCT) {
-    float4 xa[2], ya[2][kDecodeDownSlices];
-#pragma unroll
-    for (int k = 0; k < 2; k++) {
-      const int i = base + k * kCT + tid;
-      if (i < items) {
-        const int r = i / V, v = i % V;
-        xa[k] = ldcg4(xin + (size_t)r * Wd + 4 * v);
-        if (y) {
-#pragma unroll
-          for (uint32_t sl = 0; sl < kDecodeDownSlices; sl++)
-            if (sl < ny) ya[k][sl] = ldcg4(y + ((size_t)sl * M + r) * Wd + 4 * v);
-        }
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 2; k++) {
-      const int i = base + k * kCT + tid;
-      if (i < items) {
-        xs[i] = xa[k];
-        if (y) {
-          float4 sum = ya[k][0];
-#pragma unroll
-          for (uint32_t sl = 1; sl < kDecodeDownSlices; sl++)
-            if (sl < ny) sum = add4(sum, ya[k][sl]);
-          ys[i] = sum;
-        }
-      }
-    }
+  // X and the y slices arrive by 16-byte cp.async (no registers held, all
+  // of a round in flight): X into rowbuf, slice j into T_j, k slices a round
+  // in the region from xf to the gains (k >= 2); T_0 keeps the running sum,
+  // added in slice order.
+  const uint32_t sb = M * (uint32_t)Wd * 4u;
+  unsigned char* T = g_smem + a.lay.xf;
+  const uint32_t k = y ? min(ny, (a.lay.gains - a.lay.xf) / sb) : 0u;
+  if (y && k < 2u) {   // (decode_supported rules this out)
+    if (tid == 0) atomicOr(a.error, kErrNorm);
+    cbar();
+    return;
   }
-  cp_async_wait();
+  float4* t0 = reinterpret_cast<float4*>(T);
+#pragma unroll 1
+  for (uint32_t next = 0;;) {
+    const uint32_t first = next == 0 ? 0u : 1u, n = next == 0 ? k : min(k - 1u, ny - next);
+#pragma unroll 1
+    for (int i = tid; i < items; i += kCT) {
+      if (next == 0) cp_async16_cg(xs + i, xin + 4 * i);
+      for (uint32_t j = 0; j < n; j++)
+        cp_async16_cg(reinterpret_cast<float4*>(T + (first + j) * sb) + i, y + (size_t)(next + j) * M * Wd + 4 * i);
+    }
+    cp_async_wait();
+    cbar();
+    next += n;
+    if (n > 1 || first) {
+#pragma unroll 1
+      for (int i = tid; i < items; i += kCT) {
+        float4 sum = t0[i];
+        for (uint32_t j = 1; j < first + n; j++) sum = add4(sum, reinterpret_cast<const float4*>(T + j * sb)[i]);
+        t0[i] = sum;
+      }
+    }
+    if (!y || next >= ny) break;
+    cbar();
+  }
   const bool writer = blockIdx.x == 0;
   if (y) {
     cbar();
@@ -581,55 +591,95 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
 }
 
 // B fragments of the rows (src [M][K]) for blocks [kb0, kb0 + nkb); rows
-// past M are zero.  kGlobal rows were written by other CTAs this launch.
+// past M are zero.  kGlobal rows were written by other CTAs this launch.  A
+// thread takes two items at a time, all their loads in flight together.
 template <int MQ, bool kGlobal>
 __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const float* src, uint32_t K, uint32_t kb0,
                                        uint32_t nkb) {
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, items = (int)nkb * 8;
   uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
-  // Thread i: block kb_rel, half h, lane quad tq; for each quad of rows q it
+  // Item i: block kb_rel, half h, lane quad tq; for each quad of rows q it
   // writes the eight columns (rows 4q..4q+3, hi and lo) of slot tq * 8 as one
   // contiguous 64 bytes.
 #pragma unroll 1
-  for (int i = tid; i < (int)nkb * 8; i += kCT) {
-    const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
+  for (int i0 = tid; i0 < items; i0 += 2 * kCT) {
+    float4 v[2][MQ][4];   // (row r's columns 2 tq, 2 tq + 1, then 16 on)
 #pragma unroll
-    for (int q = 0; q < MQ; q++) {
-      uint2 col[8];
+    for (int u = 0; u < 2; u++) {
+      const int i = i0 + u * kCT;
+      const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
 #pragma unroll
-      for (int gp = 0; gp < 4; gp++) {
-        const int r = 4 * q + gp;
-        uint2 hi = make_uint2(0, 0), lo = make_uint2(0, 0);
-        if (r < (int)M) {
-          const float* row = src + (size_t)r * K + 32 * (kb0 + kb_rel) + 8 * h + 2 * tq;
-          float2 v01, v23;
-          if (kGlobal) {
-            v01 = __ldcg(reinterpret_cast<const float2*>(row));
-            v23 = __ldcg(reinterpret_cast<const float2*>(row + 16));
-          } else {
-            v01 = *reinterpret_cast<const float2*>(row);
-            v23 = *reinterpret_cast<const float2*>(row + 16);
+      for (int q = 0; q < MQ; q++)
+#pragma unroll
+        for (int gp = 0; gp < 4; gp++) {
+          const int r = 4 * q + gp;
+          v[u][q][gp] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (i < items && r < (int)M) {
+            const float* row = src + (size_t)r * K + 32 * (kb0 + kb_rel) + 8 * h + 2 * tq;
+            float2 v01, v23;
+            if (kGlobal) {
+              v01 = __ldcg(reinterpret_cast<const float2*>(row));
+              v23 = __ldcg(reinterpret_cast<const float2*>(row + 16));
+            } else {
+              v01 = *reinterpret_cast<const float2*>(row);
+              v23 = *reinterpret_cast<const float2*>(row + 16);
+            }
+            v[u][q][gp] = make_float4(v01.x, v01.y, v23.x, v23.y);
           }
-          __half h0, h1, h2, h3, l0, l1, l2, l3;
-          split_hi_lo(v01.x, h0, l0);
-          split_hi_lo(v01.y, h1, l1);
-          split_hi_lo(v23.x, h2, l2);
-          split_hi_lo(v23.y, h3, l3);
-          hi = pack4(h0, h1, h2, h3);
-          lo = pack4(l0, l1, l2, l3);
         }
-        col[2 * gp] = hi;
-        col[2 * gp + 1] = lo;
-      }
-      // xf_index(kb_rel, h, q, MQ, tq, g) = ((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8 + g
-      uint4* dst = xf + (((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8) / 2;
+    }
 #pragma unroll
-      for (int k = 0; k < 4; k++) dst[k] = make_uint4(col[2 * k].x, col[2 * k].y, col[2 * k + 1].x, col[2 * k + 1].y);
+    for (int u = 0; u < 2; u++) {
+      const int i = i0 + u * kCT;
+      if (i >= items) break;
+      const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        uint2 col[8];
+#pragma unroll
+        for (int gp = 0; gp < 4; gp++) {
+          const float4 w = v[u][q][gp];
+          __half h0, h1, h2, h3, l0, l1, l2, l3;
+          split_hi_lo(w.x, h0, l0);
+          split_hi_lo(w.y, h1, l1);
+          split_hi_lo(w.z, h2, l2);
+          split_hi_lo(w.w, h3, l3);
+          col[2 * gp] = pack4(h0, h1, h2, h3);
+          col[2 * gp + 1] = pack4(l0, l1, l2, l3);
+        }
+        // xf_index(kb_rel, h, q, MQ, tq, g) = ((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8 + g
+        uint4* dst = xf + (((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8) / 2;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+          dst[k] = make_uint4(col[2 * k].x, col[2 * k].y, col[2 * k + 1].x, col[2 * k + 1].y);
+      }
     }
   }
 }
 
 // ------------------------------------------------------------ attention
+
+__device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uint32_t nsplit, uint32_t c0,
+                                            uint32_t nc);
+
+// The step's key splits for one layer: keys from a0 (the earliest key the
+// window keeps, rounded down to a chunk; keys before it are masked) to pos,
+// in splits of whole chunks, at least kMinSplitKeys keys each, as many as
+// give every (row, KV head) its share of the grid's G CTAs (at most
+// max_splits).  Returns the split count; kps the keys a split takes.
+FZ_DEV uint32_t attn_splits(const DecodeArgs& a, const DecodeLayer& L, uint32_t pos, uint32_t M, uint32_t G,
+                            uint32_t& a0, uint32_t& kps) {
+  const uint32_t earliest = pos + 1 > L.window ? pos + 1 - L.window : 0;
+  a0 = earliest / kAttnChunk * kAttnChunk;
+  const uint32_t nkeys = pos + 1 - a0, share = max(1u, G / (M * a.kv_heads));
+  kps = max(kMinSplitKeys, (nkeys + share - 1) / share);
+  if ((nkeys + kps - 1) / kps > a.max_splits) kps = (nkeys + a.max_splits - 1) / a.max_splits;
+  kps = (kps + kAttnChunk - 1) / kAttnChunk * kAttnChunk;
+  return (nkeys + kps - 1) / kps;
+}
+// Up to this many splits, the output projection's CTAs fold the splits as
+// they stage their slice of the attention rows (no fold in the attention).
+constexpr uint32_t kFoldInO = 8;
 
 // The step's attention for one layer: the CTAs with work items wait for the
 // layer's QKV counter.  Run in a function of its own (attention_layer), so
@@ -752,16 +802,9 @@ struct Attn {
     const DecodeLayer& L = a.layers[l];
     const uint32_t G = gridDim.x;
     const uint32_t earliest = pos + 1 > L.window ? pos + 1 - L.window : 0;
-    // Keys from a0 (earliest rounded down to a chunk; the keys before
-    // earliest are masked).
-    const uint32_t KV = a.kv_heads, a0 = earliest / C * C, nkeys = pos + 1 - a0;
-    // Splits of whole chunks, at least kMinSplitKeys keys each, as many as
-    // give every (row, KV head) its share of the CTAs (at most max_splits).
-    const uint32_t share = max(1u, G / (M * KV));
-    kps = max(kMinSplitKeys, (nkeys + share - 1) / share);
-    if ((nkeys + kps - 1) / kps > a.max_splits) kps = (nkeys + a.max_splits - 1) / a.max_splits;
-    kps = (kps + C - 1) / C * C;
-    const uint32_t nsplit = (nkeys + kps - 1) / kps, items = M * KV * nsplit;
+    const uint32_t KV = a.kv_heads;
+    uint32_t a0;
+    const uint32_t nsplit = attn_splits(a, L, pos, M, G, a0, kps), items = M * KV * nsplit;
     uint32_t item = G - 1 - blockIdx.x;
     if (item >= items) return;
     // The region held the products' rows and fragments (generic stores).
@@ -1001,7 +1044,10 @@ struct Attn {
       a.partial_ml[at * 2] = hstat()[tid];
       a.partial_ml[at * 2 + 1] = hstat()[GH + tid];
     }
-    bool final_cta = nsplit == 1;
+    // One split, or few (the output projection folds them): every item
+    // raises the layer's attention counter.  Many: the last of (row, kvh)
+    // folds them and raises it once.
+    bool final_cta = nsplit <= kFoldInO;
     if (!final_cta) {
       cbar();
       if (tid == 0) {
@@ -1116,6 +1162,62 @@ __device__ __noinline__ uint32_t attention_layer(const DecodeArgs& a, uint32_t l
   return (s.fail ? 1u : 0u) | (s.dead ? 2u : 0u);
 }
 
+// The attention rows of columns [c0, c0 + nc) (the output projection's
+// slice) from nsplit key splits, into rowbuf as [M][nc]: each thread folds
+// one row's four columns over the splits in split order, two splits' maxima,
+// sums and outputs loaded at a time, rescaling its running sum to each new
+// maximum (the fold of attention.wgsl:403-438, online).
+__device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uint32_t nsplit, uint32_t c0,
+                                            uint32_t nc) {
+  const uint32_t H = a.heads, n4 = nc / 4;
+  float4* out = reinterpret_cast<float4*>(smem_f(a.lay.rowbuf));
+#pragma unroll 1
+  for (uint32_t i = threadIdx.x; i < M * n4; i += kCT) {
+    const uint32_t r = i / n4, c = c0 + 4 * (i % n4), h = c / kHd;
+    const size_t base = ((size_t)r * H + h) * a.max_splits;
+    const float2* ml = reinterpret_cast<const float2*>(a.partial_ml) + base;
+    const float4* po = reinterpret_cast<const float4*>(a.partial_o + base * kHd + c % kHd);
+    float m = -INFINITY, l = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+    for (uint32_t s0 = 0; s0 < nsplit; s0 += 2) {
+      float2 w[2];
+      float4 v[2];
+#pragma unroll
+      for (uint32_t s = 0; s < 2; s++)
+        if (s0 + s < nsplit) {
+          w[s] = __ldcg(ml + s0 + s);
+          v[s] = __ldcg(po + (size_t)(s0 + s) * (kHd / 4));
+        }
+#pragma unroll
+      for (uint32_t s = 0; s < 2; s++)
+        if (s0 + s < nsplit) {
+          const float mn = fmaxf(m, w[s].x);
+          const float co = m == mn ? 1.0f : exp2f(m - mn), cs = w[s].x == mn ? 1.0f : exp2f(w[s].x - mn);
+          l = __fmaf_rn(w[s].y, cs, mul(l, co));
+          acc = make_float4(__fmaf_rn(v[s].x, cs, mul(acc.x, co)), __fmaf_rn(v[s].y, cs, mul(acc.y, co)),
+                            __fmaf_rn(v[s].z, cs, mul(acc.z, co)), __fmaf_rn(v[s].w, cs, mul(acc.w, co)));
+          m = mn;
+        }
+    }
+    out[i] = make_float4(__fdiv_rn(acc.x, l), __fdiv_rn(acc.y, l), __fdiv_rn(acc.z, l), __fdiv_rn(acc.w, l));
+  }
+  cbar();
+}
+
+// The output projection's B fragments: the attention rows, folded here from
+// their key splits when there are few.
+template <int MQ>
+__device__ __noinline__ void attention_fragments(const DecodeArgs& a, uint32_t M, uint32_t nsplit, uint32_t kb0,
+                                                 uint32_t nkb) {
+  if (nsplit > 1 && nsplit <= kFoldInO) {
+    fold_attention(a, M, nsplit, kb0 * 32u, nkb * 32u);
+    fragments<MQ, false>(a, M, smem_f(a.lay.rowbuf), nkb * 32u, 0, nkb);
+  } else {
+    fragments<MQ, true>(a, M, a.attn, a.heads * kHd, kb0, nkb);
+  }
+}
+
 // ------------------------------------------------------------ consumers
 
 template <int MQ>
@@ -1176,6 +1278,7 @@ struct Consumer {
     const DecodeLayer& L = a.layers[l < Ln ? l : Ln - 1];
     const float* pg = nullptr;
     const float* gain = nullptr;
+    uint32_t o_splits = 1;   // the attention's key splits (output projection)
     if (kind == kPhQkv) {
       if (l > 0) {
         ctr = sync_of(l - 1) + kSyncDown;
@@ -1185,7 +1288,9 @@ struct Consumer {
       gain = L.attn_norm;
     } else if (kind == kPhO) {
       ctr = sync_of(l) + kSyncAttn;
-      target = M * a.kv_heads;
+      uint32_t a0, kps;
+      o_splits = attn_splits(a, L, pos, M, G, a0, kps);
+      target = M * a.kv_heads * (o_splits <= kFoldInO ? o_splits : 1u);
     } else if (kind == kPhGate) {
       ctr = sync_of(l) + kSyncO;
       target = active_ctas(L.o.n / 16, kDecodeOSlices, G);
@@ -1233,7 +1338,7 @@ struct Consumer {
       norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, none, (Ln - 1) * per + a.cap_mlp_added);
       fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
     } else if (kind == kPhO) {
-      fragments<MQ, true>(a, M, a.attn, a.heads * kHd, kb0, nkb);
+      attention_fragments<MQ>(a, M, o_splits, kb0, nkb);
     } else {
       fragments<MQ, true>(a, M, a.act, a.ffn, kb0, nkb);
     }
@@ -1462,7 +1567,7 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
     uint64_t* kvbar = reinterpret_cast<uint64_t*>(g_smem + ly.kvbar);
     uint32_t* kvstate = reinterpret_cast<uint32_t*>(g_smem + ly.kvstate);
     for (uint32_t b = 0; b < kv_bufs(MQ); b++) mb_init(kvbar + b, 1);
-    kvstate[0] = kvstate[1] = 0u;
+    kvstate[0] = kvstate[1] = kvstate[2] = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x < kDecodeMaxRows) best[threadIdx.x] = 0ull;
@@ -1595,7 +1700,10 @@ bool decode_supported(uint32_t rows, uint32_t hidden, uint32_t ffn, uint32_t hea
   const int MQ = rows <= 4 ? 1 : 2;
   const DLayout ly = layout_for(MQ, MQ == 1 ? ring_slots<1>() : ring_slots<2>(), hidden, group,
                                 nkb_max(hidden, heads, ffn));
-  return ly.total <= 227u * 1024u && layout_aligned(ly);
+  // The norm stages two y slices at a time between xf and the gains; the
+  // output projection's folded attention slice fits rowbuf.
+  return ly.total <= 227u * 1024u && layout_aligned(ly) && ly.gains - ly.xf >= 2u * rows * hidden * 4u &&
+         slice_kb(heads * kHd, kDecodeOSlices) * 32u <= hidden;
 }
 
 cudaError_t prepare_decode(uint32_t hidden, uint32_t ffn, uint32_t heads, uint32_t kv_heads) {

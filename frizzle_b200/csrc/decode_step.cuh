@@ -42,7 +42,7 @@ constexpr uint32_t kDecodeOSlices = 2;      // K slices of the output projection
 constexpr uint32_t kDecodeDownSlices = 4;   // K slices of the down projection
 constexpr uint32_t kDecodeSyncFixed = 8;    // per-layer phase counters
 constexpr uint32_t kDecodeMaxGroup = 6;     // query heads a KV head may serve
-constexpr uint32_t kDecodeSplitKeys = 128;  // fewest keys of a split attention item
+constexpr uint32_t kDecodeSplitKeys = 64;   // fewest keys of a split attention item
 constexpr uint32_t kDecodeMaxSplits = 256;  // key splits the partial buffers are sized for
 
 // Byte offsets of the decode kernel's shared-memory regions (set by the launch).

@@ -192,6 +192,7 @@ struct fz_batch {
     cudaEvent_t copied = nullptr;  // the H2D copy of this slot has run
     cudaEvent_t done = nullptr;    // the step's records are home
     bool used = false;
+    bool pending = false;          // its records not reported yet
   } slot[2];
   int next_slot = 0;
   int last_slot = -1;
@@ -1210,16 +1211,16 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   FZ_CUDA(cudaMemcpyAsync(sl.error, b->gemm_error, 4, cudaMemcpyDeviceToHost, st));
   FZ_CUDA(cudaEventRecord(sl.done, st));
   sl.used = true;
+  sl.pending = true;
   b->last_slot = b->next_slot;
   b->next_slot ^= 1;
   return FZ_OK;
 }
 
-fz_status fz_batch_wait(fz_batch* b, fz_record* records) {
-  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
-  if (b->last_slot < 0) return fail(FZ_ERR_STATE, "no step was run");
-  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
-  auto& sl = b->slot[b->last_slot];
+namespace {
+
+// Waits for slot `sl`'s step and copies its records out.
+fz_status settle(fz_batch* b, fz_batch::Slot& sl, fz_record* records) {
   cudaError_t e = cudaEventSynchronize(sl.done);
   if (e != cudaSuccess) {
     const bool lost = e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure || e == cudaErrorECCUncorrectable;
@@ -1231,7 +1232,28 @@ fz_status fz_batch_wait(fz_batch* b, fz_record* records) {
     return fail(FZ_ERR_CUDA, "a device wait gave up (code " + std::to_string(code) + ")");
   }
   if (records) std::memcpy(records, sl.records, (size_t)b->S * 16);
+  sl.pending = false;
   return FZ_OK;
+}
+
+}  // namespace
+
+fz_status fz_batch_wait(fz_batch* b, fz_record* records) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  if (b->last_slot < 0) return fail(FZ_ERR_STATE, "no step was run");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  // The last step settles every earlier one.
+  b->slot[b->last_slot ^ 1].pending = false;
+  return settle(b, b->slot[b->last_slot], records);
+}
+
+fz_status fz_batch_wait_oldest(fz_batch* b, fz_record* records) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  // With both slots pending the older is the one the next step reuses.
+  const int i = b->slot[b->next_slot].pending ? b->next_slot : b->last_slot;
+  if (i < 0 || !b->slot[i].pending) return fail(FZ_ERR_STATE, "no step to report");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  return settle(b, b->slot[i], records);
 }
 
 fz_status fz_batch_read_logits(fz_batch* b, uint32_t sequence, float* out, size_t count) {

@@ -163,6 +163,13 @@ class Batch:
         check(self.lib.fz_batch_wait(self.handle, recs))
         return np.array([(r.token, r.failed, r.u) for r in recs], dtype=object)
 
+    def wait_oldest(self) -> np.ndarray:
+        """The records of the oldest step not yet reported (two steps may be in
+        flight; steps report in the order they ran)."""
+        recs = (Record * self.sequences)()
+        check(self.lib.fz_batch_wait_oldest(self.handle, recs))
+        return np.array([(r.token, r.failed, r.u) for r in recs], dtype=object)
+
     def tokens(self) -> list:
         recs = (Record * self.sequences)()
         check(self.lib.fz_batch_wait(self.handle, recs))

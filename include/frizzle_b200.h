@@ -141,6 +141,13 @@ fz_status fz_batch_set_edits(fz_batch *batch, uint32_t sequence, const uint32_t 
  * device's stream; fz_batch_wait returns the records. */
 fz_status fz_batch_step(fz_batch *batch, const fz_step *step, const uint32_t *ids, const uint32_t *seeds);
 fz_status fz_batch_wait(fz_batch *batch, fz_record *records);
+/* The oldest step not yet reported: waits for it and returns its records, so
+ * that a caller may keep two steps in flight and read each step's records in
+ * the order the steps ran (kernels/order.h:50-100, Order::run/next with
+ * kOutstanding 2).  A step enqueued while two are unreported overwrites the
+ * older one's records.  FZ_ERR_STATE when no step is outstanding;
+ * fz_batch_wait reports the last step and with it every earlier one. */
+fz_status fz_batch_wait_oldest(fz_batch *batch, fz_record *records);
 
 /* Readback: each sequence's last logits row (vocab floats), and its capture
  * store of the last row of the step that asked for it (fz_capture_floats

@@ -267,3 +267,44 @@ def test_gemma_1b_steered_pair_decode(gemma_model_path):
     vals = rng.uniform(-10, 10, size=5).astype(np.float32)
     edits = [Edit(13, int(i), SET, float(v), 0) for i, v in zip(idx, vals)]
     run_batch(gemma_model_path, s, 2, 32, 8, edit_sets=[edits, None])
+
+
+def test_two_steps_in_flight_report_in_order(tiny_model_path):
+    """Greedy decode with the next step enqueued before the previous step's
+    records are read (wait_oldest): the same tokens, in order, as one step at
+    a time, and the oracle's greedy tokens."""
+    s = synth.TINY
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, tiny_model_path)
+    ids = prompt(s, 10, seed=21)
+    got = []
+    for pipelined in (False, True):
+        batch = engine.Batch(model, 1, 512)
+        batch.step(0, ids, tokens=10, logits=True)
+        toks = [int(batch.wait()[0][0])]
+        n = 12
+        if pipelined:
+            batch.step(10, fed=True, tokens=1, logits=True)
+            for i in range(n):
+                if i + 1 < n:
+                    batch.step(11 + i, fed=True, tokens=1, logits=True)
+                toks.append(int(batch.wait_oldest()[0][0]))
+            with pytest.raises(RuntimeError):
+                batch.wait_oldest()
+        else:
+            for i in range(n):
+                batch.step(10 + i, fed=True, tokens=1, logits=True)
+                toks.append(int(batch.wait()[0][0]))
+        got.append(toks)
+        batch.free()
+    assert got[0] == got[1], got
+    orc = oracle.OracleModel(tiny_model_path, context=512)
+    want, _ = orc.step(0, ids, logits=True)
+    expect = [int(np.argmax(want))]
+    for i in range(12):
+        want, _ = orc.step(10 + i, [expect[-1]], logits=True)
+        expect.append(int(np.argmax(want)))
+    orc.close()
+    model.free()
+    dev.close()
+    assert got[1] == expect, (got[1], expect)
