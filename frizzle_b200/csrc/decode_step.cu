@@ -482,6 +482,22 @@ FZ_DEV void tree_rms(const DecodeArgs& a, int rows, float* rms, float width) {
   cbar();
 }
 
+// The norm's fixed-order tree over the 256 invocations (norm.wgsl:75-85),
+// in one warp: lane l holds the partials of invocations l + 32 i (P[i]);
+// halving levels 128, 64 and 32 give ((P0 + P4) + (P2 + P6)) + ((P1 + P5) +
+// (P3 + P7)), the last five levels are shuffles.  Returns the row's
+// reciprocal RMS, 1 / sqrt(total / width + eps), on every lane.
+FZ_DEV float warp_tree_rms(const float (&P)[8], float width, float eps) {
+  const int lane = threadIdx.x & 31;
+  float s = add(add(add(P[0], P[4]), add(P[2], P[6])), add(add(P[1], P[5]), add(P[3], P[7])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float other = __shfl_down_sync(0xffffffffu, s, o);
+    if (lane < o) s = add(s, other);
+  }
+  return __shfl_sync(0xffffffffu, inverse_sqrt(add(__fdiv_rn(s, width), eps)), 0);
+}
+
 // The norm launch (norm.wgsl:97-198) over the M rows into rowbuf: X plus
 // the post-normed block output (y: the sum of ny K-slice partials, in slice
 // order), written back by CTA 0 with the captures; then X's RMS norm times
@@ -497,9 +513,6 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
   float4* ys = reinterpret_cast<float4*>(smem_f(a.lay.xf));  // scratch until the fragments are built
   const float4* g4 = reinterpret_cast<const float4*>(smem_f(a.lay.gains));
   const float4* pg4 = g4 + V;
-  float* part = smem_f(a.lay.part);
-  float* ry = smem_f(a.lay.stat);
-  float* rx = ry + kDecodeMaxRows;
   // X and the y slices arrive by 16-byte cp.async (no registers held, all
   // of a round in flight): X into rowbuf, slice j into T_j, k slices a round
   // in the region from xf to the gains (k >= 2); T_0 keeps the running sum,
@@ -537,55 +550,117 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
     cbar();
   }
   const bool writer = blockIdx.x == 0;
-  if (y) {
-    cbar();
+  if (M < 4) {
+    // Few rows: the CTA's 256 invocations on each row in turn, the tree
+    // across the warps.
+    float* part = smem_f(a.lay.part);
+    float* ry = smem_f(a.lay.stat);
+    float* rx = ry + kDecodeMaxRows;
+    if (y) {
+      cbar();
+#pragma unroll 1
+      for (int r = 0; r < (int)M; r++) {
+        float p = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormVec; k++) {
+          const int v = tid + k * kCT;
+          if (v < V) p = add(p, dot_self(ys[r * V + v]));
+        }
+        part[r * kCT + tid] = p;
+      }
+      tree_rms(a, (int)M, ry, wf);
+    } else {
+      cbar();
+    }
 #pragma unroll 1
     for (int r = 0; r < (int)M; r++) {
+      float* capbase = (writer && a.capture) ? a.capture + (size_t)r * a.capture_stride : nullptr;
+      float4* xc = capbase && cap_x != ~0ull ? reinterpret_cast<float4*>(capbase + cap_x) : nullptr;
+      float4* yc = capbase && cap_y != ~0ull ? reinterpret_cast<float4*>(capbase + cap_y) : nullptr;
+      float4* out4 = writer && xout ? reinterpret_cast<float4*>(xout + (size_t)r * Wd) : nullptr;
       float p = 0.f;
 #pragma unroll
       for (int k = 0; k < kNormVec; k++) {
         const int v = tid + k * kCT;
-        if (v < V) p = add(p, dot_self(ys[r * V + v]));
+        if (v < V) {
+          float4 x = xs[r * V + v];
+          if (y) {
+            const float4 yy = scale4(ys[r * V + v], ry[r], pg4[v]);
+            if (yc) yc[v] = yy;
+            x = add4(x, yy);
+          }
+          if (out4) out4[v] = x;
+          if (xc) xc[v] = x;
+          xs[r * V + v] = x;
+          p = add(p, dot_self(x));
+        }
       }
       part[r * kCT + tid] = p;
     }
-    tree_rms(a, (int)M, ry, wf);
-  } else {
-    cbar();
-  }
+    tree_rms(a, (int)M, rx, wf);
 #pragma unroll 1
-  for (int r = 0; r < (int)M; r++) {
+    for (int r = 0; r < (int)M; r++) {
+#pragma unroll
+      for (int k = 0; k < kNormVec; k++) {
+        const int v = tid + k * kCT;
+        if (v < V) xs[r * V + v] = scale4(xs[r * V + v], rx[r], g4[v]);
+      }
+    }
+    cbar();
+    return;
+  }
+  // Warp r takes row r's passes alone (invocation t = lane + 32 i holds
+  // elements t, t + 256, ...): the y statistics, X plus the post-normed y
+  // (written out by CTA 0 with the captures), X's statistics, the scaling.
+  cbar();
+  const int warp = tid >> 5, lane = tid & 31;
+#pragma unroll 1
+  for (int r = warp; r < (int)M; r += kCW) {
+    float4* xr = xs + r * V;
+    const float4* yr = ys + r * V;
+    float P[8];
+    float ryv = 0.f;
+    if (y) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        float p = 0.f;
+#pragma unroll
+        for (int k = 0; k < kNormVec; k++) {
+          const int e = lane + 32 * i + k * kCT;
+          if (e < V) p = add(p, dot_self(yr[e]));
+        }
+        P[i] = p;
+      }
+      ryv = warp_tree_rms(P, wf, a.eps);
+    }
     float* capbase = (writer && a.capture) ? a.capture + (size_t)r * a.capture_stride : nullptr;
     float4* xc = capbase && cap_x != ~0ull ? reinterpret_cast<float4*>(capbase + cap_x) : nullptr;
     float4* yc = capbase && cap_y != ~0ull ? reinterpret_cast<float4*>(capbase + cap_y) : nullptr;
     float4* out4 = writer && xout ? reinterpret_cast<float4*>(xout + (size_t)r * Wd) : nullptr;
-    float p = 0.f;
 #pragma unroll
-    for (int k = 0; k < kNormVec; k++) {
-      const int v = tid + k * kCT;
-      if (v < V) {
-        float4 x = xs[r * V + v];
-        if (y) {
-          const float4 yy = scale4(ys[r * V + v], ry[r], pg4[v]);
-          if (yc) yc[v] = yy;
-          x = add4(x, yy);
+    for (int i = 0; i < 8; i++) {
+      float p = 0.f;
+#pragma unroll
+      for (int k = 0; k < kNormVec; k++) {
+        const int e = lane + 32 * i + k * kCT;
+        if (e < V) {
+          float4 x = xr[e];
+          if (y) {
+            const float4 yy = scale4(yr[e], ryv, pg4[e]);
+            if (yc) yc[e] = yy;
+            x = add4(x, yy);
+          }
+          if (out4) out4[e] = x;
+          if (xc) xc[e] = x;
+          xr[e] = x;
+          p = add(p, dot_self(x));
         }
-        if (out4) out4[v] = x;
-        if (xc) xc[v] = x;
-        xs[r * V + v] = x;
-        p = add(p, dot_self(x));
       }
+      P[i] = p;
     }
-    part[r * kCT + tid] = p;
-  }
-  tree_rms(a, (int)M, rx, wf);
+    const float rxv = warp_tree_rms(P, wf, a.eps);
 #pragma unroll 1
-  for (int r = 0; r < (int)M; r++) {
-#pragma unroll
-    for (int k = 0; k < kNormVec; k++) {
-      const int v = tid + k * kCT;
-      if (v < V) xs[r * V + v] = scale4(xs[r * V + v], rx[r], g4[v]);
-    }
+    for (int e = lane; e < V; e += 32) xr[e] = scale4(xr[e], rxv, g4[e]);
   }
   cbar();
 }
