@@ -224,12 +224,12 @@ def gemm_roofline(torch, lib, native, m=4096, reps=10):
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     (gc, gs), (uc, us) = mats
     out = {}
-    for passes in (2, 1):
+    for passes in (3, 2, 1):
         def run():
             native.check(lib.fz_q4_0_gemm_gated(gc.data_ptr(), gs.data_ptr(), uc.data_ptr(), us.data_ptr(), f, k,
-                                                hi.data_ptr(), lo.data_ptr() if passes == 2 else None, m, None, 0, 0,
-                                                None, ahi.data_ptr(), alo.data_ptr() if passes == 2 else None,
-                                                err.data_ptr(), s))
+                                                hi.data_ptr(), lo.data_ptr() if passes >= 2 else None,
+                                                1 if passes == 3 else 0, m, None, 0, 0, None, ahi.data_ptr(),
+                                                alo.data_ptr() if passes >= 2 else None, err.data_ptr(), s))
         for _ in range(3):
             run()
         torch.cuda.synchronize()
@@ -502,15 +502,20 @@ def run_ours(args):
         _, bf16, _ = peaks()
         line["prefill_4096"] = {"tokens_per_s": 4096 / p4k, "ms": 1000.0 * p4k,
                                 "workload": "BASELINE config 3: 4096 seeded ids in one step, 26 layers, "
-                                            "f32-level products (three tcgen05 MMAs a k-slice)",
+                                            "f32-level products (X and the weights each as f16 hi + lo, three "
+                                            "tcgen05 MMAs a k-slice: the engine's default)",
                                 "tflops_algorithmic": 6.03e12 / p4k / 1e12}
+
+        def mode(p, mmas):
+            return {"achieved": gflops / gsecs[p] / 1e12, "frac": gflops / gsecs[p] / 1e12 / bf16,
+                    "us": gsecs[p] * 1e6, "mmas_per_k_slice": mmas}
         line["prefill_gemm_roofline"] = {
             "bound": "tensor", "kernel": "tcgen05 gated product 1152 -> 2 x 6912 at M = 4096",
             "unit": "TFLOP/s", "peak": bf16, "algorithmic_flops": gflops,
-            "f32_level": {"achieved": gflops / gsecs[2] / 1e12, "frac": gflops / gsecs[2] / 1e12 / bf16,
-                          "us": gsecs[2] * 1e6, "mmas_per_k_slice": 3},
-            "f16_one_pass": {"achieved": gflops / gsecs[1] / 1e12, "frac": gflops / gsecs[1] / 1e12 / bf16,
-                             "us": gsecs[1] * 1e6, "mmas_per_k_slice": 1}}
+            "x_split": mode(2, 2), "f32_level": mode(3, 3), "f16_one_pass": mode(1, 1),
+            "note": "f32_level is the engine's default: with one f16 rounding of X (x_split rounds W) or of both "
+                    "(one pass), config 1's logits land at 1.1-1.6e-3 relative RMS from the fp32 oracle, above "
+                    "the 1e-3 parity bar"}
         if world == 1 and not args.no_cpu_baseline:
             v, threads, sample = cpu_decode_sample(path)
             line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}

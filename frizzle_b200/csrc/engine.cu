@@ -180,7 +180,12 @@ struct fz_batch {
   size_t dsync_words = 0;
   unsigned long long* trace = nullptr;  // phase timeline, when enabled
   uint32_t trace_ctas = 0, trace_events = 0;
-  uint32_t passes = 2;             // f16 passes over X in the tensor-core products (1 or 2)
+  // Tensor-core products: 1 = X and W each rounded once to f16; 2 = X as f16
+  // hi + lo, W rounded once (two MMAs a k-slice); 3 = W as hi + lo too
+  // (three MMAs, f32-level).  The model runs 3: with one f16 rounding of X or
+  // of W alone, config 1's logits land at 1.1-1.3e-3 relative RMS from the
+  // fp32 oracle, above the 1e-3 parity bar.
+  uint32_t passes = 3;
   std::vector<void*> row_allocs;
   // Host staging, two slots (at most two steps in flight, kernels/order.h:70).
   struct Slot {
@@ -538,8 +543,8 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
   }
   if (M > (uint32_t)fz::kMaxTokens) {
     // Wide step: per-row norms into f16, the products on the tensor cores.
-    __half* xlo = b.passes == 2 ? b.x16_lo : nullptr;
-    __half* alo = b.passes == 2 ? b.act16_lo : nullptr;
+    __half* xlo = b.passes >= 2 ? b.x16_lo : nullptr;
+    __half* alo = b.passes >= 2 ? b.act16_lo : nullptr;
     auto gemm = [&](const DevMatrix& w, const DevMatrix* up, const __half* xh, const __half* xl, float* out,
                     uint32_t stride, int epi, uint32_t layer) -> fz_status {
       fz::GemmArgs g{};
@@ -549,6 +554,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       g.m = M;
       g.x_hi = xh;
       g.x_lo = xl;
+      g.exact_w = b.passes == 3 ? 1u : 0u;
       g.out = out;
       g.out_stride = stride;
       g.act_hi = b.act16_hi;
@@ -1074,7 +1080,10 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
       (st = b->alloc(&b->edit_tables, (size_t)sequences * b->table_words * 4)) ||
       (st = b->alloc(&b->captures, (size_t)sequences * b->capture_floats * 4)) || (st = alloc_rows(*b, M)))
     return st;
-  if (const char* v = std::getenv("FRIZZLE_B200_PASSES")) b->passes = std::atoi(v) == 1 ? 1u : 2u;
+  if (const char* v = std::getenv("FRIZZLE_B200_PASSES")) {
+    const int p = std::atoi(v);
+    b->passes = p == 1 ? 1u : p == 3 ? 3u : 2u;
+  }
   b->has_edits.assign(sequences, false);
   for (auto& sl : b->slot) {
     FZ_CUDA(cudaMallocHost(&sl.step, sizeof(DeviceStep)));
@@ -1369,7 +1378,7 @@ fz_status fz_q4_0_head(const void* codes, const void* scales, uint32_t n, uint32
 }
 
 fz_status fz_q4_0_gemm(const void* codes, const void* scales, uint32_t n, uint32_t k, const void* x_hi, const void* x_lo,
-                       uint32_t m, float* y, uint32_t* error, void* stream) {
+                       uint32_t exact_weights, uint32_t m, float* y, uint32_t* error, void* stream) {
   fz_status st;
   if ((st = check_shape(n, k))) return st;
   if (!codes || !scales || !x_hi || !y || !error || m == 0) return fail(FZ_ERR_ARGUMENT, "null pointer or m = 0");
@@ -1378,6 +1387,7 @@ fz_status fz_q4_0_gemm(const void* codes, const void* scales, uint32_t n, uint32
   a.m = m;
   a.x_hi = static_cast<const __half*>(x_hi);
   a.x_lo = static_cast<const __half*>(x_lo);
+  a.exact_w = exact_weights;
   a.out = y;
   a.out_stride = n;
   a.seq_tokens = m;
@@ -1388,8 +1398,9 @@ fz_status fz_q4_0_gemm(const void* codes, const void* scales, uint32_t n, uint32
 
 fz_status fz_q4_0_gemm_gated(const void* gate_codes, const void* gate_scales, const void* up_codes,
                              const void* up_scales, uint32_t f, uint32_t k, const void* x_hi, const void* x_lo,
-                             uint32_t m, const uint32_t* table, uint32_t layer, uint32_t position, float* act,
-                             void* act_hi, void* act_lo, uint32_t* error, void* stream) {
+                             uint32_t exact_weights, uint32_t m, const uint32_t* table, uint32_t layer,
+                             uint32_t position, float* act, void* act_hi, void* act_lo, uint32_t* error,
+                             void* stream) {
   fz_status st;
   if ((st = check_shape(f, k))) return st;
   if (!gate_codes || !gate_scales || !up_codes || !up_scales || !x_hi || !act_hi || !error || m == 0)
@@ -1401,6 +1412,7 @@ fz_status fz_q4_0_gemm_gated(const void* gate_codes, const void* gate_scales, co
   a.position = position;
   a.x_hi = static_cast<const __half*>(x_hi);
   a.x_lo = static_cast<const __half*>(x_lo);
+  a.exact_w = exact_weights;
   a.out = act;
   a.out_stride = f;
   a.act_hi = static_cast<__half*>(act_hi);

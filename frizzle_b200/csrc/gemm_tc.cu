@@ -563,13 +563,17 @@ cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bo
   if ((reinterpret_cast<uintptr_t>(a.x_hi) & 15) || (a.x_lo && (reinterpret_cast<uintptr_t>(a.x_lo) & 15)))
     return cudaErrorInvalidValue;
   // Exact weights (WP = 2) go with both halves of X: the f32-level product.
-  const bool two = a.x_lo != nullptr;
+  const bool two = a.x_lo != nullptr, exact = two && a.exact_w;
   if (epilogue == kGemmGated) {
     if (!a.act_hi || a.w[1].n != a.w[0].n || a.w[1].k != a.w[0].k) return cudaErrorInvalidValue;
-    return two ? launch_tiles<128, 2, 2, kGemmGated>(a, stream, pdl) : launch_tiles<256, 1, 1, kGemmGated>(a, stream, pdl);
+    return exact ? launch_tiles<128, 2, 2, kGemmGated>(a, stream, pdl)
+           : two ? launch_tiles<256, 2, 1, kGemmGated>(a, stream, pdl)
+                 : launch_tiles<256, 1, 1, kGemmGated>(a, stream, pdl);
   }
   if (!a.out) return cudaErrorInvalidValue;
-  return two ? launch_tiles<128, 2, 2, kGemmWrite>(a, stream, pdl) : launch_tiles<256, 1, 1, kGemmWrite>(a, stream, pdl);
+  return exact ? launch_tiles<128, 2, 2, kGemmWrite>(a, stream, pdl)
+         : two ? launch_tiles<256, 2, 1, kGemmWrite>(a, stream, pdl)
+               : launch_tiles<256, 1, 1, kGemmWrite>(a, stream, pdl);
 }
 
 cudaError_t launch_split_f16(const float* x, size_t n, __half* hi, __half* lo, cudaStream_t stream) {

@@ -19,6 +19,7 @@ struct GemmArgs {
   uint32_t m;                 // rows of X
   const __half* x_hi;         // [m][k] f16
   const __half* x_lo;         // [m][k] f16 remainder, or null (one pass)
+  uint32_t exact_w;           // with x_lo: weights as f16 hi + lo too (three MMAs, f32-level)
   float* out;                 // [m][out_stride] f32 (Write; Gated: optional)
   uint32_t out_stride;
   // Gated epilogue: act = gelu(gate) * up, edits, then f16 hi/lo for the next product.
@@ -33,7 +34,9 @@ struct GemmArgs {
   uint32_t* error;            // set nonzero when a bounded wait gives up
 };
 
-// Launches the product; `passes` is 1 (x_hi only) or 2 (x_hi + x_lo).
+// Launches the product: X_hi.W (x_lo null), X_hi.W + X_lo.W (x_lo), or with
+// exact_w also X_hi.W_lo (three MMAs a k-slice); W rounded once to f16
+// unless exact_w.
 cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bool pdl);
 
 // x -> f16 hi = f16(x), lo = f16(x - hi) (lo may be null).

@@ -215,21 +215,25 @@ fz_status fz_q4_0_head(const void *codes, const void *scales, uint32_t n, uint32
 
 /* Y[m][n] = sum_k W[n][k] X[m][k] for many rows on the tensor cores
  * (tcgen05.mma into tensor memory; the reference's prefill form,
- * src/core/kernels/matmul/matmul.wgsl:287-485): X as f16 `x_hi` [m][k] and,
- * for f32-level accuracy, its f16 remainder `x_lo` (two passes; NULL for one).
- * Weights are rounded once to f16 as they are dequantized.  `error` is a
- * device word the caller zeroes; nonzero after the call completes means a
- * bounded wait inside the kernel gave up (no result). */
+ * src/core/kernels/matmul/matmul.wgsl:287-485): X as f16 `x_hi` [m][k] and
+ * optionally its f16 remainder `x_lo` (NULL: one pass).  Weights are rounded
+ * once to f16 as they are dequantized, unless `exact_weights` (with x_lo):
+ * then they too are f16 hi + lo and the product is f32-level (three MMAs a
+ * k-slice; two with x_lo alone, one without).  `error` is a device word the
+ * caller zeroes; nonzero after the call completes means a bounded wait inside
+ * the kernel gave up (no result). */
 fz_status fz_q4_0_gemm(const void *codes, const void *scales, uint32_t n, uint32_t k, const void *x_hi,
-                       const void *x_lo, uint32_t m, float *y, uint32_t *error, void *stream);
+                       const void *x_lo, uint32_t exact_weights, uint32_t m, float *y, uint32_t *error,
+                       void *stream);
 
 /* The gated product for many rows: act = gelu_tanh(gate . x) * (up . x), the
  * edit table applied to rows at positions position + r, written as f32 `act`
  * (may be NULL) and as f16 hi/lo (`act_lo` may be NULL) for the next product. */
 fz_status fz_q4_0_gemm_gated(const void *gate_codes, const void *gate_scales, const void *up_codes,
                              const void *up_scales, uint32_t f, uint32_t k, const void *x_hi, const void *x_lo,
-                             uint32_t m, const uint32_t *table, uint32_t layer, uint32_t position, float *act,
-                             void *act_hi, void *act_lo, uint32_t *error, void *stream);
+                             uint32_t exact_weights, uint32_t m, const uint32_t *table, uint32_t layer,
+                             uint32_t position, float *act, void *act_hi, void *act_lo, uint32_t *error,
+                             void *stream);
 
 /* x -> f16 hi = f16(x) and lo = f16(x - hi) (`lo` may be NULL). */
 fz_status fz_split_f16(const float *x, size_t n, void *hi, void *lo, void *stream);
