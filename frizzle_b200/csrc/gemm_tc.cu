@@ -192,6 +192,43 @@ FZ_DEV void dequant_tile(unsigned char* tile, unsigned char* tile_lo, uint32_t r
   }
 }
 
+// One warp a (row group, block pair): lane (g, t) decodes its four code
+// words exactly as dequant_tile does and writes the f16 pairs to [n][k].
+__global__ void dequant_f16_kernel(Q4Matrix w, __half* hi, __half* lo) {
+  const uint32_t nbp = w.k / 64, lane = threadIdx.x & 31;
+  const uint32_t item = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (item >= (w.n / 16) * nbp) return;
+  const uint32_t rg = item / nbp, bp = item % nbp, g = lane >> 2, t = lane & 3;
+  const uint4 c = w.codes[(size_t)item * 32 + lane];
+  const uint2 sc = w.scales[(size_t)item * 8 + g];
+  const uint32_t kLow = 0x000F000Fu, kHigh = 0x00F000F0u, kMagic = 0x64006400u;
+  const __half2 bias = __half2half2(__ushort_as_half((unsigned short)0x6408u));
+  const __half2 sixteenth = __half2half2(__ushort_as_half((unsigned short)0x2C00u));
+  const __half2 bias16 = __half2half2(__ushort_as_half((unsigned short)0xD480u));
+  const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int wi = 0; wi < 4; wi++) {
+    const uint32_t kb = wi >> 1, h = wi & 1, wd = words[wi], w8 = wd >> 8;
+    const uint32_t sw = kb ? sc.y : sc.x;
+    const __half2 dg = u2h(__byte_perm(sw, 0, 0x1010)), dg8 = u2h(__byte_perm(sw, 0, 0x3232));
+    const uint32_t k0 = 64 * bp + 32 * kb + 8 * h + 2 * t, r0 = rg * 16 + g, r8 = r0 + 8;
+    const __half2 c4[4] = {__hsub2(u2h((wd & kLow) | kMagic), bias),
+                           __hfma2(u2h((wd & kHigh) | kMagic), sixteenth, bias16),
+                           __hsub2(u2h((w8 & kLow) | kMagic), bias),
+                           __hfma2(u2h((w8 & kHigh) | kMagic), sixteenth, bias16)};
+    const uint32_t rows[4] = {r0, r0, r8, r8};
+    const uint32_t cols[4] = {k0, k0 + 16, k0, k0 + 16};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const __half2 d = j < 2 ? dg : dg8;
+      const __half2 vh = __hmul2(c4[j], d);
+      const size_t at = (size_t)rows[j] * w.k + cols[j];
+      *reinterpret_cast<__half2*>(hi + at) = vh;
+      if (lo) *reinterpret_cast<__half2*>(lo + at) = __hfma2(c4[j], d, __hneg2(vh));
+    }
+  }
+}
+
 FZ_DEV float apply_edit_table(const uint32_t* table, uint32_t layer, uint32_t neuron, uint32_t pos, float v) {
   const uint32_t first = table[2 * layer], count = table[2 * layer + 1];
   uint32_t lo = 0, hi = count;
@@ -223,11 +260,17 @@ struct Layout {
 
 // XP: passes over X (f16 hi, + lo); WP: passes over W (f16 hi, + lo).  The
 // MMAs per 16 columns: X_hi.W_hi, X_lo.W_hi (XP = 2), X_hi.W_lo (WP = 2); the
-// dropped X_lo.W_lo term is below 2^-22 relative.
-template <int BN, int XP, int WP, int EPI>
+// dropped X_lo.W_lo term is below 2^-22 relative.  WT: the weight tiles
+// come by TMA from f16 copies (wmaps: gate or the matrix hi, lo, then up hi,
+// lo) and the producer warps stand idle.
+struct WMaps {
+  CUtensorMap m[4];
+};
+
+template <int BN, int XP, int WP, int EPI, bool WT>
 __global__ void __launch_bounds__(kThreadsG, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_hi, const __grid_constant__ CUtensorMap map_lo,
-                const GemmArgs a) {
+                const __grid_constant__ WMaps wmaps, const GemmArgs a) {
   constexpr int PASSES = XP;
   using L = Layout<BN, XP, WP>;
   constexpr int S = L::kStages;
@@ -255,7 +298,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < S; s++) {
-      mbar_init(&full[s], 1 + kProducers);
+      mbar_init(&full[s], WT ? 1 : 1 + kProducers);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
@@ -282,7 +325,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     uint32_t it = 0;
     bool stop = false;
     for (uint32_t tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x) {
-      const uint32_t m0 = m0_of(tile);
+      const uint32_t m0 = m0_of(tile), n0 = n0_of(tile);
       for (uint32_t kt = 0; kt < nkt; kt++, it++) {
         const int s = (int)(it % S);
         const uint32_t round = it / S;
@@ -291,9 +334,23 @@ __global__ void __launch_bounds__(kThreadsG, 1)
           break;
         }
         if (lane == 0) {
-          mbar_expect_tx(&full[s], (uint32_t)(L::kABytes * PASSES));
+          mbar_expect_tx(&full[s], (uint32_t)(L::kABytes * PASSES + (WT ? L::kBBytes * WP : 0)));
           tma_load_2d(a_tile(s, 0), &map_hi, &full[s], (int)(kt * kBK), (int)m0);
           if (PASSES == 2) tma_load_2d(a_tile(s, 1), &map_lo, &full[s], (int)(kt * kBK), (int)m0);
+          if (WT) {
+            // Weight rows n0 .. as the B tile's rows (gated: gate rows, then up rows).
+            if (EPI == kGemmGated) {
+              tma_load_2d(b_tile(s), &wmaps.m[0], &full[s], (int)(kt * kBK), (int)n0);
+              tma_load_2d(b_tile(s) + half_bn * 128u, &wmaps.m[2], &full[s], (int)(kt * kBK), (int)n0);
+              if (WP == 2) {
+                tma_load_2d(b_tile_lo(s), &wmaps.m[1], &full[s], (int)(kt * kBK), (int)n0);
+                tma_load_2d(b_tile_lo(s) + half_bn * 128u, &wmaps.m[3], &full[s], (int)(kt * kBK), (int)n0);
+              }
+            } else {
+              tma_load_2d(b_tile(s), &wmaps.m[0], &full[s], (int)(kt * kBK), (int)n0);
+              if (WP == 2) tma_load_2d(b_tile_lo(s), &wmaps.m[1], &full[s], (int)(kt * kBK), (int)n0);
+            }
+          }
         }
         __syncwarp();
       }
@@ -339,6 +396,9 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       }
     }
   } else if (warp < 2 + kProducers) {
+    if (WT) {
+      // (the weight tiles come by TMA)
+    } else {
     // Weight producers: warps 2..9 dequantize BN / 16 row groups a stage, the
     // codes of the next two stages already in flight; the stages run on
     // across tiles (flat index q over this CTA's tiles x k-slices).
@@ -392,6 +452,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       step(q, A, C);
       if (q + 1 < total && !stop) step(q + 1, B, A);
       if (q + 2 < total && !stop) step(q + 2, C, B);
+    }
     }
   } else {
     // Epilogue: warps 10..17; warp w reads TMEM lanes 32 * (w % 4) .. + 31,
@@ -503,35 +564,46 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// A 2D tensor map over an [rows][cols] f16 matrix: boxes of 128 rows x 64
-// columns, 128-byte swizzle, rows past `rows` read as zeros.
-bool make_map(CUtensorMap* map, const __half* base, uint32_t rows, uint32_t cols) {
+// A 2D tensor map over an [rows][cols] f16 matrix: boxes of box_rows rows x
+// 64 columns, 128-byte swizzle, rows past `rows` read as zeros.
+bool make_map(CUtensorMap* map, const __half* base, uint32_t rows, uint32_t cols, uint32_t box_rows = kBM) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
   const cuuint32_t estride[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estride,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN, int XP, int WP, int EPI>
+template <int BN, int XP, int WP, int EPI, bool WT>
 cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
   constexpr int PASSES = XP;
   using L = Layout<BN, XP, WP>;
   static std::once_flag once;
   static cudaError_t configured = cudaSuccess;
   std::call_once(once, [] {
-    configured = cudaFuncSetAttribute(gemm_kernel<BN, XP, WP, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      L::kSmem);
+    configured = cudaFuncSetAttribute(gemm_kernel<BN, XP, WP, EPI, WT>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem);
   });
   if (configured != cudaSuccess) return configured;
   CUtensorMap map_hi, map_lo;
   if (!make_map(&map_hi, a.x_hi, a.m, a.w[0].k)) return cudaErrorInvalidValue;
   if (!make_map(&map_lo, PASSES == 2 ? a.x_lo : a.x_hi, a.m, a.w[0].k)) return cudaErrorInvalidValue;
   const uint32_t cols = EPI == kGemmGated ? BN / 2 : BN;
+  WMaps wm{};
+  if (WT) {
+    const uint32_t n = a.w[0].n, k = a.w[0].k;
+    const __half* lo0 = WP == 2 ? a.w_lo[0] : a.w_hi[0];
+    if (!make_map(&wm.m[0], a.w_hi[0], n, k, cols) || !make_map(&wm.m[1], lo0, n, k, cols)) return cudaErrorInvalidValue;
+    if (EPI == kGemmGated) {
+      const __half* lo1 = WP == 2 ? a.w_lo[1] : a.w_hi[1];
+      if (!make_map(&wm.m[2], a.w_hi[1], n, k, cols) || !make_map(&wm.m[3], lo1, n, k, cols))
+        return cudaErrorInvalidValue;
+    }
+  }
   const uint32_t tiles = ((a.w[0].n + cols - 1) / cols) * ((a.m + kBM - 1) / kBM);
   static int sms = 0;
   if (!sms) {
@@ -550,7 +622,7 @@ cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, XP, WP, EPI>, map_hi, map_lo, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, XP, WP, EPI, WT>, map_hi, map_lo, wm, a);
   if (e != cudaSuccess) (void)cudaGetLastError();
   return e;
 }
@@ -564,16 +636,37 @@ cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bo
     return cudaErrorInvalidValue;
   // Exact weights (WP = 2) go with both halves of X: the f32-level product.
   const bool two = a.x_lo != nullptr, exact = two && a.exact_w;
+  const bool wt = a.w_hi[0] != nullptr;
+  if (wt) {
+    if ((reinterpret_cast<uintptr_t>(a.w_hi[0]) & 15) || (exact && !a.w_lo[0])) return cudaErrorInvalidValue;
+    if (epilogue == kGemmGated && (!a.w_hi[1] || (exact && !a.w_lo[1]))) return cudaErrorInvalidValue;
+  }
   if (epilogue == kGemmGated) {
     if (!a.act_hi || a.w[1].n != a.w[0].n || a.w[1].k != a.w[0].k) return cudaErrorInvalidValue;
-    return exact ? launch_tiles<128, 2, 2, kGemmGated>(a, stream, pdl)
-           : two ? launch_tiles<256, 2, 1, kGemmGated>(a, stream, pdl)
-                 : launch_tiles<256, 1, 1, kGemmGated>(a, stream, pdl);
+    if (wt)
+      return exact ? launch_tiles<128, 2, 2, kGemmGated, true>(a, stream, pdl)
+             : two ? launch_tiles<256, 2, 1, kGemmGated, true>(a, stream, pdl)
+                   : launch_tiles<256, 1, 1, kGemmGated, true>(a, stream, pdl);
+    return exact ? launch_tiles<128, 2, 2, kGemmGated, false>(a, stream, pdl)
+           : two ? launch_tiles<256, 2, 1, kGemmGated, false>(a, stream, pdl)
+                 : launch_tiles<256, 1, 1, kGemmGated, false>(a, stream, pdl);
   }
   if (!a.out) return cudaErrorInvalidValue;
-  return exact ? launch_tiles<128, 2, 2, kGemmWrite>(a, stream, pdl)
-         : two ? launch_tiles<256, 2, 1, kGemmWrite>(a, stream, pdl)
-               : launch_tiles<256, 1, 1, kGemmWrite>(a, stream, pdl);
+  if (wt)
+    return exact ? launch_tiles<128, 2, 2, kGemmWrite, true>(a, stream, pdl)
+           : two ? launch_tiles<256, 2, 1, kGemmWrite, true>(a, stream, pdl)
+                 : launch_tiles<256, 1, 1, kGemmWrite, true>(a, stream, pdl);
+  return exact ? launch_tiles<128, 2, 2, kGemmWrite, false>(a, stream, pdl)
+         : two ? launch_tiles<256, 2, 1, kGemmWrite, false>(a, stream, pdl)
+               : launch_tiles<256, 1, 1, kGemmWrite, false>(a, stream, pdl);
+}
+
+cudaError_t launch_dequant_f16(const Q4Matrix& w, __half* hi, __half* lo, cudaStream_t stream) {
+  if (!hi || w.k % 64 || w.n % 16) return cudaErrorInvalidValue;
+  const size_t items = (size_t)(w.n / 16) * (w.k / 64);
+  (void)cudaGetLastError();
+  dequant_f16_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(w, hi, lo);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_split_f16(const float* x, size_t n, __half* hi, __half* lo, cudaStream_t stream) {

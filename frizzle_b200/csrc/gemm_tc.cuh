@@ -16,6 +16,11 @@ struct GemmArgs {
   const DeviceStep* step;     // position of row 0, or null for `position`
   uint32_t position;
   Q4Matrix w[2];              // w[1]: the up projection of a gated product
+  // Optional f16 copies of w[0], w[1] ([n][k], the weights as f16 hi and
+  // remainder lo, from dequant_f16): when w_hi[0] is set the tiles arrive by
+  // TMA and no CTA dequantizes (w_lo with exact_w).
+  const __half* w_hi[2];
+  const __half* w_lo[2];
   uint32_t m;                 // rows of X
   const __half* x_hi;         // [m][k] f16
   const __half* x_lo;         // [m][k] f16 remainder, or null (one pass)
@@ -38,6 +43,10 @@ struct GemmArgs {
 // exact_w also X_hi.W_lo (three MMAs a k-slice); W rounded once to f16
 // unless exact_w.
 cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bool pdl);
+
+// The Q4_0 matrix as f16 [n][k]: hi = f16((code - 8) d), lo = the f16
+// remainder of the exact product (lo may be null).
+cudaError_t launch_dequant_f16(const Q4Matrix& w, __half* hi, __half* lo, cudaStream_t stream);
 
 // x -> f16 hi = f16(x), lo = f16(x - hi) (lo may be null).
 cudaError_t launch_split_f16(const float* x, size_t n, __half* hi, __half* lo, cudaStream_t stream);
