@@ -81,6 +81,9 @@ SIGNATURES = {
     "fz_q4_0_gated": (C.c_int, [VP, VP, VP, VP, U32, U32, VP, U32, VP, U32, U32, VP, VP]),
     "fz_q4_0_head": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP, VP]),
     "fz_q4_0_gemm": (C.c_int, [VP, VP, U32, U32, VP, VP, U32, U32, VP, VP, VP]),
+    "fz_q4_0_to_f16": (C.c_int, [VP, VP, U32, U32, VP, VP, VP]),
+    "fz_f16_gemm": (C.c_int, [VP, VP, U32, U32, VP, VP, U32, U32, VP, VP, VP]),
+    "fz_f16_gemm_gated": (C.c_int, [VP, VP, VP, VP, U32, U32, VP, VP, U32, U32, VP, U32, U32, VP, VP, VP, VP, VP]),
     "fz_q4_0_gemm_gated": (C.c_int, [VP, VP, VP, VP, U32, U32, VP, VP, U32, U32, VP, U32, U32, VP, VP, VP, VP, VP]),
     "fz_split_f16": (C.c_int, [VP, C.c_size_t, VP, VP, VP]),
     "fz_attention": (C.c_int, [VP, VP, VP, U32, U32, U32, U32, U32, U32, U32, VP, VP, VP, VP, VP]),

@@ -1412,6 +1412,71 @@ fz_status fz_q4_0_gemm(const void* codes, const void* scales, uint32_t n, uint32
   return FZ_OK;
 }
 
+fz_status fz_q4_0_to_f16(const void* codes, const void* scales, uint32_t n, uint32_t k, void* w_hi, void* w_lo,
+                         void* stream) {
+  fz_status st;
+  if ((st = check_shape(n, k))) return st;
+  if (!codes || !scales || !w_hi) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  const Q4Matrix w{static_cast<const uint4*>(codes), static_cast<const uint2*>(scales), n, k};
+  FZ_CUDA(fz::launch_dequant_f16(w, static_cast<__half*>(w_hi), static_cast<__half*>(w_lo),
+                                 static_cast<cudaStream_t>(stream)));
+  return FZ_OK;
+}
+
+fz_status fz_f16_gemm(const void* w_hi, const void* w_lo, uint32_t n, uint32_t k, const void* x_hi, const void* x_lo,
+                      uint32_t exact_weights, uint32_t m, float* y, uint32_t* error, void* stream) {
+  fz_status st;
+  if ((st = check_shape(n, k))) return st;
+  if (!w_hi || (exact_weights && (!w_lo || !x_lo)) || !x_hi || !y || !error || m == 0)
+    return fail(FZ_ERR_ARGUMENT, "null pointer or m = 0");
+  fz::GemmArgs a{};
+  a.w[0] = Q4Matrix{nullptr, nullptr, n, k};
+  a.w_hi[0] = static_cast<const __half*>(w_hi);
+  a.w_lo[0] = static_cast<const __half*>(w_lo);
+  a.m = m;
+  a.x_hi = static_cast<const __half*>(x_hi);
+  a.x_lo = static_cast<const __half*>(x_lo);
+  a.exact_w = exact_weights;
+  a.out = y;
+  a.out_stride = n;
+  a.seq_tokens = m;
+  a.error = error;
+  FZ_CUDA(fz::launch_gemm(a, fz::kGemmWrite, static_cast<cudaStream_t>(stream), false));
+  return FZ_OK;
+}
+
+fz_status fz_f16_gemm_gated(const void* gate_hi, const void* gate_lo, const void* up_hi, const void* up_lo, uint32_t f,
+                            uint32_t k, const void* x_hi, const void* x_lo, uint32_t exact_weights, uint32_t m,
+                            const uint32_t* table, uint32_t layer, uint32_t position, float* act, void* act_hi,
+                            void* act_lo, uint32_t* error, void* stream) {
+  fz_status st;
+  if ((st = check_shape(f, k))) return st;
+  if (!gate_hi || !up_hi || (exact_weights && (!gate_lo || !up_lo || !x_lo)) || !x_hi || !act_hi || !error || m == 0)
+    return fail(FZ_ERR_ARGUMENT, "null pointer or m = 0");
+  fz::GemmArgs a{};
+  a.w[0] = Q4Matrix{nullptr, nullptr, f, k};
+  a.w[1] = Q4Matrix{nullptr, nullptr, f, k};
+  a.w_hi[0] = static_cast<const __half*>(gate_hi);
+  a.w_lo[0] = static_cast<const __half*>(gate_lo);
+  a.w_hi[1] = static_cast<const __half*>(up_hi);
+  a.w_lo[1] = static_cast<const __half*>(up_lo);
+  a.m = m;
+  a.position = position;
+  a.x_hi = static_cast<const __half*>(x_hi);
+  a.x_lo = static_cast<const __half*>(x_lo);
+  a.exact_w = exact_weights;
+  a.out = act;
+  a.out_stride = f;
+  a.act_hi = static_cast<__half*>(act_hi);
+  a.act_lo = static_cast<__half*>(act_lo);
+  a.edit_table = table;
+  a.layer = layer;
+  a.seq_tokens = m;
+  a.error = error;
+  FZ_CUDA(fz::launch_gemm(a, fz::kGemmGated, static_cast<cudaStream_t>(stream), false));
+  return FZ_OK;
+}
+
 fz_status fz_q4_0_gemm_gated(const void* gate_codes, const void* gate_scales, const void* up_codes,
                              const void* up_scales, uint32_t f, uint32_t k, const void* x_hi, const void* x_lo,
                              uint32_t exact_weights, uint32_t m, const uint32_t* table, uint32_t layer,

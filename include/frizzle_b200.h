@@ -235,6 +235,22 @@ fz_status fz_q4_0_gemm_gated(const void *gate_codes, const void *gate_scales, co
                              uint32_t position, float *act, void *act_hi, void *act_lo, uint32_t *error,
                              void *stream);
 
+/* The Q4_0 matrix (repacked codes and scales, n x k) as f16 [n][k]: w_hi =
+ * f16((code - 8) d), w_lo = the f16 remainder of that exact product (may be
+ * NULL).  The engine makes these once at load for its prefill products. */
+fz_status fz_q4_0_to_f16(const void *codes, const void *scales, uint32_t n, uint32_t k, void *w_hi, void *w_lo,
+                         void *stream);
+
+/* fz_q4_0_gemm and fz_q4_0_gemm_gated with the weights as f16 copies
+ * (fz_q4_0_to_f16; `*_lo` needed with exact_weights): the weight tiles come
+ * by TMA like X's and no CTA dequantizes. */
+fz_status fz_f16_gemm(const void *w_hi, const void *w_lo, uint32_t n, uint32_t k, const void *x_hi,
+                      const void *x_lo, uint32_t exact_weights, uint32_t m, float *y, uint32_t *error, void *stream);
+fz_status fz_f16_gemm_gated(const void *gate_hi, const void *gate_lo, const void *up_hi, const void *up_lo,
+                            uint32_t f, uint32_t k, const void *x_hi, const void *x_lo, uint32_t exact_weights,
+                            uint32_t m, const uint32_t *table, uint32_t layer, uint32_t position, float *act,
+                            void *act_hi, void *act_lo, uint32_t *error, void *stream);
+
 /* x -> f16 hi = f16(x) and lo = f16(x - hi) (`lo` may be NULL). */
 fz_status fz_split_f16(const float *x, size_t n, void *hi, void *lo, void *stream);
 

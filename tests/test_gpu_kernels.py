@@ -250,3 +250,88 @@ def test_tensor_core_gated_with_edits(m, position):
             for r in range(m):
                 if 40 + e.start <= position + r < 40 + e.until:
                     assert got[r, e.neuron] == np.float32(e.value)
+
+
+@pytest.mark.parametrize("k,n", [(1152, 1536), (6912, 1152)])
+def test_q4_0_to_f16_split_is_exact(k, n):
+    """fz_q4_0_to_f16: hi = f16 of (code - 8) d, lo = the f16 remainder; hi + lo
+    is the exact product (in f64) wherever the remainder is a normal f16."""
+    torch = torch_cuda()
+    lib = _native.load()
+    blocks = synth.random_q4_0(n, k, seed=n + 3)
+    codes, scales = repacked(blocks, n, k)
+    hi = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    lo = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    _native.check(lib.fz_q4_0_to_f16(codes.data_ptr(), scales.data_ptr(), n, k, hi.data_ptr(), lo.data_ptr(),
+                                     stream()))
+    torch.cuda.synchronize()
+    want = oracle.dequant(blocks).reshape(n, k).astype(np.float64)
+    h = hi.cpu().numpy().astype(np.float64)
+    lo_ = lo.cpu().numpy().astype(np.float64)
+    assert np.array_equal(h, want.astype(np.float16).astype(np.float64))
+    err = np.abs(h + lo_ - want)
+    assert err.max() <= 2.0 ** -24 * max(1.0, np.abs(want).max()), err.max()
+
+
+@pytest.mark.parametrize("passes", [1, 2, 3])
+@pytest.mark.parametrize("m", [64, 300])
+def test_f16_weight_gemm(m, passes):
+    """The tensor-core product with the weight tiles by TMA from f16 copies:
+    the same tolerances as the in-kernel dequant path."""
+    torch = torch_cuda()
+    lib = _native.load()
+    k, n = 1152, 6912
+    blocks = synth.random_q4_0(n, k, seed=77)
+    codes, scales = repacked(blocks, n, k)
+    whi = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    wlo = torch.empty((n, k), dtype=torch.float16, device="cuda")
+    _native.check(lib.fz_q4_0_to_f16(codes.data_ptr(), scales.data_ptr(), n, k, whi.data_ptr(), wlo.data_ptr(),
+                                     stream()))
+    x = np.random.default_rng(m + 1).standard_normal((m, k)).astype(np.float32)
+    hi, lo = split_dev(x)
+    y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _native.check(lib.fz_f16_gemm(whi.data_ptr(), wlo.data_ptr() if passes == 3 else None, n, k, hi.data_ptr(),
+                                  lo.data_ptr() if passes >= 2 else None, 1 if passes == 3 else 0, m, y.data_ptr(),
+                                  err.data_ptr(), stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = y.cpu().numpy()
+    want = oracle.matmul(blocks, n, k, x)
+    rel = np.sqrt(np.mean((got.astype(np.float64) - want) ** 2)) / np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    assert np.isfinite(got).all()
+    assert rel < {1: 1e-3, 2: 5e-4, 3: 5e-5}[passes], rel
+
+
+def test_f16_weight_gated_with_edits():
+    torch = torch_cuda()
+    lib = _native.load()
+    m, position, f, k = 200, 7, 6912, 1152
+    gate = synth.random_q4_0(f, k, seed=1)
+    up = synth.random_q4_0(f, k, seed=2)
+    x = np.random.default_rng(5).standard_normal((m, k)).astype(np.float32) * np.float32(0.05)
+    mats = []
+    for b in (gate, up):
+        c, s = repacked(b, f, k)
+        whi = torch.empty((f, k), dtype=torch.float16, device="cuda")
+        wlo = torch.empty((f, k), dtype=torch.float16, device="cuda")
+        _native.check(lib.fz_q4_0_to_f16(c.data_ptr(), s.data_ptr(), f, k, whi.data_ptr(), wlo.data_ptr(), stream()))
+        mats.append((whi, wlo))
+    edits = [Edit(1, nn, [SET, SCALE, ZERO][nn % 3], [nn * 0.5, -1.75, 0.0][nn % 3], 0, 6) for nn in range(10, 90)]
+    words = np.array(table(edits, 3, 40), dtype=np.uint32)
+    td = dev(words.view(np.int32))
+    hi, lo = split_dev(x)
+    act = torch.empty((m, f), dtype=torch.float32, device="cuda")
+    ahi = torch.empty((m, f), dtype=torch.float16, device="cuda")
+    alo = torch.empty((m, f), dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    (ghi, glo), (uhi, ulo) = mats
+    _native.check(lib.fz_f16_gemm_gated(ghi.data_ptr(), glo.data_ptr(), uhi.data_ptr(), ulo.data_ptr(), f, k,
+                                        hi.data_ptr(), lo.data_ptr(), 1, m, td.data_ptr(), 1, position,
+                                        act.data_ptr(), ahi.data_ptr(), alo.data_ptr(), err.data_ptr(), stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = act.cpu().numpy()
+    want = oracle.edit_apply(words, 1, position, oracle.gated(gate, up, f, k, x))
+    rel = np.sqrt(np.mean((got.astype(np.float64) - want) ** 2)) / np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    assert rel < 1e-5, rel
