@@ -250,6 +250,19 @@ FZ_DEV bool cbar_or(bool p) {
   return r != 0;
 }
 
+// Flag-in-data words: a value and the epoch of the phase that wrote it, one
+// 8-byte single-copy-atomic store (no fence); a reader polls the word until
+// the epoch is the one it expects.  Epoch = launch serial << 8 | layer << 3 |
+// phase, so a word left by an earlier layer, launch or step never passes.
+FZ_DEV uint32_t phase_epoch(uint32_t serial, uint32_t l, uint32_t ph) { return (serial << 8) | (l << 3) | ph; }
+FZ_DEV void st_ll(unsigned long long* p, float v, uint32_t epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+FZ_DEV void ld_ll2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 // A phase counter: wait (thread 0) until it reaches `target`.
 FZ_DEV bool wait_counter(const uint32_t* ctr, uint32_t target, uint32_t* err) {
   const uint64_t t0 = now_ns();
@@ -762,7 +775,7 @@ constexpr uint32_t kFoldInO = 8;
 template <int GH, int NB>
 struct Attn {
   const DecodeArgs& a;
-  uint32_t M, pos, W, kps;
+  uint32_t M, pos, W, kps, serial;
   uint32_t kvp, kvf;   // per chunk buffer: bit b the parity its next completion has, bit b a copy in flight
   const unsigned char* kmap;  // the layer's key cache tensor map (the value map follows)
   unsigned long long wait_ns; // traced: thread 0's time waiting for chunks
@@ -900,11 +913,7 @@ struct Attn {
       stage_first(l, row, kvh, j0, j1);
     }
     stamp(l, 1, 0);
-    if (tid == 0 && !wait_counter(sync_of(l) + kSyncQkv, active_ctas(L.qkv.n / 16, 1, G), a.error)) fail = true;
-    if (sync_dead()) {
-      drain();
-      return;
-    }
+    // (no counter: each item's warps poll their QKV words)
     stamp(l, 1, 1);
     bool staged = true;
 #pragma unroll 1
@@ -934,9 +943,32 @@ struct Attn {
     float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
     if (warp < GH + 2) {
       const int head = warp < GH ? (int)(kvh * GH) + warp : (warp == GH ? (int)(H + kvh) : (int)(H + KV + kvh));
-      const float* src = a.qkv + (size_t)row * ((H + 2 * KV) * kHd) + head * kHd;
-      va = __ldcg(reinterpret_cast<const float4*>(src) + lane);
-      vb = __ldcg(reinterpret_cast<const float4*>(src + kHd / 2) + lane);
+      // The head's 256 products, polled until all carry this layer's QKV epoch (bounded).
+      const unsigned long long* src = a.qkv_ll + (size_t)row * ((H + 2 * KV) * kHd) + head * kHd;
+      const uint32_t want = phase_epoch(serial, l, kPhQkv);
+      unsigned long long w[8];
+      const uint64_t t0 = now_ns();
+#pragma unroll 1
+      for (uint32_t it = 0;; it++) {
+        ld_ll2(src + 4 * lane, w[0], w[1]);
+        ld_ll2(src + 4 * lane + 2, w[2], w[3]);
+        ld_ll2(src + kHd / 2 + 4 * lane, w[4], w[5]);
+        ld_ll2(src + kHd / 2 + 4 * lane + 2, w[6], w[7]);
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < 8; j++) ok = ok && (uint32_t)(w[j] >> 32) == want;
+        if (__all_sync(0xffffffffu, ok)) break;
+        if ((it & 15u) == 15u && (flags()[0] || error_word(a.error) || now_ns() - t0 > kWaitNs)) {
+          if (lane == 0 && !flags()[0] && !error_word(a.error)) atomicOr(a.error, kErrCounter);
+          fail = true;
+          break;
+        }
+        __nanosleep(32);
+      }
+      va = make_float4(__uint_as_float((uint32_t)w[0]), __uint_as_float((uint32_t)w[1]),
+                       __uint_as_float((uint32_t)w[2]), __uint_as_float((uint32_t)w[3]));
+      vb = make_float4(__uint_as_float((uint32_t)w[4]), __uint_as_float((uint32_t)w[5]),
+                       __uint_as_float((uint32_t)w[6]), __uint_as_float((uint32_t)w[7]));
       if (warp <= GH) rope_apply(va, vb, ga, gb, tt, a.eps, (int)kHd, pos, lane);
       if (warp < GH) {
         if (last && a.capture) {
@@ -1213,6 +1245,7 @@ __device__ __noinline__ uint32_t attention_layer(const DecodeArgs& a, uint32_t l
   uint32_t* kvstate = reinterpret_cast<uint32_t*>(g_smem + a.lay.kvstate);
   s.kvp = kvstate[0];
   s.kvf = kvstate[1];
+  s.serial = kvstate[3];
   s.M = a.m;
   s.pos = pos;
   s.W = kDecodeSyncFixed + a.m * a.kv_heads;
@@ -1318,6 +1351,7 @@ struct Consumer {
   FZ_DEV volatile uint32_t* flags() const { return reinterpret_cast<volatile uint32_t*>(g_smem + a.lay.flags); }
   FZ_DEV uint32_t* tags() const { return reinterpret_cast<uint32_t*>(g_smem + a.lay.tags); }
   FZ_DEV uint32_t* uses() const { return reinterpret_cast<uint32_t*>(g_smem + a.lay.uses); }
+  FZ_DEV uint32_t serial() const { return reinterpret_cast<const uint32_t*>(g_smem + a.lay.kvstate)[3]; }
   int tid, warp, lane, g, t;
   bool fail, dead;
   float acc[2][MQ][2];
@@ -1517,7 +1551,7 @@ struct Consumer {
         float v = 0.f;
         for (int w = 0; w < kCW; w++) v = add(v, rs[w * (16 * C) + row * C + tok]);
         if (kind == kPhQkv) {
-          a.qkv[(size_t)tok * ((a.heads + 2 * a.kv_heads) * kHd) + n] = v;
+          st_ll(a.qkv_ll + (size_t)tok * ((a.heads + 2 * a.kv_heads) * kHd) + n, v, phase_epoch(serial(), l, kPhQkv));
         } else if (kind == kPhO) {
           a.y_attn[((size_t)task_d * M + tok) * Hd + n] = v;
         } else if (kind == kPhDown) {
@@ -1560,9 +1594,10 @@ struct Consumer {
       stamp(a.n_layers - 1, 5, 4);
       return;
     }
-    // The flush's barrier has ordered every consumer's stores.
+    // The flush's barrier has ordered every consumer's stores.  (QKV's
+    // products are flag-in-data words: no counter.)
     const uint32_t which = kind == kPhQkv ? kSyncQkv : kind == kPhO ? kSyncO : kind == kPhGate ? kSyncGate : kSyncDown;
-    if (tid == 0) raise_counter(sync_of(l) + which);
+    if (tid == 0 && kind != kPhQkv) raise_counter(sync_of(l) + which);
     stamp(l, trace_phase(kind), 4);
   }
 
@@ -1643,6 +1678,7 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
     uint32_t* kvstate = reinterpret_cast<uint32_t*>(g_smem + ly.kvstate);
     for (uint32_t b = 0; b < kv_bufs(MQ); b++) mb_init(kvbar + b, 1);
     kvstate[0] = kvstate[1] = kvstate[2] = 0u;
+    kvstate[3] = a.step->padding[0];   // the step serial (epochs)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x < kDecodeMaxRows) best[threadIdx.x] = 0ull;

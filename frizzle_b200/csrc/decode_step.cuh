@@ -61,7 +61,11 @@ struct DecodeArgs {
   float eps, scale_log2e;
   float* hidden_a;                 // [m][hidden]: the embedding rows in, the residual stream
   float* hidden_b;                 // [m][hidden]
-  float* qkv;                      // [m][(heads + 2 kv_heads) 256] raw products
+  float* qkv;                      // [m][(heads + 2 kv_heads) 256] raw products (unused by the kernel)
+  // The QKV products as flag-in-data words: value bits low, the producing
+  // phase's epoch high ([kDecodeMaxRows][(heads + 2 kv_heads) 256]); the
+  // attention polls them instead of a phase counter.
+  unsigned long long* qkv_ll;       // (the epochs' step serial is step->padding[0], set by the engine)
   float* attn;                     // [m][heads 256]
   float* y_attn;                   // [kDecodeOSlices][m][hidden] output-projection partials
   float* act;                      // [m][ffn]

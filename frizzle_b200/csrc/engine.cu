@@ -204,6 +204,8 @@ struct fz_batch {
   } slot[2];
   int next_slot = 0;
   int last_slot = -1;
+  uint32_t serial = 1;             // steps run (the decode kernel's epochs)
+  unsigned long long* qkv_ll = nullptr;  // the decode kernel's QKV words (flag-in-data)
   std::map<GraphKey, cudaGraphExec_t> graphs;
   std::vector<void*> allocations;
 
@@ -477,6 +479,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     d.hidden_a = b.hidden_a;
     d.hidden_b = b.hidden_b;
     d.qkv = b.qkv;
+    d.qkv_ll = b.qkv_ll;
     d.attn = b.attn;
     d.y_attn = b.y_parts;
     d.act = b.act;
@@ -1076,7 +1079,8 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
       if (s.head_dim == 256 && !fz::make_kv_maps(maps[l], d, s.kv_heads, sequences))
         return fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled refused the key/value cache maps");
     }
-    if ((st = b->alloc(&b->dlayers, dl.size() * sizeof(fz::DecodeLayer))) ||
+    if ((st = b->alloc(&b->qkv_ll, (size_t)fz::kDecodeMaxRows * (s.heads + 2 * s.kv_heads) * s.head_dim * 8)) ||
+        (st = b->alloc(&b->dlayers, dl.size() * sizeof(fz::DecodeLayer))) ||
         (st = b->alloc(&b->kv_maps, maps.size() * sizeof(fz::DecodeKvMaps))))
       return st;
     if (fz::decode_supported(1, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim))
@@ -1212,6 +1216,7 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   auto& sl = b->slot[b->next_slot];
   if (sl.used) FZ_CUDA(cudaEventSynchronize(sl.copied));
   std::memcpy(sl.step, step, sizeof(DeviceStep));
+  sl.step->padding[0] = b->serial++;   // a new epoch for the decode kernel's flag-in-data words
   if (!step->fed) std::memcpy(sl.ids, ids, (size_t)T * b->S * 4);
   for (uint32_t i = 0; i < b->S; i++) {
     sl.seeds[2 * i] = seeds ? seeds[2 * i] : step->seed[0];

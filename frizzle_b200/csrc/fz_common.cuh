@@ -19,7 +19,7 @@ struct DeviceStep {
   uint32_t top_k;
   float temperature, top_p, min_p, log_min_p;
   uint32_t capture;
-  uint32_t padding[4];
+  uint32_t padding[4];   // [0]: the engine's step serial on the device copy (flag-in-data epochs)
 };
 static_assert(sizeof(DeviceStep) == 64, "the step head is 64 bytes");
 
