@@ -255,6 +255,7 @@ FZ_DEV bool cbar_or(bool p) {
 // the epoch is the one it expects.  Epoch = launch serial << 8 | layer << 3 |
 // phase, so a word left by an earlier layer, launch or step never passes.
 FZ_DEV uint32_t phase_epoch(uint32_t serial, uint32_t l, uint32_t ph) { return (serial << 8) | (l << 3) | ph; }
+constexpr uint32_t kEpAttn = 5;   // the attention's epoch phase (QKV, gate/up use their phase numbers)
 FZ_DEV void st_ll(unsigned long long* p, float v, uint32_t epoch) {
   const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
@@ -745,10 +746,84 @@ __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const fl
   }
 }
 
+// The same from flag-in-data words (another phase's output, this launch):
+// each item's words are polled until all carry `want` (bounded), two items a
+// thread at a time when the fragments are one row quad.
+template <int MQ>
+__device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const unsigned long long* src, uint32_t K,
+                                          uint32_t kb0, uint32_t nkb, uint32_t want) {
+  const int tid = threadIdx.x, items = (int)nkb * 8;
+  uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
+  const volatile uint32_t* abort = reinterpret_cast<const volatile uint32_t*>(g_smem + a.lay.flags);
+  constexpr int U = 1;
+#pragma unroll 1
+  for (int i0 = tid; i0 < items; i0 += U * kCT) {
+    float4 v[U][MQ][4];
+    const uint64_t t0 = now_ns();
+#pragma unroll 1
+    for (uint32_t it = 0;; it++) {
+      bool ok = true;
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * kCT;
+        const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
+#pragma unroll
+        for (int q = 0; q < MQ; q++)
+#pragma unroll
+          for (int gp = 0; gp < 4; gp++) {
+            const int r = 4 * q + gp;
+            v[u][q][gp] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < items && r < (int)M) {
+              const unsigned long long* row = src + (size_t)r * K + 32 * (kb0 + kb_rel) + 8 * h + 2 * tq;
+              unsigned long long w0, w1, w2, w3;
+              ld_ll2(row, w0, w1);
+              ld_ll2(row + 16, w2, w3);
+              ok = ok && (uint32_t)(w0 >> 32) == want && (uint32_t)(w1 >> 32) == want &&
+                   (uint32_t)(w2 >> 32) == want && (uint32_t)(w3 >> 32) == want;
+              v[u][q][gp] = make_float4(__uint_as_float((uint32_t)w0), __uint_as_float((uint32_t)w1),
+                                        __uint_as_float((uint32_t)w2), __uint_as_float((uint32_t)w3));
+            }
+          }
+      }
+      if (ok) break;
+      if ((it & 15u) == 15u && (*abort || error_word(a.error) || now_ns() - t0 > kWaitNs)) {
+        if (!*abort && !error_word(a.error)) atomicOr(a.error, kErrCounter);
+        break;
+      }
+      __nanosleep(it < 4 ? 64u : 256u);
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const int i = i0 + u * kCT;
+      if (i >= items) break;
+      const int kb_rel = i >> 3, h = (i >> 2) & 1, tq = i & 3;
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        uint2 col[8];
+#pragma unroll
+        for (int gp = 0; gp < 4; gp++) {
+          const float4 w = v[u][q][gp];
+          __half h0, h1, h2, h3, l0, l1, l2, l3;
+          split_hi_lo(w.x, h0, l0);
+          split_hi_lo(w.y, h1, l1);
+          split_hi_lo(w.z, h2, l2);
+          split_hi_lo(w.w, h3, l3);
+          col[2 * gp] = pack4(h0, h1, h2, h3);
+          col[2 * gp + 1] = pack4(l0, l1, l2, l3);
+        }
+        uint4* dst = xf + (((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8) / 2;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+          dst[k] = make_uint4(col[2 * k].x, col[2 * k].y, col[2 * k + 1].x, col[2 * k + 1].y);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ attention
 
 __device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uint32_t nsplit, uint32_t c0,
-                                            uint32_t nc);
+                                            uint32_t nc, uint32_t want);
 
 // The step's key splits for one layer: keys from a0 (the earliest key the
 // window keeps, rounded down to a chunk; keys before it are masked) to pos,
@@ -767,7 +842,7 @@ FZ_DEV uint32_t attn_splits(const DecodeArgs& a, const DecodeLayer& L, uint32_t 
 }
 // Up to this many splits, the output projection's CTAs fold the splits as
 // they stage their slice of the attention rows (no fold in the attention).
-constexpr uint32_t kFoldInO = 8;
+constexpr uint32_t kFoldInO = kDecodeFoldSplits;
 
 // The step's attention for one layer: the CTAs with work items wait for the
 // layer's QKV counter.  Run in a function of its own (attention_layer), so
@@ -1136,10 +1211,16 @@ struct Attn {
       if (g < GH) {
         const uint32_t head = kvh * GH + g, dim = 32 * warp + 8 * i + 2 * t;
         const float o0 = add(acc[i][0], r0), o1 = add(acc[i][1], r1);
+        const uint32_t ep = phase_epoch(serial, l, kEpAttn);
         if (nsplit == 1) {
           const float lsum = hstat()[GH + g];
-          *reinterpret_cast<float2*>(a.attn + ((size_t)row * H + head) * kHd + dim) =
-              make_float2(__fdiv_rn(o0, lsum), __fdiv_rn(o1, lsum));
+          unsigned long long* o = a.attn_ll + ((size_t)row * H + head) * kHd + dim;
+          st_ll(o, __fdiv_rn(o0, lsum), ep);
+          st_ll(o + 1, __fdiv_rn(o1, lsum), ep);
+        } else if (nsplit <= kFoldInO) {
+          unsigned long long* o = a.part_o_ll + (((size_t)row * H + head) * kFoldInO + split) * kHd + dim;
+          st_ll(o, o0, ep);
+          st_ll(o + 1, o1, ep);
         } else {
           const size_t at = ((size_t)row * H + head) * a.max_splits + split;
           *reinterpret_cast<float2*>(a.partial_o + at * kHd + dim) = make_float2(o0, o1);
@@ -1147,13 +1228,19 @@ struct Attn {
       }
     }
     if (nsplit > 1 && tid < GH) {
-      const size_t at = ((size_t)row * H + kvh * GH + tid) * a.max_splits + split;
-      a.partial_ml[at * 2] = hstat()[tid];
-      a.partial_ml[at * 2 + 1] = hstat()[GH + tid];
+      if (nsplit <= kFoldInO) {
+        unsigned long long* ml = a.part_ml_ll + (((size_t)row * H + kvh * GH + tid) * kFoldInO + split) * 2;
+        st_ll(ml, hstat()[tid], phase_epoch(serial, l, kEpAttn));
+        st_ll(ml + 1, hstat()[GH + tid], phase_epoch(serial, l, kEpAttn));
+      } else {
+        const size_t at = ((size_t)row * H + kvh * GH + tid) * a.max_splits + split;
+        a.partial_ml[at * 2] = hstat()[tid];
+        a.partial_ml[at * 2 + 1] = hstat()[GH + tid];
+      }
     }
-    // One split, or few (the output projection folds them): every item
-    // raises the layer's attention counter.  Many: the last of (row, kvh)
-    // folds them and raises it once.
+    // One split, or few (the output projection folds them): the item's
+    // words are its output.  Many: the last of (row, kvh) folds them into
+    // the output words.
     bool final_cta = nsplit <= kFoldInO;
     if (!final_cta) {
       cbar();
@@ -1165,13 +1252,10 @@ struct Attn {
       final_cta = flags()[1] != 0;
       if (final_cta) {
         __threadfence();
-        combine(row, kvh, nsplit);
+        combine(row, kvh, nsplit, l);
       }
     }
-    if (final_cta) {
-      cbar();
-      if (tid == 0) raise_counter(sync_of(l) + kSyncAttn);
-    }
+
     // Another item's copies follow: order this item's generic stores into
     // the buffers (the new key, the fold's weights) before them.
     if (more && wrote) fence_proxy_async();
@@ -1183,7 +1267,7 @@ struct Attn {
   // maxima and sums (lanes stride the splits, then a fixed-order shuffle
   // tree), then each thread one head's four dimensions, its split loads in
   // flight together.
-  FZ_DEV void combine(uint32_t row, uint32_t kvh, uint32_t nsplit) {
+  FZ_DEV void combine(uint32_t row, uint32_t kvh, uint32_t nsplit, uint32_t cur_l) {
     const uint32_t H = a.heads;
     float* fac = reinterpret_cast<float*>(ks(0));  // [GH][nsplit] weights, then [GH] sums
     float* lsum = fac + GH * nsplit;
@@ -1232,8 +1316,12 @@ struct Attn {
                           __fmaf_rn(v.w, f, acc.w));
       }
       const float ls = lsum[h];
-      reinterpret_cast<float4*>(a.attn + ((size_t)row * H + kvh * GH + h) * kHd)[d4] =
-          make_float4(__fdiv_rn(acc.x, ls), __fdiv_rn(acc.y, ls), __fdiv_rn(acc.z, ls), __fdiv_rn(acc.w, ls));
+      unsigned long long* o = a.attn_ll + ((size_t)row * H + kvh * GH + h) * kHd + 4 * d4;
+      const uint32_t ep = phase_epoch(serial, cur_l, kEpAttn);
+      st_ll(o, __fdiv_rn(acc.x, ls), ep);
+      st_ll(o + 1, __fdiv_rn(acc.y, ls), ep);
+      st_ll(o + 2, __fdiv_rn(acc.z, ls), ep);
+      st_ll(o + 3, __fdiv_rn(acc.w, ls), ep);
     }
   }
 };
@@ -1276,27 +1364,51 @@ __device__ __noinline__ uint32_t attention_layer(const DecodeArgs& a, uint32_t l
 // sums and outputs loaded at a time, rescaling its running sum to each new
 // maximum (the fold of attention.wgsl:403-438, online).
 __device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uint32_t nsplit, uint32_t c0,
-                                            uint32_t nc) {
+                                            uint32_t nc, uint32_t want) {
   const uint32_t H = a.heads, n4 = nc / 4;
   float4* out = reinterpret_cast<float4*>(smem_f(a.lay.rowbuf));
+  const volatile uint32_t* abort = reinterpret_cast<const volatile uint32_t*>(g_smem + a.lay.flags);
 #pragma unroll 1
   for (uint32_t i = threadIdx.x; i < M * n4; i += kCT) {
     const uint32_t r = i / n4, c = c0 + 4 * (i % n4), h = c / kHd;
-    const size_t base = ((size_t)r * H + h) * a.max_splits;
-    const float2* ml = reinterpret_cast<const float2*>(a.partial_ml) + base;
-    const float4* po = reinterpret_cast<const float4*>(a.partial_o + base * kHd + c % kHd);
+    const size_t base = ((size_t)r * H + h) * kFoldInO;
+    const unsigned long long* ml = a.part_ml_ll + base * 2;
+    const unsigned long long* po = a.part_o_ll + base * kHd + c % kHd;
     float m = -INFINITY, l = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
     for (uint32_t s0 = 0; s0 < nsplit; s0 += 2) {
       float2 w[2];
       float4 v[2];
+      // Two splits' words at once, polled until all carry the attention's epoch.
+      const uint64_t t0 = now_ns();
+#pragma unroll 1
+      for (uint32_t it = 0;; it++) {
+        unsigned long long q[2][6];
+        bool ok = true;
+#pragma unroll 1
+        for (uint32_t s = 0; s < 2; s++)
+          if (s0 + s < nsplit) {
+            ld_ll2(ml + (s0 + s) * 2, q[s][0], q[s][1]);
+            ld_ll2(po + (size_t)(s0 + s) * kHd, q[s][2], q[s][3]);
+            ld_ll2(po + (size_t)(s0 + s) * kHd + 2, q[s][4], q[s][5]);
+          }
 #pragma unroll
-      for (uint32_t s = 0; s < 2; s++)
-        if (s0 + s < nsplit) {
-          w[s] = __ldcg(ml + s0 + s);
-          v[s] = __ldcg(po + (size_t)(s0 + s) * (kHd / 4));
+        for (uint32_t s = 0; s < 2; s++)
+          if (s0 + s < nsplit) {
+#pragma unroll
+            for (int j = 0; j < 6; j++) ok = ok && (uint32_t)(q[s][j] >> 32) == want;
+            w[s] = make_float2(__uint_as_float((uint32_t)q[s][0]), __uint_as_float((uint32_t)q[s][1]));
+            v[s] = make_float4(__uint_as_float((uint32_t)q[s][2]), __uint_as_float((uint32_t)q[s][3]),
+                               __uint_as_float((uint32_t)q[s][4]), __uint_as_float((uint32_t)q[s][5]));
+          }
+        if (ok) break;
+        if ((it & 15u) == 15u && (*abort || error_word(a.error) || now_ns() - t0 > kWaitNs)) {
+          if (!*abort && !error_word(a.error)) atomicOr(a.error, kErrCounter);
+          break;
         }
+        __nanosleep(32);
+      }
 #pragma unroll
       for (uint32_t s = 0; s < 2; s++)
         if (s0 + s < nsplit) {
@@ -1317,12 +1429,12 @@ __device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uin
 // their key splits when there are few.
 template <int MQ>
 __device__ __noinline__ void attention_fragments(const DecodeArgs& a, uint32_t M, uint32_t nsplit, uint32_t kb0,
-                                                 uint32_t nkb) {
+                                                 uint32_t nkb, uint32_t want) {
   if (nsplit > 1 && nsplit <= kFoldInO) {
-    fold_attention(a, M, nsplit, kb0 * 32u, nkb * 32u);
+    fold_attention(a, M, nsplit, kb0 * 32u, nkb * 32u, want);
     fragments<MQ, false>(a, M, smem_f(a.lay.rowbuf), nkb * 32u, 0, nkb);
   } else {
-    fragments<MQ, true>(a, M, a.attn, a.heads * kHd, kb0, nkb);
+    fragments_ll<MQ>(a, M, a.attn_ll, a.heads * kHd, kb0, nkb, want);
   }
 }
 
@@ -1396,18 +1508,16 @@ struct Consumer {
       }
       gain = L.attn_norm;
     } else if (kind == kPhO) {
-      ctr = sync_of(l) + kSyncAttn;
+      // (no counter: the attention's output words are polled)
       uint32_t a0, kps;
       o_splits = attn_splits(a, L, pos, M, G, a0, kps);
-      target = M * a.kv_heads * (o_splits <= kFoldInO ? o_splits : 1u);
     } else if (kind == kPhGate) {
       ctr = sync_of(l) + kSyncO;
       target = active_ctas(L.o.n / 16, kDecodeOSlices, G);
       pg = L.post_attn_norm;
       gain = L.ffn_norm;
     } else if (kind == kPhDown) {
-      ctr = sync_of(l) + kSyncGate;
-      target = active_ctas(L.gate.n / 16, 1, G);
+      // (no counter: the activation words are polled)
     } else {
       ctr = sync_of(Ln - 1) + kSyncDown;
       target = active_ctas(L.down.n / 16, kDecodeDownSlices, G);
@@ -1447,9 +1557,9 @@ struct Consumer {
       norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, none, (Ln - 1) * per + a.cap_mlp_added);
       fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
     } else if (kind == kPhO) {
-      attention_fragments<MQ>(a, M, o_splits, kb0, nkb);
+      attention_fragments<MQ>(a, M, o_splits, kb0, nkb, phase_epoch(serial(), l, kEpAttn));
     } else {
-      fragments<MQ, true>(a, M, a.act, a.ffn, kb0, nkb);
+      fragments_ll<MQ>(a, M, a.act_ll, a.ffn, kb0, nkb, phase_epoch(serial(), l, kPhGate));
     }
     cbar();
     stamp(tl, trace_phase(kind), 2);
@@ -1564,7 +1674,7 @@ struct Consumer {
           for (int w = 0; w < kCW; w++) up = add(up, rs[kRedHalf + w * (16 * C) + row * C + tok]);
           v = mul(gelu_tanh(v), up);
           if (a.edit_table) v = apply_edits(a.edit_table + (size_t)tok * a.table_stride, l, n, pos, v);
-          a.act[(size_t)tok * a.ffn + n] = v;
+          st_ll(a.act_ll + (size_t)tok * a.ffn + n, v, phase_epoch(serial(), l, kPhGate));
           if (a.capture) a.capture[(size_t)tok * a.capture_stride + l * a.cap_per_layer + a.cap_neurons + n] = v;
         }
       }
@@ -1597,7 +1707,7 @@ struct Consumer {
     // The flush's barrier has ordered every consumer's stores.  (QKV's
     // products are flag-in-data words: no counter.)
     const uint32_t which = kind == kPhQkv ? kSyncQkv : kind == kPhO ? kSyncO : kind == kPhGate ? kSyncGate : kSyncDown;
-    if (tid == 0 && kind != kPhQkv) raise_counter(sync_of(l) + which);
+    if (tid == 0 && kind != kPhQkv && kind != kPhGate) raise_counter(sync_of(l) + which);
     stamp(l, trace_phase(kind), 4);
   }
 

@@ -44,6 +44,7 @@ constexpr uint32_t kDecodeSyncFixed = 8;    // per-layer phase counters
 constexpr uint32_t kDecodeMaxGroup = 6;     // query heads a KV head may serve
 constexpr uint32_t kDecodeSplitKeys = 64;   // fewest keys of a split attention item
 constexpr uint32_t kDecodeMaxSplits = 256;  // key splits the partial buffers are sized for
+constexpr uint32_t kDecodeFoldSplits = 8;   // up to this many, the output projection folds the splits
 
 // Byte offsets of the decode kernel's shared-memory regions (set by the launch).
 struct DecodeLayout {
@@ -66,6 +67,13 @@ struct DecodeArgs {
   // phase's epoch high ([kDecodeMaxRows][(heads + 2 kv_heads) 256]); the
   // attention polls them instead of a phase counter.
   unsigned long long* qkv_ll;       // (the epochs' step serial is step->padding[0], set by the engine)
+  // The attention's output [kDecodeMaxRows][heads 256], and for 2..8 key
+  // splits its split partials [rows][heads][8][256] and (max, sum) pairs
+  // [rows][heads][8][2], all as flag-in-data words the output projection polls.
+  unsigned long long* attn_ll;
+  unsigned long long* act_ll;      // the gated activation [kDecodeMaxRows][ffn] (flag-in-data)
+  unsigned long long* part_o_ll;
+  unsigned long long* part_ml_ll;
   float* attn;                     // [m][heads 256]
   float* y_attn;                   // [kDecodeOSlices][m][hidden] output-projection partials
   float* act;                      // [m][ffn]

@@ -205,7 +205,10 @@ struct fz_batch {
   int next_slot = 0;
   int last_slot = -1;
   uint32_t serial = 1;             // steps run (the decode kernel's epochs)
-  unsigned long long* qkv_ll = nullptr;  // the decode kernel's QKV words (flag-in-data)
+  // The decode kernel's flag-in-data words: QKV products, attention output and
+  // few-split partials, gated activation.
+  unsigned long long *qkv_ll = nullptr, *attn_ll = nullptr, *part_o_ll = nullptr, *part_ml_ll = nullptr,
+                     *act_ll = nullptr;
   std::map<GraphKey, cudaGraphExec_t> graphs;
   std::vector<void*> allocations;
 
@@ -480,6 +483,10 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     d.hidden_b = b.hidden_b;
     d.qkv = b.qkv;
     d.qkv_ll = b.qkv_ll;
+    d.attn_ll = b.attn_ll;
+    d.act_ll = b.act_ll;
+    d.part_o_ll = b.part_o_ll;
+    d.part_ml_ll = b.part_ml_ll;
     d.attn = b.attn;
     d.y_attn = b.y_parts;
     d.act = b.act;
@@ -1079,7 +1086,11 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
       if (s.head_dim == 256 && !fz::make_kv_maps(maps[l], d, s.kv_heads, sequences))
         return fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled refused the key/value cache maps");
     }
-    if ((st = b->alloc(&b->qkv_ll, (size_t)fz::kDecodeMaxRows * (s.heads + 2 * s.kv_heads) * s.head_dim * 8)) ||
+    const size_t R8 = (size_t)fz::kDecodeMaxRows * 8;   // rows x bytes a word
+    if ((st = b->alloc(&b->qkv_ll, R8 * (s.heads + 2 * s.kv_heads) * s.head_dim)) ||
+        (st = b->alloc(&b->attn_ll, R8 * s.heads * s.head_dim)) || (st = b->alloc(&b->act_ll, R8 * s.ffn)) ||
+        (st = b->alloc(&b->part_o_ll, R8 * s.heads * fz::kDecodeFoldSplits * s.head_dim)) ||
+        (st = b->alloc(&b->part_ml_ll, R8 * s.heads * fz::kDecodeFoldSplits * 2)) ||
         (st = b->alloc(&b->dlayers, dl.size() * sizeof(fz::DecodeLayer))) ||
         (st = b->alloc(&b->kv_maps, maps.size() * sizeof(fz::DecodeKvMaps))))
       return st;
