@@ -755,7 +755,7 @@ __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const
   const int tid = threadIdx.x, items = (int)nkb * 8;
   uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
   const volatile uint32_t* abort = reinterpret_cast<const volatile uint32_t*>(g_smem + a.lay.flags);
-  constexpr int U = 1;
+  constexpr int U = MQ == 1 ? 2 : 1;
 #pragma unroll 1
   for (int i0 = tid; i0 < items; i0 += U * kCT) {
     float4 v[U][MQ][4];
@@ -843,6 +843,10 @@ FZ_DEV uint32_t attn_splits(const DecodeArgs& a, const DecodeLayer& L, uint32_t 
 // Up to this many splits, the output projection's CTAs fold the splits as
 // they stage their slice of the attention rows (no fold in the attention).
 constexpr uint32_t kFoldInO = kDecodeFoldSplits;
+// One-row steps with 2..kFoldInO splits fold them in the output projection's
+// prologue (a thread an item); with more rows the prologue would fold four
+// items a thread, so the attention's last CTA of each (row, KV head) folds.
+FZ_DEV bool fold_in_o(uint32_t nsplit, uint32_t M) { return nsplit > 1 && nsplit <= kFoldInO && M == 1; }
 
 // The step's attention for one layer: the CTAs with work items wait for the
 // layer's QKV counter.  Run in a function of its own (attention_layer), so
@@ -1217,7 +1221,7 @@ struct Attn {
           unsigned long long* o = a.attn_ll + ((size_t)row * H + head) * kHd + dim;
           st_ll(o, __fdiv_rn(o0, lsum), ep);
           st_ll(o + 1, __fdiv_rn(o1, lsum), ep);
-        } else if (nsplit <= kFoldInO) {
+        } else if (fold_in_o(nsplit, M)) {
           unsigned long long* o = a.part_o_ll + (((size_t)row * H + head) * kFoldInO + split) * kHd + dim;
           st_ll(o, o0, ep);
           st_ll(o + 1, o1, ep);
@@ -1228,7 +1232,7 @@ struct Attn {
       }
     }
     if (nsplit > 1 && tid < GH) {
-      if (nsplit <= kFoldInO) {
+      if (fold_in_o(nsplit, M)) {
         unsigned long long* ml = a.part_ml_ll + (((size_t)row * H + kvh * GH + tid) * kFoldInO + split) * 2;
         st_ll(ml, hstat()[tid], phase_epoch(serial, l, kEpAttn));
         st_ll(ml + 1, hstat()[GH + tid], phase_epoch(serial, l, kEpAttn));
@@ -1238,10 +1242,10 @@ struct Attn {
         a.partial_ml[at * 2 + 1] = hstat()[GH + tid];
       }
     }
-    // One split, or few (the output projection folds them): the item's
-    // words are its output.  Many: the last of (row, kvh) folds them into
-    // the output words.
-    bool final_cta = nsplit <= kFoldInO;
+    // One split, or few in a one-row step (the output projection folds
+    // them): the item's words are its output.  Otherwise the last of
+    // (row, kvh) folds the splits into the output words.
+    bool final_cta = nsplit == 1 || fold_in_o(nsplit, M);
     if (!final_cta) {
       cbar();
       if (tid == 0) {
@@ -1430,7 +1434,7 @@ __device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uin
 template <int MQ>
 __device__ __noinline__ void attention_fragments(const DecodeArgs& a, uint32_t M, uint32_t nsplit, uint32_t kb0,
                                                  uint32_t nkb, uint32_t want) {
-  if (nsplit > 1 && nsplit <= kFoldInO) {
+  if (fold_in_o(nsplit, M)) {
     fold_attention(a, M, nsplit, kb0 * 32u, nkb * 32u, want);
     fragments<MQ, false>(a, M, smem_f(a.lay.rowbuf), nkb * 32u, 0, nkb);
   } else {
