@@ -46,6 +46,16 @@ class ModelInfo(C.Structure):
                 ("weight_bytes", C.c_uint64)]
 
 
+class CaptureSlot(C.Structure):
+    _fields_ = [("first", C.c_uint32), ("width", C.c_uint32)]
+
+
+class CaptureSlots(C.Structure):
+    _fields_ = [(n, CaptureSlot) for n in ("neurons", "residual", "attention_added", "mlp_added", "query",
+                                             "weights", "stats", "readout")] + \
+               [(n, C.c_uint32) for n in ("keys", "query_heads", "window", "full_attention")]
+
+
 # Every symbol the header declares, with its signature.
 VP = C.c_void_p
 U32 = C.c_uint32
@@ -70,6 +80,7 @@ SIGNATURES = {
     "fz_batch_read_logits": (C.c_int, [VP, U32, VP, C.c_size_t]),
     "fz_capture_floats": (C.c_size_t, [VP]),
     "fz_batch_read_capture": (C.c_int, [VP, U32, VP, C.c_size_t]),
+    "fz_capture_layout": (C.c_int, [VP, U32, C.POINTER(CaptureSlots)]),
     "fz_batch_cache": (C.c_int, [VP, U32, U32, C.c_int, C.POINTER(VP), C.POINTER(U32)]),
     "fz_batch_trace": (C.c_int, [VP, C.c_int]),
     "fz_batch_read_trace": (C.c_int, [VP, VP, C.c_size_t, C.POINTER(U32), C.POINTER(U32)]),

@@ -512,14 +512,29 @@ FZ_DEV float warp_tree_rms(const float (&P)[8], float width, float eps) {
   return __shfl_sync(0xffffffffu, inverse_sqrt(add(__fdiv_rn(s, width), eps)), 0);
 }
 
+// A capture slot named by (layer << 2) | kind: kind 1 the layer's residual,
+// 2 its attention addition, 3 its feed-forward addition, 0 none.
+constexpr uint32_t kCapNone = 0, kCapResidual = 1, kCapAttnAdded = 2, kCapMlpAdded = 3;
+FZ_DEV uint32_t cap_slot(uint32_t l, uint32_t kind) { return l << 2 | kind; }
+// Layer l's region-2 block in a sequence's capture store: its residual, then
+// the attention addition, the feed-forward addition and the query.
+FZ_DEV uint64_t cap_block(const DecodeArgs& a, uint32_t l) {
+  const uint32_t global = l / a.cap_pattern;
+  return a.cap_region2 + (uint64_t)l * a.cap_block +
+         (uint64_t)a.heads * ((uint64_t)(l - global) * a.cap_keys_local + (uint64_t)global * a.cap_keys_global);
+}
+FZ_DEV uint64_t cap_offset(const DecodeArgs& a, uint32_t c) {
+  return cap_block(a, c >> 2) + (uint64_t)((c & 3) - 1) * a.hidden;
+}
+
 // The norm launch (norm.wgsl:97-198) over the M rows into rowbuf: X plus
 // the post-normed block output (y: the sum of ny K-slice partials, in slice
-// order), written back by CTA 0 with the captures; then X's RMS norm times
-// the gain.  Invocation i (thread i) holds vec4s i, i + 256, ...  The gains
+// order), written back by CTA 0 with the captures (cx, cy: cap_slot names);
+// then X's RMS norm times the gain.  Invocation i (thread i) holds vec4s i, i + 256, ...  The gains
 // were copied to shared memory (gain, then post gain) before the wait; the
 // rows are staged in shared memory with every load in flight at once.
 __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const float* xin, const float* y,
-                                       uint32_t ny, float* xout, uint64_t cap_x, uint64_t cap_y) {
+                                       uint32_t ny, float* xout, uint32_t cx, uint32_t cy) {
   const int tid = threadIdx.x;
   const int Wd = (int)a.hidden, V = Wd / 4, items = (int)M * V;
   const float wf = (float)Wd;
@@ -589,8 +604,8 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
 #pragma unroll 1
     for (int r = 0; r < (int)M; r++) {
       float* capbase = (writer && a.capture) ? a.capture + (size_t)r * a.capture_stride : nullptr;
-      float4* xc = capbase && cap_x != ~0ull ? reinterpret_cast<float4*>(capbase + cap_x) : nullptr;
-      float4* yc = capbase && cap_y != ~0ull ? reinterpret_cast<float4*>(capbase + cap_y) : nullptr;
+      float4* xc = capbase && (cx & 3) ? reinterpret_cast<float4*>(capbase + cap_offset(a, cx)) : nullptr;
+      float4* yc = capbase && (cy & 3) ? reinterpret_cast<float4*>(capbase + cap_offset(a, cy)) : nullptr;
       float4* out4 = writer && xout ? reinterpret_cast<float4*>(xout + (size_t)r * Wd) : nullptr;
       float p = 0.f;
 #pragma unroll
@@ -648,8 +663,8 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
       ryv = warp_tree_rms(P, wf, a.eps);
     }
     float* capbase = (writer && a.capture) ? a.capture + (size_t)r * a.capture_stride : nullptr;
-    float4* xc = capbase && cap_x != ~0ull ? reinterpret_cast<float4*>(capbase + cap_x) : nullptr;
-    float4* yc = capbase && cap_y != ~0ull ? reinterpret_cast<float4*>(capbase + cap_y) : nullptr;
+    float4* xc = capbase && (cx & 3) ? reinterpret_cast<float4*>(capbase + cap_offset(a, cx)) : nullptr;
+    float4* yc = capbase && (cy & 3) ? reinterpret_cast<float4*>(capbase + cap_offset(a, cy)) : nullptr;
     float4* out4 = writer && xout ? reinterpret_cast<float4*>(xout + (size_t)r * Wd) : nullptr;
 #pragma unroll
     for (int i = 0; i < 8; i++) {
@@ -1051,7 +1066,7 @@ struct Attn {
       if (warp <= GH) rope_apply(va, vb, ga, gb, tt, a.eps, (int)kHd, pos, lane);
       if (warp < GH) {
         if (last && a.capture) {
-          float* cq = a.capture + (size_t)row * a.capture_stride + l * a.cap_per_layer + a.cap_query + head * kHd;
+          float* cq = a.capture + (size_t)row * a.capture_stride + cap_block(a, l) + 3 * a.hidden + head * kHd;
           reinterpret_cast<float4*>(cq)[lane] = va;
           reinterpret_cast<float4*>(cq + kHd / 2)[lane] = vb;
         }
@@ -1549,16 +1564,15 @@ struct Consumer {
     pslots = 0;
     ph_kind = kind;
     ph_l = l;
-    const uint64_t none = ~0ull, per = a.cap_per_layer;
     if (kind == kPhQkv) {
-      norm_rows(a, M, a.hidden_a, l > 0 ? a.y_mlp : nullptr, kDecodeDownSlices, a.hidden_b, l * per + a.cap_residual,
-                l > 0 ? (l - 1) * per + a.cap_mlp_added : none);
+      norm_rows(a, M, a.hidden_a, l > 0 ? a.y_mlp : nullptr, kDecodeDownSlices, a.hidden_b,
+                cap_slot(l, kCapResidual), l > 0 ? cap_slot(l - 1, kCapMlpAdded) : kCapNone);
       fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
     } else if (kind == kPhGate) {
-      norm_rows(a, M, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, none, l * per + a.cap_attn_added);
+      norm_rows(a, M, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, kCapNone, cap_slot(l, kCapAttnAdded));
       fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
     } else if (kind == kPhHead) {
-      norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, none, (Ln - 1) * per + a.cap_mlp_added);
+      norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, kCapNone, cap_slot(Ln - 1, kCapMlpAdded));
       fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
     } else if (kind == kPhO) {
       attention_fragments<MQ>(a, M, o_splits, kb0, nkb, phase_epoch(serial(), l, kEpAttn));
@@ -1679,7 +1693,7 @@ struct Consumer {
           v = mul(gelu_tanh(v), up);
           if (a.edit_table) v = apply_edits(a.edit_table + (size_t)tok * a.table_stride, l, n, pos, v);
           st_ll(a.act_ll + (size_t)tok * a.ffn + n, v, phase_epoch(serial(), l, kPhGate));
-          if (a.capture) a.capture[(size_t)tok * a.capture_stride + l * a.cap_per_layer + a.cap_neurons + n] = v;
+          if (a.capture) a.capture[(size_t)tok * a.capture_stride + (size_t)l * a.ffn + n] = v;
         }
       }
       if (kind == kPhHead) {

@@ -86,7 +86,13 @@ struct DecodeArgs {
   uint64_t table_stride;           // words between sequences' tables
   float* capture;                  // sequence 0's capture store, or null
   uint64_t capture_stride;         // floats between sequences' stores
-  uint64_t cap_residual, cap_query, cap_attn_added, cap_neurons, cap_mlp_added, cap_per_layer;
+  // The store's layout (capture.cpp:31-73): layer l's neurons at l * ffn;
+  // its block of residual, attention addition, feed-forward addition and
+  // query (then weights, stats, readout) at cap_region2 + l * cap_block +
+  // heads * (keys of the layers before it), a layer of every cap_pattern
+  // holding cap_keys_global keys a head, the others cap_keys_local.
+  uint64_t cap_region2, cap_block;
+  uint32_t cap_keys_local, cap_keys_global, cap_pattern;
   Q4Matrix head;                   // tied embedding
   const float* output_norm;
   float* logits;                   // [m][vocab], or null for no head

@@ -87,20 +87,56 @@ struct Shape {
   float eps = 0.f, rope_global = 0.f, rope_local = 0.f;
 };
 
-// Per-layer capture layout (floats): residual, query, attention addition,
-// neurons, feed-forward addition.
+// The capture store's layout in 32-bit words (capture::layout,
+// src/core/capture/capture.cpp:31-73): region 1 holds every layer's neurons
+// (its feed-forward width) in layer order; region 2, for each layer in turn,
+// its residual, attention addition and feed-forward addition (the width
+// each), its query (heads x head dimension), its attention weights (heads x
+// keys, keys = min(window, trained context)), its softmax statistics (m then
+// l a head) and its readout (64 pairs of logit bits and token).
+struct CaptureSlot {
+  uint64_t neurons, residual, attn_added, mlp_added, query, weights, stats, readout;
+  uint32_t keys, window;
+};
+constexpr uint32_t kReadoutWords = 128;  // capture::kReadoutWords: 2 x kCandidates
 struct CaptureLayout {
-  uint64_t residual, query, attn_added, neurons, mlp_added, per_layer;
+  std::vector<CaptureSlot> layer;
+  uint64_t words = 0;  // the store, one sequence's
 };
 CaptureLayout capture_layout(const Shape& s) {
-  CaptureLayout c{};
-  c.residual = 0;
-  c.query = s.hidden;
-  c.attn_added = c.query + (uint64_t)s.heads * s.head_dim;
-  c.neurons = c.attn_added + s.hidden;
-  c.mlp_added = c.neurons + s.ffn;
-  c.per_layer = c.mlp_added + s.hidden;
+  CaptureLayout c;
+  c.layer.resize(s.layers);
+  uint64_t at = 0;
+  const auto take = [&at](uint64_t width) {
+    const uint64_t first = at;
+    at += width;
+    return first;
+  };
+  for (uint32_t l = 0; l < s.layers; l++) c.layer[l].neurons = take(s.ffn);
+  for (uint32_t l = 0; l < s.layers; l++) {
+    CaptureSlot& k = c.layer[l];
+    k.window = s.window == 0 || l % s.pattern == s.pattern - 1 ? s.context : s.window;
+    k.keys = std::min(k.window, s.context);
+    k.residual = take(s.hidden);
+    k.attn_added = take(s.hidden);
+    k.mlp_added = take(s.hidden);
+    k.query = take((uint64_t)s.heads * s.head_dim);
+    k.weights = take((uint64_t)s.heads * k.keys);
+    k.stats = take(2ull * s.heads);
+    k.readout = take(kReadoutWords);
+  }
+  c.words = at;
   return c;
+}
+
+// The kernels write the residual, additions and query slots, and read the
+// residuals back, four words at a time: each slot, and each sequence's store,
+// starts on a 16-byte boundary (true whenever the head count is even).
+bool capture_aligned(const CaptureLayout& c) {
+  if (c.words % 4) return false;
+  for (const CaptureSlot& k : c.layer)
+    if ((k.neurons | k.residual | k.attn_added | k.mlp_added | k.query) % 4) return false;
+  return true;
 }
 
 }  // namespace
@@ -170,6 +206,11 @@ struct fz_batch {
   std::vector<bool> has_edits;
   float* captures = nullptr;
   uint64_t capture_floats = 0;
+  // The capture kernels' per-layer view and the readouts' scratch (up to
+  // kMaxTokens readout rows a head launch).
+  fz::CaptureLayer* cap_layers = nullptr;
+  float *ro_rows = nullptr, *ro_logits = nullptr;
+  unsigned long long *ro_argmax = nullptr, *ro_tile_best = nullptr;
   // Rows the per-row scratch holds (sequences x tokens of the widest step so
   // far); grown on demand, which drops the captured graphs.
   uint32_t rows_cap = 0;
@@ -440,7 +481,81 @@ bool decode_step_enabled() {
   return !(v && *v && *v != '0');
 }
 
+fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st);
+
+// What a capture step adds after the forward pass (capture/capture.h): each
+// layer's attention weights and statistics, then its readout.  The readout
+// rows of the layers before the last (the residual each leaves) go through
+// the final norm and the tied head kMaxTokens at a time, and the top 64 of
+// each row into the layer's slot; the last layer's readout is the top 64 of
+// the step's own logits, the candidates the draw chooses from.  A step that
+// asks for no logits has no last readout and no final addition: both slots
+// are zeroed.
+fz_status enqueue_capture(fz_batch& b, const GraphKey& key, cudaStream_t st) {
+  fz_model& m = *b.model;
+  const Shape& s = m.shape;
+  const CaptureLayout cl = capture_layout(s);
+  const bool pdl = true;
+  fz::WeightsArgs w{};
+  w.step = b.dstep;
+  w.store = b.captures;
+  w.store_stride = cl.words;
+  w.layers = b.cap_layers;
+  w.heads = s.heads;
+  w.kv_heads = s.kv_heads;
+  w.head_dim = s.head_dim;
+  w.scale_log2e = (float)((double)(1.0f / std::sqrt((float)s.head_dim)) * 1.4426950408889634);
+  FZ_CUDA(fz::launch_attention_weights(w, s.layers, b.S, st, pdl));
+  fz::ReadoutArgs r{};
+  r.store = b.captures;
+  r.store_stride = cl.words;
+  r.layers = b.cap_layers;
+  r.n_layers = s.layers;
+  r.width = s.hidden;
+  r.rows = b.ro_rows;
+  r.logits = b.ro_logits;
+  r.vocab = s.vocab;
+  r.tile_best = b.ro_tile_best;
+  const uint32_t rows = b.S * (s.layers - 1);
+  for (uint32_t g0 = 0; g0 < rows; g0 += fz::kMaxTokens) {
+    const uint32_t n = std::min<uint32_t>(fz::kMaxTokens, rows - g0);
+    FZ_CUDA(fz::launch_readout_rows(r, g0, n, st, pdl));
+    FZ_CUDA(cudaMemsetAsync(b.ro_argmax, 0, (size_t)n * 8, st));
+    fz::MatvecArgs h{};
+    h.step = b.dstep;
+    h.mat[0] = m.embd.view();
+    h.m = n;
+    h.seq_tokens = 1;
+    h.norm.hidden_in = b.ro_rows;
+    h.norm.gain = m.output_norm;
+    h.norm.eps = s.eps;
+    h.norm.width = s.hidden;
+    h.norm.row_of_token_stride = 1;
+    h.out = b.ro_logits;
+    h.out_stride = s.vocab;
+    h.head.argmax = b.ro_argmax;
+    fz_status stt;
+    if ((stt = run_matvec(h, fz::kPrologueNorm, fz::kEpilogueHead, st, pdl))) return stt;
+    FZ_CUDA(fz::launch_readout_select(r, g0, n, false, st, pdl));
+  }
+  if (key.logits) {
+    r.logits = b.logits;
+    FZ_CUDA(fz::launch_readout_select(r, 0, b.S, true, st, pdl));
+  } else {
+    const CaptureSlot& last = cl.layer[s.layers - 1];
+    FZ_CUDA(cudaMemset2DAsync(b.captures + last.mlp_added, cl.words * 4, 0, (size_t)s.hidden * 4, b.S, st));
+    FZ_CUDA(cudaMemset2DAsync(b.captures + last.readout, cl.words * 4, 0, (size_t)kReadoutWords * 4, b.S, st));
+  }
+  return FZ_OK;
+}
+
 fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
+  fz_status stt = enqueue_forward(b, key, st);
+  if (stt || !key.capture) return stt;
+  return enqueue_capture(b, key, st);
+}
+
+fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
   fz_model& m = *b.model;
   const Shape& s = m.shape;
   const uint32_t T = key.tokens, M = b.S * T;
@@ -498,13 +613,16 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     d.edit_table = key.edits ? b.edit_tables : nullptr;
     d.table_stride = b.table_words;
     d.capture = cap;
-    d.capture_stride = cl.per_layer * s.layers;
-    d.cap_residual = cl.residual;
-    d.cap_query = cl.query;
-    d.cap_attn_added = cl.attn_added;
-    d.cap_neurons = cl.neurons;
-    d.cap_mlp_added = cl.mlp_added;
-    d.cap_per_layer = cl.per_layer;
+    d.capture_stride = cl.words;
+    d.cap_region2 = cl.layer[0].residual;
+    d.cap_block = 3ull * s.hidden + (uint64_t)s.heads * s.head_dim + 2ull * s.heads + kReadoutWords;
+    d.cap_keys_local = s.window == 0 ? s.context : std::min(s.window, s.context);
+    d.cap_keys_global = s.context;
+    d.cap_pattern = s.pattern;
+    for (uint32_t l = 0; l < s.layers; l++)  // the closed form the kernel uses
+      if (cl.layer[l].keys != (s.window == 0 || l % s.pattern == s.pattern - 1 ? d.cap_keys_global
+                                                                                : d.cap_keys_local))
+        return fail(FZ_ERR_NOT_SUPPORTED, "capture layout outside the decode kernel's closed form");
     d.head = m.embd.view();
     d.output_norm = m.output_norm;
     // The head runs as its own streaming launch (below), not inside the step.
@@ -524,7 +642,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       h.mat[0] = m.embd.view();
       h.m = b.S;
       h.seq_tokens = 1;
-      h.capture_stride = cl.per_layer * s.layers;
+      h.capture_stride = cl.words;
       h.norm.hidden_in = b.hidden_a;
       h.norm.y = d.y_mlp;
       h.norm.y_parts = fz::kDecodeDownSlices;
@@ -535,7 +653,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       h.norm.eps = s.eps;
       h.norm.width = s.hidden;
       h.norm.row_of_token_stride = 1;
-      h.norm.capture_added = cap ? cap + (s.layers - 1) * cl.per_layer + cl.mlp_added : nullptr;
+      h.norm.capture_added = cap ? cap + cl.layer[s.layers - 1].mlp_added : nullptr;
       h.out = b.logits;
       h.out_stride = s.vocab;
       h.head.argmax = b.argmax;
@@ -582,8 +700,8 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       g.table_stride = b.table_words;
       g.layer = layer;
       g.seq_tokens = T;
-      g.capture_neurons = (cap && epi == fz::kGemmGated) ? cap + layer * cl.per_layer + cl.neurons : nullptr;
-      g.capture_stride = cl.per_layer * s.layers;
+      g.capture_neurons = (cap && epi == fz::kGemmGated) ? cap + cl.layer[layer].neurons : nullptr;
+      g.capture_stride = cl.words;
       g.error = b.gemm_error;
       FZ_CUDA(fz::launch_gemm(g, epi, st, pdl));
       return FZ_OK;
@@ -595,7 +713,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       a.step = b.dstep;
       a.m = M;
       a.seq_tokens = T;
-      a.capture_stride = cl.per_layer * s.layers;
+      a.capture_stride = cl.words;
       a.norm.hidden_in = b.hidden_a;
       a.norm.y = l ? b.y_mlp : nullptr;
       a.norm.post_gain = l ? m.layers[l - 1].post_ffw_norm : nullptr;
@@ -603,8 +721,8 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       a.norm.hidden_out = b.hidden_b;
       a.norm.eps = s.eps;
       a.norm.width = s.hidden;
-      a.norm.capture_residual = cap ? cap + l * cl.per_layer + cl.residual : nullptr;
-      a.norm.capture_added = (cap && l) ? cap + (l - 1) * cl.per_layer + cl.mlp_added : nullptr;
+      a.norm.capture_residual = cap ? cap + cl.layer[l].residual : nullptr;
+      a.norm.capture_added = (cap && l) ? cap + cl.layer[l - 1].mlp_added : nullptr;
       FZ_CUDA(fz::launch_norm_f16(a, b.x16_hi, xlo, st, pdl));
       if ((stt = gemm(L.qkv, nullptr, b.x16_hi, xlo, b.qkv, L.qkv.n, fz::kGemmWrite, l))) return stt;
       a.out = b.qkv;
@@ -621,7 +739,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       a.rope.slots = b.slots[l];
       a.rope.seq_stride = b.seq_stride[l];
       a.rope.query_out = b.q;
-      a.rope.capture_query = cap ? cap + l * cl.per_layer + cl.query : nullptr;
+      a.rope.capture_query = cap ? cap + cl.layer[l].query : nullptr;
       FZ_CUDA(fz::launch_rope_rows(a, st, pdl));
       fz::AttentionArgs at{};
       at.step = b.dstep;
@@ -657,7 +775,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       g.norm.gain = L.ffn_norm;
       g.norm.hidden_out = b.hidden_a;
       g.norm.capture_residual = nullptr;
-      g.norm.capture_added = cap ? cap + l * cl.per_layer + cl.attn_added : nullptr;
+      g.norm.capture_added = cap ? cap + cl.layer[l].attn_added : nullptr;
       FZ_CUDA(fz::launch_norm_f16(g, b.x16_hi, xlo, st, pdl));
       if ((stt = gemm(L.gate, &L.up, b.x16_hi, xlo, nullptr, s.ffn, fz::kGemmGated, l))) return stt;
       if ((stt = gemm(L.down, nullptr, b.act16_hi, alo, b.y_mlp, s.hidden, fz::kGemmWrite, l))) return stt;
@@ -672,7 +790,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     a.mat[0] = L.qkv.view();
     a.m = M;
     a.seq_tokens = T;
-    a.capture_stride = cl.per_layer * s.layers;
+    a.capture_stride = cl.words;
     a.norm.hidden_in = b.hidden_a;
     a.norm.y = l ? b.y_mlp : nullptr;
     a.norm.post_gain = l ? m.layers[l - 1].post_ffw_norm : nullptr;
@@ -681,8 +799,8 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     a.norm.eps = s.eps;
     a.norm.width = s.hidden;
     a.norm.row_of_token_stride = 1;
-    a.norm.capture_residual = cap ? cap + l * cl.per_layer + cl.residual : nullptr;
-    a.norm.capture_added = (cap && l) ? cap + (l - 1) * cl.per_layer + cl.mlp_added : nullptr;
+    a.norm.capture_residual = cap ? cap + cl.layer[l].residual : nullptr;
+    a.norm.capture_added = (cap && l) ? cap + cl.layer[l - 1].mlp_added : nullptr;
     a.out = b.qkv;
     a.out_stride = L.qkv.n;
     a.rope.q_gain = L.q_norm;
@@ -697,7 +815,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     a.rope.slots = b.slots[l];
     a.rope.seq_stride = b.seq_stride[l];
     a.rope.query_out = b.q;
-    a.rope.capture_query = cap ? cap + l * cl.per_layer + cl.query : nullptr;
+    a.rope.capture_query = cap ? cap + cl.layer[l].query : nullptr;
     a.counter = lc;
     if ((stt = run_matvec(a, fz::kPrologueNorm, fz::kEpilogueQkv, st, pdl))) return stt;
     // Attention.
@@ -739,7 +857,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     g.mat[1] = L.up.view();
     g.m = M;
     g.seq_tokens = T;
-    g.capture_stride = cl.per_layer * s.layers;
+    g.capture_stride = cl.words;
     g.norm.hidden_in = b.hidden_b;
     g.norm.y = b.y_attn;
     g.norm.post_gain = L.post_attn_norm;
@@ -748,13 +866,13 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     g.norm.eps = s.eps;
     g.norm.width = s.hidden;
     g.norm.row_of_token_stride = 1;
-    g.norm.capture_added = cap ? cap + l * cl.per_layer + cl.attn_added : nullptr;
+    g.norm.capture_added = cap ? cap + cl.layer[l].attn_added : nullptr;
     g.out = b.act;
     g.out_stride = s.ffn;
     g.edit.table = key.edits ? b.edit_tables : nullptr;
     g.edit.table_stride = b.table_words;
     g.edit.layer = l;
-    g.edit.capture_neurons = cap ? cap + l * cl.per_layer + cl.neurons : nullptr;
+    g.edit.capture_neurons = cap ? cap + cl.layer[l].neurons : nullptr;
     if ((stt = run_matvec(g, fz::kPrologueNorm, fz::kEpilogueGated, st, pdl))) return stt;
     // Down projection.
     fz::MatvecArgs d{};
@@ -774,7 +892,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     h.mat[0] = m.embd.view();
     h.m = b.S;
     h.seq_tokens = T;
-    h.capture_stride = cl.per_layer * s.layers;
+    h.capture_stride = cl.words;
     h.norm.hidden_in = b.hidden_a;
     h.norm.y = b.y_mlp;
     h.norm.post_gain = m.layers[s.layers - 1].post_ffw_norm;
@@ -784,7 +902,7 @@ fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     h.norm.width = s.hidden;
     h.norm.row_of_token_stride = T;
     h.norm.row_of_token_offset = T - 1;
-    h.norm.capture_added = cap ? cap + (s.layers - 1) * cl.per_layer + cl.mlp_added : nullptr;
+    h.norm.capture_added = cap ? cap + cl.layer[s.layers - 1].mlp_added : nullptr;
     h.out = b.logits;
     h.out_stride = s.vocab;
     h.head.argmax = b.argmax;
@@ -1060,6 +1178,7 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
                                         std::min<uint32_t>((keys + fz::kDecodeSplitKeys - 1) / fz::kDecodeSplitKeys,
                                                            fz::kDecodeMaxSplits)});
   }
+  const CaptureLayout cl = capture_layout(s);
   {
     std::vector<fz::DecodeLayer> dl(s.layers);
     std::vector<fz::DecodeKvMaps> maps(s.layers);
@@ -1101,7 +1220,7 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     FZ_CUDA(cudaMemcpy(b->kv_maps, maps.data(), maps.size() * sizeof(fz::DecodeKvMaps), cudaMemcpyHostToDevice));
   }
   b->table_words = 2 * s.layers + 5 * kMaxEdits;
-  b->capture_floats = capture_layout(s).per_layer * s.layers;
+  b->capture_floats = cl.words;
   const uint32_t tiles = fz::select_tiles(s.vocab);
   if ((st = b->alloc(&b->logits, (size_t)sequences * s.vocab * 4)) || (st = b->alloc(&b->argmax, (size_t)sequences * 8)) ||
       (st = b->alloc(&b->tile_best, (size_t)sequences * tiles * 64 * 8)) ||
@@ -1109,8 +1228,28 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
       (st = b->alloc(&b->dstep, sizeof(DeviceStep))) || (st = b->alloc(&b->dseeds, (size_t)sequences * 8)) ||
       (st = b->alloc(&b->gemm_error, 16)) ||
       (st = b->alloc(&b->edit_tables, (size_t)sequences * b->table_words * 4)) ||
-      (st = b->alloc(&b->captures, (size_t)sequences * b->capture_floats * 4)) || (st = alloc_rows(*b, M)))
+      (st = b->alloc(&b->captures, (size_t)sequences * b->capture_floats * 4)) ||
+      (st = b->alloc(&b->cap_layers, (size_t)s.layers * sizeof(fz::CaptureLayer))) ||
+      (st = b->alloc(&b->ro_rows, (size_t)fz::kMaxTokens * s.hidden * 4)) ||
+      (st = b->alloc(&b->ro_logits, (size_t)fz::kMaxTokens * s.vocab * 4)) ||
+      (st = b->alloc(&b->ro_argmax, (size_t)fz::kMaxTokens * 8)) ||
+      (st = b->alloc(&b->ro_tile_best, (size_t)fz::kMaxTokens * tiles * 64 * 8)) || (st = alloc_rows(*b, M)))
     return st;
+  {
+    std::vector<fz::CaptureLayer> v(s.layers);
+    for (uint32_t l = 0; l < s.layers; l++) {
+      v[l].key_cache = b->kc[l];
+      v[l].seq_stride = b->seq_stride[l];
+      v[l].slots = b->slots[l];
+      v[l].keys = cl.layer[l].keys;
+      v[l].residual = cl.layer[l].residual;
+      v[l].query = cl.layer[l].query;
+      v[l].weights = cl.layer[l].weights;
+      v[l].stats = cl.layer[l].stats;
+      v[l].readout = cl.layer[l].readout;
+    }
+    FZ_CUDA(cudaMemcpy(b->cap_layers, v.data(), v.size() * sizeof(fz::CaptureLayer), cudaMemcpyHostToDevice));
+  }
   if (const char* v = std::getenv("FRIZZLE_B200_PASSES")) {
     const int p = std::atoi(v);
     b->passes = p == 1 ? 1u : p == 3 ? 3u : 2u;
@@ -1215,6 +1354,8 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
     for (uint32_t i = 0; i < T * b->S; i++)
       if (ids[i] >= s.vocab) return fail(FZ_ERR_ARGUMENT, "a token identifier past the vocabulary");
   if (step->logits && step->temperature > 0.f && step->top_k == 0) return fail(FZ_ERR_ARGUMENT, "top_k 0");
+  if (step->capture && !capture_aligned(capture_layout(s)))
+    return fail(FZ_ERR_NOT_SUPPORTED, "a capture layout whose vector slots are not 16-byte aligned");
   cudaStream_t st = b->model->dev->stream;
   FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
   if (T * b->S > b->rows_cap) {
@@ -1307,7 +1448,31 @@ fz_status fz_batch_read_logits(fz_batch* b, uint32_t sequence, float* out, size_
   return FZ_OK;
 }
 
-size_t fz_capture_floats(const fz_model* m) { return m ? capture_layout(m->shape).per_layer * m->shape.layers : 0; }
+size_t fz_capture_floats(const fz_model* m) { return m ? capture_layout(m->shape).words : 0; }
+
+fz_status fz_capture_layout(const fz_model* m, uint32_t layer, fz_capture_slots* out) {
+  if (!m || !out) return fail(FZ_ERR_ARGUMENT, "null model or output");
+  if (!m->finished) return fail(FZ_ERR_STATE, "the model is not loaded");
+  const Shape& s = m->shape;
+  if (layer >= s.layers) return fail(FZ_ERR_ARGUMENT, "layer out of range");
+  const CaptureLayout cl = capture_layout(s);
+  if (cl.words > 0xFFFFFFFFull) return fail(FZ_ERR_NOT_SUPPORTED, "a capture store past 2^32 words");
+  const CaptureSlot& k = cl.layer[layer];
+  const auto slot = [](uint64_t first, uint64_t width) { return fz_capture_slot{(uint32_t)first, (uint32_t)width}; };
+  out->neurons = slot(k.neurons, s.ffn);
+  out->residual = slot(k.residual, s.hidden);
+  out->attention_added = slot(k.attn_added, s.hidden);
+  out->mlp_added = slot(k.mlp_added, s.hidden);
+  out->query = slot(k.query, (uint64_t)s.heads * s.head_dim);
+  out->weights = slot(k.weights, (uint64_t)s.heads * k.keys);
+  out->stats = slot(k.stats, 2ull * s.heads);
+  out->readout = slot(k.readout, kReadoutWords);
+  out->keys = k.keys;
+  out->query_heads = s.heads;
+  out->window = k.window;
+  out->full_attention = k.window >= s.context ? 1u : 0u;
+  return FZ_OK;
+}
 
 fz_status fz_batch_read_capture(fz_batch* b, uint32_t sequence, float* out, size_t count) {
   if (!b || !out || sequence >= b->S) return fail(FZ_ERR_ARGUMENT, "bad argument");

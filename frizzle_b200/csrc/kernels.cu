@@ -248,22 +248,43 @@ FZ_DEV void bitonic_desc(unsigned long long* k, int n) {
 
 FZ_DEV float temperature_of(const SelectArgs& a) { return a.step->temperature; }
 
-// Each CTA keeps the top 64 of its tile of logits (topk.wgsl first/merge:
-// the same set and order, by a sort of the tile).
+// The top 64 of one tile of a row of logits into best[0 .. 63] (topk.wgsl
+// first/merge: the same set and order, by a sort of the tile).
+FZ_DEV void tile_top64(const float* l, uint32_t vocab, uint32_t tile, unsigned long long* keys,
+                       unsigned long long* best) {
+  for (int i = threadIdx.x; i < kTile; i += blockDim.x) {
+    const uint32_t id = tile * kTile + i;
+    keys[i] = id < vocab ? packed_key(l[id], id) : 0ull;
+  }
+  __syncthreads();
+  bitonic_desc(keys, kTile);
+  if (threadIdx.x < kCandidates) best[threadIdx.x] = keys[threadIdx.x];
+}
+
+// The best 64 of the tiles' candidates (n of them at `tile_best`), as
+// (logit bits, token) pairs: pair i's bits at out[2i], its token at
+// out[2i + 1] (kernels::kCandidates pairs, best first).
+FZ_DEV void merge_top64(const unsigned long long* tile_best, int n, unsigned long long* keys, uint32_t* out) {
+  int padded = 64;
+  while (padded < n) padded <<= 1;
+  for (int i = threadIdx.x; i < padded; i += blockDim.x) keys[i] = i < n ? tile_best[i] : 0ull;
+  __syncthreads();
+  bitonic_desc(keys, padded);
+  if (threadIdx.x < kCandidates) {
+    const unsigned long long k = keys[threadIdx.x];
+    out[2 * threadIdx.x] = k ? topk_bits((uint32_t)(k >> 32)) : 0u;
+    out[2 * threadIdx.x + 1] = k ? 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu) : 0xFFFFFFFFu;
+  }
+}
+
+// Each CTA keeps the top 64 of its tile of logits.
 __global__ void __launch_bounds__(512) select_tiles_kernel(const SelectArgs a) {
   __shared__ unsigned long long keys[kTile];
   pdl_wait();
   if (!(temperature_of(a) > 0.0f)) return;
   const uint32_t seq = blockIdx.y, tile = blockIdx.x, tiles = gridDim.x;
-  const float* l = a.logits + (size_t)seq * a.vocab;
-  for (int i = threadIdx.x; i < kTile; i += blockDim.x) {
-    const uint32_t id = tile * kTile + i;
-    keys[i] = id < a.vocab ? packed_key(l[id], id) : 0ull;
-  }
-  __syncthreads();
-  bitonic_desc(keys, kTile);
-  if (threadIdx.x < kCandidates)
-    a.tile_best[((size_t)seq * tiles + tile) * kCandidates + threadIdx.x] = keys[threadIdx.x];
+  tile_top64(a.logits + (size_t)seq * a.vocab, a.vocab, tile, keys,
+             a.tile_best + ((size_t)seq * tiles + tile) * kCandidates);
 }
 
 FZ_DEV float unit_interval(uint32_t w) {
@@ -295,19 +316,8 @@ __global__ void __launch_bounds__(512) select_draw_kernel(const SelectArgs a, ui
     }
     return;
   }
-  const int n = (int)(tiles * kCandidates);
-  int padded = 64;
-  while (padded < n) padded <<= 1;
-  for (int i = threadIdx.x; i < padded; i += blockDim.x)
-    keys[i] = i < n ? a.tile_best[(size_t)seq * tiles * kCandidates + i] : 0ull;
-  __syncthreads();
-  bitonic_desc(keys, padded);
   uint32_t* cand = a.candidates + seq * kCandidates * 2;
-  if (threadIdx.x < kCandidates) {
-    const unsigned long long k = keys[threadIdx.x];
-    cand[2 * threadIdx.x] = k ? topk_bits((uint32_t)(k >> 32)) : 0u;
-    cand[2 * threadIdx.x + 1] = k ? 0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu) : 0xFFFFFFFFu;
-  }
+  merge_top64(a.tile_best + (size_t)seq * tiles * kCandidates, (int)(tiles * kCandidates), keys, cand);
   __syncthreads();
   const uint32_t k = min(st.top_k, (uint32_t)kCandidates);
   const bool use_top_p = st.top_p < 1.0f;
@@ -362,6 +372,139 @@ __global__ void __launch_bounds__(512) select_draw_kernel(const SelectArgs a, ui
   rec[3] = 0u;
 }
 
+// ------------------------------------------------------------ capture
+//
+// The capture's attention weights and statistics (capture/weights.h:24-62;
+// the scores of attention.wgsl:277-295, the fold's m and l, :394-395 and
+// :434-436) for the captured row of each sequence, at p = position + tokens
+// - 1.  A CTA takes one (KV head, layer, sequence) and the G query heads
+// that share the KV head.  Key i < count = min(p + 1, keys), at position
+// earliest + i (earliest = p + 1 - count), is scored by one thread in the
+// order the CPU restatement follows: q staged times scale*log2(e), then
+// s += ((q0 k0 + q1 k1) + q2 k2) + q3 k3 over the head's 64 quads.  m is the
+// largest score, l the sum of exp2(s - m) (each thread's keys in order, then
+// a fixed tree), and the weights exp2(s - m) / l overwrite the scores; keys
+// count .. keys - 1 get 0.  The scores are formed here from the captured
+// query and the key cache rather than kept by the attention kernels, whose
+// tensor-core products round differently: the weights are a function of
+// these scores and these statistics, as weights.h states them.
+template <int G>
+__global__ void __launch_bounds__(256) attention_weights_kernel(const WeightsArgs a) {
+  __shared__ float qs[G][kHeadDim];
+  __shared__ float red[G][8];
+  __shared__ float stat[2][G];
+  pdl_wait();
+  const uint32_t kvh = blockIdx.x, seq = blockIdx.z;
+  const CaptureLayer L = a.layers[blockIdx.y];
+  const DeviceStep& st = *a.step;
+  const uint32_t p = st.position + st.tokens - 1;
+  const uint32_t count = min(p + 1, L.keys), earliest = p + 1 - count;
+  float* store = a.store + (size_t)seq * a.store_stride;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+#pragma unroll
+  for (int h = 0; h < G; h++)
+    qs[h][tid] = mul(store[L.query + (size_t)(kvh * G + h) * kHeadDim + tid], a.scale_log2e);
+  __syncthreads();
+  const uint16_t* kc = L.key_cache + (size_t)seq * L.seq_stride;
+  auto at = [&](int h, uint32_t i) { return L.weights + (size_t)(kvh * G + h) * L.keys + i; };
+  float top[G];
+#pragma unroll
+  for (int h = 0; h < G; h++) top[h] = -INFINITY;
+  for (uint32_t i = tid; i < count; i += 256) {
+    const uint2* kr =
+        reinterpret_cast<const uint2*>(kc + ((size_t)((earliest + i) % L.slots) * a.kv_heads + kvh) * kHeadDim);
+    float s[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) s[h] = 0.f;
+#pragma unroll 4
+    for (int w = 0; w < kHeadDim / 4; w++) {
+      const uint2 u = __ldg(kr + w);
+      const float k0 = f16_unpack((uint16_t)(u.x & 0xFFFFu)), k1 = f16_unpack((uint16_t)(u.x >> 16));
+      const float k2 = f16_unpack((uint16_t)(u.y & 0xFFFFu)), k3 = f16_unpack((uint16_t)(u.y >> 16));
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        const float* q = &qs[h][4 * w];
+        s[h] = add(s[h], add(add(add(mul(q[0], k0), mul(q[1], k1)), mul(q[2], k2)), mul(q[3], k3)));
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+      store[at(h, i)] = s[h];
+      top[h] = fmaxf(top[h], s[h]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < G; h++) {
+    const float v = warp_max(top[h]);
+    if (lane == 0) red[h][warp] = v;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float m = red[tid][0];
+    for (int w = 1; w < 8; w++) m = fmaxf(m, red[tid][w]);
+    stat[0][tid] = m;
+  }
+  __syncthreads();
+  float sum[G];
+#pragma unroll
+  for (int h = 0; h < G; h++) sum[h] = 0.f;
+  for (uint32_t i = tid; i < count; i += 256) {
+#pragma unroll
+    for (int h = 0; h < G; h++) sum[h] = add(sum[h], exp2f(sub(store[at(h, i)], stat[0][h])));
+  }
+  __syncthreads();
+#pragma unroll
+  for (int h = 0; h < G; h++) {
+    const float v = warp_sum(sum[h]);
+    if (lane == 0) red[h][warp] = v;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float l = red[tid][0];
+    for (int w = 1; w < 8; w++) l = add(l, red[tid][w]);
+    stat[1][tid] = l;
+    store[L.stats + 2 * (kvh * G + tid)] = stat[0][tid];
+    store[L.stats + 2 * (kvh * G + tid) + 1] = l;
+  }
+  __syncthreads();
+  for (uint32_t i = tid; i < L.keys; i += 256) {
+#pragma unroll
+    for (int h = 0; h < G; h++)
+      store[at(h, i)] = i < count ? __fdiv_rn(exp2f(sub(store[at(h, i)], stat[0][h])), stat[1][h]) : 0.f;
+  }
+}
+
+// Readout row g (sequence g / (layers - 1), layer g % (layers - 1)): the
+// residual stream as that layer leaves it, which is the next layer's
+// captured residual (capture.h:26-33), copied into rows [n][width].
+__global__ void __launch_bounds__(256) readout_rows_kernel(const ReadoutArgs a, uint32_t g0) {
+  pdl_wait();
+  const uint32_t g = g0 + blockIdx.x, per = a.n_layers - 1, seq = g / per, l = g % per;
+  const float4* src = reinterpret_cast<const float4*>(a.store + (size_t)seq * a.store_stride + a.layers[l + 1].residual);
+  float4* dst = reinterpret_cast<float4*>(a.rows + (size_t)blockIdx.x * a.width);
+  for (uint32_t i = threadIdx.x; i < a.width / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+// The top 64 of each tile of each readout row's logits.
+__global__ void __launch_bounds__(512) readout_tiles_kernel(const ReadoutArgs a) {
+  __shared__ unsigned long long keys[kTile];
+  pdl_wait();
+  const uint32_t r = blockIdx.y, tile = blockIdx.x, tiles = gridDim.x;
+  tile_top64(a.logits + (size_t)r * a.vocab, a.vocab, tile, keys, a.tile_best + ((size_t)r * tiles + tile) * kCandidates);
+}
+
+// Merges row r's tiles into its layer's readout slot: row g0 + r of the
+// layers before the last, or with `last`, sequence g0 + r's last layer.
+__global__ void __launch_bounds__(512) readout_merge_kernel(const ReadoutArgs a, uint32_t g0, uint32_t tiles,
+                                                            uint32_t last) {
+  __shared__ unsigned long long keys[kTile];
+  pdl_wait();
+  const uint32_t g = g0 + blockIdx.x, per = a.n_layers - 1;
+  const uint32_t seq = last ? g : g / per, l = last ? per : g % per;
+  uint32_t* out = reinterpret_cast<uint32_t*>(a.store + (size_t)seq * a.store_stride + a.layers[l].readout);
+  merge_top64(a.tile_best + (size_t)blockIdx.x * tiles * kCandidates, (int)(tiles * kCandidates), keys, out);
+}
+
 cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, void** args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -401,6 +544,41 @@ cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t stream, bool pdl) {
   EmbedArgs copy = a;
   void* args[] = {&copy};
   return launch((const void*)embed_kernel, dim3(a.m), dim3(256), 0, stream, pdl, args);
+}
+
+cudaError_t launch_attention_weights(const WeightsArgs& a, uint32_t layers, uint32_t seqs, cudaStream_t stream,
+                                     bool pdl) {
+  if (a.head_dim != kHeadDim || a.kv_heads == 0 || a.heads % a.kv_heads) return cudaErrorInvalidValue;
+  WeightsArgs copy = a;
+  void* args[] = {&copy};
+  const dim3 grid(a.kv_heads, layers, seqs);
+  switch (a.heads / a.kv_heads) {
+    case 1: return launch((const void*)attention_weights_kernel<1>, grid, dim3(256), 0, stream, pdl, args);
+    case 2: return launch((const void*)attention_weights_kernel<2>, grid, dim3(256), 0, stream, pdl, args);
+    case 4: return launch((const void*)attention_weights_kernel<4>, grid, dim3(256), 0, stream, pdl, args);
+    case 8: return launch((const void*)attention_weights_kernel<8>, grid, dim3(256), 0, stream, pdl, args);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_readout_rows(const ReadoutArgs& a, uint32_t g0, uint32_t n, cudaStream_t stream, bool pdl) {
+  if (a.n_layers < 2 || a.width % 4 || n == 0) return cudaErrorInvalidValue;
+  ReadoutArgs copy = a;
+  void* args[] = {&copy, &g0};
+  return launch((const void*)readout_rows_kernel, dim3(n), dim3(256), 0, stream, pdl, args);
+}
+
+cudaError_t launch_readout_select(const ReadoutArgs& a, uint32_t g0, uint32_t n, bool last, cudaStream_t stream,
+                                  bool pdl) {
+  uint32_t tiles = (a.vocab + kTile - 1) / kTile;
+  if (tiles * kCandidates > (uint32_t)kTile || n == 0) return cudaErrorInvalidValue;
+  ReadoutArgs copy = a;
+  void* args1[] = {&copy};
+  cudaError_t e = launch((const void*)readout_tiles_kernel, dim3(tiles, n), dim3(512), 0, stream, pdl, args1);
+  if (e != cudaSuccess) return e;
+  uint32_t lf = last ? 1u : 0u;
+  void* args2[] = {&copy, &g0, &tiles, &lf};
+  return launch((const void*)readout_merge_kernel, dim3(n), dim3(512), 0, stream, pdl, args2);
 }
 
 uint32_t select_tiles(uint32_t vocab) { return (vocab + kTile - 1) / kTile; }

@@ -67,6 +67,51 @@ struct SelectArgs {
   uint32_t* candidates;            // [seqs][64][2] (logit bits, token)
   uint32_t* records;               // [seqs][4] {token, failed, u bits, 0}
 };
+// A layer's view for the capture kernels: its key cache and its slots in a
+// sequence's capture store (words from the store's start).
+struct CaptureLayer {
+  const uint16_t* key_cache;       // [seqs][slots][kv_heads][d]
+  uint64_t seq_stride;             // cache elements between sequences
+  uint32_t slots;                  // ring slots
+  uint32_t keys;                   // min(window, trained context)
+  uint64_t residual, query, weights, stats, readout;
+};
+
+// The capture's attention weights and statistics (capture/weights.h) for
+// every layer of every sequence, at the step's last position; grid (KV
+// heads, layers, sequences).
+struct WeightsArgs {
+  const DeviceStep* step;
+  float* store;                    // sequence 0's capture store
+  uint64_t store_stride;           // words between sequences' stores
+  const CaptureLayer* layers;      // [layers]
+  uint32_t heads, kv_heads, head_dim;
+  float scale_log2e;
+};
+cudaError_t launch_attention_weights(const WeightsArgs& a, uint32_t layers, uint32_t seqs, cudaStream_t stream,
+                                     bool pdl);
+
+// The per-layer readouts (capture.h:26-33): readout rows are built from the
+// captured residuals, run through the final norm and the head by the
+// matvec launch, and their top 64 (logit bits, token) pairs are written into
+// each layer's readout slot.
+struct ReadoutArgs {
+  float* store;                    // sequence 0's capture store
+  uint64_t store_stride;
+  const CaptureLayer* layers;
+  uint32_t n_layers;
+  uint32_t width;                  // embedding width
+  float* rows;                     // [n][width] readout rows
+  const float* logits;             // [n][vocab]
+  uint32_t vocab;
+  unsigned long long* tile_best;   // [n][tiles][64] scratch
+};
+cudaError_t launch_readout_rows(const ReadoutArgs& a, uint32_t g0, uint32_t n, cudaStream_t stream, bool pdl);
+// Rows g0 .. g0 + n - 1 of the layers before the last, or with `last` the
+// last layer of sequences g0 .. g0 + n - 1 (logits: their rows).
+cudaError_t launch_readout_select(const ReadoutArgs& a, uint32_t g0, uint32_t n, bool last, cudaStream_t stream,
+                                  bool pdl);
+
 uint32_t select_tiles(uint32_t vocab);
 cudaError_t launch_select(const SelectArgs& a, cudaStream_t stream, bool pdl);
 

@@ -19,7 +19,9 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import edits as E
-from ._native import FzError, ModelInfo, Record, Step, check, load
+from ._native import CaptureSlots, FzError, ModelInfo, Record, Step, check, load
+from .capture import SLOTS, Capture
+from .capture import layout as capture_layout
 
 MAX_ROWS = 16  # sequences x tokens one step takes
 
@@ -95,6 +97,15 @@ class Model:
     @property
     def capture_floats(self) -> int:
         return int(self.lib.fz_capture_floats(self.handle))
+
+    def capture_layout(self, layer: int) -> dict:
+        """fz_capture_layout: the layer's slots as {name: (first, width)} and its attention."""
+        out = CaptureSlots()
+        check(self.lib.fz_capture_layout(self.handle, layer, C.byref(out)))
+        d = {n: (getattr(out, n).first, getattr(out, n).width) for n in SLOTS}
+        d.update(keys=out.keys, query_heads=out.query_heads, window=out.window,
+                 full_attention=bool(out.full_attention))
+        return d
 
     def free(self):
         if self.handle:
@@ -186,6 +197,11 @@ class Batch:
         out = np.empty(n, dtype=np.float32)
         check(self.lib.fz_batch_read_capture(self.handle, sequence, out.ctypes.data, n))
         return out
+
+    def capture_view(self, sequence: int = 0) -> Capture:
+        """The sequence's capture store read through its layout."""
+        info = self.model.info
+        return Capture(self.capture(sequence), capture_layout(info), info.head_dim)
 
     def cache(self, sequence: int, layer: int, values: bool = False):
         p = C.c_void_p()

@@ -150,13 +150,38 @@ fz_status fz_batch_wait(fz_batch *batch, fz_record *records);
 fz_status fz_batch_wait_oldest(fz_batch *batch, fz_record *records);
 
 /* Readback: each sequence's last logits row (vocab floats), and its capture
- * store of the last row of the step that asked for it (fz_capture_floats
- * floats: per layer the residual entering the layer, the query after rope,
- * the attention block's addition, the neurons after edits, the feed-forward
- * block's addition; the capture of src/core/capture/capture.h:217-255). */
+ * store of the last row of the step that asked for it: fz_capture_floats
+ * 32-bit words laid out as capture::layout lays them
+ * (src/core/capture/capture.h:217-255, capture.cpp:31-73).  Region 1 is
+ * every layer's neurons after edits; region 2, a layer at a time, the
+ * residual entering the layer, the attention and feed-forward blocks'
+ * additions, the query after rope, the attention weights over the keys the
+ * row read (capture/weights.h; zeros past them), the softmax statistics (m
+ * then l, log2 units, a head) and the readout: the top 64 (logit bits,
+ * token) pairs of the residual the layer leaves through the final norm and
+ * head, the last layer's being the step's own logits' (zeros when the step
+ * asked for no logits).  Token and logit-bit words are integers stored in
+ * the float array. */
 fz_status fz_batch_read_logits(fz_batch *batch, uint32_t sequence, float *out, size_t count);
 size_t fz_capture_floats(const fz_model *model);
 fz_status fz_batch_read_capture(fz_batch *batch, uint32_t sequence, float *out, size_t count);
+
+/* One layer's slots of the capture store (capture::Slot and
+ * capture::LayerSlots, src/core/capture/capture.h:188-207): first word and
+ * width of each, and the layer's attention.  FZ_ERR_NOT_SUPPORTED for a
+ * store past 2^32 words (capture.cpp:37-41 aborts there). */
+typedef struct fz_capture_slot {
+  uint32_t first;
+  uint32_t width;
+} fz_capture_slot;
+typedef struct fz_capture_slots {
+  fz_capture_slot neurons, residual, attention_added, mlp_added, query, weights, stats, readout;
+  uint32_t keys;            /* min(attention window, trained context) */
+  uint32_t query_heads;
+  uint32_t window;          /* attention window, in tokens */
+  uint32_t full_attention;  /* 1: the window reaches the trained context */
+} fz_capture_slots;
+fz_status fz_capture_layout(const fz_model *model, uint32_t layer, fz_capture_slots *out);
 /* Device pointer of sequence s's key or value cache for `layer` ([slots][kv_heads][d] f16). */
 fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int values, void **ptr,
                          uint32_t *slots);

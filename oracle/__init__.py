@@ -78,6 +78,8 @@ def _declare(L):
     L.oracle_ctx_keys.argtypes = [P, C.c_int]; L.oracle_ctx_keys.restype = P
     L.oracle_ctx_values.argtypes = [P, C.c_int]; L.oracle_ctx_values.restype = P
     L.oracle_capture_floats.argtypes = [C.POINTER(Shape)]; L.oracle_capture_floats.restype = C.c_int64
+    L.oracle_capture_slots.argtypes = [C.POINTER(Shape), C.c_int, P, P]
+    L.oracle_capture_slots.restype = C.c_int64
     L.oracle_step.argtypes = [P, C.c_uint32, C.c_int, U32P, P, P, P]
     L.oracle_threads.restype = C.c_int
 
@@ -212,8 +214,24 @@ class OracleModel:
             pass
 
 
+CAPTURE_SLOTS = ("neurons", "residual", "attention_added", "mlp_added", "query", "weights", "stats", "readout")
+
+
+def cshape(shape) -> Shape:
+    return Shape(shape.layers, shape.hidden, shape.ffn, shape.heads, shape.kv_heads, shape.head_dim, shape.vocab,
+                 shape.window, shape.pattern, shape.rope_global, shape.rope_local, shape.eps, shape.context)
+
+
 def capture_layout(shape):
-    """Offsets of each captured vector in one layer's capture, and the per-layer size."""
-    H, Q, F = shape.hidden, shape.heads * shape.head_dim, shape.ffn
-    return {"residual": (0, H), "query": (H, Q), "attn_added": (H + Q, H), "neurons": (2 * H + Q, F),
-            "mlp_added": (2 * H + Q + F, H)}, 3 * H + Q + F
+    """The oracle's capture layout: per layer {slot: first word} and its keys,
+    and the store's size in words (capture/capture.cpp:31-73)."""
+    cs = cshape(shape)
+    layers = []
+    for l in range(shape.layers):
+        first = (C.c_int64 * 8)()
+        keys = C.c_uint32()
+        words = lib().oracle_capture_slots(C.byref(cs), l, C.cast(first, C.c_void_p), C.cast(C.byref(keys), C.c_void_p))
+        d = dict(zip(CAPTURE_SLOTS, list(first)))
+        d["keys"] = keys.value
+        layers.append(d)
+    return layers, int(words)

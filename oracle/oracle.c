@@ -570,12 +570,41 @@ EXPORT uint32_t oracle_ctx_slots(const oracle_ctx *c, int layer) { return c->slo
 EXPORT const uint16_t *oracle_ctx_keys(const oracle_ctx *c, int layer) { return c->kc[layer]; }
 EXPORT const uint16_t *oracle_ctx_values(const oracle_ctx *c, int layer) { return c->vc[layer]; }
 
-/* Per-layer capture of the step's last row: residual entering the layer,
- * query after rope, attention block's addition, neurons after edits, the
- * feed-forward block's addition, in that order. */
-EXPORT int64_t oracle_capture_floats(const oracle_shape *s) {
-    return (int64_t)s->layers * (2 * s->hidden + s->heads * s->head_dim + s->ffn + s->hidden);
+/* The capture store's layout in 32-bit words (capture/capture.cpp:31-73):
+ * region 1 every layer's neurons (ffn words each, in layer order); region 2,
+ * for each layer, its residual, attention addition, feed-forward addition
+ * (hidden each), query (heads x d), weights (heads x keys, keys = min(window,
+ * trained context)), stats (2 x heads) and readout (128 words).  slots[0..7]
+ * get layer `layer`'s first words in that order (neurons first); returns
+ * the store's size. */
+static uint32_t layer_window(const oracle_shape *s, int l) {
+    return s->window == 0 || l % s->pattern == s->pattern - 1 ? (uint32_t)s->context : (uint32_t)s->window;
 }
+
+EXPORT int64_t oracle_capture_slots(const oracle_shape *s, int layer, int64_t *slots, uint32_t *keys_out) {
+    int64_t at = (int64_t)s->layers * s->ffn;
+    for (int l = 0; l < s->layers; l++) {
+        uint32_t w = layer_window(s, l);
+        int64_t keys = w < (uint32_t)s->context ? w : (uint32_t)s->context;
+        int64_t first[8];
+        first[0] = (int64_t)l * s->ffn;
+        first[1] = at;
+        first[2] = first[1] + s->hidden;
+        first[3] = first[2] + s->hidden;
+        first[4] = first[3] + s->hidden;
+        first[5] = first[4] + (int64_t)s->heads * s->head_dim;
+        first[6] = first[5] + (int64_t)s->heads * keys;
+        first[7] = first[6] + 2 * s->heads;
+        at = first[7] + 128;
+        if (l == layer) {
+            if (slots) memcpy(slots, first, sizeof(first));
+            if (keys_out) *keys_out = (uint32_t)keys;
+        }
+    }
+    return at;
+}
+
+EXPORT int64_t oracle_capture_floats(const oracle_shape *s) { return oracle_capture_slots(s, -1, NULL, NULL); }
 
 /* One step (graph/graph.cpp:298-476, arch/gemma3/gemma3.cpp:100-111): embed,
  * 26 x (attention block, gated feed-forward block), and, when `logits_out`
@@ -589,8 +618,12 @@ EXPORT void oracle_step(oracle_ctx *c, uint32_t position, int tokens, const uint
     float *output = malloc(sizeof(float) * T * H), *q = malloc(sizeof(float) * T * QW);
     float *k = malloc(sizeof(float) * T * KW), *v = malloc(sizeof(float) * T * KW);
     float *att = malloc(sizeof(float) * T * QW), *act = malloc(sizeof(float) * (size_t)T * F);
-    int64_t per_layer = 2 * H + QW + F + H;
     float *cap = capture;
+    /* slot first words, per layer: neurons, residual, attention addition,
+     * feed-forward addition, query, weights, stats, readout */
+    int64_t (*slot)[8] = cap ? malloc(sizeof(int64_t[8]) * s->layers) : NULL;
+    uint32_t *keys = cap ? malloc(sizeof(uint32_t) * s->layers) : NULL;
+    for (int l = 0; cap && l < s->layers; l++) oracle_capture_slots(s, l, slot[l], &keys[l]);
     /* embed (gather.wgsl:25-48), scale sqrt(width) in f32 (gemma3.cpp:105) */
     float scale = sqrtf((float)H);
     for (int t = 0; t < T; t++) {
@@ -605,15 +638,15 @@ EXPORT void oracle_step(oracle_ctx *c, uint32_t position, int tokens, const uint
         int global = l % s->pattern == s->pattern - 1;
         uint32_t window = global ? (uint32_t)s->context : (uint32_t)s->window;
         const float *turns = global ? c->turns_global : c->turns_local;
-        float *lc = cap ? cap + l * per_layer : NULL;
+        int lc = cap != NULL;
         /* attention.norm: with the last layer's post-ffw norm add, except layer 0 */
 #pragma omp parallel for
         for (int t = 0; t < T; t++)
             oracle_norm_row(hidden + (int64_t)t * H, l ? output + (int64_t)t * H : NULL,
                             l ? c->layer[l - 1].post_ffw_norm : NULL, L->attn_norm, H, s->eps,
                             normed + (int64_t)t * H,
-                            (l && lc && t == T - 1) ? lc - per_layer + 2 * H + QW + F : NULL);
-        if (lc) memcpy(lc, hidden + (int64_t)(T - 1) * H, sizeof(float) * H);
+                            (l && lc && t == T - 1) ? cap + slot[l - 1][3] : NULL);
+        if (lc) memcpy(cap + slot[l][1], hidden + (int64_t)(T - 1) * H, sizeof(float) * H);
         oracle_matmul(L->q, QW, H, normed, T, q);
         oracle_matmul(L->k, KW, H, normed, T, k);
         oracle_matmul(L->v, KW, H, normed, T, v);
@@ -634,36 +667,68 @@ EXPORT void oracle_step(oracle_ctx *c, uint32_t position, int tokens, const uint
                 for (int i = 0; i < d; i++) { kd[i] = oracle_f16_pack(kh[i]); vd[i] = oracle_f16_pack(vh[i]); }
             }
         }
-        if (lc) memcpy(lc + H, q + (int64_t)(T - 1) * QW, sizeof(float) * QW);
+        if (lc) memcpy(cap + slot[l][4], q + (int64_t)(T - 1) * QW, sizeof(float) * QW);
         int G = s->heads / s->kv_heads;
+        /* The captured row's scores and the fold's statistics
+         * (attention.wgsl:290-295, :394-395), then its weights
+         * (weights.wgsl): exp2(s - m) / l for the keys read, 0 past them. */
+        uint32_t p_last = position + (uint32_t)T - 1;
+        uint32_t count = lc ? (p_last + 1 < keys[l] ? p_last + 1 : keys[l]) : 0;
+        uint32_t earliest = p_last + 1 - count;
 #pragma omp parallel for collapse(2)
         for (int t = 0; t < T; t++)
-            for (int h = 0; h < s->heads; h++)
+            for (int h = 0; h < s->heads; h++) {
+                int cap_row = lc && t == T - 1;
+                float *w = cap_row ? cap + slot[l][5] + (int64_t)h * keys[l] : NULL;
+                float *st = cap_row ? cap + slot[l][6] + 2 * h : NULL;
                 attend_query(q + (int64_t)t * QW + h * d, c->kc[l], c->vc[l], c->slots[l], s->kv_heads, h / G, d,
-                             window, c->scale_log2e, position + (uint32_t)t, att + (int64_t)t * QW + h * d, NULL, 0,
-                             NULL);
+                             window, c->scale_log2e, position + (uint32_t)t, att + (int64_t)t * QW + h * d, w,
+                             earliest, st);
+                if (cap_row)
+                    for (uint32_t i = 0; i < keys[l]; i++) w[i] = i < count ? exp2f(w[i] - st[0]) / st[1] : 0.0f;
+            }
         oracle_matmul(L->o, H, QW, att, T, output);
         /* ffn.norm: add the attention block's output through its post-norm */
 #pragma omp parallel for
         for (int t = 0; t < T; t++)
             oracle_norm_row(hidden + (int64_t)t * H, output + (int64_t)t * H, L->post_attn_norm, L->ffn_norm, H,
-                            s->eps, normed + (int64_t)t * H, (lc && t == T - 1) ? lc + H + QW : NULL);
+                            s->eps, normed + (int64_t)t * H, (lc && t == T - 1) ? cap + slot[l][2] : NULL);
         oracle_gated(L->gate, L->up, F, H, normed, T, act);
         oracle_edit_apply(edit_table, (uint32_t)l, position, T, F, act);
-        if (lc) memcpy(lc + 2 * H + QW, act + (int64_t)(T - 1) * F, sizeof(float) * F);
+        if (lc) memcpy(cap + slot[l][0], act + (int64_t)(T - 1) * F, sizeof(float) * F);
         oracle_matmul(L->down, H, F, act, T, output);
     }
     if (logits_out) {
         float *x = hidden + (int64_t)(T - 1) * H;
-        float *lc = cap ? cap + (s->layers - 1) * per_layer : NULL;
         float fin[8192];
         oracle_norm_row(x, output + (int64_t)(T - 1) * H, c->layer[s->layers - 1].post_ffw_norm, c->output_norm, H,
-                        s->eps, fin, lc ? lc + 2 * H + QW + F : NULL);
+                        s->eps, fin, cap ? cap + slot[s->layers - 1][3] : NULL);
         oracle_matmul(c->token_embd, s->vocab, H, fin, 1, logits_out);
-    } else if (cap) {
-        /* no final norm: the last block's addition is captured as computed */
-        float *lc = cap + (s->layers - 1) * per_layer;
-        memset(lc + 2 * H + QW + F, 0, sizeof(float) * H);
+    }
+    if (cap) {
+        const int L = s->layers;
+        /* No logits: no final norm, so neither the last block's addition nor
+         * the last readout exists; both slots are zero. */
+        if (!logits_out) {
+            memset(cap + slot[L - 1][3], 0, sizeof(float) * H);
+            memset(cap + slot[L - 1][7], 0, sizeof(float) * 128);
+        } else {
+            oracle_topk64(logits_out, s->vocab, (uint32_t *)(cap + slot[L - 1][7]));
+        }
+        /* Readouts of the layers before the last (capture.h:26-33): the
+         * residual each leaves, which is the next layer's captured residual,
+         * through the final norm and the tied head, its top 64. */
+        float *lrow = malloc(sizeof(float) * (size_t)s->vocab);
+        for (int l = 0; l + 1 < L; l++) {
+            float xr[8192], fin[8192];
+            memcpy(xr, cap + slot[l + 1][1], sizeof(float) * H);
+            oracle_norm_row(xr, NULL, NULL, c->output_norm, H, s->eps, fin, NULL);
+            oracle_matmul(c->token_embd, s->vocab, H, fin, 1, lrow);
+            oracle_topk64(lrow, s->vocab, (uint32_t *)(cap + slot[l][7]));
+        }
+        free(lrow);
+        free(slot);
+        free(keys);
     }
     free(hidden); free(normed); free(output); free(q); free(k); free(v); free(att); free(act);
 }

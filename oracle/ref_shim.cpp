@@ -1,7 +1,9 @@
-// C entry points over the reference's own edit and prefix code, compiled in
-// place from the plainsight-systems/frizzle sources (src/core/edit/edit.cpp,
-// src/core/cache/prefix.cpp).  TEST INFRASTRUCTURE ONLY: it pins the oracle's
-// and the engine's edit-table handling to the reference itself.  Built by
+// C entry points over the reference's own edit, prefix and capture-layout
+// code, compiled in place from the plainsight-systems/frizzle sources
+// (src/core/edit/edit.cpp, src/core/cache/prefix.cpp,
+// src/core/capture/capture.cpp).  TEST INFRASTRUCTURE ONLY: it pins the
+// oracle's and the engine's edit-table handling and capture-store layout to
+// the reference itself.  Built by
 // `make ref` into oracle/_ref/, never committed, and only when the reference
 // sources are present.
 #include <cstdint>
@@ -10,6 +12,7 @@
 #include <vector>
 
 #include "core/cache/prefix.h"
+#include "core/capture/capture.h"
 #include "core/edit/edit.h"
 
 namespace {
@@ -64,6 +67,45 @@ float ref_edit_apply(std::uint32_t kind, float value, float neuron) {
 
 std::uint32_t ref_first_edit_difference(const RefEdit* a, std::size_t na, const RefEdit* b, std::size_t nb) {
   return frizzle::cache::first_edit_difference(edits_of(a, na), edits_of(b, nb));
+}
+
+// capture::layout() of a Gemma-3-shaped description: `layers` layers of
+// `width` embedding, `ffn` feed-forward, `heads` query heads of `head_dim`,
+// window `window` except every `pattern`-th layer (pattern - 1, 2 pattern - 1,
+// ...), which attends over the trained context `context`.  Per layer 20 words
+// into out: the eight slots' (first, width) in capture.h's order, then keys,
+// query heads, window and full attention.  Returns the store's words.
+std::uint64_t ref_capture_layout(std::uint32_t layers, std::uint32_t width, std::uint32_t ffn,
+                                 std::uint32_t heads, std::uint32_t head_dim, std::uint32_t window,
+                                 std::uint32_t pattern, std::uint32_t context, std::uint32_t* out) {
+  frizzle::model::ModelDescription m{};
+  m.embedding_width = width;
+  m.trained_context = context;
+  m.layers.resize(layers);
+  for (std::uint32_t l = 0; l < layers; ++l) {
+    auto& d = m.layers[l];
+    d.query_heads = heads;
+    d.key_value_heads = 1;
+    d.head_dimension = head_dim;
+    d.feed_forward_width = ffn;
+    d.attention_window = l % pattern == pattern - 1 ? context : window;
+  }
+  const auto lay = frizzle::capture::layout(m);
+  for (std::uint32_t l = 0; l < layers; ++l) {
+    const auto& s = lay.layers[l];
+    const frizzle::capture::Slot slots[8] = {s.neurons, s.residual, s.attention_added, s.mlp_added,
+                                             s.query,   s.weights,  s.stats,           s.readout};
+    std::uint32_t* o = out + 20 * l;
+    for (int i = 0; i < 8; ++i) {
+      o[2 * i] = slots[i].first;
+      o[2 * i + 1] = slots[i].width;
+    }
+    o[16] = s.keys;
+    o[17] = s.query_heads;
+    o[18] = s.window;
+    o[19] = s.full_attention ? 1u : 0u;
+  }
+  return lay.words;
 }
 
 std::size_t ref_longest_common_prefix(const std::uint32_t* a, std::size_t na, const std::uint32_t* b,

@@ -1,8 +1,10 @@
-"""Writes tests/golden/edits.json from the reference's own edit code.
+"""Writes tests/golden/edits.json and capture_layout.json from the reference's
+own edit and capture code.
 
-Runs Frizzle's ``edit::check`` and ``edit::table`` (src/core/edit/edit.cpp),
-compiled in place into oracle/_ref/libfrizzle_ref.so by ``make -C oracle ref``,
-over the edit sets below, and records what they return.  The sets cover the
+Runs Frizzle's ``edit::check`` and ``edit::table`` (src/core/edit/edit.cpp)
+and ``capture::layout`` (src/core/capture/capture.cpp), compiled in place into
+oracle/_ref/libfrizzle_ref.so by ``make -C oracle ref``, over the edit sets
+and model shapes below, and records what they return.  The sets cover the
 cases the reference's edit tests cover (every fault with its index, overlap
 naming the later edit, touching ranges, placement and saturation, the edit
 kernel's 150-edit known-answer set); the sets themselves are written here.
@@ -129,6 +131,23 @@ def main():
     with open(os.path.join(HERE, "edits.json"), "w") as f:
         json.dump(out, f, indent=0, sort_keys=True)
     print("wrote", len(out), "cases", file=sys.stderr)
+    # capture::layout over Gemma 3 1B's shape and the tiny test model's.
+    lib.ref_capture_layout.restype = C.c_uint64
+    lib.ref_capture_layout.argtypes = [C.c_uint32] * 8 + [C.c_void_p]
+    shapes = {"gemma3_1b": dict(layers=26, width=1152, ffn=6912, heads=4, head_dim=256, window=512, pattern=6,
+                                context=32768),
+              "tiny": dict(layers=7, width=512, ffn=1024, heads=4, head_dim=256, window=16, pattern=6,
+                           context=4096)}
+    lay = {}
+    for name, sh in shapes.items():
+        words = (C.c_uint32 * (20 * sh["layers"]))()
+        total = lib.ref_capture_layout(sh["layers"], sh["width"], sh["ffn"], sh["heads"], sh["head_dim"],
+                                       sh["window"], sh["pattern"], sh["context"], words)
+        lay[name] = {"shape": sh, "words": total,
+                     "layers": [list(words)[20 * l:20 * l + 20] for l in range(sh["layers"])]}
+    with open(os.path.join(HERE, "capture_layout.json"), "w") as f:
+        json.dump(lay, f, indent=0, sort_keys=True)
+    print("wrote capture layouts", {k: v["words"] for k, v in lay.items()}, file=sys.stderr)
 
 
 if __name__ == "__main__":

@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 import oracle
+from frizzle_b200 import capture as C
 from frizzle_b200 import engine, synth
 from frizzle_b200.edits import Edit, SET, SCALE, ZERO, check, table
 
@@ -21,6 +22,40 @@ MAX_ABS, REL_RMS = 1e-2, 1e-3
 
 def prompt(shape, n, seed=0):
     return np.random.default_rng([seed, n]).integers(2, shape.vocab, size=n).astype(np.uint32)
+
+
+def compare_capture(got, want, shape, got_logits=None):
+    """Two capture stores slot kind by slot kind: the activations (neurons,
+    residuals, additions, queries) and the attention weights against the
+    north-star bars; the statistics (m in log2 units, l relative); each
+    readout's logits in order, and its tokens wherever the oracle's logits
+    stand more than twice the logit bar from their neighbours; and the last
+    layer's readout against the top 64 of the GPU's own logits, bit for bit."""
+    lay = C.layout(shape)
+    g, w = C.Capture(got, lay, shape.head_dim), C.Capture(want, lay, shape.head_dim)
+    L = shape.layers
+    r = {"act_rms": rel_rms(g.activations(), w.activations()), "act_abs": max_abs(g.activations(), w.activations())}
+    gw = np.concatenate([g.weights(l).ravel() for l in range(L)])
+    ww = np.concatenate([w.weights(l).ravel() for l in range(L)])
+    r["w_rms"], r["w_abs"] = rel_rms(gw, ww), max_abs(gw, ww)
+    r["w_zeros"] = bool(np.array_equal(gw == 0, ww == 0))
+    gs = np.stack([g.stats(l) for l in range(L)])
+    ws = np.stack([w.stats(l) for l in range(L)])
+    r["m_abs"] = max_abs(gs[..., 0], ws[..., 0])
+    r["l_rel"] = float(np.max(np.abs(gs[..., 1] / ws[..., 1] - 1)))
+    r["readout_abs"], r["readout_tokens"] = 0.0, True
+    for l in range(L):
+        gl, gt = g.readout(l)
+        wl, wt = w.readout(l)
+        r["readout_abs"] = max(r["readout_abs"], max_abs(gl, wl))
+        gap = np.minimum(np.abs(np.diff(wl, prepend=np.inf)), np.abs(np.diff(wl, append=-np.inf)))
+        clear = gap > 2 * MAX_ABS
+        r["readout_tokens"] &= bool(np.array_equal(gt[clear], wt[clear]))
+    if got_logits is not None:
+        gl, gt = g.readout(L - 1)
+        mine = oracle.topk64(got_logits).reshape(64, 2)
+        r["last_readout_own"] = bool(np.array_equal(gl.view(np.uint32), mine[:, 0]) and np.array_equal(gt, mine[:, 1]))
+    return r
 
 
 def run_both(path, shape, n_prompt, steps, edits=None, capture=True, context=4096, block=16):
@@ -37,7 +72,7 @@ def run_both(path, shape, n_prompt, steps, edits=None, capture=True, context=409
         assert check(edits, shape.layers, shape.ffn).ok
         words = np.array(table(edits, shape.layers, n_prompt - 1), dtype=np.uint32)
         batch.set_edits(0, words)
-    out = {"tokens_gpu": [], "tokens_cpu": [], "logit_rms": [], "logit_abs": [], "cap_rms": [], "cap_abs": []}
+    out = {"tokens_gpu": [], "tokens_cpu": [], "logit_rms": [], "logit_abs": [], "captures": []}
     # Prefill in blocks, the last asking for logits.
     pos = 0
     while pos < n_prompt:
@@ -53,15 +88,17 @@ def run_both(path, shape, n_prompt, steps, edits=None, capture=True, context=409
         out["tokens_cpu"].append(int(np.argmax(want_logits)))
         out["logit_rms"].append(rel_rms(got, want_logits))
         out["logit_abs"].append(max_abs(got, want_logits))
-        if capture and i == 0:
+        if capture and i < 2 and want_cap is not None:
+            # The prompt's last step, then the first decode step (one row).
             cap = batch.capture(0)
-            out["cap_rms"].append(rel_rms(cap, want_cap))
-            out["cap_abs"].append(max_abs(cap, want_cap))
-            out["cap_layers"] = (cap, want_cap)
+            out["captures"].append(compare_capture(cap, want_cap, shape, got))
+            if i == 0:
+                out["cap_layers"] = (cap, want_cap)
         if i + 1 < steps:
             nxt = out["tokens_cpu"][-1]
-            batch.step(n_prompt + i, fed=True, tokens=1, logits=True)
-            want_logits, _ = orc.step(n_prompt + i, [nxt], logits=True, edit_table=words)
+            cap_now = capture and i == 0
+            batch.step(n_prompt + i, fed=True, tokens=1, logits=True, capture=cap_now)
+            want_logits, want_cap = orc.step(n_prompt + i, [nxt], logits=True, edit_table=words, capture=cap_now)
     kv = []
     for layer in (0, shape.pattern - 1):
         ptr, slots = batch.cache(0, layer)
@@ -77,9 +114,12 @@ def assert_parity(out):
     assert out["tokens_gpu"] == out["tokens_cpu"], (out["tokens_gpu"], out["tokens_cpu"])
     assert max(out["logit_rms"]) < REL_RMS, max(out["logit_rms"])
     assert max(out["logit_abs"]) < MAX_ABS, max(out["logit_abs"])
-    if out["cap_rms"]:
-        assert max(out["cap_rms"]) < REL_RMS
-        assert max(out["cap_abs"]) < MAX_ABS
+    for c in out["captures"]:
+        assert c["act_rms"] < REL_RMS and c["act_abs"] < MAX_ABS, c
+        assert c["w_rms"] < REL_RMS and c["w_abs"] < MAX_ABS and c["w_zeros"], c
+        assert c["m_abs"] < MAX_ABS and c["l_rel"] < REL_RMS, c
+        assert c["readout_abs"] < MAX_ABS and c["readout_tokens"], c
+        assert c["last_readout_own"], c
 
 
 def test_tiny_model_greedy(tiny_model_path):
@@ -93,8 +133,7 @@ def test_tiny_model_steered(tiny_model_path):
     out = run_both(tiny_model_path, s, 9, 8, edits=edits)
     assert_parity(out)
     cap, _ = out["cap_layers"]
-    per = 3 * s.hidden + s.heads * s.head_dim + s.ffn
-    neurons = cap[3 * per + 2 * s.hidden + s.heads * s.head_dim:][:s.ffn]
+    neurons = C.Capture(cap, C.layout(s), s.head_dim).neurons(3)
     assert neurons[5] == np.float32(8.0) and neurons[900] == 0.0
 
 
@@ -308,3 +347,58 @@ def test_two_steps_in_flight_report_in_order(tiny_model_path):
     model.free()
     dev.close()
     assert got[1] == expect, (got[1], expect)
+
+
+@pytest.mark.parametrize("path_fixture,shape", [("tiny_model_path", synth.TINY),
+                                                ("gemma_model_path", synth.GEMMA3_1B)])
+def test_capture_layout_through_the_abi(request, path_fixture, shape):
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, request.getfixturevalue(path_fixture))
+    lay = C.layout(shape)
+    assert model.capture_floats == lay.words
+    for l in range(shape.layers):
+        got = model.capture_layout(l)
+        want = lay.layers[l]
+        for n in C.SLOTS:
+            assert got[n] == getattr(want, n), (l, n)
+        assert (got["keys"], got["query_heads"], got["window"], got["full_attention"]) == \
+            (want.keys, want.query_heads, want.window, want.full_attention)
+    model.free()
+    dev.close()
+
+
+@pytest.mark.parametrize("S", [3])
+def test_tiny_model_batch_capture(tiny_model_path, S):
+    """Each sequence's store against its own oracle run: the prompt's last
+    step (rows of three sequences) and a one-row decode step (the persistent
+    decode kernel), one sequence steered."""
+    s = synth.TINY
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, tiny_model_path)
+    batch = engine.Batch(model, S, 512)
+    prompts = [prompt(s, 12, seed=21 + q) for q in range(S)]
+    words = [None] * S
+    words[1] = np.array(table([Edit(3, 5, SET, 8.0, 0)], s.layers, 11), dtype=np.uint32)
+    batch.set_edits(1, words[1])
+    batch.step(0, np.array(prompts, dtype=np.uint32), tokens=12, logits=True, capture=True)
+    toks = batch.tokens()
+    caps = [batch.capture(q) for q in range(S)]
+    logits = [batch.logits(q) for q in range(S)]
+    batch.step(12, fed=True, tokens=1, logits=True, capture=True)
+    batch.tokens()
+    caps2 = [batch.capture(q) for q in range(S)]
+    logits2 = [batch.logits(q) for q in range(S)]
+    batch.free()
+    model.free()
+    dev.close()
+    for q in range(S):
+        orc = oracle.OracleModel(tiny_model_path, context=512)
+        want_logits, want_cap = orc.step(0, prompts[q], logits=True, edit_table=words[q], capture=True)
+        assert toks[q] == int(np.argmax(want_logits))
+        _, want_cap2 = orc.step(12, [toks[q]], logits=True, edit_table=words[q], capture=True)
+        orc.close()
+        for c in (compare_capture(caps[q], want_cap, s, logits[q]), compare_capture(caps2[q], want_cap2, s, logits2[q])):
+            assert c["act_rms"] < REL_RMS and c["act_abs"] < MAX_ABS, (q, c)
+            assert c["w_rms"] < REL_RMS and c["w_abs"] < MAX_ABS and c["w_zeros"], (q, c)
+            assert c["m_abs"] < MAX_ABS and c["l_rel"] < REL_RMS, (q, c)
+            assert c["readout_abs"] < MAX_ABS and c["readout_tokens"] and c["last_readout_own"], (q, c)
