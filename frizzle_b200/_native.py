@@ -82,6 +82,9 @@ SIGNATURES = {
     "fz_batch_read_capture": (C.c_int, [VP, U32, VP, C.c_size_t]),
     "fz_capture_layout": (C.c_int, [VP, U32, C.POINTER(CaptureSlots)]),
     "fz_batch_cache": (C.c_int, [VP, U32, U32, C.c_int, C.POINTER(VP), C.POINTER(U32)]),
+    "fz_batch_truncate": (C.c_int, [VP, U32, C.POINTER(U32)]),
+    "fz_batch_cache_state": (C.c_int, [VP, C.POINTER(U32), C.POINTER(U32)]),
+    "fz_cache_truncate_keeps": (C.c_int, [VP, VP, U32, U32, U32]),
     "fz_batch_trace": (C.c_int, [VP, C.c_int]),
     "fz_batch_read_trace": (C.c_int, [VP, VP, C.c_size_t, C.POINTER(U32), C.POINTER(U32)]),
     "fz_q4_0_codes_bytes": (C.c_size_t, [U32, U32]),

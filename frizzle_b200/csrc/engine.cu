@@ -246,6 +246,11 @@ struct fz_batch {
   int next_slot = 0;
   int last_slot = -1;
   uint32_t serial = 1;             // steps run (the decode kernel's epochs)
+  // The KV cache's bookkeeping (cache::KvCache, src/core/cache/kv.h): the
+  // tokens every sequence's cache holds, and the most written since it was
+  // last emptied; each layer's attention window beside b.slots.
+  uint32_t length = 0, written = 0;
+  std::vector<uint32_t> windows;
   // The decode kernel's flag-in-data words: QKV products, attention output and
   // few-split partials, gated activation.
   unsigned long long *qkv_ll = nullptr, *attn_ll = nullptr, *part_o_ll = nullptr, *part_ml_ll = nullptr,
@@ -1170,6 +1175,7 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     b->kc.push_back(k);
     b->vc.push_back(v);
     b->slots.push_back(slots);
+    b->windows.push_back(L.window);
     b->seq_stride.push_back(per_seq);
     // The per-op attention splits its keys kSplitKeys at a time; the decode
     // kernel into up to one split a CTA (kDecodeSplitKeys keys at least).
@@ -1356,6 +1362,16 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   if (step->logits && step->temperature > 0.f && step->top_k == 0) return fail(FZ_ERR_ARGUMENT, "top_k 0");
   if (step->capture && !capture_aligned(capture_layout(s)))
     return fail(FZ_ERR_NOT_SUPPORTED, "a capture layout whose vector slots are not 16-byte aligned");
+  // The step's first position is the cache's length: a later one would read
+  // keys nobody wrote, an earlier one rewinds the cache first (kv.h:36-44).
+  if (step->position > b->length) return fail(FZ_ERR_ARGUMENT, "the step starts past the tokens the cache holds");
+  if (step->position < b->length &&
+      !fz_cache_truncate_keeps(b->windows.data(), b->slots.data(), s.layers, b->written, step->position)) {
+    b->length = b->written = 0;
+    return fail(FZ_ERR_ARGUMENT,
+                "a rewind past the rollback reserve: the cache no longer holds the window before this position, "
+                "and was emptied; prefill from position 0");
+  }
   cudaStream_t st = b->model->dev->stream;
   FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
   if (T * b->S > b->rows_cap) {
@@ -1396,6 +1412,42 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   sl.pending = true;
   b->last_slot = b->next_slot;
   b->next_slot ^= 1;
+  // KvCache::advance: the step's rows are written.
+  b->length = step->position + T;
+  b->written = std::max(b->written, b->length);
+  return FZ_OK;
+}
+
+int fz_cache_truncate_keeps(const uint32_t* windows, const uint32_t* slots, uint32_t layers, uint32_t written,
+                            uint32_t tokens) {
+  if (tokens == 0) return 1;
+  for (uint32_t l = 0; l < layers; l++) {
+    // The next query, at `tokens`, reads back to tokens - window + 1; the
+    // ring still holds back to written - slots.
+    if (windows[l] <= 1) continue;
+    const uint32_t oldest_held = written > slots[l] ? written - slots[l] : 0;
+    const uint32_t oldest_read = tokens >= windows[l] ? tokens - windows[l] + 1 : 0;
+    if (oldest_held > oldest_read) return 0;
+  }
+  return 1;
+}
+
+fz_status fz_batch_truncate(fz_batch* b, uint32_t tokens, uint32_t* kept) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  const uint32_t t = std::min(tokens, b->length);
+  if (t > 0 && fz_cache_truncate_keeps(b->windows.data(), b->slots.data(), b->model->shape.layers, b->written, t)) {
+    b->length = t;
+  } else {
+    b->length = b->written = 0;
+  }
+  if (kept) *kept = b->length;
+  return FZ_OK;
+}
+
+fz_status fz_batch_cache_state(fz_batch* b, uint32_t* length, uint32_t* written) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  if (length) *length = b->length;
+  if (written) *written = b->written;
   return FZ_OK;
 }
 

@@ -19,6 +19,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 from . import edits as E
+from . import prefix as P
 from ._native import CaptureSlots, FzError, ModelInfo, Record, Step, check, load
 from .capture import SLOTS, Capture
 from .capture import layout as capture_layout
@@ -203,6 +204,18 @@ class Batch:
         info = self.model.info
         return Capture(self.capture(sequence), capture_layout(info), info.head_dim)
 
+    def truncate(self, tokens: int) -> int:
+        """KvCache::truncate (clamped to the length): the tokens kept."""
+        kept = C.c_uint32()
+        check(self.lib.fz_batch_truncate(self.handle, tokens, C.byref(kept)))
+        return kept.value
+
+    def cache_state(self):
+        """(tokens held, high-water mark) of the batch's KV cache."""
+        length, written = C.c_uint32(), C.c_uint32()
+        check(self.lib.fz_batch_cache_state(self.handle, C.byref(length), C.byref(written)))
+        return length.value, written.value
+
     def cache(self, sequence: int, layer: int, values: bool = False):
         p = C.c_void_p()
         slots = C.c_uint32()
@@ -223,12 +236,14 @@ class Turn:
 
 
 def generate(batch: Batch, prompts, steps: int, sampling: Sampling = Sampling(), edit_sets=None,
-             seeds=None, keep_logits: bool = False, capture: bool = False) -> Turn:
+             seeds=None, keep_logits: bool = False, capture: bool = False, start: int = 0) -> Turn:
     """Prefill every sequence's prompt (same length) then `steps` fed decode steps.
 
     ``edit_sets[s]`` is sequence s's list of ``edits.Edit`` with ranges in steps
     from the prompt's last position (origin = prompt length - 1, as
-    Engine::generate places them).  Returns each sequence's drawn tokens.
+    Engine::generate places them).  The prefill starts at `start`: the
+    tokens before it are the ones the cache already holds (``Session``).
+    Returns each sequence's drawn tokens.
     """
     S = batch.sequences
     prompts = [list(p) for p in prompts]
@@ -248,7 +263,9 @@ def generate(batch: Batch, prompts, steps: int, sampling: Sampling = Sampling(),
             batch.set_edits(s, None)
     block = MAX_ROWS // S
     turn = Turn(tokens=[[] for _ in range(S)])
-    pos = 0
+    if not 0 <= start < n:
+        raise ValueError("the prefill must start inside the prompt")
+    pos = start
     while pos < n:
         t = min(block, n - pos)
         last = pos + t == n
@@ -264,3 +281,42 @@ def generate(batch: Batch, prompts, steps: int, sampling: Sampling = Sampling(),
         if i + 1 < steps:
             batch.step(n + i, fed=True, tokens=1, logits=True, sampling=sampling, seeds=seeds)
     return turn
+
+
+class Session:
+    """Turns on one batch that reuse its KV cache across runs.
+
+    Runtime::start with Engine::generate's rewind (runtime.cpp:236-275,
+    engine.cpp:690-701): each sequence's held tokens, and the placed edits of
+    the run that wrote its cache, are kept between turns.  A turn keeps what
+    every sequence may reuse (``prefix.reusable``: the common prefix, cut at
+    the first edit difference and short of the prompt's last token), which
+    the cache's window rule may still empty (``Batch.truncate``), and
+    prefills the rest.  The reply's tokens fed back in stay cached, so the
+    next turn's prompt may extend this one's conversation, or the same
+    prompt may run again with other edits from the position they change."""
+
+    def __init__(self, batch: Batch):
+        self.batch = batch
+        self.held = [[] for _ in range(batch.sequences)]
+        self.held_edits = [[] for _ in range(batch.sequences)]
+        self.reused = 0
+
+    def run(self, prompts, steps: int, sampling: Sampling = Sampling(), edit_sets=None, seeds=None,
+            keep_logits: bool = False, capture: bool = False) -> Turn:
+        S = self.batch.sequences
+        prompts = [[int(t) for t in p] for p in prompts]
+        if len(prompts) != S or len({len(p) for p in prompts}) != 1 or not prompts[0]:
+            raise ValueError("one non-empty prompt a sequence, all the same length")
+        origin = len(prompts[0]) - 1
+        sets = list(edit_sets or [None] * S)
+        placed = [E.placed(es, origin) if es else [] for es in sets]
+        keep = min(P.reusable(self.held[s], self.held_edits[s], prompts[s], placed[s]) for s in range(S))
+        self.reused = self.batch.truncate(keep)
+        turn = generate(self.batch, prompts, steps, sampling, sets, seeds, keep_logits, capture,
+                        start=self.reused)
+        for s in range(S):
+            self.held[s] = prompts[s] + turn.tokens[s][:steps - 1]
+            self.held_edits[s] = placed[s]
+        return turn
+

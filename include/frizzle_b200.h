@@ -182,6 +182,23 @@ typedef struct fz_capture_slots {
   uint32_t full_attention;  /* 1: the window reaches the trained context */
 } fz_capture_slots;
 fz_status fz_capture_layout(const fz_model *model, uint32_t layer, fz_capture_slots *out);
+/* The KV cache's bookkeeping (cache::KvCache, src/core/cache/kv.h:15-63),
+ * shared by the batch's sequences, which step together.  A step advances
+ * the cache to position + tokens; its position must be the cache's length
+ * or earlier, and an earlier one rewinds the cache first (a rewind that
+ * fails, below, empties the cache and refuses the step with
+ * FZ_ERR_ARGUMENT).  fz_batch_truncate(tokens) is KvCache::truncate with
+ * Runtime::rewind's clamp (runtime.cpp:291-299): it keeps min(tokens,
+ * length) tokens when every window layer still holds the window before
+ * that position, otherwise it empties the cache; *kept is the new length.
+ * fz_batch_cache_state reports the length and the high-water mark. */
+fz_status fz_batch_truncate(fz_batch *batch, uint32_t tokens, uint32_t *kept);
+fz_status fz_batch_cache_state(fz_batch *batch, uint32_t *length, uint32_t *written);
+/* KvCache::truncate's rule, as a pure function of the layers' windows and
+ * ring slots, the high-water mark and the tokens kept: 1 when the cache
+ * survives the truncation (kv.h:56-63).  Host only; needs no device. */
+int fz_cache_truncate_keeps(const uint32_t *windows, const uint32_t *slots, uint32_t layers, uint32_t written,
+                            uint32_t tokens);
 /* Device pointer of sequence s's key or value cache for `layer` ([slots][kv_heads][d] f16). */
 fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int values, void **ptr,
                          uint32_t *slots);

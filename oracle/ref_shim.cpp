@@ -1,6 +1,7 @@
-// C entry points over the reference's own edit, prefix and capture-layout
-// code, compiled in place from the plainsight-systems/frizzle sources
-// (src/core/edit/edit.cpp, src/core/cache/prefix.cpp,
+// C entry points over the reference's own edit, prefix, KV-cache bookkeeping
+// and capture-layout code, compiled in place from the
+// plainsight-systems/frizzle sources (src/core/edit/edit.cpp,
+// src/core/cache/prefix.cpp, src/core/cache/kv.cpp,
 // src/core/capture/capture.cpp).  TEST INFRASTRUCTURE ONLY: it pins the
 // oracle's and the engine's edit-table handling and capture-store layout to
 // the reference itself.  Built by
@@ -11,6 +12,7 @@
 #include <span>
 #include <vector>
 
+#include "core/cache/kv.h"
 #include "core/cache/prefix.h"
 #include "core/capture/capture.h"
 #include "core/edit/edit.h"
@@ -106,6 +108,32 @@ std::uint64_t ref_capture_layout(std::uint32_t layers, std::uint32_t width, std:
     o[19] = s.full_attention ? 1u : 0u;
   }
   return lay.words;
+}
+
+// A KvCache over `layers` layers of the given windows and ring slots, run
+// through n operations: op[2i] 0 = advance(op[2i + 1]), 1 =
+// truncate(op[2i + 1]).  After operation i, out[2i] is its result (truncate's
+// return, or the new length after an advance) and out[2i + 1] the length.
+void ref_kv_run(const std::uint32_t* windows, const std::uint32_t* slots, std::uint32_t layers,
+                std::uint32_t capacity, const std::uint32_t* op, std::size_t n, std::uint32_t* out) {
+  frizzle::model::ModelDescription m{};
+  m.layers.resize(layers);
+  frizzle::residency::ResidencyPlan plan{};
+  plan.cache.resize(layers);
+  for (std::uint32_t l = 0; l < layers; ++l) {
+    m.layers[l].attention_window = windows[l];
+    plan.cache[l].slots = slots[l];
+  }
+  frizzle::cache::KvCache kv(m, plan, frizzle::policy::CachePrecision{}, capacity);
+  for (std::size_t i = 0; i < n; ++i) {
+    if (op[2 * i] == 0) {
+      kv.advance(op[2 * i + 1]);
+      out[2 * i] = kv.length();
+    } else {
+      out[2 * i] = kv.truncate(op[2 * i + 1]);
+    }
+    out[2 * i + 1] = kv.length();
+  }
 }
 
 std::size_t ref_longest_common_prefix(const std::uint32_t* a, std::size_t na, const std::uint32_t* b,

@@ -1,10 +1,13 @@
-"""Writes tests/golden/edits.json and capture_layout.json from the reference's
-own edit and capture code.
+"""Writes tests/golden/edits.json, capture_layout.json and prefix.json from
+the reference's own edit, capture and cache code.
 
-Runs Frizzle's ``edit::check`` and ``edit::table`` (src/core/edit/edit.cpp)
-and ``capture::layout`` (src/core/capture/capture.cpp), compiled in place into
-oracle/_ref/libfrizzle_ref.so by ``make -C oracle ref``, over the edit sets
-and model shapes below, and records what they return.  The sets cover the
+Runs Frizzle's ``edit::check`` and ``edit::table`` (src/core/edit/edit.cpp),
+``capture::layout`` (src/core/capture/capture.cpp), ``longest_common_prefix``
+and ``first_edit_difference`` (src/core/cache/prefix.cpp) and
+``KvCache::truncate``/``advance`` (src/core/cache/kv.cpp), compiled in place
+into oracle/_ref/libfrizzle_ref.so by ``make -C oracle ref``, over the edit
+sets, model shapes, token sequences and cache histories below, and records
+what they return.  The sets cover the
 cases the reference's edit tests cover (every fault with its index, overlap
 naming the later edit, touching ranges, placement and saturation, the edit
 kernel's 150-edit known-answer set); the sets themselves are written here.
@@ -148,6 +151,119 @@ def main():
     with open(os.path.join(HERE, "capture_layout.json"), "w") as f:
         json.dump(lay, f, indent=0, sort_keys=True)
     print("wrote capture layouts", {k: v["words"] for k, v in lay.items()}, file=sys.stderr)
+    write_prefix(lib)
+
+
+def prefix_cases():
+    """(cached, incoming) token sequences and placed edit sets."""
+    import random
+    rng = random.Random(7)
+    seq = [rng.randrange(2, 262144) for _ in range(300)]
+    tokens = [([], []), (seq[:10], []), ([], seq[:10]), (seq, seq), (seq[:120], seq), (seq, seq[:120]),
+              (seq[:50] + [1] + seq[51:], seq), ([5] + seq[1:], seq), (seq[:299] + [3], seq)]
+    A = e(13, 7, SET, 4.0, 3, 9)
+    edits = [
+        ([], []),
+        ([A], [A]),
+        ([A], [e(13, 7, SET, 4.5, 3, 9)]),                            # value differs: its start
+        ([e(13, 7, SET, 4.0, 3, 5), e(13, 7, SET, 4.0, 5, 9)], [A]),  # split ranges are one edit
+        ([A], [e(13, 7, SCALE, 4.0, 3, 9)]),                          # kind differs
+        ([A], [e(13, 7, SET, 4.0, 3, 7)]),                            # shorter range: its end
+        ([A], [e(13, 7, SET, 4.0, 5, 9)]),                            # later start
+        ([A], []), ([], [A]),                                          # only in one set
+        ([e(2, 1, SET, 0.0, 0, 4)], [e(2, 1, SET, -0.0, 0, 4)]),      # value bits differ
+        ([e(2, 1, SET, float("nan"), 0, 4)], [e(2, 1, SET, float("nan"), 0, 4)]),
+        ([A, e(2, 1, ZERO, 0.0, 10, TO_END)], [e(2, 1, ZERO, 0.0, 10, TO_END), A]),  # order does not matter
+        ([A, e(2, 1, ZERO, 0.0, 10, TO_END)], [A, e(2, 1, ZERO, 0.0, 12, TO_END)]),
+        ([e(0, 0, SET, 1.0, 0, TO_END)], [e(0, 0, SET, 1.0, 0, 100)]),
+        ([e(4, 9, SCALE, 2.0, 20, 30), e(4, 9, SCALE, 2.0, 40, 50)], [e(4, 9, SCALE, 2.0, 20, 30)]),
+    ]
+    for trial in range(12):
+        base = []
+        for _ in range(rng.randrange(1, 40)):
+            a = rng.randrange(0, 300)
+            base.append(e(rng.randrange(26), rng.randrange(6912), rng.randrange(3), float(rng.randrange(-8, 9)) / 2,
+                          a, a + rng.randrange(1, 60) if rng.random() < 0.8 else TO_END))
+        other = list(base)
+        rng.shuffle(other)
+        if trial % 3:
+            i = rng.randrange(len(other))
+            l, n, k, v, a, u = other[i]
+            other[i] = (l, n, k, v + 0.5, a, u) if trial % 3 == 1 else (l, n, k, v, a + 1, u)
+        edits.append((base, other))
+    return tokens, edits
+
+
+def kv_cases():
+    """KvCache histories: (windows, slots, capacity, operations)."""
+    import random
+    rng = random.Random(11)
+    g_win = [32768 if l % 6 == 5 else 512 for l in range(26)]
+    g_slots = [8192 if w == 32768 else 5120 for w in g_win]
+    t_win = [4096 if l % 6 == 5 else 16 for l in range(7)]
+    t_slots = [2048 if w == 4096 else 544 for w in t_win]
+    out = []
+    for windows, slots, cap in ((g_win, g_slots, 8192), (t_win, t_slots, 2048)):
+        for trial in range(6):
+            ops, length = [], 0
+            for _ in range(40):
+                if length and rng.random() < 0.45:
+                    t = rng.choice([0, length, rng.randrange(length + 1), max(0, length - rng.randrange(1, 700))])
+                    ops.append((1, t))
+                    length = t  # provisional: the reference's answer decides
+                else:
+                    n = min(cap - length, rng.choice([1, 16, 300, 1500, rng.randrange(1, 4000)]))
+                    if n <= 0:
+                        continue
+                    ops.append((0, n))
+                    length += n
+            out.append([windows, slots, cap, ops])
+    return out
+
+
+def write_prefix(lib):
+    lib.ref_longest_common_prefix.restype = C.c_size_t
+    lib.ref_longest_common_prefix.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]
+    lib.ref_first_edit_difference.restype = C.c_uint32
+    lib.ref_first_edit_difference.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]
+    lib.ref_kv_run.restype = None
+    lib.ref_kv_run.argtypes = [C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p]
+    tokens, edits = prefix_cases()
+    out = {"lcp": [], "fed": [], "kv": []}
+    for a, b in tokens:
+        x = (C.c_uint32 * max(1, len(a)))(*a)
+        y = (C.c_uint32 * max(1, len(b)))(*b)
+        out["lcp"].append([a, b, lib.ref_longest_common_prefix(x, len(a), y, len(b))])
+    for a, b in edits:
+        x = (RefEdit * max(1, len(a)))(*[RefEdit(*r) for r in a])
+        y = (RefEdit * max(1, len(b)))(*[RefEdit(*r) for r in b])
+        enc = lambda rs: [[l, n, k, ("nan" if v != v else v), f, u] for l, n, k, v, f, u in rs]
+        out["fed"].append([enc(a), enc(b), lib.ref_first_edit_difference(x, len(a), y, len(b))])
+    # The histories' truncations may be refused (the cache empties): replay
+    # them so each later operation stays within the reference's length.
+    for windows, slots, cap, ops in kv_cases():
+        fixed, res = [], []
+        for op in ops:
+            trial = fixed + [op]
+            w = (C.c_uint32 * len(windows))(*windows)
+            s_ = (C.c_uint32 * len(slots))(*slots)
+            o = (C.c_uint32 * (2 * len(trial)))(*[v for p in trial for v in p])
+            r = (C.c_uint32 * (2 * len(trial)))()
+            length = 0 if not fixed else res[-1][1]
+            if op[0] == 1 and op[1] > length:
+                op = (1, length)
+            if op[0] == 0 and length + op[1] > cap:
+                continue
+            trial = fixed + [op]
+            o = (C.c_uint32 * (2 * len(trial)))(*[v for p in trial for v in p])
+            lib.ref_kv_run(w, s_, len(windows), cap, o, len(trial), r)
+            fixed = trial
+            res = [(r[2 * i], r[2 * i + 1]) for i in range(len(trial))]
+        out["kv"].append({"windows": windows, "slots": slots, "capacity": cap,
+                          "ops": [list(p) for p in fixed], "results": [list(p) for p in res]})
+    with open(os.path.join(HERE, "prefix.json"), "w") as f:
+        json.dump(out, f, indent=0, sort_keys=True)
+    print("wrote prefix cases", {k: len(v) for k, v in out.items()}, file=sys.stderr)
 
 
 if __name__ == "__main__":

@@ -402,3 +402,62 @@ def test_tiny_model_batch_capture(tiny_model_path, S):
             assert c["w_rms"] < REL_RMS and c["w_abs"] < MAX_ABS and c["w_zeros"], (q, c)
             assert c["m_abs"] < MAX_ABS and c["l_rel"] < REL_RMS, (q, c)
             assert c["readout_abs"] < MAX_ABS and c["readout_tokens"] and c["last_readout_own"], (q, c)
+
+
+def oracle_greedy(path, ids, steps, edits=None, context=512):
+    """The oracle's greedy tokens and first logits for a prompt from position 0."""
+    orc = oracle.OracleModel(path, context=context)
+    words = None
+    if edits:
+        words = np.array(table(edits, synth.TINY.layers, len(ids) - 1), dtype=np.uint32)
+    logits, _ = orc.step(0, np.asarray(ids, dtype=np.uint32), logits=True, edit_table=words)
+    first = logits
+    toks = [int(np.argmax(logits))]
+    for i in range(steps - 1):
+        logits, _ = orc.step(len(ids) + i, [toks[-1]], logits=True, edit_table=words)
+        toks.append(int(np.argmax(logits)))
+    orc.close()
+    return toks, first
+
+
+def test_session_reuses_the_cache_across_turns(tiny_model_path):
+    """Runtime::start's reuse: a turn extending the last one's conversation
+    prefills only its new tokens; the same prompt with edits from a later
+    position recomputes from there; a rewind past the rollback reserve empties
+    the cache.  Every turn's tokens are the oracle's from scratch."""
+    s = synth.TINY
+    dev = engine.Device(0)
+    model = engine.Model.from_file(dev, tiny_model_path)
+    batch = engine.Batch(model, 1, 1024, rollback=0)
+    sess = engine.Session(batch)
+    a = list(prompt(s, 20, seed=31))
+    t1 = sess.run([a], 6, keep_logits=True)
+    assert sess.reused == 0
+    assert t1.tokens[0] == oracle_greedy(tiny_model_path, a, 6)[0]
+    assert batch.cache_state()[0] == 25
+    # The conversation goes on: the held prompt and reply, then new tokens.
+    b = a + t1.tokens[0][:5] + list(prompt(s, 7, seed=32))
+    t2 = sess.run([b], 6, keep_logits=True)
+    assert sess.reused == 25
+    want, first = oracle_greedy(tiny_model_path, b, 6)
+    assert t2.tokens[0] == want
+    assert rel_rms(t2.logits[0][0], first) < REL_RMS and max_abs(t2.logits[0][0], first) < MAX_ABS
+    # The same prompt, steered from its last position: only that position is recomputed.
+    edits = [Edit(3, 5, SET, 8.0, 0), Edit(4, 900, ZERO, 0.0, 0)]
+    t3 = sess.run([b], 4, edit_sets=[edits])
+    assert sess.reused == len(b) - 1
+    assert t3.tokens[0] == oracle_greedy(tiny_model_path, b, 4, edits)[0]
+    # A step past the cached tokens is refused.
+    with pytest.raises(engine.FzError):
+        batch.step(batch.cache_state()[0] + 1, [1], tokens=1)
+    # Past the reserve: 600 more tokens, then a prompt sharing only 10 of them.
+    long = b + list(prompt(s, 600, seed=33))
+    sess.run([long], 2)
+    assert sess.reused == len(b) - 1   # the last turn's edits were in force from there
+    short = long[:10] + list(prompt(s, 5, seed=34))
+    t5 = sess.run([short], 3)
+    assert sess.reused == 0        # the window layers' rings have moved on
+    assert t5.tokens[0] == oracle_greedy(tiny_model_path, short, 3)[0]
+    batch.free()
+    model.free()
+    dev.close()
