@@ -27,7 +27,8 @@ def prompt(shape, n, seed=0):
 def compare_capture(got, want, shape, got_logits=None):
     """Two capture stores slot kind by slot kind: the activations (neurons,
     residuals, additions, queries) and the attention weights against the
-    north-star bars; the statistics (m in log2 units, l relative); each
+    north-star bars; the statistics (m in log2 units within the max-abs bar,
+    the sums l within the relative-RMS bar over every layer and head); each
     readout's logits in order, and its tokens wherever the oracle's logits
     stand more than twice the logit bar from their neighbours; and the last
     layer's readout against the top 64 of the GPU's own logits, bit for bit."""
@@ -42,7 +43,8 @@ def compare_capture(got, want, shape, got_logits=None):
     gs = np.stack([g.stats(l) for l in range(L)])
     ws = np.stack([w.stats(l) for l in range(L)])
     r["m_abs"] = max_abs(gs[..., 0], ws[..., 0])
-    r["l_rel"] = float(np.max(np.abs(gs[..., 1] / ws[..., 1] - 1)))
+    r["l_rms"] = rel_rms(gs[..., 1], ws[..., 1])
+    r["l_rel_max"] = float(np.max(np.abs(gs[..., 1] / ws[..., 1] - 1)))
     r["readout_abs"], r["readout_tokens"] = 0.0, True
     for l in range(L):
         gl, gt = g.readout(l)
@@ -117,7 +119,7 @@ def assert_parity(out):
     for c in out["captures"]:
         assert c["act_rms"] < REL_RMS and c["act_abs"] < MAX_ABS, c
         assert c["w_rms"] < REL_RMS and c["w_abs"] < MAX_ABS and c["w_zeros"], c
-        assert c["m_abs"] < MAX_ABS and c["l_rel"] < REL_RMS, c
+        assert c["m_abs"] < MAX_ABS and c["l_rms"] < REL_RMS, c
         assert c["readout_abs"] < MAX_ABS and c["readout_tokens"], c
         assert c["last_readout_own"], c
 
@@ -400,7 +402,7 @@ def test_tiny_model_batch_capture(tiny_model_path, S):
         for c in (compare_capture(caps[q], want_cap, s, logits[q]), compare_capture(caps2[q], want_cap2, s, logits2[q])):
             assert c["act_rms"] < REL_RMS and c["act_abs"] < MAX_ABS, (q, c)
             assert c["w_rms"] < REL_RMS and c["w_abs"] < MAX_ABS and c["w_zeros"], (q, c)
-            assert c["m_abs"] < MAX_ABS and c["l_rel"] < REL_RMS, (q, c)
+            assert c["m_abs"] < MAX_ABS and c["l_rms"] < REL_RMS, (q, c)
             assert c["readout_abs"] < MAX_ABS and c["readout_tokens"] and c["last_readout_own"], (q, c)
 
 
