@@ -29,6 +29,7 @@ using namespace q4dev;
 constexpr int kThreads = 256;   // every matvec CTA: 8 warps, the norm's 256 invocations
 constexpr int kWarps = kThreads / 32;
 constexpr int kU = 4;           // block pairs a warp loads at once
+constexpr int kUW = 6;          // the same, when a warp streams whole row groups (K = 1152: 3 batches)
 
 // A warp's registers for kU block pairs of one row group.
 struct Batch {
@@ -75,6 +76,53 @@ FZ_DEV void compute_batch(const Batch& b, int bp, int bp1, const uint2* xf, int 
           acc[q][0] = __fmaf_rn(dg, d[0] + d[1], acc[q][0]);
           acc[q][1] = __fmaf_rn(dg8, d[2] + d[3], acc[q][1]);
         }
+      }
+    }
+  }
+}
+
+// Whole batches of U block pairs, for the warp-streaming form: no bounds
+// test (the row group's block pairs are a multiple of U).
+template <int U>
+struct BatchU {
+  uint4 c[U];
+  uint2 s[U];
+};
+
+template <int U>
+FZ_DEV void load_u(const uint4* codes, const uint2* scales, int bp, int lane, BatchU<U>& b) {
+  const int g = lane >> 2;
+#pragma unroll
+  for (int u = 0; u < U; u++) {
+    b.c[u] = ld_stream(codes + (size_t)(bp + u) * 32 + lane);
+    b.s[u] = ld_stream2(scales + (size_t)(bp + u) * 8 + g);
+  }
+}
+
+template <int U, int MQ>
+FZ_DEV void compute_u(const BatchU<U>& b, int bp, const uint2* xf, int lane, float acc[MQ][2]) {
+  const int g = lane >> 2, t = lane & 3;
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int u = 0; u < U; u++) {
+#pragma unroll
+    for (int kbi = 0; kbi < 2; kbi++) {
+      const int kb = 2 * (bp + u) + kbi;
+      uint32_t a0[4], a1[4];
+      dequant_word(kbi ? b.c[u].z : b.c[u].x, a0);
+      dequant_word(kbi ? b.c[u].w : b.c[u].y, a1);
+      const uint32_t sw = kbi ? b.s[u].y : b.s[u].x;
+      const float dg = __half2float(__ushort_as_half((unsigned short)(sw & 0xffffu)));
+      const float dg8 = __half2float(__ushort_as_half((unsigned short)(sw >> 16)));
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        const uint2 b0 = xf[xf_index(kb, 0, q, MQ, t, g)];
+        const uint2 b1 = xf[xf_index(kb, 1, q, MQ, t, g)];
+        float d[4];
+        mma16816(d, a0, b0, zero);
+        mma16816(d, a1, b1, d);
+        acc[q][0] = __fmaf_rn(dg, d[0] + d[1], acc[q][0]);
+        acc[q][1] = __fmaf_rn(dg8, d[2] + d[3], acc[q][1]);
       }
     }
   }
@@ -281,7 +329,72 @@ __global__ void __launch_bounds__(kThreads) matvec_kernel(const MatvecArgs a) {
   Batch first;
   float acc[MQ][2];
 
-  if (warp_mode) {
+  if (warp_mode && geo.NBP % kUW == 0) {
+    // Each warp streams its row groups rg, rg + total, ... as one sequence of
+    // kUW-block-pair batches: the next batch's loads (the next row group's
+    // first, at a row group's end) are in flight while one is computed.
+    const uint32_t nrg = a.mat[0].n / 16, NBP = geo.NBP, nb = NBP / kUW;
+    const uint32_t total = gridDim.x * kWarps;
+    const Q4Matrix& mat = a.mat[0];
+    auto codes_of = [&](uint32_t r) { return mat.codes + (size_t)r * NBP * 32; };
+    auto scales_of = [&](uint32_t r) { return mat.scales + (size_t)r * NBP * 8; };
+    uint32_t rg = blockIdx.x * kWarps + warp, j = 0;
+    BatchU<kUW> b0, b1;
+    if (rg < nrg) load_u<kUW>(codes_of(rg), scales_of(rg), 0, lane, b0);
+    pdl_wait();
+    prologue<MQ, PRO>(a, sm, geo);
+    unsigned long long best[MQ];
+#pragma unroll
+    for (int q = 0; q < MQ; q++) {
+      best[q] = 0ull;
+      acc[q][0] = acc[q][1] = 0.f;
+    }
+    auto finish = [&](uint32_t r) {
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        const int tok = 4 * q + t;
+        if (tok < M) {
+          const uint32_t n0 = r * 16 + g, n8 = n0 + 8;
+          a.out[(size_t)tok * a.out_stride + n0] = acc[q][0];
+          a.out[(size_t)tok * a.out_stride + n8] = acc[q][1];
+          if (EPI == kEpilogueHead) best[q] = max(best[q], max(head_key(acc[q][0], n0), head_key(acc[q][1], n8)));
+        }
+        acc[q][0] = acc[q][1] = 0.f;
+      }
+    };
+    auto next = [&](uint32_t& r, uint32_t& k) {
+      if (++k == nb) {
+        k = 0;
+        r += total;
+      }
+    };
+    while (rg < nrg) {
+      uint32_t rg1 = rg, j1 = j;
+      next(rg1, j1);
+      if (rg1 < nrg) load_u<kUW>(codes_of(rg1), scales_of(rg1), (int)(j1 * kUW), lane, b1);
+      compute_u<kUW, MQ>(b0, (int)(j * kUW), sm.xf, lane, acc);
+      if (j == nb - 1) finish(rg);
+      if (rg1 >= nrg) break;
+      uint32_t rg2 = rg1, j2 = j1;
+      next(rg2, j2);
+      if (rg2 < nrg) load_u<kUW>(codes_of(rg2), scales_of(rg2), (int)(j2 * kUW), lane, b0);
+      compute_u<kUW, MQ>(b1, (int)(j1 * kUW), sm.xf, lane, acc);
+      if (j1 == nb - 1) finish(rg1);
+      rg = rg2;
+      j = j2;
+    }
+    pdl_launch_dependents();
+    if (EPI == kEpilogueHead) {
+#pragma unroll
+      for (int q = 0; q < MQ; q++) {
+        unsigned long long b = best[q];
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+        const int tok = 4 * q + t;
+        if (g == 0 && tok < M && b) atomicMax(a.head.argmax + tok, b);
+      }
+    }
+  } else if (warp_mode) {
     // Each warp streams whole row groups on its own; no CTA barrier in the loop.
     const uint32_t nrg = a.mat[0].n / 16, NBP = geo.NBP;
     const uint32_t total = gridDim.x * kWarps;
