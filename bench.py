@@ -382,6 +382,58 @@ def run_ours(args):
         engine.check(lib.fz_batch_trace(batch.handle, 0))
         pos += 4
         decode_kernel_us = float(np.median(spans[1:]))
+    # The capture step and prefix reuse (rank 0): config 1's 32-token prompt as one step with and without
+    # the per-layer capture (weights, statistics and 25 readouts through the head), and a second turn
+    # that extends a 1024-token first turn's conversation by 16 tokens, prefilled fresh or after the cache
+    # keeps the 1039 tokens it already holds.
+    extras = None
+    if rank == 0:
+        def timed(fn, reps=5):
+            out = []
+            for _ in range(reps):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    e0.record()
+                fn()
+                with torch.cuda.stream(stream):
+                    e1.record()
+                torch.cuda.synchronize()
+                out.append(e0.elapsed_time(e1))
+            return float(np.median(out))
+        cb = engine.Batch(model, 1, 4096)
+
+        def pre(capture):
+            cb.step(0, ids, tokens=PROMPT, logits=True, capture=capture)
+            cb.wait()
+        pre(False)
+        pre(True)
+        plain_ms, capture_ms = timed(lambda: pre(False)), timed(lambda: pre(True))
+        sess = engine.Session(cb)
+        long_ids = np.random.default_rng([rank, 1024]).integers(2, synth.GEMMA3_1B.vocab, size=1024)
+        first = sess.run([long_ids], 16)
+        convo = list(long_ids) + first.tokens[0][:15] + list(
+            np.random.default_rng([rank, 16]).integers(2, synth.GEMMA3_1B.vocab, size=16))
+        held = len(convo) - 16
+        fresh = engine.Batch(model, 1, 4096)
+        full = np.asarray(convo, dtype=np.uint32)
+
+        def fresh_prefill():
+            fresh.step(0, full, tokens=len(full), logits=True)
+            fresh.wait()
+
+        def reuse_prefill():
+            assert cb.truncate(held) == held
+            cb.step(held, full[held:], tokens=len(full) - held, logits=True)
+            cb.wait()
+        fresh_ms, reuse_ms = timed(fresh_prefill), timed(reuse_prefill)
+        fresh.free()
+        cb.free()
+        extras = {"capture_step": {"workload": "config 1's 32-token prompt in one step", "plain_ms": plain_ms,
+                                   "with_capture_ms": capture_ms},
+                  "prefix_reuse": {"workload": "a second turn: the first turn's 1024-token prompt and 15 fed reply "
+                                               "tokens, then 16 new tokens",
+                                   "prompt_tokens": len(full), "reused_tokens": held, "fresh_prefill_ms": fresh_ms,
+                                   "reused_prefill_ms": reuse_ms}}
     long_line = None
     if not args.no_long:
         # 8 sequences, each a seeded prompt prefilled into the KV cache, then 256 greedy
@@ -495,6 +547,8 @@ def run_ours(args):
                     "bound": "hbm (latency-bound in practice: 130 dependent phases)",
                     "timing": "device global timer inside the kernel (fz_batch_trace), median of 3 steps"},
                 "clocks": clocks.summary()}
+        if extras:
+            line.update(extras)
         if sweep_line:
             line["steering_sweep"] = sweep_line
         if long_line:

@@ -24,7 +24,8 @@ from ._native import CaptureSlots, FzError, ModelInfo, Record, Step, check, load
 from .capture import SLOTS, Capture
 from .capture import layout as capture_layout
 
-MAX_ROWS = 16  # sequences x tokens one step takes
+MAX_ROWS = 16  # sequences x tokens the skinny (matvec) path takes in one step
+PREFILL_BLOCK = 512  # prompt tokens a step (residency::kPrefillBlock, src/core/residency/plan.h:175)
 
 
 class Device:
@@ -261,7 +262,7 @@ def generate(batch: Batch, prompts, steps: int, sampling: Sampling = Sampling(),
             batch.set_edits(s, E.table(es, layers, origin))
         else:
             batch.set_edits(s, None)
-    block = MAX_ROWS // S
+    block = max(1, PREFILL_BLOCK // S)
     turn = Turn(tokens=[[] for _ in range(S)])
     if not 0 <= start < n:
         raise ValueError("the prefill must start inside the prompt")
