@@ -49,7 +49,16 @@ namespace {
   } while (0)
 
 constexpr uint32_t kMaxEdits = 4096;  // edit::kMaxEdits
-constexpr uint32_t kSplitKeys = 512;  // keys an attention CTA takes
+constexpr uint32_t kSplitKeys = 512;  // most keys a per-op attention CTA takes (its score buffer)
+
+// Keys a per-op attention CTA takes for a layer reading up to `keys` keys:
+// 64-key splits while that gives at most 64 of them (a 512-key window is 8
+// CTAs a row and KV head, not one), longer splits, in 64s, beyond.
+uint32_t split_keys_for(uint32_t keys) {
+  const uint32_t per = (keys + 63) / 64;                     // splits of 64 keys
+  const uint32_t split = std::max<uint32_t>(64, (per + 63) / 64 * 64);
+  return std::min(split, kSplitKeys);
+}
 
 }  // namespace
 
@@ -760,8 +769,8 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       at.seq_tokens = T;
       at.m = M;
       at.scale_log2e = (float)((double)(1.0f / std::sqrt((float)s.head_dim)) * 1.4426950408889634);
-      at.split_keys = kSplitKeys;
-      at.splits = (std::min(L.window, b.context) + kSplitKeys - 1) / kSplitKeys;
+      at.split_keys = split_keys_for(std::min(L.window, b.context));
+      at.splits = (std::min(L.window, b.context) + at.split_keys - 1) / at.split_keys;
       at.partial_o = b.partial_o;
       at.partial_ml = b.partial_ml;
       at.counters = lc + 1;
@@ -838,8 +847,8 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     at.seq_tokens = T;
     at.m = M;
     at.scale_log2e = (float)((double)(1.0f / std::sqrt((float)s.head_dim)) * 1.4426950408889634);
-    at.split_keys = kSplitKeys;
-    at.splits = (std::min(L.window, b.context) + kSplitKeys - 1) / kSplitKeys;
+    at.split_keys = split_keys_for(std::min(L.window, b.context));
+    at.splits = (std::min(L.window, b.context) + at.split_keys - 1) / at.split_keys;
     at.partial_o = b.partial_o;
     at.partial_ml = b.partial_ml;
     at.counters = lc + 1;
@@ -1177,10 +1186,10 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     b->slots.push_back(slots);
     b->windows.push_back(L.window);
     b->seq_stride.push_back(per_seq);
-    // The per-op attention splits its keys kSplitKeys at a time; the decode
+    // The per-op attention splits its keys split_keys_for(keys) at a time; the decode
     // kernel into up to one split a CTA (kDecodeSplitKeys keys at least).
     const uint32_t keys = std::min(L.window, context);
-    b->splits_max = std::max<uint32_t>({b->splits_max, (keys + kSplitKeys - 1) / kSplitKeys,
+    b->splits_max = std::max<uint32_t>({b->splits_max, (keys + split_keys_for(keys) - 1) / split_keys_for(keys),
                                         std::min<uint32_t>((keys + fz::kDecodeSplitKeys - 1) / fz::kDecodeSplitKeys,
                                                            fz::kDecodeMaxSplits)});
   }

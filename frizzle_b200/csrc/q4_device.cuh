@@ -93,6 +93,44 @@ FZ_DEV void build_fragments(uint2* xf, int MQ, int row, const float* src, int kb
   }
 }
 
+// As build_fragments, for rows 0 .. 4 MQ - 1 of X at once (row r at src + r
+// ld; rows from M on are zeros): each item's loads for every row are in
+// flight together instead of one row's at a time.
+template <int MQ>
+FZ_DEV void build_fragments_rows(uint2* xf, int M, const float* src, int ld, int kb_base, int nkb, int first,
+                                 int step) {
+  for (int i = first; i < nkb * 8; i += step) {
+    const int kb_rel = i >> 3, h = (i >> 2) & 1, t = i & 3;
+    const int k0 = 32 * (kb_base + kb_rel) + 8 * h + 2 * t;
+    float2 v01[4 * MQ], v23[4 * MQ];
+#pragma unroll
+    for (int r = 0; r < 4 * MQ; r++) {
+      v01[r] = v23[r] = make_float2(0.f, 0.f);
+      if (r < M) {
+        v01[r] = *reinterpret_cast<const float2*>(src + (size_t)r * ld + k0);
+        v23[r] = *reinterpret_cast<const float2*>(src + (size_t)r * ld + k0 + 16);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 4 * MQ; r++) {
+      __half h0, h1, h2, h3, l0, l1, l2, l3;
+      split_hi_lo(v01[r].x, h0, l0);
+      split_hi_lo(v01[r].y, h1, l1);
+      split_hi_lo(v23[r].x, h2, l2);
+      split_hi_lo(v23[r].y, h3, l3);
+      xf[xf_index(kb_rel, h, r >> 2, MQ, t, 2 * (r & 3))] = pack4(h0, h1, h2, h3);
+      xf[xf_index(kb_rel, h, r >> 2, MQ, t, 2 * (r & 3) + 1)] = pack4(l0, l1, l2, l3);
+    }
+  }
+}
+
+// 16 bytes global -> shared by cp.async (L2 only), waited for by stage_wait.
+FZ_DEV void stage16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+FZ_DEV void stage_wait() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // QK-norm and RoPE of one head held by a warp (rope.wgsl:40-138, d = 256:
 // lane l holds elements 4l..4l+3 in a and 128+4l..128+4l+3 in b), given the
 // lane's gains ga, gb and its four theta/2pi turns.

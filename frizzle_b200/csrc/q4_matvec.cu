@@ -184,19 +184,37 @@ FZ_DEV float4 y_sum(const NormArgs& n, const float* yr, int v) {
 // The norm launch over the step's rows, by the whole CTA (norm.wgsl:97-198):
 // invocation i of the reference is thread i, holding vec4s i, i + 256, ...
 // Leaves the normed rows in `rowbuf` [rows][width]; CTA 0 writes X after the
-// add to hidden_out and the captures of each sequence's last row.
+// add to hidden_out and the captures of each sequence's last row.  With
+// `ystage` ([rows][width] of shared memory) and several rows, every row's X
+// and y are first staged by 16-byte cp.async with all the loads in flight,
+// so the passes read shared memory instead of waiting on one row at a time.
 FZ_DEV void norm_rows_cta(const MatvecArgs& a, const NormArgs& n, int rows, float* rowbuf, float* part, float* stat,
-                          bool writer) {
+                          bool writer, float* ystage = nullptr) {
   const int tid = threadIdx.x, W = (int)n.width, V = W / 4;
   const float wf = (float)W;
   float* ry = stat;
   float* rx = stat + kMaxTokens;
   auto hrow_of = [&](int r) { return r * (int)n.row_of_token_stride + (int)n.row_of_token_offset; };
+  const bool staged = ystage != nullptr && n.y_parts <= 1 && rows > 1;
+  if (staged) {
+    for (int i = tid; i < rows * V; i += kThreads) {
+      const int r = i / V, v = i % V;
+      const size_t off = (size_t)hrow_of(r) * W + 4 * v;
+      stage16(rowbuf + (size_t)r * W + 4 * v, n.hidden_in + off);
+      if (n.y) stage16(ystage + (size_t)r * W + 4 * v, n.y + off);
+    }
+    stage_wait();
+    __syncthreads();
+  }
+  // Row r's y at vec4 v: staged, or the sum of its K-slice partials.
+  auto y_at = [&](int r, const float* yr, int v) -> float4 {
+    return staged ? reinterpret_cast<const float4*>(ystage + (size_t)r * W)[v] : y_sum(n, yr, v);
+  };
   if (n.y && n.post_gain) {
     for (int r = 0; r < rows; r++) {
       const float* yr = n.y + (size_t)hrow_of(r) * W;
       float p = 0.f;
-      for (int v = tid; v < V; v += kThreads) p = add(p, dot_self(y_sum(n, yr, v)));
+      for (int v = tid; v < V; v += kThreads) p = add(p, dot_self(y_at(r, yr, v)));
       part[r * kThreads + tid] = p;
     }
     tree_reduce(part, rows, ry);
@@ -207,7 +225,8 @@ FZ_DEV void norm_rows_cta(const MatvecArgs& a, const NormArgs& n, int rows, floa
     const int hrow = hrow_of(r);
     const uint32_t seq = (uint32_t)hrow / a.seq_tokens;
     const bool last = (uint32_t)hrow % a.seq_tokens == a.seq_tokens - 1;
-    const float4* x4 = reinterpret_cast<const float4*>(n.hidden_in + (size_t)hrow * W);
+    float4* buf = reinterpret_cast<float4*>(rowbuf + (size_t)r * W);
+    const float4* x4 = staged ? buf : reinterpret_cast<const float4*>(n.hidden_in + (size_t)hrow * W);
     const float* yr = n.y ? n.y + (size_t)hrow * W : nullptr;
     const float4* pg4 = reinterpret_cast<const float4*>(n.post_gain);
     float4* out4 = writer && n.hidden_out ? reinterpret_cast<float4*>(n.hidden_out + (size_t)hrow * W) : nullptr;
@@ -215,12 +234,11 @@ FZ_DEV void norm_rows_cta(const MatvecArgs& a, const NormArgs& n, int rows, floa
                        ? reinterpret_cast<float4*>(n.capture_residual + seq * a.capture_stride) : nullptr;
     float4* ycap = writer && last && n.capture_added
                        ? reinterpret_cast<float4*>(n.capture_added + seq * a.capture_stride) : nullptr;
-    float4* buf = reinterpret_cast<float4*>(rowbuf + (size_t)r * W);
     float p = 0.f;
     for (int v = tid; v < V; v += kThreads) {
       float4 x = x4[v];
       if (yr) {
-        float4 y = y_sum(n, yr, v);
+        float4 y = y_at(r, yr, v);
         if (n.post_gain) {
           const float s = ry[r];
           const float4 g = pg4[v];
@@ -286,12 +304,13 @@ FZ_DEV void prologue(const MatvecArgs& a, const Smem& sm, const Geometry& geo) {
   const int M = (int)a.m, K = (int)a.mat[0].k;
   const float* rows = a.x;
   if (PRO == kPrologueNorm) {
-    norm_rows_cta(a, a.norm, M, sm.rowbuf, sm.part, sm.stat, blockIdx.x == 0);
+    // The fragments' region holds the staged y rows until the fragments are built.
+    const size_t xf_bytes = (size_t)geo.nkb_max * 2 * MQ * 32 * sizeof(uint2);
+    float* ystage = geo.C == 1 && (size_t)M * a.norm.width * 4 <= xf_bytes ? reinterpret_cast<float*>(sm.xf) : nullptr;
+    norm_rows_cta(a, a.norm, M, sm.rowbuf, sm.part, sm.stat, blockIdx.x == 0, ystage);
     rows = sm.rowbuf;
   }
-  for (int r = 0; r < 4 * MQ; r++)
-    build_fragments(sm.xf, MQ, r, r < M ? rows + (size_t)r * K : nullptr, geo.kb_base, geo.nkb, threadIdx.x,
-                    kThreads);
+  build_fragments_rows<MQ>(sm.xf, M, rows, K, geo.kb_base, geo.nkb, threadIdx.x, kThreads);
   __syncthreads();
 }
 
