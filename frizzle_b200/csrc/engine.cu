@@ -831,7 +831,14 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     a.rope.query_out = b.q;
     a.rope.capture_query = cap ? cap + cl.layer[l].query : nullptr;
     a.counter = lc;
-    if ((stt = run_matvec(a, fz::kPrologueNorm, fz::kEpilogueQkv, st, pdl))) return stt;
+    if (M <= 4) {
+      // The product's last CTA runs QK-norm, RoPE and the KV append.
+      if ((stt = run_matvec(a, fz::kPrologueNorm, fz::kEpilogueQkv, st, pdl))) return stt;
+    } else {
+      // More rows: a warp a (row, head) in a launch of its own, not M x 6 heads in one CTA.
+      if ((stt = run_matvec(a, fz::kPrologueNorm, fz::kEpilogueWrite, st, pdl))) return stt;
+      FZ_CUDA(fz::launch_rope_rows(a, st, pdl));
+    }
     // Attention.
     fz::AttentionArgs at{};
     at.step = b.dstep;
