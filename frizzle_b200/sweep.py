@@ -57,9 +57,12 @@ def sequences(pairs: list) -> list:
 
 
 def run(model, prompt, pairs: list, steps: int, layer: int, batch_seqs: int = 8, context: int = 1024,
-        top_k: int = 64, temperature: float = 1.0) -> dict:
+        top_k: int = 64, temperature: float = 1.0, batches: dict = None) -> dict:
     """Generates `steps` tokens for every sequence of `pairs` on this rank's GPU.
 
+    `batches` ({group size: engine.Batch}) keeps the batches, with their
+    captured step graphs, for the caller to reuse and free; by default they
+    are made here and freed at the end.
     Returns {pair index: int32 [2][steps]} (row 0 steered, row 1 unsteered)."""
     from . import engine
     seqs = sequences(pairs)
@@ -68,7 +71,9 @@ def run(model, prompt, pairs: list, steps: int, layer: int, batch_seqs: int = 8,
     sampling = engine.Sampling(temperature=temperature, top_k=top_k, top_p=1.0, min_p=0.0)
     # One batch serves every group of the same size (a new group's prefill rewrites its caches from
     # position 0, and the step graphs captured for the first group are reused).
-    batches = {}
+    own = batches is None
+    if own:
+        batches = {}
     try:
         for b0 in range(0, len(seqs), batch_seqs):
             group = seqs[b0:b0 + batch_seqs]
@@ -90,8 +95,9 @@ def run(model, prompt, pairs: list, steps: int, layer: int, batch_seqs: int = 8,
                 if i + 1 < steps:
                     batch.step(n + i, fed=True, tokens=1, logits=True, sampling=sampling, seeds=seeds)
     finally:
-        for b in batches.values():
-            b.free()
+        if own:
+            for b in batches.values():
+                b.free()
     return out
 
 
