@@ -199,6 +199,53 @@ def head_roofline(torch, lib, native, reps=20):
     return bytes_, secs
 
 
+def formats_roofline(torch, lib, native, reps=20):
+    """The pinned file's other block formats at the head's shape (262144 x 1152,
+    M = 1): Q8_0 (its tied embedding/head) and Q4_1, each timed alone with CUDA
+    events on its stream, two weight copies alternating so L2 holds neither.
+    Algorithmic bytes: codes + scales + x + y."""
+    from frizzle_b200 import synth
+    n, k = HEAD_N, HEAD_K
+    s = torch.cuda.current_stream().cuda_stream
+    x = torch.randn(1, k, device="cuda")
+    y = torch.empty(1, n, device="cuda")
+    out = {}
+    for name, gen, cb, sb, repack, matvec in (
+            ("q8_0", synth.random_q8_0, lib.fz_q8_0_codes_bytes, lib.fz_q8_0_scales_bytes, lib.fz_q8_0_repack,
+             lib.fz_q8_0_matvec),
+            ("q4_1", synth.random_q4_1, lib.fz_q4_1_codes_bytes, lib.fz_q4_1_scales_bytes, lib.fz_q4_1_repack,
+             lib.fz_q4_1_matvec)):
+        mats = []
+        for c in range(2):
+            src = torch.from_numpy(gen(n, k, seed=c)).cuda()
+            codes = torch.empty(cb(n, k), dtype=torch.uint8, device="cuda")
+            scales = torch.empty(sb(n, k), dtype=torch.uint8, device="cuda")
+            native.check(repack(src.data_ptr(), n, k, codes.data_ptr(), scales.data_ptr(), s))
+            torch.cuda.synchronize()
+            del src
+            mats.append((codes, scales))
+        for i in range(4):
+            c, sc = mats[i % 2]
+            native.check(matvec(c.data_ptr(), sc.data_ptr(), n, k, x.data_ptr(), 1, y.data_ptr(), s))
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for i in range(reps):
+            c, sc = mats[i % 2]
+            native.check(matvec(c.data_ptr(), sc.data_ptr(), n, k, x.data_ptr(), 1, y.data_ptr(), s))
+        end.record()
+        torch.cuda.synchronize()
+        secs = start.elapsed_time(end) / 1000.0 / reps
+        bytes_ = cb(n, k) + sb(n, k) + 4 * k + 4 * n
+        hbm, _, which = peaks()
+        out[name] = {"kernel": f"{name} matvec 262144 x 1152, M=1", "us": secs * 1e6, "algorithmic_bytes": bytes_,
+                     "achieved_gbs": bytes_ / secs / 1e9, "frac": bytes_ / secs / 1e9 / hbm, "peak": hbm,
+                     "peak_source": which}
+        del mats
+        torch.cuda.empty_cache()
+    return out
+
+
 def gemm_roofline(torch, lib, native, m=4096, reps=10):
     """The prefill's dominant product (gate and up, 1152 -> 2 x 6912, GELU and
     the f16 hand-off) on the tensor cores at m rows, timed alone."""
@@ -577,6 +624,7 @@ def run_ours(args):
         pre.wait()
         p4k = e0.elapsed_time(e1) / 1000.0
         pre.free()
+        line["formats_matvec"] = formats_roofline(torch, lib, _native)
         gflops, gsecs = gemm_roofline(torch, lib, _native)
         _, bf16, _ = peaks()
         line["prefill_4096"] = {"tokens_per_s": 4096 / p4k, "ms": 1000.0 * p4k,
@@ -622,6 +670,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemm-only", action="store_true",
                     help="time only the tensor-core gated product at M = 4096 and print its numbers")
+    ap.add_argument("--formats-only", action="store_true",
+                    help="time only the Q8_0 and Q4_1 matvecs at the head's shape and print their numbers")
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-4 steering sweep")
@@ -647,6 +697,11 @@ def main():
                           "tflops": {p: flops / t / 1e12 for p, t in secs.items()},
                           "frac": {p: flops / t / 1e12 / bf16 for p, t in secs.items()},
                           "us": {p: t * 1e6 for p, t in secs.items()}}))
+        return 0
+    if args.formats_only:
+        import torch
+        from frizzle_b200 import _native
+        print(json.dumps(formats_roofline(torch, _native.load(), _native, reps=args.steps)))
         return 0
     if args.trace:
         return run_trace(args)

@@ -94,6 +94,16 @@ SIGNATURES = {
     "fz_q4_0_matvec": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP]),
     "fz_q4_0_gated": (C.c_int, [VP, VP, VP, VP, U32, U32, VP, U32, VP, U32, U32, VP, VP]),
     "fz_q4_0_head": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP, VP]),
+    "fz_q8_0_codes_bytes": (C.c_size_t, [U32, U32]),
+    "fz_q8_0_scales_bytes": (C.c_size_t, [U32, U32]),
+    "fz_q4_1_codes_bytes": (C.c_size_t, [U32, U32]),
+    "fz_q4_1_scales_bytes": (C.c_size_t, [U32, U32]),
+    "fz_q8_0_repack": (C.c_int, [VP, U32, U32, VP, VP, VP]),
+    "fz_q4_1_repack": (C.c_int, [VP, U32, U32, VP, VP, VP]),
+    "fz_q8_0_rows": (C.c_int, [VP, VP, U32, U32, VP, U32, C.c_float, VP, VP]),
+    "fz_q4_1_rows": (C.c_int, [VP, VP, U32, U32, VP, U32, C.c_float, VP, VP]),
+    "fz_q8_0_matvec": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP]),
+    "fz_q4_1_matvec": (C.c_int, [VP, VP, U32, U32, VP, U32, VP, VP]),
     "fz_q4_0_gemm": (C.c_int, [VP, VP, U32, U32, VP, VP, U32, U32, VP, VP, VP]),
     "fz_q4_0_to_f16": (C.c_int, [VP, VP, U32, U32, VP, VP, VP]),
     "fz_f16_gemm": (C.c_int, [VP, VP, U32, U32, VP, VP, U32, U32, VP, VP, VP]),

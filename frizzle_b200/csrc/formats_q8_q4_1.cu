@@ -1,0 +1,422 @@
+// Q8_0 and Q4_1: the two block formats of Gemma 3 1B's pinned file besides
+// Q4_0 (the Q8_0 token embedding the head is tied to, Q4_1 ffn_down in
+// layers 0-2), as kernel-level entry points: repack from GGUF blocks, row
+// gather, and the HBM-streaming product y[m][n] = sum_k W[n][k] x[m][k] for up
+// to eight rows of x.
+//
+// Device layout: the reference's piece layout with the whole matrix as one
+// piece (src/core/formats/device_layout.h:115-121).  First every block's code
+// bytes, row-major (row r, block g at (r*K/32 + g) * code_bytes: 32 for Q8_0,
+// 16 for Q4_1), then every block's scale word (Q8_0: d, 2 bytes; Q4_1: d and
+// m, 4 bytes, d in the low half).  The codes keep the file's bits; a row's
+// codes are contiguous, so a warp streams a row with 128-bit loads.
+//
+// The product: each warp takes four rows of W at a time; every lane loads up
+// to three 16-byte code chunks of each row before any arithmetic (twelve
+// loads in flight a lane), decodes bytes to f32 exactly through the 2^23
+// exponent trick (one byte permute and one subtract a code), multiplies by x
+// staged in shared memory (a swizzle makes the lanes' float4 reads conflict
+// free), and applies the block scale once per chunk.  Q4_1's minimum enters as
+// m * (sum of x over the block), precomputed per block when x is staged.  The
+// lanes' sums meet in a reduce-scatter over the warp (4*M values, one per lane
+// group).  Sums are f32 in another order than the reference's 32 ranges
+// (matmul.wgsl:154-185), so results agree with it within rounding, not bit
+// for bit; the gather is bit-exact.
+#include <algorithm>
+#include <string>
+
+#include "frizzle_b200.h"
+#include "fz_common.cuh"
+#include "last_error.h"
+
+namespace {
+
+enum Format : int { kQ8_0 = 0, kQ4_1 = 1 };
+
+template <int F>
+struct Fmt;
+template <>
+struct Fmt<kQ8_0> {
+  static constexpr uint32_t file_bytes = 34, code_bytes = 32, scale_bytes = 2, code_offset = 2;
+  static constexpr uint32_t chunk_cols = 16;  // columns a 16-byte code chunk covers
+};
+template <>
+struct Fmt<kQ4_1> {
+  static constexpr uint32_t file_bytes = 20, code_bytes = 16, scale_bytes = 4, code_offset = 4;
+  static constexpr uint32_t chunk_cols = 32;
+};
+
+constexpr int kWarps = 8;       // warps a CTA
+constexpr int kRows = 4;        // rows of W a warp takes at a time
+constexpr int kBatch = 3;       // code chunks a lane loads from each row per pass
+constexpr int kMaxRows = 8;     // rows of x
+constexpr size_t kMaxShared = 200 * 1024;
+
+FZ_DEV uint4 load_stream(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Byte `i` of `word` as the f32 2^23 + byte: the byte becomes the low
+// mantissa bits under the exponent of 2^23 (exact; subtracting 2^23 gives it).
+template <int I>
+FZ_DEV float byte_as_f32_biased(uint32_t word) {
+  return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7440u | I));
+}
+
+// The float4 unit q of chunk c, stored at c*CW + (q ^ swizzle(c)) so that
+// eight lanes reading the same q of eight consecutive chunks hit eight
+// different 16-byte bank groups.
+template <int CW>
+FZ_DEV uint32_t swizzle(uint32_t c) {
+  return CW == 4 ? (c >> 1) & 3u : c & 7u;
+}
+
+template <int NV>
+struct Log2 {
+  static constexpr int value = NV <= 1 ? 0 : 1 + Log2<(NV > 1 ? NV / 2 : 1)>::value;
+};
+template <>
+struct Log2<1> {
+  static constexpr int value = 0;
+};
+
+// After the call, lane L holds the warp total of v[L >> (5 - log2 NV)]; NV - 1
+// shuffles for the halving steps, then plain butterflies.
+template <int NV>
+FZ_DEV float reduce_scatter(float (&v)[NV], uint32_t lane) {
+  constexpr int LOG = Log2<NV>::value;
+#pragma unroll
+  for (int s = 0; s < LOG; s++) {
+    const int half = NV >> (s + 1);
+    const int off = 16 >> s;
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < half; j++) {
+      const float send = upper ? v[j] : v[j + half];
+      const float keep = upper ? v[j + half] : v[j];
+      v[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+#pragma unroll
+  for (int off = 16 >> LOG; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+  return v[0];
+}
+
+template <int F>
+__global__ void repack_blocks_kernel(const uint8_t* file, size_t blocks, uint8_t* codes, uint8_t* scales) {
+  for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks; b += (size_t)gridDim.x * blockDim.x) {
+    const uint8_t* src = file + b * Fmt<F>::file_bytes;
+    if (F == kQ8_0) {
+      // 34-byte blocks: the codes start 2-byte aligned.
+      const uint16_t* s16 = reinterpret_cast<const uint16_t*>(src);
+      uint32_t w[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) w[i] = (uint32_t)s16[1 + 2 * i] | ((uint32_t)s16[2 + 2 * i] << 16);
+      uint4* dst = reinterpret_cast<uint4*>(codes + b * 32);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      reinterpret_cast<uint16_t*>(scales)[b] = s16[0];
+    } else {
+      const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src);
+      reinterpret_cast<uint4*>(codes)[b] = make_uint4(s32[1], s32[2], s32[3], s32[4]);
+      reinterpret_cast<uint32_t*>(scales)[b] = s32[0];
+    }
+  }
+}
+
+// out[i][j] = unpack(row rows[i])[j] * scale, in f32 as the gather forms it
+// (gather.wgsl:25-48 over q8_0.wgsl / q4_1.wgsl's unpack).
+template <int F>
+__global__ void rows_kernel(const uint8_t* codes, const uint8_t* scales, uint32_t n, uint32_t k, const uint32_t* rows,
+                            uint32_t count, float scale, float* out) {
+  const uint32_t i = blockIdx.x;
+  if (i >= count) return;
+  const uint32_t r = rows[i];
+  if (r >= n) return;
+  const size_t kb = k / 32;
+  for (uint32_t j = threadIdx.x; j < k; j += blockDim.x) {
+    const size_t g = (size_t)r * kb + j / 32;
+    float w;
+    if (F == kQ8_0) {
+      const int8_t q = static_cast<int8_t>(codes[(size_t)r * k + j]);
+      const float d = fz::f16_unpack(reinterpret_cast<const uint16_t*>(scales)[g]);
+      w = fz::mul((float)q, d);
+    } else {
+      const uint8_t byte = codes[g * 16 + (j % 16)];
+      const uint32_t q = (j % 32) < 16 ? byte & 0xFu : byte >> 4;
+      const uint32_t dm = reinterpret_cast<const uint32_t*>(scales)[g];
+      w = fz::add(fz::mul((float)q, fz::f16_unpack((uint16_t)(dm & 0xffffu))), fz::f16_unpack((uint16_t)(dm >> 16)));
+    }
+    out[(size_t)i * k + j] = fz::mul(w, scale);
+  }
+}
+
+template <int F, int MT>
+__global__ void __launch_bounds__(kWarps * 32) matvec_kernel(const uint8_t* __restrict__ codes,
+                                                             const uint8_t* __restrict__ scales, uint32_t n,
+                                                             uint32_t k, const float* __restrict__ x,
+                                                             float* __restrict__ y) {
+  constexpr uint32_t CW = Fmt<F>::chunk_cols / 4;  // float4 units a chunk
+  constexpr int MTP = MT == 1 ? 1 : MT == 2 ? 2 : MT <= 4 ? 4 : 8;
+  constexpr int NV = kRows * MTP;
+  extern __shared__ float4 smem[];
+  const uint32_t units = k / 4, chunks = k / Fmt<F>::chunk_cols, kb = k / 32;
+  float4* xs = smem;                                   // [MT][units], swizzled within chunks
+  float* bsum = reinterpret_cast<float*>(smem + MT * units);  // Q4_1: [MT][kb]
+
+  for (uint32_t i = threadIdx.x; i < MT * units; i += blockDim.x) {
+    const uint32_t mr = i / units, u = i % units, c = u / CW, q = u % CW;
+    xs[mr * units + c * CW + (q ^ swizzle<CW>(c))] = reinterpret_cast<const float4*>(x)[i];
+  }
+  if (F == kQ4_1) {
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < MT * kb; i += blockDim.x) {
+      const uint32_t mr = i / kb, c = i % kb;
+      float s = 0.0f;
+#pragma unroll
+      for (uint32_t q = 0; q < CW; q++) {
+        const float4 v = xs[mr * units + c * CW + q];
+        s += (v.x + v.y) + (v.z + v.w);
+      }
+      bsum[i] = s;
+    }
+  }
+  __syncthreads();
+
+  const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t quads = (n + kRows - 1) / kRows;
+  const size_t row_bytes = (size_t)kb * Fmt<F>::code_bytes;
+  for (uint32_t task = blockIdx.x * kWarps + warp; task < quads; task += gridDim.x * kWarps) {
+    const uint32_t r0 = task * kRows;
+    float acc[kRows][MT];
+#pragma unroll
+    for (int r = 0; r < kRows; r++)
+#pragma unroll
+      for (int m = 0; m < MT; m++) acc[r][m] = 0.0f;
+
+    for (uint32_t base = 0; base < chunks; base += 32 * kBatch) {
+      uint4 w[kRows][kBatch];
+      uint32_t sw[kRows][kBatch];
+#pragma unroll
+      for (int r = 0; r < kRows; r++)
+#pragma unroll
+        for (int b = 0; b < kBatch; b++) {
+          const uint32_t c = base + 32 * b + lane;
+          const uint32_t row = r0 + r;
+          if (c < chunks && row < n) {
+            w[r][b] = load_stream(codes + row * row_bytes + (size_t)c * 16);
+            if (F == kQ8_0)
+              sw[r][b] = __ldg(reinterpret_cast<const uint16_t*>(scales) + (size_t)row * kb + c / 2);
+            else
+              sw[r][b] = __ldg(reinterpret_cast<const uint32_t*>(scales) + (size_t)row * kb + c);
+          } else {
+            w[r][b] = make_uint4(0, 0, 0, 0);
+            sw[r][b] = 0;
+          }
+        }
+#pragma unroll
+      for (int b = 0; b < kBatch; b++) {
+        const uint32_t c = base + 32 * b + lane;
+        if (c >= chunks) continue;
+        const uint32_t sz = swizzle<CW>(c);
+#pragma unroll
+        for (int r = 0; r < kRows; r++) {
+          if (r0 + r >= n) continue;
+          float part[MT];
+#pragma unroll
+          for (int m = 0; m < MT; m++) part[m] = 0.0f;
+          const uint32_t words[4] = {w[r][b].x, w[r][b].y, w[r][b].z, w[r][b].w};
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            if (F == kQ8_0) {
+              // Signed codes biased by 128: 2^23 + 128 + code, exact.
+              const uint32_t t = words[q] ^ 0x80808080u;
+              const float f0 = byte_as_f32_biased<0>(t) - 8388736.0f, f1 = byte_as_f32_biased<1>(t) - 8388736.0f;
+              const float f2 = byte_as_f32_biased<2>(t) - 8388736.0f, f3 = byte_as_f32_biased<3>(t) - 8388736.0f;
+#pragma unroll
+              for (int m = 0; m < MT; m++) {
+                const float4 xv = xs[m * units + c * CW + (q ^ sz)];
+                part[m] = fmaf(f0, xv.x, part[m]);
+                part[m] = fmaf(f1, xv.y, part[m]);
+                part[m] = fmaf(f2, xv.z, part[m]);
+                part[m] = fmaf(f3, xv.w, part[m]);
+              }
+            } else {
+              // Byte j's low nibble is column j, its high nibble column j + 16.
+              const uint32_t lo = words[q] & 0x0F0F0F0Fu, hi = (words[q] >> 4) & 0x0F0F0F0Fu;
+              const float l0 = byte_as_f32_biased<0>(lo) - 8388608.0f, l1 = byte_as_f32_biased<1>(lo) - 8388608.0f;
+              const float l2 = byte_as_f32_biased<2>(lo) - 8388608.0f, l3 = byte_as_f32_biased<3>(lo) - 8388608.0f;
+              const float h0 = byte_as_f32_biased<0>(hi) - 8388608.0f, h1 = byte_as_f32_biased<1>(hi) - 8388608.0f;
+              const float h2 = byte_as_f32_biased<2>(hi) - 8388608.0f, h3 = byte_as_f32_biased<3>(hi) - 8388608.0f;
+#pragma unroll
+              for (int m = 0; m < MT; m++) {
+                const float4 xl = xs[m * units + c * CW + (q ^ sz)];
+                const float4 xh = xs[m * units + c * CW + ((4 + q) ^ sz)];
+                part[m] = fmaf(l0, xl.x, part[m]);
+                part[m] = fmaf(l1, xl.y, part[m]);
+                part[m] = fmaf(l2, xl.z, part[m]);
+                part[m] = fmaf(l3, xl.w, part[m]);
+                part[m] = fmaf(h0, xh.x, part[m]);
+                part[m] = fmaf(h1, xh.y, part[m]);
+                part[m] = fmaf(h2, xh.z, part[m]);
+                part[m] = fmaf(h3, xh.w, part[m]);
+              }
+            }
+          }
+          if (F == kQ8_0) {
+            const float d = fz::f16_unpack((uint16_t)sw[r][b]);
+#pragma unroll
+            for (int m = 0; m < MT; m++) acc[r][m] = fmaf(d, part[m], acc[r][m]);
+          } else {
+            const float d = fz::f16_unpack((uint16_t)(sw[r][b] & 0xffffu));
+            const float mn = fz::f16_unpack((uint16_t)(sw[r][b] >> 16));
+#pragma unroll
+            for (int m = 0; m < MT; m++)
+              acc[r][m] = fmaf(mn, bsum[m * kb + c], fmaf(d, part[m], acc[r][m]));
+          }
+        }
+      }
+    }
+
+    float v[NV];
+#pragma unroll
+    for (int r = 0; r < kRows; r++)
+#pragma unroll
+      for (int m = 0; m < MTP; m++) v[r * MTP + m] = m < MT ? acc[r][m < MT ? m : 0] : 0.0f;
+    const float total = reduce_scatter<NV>(v, lane);
+    constexpr int SHIFT = 5 - Log2<NV>::value;
+    if ((lane & ((1u << SHIFT) - 1)) == 0) {
+      const uint32_t idx = lane >> SHIFT, r = idx / MTP, m = idx % MTP;
+      if (m < MT && r0 + r < n) y[(size_t)m * n + r0 + r] = total;
+    }
+  }
+}
+
+fz_status refuse(fz_status s, const std::string& why) {
+  fz::set_last_error(why.c_str());
+  return s;
+}
+
+fz_status cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return FZ_OK;
+  return refuse(e == cudaErrorIllegalAddress || e == cudaErrorLaunchFailure ? FZ_ERR_DEVICE_LOST : FZ_ERR_CUDA,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+fz_status check_matrix(uint32_t n, uint32_t k) {
+  if (n == 0 || k == 0 || k % 32) return refuse(FZ_ERR_ARGUMENT, "n must be at least 1 and k a multiple of 32");
+  return FZ_OK;
+}
+
+template <int F>
+fz_status repack(const void* file_blocks, uint32_t n, uint32_t k, void* codes, void* scales, void* stream) {
+  fz_status st;
+  if ((st = check_matrix(n, k))) return st;
+  if (!file_blocks || !codes || !scales) return refuse(FZ_ERR_ARGUMENT, "null pointer");
+  if (!aligned(file_blocks, F == kQ8_0 ? 2 : 4) || !aligned(codes, 16) || !aligned(scales, Fmt<F>::scale_bytes))
+    return refuse(FZ_ERR_ARGUMENT, "misaligned pointer (file blocks 2 or 4 bytes, codes 16, scales 2 or 4)");
+  const size_t blocks = (size_t)n * (k / 32);
+  const int grid = (int)std::min<size_t>((blocks + 255) / 256, 148 * 16);
+  (void)cudaGetLastError();
+  repack_blocks_kernel<F><<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(file_blocks), blocks, static_cast<uint8_t*>(codes), static_cast<uint8_t*>(scales));
+  return cuda_status(cudaGetLastError(), "repack");
+}
+
+template <int F>
+fz_status rows(const void* codes, const void* scales, uint32_t n, uint32_t k, const uint32_t* row_ids, uint32_t count,
+               float scale, float* out, void* stream) {
+  fz_status st;
+  if ((st = check_matrix(n, k))) return st;
+  if (!codes || !scales || !row_ids || !out) return refuse(FZ_ERR_ARGUMENT, "null pointer");
+  if (!aligned(scales, Fmt<F>::scale_bytes)) return refuse(FZ_ERR_ARGUMENT, "misaligned scales");
+  if (count == 0) return FZ_OK;
+  (void)cudaGetLastError();
+  rows_kernel<F><<<count, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(codes), static_cast<const uint8_t*>(scales), n, k, row_ids, count, scale, out);
+  return cuda_status(cudaGetLastError(), "rows");
+}
+
+template <int F, int MT>
+fz_status launch_mt(const uint8_t* codes, const uint8_t* scales, uint32_t n, uint32_t k, const float* x, float* y,
+                    size_t smem, cudaStream_t stream) {
+  auto kernel = matvec_kernel<F, MT>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return cuda_status(e, "matvec attribute");
+  int dev = 0, sms = 0, per_sm = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess || (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+      (e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kWarps * 32, smem)) != cudaSuccess)
+    return cuda_status(e, "matvec occupancy");
+  const size_t quads = ((size_t)n + kRows - 1) / kRows;
+  const size_t want = (quads + kWarps - 1) / kWarps;
+  const int grid = (int)std::max<size_t>(1, std::min<size_t>(want, (size_t)sms * std::max(per_sm, 1)));
+  (void)cudaGetLastError();
+  kernel<<<grid, kWarps * 32, smem, stream>>>(codes, scales, n, k, x, y);
+  return cuda_status(cudaGetLastError(), "matvec");
+}
+
+template <int F>
+fz_status matvec(const void* codes, const void* scales, uint32_t n, uint32_t k, const float* x, uint32_t m, float* y,
+                 void* stream) {
+  fz_status st;
+  if ((st = check_matrix(n, k))) return st;
+  if (!codes || !scales || !x || !y) return refuse(FZ_ERR_ARGUMENT, "null pointer");
+  if (m < 1 || m > (uint32_t)kMaxRows) return refuse(FZ_ERR_ARGUMENT, "m outside 1 .. 8");
+  if (!aligned(codes, 16) || !aligned(x, 16) || !aligned(scales, Fmt<F>::scale_bytes))
+    return refuse(FZ_ERR_ARGUMENT, "misaligned pointer (codes and x 16 bytes, scales 2 or 4)");
+  const size_t smem = (size_t)m * k * 4 + (F == kQ4_1 ? (size_t)m * (k / 32) * 4 : 0);
+  if (smem > kMaxShared) return refuse(FZ_ERR_ARGUMENT, "m x k too large: x is staged in 200 KiB of shared memory");
+  const auto* c = static_cast<const uint8_t*>(codes);
+  const auto* s = static_cast<const uint8_t*>(scales);
+  cudaStream_t st_ = static_cast<cudaStream_t>(stream);
+  switch (m) {
+    case 1: return launch_mt<F, 1>(c, s, n, k, x, y, smem, st_);
+    case 2: return launch_mt<F, 2>(c, s, n, k, x, y, smem, st_);
+    case 3: return launch_mt<F, 3>(c, s, n, k, x, y, smem, st_);
+    case 4: return launch_mt<F, 4>(c, s, n, k, x, y, smem, st_);
+    case 5: return launch_mt<F, 5>(c, s, n, k, x, y, smem, st_);
+    case 6: return launch_mt<F, 6>(c, s, n, k, x, y, smem, st_);
+    case 7: return launch_mt<F, 7>(c, s, n, k, x, y, smem, st_);
+    default: return launch_mt<F, 8>(c, s, n, k, x, y, smem, st_);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fz_q8_0_codes_bytes(uint32_t n, uint32_t k) { return (size_t)n * k; }
+size_t fz_q8_0_scales_bytes(uint32_t n, uint32_t k) { return (size_t)n * (k / 32) * 2; }
+size_t fz_q4_1_codes_bytes(uint32_t n, uint32_t k) { return (size_t)n * k / 2; }
+size_t fz_q4_1_scales_bytes(uint32_t n, uint32_t k) { return (size_t)n * (k / 32) * 4; }
+
+fz_status fz_q8_0_repack(const void* file_blocks, uint32_t n, uint32_t k, void* codes, void* scales, void* stream) {
+  return repack<kQ8_0>(file_blocks, n, k, codes, scales, stream);
+}
+fz_status fz_q4_1_repack(const void* file_blocks, uint32_t n, uint32_t k, void* codes, void* scales, void* stream) {
+  return repack<kQ4_1>(file_blocks, n, k, codes, scales, stream);
+}
+fz_status fz_q8_0_rows(const void* codes, const void* scales, uint32_t n, uint32_t k, const uint32_t* row_ids,
+                       uint32_t count, float scale, float* out, void* stream) {
+  return rows<kQ8_0>(codes, scales, n, k, row_ids, count, scale, out, stream);
+}
+fz_status fz_q4_1_rows(const void* codes, const void* scales, uint32_t n, uint32_t k, const uint32_t* row_ids,
+                       uint32_t count, float scale, float* out, void* stream) {
+  return rows<kQ4_1>(codes, scales, n, k, row_ids, count, scale, out, stream);
+}
+fz_status fz_q8_0_matvec(const void* codes, const void* scales, uint32_t n, uint32_t k, const float* x, uint32_t m,
+                         float* y, void* stream) {
+  return matvec<kQ8_0>(codes, scales, n, k, x, m, y, stream);
+}
+fz_status fz_q4_1_matvec(const void* codes, const void* scales, uint32_t n, uint32_t k, const float* x, uint32_t m,
+                         float* y, void* stream) {
+  return matvec<kQ4_1>(codes, scales, n, k, x, m, y, stream);
+}
+
+}  // extern "C"

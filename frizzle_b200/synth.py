@@ -114,6 +114,34 @@ def random_q4_0(rows: int, k: int, seed: int, scale_sigma: float = 0.005) -> np.
     return out.reshape(-1)
 
 
+def random_q8_0(rows: int, k: int, seed: int, scale_sigma: float = 0.0005) -> np.ndarray:
+    """Q8_0 blocks (fp16 d, 32 signed codes) with codes uniform in [-128, 127]
+    and fp16 scales |N(0, sigma)|: weights of Q4_0's magnitude at 16x the
+    resolution."""
+    rng = np.random.default_rng([seed, rows, k, 8])
+    n = rows * k // 32
+    out = np.empty((n, 34), dtype=np.uint8)
+    d = np.abs(rng.standard_normal(n, dtype=np.float32) * np.float32(scale_sigma))
+    out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = rng.integers(0, 256, size=(n, 32), dtype=np.uint8)
+    return out.reshape(-1)
+
+
+def random_q4_1(rows: int, k: int, seed: int, scale_sigma: float = 0.005) -> np.ndarray:
+    """Q4_1 blocks (fp16 d, fp16 m, 16 code bytes) with codes uniform in
+    [0, 15], d = |N(0, sigma)| and m = -8 d + N(0, sigma): a block's minimum
+    near its centred range, as a quantiser sets it."""
+    rng = np.random.default_rng([seed, rows, k, 3])
+    n = rows * k // 32
+    out = np.empty((n, 20), dtype=np.uint8)
+    d = np.abs(rng.standard_normal(n, dtype=np.float32) * np.float32(scale_sigma))
+    m = -8.0 * d + rng.standard_normal(n, dtype=np.float32) * np.float32(scale_sigma)
+    out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:4] = m.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 4:] = rng.integers(0, 256, size=(n, 16), dtype=np.uint8)
+    return out.reshape(-1)
+
+
 def tensor_plan(shape: ModelShape):
     """(name, dims innermost first, ggml type, kind) in file order."""
     H, F, Q, KV, D = shape.hidden, shape.ffn, shape.q_width, shape.kv_width, shape.head_dim

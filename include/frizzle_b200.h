@@ -255,6 +255,41 @@ fz_status fz_q4_0_gated(const void *gate_codes, const void *gate_scales, const v
 fz_status fz_q4_0_head(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
                        uint32_t m, float *logits, unsigned long long *argmax, void *stream);
 
+/* Q8_0 (the pinned file's token embedding and tied head) and Q4_1 (its
+ * ffn_down in layers 0-2): src/core/formats/q8_0/q8_0.h, q4_1/q4_1.h.  The
+ * device layout is the reference's piece layout over the whole matrix
+ * (src/core/formats/device_layout.h:115-121): every block's code bytes, row
+ * after row (32 a block for Q8_0, 16 for Q4_1), then every block's scale word
+ * (Q8_0: d; Q4_1: d then m).  n >= 1, k a multiple of 32; codes and x 16-byte
+ * aligned. */
+size_t fz_q8_0_codes_bytes(uint32_t n, uint32_t k);
+size_t fz_q8_0_scales_bytes(uint32_t n, uint32_t k);
+size_t fz_q4_1_codes_bytes(uint32_t n, uint32_t k);
+size_t fz_q4_1_scales_bytes(uint32_t n, uint32_t k);
+
+/* GGUF blocks (34 or 20 bytes, row-major; 2- or 4-byte aligned) into the
+ * layout (PieceWriter's transpose, src/core/residency/piece_writer.h:165-245). */
+fz_status fz_q8_0_repack(const void *file_blocks, uint32_t n, uint32_t k, void *codes, void *scales,
+                         void *stream);
+fz_status fz_q4_1_repack(const void *file_blocks, uint32_t n, uint32_t k, void *codes, void *scales,
+                         void *stream);
+
+/* Rows back to f32 times `scale`, bit-exact (the gather,
+ * src/core/kernels/gather/gather.wgsl:25-48, over q8_0.wgsl:11-23 and
+ * q4_1.wgsl:12-26). */
+fz_status fz_q8_0_rows(const void *codes, const void *scales, uint32_t n, uint32_t k, const uint32_t *rows,
+                       uint32_t count, float scale, float *out, void *stream);
+fz_status fz_q4_1_rows(const void *codes, const void *scales, uint32_t n, uint32_t k, const uint32_t *rows,
+                       uint32_t count, float scale, float *out, void *stream);
+
+/* y[m][n] = sum_k W[n][k] x[m][k], 1 <= m <= 8, m*k*4 bytes of x (plus m*k/8
+ * for Q4_1) at most 200 KiB (matmul_launches with the Write epilogue,
+ * src/core/kernels/matmul/matmul.cpp:258-312). */
+fz_status fz_q8_0_matvec(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
+                         uint32_t m, float *y, void *stream);
+fz_status fz_q4_1_matvec(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
+                         uint32_t m, float *y, void *stream);
+
 /* Y[m][n] = sum_k W[n][k] X[m][k] for many rows on the tensor cores
  * (tcgen05.mma into tensor memory; the reference's prefill form,
  * src/core/kernels/matmul/matmul.wgsl:287-485): X as f16 `x_hi` [m][k] and

@@ -58,6 +58,10 @@ def _declare(L):
     L.oracle_f16_pack.argtypes = [C.c_float]; L.oracle_f16_pack.restype = C.c_uint16
     L.oracle_q4_0_dequant.argtypes = [U8P, C.c_int64, F32P]
     L.oracle_matmul.argtypes = [U8P, C.c_int, C.c_int, F32P, C.c_int, F32P]
+    L.oracle_matmul_fmt.argtypes = [C.c_int, U8P, C.c_int, C.c_int, F32P, C.c_int, F32P]
+    L.oracle_matmul_fmt.restype = C.c_int
+    L.oracle_blocks_dequant.argtypes = [C.c_int, U8P, C.c_int64, F32P]
+    L.oracle_blocks_dequant.restype = C.c_int
     L.oracle_gated.argtypes = [U8P, U8P, C.c_int, C.c_int, F32P, C.c_int, F32P]
     L.oracle_exp_nonpositive.argtypes = [C.c_float]; L.oracle_exp_nonpositive.restype = C.c_float
     L.oracle_gelu.argtypes = [C.c_float]; L.oracle_gelu.restype = C.c_float
@@ -99,6 +103,31 @@ def gated(gate: np.ndarray, up: np.ndarray, f: int, k: int, x: np.ndarray) -> np
     lib().oracle_gated(np.ascontiguousarray(gate, dtype=np.uint8), np.ascontiguousarray(up, dtype=np.uint8),
                        f, k, x, x.shape[0], y)
     return y
+
+
+# GGUF type numbers (gguf::TensorType) and block bytes of the formats the
+# oracle restates.
+TYPE_Q4_0, TYPE_Q4_1, TYPE_Q8_0 = 2, 3, 8
+BLOCK_BYTES = {TYPE_Q4_0: 18, TYPE_Q4_1: 20, TYPE_Q8_0: 34}
+
+
+def matmul_fmt(gguf_type: int, blocks: np.ndarray, n: int, k: int, x: np.ndarray) -> np.ndarray:
+    """y = x W^T over blocks of any restated format, in the reference's order."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+    y = np.empty((x.shape[0], n), dtype=np.float32)
+    rc = lib().oracle_matmul_fmt(gguf_type, np.ascontiguousarray(blocks, dtype=np.uint8), n, k, x, x.shape[0], y)
+    if rc != 0:
+        raise ValueError(f"type {gguf_type} is not restated")
+    return y
+
+
+def dequant_fmt(gguf_type: int, blocks: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(blocks, dtype=np.uint8)
+    nb = b.size // BLOCK_BYTES[gguf_type]
+    out = np.empty(nb * 32, dtype=np.float32)
+    if lib().oracle_blocks_dequant(gguf_type, b, nb, out) != 0:
+        raise ValueError(f"type {gguf_type} is not restated")
+    return out
 
 
 def dequant(blocks: np.ndarray) -> np.ndarray:

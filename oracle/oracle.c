@@ -88,6 +88,53 @@ EXPORT void oracle_q4_0_dequant(const uint8_t *blocks, int64_t nblocks, float *o
     for (int64_t b = 0; b < nblocks; b++) oracle_q4_0_unpack(blocks + 18 * b, out + 32 * b);
 }
 
+/* ------------------------------------------------------------ Q8_0 and Q4_1 */
+
+/* Q8_0 block of 34 bytes as the file stores it: fp16 d, then 32 signed code
+ * bytes; weight j = qs[j] * d, exact in f32 (formats/q8_0/q8_0.h:19-21,
+ * formats/q8_0/q8_0.wgsl:11-23). */
+EXPORT void oracle_q8_0_unpack(const uint8_t *block, float out[32]) {
+    float d = oracle_f16_to_f32((uint16_t)(block[0] | (block[1] << 8)));
+    for (int j = 0; j < 32; j++) out[j] = (float)(int8_t)block[2 + j] * d;
+}
+
+/* Q4_1 block of 20 bytes: fp16 d, fp16 m, then 16 code bytes; weight j =
+ * (qs[j] & 0xF) * d + m, weight j + 16 = (qs[j] >> 4) * d + m
+ * (formats/q4_1/q4_1.h:20-23, formats/q4_1/q4_1.wgsl:12-26).  The product of
+ * a 4-bit code and an 11-bit significand is exact in f32, so the shader's
+ * `code * d + m` rounds once whether or not it is fused. */
+EXPORT void oracle_q4_1_unpack(const uint8_t *block, float out[32]) {
+    float d = oracle_f16_to_f32((uint16_t)(block[0] | (block[1] << 8)));
+    float m = oracle_f16_to_f32((uint16_t)(block[2] | (block[3] << 8)));
+    for (int j = 0; j < 16; j++) {
+        out[j] = (float)(block[4 + j] & 0xF) * d + m;
+        out[j + 16] = (float)(block[4 + j] >> 4) * d + m;
+    }
+}
+
+typedef void (*unpack_fn)(const uint8_t *, float *);
+
+/* Formats by their GGUF type number (gguf::TensorType): 2 Q4_0, 3 Q4_1, 8 Q8_0. */
+static int format_of(int type, unpack_fn *unpack) {
+    switch (type) {
+    case 2: *unpack = oracle_q4_0_unpack; return 18;
+    case 3: *unpack = oracle_q4_1_unpack; return 20;
+    case 8: *unpack = oracle_q8_0_unpack; return 34;
+    default: *unpack = 0; return 0;
+    }
+}
+
+/* Every block of a run of `nblocks` blocks of GGUF type `type`, unpacked;
+ * returns 0, or -1 for a type this oracle does not restate. */
+EXPORT int oracle_blocks_dequant(int type, const uint8_t *blocks, int64_t nblocks, float *out) {
+    unpack_fn unpack;
+    int bytes = format_of(type, &unpack);
+    if (!bytes) return -1;
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nblocks; b++) unpack(blocks + (int64_t)bytes * b, out + 32 * b);
+    return 0;
+}
+
 /* ------------------------------------------------------------ matmul */
 
 /* y[t][o] = sum_k W[o][k] x[t][k] over K/32 groups split into 32 ranges,
@@ -96,8 +143,8 @@ EXPORT void oracle_q4_0_dequant(const uint8_t *blocks, int64_t nblocks, float *o
  * zero (matmul.wgsl:154-185 decode_ranges/slot_total, :320-405 tile_range/
  * prefill_tile, :548-571 combine; matmul.h:88-97).  Every form of the
  * reference produces these bits. */
-static void matmul_rows(const uint8_t *W, int K, const float *X, int M, int row_stride_x,
-                        int o, float *y_out /* M values, stride given */, int y_stride) {
+static void matmul_rows_fmt(unpack_fn unpack, int block_bytes, const uint8_t *W, int K, const float *X, int M,
+                            int row_stride_x, int o, float *y_out /* M values, stride given */, int y_stride) {
     int G = K / 32;
     float w[32];
     float totals[64];
@@ -110,7 +157,7 @@ static void matmul_rows(const uint8_t *W, int K, const float *X, int M, int row_
             int lo = r * G / 32, hi = (r + 1) * G / 32;
             for (int t = 0; t < tn; t++) parts[t] = 0.0f;
             for (int g = lo; g < hi; g++) {
-                oracle_q4_0_unpack(W + ((int64_t)o * G + g) * 18, w);
+                unpack(W + ((int64_t)o * G + g) * block_bytes, w);
                 for (int t = 0; t < tn; t++) {
                     const float *x = X + (int64_t)(t0 + t) * row_stride_x + g * 32;
                     float a = parts[t];
@@ -122,6 +169,23 @@ static void matmul_rows(const uint8_t *W, int K, const float *X, int M, int row_
         }
         for (int t = 0; t < tn; t++) y_out[(int64_t)(t0 + t) * y_stride] = totals[t];
     }
+}
+
+static void matmul_rows(const uint8_t *W, int K, const float *X, int M, int row_stride_x,
+                        int o, float *y_out, int y_stride) {
+    matmul_rows_fmt(oracle_q4_0_unpack, 18, W, K, X, M, row_stride_x, o, y_out, y_stride);
+}
+
+/* The same product over blocks of GGUF type `type` (the reference's matmul
+ * is one shader over every format's unpack: matmul.wgsl:84-245 with
+ * formats/format.h); returns -1 for a type this oracle does not restate. */
+EXPORT int oracle_matmul_fmt(int type, const uint8_t *W, int N, int K, const float *X, int M, float *Y) {
+    unpack_fn unpack;
+    int bytes = format_of(type, &unpack);
+    if (!bytes) return -1;
+#pragma omp parallel for schedule(dynamic, 16)
+    for (int o = 0; o < N; o++) matmul_rows_fmt(unpack, bytes, W, K, X, M, K, o, Y + o, N);
+    return 0;
 }
 
 EXPORT void oracle_matmul(const uint8_t *W, int N, int K, const float *X, int M, float *Y) {
