@@ -11,9 +11,11 @@
 // m, 4 bytes, d in the low half).  The codes keep the file's bits; a row's
 // codes are contiguous, so a warp streams a row with 128-bit loads.
 //
-// The product: each warp takes four rows of W at a time; every lane loads up
-// to three 16-byte code chunks of each row before any arithmetic (twelve
-// loads in flight a lane), decodes bytes to f32 exactly through the 2^23
+// The product: each warp takes four rows of W at a time, their 16-byte code
+// chunks as one stream shared over the lanes; every lane holds two batches of
+// up to three chunks (two for more than two rows of x) in registers, the next
+// batch's loads in flight while the current one's arithmetic runs, decodes
+// bytes to f32 exactly through the 2^23
 // exponent trick (one byte permute and one subtract a code), multiplies by x
 // staged in shared memory (a swizzle makes the lanes' float4 reads conflict
 // free), and applies the block scale once per chunk.  Q4_1's minimum enters as
@@ -48,7 +50,6 @@ struct Fmt<kQ4_1> {
 
 constexpr int kWarps = 8;       // warps a CTA
 constexpr int kRows = 4;        // rows of W a warp takes at a time
-constexpr int kBatch = 3;       // code chunks a lane loads from each row per pass
 constexpr int kMaxRows = 8;     // rows of x
 constexpr size_t kMaxShared = 200 * 1024;
 
@@ -155,14 +156,26 @@ __global__ void rows_kernel(const uint8_t* codes, const uint8_t* scales, uint32_
   }
 }
 
+// One batch of a lane's code chunks: their words, scale words and places
+// ((row in quad << 16) | chunk, ~0u for an empty slot), and the quad they
+// belong to, `last` when the batch completes it.
+template <int B>
+struct Batch {
+  uint4 w[B];
+  uint32_t sw[B], at[B];
+  uint32_t task;
+  bool last;
+};
+
 template <int F, int MT>
-__global__ void __launch_bounds__(kWarps * 32) matvec_kernel(const uint8_t* __restrict__ codes,
+__global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) matvec_kernel(const uint8_t* __restrict__ codes,
                                                              const uint8_t* __restrict__ scales, uint32_t n,
                                                              uint32_t k, const float* __restrict__ x,
                                                              float* __restrict__ y) {
   constexpr uint32_t CW = Fmt<F>::chunk_cols / 4;  // float4 units a chunk
   constexpr int MTP = MT == 1 ? 1 : MT == 2 ? 2 : MT <= 4 ? 4 : 8;
   constexpr int NV = kRows * MTP;
+  constexpr int B = MT <= 2 ? 3 : 2;  // chunks a lane loads a batch (3: a 1152- or 6912-wide Q8_0 quad in whole batches)
   extern __shared__ float4 smem[];
   const uint32_t units = k / 4, chunks = k / Fmt<F>::chunk_cols, kb = k / 32;
   float4* xs = smem;                                   // [MT][units], swizzled within chunks
@@ -188,111 +201,149 @@ __global__ void __launch_bounds__(kWarps * 32) matvec_kernel(const uint8_t* __re
   __syncthreads();
 
   const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const uint32_t quads = (n + kRows - 1) / kRows;
+  const uint32_t quads = (n + kRows - 1) / kRows, stride = gridDim.x * kWarps;
   const size_t row_bytes = (size_t)kb * Fmt<F>::code_bytes;
-  for (uint32_t task = blockIdx.x * kWarps + warp; task < quads; task += gridDim.x * kWarps) {
-    const uint32_t r0 = task * kRows;
-    float acc[kRows][MT];
-#pragma unroll
-    for (int r = 0; r < kRows; r++)
-#pragma unroll
-      for (int m = 0; m < MT; m++) acc[r][m] = 0.0f;
+  // A warp's quads' chunks as one stream: quad `task`'s kRows * chunks items,
+  // item f being chunk f % chunks of row f / chunks, so every lane has work in
+  // every batch whatever the row length; a lane's items advance by 32 a slot.
+  // Two batches in registers: one batch's loads are in flight while the
+  // other's arithmetic runs, across quad boundaries too.
+  const uint32_t items = kRows * chunks;
+  const uint32_t rl0 = lane / chunks, c0 = lane % chunks;
+  uint32_t task = blockIdx.x * kWarps + warp, f0 = 0, rl = rl0, c = c0;
 
-    for (uint32_t base = 0; base < chunks; base += 32 * kBatch) {
-      uint4 w[kRows][kBatch];
-      uint32_t sw[kRows][kBatch];
+  float acc[kRows][MT];
 #pragma unroll
-      for (int r = 0; r < kRows; r++)
+  for (int r = 0; r < kRows; r++)
 #pragma unroll
-        for (int b = 0; b < kBatch; b++) {
-          const uint32_t c = base + 32 * b + lane;
-          const uint32_t row = r0 + r;
-          if (c < chunks && row < n) {
-            w[r][b] = load_stream(codes + row * row_bytes + (size_t)c * 16);
-            if (F == kQ8_0)
-              sw[r][b] = __ldg(reinterpret_cast<const uint16_t*>(scales) + (size_t)row * kb + c / 2);
-            else
-              sw[r][b] = __ldg(reinterpret_cast<const uint32_t*>(scales) + (size_t)row * kb + c);
-          } else {
-            w[r][b] = make_uint4(0, 0, 0, 0);
-            sw[r][b] = 0;
+    for (int m = 0; m < MT; m++) acc[r][m] = 0.0f;
+
+  Batch<B> bufA, bufB;
+  auto fetch = [&](Batch<B>& bt) {
+    bt.task = task;
+    bt.last = false;
+    if (task >= quads) return;
+    const uint32_t r0 = task * kRows;
+#pragma unroll
+    for (int i = 0; i < B; i++) {
+      const uint32_t row = r0 + rl;
+      if (f0 + 32 * i + lane < items && row < n) {
+        bt.w[i] = load_stream(codes + row * row_bytes + (size_t)c * 16);
+        if (F == kQ8_0)
+          bt.sw[i] = __ldg(reinterpret_cast<const uint16_t*>(scales) + (size_t)row * kb + c / 2);
+        else
+          bt.sw[i] = __ldg(reinterpret_cast<const uint32_t*>(scales) + (size_t)row * kb + c);
+        bt.at[i] = (rl << 16) | c;
+      } else {
+        bt.at[i] = ~0u;
+      }
+      c += 32;
+      while (c >= chunks) {
+        c -= chunks;
+        rl++;
+      }
+    }
+    f0 += 32 * B;
+    if (f0 >= items) {
+      bt.last = true;
+      task += stride;
+      f0 = 0;
+      rl = rl0;
+      c = c0;
+    }
+  };
+  auto consume = [&](const Batch<B>& bt) {
+#pragma unroll
+    for (int i = 0; i < B; i++) {
+      if (bt.at[i] == ~0u) continue;
+      const uint32_t cc = bt.at[i] & 0xffffu, rr = bt.at[i] >> 16;
+      const uint32_t sz = swizzle<CW>(cc);
+      const float4* xc = xs + cc * CW;
+      float part[MT];
+#pragma unroll
+      for (int m = 0; m < MT; m++) part[m] = 0.0f;
+      const uint32_t words[4] = {bt.w[i].x, bt.w[i].y, bt.w[i].z, bt.w[i].w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        if (F == kQ8_0) {
+          // Signed codes biased by 128: 2^23 + 128 + code, exact.
+          const uint32_t t = words[q] ^ 0x80808080u;
+          const float e0 = byte_as_f32_biased<0>(t) - 8388736.0f, e1 = byte_as_f32_biased<1>(t) - 8388736.0f;
+          const float e2 = byte_as_f32_biased<2>(t) - 8388736.0f, e3 = byte_as_f32_biased<3>(t) - 8388736.0f;
+#pragma unroll
+          for (int m = 0; m < MT; m++) {
+            const float4 xv = xc[m * units + (q ^ sz)];
+            part[m] = fmaf(e0, xv.x, part[m]);
+            part[m] = fmaf(e1, xv.y, part[m]);
+            part[m] = fmaf(e2, xv.z, part[m]);
+            part[m] = fmaf(e3, xv.w, part[m]);
           }
-        }
+        } else {
+          // Byte j's low nibble is column j, its high nibble column j + 16.
+          const uint32_t lo = words[q] & 0x0F0F0F0Fu, hi = (words[q] >> 4) & 0x0F0F0F0Fu;
+          const float l0 = byte_as_f32_biased<0>(lo) - 8388608.0f, l1 = byte_as_f32_biased<1>(lo) - 8388608.0f;
+          const float l2 = byte_as_f32_biased<2>(lo) - 8388608.0f, l3 = byte_as_f32_biased<3>(lo) - 8388608.0f;
+          const float h0 = byte_as_f32_biased<0>(hi) - 8388608.0f, h1 = byte_as_f32_biased<1>(hi) - 8388608.0f;
+          const float h2 = byte_as_f32_biased<2>(hi) - 8388608.0f, h3 = byte_as_f32_biased<3>(hi) - 8388608.0f;
 #pragma unroll
-      for (int b = 0; b < kBatch; b++) {
-        const uint32_t c = base + 32 * b + lane;
-        if (c >= chunks) continue;
-        const uint32_t sz = swizzle<CW>(c);
-#pragma unroll
-        for (int r = 0; r < kRows; r++) {
-          if (r0 + r >= n) continue;
-          float part[MT];
-#pragma unroll
-          for (int m = 0; m < MT; m++) part[m] = 0.0f;
-          const uint32_t words[4] = {w[r][b].x, w[r][b].y, w[r][b].z, w[r][b].w};
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            if (F == kQ8_0) {
-              // Signed codes biased by 128: 2^23 + 128 + code, exact.
-              const uint32_t t = words[q] ^ 0x80808080u;
-              const float f0 = byte_as_f32_biased<0>(t) - 8388736.0f, f1 = byte_as_f32_biased<1>(t) - 8388736.0f;
-              const float f2 = byte_as_f32_biased<2>(t) - 8388736.0f, f3 = byte_as_f32_biased<3>(t) - 8388736.0f;
-#pragma unroll
-              for (int m = 0; m < MT; m++) {
-                const float4 xv = xs[m * units + c * CW + (q ^ sz)];
-                part[m] = fmaf(f0, xv.x, part[m]);
-                part[m] = fmaf(f1, xv.y, part[m]);
-                part[m] = fmaf(f2, xv.z, part[m]);
-                part[m] = fmaf(f3, xv.w, part[m]);
-              }
-            } else {
-              // Byte j's low nibble is column j, its high nibble column j + 16.
-              const uint32_t lo = words[q] & 0x0F0F0F0Fu, hi = (words[q] >> 4) & 0x0F0F0F0Fu;
-              const float l0 = byte_as_f32_biased<0>(lo) - 8388608.0f, l1 = byte_as_f32_biased<1>(lo) - 8388608.0f;
-              const float l2 = byte_as_f32_biased<2>(lo) - 8388608.0f, l3 = byte_as_f32_biased<3>(lo) - 8388608.0f;
-              const float h0 = byte_as_f32_biased<0>(hi) - 8388608.0f, h1 = byte_as_f32_biased<1>(hi) - 8388608.0f;
-              const float h2 = byte_as_f32_biased<2>(hi) - 8388608.0f, h3 = byte_as_f32_biased<3>(hi) - 8388608.0f;
-#pragma unroll
-              for (int m = 0; m < MT; m++) {
-                const float4 xl = xs[m * units + c * CW + (q ^ sz)];
-                const float4 xh = xs[m * units + c * CW + ((4 + q) ^ sz)];
-                part[m] = fmaf(l0, xl.x, part[m]);
-                part[m] = fmaf(l1, xl.y, part[m]);
-                part[m] = fmaf(l2, xl.z, part[m]);
-                part[m] = fmaf(l3, xl.w, part[m]);
-                part[m] = fmaf(h0, xh.x, part[m]);
-                part[m] = fmaf(h1, xh.y, part[m]);
-                part[m] = fmaf(h2, xh.z, part[m]);
-                part[m] = fmaf(h3, xh.w, part[m]);
-              }
-            }
-          }
-          if (F == kQ8_0) {
-            const float d = fz::f16_unpack((uint16_t)sw[r][b]);
-#pragma unroll
-            for (int m = 0; m < MT; m++) acc[r][m] = fmaf(d, part[m], acc[r][m]);
-          } else {
-            const float d = fz::f16_unpack((uint16_t)(sw[r][b] & 0xffffu));
-            const float mn = fz::f16_unpack((uint16_t)(sw[r][b] >> 16));
-#pragma unroll
-            for (int m = 0; m < MT; m++)
-              acc[r][m] = fmaf(mn, bsum[m * kb + c], fmaf(d, part[m], acc[r][m]));
+          for (int m = 0; m < MT; m++) {
+            const float4 xl = xc[m * units + (q ^ sz)];
+            const float4 xh = xc[m * units + ((4 + q) ^ sz)];
+            part[m] = fmaf(l0, xl.x, part[m]);
+            part[m] = fmaf(l1, xl.y, part[m]);
+            part[m] = fmaf(l2, xl.z, part[m]);
+            part[m] = fmaf(l3, xl.w, part[m]);
+            part[m] = fmaf(h0, xh.x, part[m]);
+            part[m] = fmaf(h1, xh.y, part[m]);
+            part[m] = fmaf(h2, xh.z, part[m]);
+            part[m] = fmaf(h3, xh.w, part[m]);
           }
         }
       }
+      float val[MT];
+      if (F == kQ8_0) {
+        const float d = fz::f16_unpack((uint16_t)bt.sw[i]);
+#pragma unroll
+        for (int m = 0; m < MT; m++) val[m] = d * part[m];
+      } else {
+        const float d = fz::f16_unpack((uint16_t)(bt.sw[i] & 0xffffu));
+        const float mn = fz::f16_unpack((uint16_t)(bt.sw[i] >> 16));
+#pragma unroll
+        for (int m = 0; m < MT; m++) val[m] = fmaf(mn, bsum[m * kb + cc], d * part[m]);
+      }
+#pragma unroll
+      for (int r = 0; r < kRows; r++)
+#pragma unroll
+        for (int m = 0; m < MT; m++) acc[r][m] += rr == (uint32_t)r ? val[m] : 0.0f;
     }
-
+    if (!bt.last) return;
+    // The quad is complete: its kRows x MT sums meet across the warp.
     float v[NV];
 #pragma unroll
     for (int r = 0; r < kRows; r++)
 #pragma unroll
       for (int m = 0; m < MTP; m++) v[r * MTP + m] = m < MT ? acc[r][m < MT ? m : 0] : 0.0f;
-    const float total = reduce_scatter<NV>(v, lane);
+    const float sum = reduce_scatter<NV>(v, lane);
     constexpr int SHIFT = 5 - Log2<NV>::value;
     if ((lane & ((1u << SHIFT) - 1)) == 0) {
       const uint32_t idx = lane >> SHIFT, r = idx / MTP, m = idx % MTP;
-      if (m < MT && r0 + r < n) y[(size_t)m * n + r0 + r] = total;
+      const uint32_t row = bt.task * kRows + r;
+      if (m < MT && row < n) y[(size_t)m * n + row] = sum;
     }
+#pragma unroll
+    for (int r = 0; r < kRows; r++)
+#pragma unroll
+      for (int m = 0; m < MT; m++) acc[r][m] = 0.0f;
+  };
+
+  // task, and so every branch below, is uniform over the warp.
+  fetch(bufA);
+  while (bufA.task < quads) {
+    fetch(bufB);
+    consume(bufA);
+    if (bufB.task >= quads) break;
+    fetch(bufA);
+    consume(bufB);
   }
 }
 
