@@ -13,17 +13,17 @@
 //
 // The product: each warp takes four rows of W at a time, their 16-byte code
 // chunks as one stream shared over the lanes; every lane holds two batches of
-// up to three chunks (two for more than two rows of x) in registers, the next
-// batch's loads in flight while the current one's arithmetic runs, decodes
-// bytes to f32 exactly through the 2^23
-// exponent trick (one byte permute and one subtract a code), multiplies by x
-// staged in shared memory (a swizzle makes the lanes' float4 reads conflict
-// free), and applies the block scale once per chunk.  Q4_1's minimum enters as
-// m * (sum of x over the block), precomputed per block when x is staged.  The
-// lanes' sums meet in a reduce-scatter over the warp (4*M values, one per lane
-// group).  Sums are f32 in another order than the reference's 32 ranges
-// (matmul.wgsl:154-185), so results agree with it within rounding, not bit
-// for bit; the gather is bit-exact.
+// up to three chunks in registers, the next batch's loads in flight while the
+// current one's arithmetic runs.  x is staged once per CTA as three signed
+// 8-bit digit planes and an f32 scale per 32-column block (x = s (d0 + d1/254
+// + d2/254^2) to about 6e-8 of the block's largest |x|), so the codes, as they
+// come from memory (Q8_0) or masked to nibbles (Q4_1), meet x in dp4a integer
+// dot products, exact in i32, with one f32 combination a chunk.  Q4_1's
+// minimum enters as m * (f32 sum of x over the block).  The lanes' sums meet
+// in a reduce-scatter over the warp (4*M values, one per lane group).  The
+// result agrees with the reference's f32 sums (matmul.wgsl:154-185) within
+// rounding, not bit for bit; a row of x with a non-finite value gives NaN
+// sums.  The gather is bit-exact.
 #include <algorithm>
 #include <string>
 
@@ -39,12 +39,12 @@ template <int F>
 struct Fmt;
 template <>
 struct Fmt<kQ8_0> {
-  static constexpr uint32_t file_bytes = 34, code_bytes = 32, scale_bytes = 2, code_offset = 2;
+  static constexpr uint32_t file_bytes = 34, code_bytes = 32, scale_bytes = 2;
   static constexpr uint32_t chunk_cols = 16;  // columns a 16-byte code chunk covers
 };
 template <>
 struct Fmt<kQ4_1> {
-  static constexpr uint32_t file_bytes = 20, code_bytes = 16, scale_bytes = 4, code_offset = 4;
+  static constexpr uint32_t file_bytes = 20, code_bytes = 16, scale_bytes = 4;
   static constexpr uint32_t chunk_cols = 32;
 };
 
@@ -59,21 +59,6 @@ FZ_DEV uint4 load_stream(const uint8_t* p) {
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
-}
-
-// Byte `i` of `word` as the f32 2^23 + byte: the byte becomes the low
-// mantissa bits under the exponent of 2^23 (exact; subtracting 2^23 gives it).
-template <int I>
-FZ_DEV float byte_as_f32_biased(uint32_t word) {
-  return __uint_as_float(__byte_perm(word, 0x4B000000u, 0x7440u | I));
-}
-
-// The float4 unit q of chunk c, stored at c*CW + (q ^ swizzle(c)) so that
-// eight lanes reading the same q of eight consecutive chunks hit eight
-// different 16-byte bank groups.
-template <int CW>
-FZ_DEV uint32_t swizzle(uint32_t c) {
-  return CW == 4 ? (c >> 1) & 3u : c & 7u;
 }
 
 template <int NV>
@@ -172,30 +157,45 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) matvec_kernel(co
                                                              const uint8_t* __restrict__ scales, uint32_t n,
                                                              uint32_t k, const float* __restrict__ x,
                                                              float* __restrict__ y) {
-  constexpr uint32_t CW = Fmt<F>::chunk_cols / 4;  // float4 units a chunk
   constexpr int MTP = MT == 1 ? 1 : MT == 2 ? 2 : MT <= 4 ? 4 : 8;
   constexpr int NV = kRows * MTP;
   constexpr int B = MT <= 2 ? 3 : 2;  // chunks a lane loads a batch (3: a 1152- or 6912-wide Q8_0 quad in whole batches)
   extern __shared__ float4 smem[];
-  const uint32_t units = k / 4, chunks = k / Fmt<F>::chunk_cols, kb = k / 32;
-  float4* xs = smem;                                   // [MT][units], swizzled within chunks
-  float* bsum = reinterpret_cast<float*>(smem + MT * units);  // Q4_1: [MT][kb]
-
-  for (uint32_t i = threadIdx.x; i < MT * units; i += blockDim.x) {
-    const uint32_t mr = i / units, u = i % units, c = u / CW, q = u % CW;
-    xs[mr * units + c * CW + (q ^ swizzle<CW>(c))] = reinterpret_cast<const float4*>(x)[i];
-  }
-  if (F == kQ4_1) {
-    __syncthreads();
-    for (uint32_t i = threadIdx.x; i < MT * kb; i += blockDim.x) {
-      const uint32_t mr = i / kb, c = i % kb;
-      float s = 0.0f;
+  const uint32_t chunks = k / Fmt<F>::chunk_cols, kb = k / 32;
+  // x staged as digits: per row and 32-column block, s = max|x| / 127 and
+  // three signed 8-bit digit planes with x = s (d0 + d1 / 254 + d2 / 254^2)
+  // to within s / 2 / 254^2 (about 6e-8 of the block's largest |x|).
+  int8_t* digits = reinterpret_cast<int8_t*>(smem);                  // [MT][3][k]
+  float* xscale = reinterpret_cast<float*>(digits + (size_t)MT * 3 * k);  // [MT][kb]
+  float* bsum = xscale + MT * kb;                                     // Q4_1: [MT][kb], sum of x
+  {
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    for (uint32_t i = warp; i < MT * kb; i += kWarps) {
+      const uint32_t mr = i / kb, g = i % kb;
+      const float v = x[(size_t)mr * k + g * 32 + lane];
+      float mx = fabsf(v);
 #pragma unroll
-      for (uint32_t q = 0; q < CW; q++) {
-        const float4 v = xs[mr * units + c * CW + q];
-        s += (v.x + v.y) + (v.z + v.w);
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      // Blocks below 2^-100 are scaled up by 2^64 first, so 127 / max stays
+      // finite; a non-finite block gets a NaN scale (its rows' sums become NaN).
+      const float pre = mx < 0x1p-100f ? 0x1p64f : 1.0f;
+      const bool finite = mx <= 3.402823466e38f;
+      const float inv = mx > 0.0f && finite ? 127.0f / (mx * pre) : 0.0f;
+      const float t = finite ? v * pre * inv : 0.0f;
+      const float d0 = fminf(fmaxf(rintf(t), -127.0f), 127.0f);
+      const float r1 = (t - d0) * 254.0f;
+      const float d1 = fminf(fmaxf(rintf(r1), -127.0f), 127.0f);
+      const float r2 = (r1 - d1) * 254.0f;
+      const float d2 = fminf(fmaxf(rintf(r2), -127.0f), 127.0f);
+      int8_t* dg = digits + (size_t)mr * 3 * k + g * 32 + lane;
+      dg[0] = (int8_t)d0;
+      dg[k] = (int8_t)d1;
+      dg[2 * k] = (int8_t)d2;
+      if (lane == 0) xscale[i] = finite ? mx * pre / 127.0f / pre : __int_as_float(0x7fc00000);
+      if (F == kQ4_1) {
+        const float sum = fz::warp_sum(v);
+        if (lane == 0) bsum[i] = sum;
       }
-      bsum[i] = s;
     }
   }
   __syncthreads();
@@ -257,59 +257,59 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) matvec_kernel(co
     for (int i = 0; i < B; i++) {
       if (bt.at[i] == ~0u) continue;
       const uint32_t cc = bt.at[i] & 0xffffu, rr = bt.at[i] >> 16;
-      const uint32_t sz = swizzle<CW>(cc);
-      const float4* xc = xs + cc * CW;
-      float part[MT];
-#pragma unroll
-      for (int m = 0; m < MT; m++) part[m] = 0.0f;
-      const uint32_t words[4] = {bt.w[i].x, bt.w[i].y, bt.w[i].z, bt.w[i].w};
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        if (F == kQ8_0) {
-          // Signed codes biased by 128: 2^23 + 128 + code, exact.
-          const uint32_t t = words[q] ^ 0x80808080u;
-          const float e0 = byte_as_f32_biased<0>(t) - 8388736.0f, e1 = byte_as_f32_biased<1>(t) - 8388736.0f;
-          const float e2 = byte_as_f32_biased<2>(t) - 8388736.0f, e3 = byte_as_f32_biased<3>(t) - 8388736.0f;
-#pragma unroll
-          for (int m = 0; m < MT; m++) {
-            const float4 xv = xc[m * units + (q ^ sz)];
-            part[m] = fmaf(e0, xv.x, part[m]);
-            part[m] = fmaf(e1, xv.y, part[m]);
-            part[m] = fmaf(e2, xv.z, part[m]);
-            part[m] = fmaf(e3, xv.w, part[m]);
-          }
-        } else {
-          // Byte j's low nibble is column j, its high nibble column j + 16.
-          const uint32_t lo = words[q] & 0x0F0F0F0Fu, hi = (words[q] >> 4) & 0x0F0F0F0Fu;
-          const float l0 = byte_as_f32_biased<0>(lo) - 8388608.0f, l1 = byte_as_f32_biased<1>(lo) - 8388608.0f;
-          const float l2 = byte_as_f32_biased<2>(lo) - 8388608.0f, l3 = byte_as_f32_biased<3>(lo) - 8388608.0f;
-          const float h0 = byte_as_f32_biased<0>(hi) - 8388608.0f, h1 = byte_as_f32_biased<1>(hi) - 8388608.0f;
-          const float h2 = byte_as_f32_biased<2>(hi) - 8388608.0f, h3 = byte_as_f32_biased<3>(hi) - 8388608.0f;
-#pragma unroll
-          for (int m = 0; m < MT; m++) {
-            const float4 xl = xc[m * units + (q ^ sz)];
-            const float4 xh = xc[m * units + ((4 + q) ^ sz)];
-            part[m] = fmaf(l0, xl.x, part[m]);
-            part[m] = fmaf(l1, xl.y, part[m]);
-            part[m] = fmaf(l2, xl.z, part[m]);
-            part[m] = fmaf(l3, xl.w, part[m]);
-            part[m] = fmaf(h0, xh.x, part[m]);
-            part[m] = fmaf(h1, xh.y, part[m]);
-            part[m] = fmaf(h2, xh.z, part[m]);
-            part[m] = fmaf(h3, xh.w, part[m]);
-          }
-        }
-      }
+      // Integer products of the codes with each digit plane (exact in i32),
+      // then one f32 combination a chunk.
       float val[MT];
       if (F == kQ8_0) {
         const float d = fz::f16_unpack((uint16_t)bt.sw[i]);
 #pragma unroll
-        for (int m = 0; m < MT; m++) val[m] = d * part[m];
+        for (int m = 0; m < MT; m++) {
+          const int8_t* dg = digits + (size_t)m * 3 * k + cc * 16;
+          const uint4 p0 = *reinterpret_cast<const uint4*>(dg);
+          const uint4 p1 = *reinterpret_cast<const uint4*>(dg + k);
+          const uint4 p2 = *reinterpret_cast<const uint4*>(dg + 2 * k);
+          const uint4 w = bt.w[i];
+          const int s0 = __dp4a((int)w.w, (int)p0.w, __dp4a((int)w.z, (int)p0.z,
+                         __dp4a((int)w.y, (int)p0.y, __dp4a((int)w.x, (int)p0.x, 0))));
+          const int s1 = __dp4a((int)w.w, (int)p1.w, __dp4a((int)w.z, (int)p1.z,
+                         __dp4a((int)w.y, (int)p1.y, __dp4a((int)w.x, (int)p1.x, 0))));
+          const int s2 = __dp4a((int)w.w, (int)p2.w, __dp4a((int)w.z, (int)p2.z,
+                         __dp4a((int)w.y, (int)p2.y, __dp4a((int)w.x, (int)p2.x, 0))));
+          const float sum = fmaf((float)s2, 1.0f / 64516.0f, fmaf((float)s1, 1.0f / 254.0f, (float)s0));
+          val[m] = d * xscale[m * kb + cc / 2] * sum;
+        }
       } else {
         const float d = fz::f16_unpack((uint16_t)(bt.sw[i] & 0xffffu));
         const float mn = fz::f16_unpack((uint16_t)(bt.sw[i] >> 16));
+        // Byte j's low nibble is column j, its high nibble column j + 16;
+        // nibbles are 0..15, the same bytes signed or unsigned.
+        const uint32_t words[4] = {bt.w[i].x, bt.w[i].y, bt.w[i].z, bt.w[i].w};
+        uint32_t lo[4], hi[4];
 #pragma unroll
-        for (int m = 0; m < MT; m++) val[m] = fmaf(mn, bsum[m * kb + cc], d * part[m]);
+        for (int q = 0; q < 4; q++) {
+          lo[q] = words[q] & 0x0F0F0F0Fu;
+          hi[q] = (words[q] >> 4) & 0x0F0F0F0Fu;
+        }
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+          int sp[3];
+#pragma unroll
+          for (int pl = 0; pl < 3; pl++) {
+            const int8_t* dg = digits + ((size_t)m * 3 + pl) * k + cc * 32;
+            const uint4 a0 = *reinterpret_cast<const uint4*>(dg);
+            const uint4 a1 = *reinterpret_cast<const uint4*>(dg + 16);
+            int t = __dp4a((int)lo[0], (int)a0.x, 0);
+            t = __dp4a((int)lo[1], (int)a0.y, t);
+            t = __dp4a((int)lo[2], (int)a0.z, t);
+            t = __dp4a((int)lo[3], (int)a0.w, t);
+            t = __dp4a((int)hi[0], (int)a1.x, t);
+            t = __dp4a((int)hi[1], (int)a1.y, t);
+            t = __dp4a((int)hi[2], (int)a1.z, t);
+            sp[pl] = __dp4a((int)hi[3], (int)a1.w, t);
+          }
+          const float sum = fmaf((float)sp[2], 1.0f / 64516.0f, fmaf((float)sp[1], 1.0f / 254.0f, (float)sp[0]));
+          val[m] = fmaf(mn, bsum[m * kb + cc], d * xscale[m * kb + cc] * sum);
+        }
       }
 #pragma unroll
       for (int r = 0; r < kRows; r++)
@@ -421,8 +421,11 @@ fz_status matvec(const void* codes, const void* scales, uint32_t n, uint32_t k, 
   if (m < 1 || m > (uint32_t)kMaxRows) return refuse(FZ_ERR_ARGUMENT, "m outside 1 .. 8");
   if (!aligned(codes, 16) || !aligned(x, 16) || !aligned(scales, Fmt<F>::scale_bytes))
     return refuse(FZ_ERR_ARGUMENT, "misaligned pointer (codes and x 16 bytes, scales 2 or 4)");
-  const size_t smem = (size_t)m * k * 4 + (F == kQ4_1 ? (size_t)m * (k / 32) * 4 : 0);
-  if (smem > kMaxShared) return refuse(FZ_ERR_ARGUMENT, "m x k too large: x is staged in 200 KiB of shared memory");
+  // Staged x: three digit bytes a value and a scale a block (Q4_1: and a block sum).
+  const size_t smem = (size_t)m * k * 3 + (size_t)m * (k / 32) * 4 * (F == kQ4_1 ? 2 : 1);
+  if (smem > kMaxShared)
+    return refuse(FZ_ERR_ARGUMENT, "m x k too large: x is staged in 200 KiB of shared memory, 3.125 bytes a value "
+                                   "(3.25 for Q4_1)");
   const auto* c = static_cast<const uint8_t*>(codes);
   const auto* s = static_cast<const uint8_t*>(scales);
   cudaStream_t st_ = static_cast<cudaStream_t>(stream);

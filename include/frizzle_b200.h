@@ -282,8 +282,9 @@ fz_status fz_q8_0_rows(const void *codes, const void *scales, uint32_t n, uint32
 fz_status fz_q4_1_rows(const void *codes, const void *scales, uint32_t n, uint32_t k, const uint32_t *rows,
                        uint32_t count, float scale, float *out, void *stream);
 
-/* y[m][n] = sum_k W[n][k] x[m][k], 1 <= m <= 8, m*k*4 bytes of x (plus m*k/8
- * for Q4_1) at most 200 KiB (matmul_launches with the Write epilogue,
+/* y[m][n] = sum_k W[n][k] x[m][k], 1 <= m <= 8, x staged in shared memory as
+ * 8-bit digit planes at 3.125 bytes a value (3.25 for Q4_1), at most 200 KiB
+ * (m = 8 at k = 6912 fits); a non-finite x gives NaN sums for its row (matmul_launches with the Write epilogue,
  * src/core/kernels/matmul/matmul.cpp:258-312). */
 fz_status fz_q8_0_matvec(const void *codes, const void *scales, uint32_t n, uint32_t k, const float *x,
                          uint32_t m, float *y, void *stream);

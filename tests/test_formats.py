@@ -94,7 +94,7 @@ def test_format_entry_points_refuse_bad_arguments():
         assert matvec(fake, fake, 64, 1024, fake, 0, fake, None) == 1
         assert matvec(fake + 4, fake, 64, 1024, fake, 1, fake, None) == 1      # codes misaligned
         assert matvec(fake, fake, 64, 1024, fake + 4, 1, fake, None) == 1      # x misaligned
-        assert matvec(fake, fake, 64, 8 * 6912, fake, 1, fake, None) == 1      # x past 200 KiB
+        assert matvec(fake, fake, 64, 8 * 6912, fake, 8, fake, None) == 1      # staged x past 200 KiB
         assert matvec(None, fake, 64, 1024, fake, 1, fake, None) == 1
     assert lib.fz_q8_0_repack(fake + 1, 16, 64, fake, fake, None) == 1
     assert lib.fz_q4_1_repack(fake + 2, 16, 64, fake, fake, None) == 1

@@ -1,9 +1,10 @@
 """Q8_0 and Q4_1 kernels through the C ABI on the GPU, against the CPU oracle
 on the same seeded blocks: the repacked streams are the file's fields moved
 whole, the gather is bit-exact, and the product is within 1e-5 relative RMS
-and 1e-4 x max|y| of the oracle's f32 (the kernel sums exact code-times-x
-products per chunk and scales once per chunk, in another order than the
-reference's 32 ranges)."""
+and 1e-4 x max|y| of the oracle's f32 (the kernel takes x as three 8-bit
+digit planes a 32-column block, exact integer products with the codes, and
+one f32 combination a chunk: about 6e-8 of a block's largest |x| lost, and
+another order of sums than the reference's 32 ranges)."""
 import numpy as np
 import pytest
 
@@ -71,12 +72,13 @@ def test_rows_bit_exact(fmt, scale):
     assert np.array_equal(out.cpu().numpy().reshape(len(rows), k).view(np.uint32), want.view(np.uint32))
 
 
-def matvec_case(fmt, n, k, m, seed):
+def matvec_case(fmt, n, k, m, seed, x=None):
     torch = torch_cuda()
     gtype, gen, _, _ = FORMATS[fmt]
     blocks = gen(n, k, seed=seed)
     codes, scales = repacked(fmt, blocks, n, k)
-    x = np.random.default_rng([seed, m]).standard_normal((m, k)).astype(np.float32)
+    if x is None:
+        x = np.random.default_rng([seed, m]).standard_normal((m, k)).astype(np.float32)
     xd = torch.from_numpy(x).cuda()
     y = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
     _native.check(fn(fmt, "matvec")(codes.data_ptr(), scales.data_ptr(), n, k, xd.data_ptr(), m, y.data_ptr(),
@@ -93,7 +95,7 @@ def matvec_case(fmt, n, k, m, seed):
 # counts (not a multiple of the four rows a warp takes) and small K.
 @pytest.mark.parametrize("fmt,k,n,m", [
     ("q8_0", 1152, 4096, 1), ("q8_0", 1152, 4096, 3), ("q8_0", 1152, 2048, 8), ("q8_0", 6912, 1152, 6),
-    ("q8_0", 1152, 1001, 2), ("q8_0", 32, 37, 1), ("q8_0", 1024, 1152, 5),
+    ("q8_0", 1152, 1001, 2), ("q8_0", 6912, 1152, 8), ("q8_0", 32, 37, 1), ("q8_0", 1024, 1152, 5),
     ("q4_1", 6912, 1152, 1), ("q4_1", 6912, 1152, 4), ("q4_1", 6912, 1152, 7), ("q4_1", 1152, 6912, 8),
     ("q4_1", 1152, 1001, 3), ("q4_1", 64, 19, 2), ("q4_1", 1152, 1024, 1),
 ])
@@ -104,3 +106,33 @@ def test_matvec_against_oracle(fmt, k, n, m):
 def test_q8_0_head_full_shape():
     """The tied head of the pinned file: 262144 x 1152 Q8_0, one row."""
     matvec_case("q8_0", 262144, 1152, 1, seed=24)
+
+
+@pytest.mark.parametrize("fmt", sorted(FORMATS))
+def test_matvec_block_ranges(fmt):
+    """x blocks of very different magnitudes, an all-zero block and a block
+    below 2^-100: each block's digits carry its own scale."""
+    k, m = 1152, 2
+    x = np.random.default_rng(25).standard_normal((m, k)).astype(np.float32)
+    x[0, 0:32] = 0.0
+    x[0, 32:64] *= np.float32(1e-35)
+    x[0, 64:96] *= np.float32(1e20)
+    x[1, 96:128] *= np.float32(1e-20)
+    x[1, 128:160] = 0.0
+    x[1, 128] = np.float32(3.0)
+    matvec_case(fmt, 512, k, m, seed=26, x=x)
+
+
+@pytest.mark.parametrize("fmt", sorted(FORMATS))
+def test_matvec_non_finite_row(fmt):
+    torch = torch_cuda()
+    n, k = 64, 1152
+    codes, scales = repacked(fmt, FORMATS[fmt][1](n, k, seed=27), n, k)
+    x = np.random.default_rng(28).standard_normal((2, k)).astype(np.float32)
+    x[1, 500] = np.inf
+    xd = torch.from_numpy(x).cuda()
+    y = torch.zeros((2, n), dtype=torch.float32, device="cuda")
+    _native.check(fn(fmt, "matvec")(codes.data_ptr(), scales.data_ptr(), n, k, xd.data_ptr(), 2, y.data_ptr(),
+                                    stream()))
+    got = y.cpu().numpy()
+    assert np.all(np.isfinite(got[0])) and np.all(np.isnan(got[1]))
