@@ -209,8 +209,8 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) matvec_kernel(co
   // Two batches in registers: one batch's loads are in flight while the
   // other's arithmetic runs, across quad boundaries too.
   const uint32_t items = kRows * chunks;
-  const float inv_chunks = 1.0f / (float)chunks;
-  uint32_t task = blockIdx.x * kWarps + warp, f0 = 0;
+  const uint32_t rl0 = lane / chunks, c0 = lane % chunks;
+  uint32_t task = blockIdx.x * kWarps + warp, f0 = 0, rl = rl0, c = c0;
 
   float acc[kRows][MT];
 #pragma unroll
@@ -223,27 +223,24 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) matvec_kernel(co
     bt.task = task;
     bt.last = false;
     if (task >= quads) return;
-    // A quad's rows are contiguous in both streams: item f's codes are at
-    // 16 f from the quad's first code byte, its scale word f / 2 (Q8_0: two
-    // chunks a block) or f (Q4_1) after the quad's first scale.
     const uint32_t r0 = task * kRows;
-    const uint32_t limit = min(items, (n - r0) * chunks);
-    const uint8_t* qc = codes + (size_t)r0 * row_bytes;
 #pragma unroll
     for (int i = 0; i < B; i++) {
-      const uint32_t f = f0 + 32 * i + lane;
-      if (f < limit) {
-        bt.w[i] = load_stream(qc + (size_t)f * 16);
+      const uint32_t row = r0 + rl;
+      if (f0 + 32 * i + lane < items && row < n) {
+        bt.w[i] = load_stream(codes + row * row_bytes + (size_t)c * 16);
         if (F == kQ8_0)
-          bt.sw[i] = __ldg(reinterpret_cast<const uint16_t*>(scales) + (size_t)r0 * kb + f / 2);
+          bt.sw[i] = __ldg(reinterpret_cast<const uint16_t*>(scales) + (size_t)row * kb + c / 2);
         else
-          bt.sw[i] = __ldg(reinterpret_cast<const uint32_t*>(scales) + (size_t)r0 * kb + f);
-        // f / chunks, exact: f < 2^22, and the 0.5 keeps the f32 quotient
-        // inside the right integer's interval.
-        const uint32_t rr = __float2uint_rz(((float)f + 0.5f) * inv_chunks);
-        bt.at[i] = (rr << 16) | (f - rr * chunks);
+          bt.sw[i] = __ldg(reinterpret_cast<const uint32_t*>(scales) + (size_t)row * kb + c);
+        bt.at[i] = (rl << 16) | c;
       } else {
         bt.at[i] = ~0u;
+      }
+      c += 32;
+      while (c >= chunks) {
+        c -= chunks;
+        rl++;
       }
     }
     f0 += 32 * B;
@@ -251,6 +248,8 @@ __global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) matvec_kernel(co
       bt.last = true;
       task += stride;
       f0 = 0;
+      rl = rl0;
+      c = c0;
     }
   };
   auto consume = [&](const Batch<B>& bt) {
