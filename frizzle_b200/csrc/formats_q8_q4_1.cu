@@ -153,7 +153,7 @@ struct Batch {
 };
 
 template <int F, int MT>
-__global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 3 : 2) matvec_kernel(const uint8_t* __restrict__ codes,
+__global__ void __launch_bounds__(kWarps * 32, MT == 1 ? 4 : 2) matvec_kernel(const uint8_t* __restrict__ codes,
                                                              const uint8_t* __restrict__ scales, uint32_t n,
                                                              uint32_t k, const float* __restrict__ x,
                                                              float* __restrict__ y) {
