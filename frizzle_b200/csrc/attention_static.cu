@@ -9,6 +9,9 @@
 // key splits; this variant keeps that scratch in a static device array that
 // every GPU loading the library holds until the process exits, so the caller
 // passes only its inputs and outputs.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <mutex>
 
 #include "frizzle_b200.h"
@@ -31,11 +34,40 @@ struct StaticScratch {
 };
 static __device__ __align__(256) StaticScratch g_scratch;
 
-// Device addresses of g_scratch, one per device, looked up once with that
-// device current.  In host code `g_scratch` names a host-side stand-in, so its
-// address must never reach a kernel.
+// Device addresses of g_scratch, one per CUDA context, looked up once with
+// that context current.  In host code `g_scratch` names a host-side stand-in,
+// so its address must never reach a kernel.  The key is the context's unique
+// ID (cuCtxGetId), not the device ordinal: a non-primary context on the same
+// device, or the primary context made again after cudaDeviceReset, loads the
+// module afresh at another address, and IDs are never reused in a process.
+struct ContextAddress {
+  unsigned long long context_id;
+  StaticScratch* address;
+};
+constexpr int kContexts = 64;
 std::mutex g_mu;
-StaticScratch* g_address[64] = {};
+ContextAddress g_address[kContexts] = {};
+int g_next = 0;
+
+PFN_cuCtxGetCurrent_v4000 g_get_current = nullptr;
+PFN_cuCtxGetId_v12000 g_get_id = nullptr;
+std::once_flag g_once;
+
+// The current context's ID, or false when the driver cannot say.
+bool current_context_id(unsigned long long& id) {
+  std::call_once(g_once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+  });
+  CUcontext ctx = nullptr;
+  return g_get_current && g_get_id && g_get_current(&ctx) == CUDA_SUCCESS && ctx && g_get_id(ctx, &id) == CUDA_SUCCESS;
+}
 
 fz_status refuse(fz_status s, const char* why) {
   fz::set_last_error(why);
@@ -49,7 +81,10 @@ extern "C" fz_status fz_attention_static(const float* q, const void* key_cache, 
                                          uint32_t position, uint32_t rows, float* out, void* stream) {
   if (!q || !key_cache || !value_cache || !out) return refuse(FZ_ERR_ARGUMENT, "null pointer");
   if (head_dim != kHeadDim) return refuse(FZ_ERR_NOT_SUPPORTED, "head dimension other than 256");
-  if (kv_heads == 0 || heads % kv_heads || heads / kv_heads > 8) return refuse(FZ_ERR_ARGUMENT, "heads per KV head 1..8");
+  if (kv_heads == 0 || heads % kv_heads) return refuse(FZ_ERR_ARGUMENT, "heads must be a multiple of kv_heads");
+  const uint32_t group = heads / kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8)
+    return refuse(FZ_ERR_ARGUMENT, "heads per KV head must be 1, 2, 4 or 8");
   if (rows == 0 || window == 0 || slots == 0) return refuse(FZ_ERR_ARGUMENT, "rows, window and slots must be nonzero");
   if ((uint64_t)position + rows > (1u << 24)) return refuse(FZ_ERR_ARGUMENT, "position past 2^24");
   const uint64_t keys = (uint64_t)window < (uint64_t)position + rows ? window : (uint64_t)position + rows;
@@ -61,22 +96,35 @@ extern "C" fz_status fz_attention_static(const float* q, const void* key_cache, 
   if ((uint64_t)rows * kv_heads > kStaticCounters)
     return refuse(FZ_ERR_ARGUMENT, "rows x kv_heads exceeds FZ_ATTENTION_STATIC_MAX_COUNTERS");
 
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess || device < 0 || device >= 64) return refuse(FZ_ERR_CUDA, "cudaGetDevice failed");
+  // The array's address in the current context: looked up on the first call
+  // in that context (cudaGetSymbolAddress also makes the runtime's context
+  // current on a thread that has none), then cached under the context's ID.
+  cudaError_t e = cudaSuccess;
+  unsigned long long ctx = 0;
+  if (!current_context_id(ctx)) {
+    // No context is current on this thread yet: a runtime call makes the
+    // current device's primary context current.
+    void* p = nullptr;
+    (void)cudaGetSymbolAddress(&p, g_scratch);
+    (void)cudaGetLastError();
+    if (!current_context_id(ctx)) return refuse(FZ_ERR_CUDA, "cannot identify the current CUDA context");
+  }
   StaticScratch* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_address[device]) {
+    for (const ContextAddress& c : g_address)
+      if (c.address && c.context_id == ctx) scratch = c.address;
+    if (!scratch) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_scratch);
       if (e != cudaSuccess || !p) {
         (void)cudaGetLastError();
         return refuse(FZ_ERR_CUDA, "cudaGetSymbolAddress of the static attention scratch failed");
       }
-      g_address[device] = static_cast<StaticScratch*>(p);
+      scratch = static_cast<StaticScratch*>(p);
+      g_address[g_next] = ContextAddress{ctx, scratch};
+      g_next = (g_next + 1) % kContexts;
     }
-    scratch = g_address[device];
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // The split counters must start at zero; the previous call left them at

@@ -1025,8 +1025,9 @@ fz_status fz_model_index_check(const void* head, uint64_t head_bytes, uint64_t f
   }
   if (e != fz::GgufError::Ok) return fail(FZ_ERR_INDEX, msg);
   uint64_t end = 0;
-  for (auto& t : m.index.tensors) end = std::max(end, t.offset + t.bytes);
-  if (m.index.data_offset + end > file_bytes) return fail(FZ_ERR_INDEX, "tensor data runs past the end of the file");
+  for (auto& t : m.index.tensors) end = std::max(end, t.offset + t.bytes);   // (the parser refuses wraps)
+  if (end > file_bytes || m.index.data_offset > file_bytes - end)
+    return fail(FZ_ERR_INDEX, "tensor data runs past the end of the file");
   fz_status st;
   if ((st = describe(m))) return st;
   const Shape& s = m.shape;
@@ -1054,8 +1055,9 @@ fz_status fz_model_load_begin(fz_device* dev, const void* head, uint64_t head_by
   }
   if (e != fz::GgufError::Ok) return fail(FZ_ERR_INDEX, msg);
   uint64_t end = 0;
-  for (auto& t : m->index.tensors) end = std::max(end, t.offset + t.bytes);
-  if (m->index.data_offset + end > file_bytes) return fail(FZ_ERR_INDEX, "tensor data runs past the end of the file");
+  for (auto& t : m->index.tensors) end = std::max(end, t.offset + t.bytes);   // (the parser refuses wraps)
+  if (end > file_bytes || m->index.data_offset > file_bytes - end)
+    return fail(FZ_ERR_INDEX, "tensor data runs past the end of the file");
   fz_status st;
   if ((st = describe(*m))) return st;
   m->staging_bytes = end;
@@ -1771,7 +1773,10 @@ fz_status fz_attention(const float* q, const void* key_cache, const void* value_
                        float* partial_o, float* partial_ml, uint32_t* counters, float* out, void* stream) {
   if (!q || !key_cache || !value_cache || !out) return fail(FZ_ERR_ARGUMENT, "null pointer");
   if (head_dim != 256) return fail(FZ_ERR_NOT_SUPPORTED, "head dimension other than 256");
-  if (kv_heads == 0 || heads % kv_heads || heads / kv_heads > 8) return fail(FZ_ERR_ARGUMENT, "heads per KV head 1..8");
+  if (kv_heads == 0 || heads % kv_heads) return fail(FZ_ERR_ARGUMENT, "heads must be a multiple of kv_heads");
+  const uint32_t group = heads / kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8)
+    return fail(FZ_ERR_ARGUMENT, "heads per KV head must be 1, 2, 4 or 8");
   if (rows == 0 || window == 0 || slots == 0) return fail(FZ_ERR_ARGUMENT, "rows, window and slots must be nonzero");
   if ((uint64_t)position + rows > (1u << 24)) return fail(FZ_ERR_ARGUMENT, "position past 2^24");
   const uint32_t splits = fz_attention_splits(window, position, rows);

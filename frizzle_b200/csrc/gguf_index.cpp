@@ -251,6 +251,13 @@ GgufError parse_gguf_index(const uint8_t* bytes, uint64_t n, GgufIndex& out, uin
       return GgufError::Malformed;
     }
     t.bytes = t.elements / be * bb;
+    // The offset comes from the file: its end must not wrap past 2^64, or
+    // every later bound (data in the file, no overlap) would pass on the
+    // wrapped value.
+    if (t.offset > UINT64_MAX - t.bytes) {
+      message = "tensor " + t.name + " offset is out of range";
+      return GgufError::Malformed;
+    }
     if (out.by_name.count(t.name)) {
       message = "duplicate tensor " + t.name;
       return GgufError::Duplicate;

@@ -56,7 +56,8 @@ typedef struct fz_batch fz_batch;
  * activation capture of each sequence's last row. */
 typedef struct fz_step {
   uint32_t position;      /* the first token's position in the context */
-  uint32_t tokens;        /* tokens a sequence this step, 1 .. 16 */
+  uint32_t tokens;        /* tokens a sequence this step: 1 .. 65536 / sequences (the reference takes
+                             1 .. 512, interface.h:165; a fed step is 1) */
   uint32_t logits;        /* 1: the last row's logits, selection and draw */
   uint32_t fed;           /* 1: the one token is each sequence's last draw, read on the device */
   uint32_t seed[2];       /* the draw's seed, low word first */
@@ -341,7 +342,8 @@ fz_status fz_split_f16(const float *x, size_t n, void *hi, void *lo, void *strea
  * partials in caller scratch: partial_o rows x heads x splits x 256 floats,
  * partial_ml rows x heads x splits x 2 floats, counters rows x kv_heads words
  * that start at zero (the kernel leaves them zero), with
- * splits = ceil(min(window, position + rows) / 512). */
+ * splits = ceil(min(window, position + rows) / 512).  heads / kv_heads must
+ * be 1, 2, 4 or 8 (FZ_ERR_ARGUMENT otherwise). */
 fz_status fz_attention(const float *q, const void *key_cache, const void *value_cache, uint32_t slots,
                        uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t window, uint32_t position,
                        uint32_t rows, float *partial_o, float *partial_ml, uint32_t *counters, float *out,
@@ -357,11 +359,14 @@ uint32_t fz_attention_splits(uint32_t window, uint32_t position, uint32_t rows);
  * device that loads it, until the process exits: 2 MiB + 16 KiB + 512 B.
  * Limits: rows x heads x key splits <= FZ_ATTENTION_STATIC_MAX_PARTIALS and
  * rows x kv_heads <= FZ_ATTENTION_STATIC_MAX_COUNTERS; larger calls are
- * refused with FZ_ERR_ARGUMENT.  It calls no cudaMalloc or cudaFree: the
- * first call on a device looks up the array's device address there
- * (cudaGetSymbolAddress), so make that first call before any stream capture.
- * Every call shares the one array and clears its split counters before the
- * launch; calls whose launches overlap on the GPU race on the scratch. */
+ * refused with FZ_ERR_ARGUMENT, as are heads per KV head other than 1, 2, 4
+ * or 8.  It calls no cudaMalloc or cudaFree: the first call in a CUDA
+ * context looks up the array's device address in that context
+ * (cudaGetSymbolAddress) and keeps it under the context's ID, so make that
+ * first call before any stream capture, and again first after
+ * cudaDeviceReset or when a different context is made current.  Every call
+ * shares the one array and clears its split counters before the launch;
+ * calls whose launches overlap on the GPU race on the scratch. */
 #define FZ_ATTENTION_STATIC_MAX_PARTIALS 2048u
 #define FZ_ATTENTION_STATIC_MAX_COUNTERS 128u
 fz_status fz_attention_static(const float *q, const void *key_cache, const void *value_cache, uint32_t slots,

@@ -100,7 +100,13 @@ def cases():
 
 def main():
     if not os.path.exists(LIB):
-        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref"], check=True)
+        # The checkout's root: FRIZZLE_REFERENCE, or the path BASELINE.json records.
+        sys.path.insert(0, ROOT)
+        import __graft_entry__
+        ref = __graft_entry__.reference_checkout()
+        if not ref:
+            sys.exit("make_golden.py needs the reference checkout (set FRIZZLE_REFERENCE)")
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", f"REF={ref}"], check=True)
     lib = C.CDLL(LIB)
     lib.ref_edit_check.restype = C.c_int
     lib.ref_edit_check.argtypes = [C.c_void_p, C.c_size_t, C.c_uint32, C.c_uint32, C.POINTER(C.c_size_t),

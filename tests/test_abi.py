@@ -121,6 +121,20 @@ def test_index_refuses_duplicates_and_bad_alignment(tmp_path):
     assert _index_check(bad, len(bad))[0] == 3
 
 
+def test_index_refuses_offset_that_wraps(tmp_path):
+    # Tensor b's offset rewritten to 2^64 - 64: offset + 128 bytes wraps to 64, which would pass the
+    # data-in-file and overlap checks if the parser let it through.  Refused as an index error.
+    data = _write(tmp_path, tensors=[("a", (32,), gguf.TYPE_F32), ("b", (32,), gguf.TYPE_F32)])
+    info_b = gguf._pack_string("b") + struct.pack("<IQ", 1, 32)
+    at = data.index(info_b + struct.pack("<IQ", gguf.TYPE_F32, 128))
+    field = at + len(info_b) + 4
+    bad = data[:field] + struct.pack("<Q", (1 << 64) - 64) + data[field + 8:]
+    st, msg, _ = _index_check(bad, len(bad))
+    assert st == 3 and "out of range" in msg, msg
+    # The same file untouched is well formed (refused only for missing layers).
+    assert _index_check(data, len(data))[0] == 4
+
+
 def test_index_refuses_softcapping(tmp_path):
     def cap(w):
         w.add("gemma3.final_logit_softcapping", gguf.F32, 30.0)

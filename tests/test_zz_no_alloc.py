@@ -60,13 +60,26 @@ def _assert_close(got, want):
 
 
 def test_static_scratch_matches_caller_scratch_twice_in_a_row():
-    # Two calls back to back, each spanning several 512-key splits, so the
-    # second reads scratch the first left behind and must not be affected by it.
+    """Two calls back to back, each spanning several 512-key splits, so the
+    second reads scratch the first left behind and must not be affected by it.
+
+    The entry point also clears the shared split counters before each launch.
+    A finished launch leaves them at zero already (its last split resets
+    them), and no call through the C ABI can leave them otherwise, so this
+    test cannot show that the clear itself works: it guards only a launch
+    that never finished."""
     got, want, splits = _both(rows=2, position=1500, window=32768, slots=4096, seed=1)
     assert splits == 3
     _assert_close(got, want)
     got, want, splits = _both(rows=4, position=2500, window=32768, slots=4096, seed=2)
     assert splits == 5
+    _assert_close(got, want)
+
+
+def test_static_scratch_single_split():
+    # Every row's keys fit one 512-key split: no partials, no counters.
+    got, want, splits = _both(rows=3, position=200, window=512, slots=1024, seed=3)
+    assert splits == 1
     _assert_close(got, want)
 
 
@@ -81,3 +94,24 @@ def test_static_scratch_refuses_calls_past_its_limit():
                                  16, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert st == 1
     assert b"FZ_ATTENTION_STATIC_MAX_PARTIALS" in lib.fz_last_error()
+
+
+def test_static_scratch_refuses_counters_and_group_sizes_past_its_limits():
+    torch = _torch()
+    lib = _native.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    rows = 129   # 129 x 1 KV head split counters, above the 128 the array holds (partials: 129 x 4 x 1)
+    q = torch.zeros((rows, HEADS, D), dtype=torch.float32, device="cuda")
+    cache = torch.zeros((1024, KV, D), dtype=torch.int16, device="cuda")
+    out = torch.zeros_like(q)
+    st = lib.fz_attention_static(q.data_ptr(), cache.data_ptr(), cache.data_ptr(), 1024, HEADS, KV, D, 256, 0, rows,
+                                 out.data_ptr(), stream)
+    assert st == 1
+    assert b"FZ_ATTENTION_STATIC_MAX_COUNTERS" in lib.fz_last_error()
+    # Three query heads a KV head: no kernel takes that grouping, refused before any launch.
+    q3 = torch.zeros((1, 3, D), dtype=torch.float32, device="cuda")
+    st = lib.fz_attention_static(q3.data_ptr(), cache.data_ptr(), cache.data_ptr(), 1024, 3, 1, D, 256, 10, 1,
+                                 q3.data_ptr(), stream)
+    assert st == 1
+    assert b"1, 2, 4 or 8" in lib.fz_last_error()
+    torch.cuda.synchronize()
