@@ -694,6 +694,148 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
   cbar();
 }
 
+// The norm launch of one row (M = 1), straight into the B fragments of the
+// whole row: X plus the post-normed block output (y: the sum of ny K-slice
+// partials, in slice order), written back by CTA 0 with the captures; then
+// X's RMS norm times the gain, split into f16 part and remainder.  Thread i
+// holds fragment items i and i + 256 (item (block, half, tq): columns c, c +
+// 1, c + 16, c + 17 with c = 32 block + 8 half + 2 tq, the layout's column
+// permutation), with every load of both items in flight at once; each sum of
+// squares is a warp shuffle reduction and one exchange of the 8 warps'
+// sums through shared memory (summed in warp order by every thread).  The
+// sums' order is not the reference's 256-invocation tree: the difference is
+// a few f32 roundings of the statistics, far inside the 1e-3 bar.
+constexpr uint32_t kNormMaxSlices = kDecodeDownSlices > kDecodeOSlices ? kDecodeDownSlices : kDecodeOSlices;
+__device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, const float* y, uint32_t ny, float* xout,
+                                      uint32_t cx, uint32_t cy) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int items = (int)a.hidden / 4;
+  const float wf = (float)a.hidden;
+  const float* gs = smem_f(a.lay.gains);   // gain [hidden], then the post gain [hidden]
+  float* sums = smem_f(a.lay.part);        // [2][kCW] warp sums
+  uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
+  float x[2][4], yv[2][4];
+  int col[2];
+  bool live[2];
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    const int i = tid + u * kCT;
+    live[u] = i < items;
+    col[u] = 32 * (i >> 3) + 8 * ((i >> 2) & 1) + 2 * (i & 3);
+#pragma unroll
+    for (int e = 0; e < 4; e++) x[u][e] = yv[u][e] = 0.f;
+  }
+  // Every load first: X, then the y slices.
+  float2 xa[2], xb[2], ya[2][kNormMaxSlices], yb[2][kNormMaxSlices];
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    xa[u] = xb[u] = make_float2(0.f, 0.f);
+    if (live[u]) {
+      xa[u] = __ldcg(reinterpret_cast<const float2*>(xin + col[u]));
+      xb[u] = __ldcg(reinterpret_cast<const float2*>(xin + col[u] + 16));
+    }
+#pragma unroll
+    for (uint32_t j = 0; j < kNormMaxSlices; j++) {
+      ya[u][j] = yb[u][j] = make_float2(0.f, 0.f);
+      if (y && j < ny && live[u]) {
+        const float* yj = y + (size_t)j * a.hidden + col[u];
+        ya[u][j] = __ldcg(reinterpret_cast<const float2*>(yj));
+        yb[u][j] = __ldcg(reinterpret_cast<const float2*>(yj + 16));
+      }
+    }
+  }
+  // The gains' copies (issued before the phase's wait) land before the
+  // first barrier below, which makes them visible to every thread.
+  cp_async_wait();
+  float ry = 0.f;
+  if (!y) cbar();
+  if (y) {
+    float p = 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      float2 sa = ya[u][0], sb = yb[u][0];
+#pragma unroll
+      for (uint32_t j = 1; j < kNormMaxSlices; j++)
+        if (j < ny) {
+          sa = make_float2(add(sa.x, ya[u][j].x), add(sa.y, ya[u][j].y));
+          sb = make_float2(add(sb.x, yb[u][j].x), add(sb.y, yb[u][j].y));
+        }
+      yv[u][0] = sa.x;
+      yv[u][1] = sa.y;
+      yv[u][2] = sb.x;
+      yv[u][3] = sb.y;
+#pragma unroll
+      for (int e = 0; e < 4; e++) p = __fmaf_rn(yv[u][e], yv[u][e], p);
+    }
+    p = warp_sum(p);
+    if (lane == 0) sums[warp] = p;
+    cbar();
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCW; w++) s = add(s, sums[w]);
+    ry = inverse_sqrt(add(__fdiv_rn(s, wf), a.eps));
+  }
+  const bool writer = blockIdx.x == 0;
+  float* capbase = writer && a.capture ? a.capture : nullptr;
+  float* xc = capbase && (cx & 3) ? capbase + cap_offset(a, cx) : nullptr;
+  float* yc = capbase && (cy & 3) ? capbase + cap_offset(a, cy) : nullptr;
+  float p = 0.f;
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    x[u][0] = xa[u].x;
+    x[u][1] = xa[u].y;
+    x[u][2] = xb[u].x;
+    x[u][3] = xb[u].y;
+    if (!live[u]) continue;
+    const int cc[4] = {col[u], col[u] + 1, col[u] + 16, col[u] + 17};
+    if (y) {
+      float yy[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        yy[e] = mul(mul(yv[u][e], ry), gs[a.hidden + cc[e]]);
+        x[u][e] = add(x[u][e], yy[e]);
+      }
+      if (yc) {
+        *reinterpret_cast<float2*>(yc + cc[0]) = make_float2(yy[0], yy[1]);
+        *reinterpret_cast<float2*>(yc + cc[2]) = make_float2(yy[2], yy[3]);
+      }
+    }
+    if (writer && xout) {
+      *reinterpret_cast<float2*>(xout + cc[0]) = make_float2(x[u][0], x[u][1]);
+      *reinterpret_cast<float2*>(xout + cc[2]) = make_float2(x[u][2], x[u][3]);
+    }
+    if (xc) {
+      *reinterpret_cast<float2*>(xc + cc[0]) = make_float2(x[u][0], x[u][1]);
+      *reinterpret_cast<float2*>(xc + cc[2]) = make_float2(x[u][2], x[u][3]);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; e++) p = __fmaf_rn(x[u][e], x[u][e], p);
+  }
+  p = warp_sum(p);
+  if (lane == 0) sums[kCW + warp] = p;
+  cbar();
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCW; w++) s = add(s, sums[kCW + w]);
+  const float rx = inverse_sqrt(add(__fdiv_rn(s, wf), a.eps));
+  // The fragments of the row quad: row 0 the normed row, rows 1..3 zero.
+  // Item i's slot of row r: uint4 (i / 4) * 16 + (i % 4) * 4 + r (part, then remainder).
+#pragma unroll
+  for (int u = 0; u < 2; u++) {
+    if (!live[u]) continue;
+    const int i = tid + u * kCT;
+    const int cc[4] = {col[u], col[u] + 1, col[u] + 16, col[u] + 17};
+    __half hi[4], lo[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) split_hi_lo(mul(mul(x[u][e], rx), gs[cc[e]]), hi[e], lo[e]);
+    const uint2 h = pack4(hi[0], hi[1], hi[2], hi[3]), l = pack4(lo[0], lo[1], lo[2], lo[3]);
+    uint4* dst = xf + (i >> 2) * 16 + (i & 3) * 4;
+    dst[0] = make_uint4(h.x, h.y, l.x, l.y);
+    dst[1] = dst[2] = dst[3] = make_uint4(0u, 0u, 0u, 0u);
+  }
+  cbar();
+}
+
 // B fragments of the rows (src [M][K]) for blocks [kb0, kb0 + nkb); rows
 // past M are zero.  kGlobal rows were written by other CTAs this launch.  A
 // thread takes two items at a time, all their loads in flight together.
@@ -1134,20 +1276,29 @@ struct Attn {
         const int nt = warp & 3, kh = warp >> 2;
         const uint16_t* qrow = qh() + g * QS + 2 * t + 128 * kh;
         const uint32_t key = 8 * nt + (lane & 7), d0 = 128 * kh + 8 * (lane >> 3);
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        // Four independent k-pair chains (their MMAs issued side by side,
+        // so the latencies overlap), summed at the end.
+        uint32_t af[4][2][4], kr[4][4];
+        const float zero[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int kp = 0; kp < 4; kp++) {
-          const uint32_t af0[4] = {*reinterpret_cast<const uint32_t*>(qrow + 32 * kp), 0u,
-                                   *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 8), 0u};
-          const uint32_t af1[4] = {*reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 16), 0u,
-                                   *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 24), 0u};
-          uint32_t r0, r1, r2, r3;
+          af[kp][0][0] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp);
+          af[kp][0][2] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 8);
+          af[kp][1][0] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 16);
+          af[kp][1][2] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 24);
+          af[kp][0][1] = af[kp][0][3] = af[kp][1][1] = af[kp][1][3] = 0u;
           asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                       : "=r"(kr[kp][0]), "=r"(kr[kp][1]), "=r"(kr[kp][2]), "=r"(kr[kp][3])
                        : "r"(su32(ks(b) + at(key, d0 + 32 * kp))));
-          mma16816(d, af0, make_uint2(r0, r1), d);
-          mma16816(d, af1, make_uint2(r2, r3), d);
         }
+        float dk[4][4];
+#pragma unroll
+        for (int kp = 0; kp < 4; kp++) mma16816(dk[kp], af[kp][0], make_uint2(kr[kp][0], kr[kp][1]), zero);
+#pragma unroll
+        for (int kp = 0; kp < 4; kp++) mma16816(dk[kp], af[kp][1], make_uint2(kr[kp][2], kr[kp][3]), dk[kp]);
+        float d[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) d[e] = add(add(dk[0][e], dk[1][e]), add(dk[2][e], dk[3][e]));
         // Row g < GH: head g's part; row g + GH its remainder, GH lanes-of-4 down.
         const float r0 = __shfl_down_sync(0xffffffffu, d[0], 4 * GH);
         const float r1 = __shfl_down_sync(0xffffffffu, d[1], 4 * GH);
@@ -1186,18 +1337,27 @@ struct Attn {
           af[k][2] = *reinterpret_cast<const uint32_t*>(ph() + g * PS + 16 * k + 8 + 2 * t);
           af[k][3] = 0u;
         }
-#pragma unroll 2
+        // The four n-tiles' first MMAs side by side, then their second ones.
+        uint32_t vr[4][4];
+        float d[4][4];
+#pragma unroll
         for (int i = 0; i < 4; i++) {
           const uint32_t nt = 4 * warp + i;
-          uint32_t r0, r1, r2, r3;
           asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                       : "=r"(vr[i][0]), "=r"(vr[i][1]), "=r"(vr[i][2]), "=r"(vr[i][3])
                        : "r"(su32(vs(b) + at((uint32_t)lane, nt * 8))));
-          float d[4] = {mul(acc[i][0], corr), mul(acc[i][1], corr), 0.f, 0.f};
-          mma16816(d, af[0], make_uint2(r0, r1), d);
-          mma16816(d, af[1], make_uint2(r2, r3), d);
-          acc[i][0] = d[0];
-          acc[i][1] = d[1];
+          d[i][0] = mul(acc[i][0], corr);
+          d[i][1] = mul(acc[i][1], corr);
+          d[i][2] = d[i][3] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) mma16816(d[i], af[0], make_uint2(vr[i][0], vr[i][1]), d[i]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) mma16816(d[i], af[1], make_uint2(vr[i][2], vr[i][3]), d[i]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          acc[i][0] = d[i][0];
+          acc[i][1] = d[i][1];
         }
       }
       // Buffer b is read: its next chunk (after a proxy fence by the threads
@@ -1564,16 +1724,31 @@ struct Consumer {
     pslots = 0;
     ph_kind = kind;
     ph_l = l;
+    // One row: the norm writes the fragments itself (norm_one).
+    const bool one = MQ == 1 && M == 1;
     if (kind == kPhQkv) {
-      norm_rows(a, M, a.hidden_a, l > 0 ? a.y_mlp : nullptr, kDecodeDownSlices, a.hidden_b,
-                cap_slot(l, kCapResidual), l > 0 ? cap_slot(l - 1, kCapMlpAdded) : kCapNone);
-      fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+      const float* y = l > 0 ? a.y_mlp : nullptr;
+      const uint32_t cy = l > 0 ? cap_slot(l - 1, kCapMlpAdded) : kCapNone;
+      if (one) {
+        norm_one(a, a.hidden_a, y, kDecodeDownSlices, a.hidden_b, cap_slot(l, kCapResidual), cy);
+      } else {
+        norm_rows(a, M, a.hidden_a, y, kDecodeDownSlices, a.hidden_b, cap_slot(l, kCapResidual), cy);
+        fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+      }
     } else if (kind == kPhGate) {
-      norm_rows(a, M, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, kCapNone, cap_slot(l, kCapAttnAdded));
-      fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+      if (one) {
+        norm_one(a, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, kCapNone, cap_slot(l, kCapAttnAdded));
+      } else {
+        norm_rows(a, M, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, kCapNone, cap_slot(l, kCapAttnAdded));
+        fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+      }
     } else if (kind == kPhHead) {
-      norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, kCapNone, cap_slot(Ln - 1, kCapMlpAdded));
-      fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+      if (one) {
+        norm_one(a, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, kCapNone, cap_slot(Ln - 1, kCapMlpAdded));
+      } else {
+        norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, kCapNone, cap_slot(Ln - 1, kCapMlpAdded));
+        fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+      }
     } else if (kind == kPhO) {
       attention_fragments<MQ>(a, M, o_splits, kb0, nkb, phase_epoch(serial(), l, kEpAttn));
     } else {
@@ -1586,26 +1761,55 @@ struct Consumer {
   }
 
   // One block pair's products into ac (rows g, g + 8 against X rows 4q + t).
+  // The warp issues in order, so an MMA chained on another waits out that
+  // one's latency: the first k-halves of the pair's two blocks (and row
+  // quads) are issued side by side, then the chained second halves, so that
+  // one latency covers both blocks.  Each block's sum and scaling are made
+  // in the same order as block by block.
   FZ_DEV void bp_dot(uint4 c, uint2 sc, int kb_rel0, float ac[MQ][2]) {
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    float d[2][MQ][4];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      uint32_t af[2][4];
+      dequant_word(h ? c.y : c.x, af[0]);
+      dequant_word(h ? c.w : c.z, af[1]);
+#pragma unroll
+      for (int kbi = 0; kbi < 2; kbi++)
+#pragma unroll
+        for (int q = 0; q < MQ; q++)
+          mma16816(d[kbi][q], af[kbi], xf()[xf_index(kb_rel0 + kbi, h, q, MQ, t, g)], h ? d[kbi][q] : zero);
+    }
 #pragma unroll
     for (int kbi = 0; kbi < 2; kbi++) {
-      uint32_t a0[4], a1[4];
-      dequant_word(kbi ? c.z : c.x, a0);
-      dequant_word(kbi ? c.w : c.y, a1);
       const uint32_t sw = kbi ? sc.y : sc.x;
       const float dg = __half2float(__ushort_as_half((unsigned short)(sw & 0xffffu)));
       const float dg8 = __half2float(__ushort_as_half((unsigned short)(sw >> 16)));
 #pragma unroll
       for (int q = 0; q < MQ; q++) {
-        const uint2 b0 = xf()[xf_index(kb_rel0 + kbi, 0, q, MQ, t, g)];
-        const uint2 b1 = xf()[xf_index(kb_rel0 + kbi, 1, q, MQ, t, g)];
-        float d[4];
-        mma16816(d, a0, b0, zero);
-        mma16816(d, a1, b1, d);
-        ac[q][0] = __fmaf_rn(dg, d[0] + d[1], ac[q][0]);
-        ac[q][1] = __fmaf_rn(dg8, d[2] + d[3], ac[q][1]);
+        ac[q][0] = __fmaf_rn(dg, d[kbi][q][0] + d[kbi][q][1], ac[q][0]);
+        ac[q][1] = __fmaf_rn(dg8, d[kbi][q][2] + d[kbi][q][3], ac[q][1]);
       }
+    }
+  }
+
+  // The warp's block pairs of a tile (w, w + 8, ..., at most four) into
+  // acc[W], two at a time (their loads first, then the products).
+  template <int W>
+  FZ_DEV void tile_math(const uint4* cs, const uint2* ss, uint32_t nb, uint32_t b) {
+#pragma unroll 1
+    for (uint32_t j = warp; j < nb; j += 2 * kCW) {
+      const bool two = j + kCW < nb;
+      const uint4 c0 = cs[j * 32 + lane];
+      const uint2 s0 = ss[j * 8 + g];
+      uint4 c1 = make_uint4(0u, 0u, 0u, 0u);
+      uint2 s1 = make_uint2(0u, 0u);
+      if (two) {
+        c1 = cs[(j + kCW) * 32 + lane];
+        s1 = ss[(j + kCW) * 8 + g];
+      }
+      bp_dot(c0, s0, (int)(2 * (b + j) - kb_base), acc[W]);
+      if (two) bp_dot(c1, s1, (int)(2 * (b + j + kCW) - kb_base), acc[W]);
     }
   }
 
@@ -1624,13 +1828,8 @@ struct Consumer {
       const uint4* cs = codes() + (size_t)slot * (kSlotCodes / 16);
       const uint2* ss = scales() + (size_t)slot * (kSlotScales / 8);
       // (two calls, so that acc stays in registers)
-      if (which) {
-#pragma unroll 1
-        for (uint32_t j = warp; j < nb; j += kCW) bp_dot(cs[j * 32 + lane], ss[j * 8 + g], (int)(2 * (b + j) - kb_base), acc[1]);
-      } else {
-#pragma unroll 1
-        for (uint32_t j = warp; j < nb; j += kCW) bp_dot(cs[j * 32 + lane], ss[j * 8 + g], (int)(2 * (b + j) - kb_base), acc[0]);
-      }
+      if (which) tile_math<1>(cs, ss, nb, b);
+      else tile_math<0>(cs, ss, nb, b);
     }
     __syncwarp();
     if (lane == 0) mb_arrive(empty() + slot, 1u);
