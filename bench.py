@@ -104,24 +104,41 @@ class Clocks:
 
 # ------------------------------------------------------------------ CPU legs
 
-def cpu_decode_sample(path, decode_tokens=2, prefill=4):
-    """The oracle's decode tokens/s on this host's cores: a `prefill`-token prompt,
-    then `decode_tokens` timed decode steps of the full model."""
+def host_threads():
+    """The host cores this process may run on (not OMP_NUM_THREADS, which a
+    launcher such as torchrun sets to 1)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
+def cpu_decode_sample(path, decode_tokens=2, prefill=4, warmup=0):
+    """The oracle's decode tokens/s on this host's cores (all of them): a
+    `prefill`-token prompt, `warmup` untimed decode steps, then
+    `decode_tokens` timed decode steps of the full model."""
     import numpy as np
     import oracle
     from frizzle_b200 import synth
-    orc = oracle.OracleModel(path, context=256)
+    oracle.lib().oracle_set_threads(host_threads())
+    orc = oracle.OracleModel(path, context=max(256, prefill + warmup + decode_tokens + 1))
     ids = np.random.default_rng(0).integers(2, synth.GEMMA3_1B.vocab, size=prefill).astype(np.uint32)
     logits, _ = orc.step(0, ids, logits=True)
+    pos = prefill
+    for _ in range(warmup):
+        tok = int(np.argmax(logits))
+        logits, _ = orc.step(pos, [tok], logits=True)
+        pos += 1
     t0 = time.perf_counter()
     for i in range(decode_tokens):
         tok = int(np.argmax(logits))
-        logits, _ = orc.step(prefill + i, [tok], logits=True)
+        logits, _ = orc.step(pos + i, [tok], logits=True)
     dt = time.perf_counter() - t0
     threads = oracle.lib().oracle_threads()
     orc.close()
-    return decode_tokens / dt, threads, f"{decode_tokens} greedy decode tokens of the 26-layer model after a " \
-                                        f"{prefill}-token prompt, oracle port on {threads} host threads"
+    return decode_tokens / dt, threads, f"{decode_tokens} timed greedy decode tokens of the 26-layer model after a " \
+                                        f"{prefill}-token prompt and {warmup} untimed ones, oracle port on " \
+                                        f"{threads} host threads"
 
 
 def run_reference(args):
@@ -131,9 +148,9 @@ def run_reference(args):
     from frizzle_b200 import synth
     path = synth.model_path(synth.GEMMA3_1B, 0)
     steps, warmup = max(1, args.steps), max(0, args.warmup)
-    # Bounded: the whole arm is a handful of CPU decode tokens.
-    decode = min(steps, 3)
-    value, threads, sample = cpu_decode_sample(path, decode_tokens=decode)
+    # Config 1's 32-token prompt, the warm-up decode tokens untimed, then every
+    # claimed step timed (about 50 ms a token on 16 host threads).
+    value, threads, sample = cpu_decode_sample(path, decode_tokens=steps, prefill=PROMPT, warmup=warmup)
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
             "warmup": warmup, "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init Q4_0 weights, seeded ids)",
@@ -309,14 +326,102 @@ def gemm_roofline(torch, lib, native, m=4096, reps=10):
     return flops, out
 
 
-def traffic_from_profile():
-    p = os.path.join(ROOT, "profiles", "head_matvec_traffic.json")
+def traffic_from_profile(name):
+    """DRAM bytes (read + write) a launch of the kernel moved under ncu, from a
+    committed one-launch summary (profiles/<name>), or None."""
+    p = os.path.join(ROOT, "profiles", name)
     if os.path.exists(p):
         try:
             return json.load(open(p)).get("dram_bytes_per_launch")
         except (OSError, ValueError):
             return None
     return None
+
+
+def kv_bytes(shape, positions):
+    """Key and value bytes the decode attention reads over one-token steps at
+    `positions`: each layer reads the keys it attends (the window's for the
+    sliding-window layers, every earlier one for the global layers), f16 keys
+    and values of its KV heads."""
+    per_key = 2 * shape.kv_heads * shape.head_dim * 2
+    total = 0
+    for p in positions:
+        for layer in range(shape.layers):
+            glob = layer % shape.pattern == shape.pattern - 1
+            total += (p + 1 if glob else min(p + 1, shape.window)) * per_key
+    return total
+
+
+C2_SHAPES = (("q", 1152, 1024), ("k", 1152, 256), ("v", 1152, 256), ("o", 1024, 1152), ("gate_up", 1152, 6912),
+             ("down", 6912, 1152), ("head", 1152, 262144))
+
+
+def c2_sweep(torch, lib, native, reps=5):
+    """the isolated Q4_0 product over Gemma-3-1B's linear
+    shapes (K -> N) at M = 1, 8, 64 and 512 rows: codes uniform in [0, 15],
+    fp16 scales |N(0, 0.005)|, X ~ N(0, 1) f32, seeded.  M <= 16 runs the
+    skinny matvec (fz_q4_0_matvec), more rows the tcgen05 GEMM on the Q4_0
+    codes (fz_q4_0_gemm, f32-level: X split into f16 part and remainder by
+    fz_split_f16, timed with it).  L2 is flushed (a 256 MiB write) before every
+    timed launch, each launch timed alone with CUDA events, median of `reps`.
+    The roofline is whichever bound is slower: algorithmic bytes N K 9/16 +
+    4 M K + 4 M N at the measured HBM rate, or 2 M N K flops at the measured
+    bf16 rate; frac = that time / the measured time."""
+    import numpy as np
+    from frizzle_b200 import synth
+    hbm, bf16, which = peaks()
+    s = torch.cuda.current_stream().cuda_stream
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rows = []
+    for name, k, n in C2_SHAPES:
+        src = torch.from_numpy(synth.random_q4_0(n, k, seed=2)).cuda()
+        codes = torch.empty(lib.fz_q4_0_codes_bytes(n, k), dtype=torch.uint8, device="cuda")
+        scales = torch.empty(lib.fz_q4_0_scales_bytes(n, k), dtype=torch.uint8, device="cuda")
+        native.check(lib.fz_q4_0_repack(src.data_ptr(), n, k, codes.data_ptr(), scales.data_ptr(), s))
+        del src
+        for m in (1, 8, 64, 512):
+            g = torch.Generator(device="cuda").manual_seed(m)
+            x = torch.randn(m, k, device="cuda", generator=g)
+            y = torch.empty(m, n, device="cuda")
+            xh = torch.empty(m, k, dtype=torch.float16, device="cuda")
+            xl = torch.empty(m, k, dtype=torch.float16, device="cuda")
+
+            def run():
+                if m <= 16:
+                    native.check(lib.fz_q4_0_matvec(codes.data_ptr(), scales.data_ptr(), n, k, x.data_ptr(), m,
+                                                    y.data_ptr(), s))
+                else:
+                    native.check(lib.fz_split_f16(x.data_ptr(), m * k, xh.data_ptr(), xl.data_ptr(), s))
+                    native.check(lib.fz_q4_0_gemm(codes.data_ptr(), scales.data_ptr(), n, k, xh.data_ptr(),
+                                                  xl.data_ptr(), 1, m, y.data_ptr(), err.data_ptr(), s))
+            run()
+            times = []
+            for _ in range(reps):
+                flush.zero_()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                run()
+                b.record()
+                torch.cuda.synchronize()
+                times.append(a.elapsed_time(b) / 1000.0)
+            assert int(err.item()) == 0
+            t = float(np.median(times))
+            bytes_ = n * k * 9 // 16 + 4 * m * k + 4 * m * n
+            flops = 2.0 * m * n * k
+            t_hbm, t_tc = bytes_ / (hbm * 1e9), flops / (bf16 * 1e12)
+            rows.append({"shape": name, "k": k, "n": n, "m": m, "us": t * 1e6,
+                         "kernel": "fz_q4_0_matvec" if m <= 16 else "fz_split_f16 + fz_q4_0_gemm (tcgen05, f32-level)",
+                         "algorithmic_bytes": bytes_, "flops": flops, "achieved_gbs": bytes_ / t / 1e9,
+                         "achieved_tflops": flops / t / 1e12, "bound": "hbm" if t_hbm >= t_tc else "tensor",
+                         "frac": max(t_hbm, t_tc) / t})
+            del x, y, xh, xl
+        del codes, scales
+    del flush
+    torch.cuda.empty_cache()
+    return {"workload": "BASELINE config 2: isolated Q4_0 products, Gemma-3-1B's linear shapes x M in "
+                        "{1, 8, 64, 512}; L2 flushed before each timed launch", "peak_hbm_gbs": hbm,
+            "peak_bf16_tflops": bf16, "peak_source": which, "points": rows}
 
 
 def run_ours(args):
@@ -409,26 +514,25 @@ def run_ours(args):
         pos += K
     dec_s = ev[2].elapsed_time(ev[3]) / 1000.0
     e2e_s = ev[4].elapsed_time(ev[5]) / 1000.0
-    # The persistent decode kernel's own duration, from its device timestamps (first phase start
-    # to last phase end, fz_batch_trace), over a few traced steps after the timed region.
-    decode_kernel_us = None
-    if rank == 0:
-        import ctypes as C
-        engine.check(lib.fz_batch_trace(batch.handle, 1))
-        ctas, events = C.c_uint32(), C.c_uint32()
-        engine.check(lib.fz_batch_read_trace(batch.handle, None, 0, C.byref(ctas), C.byref(events)))
-        spans = []
-        for i in range(4):
-            batch.step(pos + i, fed=True, tokens=1, logits=True)
-            batch.wait()
-            buf = np.zeros(ctas.value * events.value, dtype=np.uint64)
-            engine.check(lib.fz_batch_read_trace(batch.handle, buf.ctypes.data, buf.size, None, None))
-            body = buf.reshape(ctas.value, events.value)[:, :synth.GEMMA3_1B.layers * 6 * 5].astype(np.float64)
-            body[body == 0] = np.nan
-            spans.append((np.nanmax(body) - np.nanmin(body)) / 1000.0)
-        engine.check(lib.fz_batch_trace(batch.handle, 0))
-        pos += 4
-        decode_kernel_us = float(np.median(spans[1:]))
+    # The dominant kernel, the persistent decode step, untraced: one-token steps that ask for no logits run
+    # only the embedding gather and the decode kernel (no head, no selection); K of them back to back,
+    # CUDA events on the device stream around them.  Its algorithmic bytes: the 26 layers' Q4_0 weights and
+    # norm gains plus the keys and values the steps' attention reads (1 KiB a key a layer).
+    dk_ids = np.random.default_rng([rank, 7]).integers(2, synth.GEMMA3_1B.vocab, size=K + 3).astype(np.uint32)
+    for i in range(3):
+        batch.step(pos + i, dk_ids[i:i + 1], tokens=1, logits=False)
+    pos += 3
+    dk = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    with torch.cuda.stream(stream):
+        dk[0].record()
+    for i in range(K):
+        batch.step(pos + i, dk_ids[3 + i:4 + i], tokens=1, logits=False)
+    with torch.cuda.stream(stream):
+        dk[1].record()
+    torch.cuda.synchronize()
+    dk_secs = dk[0].elapsed_time(dk[1]) / 1000.0 / K
+    dk_bytes = LAYER_BYTES + kv_bytes(synth.GEMMA3_1B, range(pos, pos + K)) / K
+    pos += K
     # The capture step and prefix reuse (rank 0): config 1's 32-token prompt as one step with and without
     # the per-layer capture (weights, statistics and 25 readouts through the head), and a second turn
     # that extends a 1024-token first turn's conversation by 16 tokens, prefilled fresh or after the cache
@@ -591,17 +695,21 @@ def run_ours(args):
                 "prefill_tokens_per_s": world * PROMPT / prefill_s,
                 "decode_step_hbm_gbs": DECODE_BYTES / (dec_s / K) / 1e9,
                 "decode_step_hbm_frac": DECODE_BYTES / (dec_s / K) / 1e9 / hbm,
-                "roofline": {"bound": "hbm", "kernel": "q4_0 head matvec 262144 x 1152, M=1",
-                             "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                             "peak_source": which, "algorithmic_bytes": head_bytes,
-                             "launch_us": head_secs * 1e6, "traffic": traffic_from_profile()},
-                "decode_kernel": {
-                    "kernel": "persistent decode step (26 layers), the step's dominant launch by time",
-                    "us": decode_kernel_us, "algorithmic_bytes": LAYER_BYTES,
-                    "achieved_gbs": LAYER_BYTES / (decode_kernel_us * 1e-6) / 1e9 if decode_kernel_us else None,
-                    "frac": LAYER_BYTES / (decode_kernel_us * 1e-6) / 1e9 / hbm if decode_kernel_us else None,
-                    "bound": "hbm (latency-bound in practice: 130 dependent phases)",
-                    "timing": "device global timer inside the kernel (fz_batch_trace), median of 3 steps"},
+                "roofline": {"bound": "hbm", "kernel": "decode_kernel<1>: the persistent decode step, 26 layers "
+                                                        "(the step's dominant launch by time)",
+                             "achieved": dk_bytes / dk_secs / 1e9, "peak": hbm, "unit": "GB/s",
+                             "frac": dk_bytes / dk_secs / 1e9 / hbm, "peak_source": which,
+                             "algorithmic_bytes": dk_bytes, "launch_us": dk_secs * 1e6,
+                             "traffic": traffic_from_profile("decode_kernel_traffic.json"),
+                             "timing": "CUDA events on the device stream around one-token steps without logits "
+                                       "(the embedding gather + the decode kernel), untraced, mean of K steps",
+                             "bytes": "26 layers' Q4_0 weights + norm gains (392,491,008 + 532,480 B) + the keys "
+                                      "and values the steps' attention reads (1 KiB a key a layer)"},
+                "head_roofline": {"bound": "hbm", "kernel": "q4_0 head matvec 262144 x 1152, M=1, timed alone",
+                                  "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                                  "peak_source": which, "algorithmic_bytes": head_bytes,
+                                  "launch_us": head_secs * 1e6,
+                                  "traffic": traffic_from_profile("head_matvec_traffic.json")},
                 "clocks": clocks.summary()}
         if extras:
             line.update(extras)
@@ -625,6 +733,8 @@ def run_ours(args):
         p4k = e0.elapsed_time(e1) / 1000.0
         pre.free()
         line["formats_matvec"] = formats_roofline(torch, lib, _native)
+        if not args.no_c2:
+            line["c2_sweep"] = c2_sweep(torch, lib, _native)
         gflops, gsecs = gemm_roofline(torch, lib, _native)
         _, bf16, _ = peaks()
         line["prefill_4096"] = {"tokens_per_s": 4096 / p4k, "ms": 1000.0 * p4k,
@@ -648,7 +758,7 @@ def run_ours(args):
                     "(one pass), config 1's logits land at 1.1-1.6e-3 relative RMS from the fp32 oracle, above "
                     "the 1e-3 parity bar; tensor_pipe_frac counts the MMAs the tensor pipe runs"}
         if world == 1 and not args.no_cpu_baseline:
-            v, threads, sample = cpu_decode_sample(path)
+            v, threads, sample = cpu_decode_sample(path, decode_tokens=8, prefill=PROMPT, warmup=1)
             line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample}
     batch.free()
     model.free()
@@ -676,6 +786,8 @@ def main():
                     help="run only this many decode steps between cudaProfilerStart/Stop, print nothing")
     ap.add_argument("--no-sweep", action="store_true", help="skip the config-4 steering sweep")
     ap.add_argument("--no-long", action="store_true", help="skip the config-5 long-context run")
+    ap.add_argument("--no-c2", action="store_true", help="skip the config-2 product sweep")
+    ap.add_argument("--c2-only", action="store_true", help="run only the config-2 product sweep and print it")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="run one config-3 4096-token prefill step between cudaProfilerStart/Stop (after a warm-up one)")
     ap.add_argument("--seqs", type=int, default=1, help="sequences a batch in --trace")
@@ -702,6 +814,11 @@ def main():
         import torch
         from frizzle_b200 import _native
         print(json.dumps(formats_roofline(torch, _native.load(), _native, reps=args.steps)))
+        return 0
+    if args.c2_only:
+        import torch
+        from frizzle_b200 import _native
+        print(json.dumps(c2_sweep(torch, _native.load(), _native)))
         return 0
     if args.trace:
         return run_trace(args)

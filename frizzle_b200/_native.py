@@ -86,6 +86,8 @@ SIGNATURES = {
     "fz_batch_cache_state": (C.c_int, [VP, C.POINTER(U32), C.POINTER(U32)]),
     "fz_cache_truncate_keeps": (C.c_int, [VP, VP, U32, U32, U32]),
     "fz_batch_trace": (C.c_int, [VP, C.c_int]),
+    "fz_batch_set_wait_limit": (C.c_int, [VP, C.c_uint32]),
+    "fz_batch_inject_stale_epoch": (C.c_int, [VP, C.c_int]),
     "fz_batch_read_trace": (C.c_int, [VP, VP, C.c_size_t, C.POINTER(U32), C.POINTER(U32)]),
     "fz_q4_0_codes_bytes": (C.c_size_t, [U32, U32]),
     "fz_q4_0_scales_bytes": (C.c_size_t, [U32, U32]),

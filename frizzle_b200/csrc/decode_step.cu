@@ -51,7 +51,11 @@ constexpr uint32_t kSlotBp = 32;        // block pairs a ring slot holds
 constexpr uint32_t kSlotCodes = kSlotBp * 512, kSlotScales = kSlotBp * 64;
 constexpr uint32_t kHd = 256;           // head dimension
 constexpr uint32_t kMinSplitKeys = kDecodeSplitKeys;
-constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr uint64_t kWaitNs = 2000000000ull;   // every bounded wait's default limit
+// The step's wait limit (ns): the device Step's padding[1] in microseconds,
+// or kWaitNs when it is zero; set by thread 0 at the kernel's start.
+__shared__ unsigned long long g_wait_ns;
+FZ_DEV uint64_t wait_limit() { return g_wait_ns; }
 constexpr uint32_t kWaitIters = 1u << 30;
 constexpr int kNormVec = 3;             // vec4s of a row an invocation holds (hidden <= 3072)
 // Task partials reduced together: half-slots of [warps][16 rows][4 MQ
@@ -203,16 +207,19 @@ FZ_DEV uint64_t now_ns() {
 }
 FZ_DEV uint32_t error_word(const uint32_t* e) { return *reinterpret_cast<const volatile uint32_t*>(e); }
 
-// Waits for the phase of parity `parity`; gives up after kWaitNs, or early
+// Waits for the phase of parity `parity`; gives up after wait_limit(), or early
 // once `abort` (shared) or the error word is set (either may be null).
 FZ_DEV bool mb_wait(uint64_t* b, uint32_t parity, const uint32_t* err, const volatile uint32_t* abort) {
   if (mb_try(b, parity)) return true;
+  // (a drain, which has neither, keeps the default limit: a copy in flight
+  // must land before the CTA moves on, whatever the step's limit)
+  const uint64_t limit = err || abort ? wait_limit() : kWaitNs;
   const uint64_t t0 = now_ns();
   for (uint32_t i = 1; i < kWaitIters; i++) {
     if (mb_try_sleep(b, parity)) return true;
     if ((i & 3u) == 0) {
       if ((abort && *abort) || (err && error_word(err))) return false;
-      if (now_ns() - t0 > kWaitNs) return false;
+      if (now_ns() - t0 > limit) return false;
     }
   }
   return false;
@@ -274,7 +281,7 @@ FZ_DEV bool wait_counter(const uint32_t* ctr, uint32_t target, uint32_t* err) {
     __nanosleep(32);
     if ((i & 15u) == 15u) {
       if (error_word(err)) return false;
-      if (now_ns() - t0 > kWaitNs) {
+      if (now_ns() - t0 > wait_limit()) {
         atomicOr(err, kErrCounter);
         return false;
       }
@@ -943,7 +950,7 @@ __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const
           }
       }
       if (ok) break;
-      if ((it & 15u) == 15u && (*abort || error_word(a.error) || now_ns() - t0 > kWaitNs)) {
+      if ((it & 15u) == 15u && (*abort || error_word(a.error) || now_ns() - t0 > wait_limit())) {
         if (!*abort && !error_word(a.error)) atomicOr(a.error, kErrCounter);
         break;
       }
@@ -1194,7 +1201,7 @@ struct Attn {
 #pragma unroll
         for (int j = 0; j < 8; j++) ok = ok && (uint32_t)(w[j] >> 32) == want;
         if (__all_sync(0xffffffffu, ok)) break;
-        if ((it & 15u) == 15u && (flags()[0] || error_word(a.error) || now_ns() - t0 > kWaitNs)) {
+        if ((it & 15u) == 15u && (flags()[0] || error_word(a.error) || now_ns() - t0 > wait_limit())) {
           if (lane == 0 && !flags()[0] && !error_word(a.error)) atomicOr(a.error, kErrCounter);
           fail = true;
           break;
@@ -1582,7 +1589,7 @@ __device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uin
                                __uint_as_float((uint32_t)q[s][4]), __uint_as_float((uint32_t)q[s][5]));
           }
         if (ok) break;
-        if ((it & 15u) == 15u && (*abort || error_word(a.error) || now_ns() - t0 > kWaitNs)) {
+        if ((it & 15u) == 15u && (*abort || error_word(a.error) || now_ns() - t0 > wait_limit())) {
           if (!*abort && !error_word(a.error)) atomicOr(a.error, kErrCounter);
           break;
         }
@@ -1643,6 +1650,7 @@ struct Consumer {
   FZ_DEV uint32_t* tags() const { return reinterpret_cast<uint32_t*>(g_smem + a.lay.tags); }
   FZ_DEV uint32_t* uses() const { return reinterpret_cast<uint32_t*>(g_smem + a.lay.uses); }
   FZ_DEV uint32_t serial() const { return reinterpret_cast<const uint32_t*>(g_smem + a.lay.kvstate)[3]; }
+  FZ_DEV bool stale() const { return reinterpret_cast<const uint32_t*>(g_smem + a.lay.kvstate)[2] != 0u; }
   int tid, warp, lane, g, t;
   bool fail, dead;
   float acc[2][MQ][2];
@@ -1878,7 +1886,8 @@ struct Consumer {
         float v = 0.f;
         for (int w = 0; w < kCW; w++) v = add(v, rs[w * (16 * C) + row * C + tok]);
         if (kind == kPhQkv) {
-          st_ll(a.qkv_ll + (size_t)tok * ((a.heads + 2 * a.kv_heads) * kHd) + n, v, phase_epoch(serial(), l, kPhQkv));
+          const uint32_t sr = stale() ? serial() - 1u : serial();
+          st_ll(a.qkv_ll + (size_t)tok * ((a.heads + 2 * a.kv_heads) * kHd) + n, v, phase_epoch(sr, l, kPhQkv));
         } else if (kind == kPhO) {
           a.y_attn[((size_t)task_d * M + tok) * Hd + n] = v;
         } else if (kind == kPhDown) {
@@ -2004,8 +2013,12 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
     uint64_t* kvbar = reinterpret_cast<uint64_t*>(g_smem + ly.kvbar);
     uint32_t* kvstate = reinterpret_cast<uint32_t*>(g_smem + ly.kvstate);
     for (uint32_t b = 0; b < kv_bufs(MQ); b++) mb_init(kvbar + b, 1);
-    kvstate[0] = kvstate[1] = kvstate[2] = 0u;
+    kvstate[0] = kvstate[1] = 0u;
     kvstate[3] = a.step->padding[0];   // the step serial (epochs)
+    // The test hook (padding[2] nonzero) publishes the QKV products under the
+    // previous serial (see flush), so the attention's wait for them runs out.
+    kvstate[2] = a.step->padding[2];
+    g_wait_ns = a.step->padding[1] ? (unsigned long long)a.step->padding[1] * 1000ull : kWaitNs;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (threadIdx.x < kDecodeMaxRows) best[threadIdx.x] = 0ull;

@@ -255,6 +255,8 @@ struct fz_batch {
   int next_slot = 0;
   int last_slot = -1;
   uint32_t serial = 1;             // steps run (the decode kernel's epochs)
+  uint32_t wait_us = 0;            // the decode step's wait limit (0: the kernel's default)
+  uint32_t stale_epoch = 0;        // test hook: publish QKV under the previous epoch
   // The KV cache's bookkeeping (cache::KvCache, src/core/cache/kv.h): the
   // tokens every sequence's cache holds, and the most written since it was
   // last emptied; each layer's attention window beside b.slots.
@@ -1292,6 +1294,20 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
   return FZ_OK;
 }
 
+fz_status fz_batch_set_wait_limit(fz_batch* b, uint32_t microseconds) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  if (microseconds != 0 && (microseconds < 100 || microseconds > 10000000))
+    return fail(FZ_ERR_ARGUMENT, "a wait limit outside 100 us .. 10 s");
+  b->wait_us = microseconds;
+  return FZ_OK;
+}
+
+fz_status fz_batch_inject_stale_epoch(fz_batch* b, int enable) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  b->stale_epoch = enable ? 1u : 0u;
+  return FZ_OK;
+}
+
 fz_status fz_batch_trace(fz_batch* b, int enable) {
   if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
   FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
@@ -1403,6 +1419,9 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   if (sl.used) FZ_CUDA(cudaEventSynchronize(sl.copied));
   std::memcpy(sl.step, step, sizeof(DeviceStep));
   sl.step->padding[0] = b->serial++;   // a new epoch for the decode kernel's flag-in-data words
+  sl.step->padding[1] = b->wait_us;    // its waits' limit, microseconds (0: default)
+  sl.step->padding[2] = b->stale_epoch;
+  sl.step->padding[3] = 0;
   if (!step->fed) std::memcpy(sl.ids, ids, (size_t)T * b->S * 4);
   for (uint32_t i = 0; i < b->S; i++) {
     sl.seeds[2 * i] = seeds ? seeds[2 * i] : step->seed[0];
@@ -1471,6 +1490,20 @@ fz_status fz_batch_cache_state(fz_batch* b, uint32_t* length, uint32_t* written)
 
 namespace {
 
+// The waits a device error word names (the decode step's bits, or the
+// tensor-core product's codes 1..5).
+std::string wait_names(uint32_t code) {
+  if (code < 0x100) return "a tensor-core product's pipeline wait";
+  static const std::pair<uint32_t, const char*> bits[] = {
+      {0x100u, "a phase's wait for another phase's output"}, {0x200u, "a wait for a weight tile"},
+      {0x400u, "the copy issuer's wait for a free slot"}, {0x800u, "a copy's drain"},
+      {0x1000u, "a weight tile out of sequence"}, {0x2000u, "a norm's staging"}};
+  std::string out;
+  for (const auto& b : bits)
+    if (code & b.first) out += (out.empty() ? "" : ", ") + std::string(b.second);
+  return out.empty() ? "an unnamed wait" : out;
+}
+
 // Waits for slot `sl`'s step and copies its records out.
 fz_status settle(fz_batch* b, fz_batch::Slot& sl, fz_record* records) {
   cudaError_t e = cudaEventSynchronize(sl.done);
@@ -1481,7 +1514,9 @@ fz_status settle(fz_batch* b, fz_batch::Slot& sl, fz_record* records) {
   if (*sl.error) {
     const uint32_t code = *sl.error;
     FZ_CUDA(cudaMemsetAsync(b->gemm_error, 0, 4, b->model->dev->stream));
-    return fail(FZ_ERR_CUDA, "a device wait gave up (code " + std::to_string(code) + ")");
+    sl.pending = false;
+    return fail(FZ_ERR_CUDA, "a device wait gave up, the step was abandoned: " + wait_names(code) + " (code " +
+                                 std::to_string(code) + ")");
   }
   if (records) std::memcpy(records, sl.records, (size_t)b->S * 16);
   sl.pending = false;

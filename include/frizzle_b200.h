@@ -219,6 +219,24 @@ fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int
 fz_status fz_batch_trace(fz_batch *batch, int enable);
 fz_status fz_batch_read_trace(fz_batch *batch, uint64_t *out, size_t count, uint32_t *ctas, uint32_t *events);
 
+/* Every wait inside a one-token step (a phase waiting for another's output,
+ * a weight tile, a key/value chunk) is bounded; when one gives up, the step
+ * is abandoned by every CTA and fz_batch_wait reports FZ_ERR_CUDA naming the
+ * wait, and the next step runs normally (the device-lost and step-failure
+ * reports of src/core/kernels/program.cpp:621-625 and
+ * src/core/runtime/turn.h:108-113, and the reference tests' bounded pump,
+ * tests/support/gpu.h:41-54).  This sets the limit for the batch's
+ * following steps, in microseconds (100 .. 10,000,000; 0 restores the
+ * default of 2 s). */
+fz_status fz_batch_set_wait_limit(fz_batch *batch, uint32_t microseconds);
+
+/* Test hook, no counterpart in the reference: while enabled, each one-token
+ * step publishes its QKV products under the previous step's epoch, so the
+ * attention's bounded wait for them runs out and the step reports the
+ * failure as above.  Nothing faults; the batch's cache then holds the
+ * tokens before the failed step's position only after fz_batch_truncate. */
+fz_status fz_batch_inject_stale_epoch(fz_batch *batch, int enable);
+
 /* ------------------------------------------------------------------ kernel level
  * Device pointers throughout; `stream` is a cudaStream_t or NULL (the legacy
  * default stream). */

@@ -86,6 +86,7 @@ def _declare(L):
     L.oracle_capture_slots.restype = C.c_int64
     L.oracle_step.argtypes = [P, C.c_uint32, C.c_int, U32P, P, P, P]
     L.oracle_threads.restype = C.c_int
+    L.oracle_set_threads.argtypes = [C.c_int]
 
 
 # ------------------------------------------------------------ small helpers

@@ -804,3 +804,13 @@ EXPORT int oracle_threads(void) {
     return 1;
 #endif
 }
+
+/* Sets the host threads the restatement runs on (a launcher such as torchrun
+ * may have set OMP_NUM_THREADS=1 for the process). */
+EXPORT void oracle_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
