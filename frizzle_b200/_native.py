@@ -87,6 +87,9 @@ SIGNATURES = {
     "fz_cache_truncate_keeps": (C.c_int, [VP, VP, U32, U32, U32]),
     "fz_batch_trace": (C.c_int, [VP, C.c_int]),
     "fz_batch_set_wait_limit": (C.c_int, [VP, C.c_uint32]),
+    "fz_batch_time_decode": (C.c_int, [VP, C.c_int]),
+    "fz_batch_cache_advance": (C.c_int, [VP, C.c_uint32]),
+    "fz_batch_decode_time": (C.c_int, [VP, C.POINTER(C.c_float)]),
     "fz_batch_inject_stale_epoch": (C.c_int, [VP, C.c_int]),
     "fz_batch_read_trace": (C.c_int, [VP, VP, C.c_size_t, C.POINTER(U32), C.POINTER(U32)]),
     "fz_q4_0_codes_bytes": (C.c_size_t, [U32, U32]),

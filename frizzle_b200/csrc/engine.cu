@@ -184,10 +184,13 @@ struct fz_model {
 
 namespace {
 
+// A step graph's shape; `slot` names the host slot its first and last
+// launches read from and write to (two steps may be in flight).
 struct GraphKey {
-  uint32_t tokens, logits, capture, edits;
+  uint32_t tokens, logits, capture, edits, timed, slot;
   bool operator<(const GraphKey& o) const {
-    return std::tie(tokens, logits, capture, edits) < std::tie(o.tokens, o.logits, o.capture, o.edits);
+    return std::tie(tokens, logits, capture, edits, timed, slot) <
+           std::tie(o.tokens, o.logits, o.capture, o.edits, o.timed, o.slot);
   }
 };
 
@@ -256,6 +259,8 @@ struct fz_batch {
   int last_slot = -1;
   uint32_t serial = 1;             // steps run (the decode kernel's epochs)
   uint32_t wait_us = 0;            // the decode step's wait limit (0: the kernel's default)
+  bool time_decode = false;        // record events around the persistent decode kernel
+  cudaEvent_t dk_start = nullptr, dk_end = nullptr;
   uint32_t stale_epoch = 0;        // test hook: publish QKV under the previous epoch
   // The KV cache's bookkeeping (cache::KvCache, src/core/cache/kv.h): the
   // tokens every sequence's cache holds, and the most written since it was
@@ -272,6 +277,8 @@ struct fz_batch {
   ~fz_batch() {
     for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
     if (trace) cudaFree(trace);
+    if (dk_start) cudaEventDestroy(dk_start);
+    if (dk_end) cudaEventDestroy(dk_end);
     for (void* p : allocations) cudaFree(p);
     for (void* p : row_allocs) cudaFree(p);
     for (auto& s : slot) {
@@ -565,10 +572,43 @@ fz_status enqueue_capture(fz_batch& b, const GraphKey& key, cudaStream_t st) {
   return FZ_OK;
 }
 
+// Device address of a pinned host buffer (mapped into the device's address space).
+template <typename T>
+fz_status mapped(T* host, T** dev) {
+  void* d = nullptr;
+  FZ_CUDA(cudaHostGetDevicePointer(&d, const_cast<void*>(static_cast<const void*>(host)), 0));
+  *dev = static_cast<T*>(d);
+  return FZ_OK;
+}
+
+// The whole step: its inputs staged from the host slot by a kernel, the
+// forward pass (and the capture), its records and error word published into
+// the slot by a kernel.
 fz_status enqueue_step(fz_batch& b, const GraphKey& key, cudaStream_t st) {
-  fz_status stt = enqueue_forward(b, key, st);
-  if (stt || !key.capture) return stt;
-  return enqueue_capture(b, key, st);
+  auto& sl = b.slot[key.slot];
+  fz::StageArgs sa{};
+  fz_status stt;
+  if ((stt = mapped<const DeviceStep>(sl.step, &sa.step_h)) || (stt = mapped<const uint32_t>(sl.seeds, &sa.seeds_h)) ||
+      (stt = mapped<const uint32_t>(sl.ids, &sa.ids_h)))
+    return stt;
+  sa.step_d = b.dstep;
+  sa.seeds_d = b.dseeds;
+  sa.ids_d = b.dids;
+  sa.seed_words = 2 * b.S;
+  sa.id_words = key.tokens * b.S;   // (a fed step's are not read)
+  sa.zero = b.dsync;                // the decode kernel's phase counters start at zero
+  sa.zero_words = (uint32_t)b.dsync_words;
+  FZ_CUDA(fz::launch_stage(sa, st));
+  stt = enqueue_forward(b, key, st);
+  if (!stt && key.capture) stt = enqueue_capture(b, key, st);
+  if (stt) return stt;
+  fz::PublishArgs pa{};
+  pa.records_d = b.records;
+  pa.record_words = 4 * b.S;
+  pa.error_d = b.gemm_error;
+  if ((stt = mapped(sl.records, &pa.records_h)) || (stt = mapped(sl.error, &pa.error_h))) return stt;
+  FZ_CUDA(fz::launch_publish(pa, st));
+  return FZ_OK;
 }
 
 fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
@@ -597,7 +637,7 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
   if (T == 1 && decode_step_enabled() &&
       fz::decode_supported(b.S, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim)) {
     // One token for each sequence: the whole step in one persistent kernel.
-    FZ_CUDA(cudaMemsetAsync(b.dsync, 0, b.dsync_words * 4, st));
+    // (the stage kernel cleared the phase counters, b.dsync)
     fz::DecodeArgs d{};
     d.step = b.dstep;
     d.layers = b.dlayers;
@@ -650,7 +690,9 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       d.trace = b.trace;
       d.trace_stride = b.trace_events;
     }
+    if (key.timed) FZ_CUDA(cudaEventRecordWithFlags(b.dk_start, st, cudaEventRecordExternal));
     FZ_CUDA(fz::launch_decode(d, st));
+    if (key.timed) FZ_CUDA(cudaEventRecordWithFlags(b.dk_end, st, cudaEventRecordExternal));
     if (key.logits) {
       // Final norm (X plus the last down projection's K-slice partials) and the tied head.
       fz::MatvecArgs h{};
@@ -1302,6 +1344,28 @@ fz_status fz_batch_set_wait_limit(fz_batch* b, uint32_t microseconds) {
   return FZ_OK;
 }
 
+fz_status fz_batch_time_decode(fz_batch* b, int enable) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  if (enable && !b->dk_start) {
+    FZ_CUDA(cudaEventCreate(&b->dk_start));
+    FZ_CUDA(cudaEventCreate(&b->dk_end));
+  }
+  b->time_decode = enable != 0;
+  return FZ_OK;
+}
+
+fz_status fz_batch_decode_time(fz_batch* b, float* microseconds) {
+  if (!b || !microseconds) return fail(FZ_ERR_ARGUMENT, "null argument");
+  if (!b->time_decode) return fail(FZ_ERR_STATE, "decode timing is off (fz_batch_time_decode)");
+  FZ_CUDA(cudaSetDevice(b->model->dev->ordinal));
+  float ms = 0.f;
+  FZ_CUDA(cudaEventSynchronize(b->dk_end));
+  FZ_CUDA(cudaEventElapsedTime(&ms, b->dk_start, b->dk_end));
+  *microseconds = ms * 1000.f;
+  return FZ_OK;
+}
+
 fz_status fz_batch_inject_stale_epoch(fz_batch* b, int enable) {
   if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
   b->stale_epoch = enable ? 1u : 0u;
@@ -1427,13 +1491,12 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
     sl.seeds[2 * i] = seeds ? seeds[2 * i] : step->seed[0];
     sl.seeds[2 * i + 1] = seeds ? seeds[2 * i + 1] : step->seed[1];
   }
-  FZ_CUDA(cudaMemcpyAsync(b->dstep, sl.step, sizeof(DeviceStep), cudaMemcpyHostToDevice, st));
-  if (!step->fed) FZ_CUDA(cudaMemcpyAsync(b->dids, sl.ids, (size_t)T * b->S * 4, cudaMemcpyHostToDevice, st));
-  FZ_CUDA(cudaMemcpyAsync(b->dseeds, sl.seeds, (size_t)b->S * 8, cudaMemcpyHostToDevice, st));
-  FZ_CUDA(cudaEventRecord(sl.copied, st));
+  // (the step's first launch reads the slot's Step, ids and seeds from the
+  // pinned host memory; its last writes the records and the error word back)
   bool edits = false;
   for (bool e : b->has_edits) edits = edits || e;
-  const GraphKey key{T, step->logits ? 1u : 0u, step->capture ? 1u : 0u, edits ? 1u : 0u};
+  const GraphKey key{T, step->logits ? 1u : 0u, step->capture ? 1u : 0u, edits ? 1u : 0u,
+                     b->time_decode && T == 1 ? 1u : 0u, (uint32_t)b->next_slot};
   fz_status stt;
   if (direct_launch()) {
     if ((stt = enqueue_step(*b, key, st))) return stt;
@@ -1442,8 +1505,7 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
     if ((stt = graph_for(*b, key, &exec))) return stt;
     FZ_CUDA(cudaGraphLaunch(exec, st));
   }
-  FZ_CUDA(cudaMemcpyAsync(sl.records, b->records, (size_t)b->S * 16, cudaMemcpyDeviceToHost, st));
-  FZ_CUDA(cudaMemcpyAsync(sl.error, b->gemm_error, 4, cudaMemcpyDeviceToHost, st));
+  FZ_CUDA(cudaEventRecord(sl.copied, st));   // the slot's inputs are read by now
   FZ_CUDA(cudaEventRecord(sl.done, st));
   sl.used = true;
   sl.pending = true;
@@ -1478,6 +1540,14 @@ fz_status fz_batch_truncate(fz_batch* b, uint32_t tokens, uint32_t* kept) {
     b->length = b->written = 0;
   }
   if (kept) *kept = b->length;
+  return FZ_OK;
+}
+
+fz_status fz_batch_cache_advance(fz_batch* b, uint32_t tokens) {
+  if (!b) return fail(FZ_ERR_ARGUMENT, "null batch");
+  if ((uint64_t)b->length + tokens > b->context) return fail(FZ_ERR_ARGUMENT, "advance past the batch's context");
+  b->length += tokens;
+  b->written = std::max(b->written, b->length);
   return FZ_OK;
 }
 

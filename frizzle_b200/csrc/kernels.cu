@@ -595,4 +595,39 @@ cudaError_t launch_select(const SelectArgs& a, cudaStream_t stream, bool pdl) {
   return launch((const void*)select_draw_kernel, dim3(a.seqs), dim3(512), 0, stream, pdl, args2);
 }
 
+
+// ------------------------------------------------------------ step inputs and outputs
+
+namespace {
+
+__global__ void __launch_bounds__(256) stage_kernel(const StageArgs a) {
+  const uint32_t n = gridDim.x * blockDim.x, i0 = blockIdx.x * blockDim.x + threadIdx.x;
+  constexpr uint32_t kStepWords = sizeof(DeviceStep) / 4;
+  const uint32_t* sh = reinterpret_cast<const uint32_t*>(a.step_h);
+  uint32_t* sd = reinterpret_cast<uint32_t*>(a.step_d);
+  for (uint32_t i = i0; i < kStepWords; i += n) sd[i] = sh[i];
+  for (uint32_t i = i0; i < a.seed_words; i += n) a.seeds_d[i] = a.seeds_h[i];
+  for (uint32_t i = i0; i < a.id_words; i += n) a.ids_d[i] = a.ids_h[i];
+  for (uint32_t i = i0; i < a.zero_words; i += n) a.zero[i] = 0u;
+}
+
+__global__ void __launch_bounds__(64) publish_kernel(const PublishArgs a) {
+  for (uint32_t i = threadIdx.x; i < a.record_words; i += blockDim.x) a.records_h[i] = a.records_d[i];
+  if (threadIdx.x == 0) a.error_h[0] = *reinterpret_cast<const volatile uint32_t*>(a.error_d);
+}
+
+}  // namespace
+
+cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream) {
+  const uint32_t words = std::max(std::max(a.id_words, a.zero_words), std::max(a.seed_words, 16u));
+  const uint32_t blocks = std::min(64u, (words + 255u) / 256u);
+  stage_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_publish(const PublishArgs& a, cudaStream_t stream) {
+  publish_kernel<<<1, 64, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace fz

@@ -115,4 +115,32 @@ cudaError_t launch_readout_select(const ReadoutArgs& a, uint32_t g0, uint32_t n,
 uint32_t select_tiles(uint32_t vocab);
 cudaError_t launch_select(const SelectArgs& a, cudaStream_t stream, bool pdl);
 
+// A step's inputs and outputs moved by kernels instead of copies: the stage
+// kernel, the step's first launch, reads the host slot's Step, seeds and
+// token ids straight from pinned host memory (mapped into the device's
+// address space) into their device copies and clears `zero_words` words;
+// the publish kernel, its last, writes the step's records and error word
+// into the slot's pinned memory.  (Each small host-device copy on the
+// step's stream cost several microseconds between the launches.)
+struct StageArgs {
+  const DeviceStep* step_h;
+  const uint32_t* seeds_h;
+  const uint32_t* ids_h;
+  DeviceStep* step_d;
+  uint32_t* seeds_d;
+  uint32_t* ids_d;
+  uint32_t seed_words, id_words;
+  uint32_t* zero;
+  uint32_t zero_words;
+};
+struct PublishArgs {
+  const uint32_t* records_d;
+  uint32_t* records_h;
+  uint32_t record_words;
+  const uint32_t* error_d;
+  uint32_t* error_h;
+};
+cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream);
+cudaError_t launch_publish(const PublishArgs& a, cudaStream_t stream);
+
 }  // namespace fz

@@ -200,6 +200,11 @@ fz_status fz_batch_cache_state(fz_batch *batch, uint32_t *length, uint32_t *writ
  * survives the truncation (kv.h:56-63).  Host only; needs no device. */
 int fz_cache_truncate_keeps(const uint32_t *windows, const uint32_t *slots, uint32_t layers, uint32_t written,
                             uint32_t tokens);
+/* KvCache::advance (src/core/cache/kv.h:64, kv.cpp:52-55): the length grows
+ * by `tokens` and the high-water mark follows it, for a caller that wrote
+ * the caches' keys and values itself (through fz_batch_cache); refused past
+ * the batch's context. */
+fz_status fz_batch_cache_advance(fz_batch *batch, uint32_t tokens);
 /* Device pointer of sequence s's key or value cache for `layer` ([slots][kv_heads][d] f16). */
 fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int values, void **ptr,
                          uint32_t *slots);
@@ -218,6 +223,14 @@ fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int
  * With out = NULL it only reports the shape. */
 fz_status fz_batch_trace(fz_batch *batch, int enable);
 fz_status fz_batch_read_trace(fz_batch *batch, uint64_t *out, size_t count, uint32_t *ctas, uint32_t *events);
+
+/* Times the persistent decode kernel of each following one-token step with
+ * CUDA events recorded around its launch on the step's stream (Frizzle's
+ * profiled step times its launches, src/core/kernels/program.h:142-168);
+ * fz_batch_decode_time gives the last such step's kernel duration once the
+ * step has run. */
+fz_status fz_batch_time_decode(fz_batch *batch, int enable);
+fz_status fz_batch_decode_time(fz_batch *batch, float *microseconds);
 
 /* Every wait inside a one-token step (a phase waiting for another's output,
  * a weight tile, a key/value chunk) is bounded; when one gives up, the step

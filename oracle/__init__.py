@@ -232,6 +232,15 @@ class OracleModel:
         v = np.ctypeslib.as_array(C.cast(lib().oracle_ctx_values(self.ctx, layer), C.POINTER(C.c_uint16)), (n,))
         return k.copy(), v.copy()
 
+    def write_cache(self, layer: int, keys: np.ndarray, values: np.ndarray) -> None:
+        """Overwrites the layer's key and value rings ([slots][kv_heads][d]
+        f16 bits) with the given ones (a test's seeded cache)."""
+        n = self.slots(layer) * self.shape.kv_heads * self.shape.head_dim
+        for ptr, src in ((lib().oracle_ctx_keys(self.ctx, layer), keys), (lib().oracle_ctx_values(self.ctx, layer),
+                                                                           values)):
+            dst = np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_uint16)), (n,))
+            dst[:] = np.ascontiguousarray(src, dtype=np.uint16).reshape(-1)
+
     def close(self):
         if self.ctx:
             lib().oracle_ctx_free(self.ctx)

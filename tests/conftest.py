@@ -10,6 +10,7 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 GPU (B200); parity tests through the C ABI")
+    config.addinivalue_line("markers", "slow: takes minutes (the oracle's side of a large config); still a gpu test")
 
 
 @pytest.fixture(scope="session")
