@@ -724,8 +724,9 @@ def run_ours(args):
                              "frac": dk_bytes / dk_secs / 1e9 / hbm, "peak_source": which,
                              "algorithmic_bytes": dk_bytes, "launch_us": dk_secs * 1e6,
                              "traffic": traffic_from_profile("decode_kernel_traffic.json"),
-                             "timing": "CUDA events recorded around the kernel's launch on its stream inside each "
-                                       "step (fz_batch_time_decode), untraced, mean of K decode steps",
+                             "timing": "CUDA events recorded around the kernel's launch on its stream in each step "
+                                       "(fz_batch_time_decode: the step launched directly, not from its graph), "
+                                       "untraced, mean of K decode steps",
                              "bytes": "26 layers' Q4_0 weights + norm gains (392,491,008 + 532,480 B) + the keys "
                                       "and values the steps' attention reads (1 KiB a key a layer)"},
                 "head_roofline": {"bound": "hbm", "kernel": "q4_0 head matvec 262144 x 1152, M=1, timed alone",
@@ -944,6 +945,9 @@ def run_trace(args):
     out["tile_wait_us_per_cta"] = {name: float(np.mean(tl[:, i]) / 1000.0) for i, name in enumerate(PHASES)}
     out["issuer"] = {"wait_us": float(np.mean(tl[:, 6]) / 1000.0), "issue_us": float(np.mean(tl[:, 7]) / 1000.0),
                      "tiles": float(np.mean(tl[:, 8]))}
+    out["cta_span_us"] = {"entry_spread": float(np.ptp(tl[:, 9]) / 1000.0),
+                          "exit_spread": float(np.ptp(tl[:, 10]) / 1000.0),
+                          "first_entry_to_last_exit": float((tl[:, 10].max() - tl[:, 9].min()) / 1000.0)}
     for ph, name in enumerate(PHASES):
         rows = range(L - 1, L) if ph == 5 else range(L)
         if not spread[ph]["work_max"]:

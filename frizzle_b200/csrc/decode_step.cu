@@ -2002,6 +2002,10 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
   volatile uint32_t* flags = reinterpret_cast<volatile uint32_t*>(g_smem + ly.flags);
   unsigned long long* best = reinterpret_cast<unsigned long long*>(g_smem + ly.best);
   uint32_t* uses = reinterpret_cast<uint32_t*>(g_smem + ly.uses);
+  unsigned long long* trace_tail =
+      a.trace ? a.trace + (size_t)blockIdx.x * a.trace_stride + a.n_layers * kDecodeTracePhases * kDecodeTraceStamps
+              : nullptr;
+  if (trace_tail && threadIdx.x == 0) trace_tail[9] = now_ns();
   if (threadIdx.x == 0) {
     for (uint32_t s = 0; s < S; s++) {
       mb_init(full + s, 1);
@@ -2055,6 +2059,7 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
       if (uses[s] && !mb_wait(full + s, (uses[s] - 1) & 1u, nullptr, nullptr)) atomicOr(a.error, kErrDrain);
     // (Key/value chunk copies are drained by the attention itself: only a
     // drain that timed out leaves one in flight, and it reported kErrDrain.)
+    if (trace_tail) trace_tail[10] = now_ns();
   }
 }
 

@@ -105,7 +105,8 @@ struct DecodeArgs {
   // the prologue; attention: queries roped), 3 products done (attention:
   // keys folded), 4 done.  Then kDecodeTraceTail words: per phase the
   // time thread 0 waited for weight tiles (ns), the producer's time waiting
-  // for free slots and issuing copies (ns), and its tile count.  Null: no trace.
+  // for free slots and issuing copies (ns), its tile count, and the global
+  // timer at the CTA's entry and at its exit.  Null: no trace.
   unsigned long long* trace;
   uint32_t trace_stride;
   DecodeLayout lay;                // filled by launch_decode
@@ -113,7 +114,7 @@ struct DecodeArgs {
 
 constexpr uint32_t kDecodeTracePhases = 6;
 constexpr uint32_t kDecodeTraceStamps = 5;
-constexpr uint32_t kDecodeTraceTail = 9;
+constexpr uint32_t kDecodeTraceTail = 11;   // (+ the CTA's entry and exit times)
 
 inline size_t decode_sync_words(uint32_t layers, uint32_t rows, uint32_t kv_heads) {
   return (size_t)layers * (kDecodeSyncFixed + (size_t)rows * kv_heads);

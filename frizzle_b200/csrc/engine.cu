@@ -690,9 +690,11 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       d.trace = b.trace;
       d.trace_stride = b.trace_events;
     }
-    if (key.timed) FZ_CUDA(cudaEventRecordWithFlags(b.dk_start, st, cudaEventRecordExternal));
+    // (a timed step is launched directly, not from a graph: plain events on
+    // the stream bracket the kernel alone)
+    if (key.timed) FZ_CUDA(cudaEventRecord(b.dk_start, st));
     FZ_CUDA(fz::launch_decode(d, st));
-    if (key.timed) FZ_CUDA(cudaEventRecordWithFlags(b.dk_end, st, cudaEventRecordExternal));
+    if (key.timed) FZ_CUDA(cudaEventRecord(b.dk_end, st));
     if (key.logits) {
       // Final norm (X plus the last down projection's K-slice partials) and the tied head.
       fz::MatvecArgs h{};
@@ -987,12 +989,26 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
   return FZ_OK;
 }
 
+fz_status capture_graph(fz_batch& b, const GraphKey& key, cudaGraphExec_t* out);
+
+// The step graph for `key`; a shape seen for the first time is captured for
+// both host slots at once, so that a later step on the other slot finds its
+// graph made.
 fz_status graph_for(fz_batch& b, const GraphKey& key, cudaGraphExec_t* out) {
   auto it = b.graphs.find(key);
   if (it != b.graphs.end()) {
     *out = it->second;
     return FZ_OK;
   }
+  GraphKey other = key;
+  other.slot ^= 1u;
+  cudaGraphExec_t unused = nullptr;
+  fz_status st;
+  if (!b.graphs.count(other) && (st = capture_graph(b, other, &unused))) return st;
+  return capture_graph(b, key, out);
+}
+
+fz_status capture_graph(fz_batch& b, const GraphKey& key, cudaGraphExec_t* out) {
   cudaStream_t cs = b.model->dev->capture;
   FZ_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
   fz_status st = enqueue_step(b, key, cs);
@@ -1498,7 +1514,7 @@ fz_status fz_batch_step(fz_batch* b, const fz_step* step, const uint32_t* ids, c
   const GraphKey key{T, step->logits ? 1u : 0u, step->capture ? 1u : 0u, edits ? 1u : 0u,
                      b->time_decode && T == 1 ? 1u : 0u, (uint32_t)b->next_slot};
   fz_status stt;
-  if (direct_launch()) {
+  if (direct_launch() || key.timed) {
     if ((stt = enqueue_step(*b, key, st))) return stt;
   } else {
     cudaGraphExec_t exec = nullptr;

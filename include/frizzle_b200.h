@@ -218,8 +218,9 @@ fz_status fz_batch_cache(fz_batch *batch, uint32_t sequence, uint32_t layer, int
  * + k (phase 0 QKV, 1 attention, 2 output projection, 3 gate/up, 4 down,
  * 5 head in the last layer's slots; k 0 began waiting, 1 inputs complete,
  * 2 inputs staged, 3 products done, 4 done), 0 where a CTA had no work;
- * then 9 totals: per phase the ns spent waiting for weight tiles, the ns the
- * copy issuer waited for free slots, the ns it spent issuing, its tile count.
+ * then 11 words: per phase the ns spent waiting for weight tiles, the ns the
+ * copy issuer waited for free slots, the ns it spent issuing, its tile count,
+ * and the global timer at the CTA's entry and at its exit.
  * With out = NULL it only reports the shape. */
 fz_status fz_batch_trace(fz_batch *batch, int enable);
 fz_status fz_batch_read_trace(fz_batch *batch, uint64_t *out, size_t count, uint32_t *ctas, uint32_t *events);
@@ -227,8 +228,9 @@ fz_status fz_batch_read_trace(fz_batch *batch, uint64_t *out, size_t count, uint
 /* Times the persistent decode kernel of each following one-token step with
  * CUDA events recorded around its launch on the step's stream (Frizzle's
  * profiled step times its launches, src/core/kernels/program.h:142-168);
- * fz_batch_decode_time gives the last such step's kernel duration once the
- * step has run. */
+ * timed steps are launched directly rather than from the step's graph, so
+ * the events bracket the kernel alone.  fz_batch_decode_time gives the last
+ * such step's kernel duration once the step has run. */
 fz_status fz_batch_time_decode(fz_batch *batch, int enable);
 fz_status fz_batch_decode_time(fz_batch *batch, float *microseconds);
 
