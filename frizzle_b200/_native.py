@@ -46,6 +46,12 @@ class ModelInfo(C.Structure):
                 ("weight_bytes", C.c_uint64)]
 
 
+class Plan(C.Structure):
+    _fields_ = [(n, C.c_uint32) for n in ("sequences", "context", "rollback", "rows")] + \
+               [(n, C.c_uint64) for n in ("budget", "weight_bytes", "copy_bytes", "scratch_bytes", "cache_bytes",
+                                           "total_bytes")]
+
+
 class CaptureSlot(C.Structure):
     _fields_ = [("first", C.c_uint32), ("width", C.c_uint32)]
 
@@ -89,6 +95,8 @@ SIGNATURES = {
     "fz_batch_set_wait_limit": (C.c_int, [VP, C.c_uint32]),
     "fz_batch_time_decode": (C.c_int, [VP, C.c_int]),
     "fz_batch_cache_advance": (C.c_int, [VP, C.c_uint32]),
+    "fz_model_plan": (C.c_int, [VP, C.POINTER(Plan)]),
+    "fz_model_index_plan": (C.c_int, [VP, C.c_uint64, C.c_uint64, C.POINTER(Plan)]),
     "fz_batch_decode_time": (C.c_int, [VP, C.POINTER(C.c_float)]),
     "fz_batch_inject_stale_epoch": (C.c_int, [VP, C.c_int]),
     "fz_batch_read_trace": (C.c_int, [VP, VP, C.c_size_t, C.POINTER(U32), C.POINTER(U32)]),

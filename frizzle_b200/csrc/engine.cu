@@ -452,6 +452,120 @@ fz_status run_matvec(fz::MatvecArgs a, int pro, int epi, cudaStream_t stream, bo
 
 // ------------------------------------------------------------ per-row scratch
 
+// A layer's key/value ring for one sequence: a window layer keeps its window,
+// a prefill block (512) and the rollback reserve (plan.cpp:335-336), rounded
+// up to whole 32-slot chunks so that a decode chunk's tensor copy never
+// wraps; never more than the context.  A global layer's window is the
+// trained context, so its ring is the context.
+uint32_t ring_slots(uint32_t window, uint32_t context, uint32_t rollback) {
+  const uint64_t ring = ((uint64_t)window + 512 + rollback + 31) / 32 * 32;
+  return (uint32_t)std::min<uint64_t>(context, ring);
+}
+
+// Every layer's attention window (the trained context for global layers).
+std::vector<uint32_t> layer_windows(const Shape& s) {
+  std::vector<uint32_t> w(s.layers);
+  for (uint32_t l = 0; l < s.layers; l++)
+    w[l] = s.window == 0 || l % s.pattern == s.pattern - 1 ? s.context : s.window;
+  return w;
+}
+
+// The device bytes of a batch, counted with the expressions its allocations
+// use (fz_batch_create, alloc_rows): the key/value rings, and the scratch
+// for `rows` token rows a step.
+struct BatchBytes {
+  uint64_t cache = 0, scratch = 0;
+};
+BatchBytes batch_bytes(const Shape& s, uint32_t S, uint32_t context, uint32_t rollback, uint32_t rows) {
+  BatchBytes out;
+  uint32_t splits_max = 1;
+  for (uint32_t w : layer_windows(s)) {
+    const uint64_t per_seq = (uint64_t)ring_slots(w, context, rollback) * s.kv_heads * s.head_dim;
+    out.cache += 2 * per_seq * S * 2;
+    const uint32_t keys = std::min(w, context);
+    splits_max = std::max<uint32_t>({splits_max, (keys + split_keys_for(keys) - 1) / split_keys_for(keys),
+                                     std::min<uint32_t>((keys + fz::kDecodeSplitKeys - 1) / fz::kDecodeSplitKeys,
+                                                        fz::kDecodeMaxSplits)});
+  }
+  const uint64_t Q = (uint64_t)s.heads * s.head_dim, KV = (uint64_t)s.kv_heads * s.head_dim;
+  const uint64_t R8 = (uint64_t)fz::kDecodeMaxRows * 8, V = s.vocab, T16 = fz::kMaxTokens;
+  const uint64_t tiles = fz::select_tiles(s.vocab), table_words = 2ull * s.layers + 5ull * kMaxEdits;
+  uint64_t f = R8 * (Q + 2 * KV) + R8 * Q + R8 * s.ffn + R8 * s.heads * fz::kDecodeFoldSplits * s.head_dim +
+               R8 * s.heads * fz::kDecodeFoldSplits * 2;
+  f += S * V * 4 + S * 8 + S * tiles * 64 * 8 + S * 128 * 4 + S * 16 + 64 + S * 8 + 16 + S * table_words * 4 +
+       S * capture_layout(s).words * 4 + T16 * s.hidden * 4 + T16 * V * 4 + T16 * 8 + T16 * tiles * 64 * 8;
+  const uint64_t M = rows, X = std::max<uint64_t>(s.hidden, Q);
+  const uint64_t PM = fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim) ? std::min<uint64_t>(M, T16) : M;
+  f += M * s.hidden * 4 * 2 + M * (Q + 2 * KV) * 4 + M * Q * 4 * 2 + M * s.hidden * 4 * 2 + M * s.ffn * 4 +
+       PM * s.heads * splits_max * s.head_dim * 4 + PM * s.heads * splits_max * 2 * 4 +
+       (uint64_t)s.layers * (1 + M * s.kv_heads) * 4 + M * 4 + M * X * 2 * 2 + M * s.ffn * 2 * 2 +
+       (fz::kDecodeOSlices + fz::kDecodeDownSlices) * M * s.hidden * 4 +
+       fz::decode_sync_words(s.layers, (uint32_t)M, s.kv_heads) * 4;
+  out.scratch = f;
+  return out;
+}
+
+// plan_residency's sizing (plan.cpp:321-419) for one batch: `fixed` bytes
+// (weights, copies) plus the batch's scratch and rings must stay within the
+// budget.  The cost never falls as the context or the sequences grow, so the
+// largest context (or sequence count) that fits is found by bisection.
+fz_status plan_batch(const Shape& s, uint64_t fixed, fz_plan* p) {
+  if (p->sequences > (uint32_t)fz::kMaxTokens) return fail(FZ_ERR_ARGUMENT, "more than 16 sequences a batch");
+  if (p->context > s.context) return fail(FZ_ERR_ARGUMENT, "a context past the trained context");
+  const uint32_t rows = p->rows ? p->rows : 4096u;
+  if (rows < fz::kMaxTokens) return fail(FZ_ERR_ARGUMENT, "fewer than 16 rows a step");
+  const uint64_t slack = 1ull << 26;   // allocation granules and small per-batch buffers: 64 MiB
+  const auto cost = [&](uint32_t S, uint32_t ctx) {
+    const BatchBytes b = batch_bytes(s, S, ctx, p->rollback, std::max<uint32_t>(rows, S * fz::kMaxTokens));
+    return fixed + slack + b.scratch + b.cache;
+  };
+  const uint32_t shortest = std::min<uint32_t>(512, s.context);
+  uint32_t S = p->sequences ? p->sequences : 1u;
+  uint32_t ctx = p->context ? p->context : shortest;
+  if (cost(S, ctx) > p->budget) {
+    p->total_bytes = cost(S, ctx);
+    return fail(FZ_ERR_FIT, "the weights, scratch and shortest cache exceed the budget (PlanError::ExceedsBudget)");
+  }
+  if (!p->sequences) {
+    uint32_t lo = 1, hi = fz::kMaxTokens;   // the most sequences that fit at the context
+    while (lo < hi) {
+      const uint32_t mid = lo + (hi - lo + 1) / 2;
+      if (cost(mid, ctx) <= p->budget) lo = mid;
+      else hi = mid - 1;
+    }
+    S = lo;
+  }
+  if (!p->context) {
+    uint32_t lo = shortest, hi = s.context;   // the largest context that fits for S sequences
+    while (lo < hi) {
+      const uint32_t mid = lo + (hi - lo + 1) / 2;
+      if (cost(S, mid) <= p->budget) lo = mid;
+      else hi = mid - 1;
+    }
+    ctx = lo;
+  }
+  const BatchBytes b = batch_bytes(s, S, ctx, p->rollback, std::max<uint32_t>(rows, S * fz::kMaxTokens));
+  p->sequences = S;
+  p->context = ctx;
+  p->rows = rows;
+  p->scratch_bytes = b.scratch;
+  p->cache_bytes = b.cache;
+  p->total_bytes = cost(S, ctx);
+  return FZ_OK;
+}
+
+// The model's weights on the device (every tensor's bytes in its file form,
+// the repacked layout being the same size, and the RoPE turns), and its f16
+// prefill copies (f16 part and remainder of every layer product).
+void weight_bytes_of(const fz_model& m, uint64_t& weights, uint64_t& copies) {
+  const Shape& s = m.shape;
+  weights = 0;
+  for (const auto& t : m.index.tensors) weights += t.bytes;
+  weights += (uint64_t)s.layers * (s.head_dim / 2) * 4;
+  const uint64_t Q = (uint64_t)s.heads * s.head_dim, KV = (uint64_t)s.kv_heads * s.head_dim;
+  copies = (uint64_t)s.layers * ((Q + 2 * KV) * s.hidden + s.hidden * Q + 3ull * s.ffn * s.hidden) * 2 * 2;
+}
+
 // (Re)allocates every buffer sized by the step's rows for `rows` rows.
 fz_status alloc_rows(fz_batch& b, uint32_t rows) {
   const Shape& s = b.model->shape;
@@ -1218,6 +1332,39 @@ fz_status fz_model_info_get(const fz_model* m, fz_model_info* o) {
   return FZ_OK;
 }
 
+fz_status fz_model_plan(const fz_model* m, fz_plan* p) {
+  if (!m || !p) return fail(FZ_ERR_ARGUMENT, "null argument");
+  if (!m->finished) return fail(FZ_ERR_STATE, "the model is not loaded");
+  weight_bytes_of(*m, p->weight_bytes, p->copy_bytes);
+  if (!p->budget) {
+    // The device's free memory now: the weights and copies are already in place.
+    FZ_CUDA(cudaSetDevice(m->dev->ordinal));
+    size_t free_b = 0, total_b = 0;
+    FZ_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    p->budget = free_b + p->weight_bytes + p->copy_bytes;
+  }
+  return plan_batch(m->shape, p->weight_bytes + p->copy_bytes, p);
+}
+
+fz_status fz_model_index_plan(const void* head, uint64_t head_bytes, uint64_t file_bytes, fz_plan* p) {
+  if (!head || !p) return fail(FZ_ERR_ARGUMENT, "null argument");
+  if (!p->budget) return fail(FZ_ERR_ARGUMENT, "a plan without a device needs a budget");
+  fz_model m;
+  uint64_t needed = 0;
+  std::string msg;
+  const fz::GgufError e = fz::parse_gguf_index(static_cast<const uint8_t*>(head), head_bytes, m.index, needed, msg);
+  if (e == fz::GgufError::Truncated) {
+    g_index_needed = needed;
+    return fail(FZ_ERR_TRUNCATED, msg);
+  }
+  if (e != fz::GgufError::Ok) return fail(FZ_ERR_INDEX, msg);
+  fz_status st;
+  if ((st = describe(m))) return st;
+  (void)file_bytes;
+  weight_bytes_of(m, p->weight_bytes, p->copy_bytes);
+  return plan_batch(m.shape, p->weight_bytes + p->copy_bytes, p);
+}
+
 fz_status fz_model_free(fz_model* m) {
   if (m) {
     cudaSetDevice(m->dev->ordinal);
@@ -1245,8 +1392,7 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     const Layer& L = m->layers[l];
     // plan.cpp:335-336, rounded up to whole 32-slot chunks (the decode
     // kernel's tensor-map boxes never wrap).
-    const uint64_t ring = ((uint64_t)L.window + 512 + rollback + 31) / 32 * 32;
-    const uint32_t slots = (uint32_t)std::min<uint64_t>(context, ring);
+    const uint32_t slots = ring_slots(L.window, context, rollback);
     const uint64_t per_seq = (uint64_t)slots * s.kv_heads * s.head_dim;
     uint16_t *k = nullptr, *v = nullptr;
     if ((st = b->alloc(&k, per_seq * sequences * 2)) || (st = b->alloc(&v, per_seq * sequences * 2))) return st;

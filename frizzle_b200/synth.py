@@ -176,7 +176,18 @@ def _slice_job(args):
     return quantize_q4_0(x).tobytes()
 
 
-def write_model(path: str, shape: ModelShape = GEMMA3_1B, seed: int = 0, threads: int | None = None) -> None:
+def model_header(shape: ModelShape = GEMMA3_1B, seed: int = 0) -> tuple:
+    """The GGUF head ``write_model`` writes for (shape, seed) -- metadata and
+    tensor infos, padded to the data section -- and the whole file's size,
+    without generating the tensor data."""
+    w = _writer(None, shape, seed)
+    for name, dims, ttype, _ in tensor_plan(shape):
+        w.add_tensor(name, dims, ttype)
+    head = w._header()
+    return head, len(head) + w._next
+
+
+def _writer(path, shape: ModelShape, seed: int):
     w = gguf.GgufWriter(path)
     a = "gemma3."
     w.add("general.architecture", gguf.STRING, "gemma3")
@@ -198,6 +209,11 @@ def write_model(path: str, shape: ModelShape = GEMMA3_1B, seed: int = 0, threads
     w.add("tokenizer.ggml.tokens", gguf.ARRAY, (gguf.STRING, [f"t{i}" for i in range(shape.vocab)]))
     w.add("tokenizer.ggml.bos_token_id", gguf.U32, 2)
     w.add("tokenizer.ggml.eos_token_id", gguf.U32, 106)
+    return w
+
+
+def write_model(path: str, shape: ModelShape = GEMMA3_1B, seed: int = 0, threads: int | None = None) -> None:
+    w = _writer(path, shape, seed)
     plan = tensor_plan(shape)
     jobs = []
     for index, (name, dims, ttype, kind) in enumerate(plan):

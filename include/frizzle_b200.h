@@ -117,6 +117,30 @@ uint64_t fz_model_index_needed(void);
 fz_status fz_model_load_write(fz_model *model, uint64_t offset, const void *chunk, uint64_t bytes);
 fz_status fz_model_load_finish(fz_model *model);
 fz_status fz_model_info_get(const fz_model *model, fz_model_info *out);
+
+/* The residency plan for one batch on one GPU (residency::plan_residency and
+ * place_cache, src/core/residency/plan.cpp:321-419, restated for a B200's
+ * 180 GB and a batch of sequences): the device bytes of the weights (every
+ * tensor's bytes and the RoPE turns), of their f16 prefill copies, of the
+ * batch's scratch for `rows` token rows a step, and of its key/value rings
+ * (per sequence and layer: a window layer window + 512 + rollback slots
+ * rounded up to whole 32-slot chunks, a global layer `context` slots; f16
+ * keys and values), plus 64 MiB of slack.  In: `sequences` (1 .. 16; 0: the
+ * most that fit at `context`), `context` (0: the largest that fits, found by
+ * bisection between min(512, trained context) and the trained context, as
+ * place_cache finds the context offered, plan.cpp:373-383), `rollback`,
+ * `rows` (0: 4096), `budget` (bytes; 0 with a loaded model: the device's free
+ * memory now, the model's own bytes counted as already placed).  Out: the
+ * sequences and context chosen and the byte counts; FZ_ERR_FIT when even the
+ * shortest context does not fit (PlanError::ExceedsBudget). */
+typedef struct fz_plan {
+  uint32_t sequences, context, rollback, rows;
+  uint64_t budget;
+  uint64_t weight_bytes, copy_bytes, scratch_bytes, cache_bytes, total_bytes;
+} fz_plan;
+fz_status fz_model_plan(const fz_model *model, fz_plan *plan);
+/* The same from a file's index, without a device (a budget is required). */
+fz_status fz_model_index_plan(const void *head, uint64_t head_bytes, uint64_t file_bytes, fz_plan *plan);
 fz_status fz_model_free(fz_model *model);
 
 /* ------------------------------------------------------------------ sequences
