@@ -611,6 +611,16 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageArgs a) {
   for (uint32_t i = i0; i < a.zero_words; i += n) a.zero[i] = 0u;
 }
 
+__global__ void delay_kernel(uint32_t ns) {
+  uint64_t t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (uint32_t i = 0; i < (1u << 20); i++) {
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 >= ns) break;
+    __nanosleep(500);
+  }
+}
+
 __global__ void __launch_bounds__(64) publish_kernel(const PublishArgs a) {
   for (uint32_t i = threadIdx.x; i < a.record_words; i += blockDim.x) a.records_h[i] = a.records_d[i];
   if (threadIdx.x == 0) a.error_h[0] = *reinterpret_cast<const volatile uint32_t*>(a.error_d);
@@ -622,6 +632,11 @@ cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream) {
   const uint32_t words = std::max(std::max(a.id_words, a.zero_words), std::max(a.seed_words, 16u));
   const uint32_t blocks = std::min(64u, (words + 255u) / 256u);
   stage_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_delay(uint32_t ns, cudaStream_t stream) {
+  delay_kernel<<<1, 1, 0, stream>>>(ns);
   return cudaGetLastError();
 }
 

@@ -141,6 +141,10 @@ struct PublishArgs {
   uint32_t* error_h;
 };
 cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream);
+// One thread waits `ns` nanoseconds by the global timer (bounded): queued
+// ahead of a timed launch, it keeps the stream busy while the host submits
+// the launch, so that events around the launch bracket the kernel alone.
+cudaError_t launch_delay(uint32_t ns, cudaStream_t stream);
 cudaError_t launch_publish(const PublishArgs& a, cudaStream_t stream);
 
 }  // namespace fz

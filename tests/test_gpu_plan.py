@@ -28,7 +28,7 @@ def test_plan_matches_the_batch_it_sizes(gemma_model_path):
     counted = p.cache_bytes + p.scratch_bytes
     assert used <= counted + (64 << 20), (used, counted)
     assert used >= 0.9 * counted, (used, counted)
-    # A budget of what is free now minus 200 GB cannot fit: refused.
+    # A 1 GiB budget cannot hold even the weights: refused.
     q = _native.Plan(sequences=1, context=0, rollback=4096, rows=0, budget=1 << 30)
     assert lib.fz_model_plan(model.handle, C.byref(q)) == 5
     batch.free()
