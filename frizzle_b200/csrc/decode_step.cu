@@ -915,13 +915,15 @@ __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const fl
 // thread at a time when the fragments are one row quad.
 template <int MQ>
 __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const unsigned long long* src, uint32_t K,
-                                          uint32_t kb0, uint32_t nkb, uint32_t want) {
+                                          uint32_t kb0, uint32_t nkb, uint32_t want, float* bsum = nullptr) {
   const int tid = threadIdx.x, items = (int)nkb * 8;
   uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
   const volatile uint32_t* abort = reinterpret_cast<const volatile uint32_t*>(g_smem + a.lay.flags);
   constexpr int U = MQ == 1 ? 2 : 1;
+  // (warp-uniform trips: a lane past the items runs with zeros, so that the
+  // block sums' shuffles see every lane)
 #pragma unroll 1
-  for (int i0 = tid; i0 < items; i0 += U * kCT) {
+  for (int i0 = tid; i0 - (tid & 31) < items; i0 += U * kCT) {
     float4 v[U][MQ][4];
     const uint64_t t0 = now_ns();
 #pragma unroll 1
@@ -955,6 +957,25 @@ __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const
         break;
       }
       __nanosleep(it < 4 ? 64u : 256u);
+    }
+    if (bsum) {
+      // Each block's sum per row ([row][nkb]): a block's 32 values are the
+      // 8 consecutive items of 8 consecutive lanes, summed in a fixed order.
+#pragma unroll
+      for (int u = 0; u < U; u++) {
+        const int i = i0 + u * kCT;
+#pragma unroll
+        for (int q = 0; q < MQ; q++)
+#pragma unroll
+          for (int gp = 0; gp < 4; gp++) {
+            const float4 w = v[u][q][gp];
+            float p = add(add(w.x, w.y), add(w.z, w.w));
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) p = add(p, __shfl_xor_sync(0xffffffffu, p, o));
+            const int r = 4 * q + gp;
+            if ((threadIdx.x & 7) == 0 && i < items && r < (int)M) bsum[r * (int)nkb + (i >> 3)] = p;
+          }
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; u++) {
@@ -1632,7 +1653,7 @@ struct Consumer {
   static constexpr int R = 4 * MQ;        // rows of X the fragments carry
   static constexpr int C = 4 * MQ;        // columns of a warp's partial block
   const DecodeArgs& a;
-  uint32_t idx, kb_base, M, pos, W, pending, pslots, task_d, ph_kind, ph_l;
+  uint32_t idx, kb_base, kb_count, M, pos, W, pending, pslots, task_d, ph_kind, ph_l;
   unsigned long long wait_ns;   // thread 0: time waiting for tiles (trace)
   // Shared-memory regions (offsets from the launch, so no registers hold them).
   FZ_DEV const uint4* codes() const { return reinterpret_cast<const uint4*>(g_smem + a.lay.codes); }
@@ -1728,6 +1749,7 @@ struct Consumer {
     if (sync_dead()) return false;
     stamp(tl, trace_phase(kind), 1);
     kb_base = kb0;
+    kb_count = nkb;
     pending = 0;
     pslots = 0;
     ph_kind = kind;
@@ -1760,7 +1782,9 @@ struct Consumer {
     } else if (kind == kPhO) {
       attention_fragments<MQ>(a, M, o_splits, kb0, nkb, phase_epoch(serial(), l, kEpAttn));
     } else {
-      fragments_ll<MQ>(a, M, a.act_ll, a.ffn, kb0, nkb, phase_epoch(serial(), l, kPhGate));
+      // (a Q4_1 down projection: the activation's block sums for the correction, in `part`)
+      fragments_ll<MQ>(a, M, a.act_ll, a.ffn, kb0, nkb, phase_epoch(serial(), l, kPhGate),
+                       L.down_corr ? part() : nullptr);
     }
     cbar();
     stamp(tl, trace_phase(kind), 2);
@@ -1891,6 +1915,14 @@ struct Consumer {
         } else if (kind == kPhO) {
           a.y_attn[((size_t)task_d * M + tok) * Hd + n] = v;
         } else if (kind == kPhDown) {
+          const float* corr = a.layers[l].down_corr;
+          if (corr) {   // the Q4_1 correction over the slice's blocks
+            const float* c = corr + (size_t)n * (a.ffn / 32) + kb_base;
+            const float* bs = part() + tok * kb_count;
+            float cv = 0.f;
+            for (uint32_t j = 0; j < kb_count; j++) cv = __fmaf_rn(c[j], bs[j], cv);
+            v = add(v, cv);
+          }
           a.y_mlp[((size_t)task_d * M + tok) * Hd + n] = v;
         } else if (kind == kPhHead) {
           a.logits[(size_t)tok * a.head.n + n] = v;
@@ -2034,6 +2066,7 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
     Consumer<MQ> c{a};
     c.idx = 0;
     c.kb_base = 0;
+    c.kb_count = 0;
     c.M = a.m;
     c.pos = a.step->position;
     c.W = kDecodeSyncFixed + a.m * a.kv_heads;
@@ -2157,9 +2190,10 @@ bool decode_supported(uint32_t rows, uint32_t hidden, uint32_t ffn, uint32_t hea
   const DLayout ly = layout_for(MQ, MQ == 1 ? ring_slots<1>() : ring_slots<2>(), hidden, group,
                                 nkb_max(hidden, heads, ffn));
   // The norm stages two y slices at a time between xf and the gains; the
-  // output projection's folded attention slice fits rowbuf.
+  // output projection's folded attention slice fits rowbuf; a down slice's
+  // block sums (a Q4_1 correction, [rows][blocks]) fit the 4 MQ x 256 floats of `part`.
   return ly.total <= 227u * 1024u && layout_aligned(ly) && ly.gains - ly.xf >= 2u * rows * hidden * 4u &&
-         slice_kb(heads * kHd, kDecodeOSlices) * 32u <= hidden;
+         slice_kb(heads * kHd, kDecodeOSlices) * 32u <= hidden && slice_kb(ffn, kDecodeDownSlices) <= (uint32_t)kCT;
 }
 
 cudaError_t prepare_decode(uint32_t hidden, uint32_t ffn, uint32_t heads, uint32_t kv_heads) {

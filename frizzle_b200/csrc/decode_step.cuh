@@ -24,6 +24,10 @@ struct DecodeLayer {
   uint16_t *key_cache, *value_cache;
   uint64_t seq_stride;             // cache elements between sequences
   uint32_t slots, window;
+  // A Q4_1 down projection is held as its Q4_0 part (`down`) and the
+  // correction corr[row][block] = 8 d + m, added times the block's sum of
+  // the activation; null for a Q4_0 one.
+  const float* down_corr;
 };
 
 // A layer's TMA tensor maps (CUtensorMap) of its key and value caches, 4D

@@ -80,8 +80,15 @@ struct DevMatrix {
   Q4Matrix view() const { return Q4Matrix{codes, scales, n, k}; }
 };
 
+// GGML type ids of the formats the model reads.
+constexpr uint32_t kTypeF32 = 0, kTypeQ4_0 = 2, kTypeQ4_1 = 3, kTypeQ8_0 = 8;
+
 struct Layer {
   DevMatrix qkv, o, gate, up, down;
+  // A Q4_1 down projection (the pinned file's layers 0-2) is held as its
+  // Q4_0 part in `down` and the per-block correction 8 d + m [hidden][ffn/32].
+  uint32_t down_type = kTypeQ4_0;
+  float* down_corr = nullptr;
   float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn_norm = nullptr,
         *ffn_norm = nullptr, *post_ffw_norm = nullptr;
   float* turns = nullptr;
@@ -164,6 +171,10 @@ struct fz_model {
     uint64_t begin = 0, end = 0;   // the tensor's bytes in the file (absolute offsets)
     DevMatrix* mat = nullptr;      // a Q4_0 matrix ...
     uint32_t row0 = 0, k = 0;      //   ... its first row in `mat`, its row length
+    uint32_t type = kTypeQ4_0;     //   ... the file's format (Q4_1: split into Q4_0 and `corr`)
+    float* corr = nullptr;         //   ... a Q4_1 matrix's corrections [rows][k/32]
+    uint8_t* q8_codes = nullptr;   // or a Q8_0 table, repacked a row at a time
+    uint16_t* q8_scales = nullptr;
     float* gain = nullptr;         // or an f32 vector
     int group = -1;                // the layer product whose f16 copies it completes, or -1
     std::string name;
@@ -174,10 +185,14 @@ struct fz_model {
   uint32_t rows_done = 0;          // rows of the current matrix sink repacked
   uint8_t* stage = nullptr;        // bounded device staging of a matrix's partial row groups
   uint64_t stage_fill = 0;
+  uint8_t* stage_q4_0 = nullptr;   // a Q4_1 stage's row groups as Q4_0 blocks (Q4_1 files only)
   std::vector<DevMatrix*> groups;  // the layer products (f16 copies made once complete)
   std::vector<uint32_t> group_left;
   std::vector<Layer> layers;
-  DevMatrix embd;
+  DevMatrix embd;                  // the tied embedding and head (n, k; codes when Q4_0)
+  uint32_t embd_type = kTypeQ4_0;
+  uint8_t* embd_q8 = nullptr;      // a Q8_0 table: codes [vocab][hidden], scales [vocab][hidden/32]
+  uint16_t* embd_q8_scales = nullptr;
   float* output_norm = nullptr;
   bool finished = false;
   uint64_t weight_bytes = 0;
@@ -186,6 +201,7 @@ struct fz_model {
   ~fz_model() {
     for (void* p : allocations) cudaFree(p);
     if (stage) cudaFree(stage);
+    if (stage_q4_0) cudaFree(stage_q4_0);
   }
   template <typename T>
   fz_status alloc(T** p, size_t bytes) {
@@ -240,6 +256,8 @@ struct fz_batch {
   // kMaxTokens readout rows a head launch).
   fz::CaptureLayer* cap_layers = nullptr;
   float *ro_rows = nullptr, *ro_logits = nullptr;
+  float* head_x = nullptr;         // a Q8_0 head's normed rows [head_rows][hidden]
+  uint32_t head_rows = 0;
   unsigned long long *ro_argmax = nullptr, *ro_tile_best = nullptr;
   // Rows the per-row scratch holds (sequences x tokens of the widest step so
   // far); grown on demand, which drops the captured graphs.
@@ -373,15 +391,20 @@ fz_status describe(fz_model& m) {
   if (s.hidden % 64 || s.ffn % 64 || (s.heads * s.head_dim) % 64 || s.hidden > 8192)
     return fail(FZ_ERR_NOT_SUPPORTED, "widths must be multiples of 64 (hidden at most 8192)");
   const fz::GgufTensor* embd = ix.find("token_embd.weight");
-  if (!embd || embd->type != 2 || embd->dims.size() != 2 || embd->dims[0] != s.hidden)
-    return fail(FZ_ERR_ARCHITECTURE, "token_embd.weight missing or not Q4_0 [hidden, vocab]");
+  if (!embd || embd->dims.size() != 2 || embd->dims[0] != s.hidden)
+    return fail(FZ_ERR_ARCHITECTURE, "token_embd.weight missing or not [hidden, vocab]");
+  if (embd->type != kTypeQ4_0 && embd->type != kTypeQ8_0)
+    return fail(FZ_ERR_NOT_SUPPORTED, "token_embd.weight: type " + std::to_string(embd->type) + " (Q4_0 or Q8_0)");
+  m.embd_type = embd->type;
   s.vocab = (uint32_t)embd->dims[1];
   if (s.vocab % 16) return fail(FZ_ERR_NOT_SUPPORTED, "vocabulary not a multiple of 16");
   if (ix.find("output.weight")) return fail(FZ_ERR_NOT_SUPPORTED, "an untied output head");
+  // (type 3 names a down projection, which may be Q4_0 or Q4_1)
   auto need = [&](const std::string& name, uint32_t type, uint64_t d0, uint64_t d1) -> fz_status {
     const fz::GgufTensor* t = ix.find(name);
     if (!t) return fail(FZ_ERR_ARCHITECTURE, "missing tensor " + name);
-    if (t->type != type) return fail(FZ_ERR_NOT_SUPPORTED, name + ": type " + std::to_string(t->type));
+    const bool ok = type == kTypeQ4_1 ? (t->type == kTypeQ4_0 || t->type == kTypeQ4_1) : t->type == type;
+    if (!ok) return fail(FZ_ERR_NOT_SUPPORTED, name + ": type " + std::to_string(t->type));
     if (t->dims[0] != d0 || (d1 && (t->dims.size() != 2 || t->dims[1] != d1)))
       return fail(FZ_ERR_ARCHITECTURE, name + ": unexpected shape");
     return FZ_OK;
@@ -398,7 +421,7 @@ fz_status describe(fz_model& m) {
         (st = need(p + "attn_output.weight", 2, Q, s.hidden)) ||
         (st = need(p + "post_attention_norm.weight", 0, s.hidden, 0)) ||
         (st = need(p + "ffn_norm.weight", 0, s.hidden, 0)) || (st = need(p + "ffn_gate.weight", 2, s.hidden, s.ffn)) ||
-        (st = need(p + "ffn_up.weight", 2, s.hidden, s.ffn)) || (st = need(p + "ffn_down.weight", 2, s.ffn, s.hidden)) ||
+        (st = need(p + "ffn_up.weight", 2, s.hidden, s.ffn)) || (st = need(p + "ffn_down.weight", kTypeQ4_1, s.ffn, s.hidden)) ||
         (st = need(p + "post_ffw_norm.weight", 0, s.hidden, 0)))
       return st;
   }
@@ -422,7 +445,7 @@ fz_status place_model(fz_model& m) {
   const uint32_t Q = s.heads * s.head_dim, KV = s.kv_heads * s.head_dim;
   fz_status st;
   m.weight_bytes = 0;
-  auto add_matrix = [&](const std::string& name, DevMatrix& d, uint32_t row0, int group) {
+  auto add_matrix = [&](const std::string& name, DevMatrix& d, uint32_t row0, int group, float* corr = nullptr) {
     const fz::GgufTensor* t = m.index.find(name);
     fz_model::Sink k;
     k.begin = m.index.data_offset + t->offset;
@@ -430,6 +453,8 @@ fz_status place_model(fz_model& m) {
     k.mat = &d;
     k.row0 = row0;
     k.k = (uint32_t)t->dims[0];
+    k.type = t->type;
+    k.corr = corr;
     k.group = group;
     k.name = name;
     m.sinks.push_back(k);
@@ -446,8 +471,20 @@ fz_status place_model(fz_model& m) {
     m.sinks.push_back(k);
     return FZ_OK;
   };
-  if ((st = place_matrix(m, m.embd, s.vocab, s.hidden))) return st;
-  add_matrix("token_embd.weight", m.embd, 0, -1);
+  if (m.embd_type == kTypeQ8_0) {
+    m.embd.n = s.vocab;
+    m.embd.k = s.hidden;
+    if ((st = m.alloc(&m.embd_q8, (size_t)s.vocab * s.hidden)) ||
+        (st = m.alloc(&m.embd_q8_scales, (size_t)s.vocab * (s.hidden / 32) * 2)))
+      return st;
+    add_matrix("token_embd.weight", m.embd, 0, -1);
+    m.sinks.back().q8_codes = m.embd_q8;
+    m.sinks.back().q8_scales = m.embd_q8_scales;
+  } else {
+    if ((st = place_matrix(m, m.embd, s.vocab, s.hidden))) return st;
+    add_matrix("token_embd.weight", m.embd, 0, -1);
+  }
+  bool any_q4_1 = false;
   if ((st = add_gain("output_norm.weight", &m.output_norm))) return st;
   m.layers.resize(s.layers);
   for (uint32_t l = 0; l < s.layers; l++) {
@@ -467,7 +504,12 @@ fz_status place_model(fz_model& m) {
     add_matrix(p + "attn_output.weight", L.o, 0, g0 + 1);
     add_matrix(p + "ffn_gate.weight", L.gate, 0, g0 + 2);
     add_matrix(p + "ffn_up.weight", L.up, 0, g0 + 3);
-    add_matrix(p + "ffn_down.weight", L.down, 0, g0 + 4);
+    L.down_type = m.index.find(p + "ffn_down.weight")->type;
+    if (L.down_type == kTypeQ4_1) {
+      if ((st = m.alloc(&L.down_corr, (size_t)s.hidden * (s.ffn / 32) * 4))) return st;
+      any_q4_1 = true;
+    }
+    add_matrix(p + "ffn_down.weight", L.down, 0, g0 + 4, L.down_corr);
     if ((st = add_gain(p + "attn_norm.weight", &L.attn_norm)) || (st = add_gain(p + "attn_q_norm.weight", &L.q_norm)) ||
         (st = add_gain(p + "attn_k_norm.weight", &L.k_norm)) ||
         (st = add_gain(p + "post_attention_norm.weight", &L.post_attn_norm)) ||
@@ -496,21 +538,40 @@ fz_status place_model(fz_model& m) {
   std::sort(m.sinks.begin(), m.sinks.end(),
             [](const fz_model::Sink& a, const fz_model::Sink& b) { return a.begin < b.begin; });
   FZ_CUDA(cudaMalloc(&m.stage, kLoadStage));
+  if (any_q4_1) FZ_CUDA(cudaMalloc(&m.stage_q4_0, kLoadStage));
   m.cursor = 0;
   return FZ_OK;
 }
 
 // Repacks the whole 16-row groups the stage holds of the current matrix sink
 // and moves the remainder (part of a group) to the stage's start.
+// A Q8_0 table is repacked a whole row at a time instead; a Q4_1 matrix's
+// groups are first split into Q4_0 blocks and their corrections.
 fz_status drain_stage(fz_model& m, fz_model::Sink& k) {
-  const uint64_t group_bytes = 16ull * (k.k / 32) * 18;
+  const uint32_t kb = k.k / 32;
+  const bool q8 = k.type == kTypeQ8_0;
+  const uint64_t group_bytes = q8 ? (uint64_t)kb * 34 : 16ull * kb * (k.type == kTypeQ4_1 ? 20 : 18);
   const uint64_t groups = m.stage_fill / group_bytes;
   if (!groups) return FZ_OK;
   DevMatrix& d = *k.mat;
   const uint32_t row = k.row0 + m.rows_done;
-  FZ_CUDA(fz::launch_repack(m.stage, (uint32_t)(16 * groups), k.k, d.codes + (size_t)(row / 16) * (k.k / 64) * 32,
-                            d.scales + (size_t)(row / 16) * (k.k / 64) * 8, m.dev->stream));
-  m.rows_done += (uint32_t)(16 * groups);
+  const uint32_t rows = (uint32_t)(q8 ? groups : 16 * groups);
+  if (q8) {
+    fz_status st;
+    if ((st = fz_q8_0_repack(m.stage, rows, k.k, k.q8_codes + (size_t)row * k.k, k.q8_scales + (size_t)row * kb,
+                             m.dev->stream)))
+      return st;
+  } else {
+    const uint8_t* blocks = m.stage;
+    if (k.type == kTypeQ4_1) {
+      FZ_CUDA(fz::launch_q4_1_split(m.stage, (size_t)rows * kb, m.stage_q4_0, k.corr + (size_t)row * kb,
+                                    m.dev->stream));
+      blocks = m.stage_q4_0;
+    }
+    FZ_CUDA(fz::launch_repack(blocks, rows, k.k, d.codes + (size_t)(row / 16) * (k.k / 64) * 32,
+                              d.scales + (size_t)(row / 16) * (k.k / 64) * 8, m.dev->stream));
+  }
+  m.rows_done += rows;
   const uint64_t rest = m.stage_fill - groups * group_bytes;
   if (rest)   // (rest < one group <= the bytes just repacked: the ranges do not overlap)
     FZ_CUDA(cudaMemcpyAsync(m.stage, m.stage + groups * group_bytes, rest, cudaMemcpyDeviceToDevice, m.dev->stream));
@@ -524,7 +585,8 @@ fz_status finish_sink(fz_model& m, const fz_model::Sink& k) {
   if (k.mat && m.stage_fill) return fail(FZ_ERR_UPLOAD, "tensor " + k.name + " is not whole 16-row groups");
   if (k.group >= 0 && --m.group_left[k.group] == 0) {
     DevMatrix* d = m.groups[k.group];
-    FZ_CUDA(fz::launch_dequant_f16(d->view(), d->f16_hi, d->f16_lo, m.dev->stream));
+    // (a layer's Q4_1 down projection is a group of its own: its corrections are k.corr)
+    FZ_CUDA(fz::launch_dequant_f16(d->view(), d->f16_hi, d->f16_lo, m.dev->stream, k.corr));
   }
   m.rows_done = 0;
   m.stage_fill = 0;
@@ -560,6 +622,28 @@ fz_status run_matvec(fz::MatvecArgs a, int pro, int epi, cudaStream_t stream, bo
   a.k_split = s.ks;
   a.cluster = s.cluster;
   FZ_CUDA(fz::launch_matvec(a, pro, epi, stream, pdl));
+  return FZ_OK;
+}
+
+// The tied head over h.m rows with the norm prologue h.norm (logits into
+// h.out, the greedy keys max-reduced into h.head.argmax, cleared by the
+// caller).  A Q4_0 table streams through the head matvec with the norm and
+// argmax fused; a Q8_0 one (the pinned file's) as the norm's rows in f32,
+// the Q8_0 product eight rows a launch, then the argmax over each row.
+fz_status run_head(fz_batch& b, const fz::MatvecArgs& h, cudaStream_t st, bool pdl) {
+  const fz_model& m = *b.model;
+  if (m.embd_type != kTypeQ8_0) return run_matvec(h, fz::kPrologueNorm, fz::kEpilogueHead, st, pdl);
+  const uint32_t width = m.shape.hidden, vocab = m.shape.vocab;
+  if (h.m > b.head_rows || h.out_stride != vocab) return fail(FZ_ERR_ARGUMENT, "head rows outside its scratch");
+  FZ_CUDA(fz::launch_norm_f32(h, b.head_x, st, pdl));
+  fz_status stt;
+  for (uint32_t r0 = 0; r0 < h.m; r0 += 8) {
+    const uint32_t n = std::min<uint32_t>(8, h.m - r0);
+    if ((stt = fz_q8_0_matvec(m.embd_q8, m.embd_q8_scales, vocab, width, b.head_x + (size_t)r0 * width, n,
+                              h.out + (size_t)r0 * vocab, st)))
+      return stt;
+  }
+  FZ_CUDA(fz::launch_argmax_rows(h.out, h.m, vocab, h.head.argmax, st));
   return FZ_OK;
 }
 
@@ -673,7 +757,9 @@ fz_status plan_batch(const Shape& s, uint64_t fixed, fz_plan* p) {
 void weight_bytes_of(const fz_model& m, uint64_t& weights, uint64_t& copies) {
   const Shape& s = m.shape;
   weights = 0;
-  for (const auto& t : m.index.tensors) weights += t.bytes;
+  // Q4_0, Q8_0 and f32 tensors take their file bytes on the device; a Q4_1
+  // block (20 bytes) becomes a Q4_0 block and a 4-byte correction (22).
+  for (const auto& t : m.index.tensors) weights += t.bytes + (t.type == kTypeQ4_1 ? t.bytes / 10 : 0);
   weights += (uint64_t)s.layers * (s.head_dim / 2) * 4;
   const uint64_t Q = (uint64_t)s.heads * s.head_dim, KV = (uint64_t)s.kv_heads * s.head_dim;
   copies = (uint64_t)s.layers * ((Q + 2 * KV) * s.hidden + s.hidden * Q + 3ull * s.ffn * s.hidden) * 2 * 2;
@@ -785,7 +871,7 @@ fz_status enqueue_capture(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     h.out_stride = s.vocab;
     h.head.argmax = b.ro_argmax;
     fz_status stt;
-    if ((stt = run_matvec(h, fz::kPrologueNorm, fz::kEpilogueHead, st, pdl))) return stt;
+    if ((stt = run_head(b, h, st, pdl))) return stt;
     FZ_CUDA(fz::launch_readout_select(r, g0, n, false, st, pdl));
   }
   if (key.logits) {
@@ -851,6 +937,8 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     fz::EmbedArgs e{};
     e.step = b.dstep;
     e.table = m.embd.view();
+    e.q8_codes = m.embd_q8;
+    e.q8_scales = m.embd_q8_scales;
     e.ids = b.dids;
     e.records = b.records;
     e.seq_tokens = T;
@@ -948,7 +1036,7 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       h.out = b.logits;
       h.out_stride = s.vocab;
       h.head.argmax = b.argmax;
-      if ((stt = run_matvec(h, fz::kPrologueNorm, fz::kEpilogueHead, st, pdl))) return stt;
+      if ((stt = run_head(b, h, st, pdl))) return stt;
       fz::SelectArgs se{};
       se.step = b.dstep;
       se.logits = b.logits;
@@ -1182,6 +1270,7 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     d.out = b.y_mlp;
     d.out_stride = s.hidden;
     if ((stt = run_matvec(d, fz::kPrologueInput, fz::kEpilogueWrite, st, pdl))) return stt;
+    if (L.down_corr) FZ_CUDA(fz::launch_block_correction(b.act, M, s.ffn, L.down_corr, s.hidden, b.y_mlp, st));
   }
   (void)QW;
   if (key.logits) {
@@ -1204,7 +1293,7 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     h.out = b.logits;
     h.out_stride = s.vocab;
     h.head.argmax = b.argmax;
-    if ((stt = run_matvec(h, fz::kPrologueNorm, fz::kEpilogueHead, st, pdl))) return stt;
+    if ((stt = run_head(b, h, st, pdl))) return stt;
     fz::SelectArgs se{};
     se.step = b.dstep;
     se.logits = b.logits;
@@ -1408,6 +1497,8 @@ fz_status fz_model_load_finish(fz_model* m) {
   FZ_CUDA(cudaStreamSynchronize(m->dev->stream));
   FZ_CUDA(cudaFree(m->stage));
   m->stage = nullptr;
+  if (m->stage_q4_0) FZ_CUDA(cudaFree(m->stage_q4_0));
+  m->stage_q4_0 = nullptr;
   m->finished = true;
   return FZ_OK;
 }
@@ -1508,6 +1599,7 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
       d.gate = L.gate.view();
       d.up = L.up.view();
       d.down = L.down.view();
+      d.down_corr = L.down_corr;
       d.attn_norm = L.attn_norm;
       d.q_norm = L.q_norm;
       d.k_norm = L.k_norm;
@@ -1553,6 +1645,8 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
       (st = b->alloc(&b->ro_argmax, (size_t)fz::kMaxTokens * 8)) ||
       (st = b->alloc(&b->ro_tile_best, (size_t)fz::kMaxTokens * tiles * 64 * 8)) || (st = alloc_rows(*b, M)))
     return st;
+  b->head_rows = std::max<uint32_t>(sequences, fz::kMaxTokens);
+  if (m->embd_type == kTypeQ8_0 && (st = b->alloc(&b->head_x, (size_t)b->head_rows * s.hidden * 4))) return st;
   {
     std::vector<fz::CaptureLayer> v(s.layers);
     for (uint32_t l = 0; l < s.layers; l++) {

@@ -194,7 +194,10 @@ FZ_DEV void dequant_tile(unsigned char* tile, unsigned char* tile_lo, uint32_t r
 
 // One warp a (row group, block pair): lane (g, t) decodes its four code
 // words exactly as dequant_tile does and writes the f16 pairs to [n][k].
-__global__ void dequant_f16_kernel(Q4Matrix w, __half* hi, __half* lo) {
+// With `corr` (a Q4_1 matrix held as its Q4_0 part, corr[row][block] = 8 d
+// + m), each weight is (code - 8) d + corr in f32, split into f16 part and
+// remainder.
+__global__ void dequant_f16_kernel(Q4Matrix w, __half* hi, __half* lo, const float* corr) {
   const uint32_t nbp = w.k / 64, lane = threadIdx.x & 31;
   const uint32_t item = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (item >= (w.n / 16) * nbp) return;
@@ -221,8 +224,19 @@ __global__ void dequant_f16_kernel(Q4Matrix w, __half* hi, __half* lo) {
 #pragma unroll
     for (int j = 0; j < 4; j++) {
       const __half2 d = j < 2 ? dg : dg8;
-      const __half2 vh = __hmul2(c4[j], d);
       const size_t at = (size_t)rows[j] * w.k + cols[j];
+      if (corr) {
+        const float c = corr[(size_t)rows[j] * (w.k / 32) + cols[j] / 32];
+        const float2 cf = __half22float2(c4[j]), df = __half22float2(d);
+        const float v0 = __fadd_rn(__fmul_rn(cf.x, df.x), c), v1 = __fadd_rn(__fmul_rn(cf.y, df.y), c);
+        const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+        *reinterpret_cast<__half2*>(hi + at) = __halves2half2(h0, h1);
+        if (lo)
+          *reinterpret_cast<__half2*>(lo + at) = __halves2half2(__float2half_rn(__fsub_rn(v0, __half2float(h0))),
+                                                                  __float2half_rn(__fsub_rn(v1, __half2float(h1))));
+        continue;
+      }
+      const __half2 vh = __hmul2(c4[j], d);
       *reinterpret_cast<__half2*>(hi + at) = vh;
       if (lo) *reinterpret_cast<__half2*>(lo + at) = __hfma2(c4[j], d, __hneg2(vh));
     }
@@ -661,11 +675,11 @@ cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bo
                : launch_tiles<256, 1, 1, kGemmWrite, false>(a, stream, pdl);
 }
 
-cudaError_t launch_dequant_f16(const Q4Matrix& w, __half* hi, __half* lo, cudaStream_t stream) {
+cudaError_t launch_dequant_f16(const Q4Matrix& w, __half* hi, __half* lo, cudaStream_t stream, const float* corr) {
   if (!hi || w.k % 64 || w.n % 16) return cudaErrorInvalidValue;
   const size_t items = (size_t)(w.n / 16) * (w.k / 64);
   (void)cudaGetLastError();
-  dequant_f16_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(w, hi, lo);
+  dequant_f16_kernel<<<(unsigned)((items + 7) / 8), 256, 0, stream>>>(w, hi, lo, corr);
   return cudaGetLastError();
 }
 

@@ -46,7 +46,8 @@ cudaError_t launch_gemm(const GemmArgs& a, int epilogue, cudaStream_t stream, bo
 
 // The Q4_0 matrix as f16 [n][k]: hi = f16((code - 8) d), lo = the f16
 // remainder of the exact product (lo may be null).
-cudaError_t launch_dequant_f16(const Q4Matrix& w, __half* hi, __half* lo, cudaStream_t stream);
+cudaError_t launch_dequant_f16(const Q4Matrix& w, __half* hi, __half* lo, cudaStream_t stream,
+                               const float* corr = nullptr);
 
 // x -> f16 hi = f16(x), lo = f16(x - hi) (lo may be null).
 cudaError_t launch_split_f16(const float* x, size_t n, __half* hi, __half* lo, cudaStream_t stream);

@@ -3,6 +3,7 @@
 #include <algorithm>
 
 #include "kernels.cuh"
+#include "q4_device.cuh"
 
 namespace fz {
 namespace {
@@ -196,6 +197,16 @@ __global__ void embed_kernel(const EmbedArgs a) {
   const uint32_t token = a.step->fed ? a.records[seq * 4] : a.ids[i];
   const Q4Matrix& mat = a.table;
   if (token >= mat.n) return;
+  if (a.q8_codes) {
+    // Q8_0 (q8_0.wgsl's unpack): code x d in f32, then the scale.
+    const uint8_t* row = a.q8_codes + (size_t)token * mat.k;
+    const uint16_t* d = a.q8_scales + (size_t)token * (mat.k / 32);
+    float* o = a.hidden + (size_t)i * mat.k;
+    for (uint32_t j = threadIdx.x; j < mat.k; j += blockDim.x)
+      o[j] = mul(mul((float)(int8_t)row[j], f16_unpack(d[j / 32])), a.scale);
+    pdl_launch_dependents();
+    return;
+  }
   const uint32_t NBP = mat.k / 64, KB = mat.k / 32;
   const uint32_t rg = token / 16, rr = token % 16, g = rr % 8, hsel = rr / 8;
   for (uint32_t j = threadIdx.x; j < KB * 8; j += blockDim.x) {
@@ -611,6 +622,55 @@ __global__ void __launch_bounds__(256) stage_kernel(const StageArgs a) {
   for (uint32_t i = i0; i < a.zero_words; i += n) a.zero[i] = 0u;
 }
 
+__global__ void q4_1_split_kernel(const uint8_t* src, size_t blocks, uint8_t* dst, float* corr) {
+  for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < blocks; b += (size_t)gridDim.x * blockDim.x) {
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src + 20 * b);
+    const uint32_t dm = s32[0];
+    uint16_t* d16 = reinterpret_cast<uint16_t*>(dst + 18 * b);
+    d16[0] = (uint16_t)(dm & 0xffffu);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      d16[1 + 2 * i] = (uint16_t)(s32[1 + i] & 0xffffu);
+      d16[2 + 2 * i] = (uint16_t)(s32[1 + i] >> 16);
+    }
+    corr[b] = add(mul(8.0f, f16_unpack((uint16_t)(dm & 0xffffu))), f16_unpack((uint16_t)(dm >> 16)));
+  }
+}
+
+// A CTA: the block sums of every row of x into shared memory (32 values in
+// order), then each warp one output at a time over the blocks.
+__global__ void __launch_bounds__(256) block_correction_kernel(const float* x, uint32_t m, uint32_t k,
+                                                               const float* corr, uint32_t n, float* y) {
+  extern __shared__ float sums[];   // [m][k / 32]
+  const uint32_t kb = k / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (uint32_t i = threadIdx.x; i < m * kb; i += blockDim.x) {
+    const float* v = x + (size_t)(i / kb) * k + (i % kb) * 32;
+    float s = 0.f;
+    for (int j = 0; j < 32; j++) s = add(s, v[j]);
+    sums[i] = s;
+  }
+  __syncthreads();
+  for (uint32_t o = blockIdx.x * 8 + warp; o < n; o += gridDim.x * 8) {
+    const float* c = corr + (size_t)o * kb;
+    for (uint32_t r = 0; r < m; r++) {
+      float acc = 0.f;
+      for (uint32_t b = lane; b < kb; b += 32) acc = __fmaf_rn(c[b], sums[r * kb + b], acc);
+      acc = warp_sum(acc);
+      if (lane == 0) y[(size_t)r * n + o] = add(y[(size_t)r * n + o], acc);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const float* logits, uint32_t v, unsigned long long* argmax) {
+  const uint32_t r = blockIdx.y;
+  unsigned long long best = 0ull;
+  for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < v; t += gridDim.x * blockDim.x)
+    best = max(best, q4dev::head_key(logits[(size_t)r * v + t], t));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if ((threadIdx.x & 31) == 0 && best) atomicMax(argmax + r, best);
+}
+
 __global__ void delay_kernel(uint32_t ns) {
   uint64_t t0, t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
@@ -632,6 +692,30 @@ cudaError_t launch_stage(const StageArgs& a, cudaStream_t stream) {
   const uint32_t words = std::max(std::max(a.id_words, a.zero_words), std::max(a.seed_words, 16u));
   const uint32_t blocks = std::min(64u, (words + 255u) / 256u);
   stage_kernel<<<blocks, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_q4_1_split(const uint8_t* q4_1_blocks, size_t blocks, uint8_t* q4_0_blocks, float* corr,
+                              cudaStream_t stream) {
+  if (reinterpret_cast<uintptr_t>(q4_1_blocks) % 4 || reinterpret_cast<uintptr_t>(q4_0_blocks) % 2)
+    return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)std::min<size_t>((blocks + 255) / 256, 148 * 8);
+  q4_1_split_kernel<<<std::max(1u, grid), 256, 0, stream>>>(q4_1_blocks, blocks, q4_0_blocks, corr);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_correction(const float* x, uint32_t m, uint32_t k, const float* corr, uint32_t n, float* y,
+                                    cudaStream_t stream) {
+  const size_t smem = (size_t)m * (k / 32) * 4;
+  if (k % 32 || smem > 48 * 1024) return cudaErrorInvalidValue;
+  const unsigned grid = std::min(148u, (n + 7) / 8);
+  block_correction_kernel<<<grid, 256, smem, stream>>>(x, m, k, corr, n, y);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_rows(const float* logits, uint32_t m, uint32_t v, unsigned long long* argmax,
+                               cudaStream_t stream) {
+  argmax_rows_kernel<<<dim3(64, m), 256, 0, stream>>>(logits, v, argmax);
   return cudaGetLastError();
 }
 

@@ -52,8 +52,27 @@ struct EmbedArgs {
   float* hidden;
   unsigned long long* argmax;      // [seqs] cleared
   uint32_t seqs;
+  // A Q8_0 table instead (codes [n][k], scales [n][k/32] f16; `table` then
+  // gives only n and k), or null.
+  const uint8_t* q8_codes;
+  const uint16_t* q8_scales;
 };
 cudaError_t launch_embed(const EmbedArgs& a, cudaStream_t stream, bool pdl);
+
+// Q4_1 blocks (20 bytes: d, m, 16 code bytes) as Q4_0 blocks (18 bytes: d
+// and the same code bytes) plus a per-block correction c = 8 d + m: since
+// code x d + m = (code - 8) x d + (8 d + m), a Q4_1 product is the Q4_0
+// product over the same codes and scales plus c times the block's sum of x.
+cudaError_t launch_q4_1_split(const uint8_t* q4_1_blocks, size_t blocks, uint8_t* q4_0_blocks, float* corr,
+                              cudaStream_t stream);
+// y[r][o] += sum over blocks b of corr[o][b] x (the sum of x[r] over block b),
+// x [m][k] f32, corr [n][k/32], y [m][n] (the Q4_1 product's correction).
+cudaError_t launch_block_correction(const float* x, uint32_t m, uint32_t k, const float* corr, uint32_t n, float* y,
+                                    cudaStream_t stream);
+// argmax[r] = max over the row's logits of the head's key (largest logit,
+// ties to the lower token): `argmax` cleared first.
+cudaError_t launch_argmax_rows(const float* logits, uint32_t m, uint32_t v, unsigned long long* argmax,
+                               cudaStream_t stream);
 
 // Selection and the draw (topk.wgsl, draw.wgsl) over each sequence's logits.
 struct SelectArgs {

@@ -622,6 +622,22 @@ __global__ void __launch_bounds__(kThreads) norm_f16_kernel(const MatvecArgs a, 
   pdl_launch_dependents();
 }
 
+// The norm prologue's rows as f32 (CTA i: the row the prologue would read for
+// slot i), for a product that takes f32 x (the Q8_0 head).
+__global__ void __launch_bounds__(kThreads) norm_f32_kernel(const MatvecArgs a, float* out) {
+  __shared__ __align__(16) float rowbuf[8192];
+  __shared__ float part[kThreads];
+  __shared__ float stat[2 * kMaxTokens];
+  pdl_wait();
+  NormArgs n = a.norm;
+  n.row_of_token_offset = a.norm.row_of_token_offset + blockIdx.x * a.norm.row_of_token_stride;
+  n.row_of_token_stride = 1;
+  norm_rows_cta(a, n, 1, rowbuf, part, stat, true);
+  const int W = (int)n.width;
+  for (int i = threadIdx.x; i < W; i += kThreads) out[(size_t)blockIdx.x * W + i] = rowbuf[i];
+  pdl_launch_dependents();
+}
+
 // QK-norm, RoPE and the KV append for many rows: one warp a (row, head).
 __global__ void __launch_bounds__(kThreads) rope_rows_kernel(const MatvecArgs a) {
   pdl_wait();
@@ -876,6 +892,13 @@ cudaError_t launch_norm_f16(const MatvecArgs& a, __half* out_hi, __half* out_lo,
   MatvecArgs copy = a;
   void* args[] = {&copy, &out_hi, &out_lo};
   return launch_plain((const void*)norm_f16_kernel, dim3(a.m), dim3(kThreads), stream, pdl, args);
+}
+
+cudaError_t launch_norm_f32(const MatvecArgs& a, float* out, cudaStream_t stream, bool pdl) {
+  if (a.norm.width > 8192 || a.norm.width % 4 || a.m == 0) return cudaErrorInvalidValue;
+  MatvecArgs copy = a;
+  void* args[] = {&copy, &out};
+  return launch_plain((const void*)norm_f32_kernel, dim3(a.m), dim3(kThreads), stream, pdl, args);
 }
 
 cudaError_t launch_rope_rows(const MatvecArgs& a, cudaStream_t stream, bool pdl) {

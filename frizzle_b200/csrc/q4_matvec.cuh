@@ -109,6 +109,9 @@ cudaError_t launch_matvec(const MatvecArgs& a, int prologue, int epilogue, cudaS
 // f16 hi/lo, and QK-norm/RoPE/KV append per (row, head) over a.out's raw QKV.
 cudaError_t launch_norm_f16(const MatvecArgs& a, __half* out_hi, __half* out_lo, cudaStream_t stream, bool pdl);
 cudaError_t launch_rope_rows(const MatvecArgs& a, cudaStream_t stream, bool pdl);
+// The norm prologue's rows as f32 [m][width] (CTA i the row the prologue
+// reads for slot i), with no product after it.
+cudaError_t launch_norm_f32(const MatvecArgs& a, float* out, cudaStream_t stream, bool pdl);
 cudaError_t launch_repack(const uint8_t* file_blocks, uint32_t n, uint32_t k, uint4* codes, uint2* scales,
                           cudaStream_t stream);
 cudaError_t launch_dequant_rows(const Q4Matrix& mat, const uint32_t* rows, uint32_t count, float scale,

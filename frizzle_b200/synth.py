@@ -20,7 +20,7 @@ from __future__ import annotations
 import os
 import tempfile
 from concurrent.futures import ThreadPoolExecutor
-from dataclasses import dataclass, asdict
+from dataclasses import asdict, dataclass, replace
 
 import numpy as np
 
@@ -42,6 +42,11 @@ class ModelShape:
     rope_local: float = 1e4
     eps: float = 1e-6
     context: int = 32768
+    # "q4_0": every linear and the tied embedding Q4_0.  "pinned": the
+    # pinned file's mix (docs/architecture/logical-overview.md:63-64): the
+    # tied embedding Q8_0, ffn_down Q4_1 in the first three layers, the
+    # rest Q4_0.
+    mix: str = "q4_0"
 
     def is_global(self, layer: int) -> bool:
         return layer % self.pattern == self.pattern - 1
@@ -58,7 +63,10 @@ class ModelShape:
         return self.kv_heads * self.head_dim
 
     def tag(self) -> str:
-        return "_".join(str(v).replace(".", "p") for v in asdict(self).values())
+        vals = asdict(self)
+        if vals["mix"] == "q4_0":
+            del vals["mix"]   # (the Q4_0 files keep their names)
+        return "_".join(str(v).replace(".", "p") for v in vals.values())
 
 
 GEMMA3_1B = ModelShape(layers=26, hidden=1152, ffn=6912, heads=4, kv_heads=1,
@@ -68,6 +76,9 @@ GEMMA3_1B = ModelShape(layers=26, hidden=1152, ffn=6912, heads=4, kv_heads=1,
 # window layers, K a multiple of 64 for every product.
 TINY = ModelShape(layers=7, hidden=512, ffn=1024, heads=4, kv_heads=1,
                   head_dim=256, vocab=4096, window=16, context=4096)
+# The same shapes with the pinned file's format mix.
+GEMMA3_1B_PINNED = replace(GEMMA3_1B, mix="pinned")
+TINY_PINNED = replace(TINY, mix="pinned")
 
 SLICE = 1 << 22
 
@@ -91,6 +102,41 @@ def quantize_q4_0(x: np.ndarray) -> np.ndarray:
     out = np.empty((b.shape[0], 18), dtype=np.uint8)
     out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
     out[:, 2:] = q[:, :16] | (q[:, 16:] << 4)
+    return out.reshape(-1)
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    """Q8_0 blocks (fp16 scale d, then 32 signed codes) of a float32 array:
+    per block of 32, d = (largest magnitude) / 127 and each code is x / d
+    rounded half away from zero; a block of zeros has d = 0, codes 0.  Weight
+    j is code j x d (``src/core/formats/q8_0/q8_0.h:19-21``)."""
+    b = x.reshape(-1, 32).astype(np.float32, copy=False)
+    d = np.abs(b).max(axis=1) / np.float32(127.0)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(d[:, None] != 0, np.round(b / d[:, None]), 0)
+    q = np.clip(q, -127, 127).astype(np.int8)
+    out = np.empty((b.shape[0], 34), dtype=np.uint8)
+    out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:] = q.view(np.uint8)
+    return out.reshape(-1)
+
+
+def quantize_q4_1(x: np.ndarray) -> np.ndarray:
+    """Q4_1 blocks (fp16 scale d, fp16 minimum m, then 16 code bytes) of a
+    float32 array: per block of 32, m = the smallest value, d = (largest -
+    m) / 15, each code (x - m) / d rounded to nearest and clamped to [0, 15];
+    byte j holds code j low and code j + 16 high.  Weight j is code j x d + m
+    (``src/core/formats/q4_1/q4_1.h:20-23``)."""
+    b = x.reshape(-1, 32).astype(np.float32, copy=False)
+    lo, hi = b.min(axis=1), b.max(axis=1)
+    d = (hi - lo) / np.float32(15.0)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        q = np.where(d[:, None] != 0, np.round((b - lo[:, None]) / d[:, None]), 0)
+    q = np.clip(q, 0, 15).astype(np.uint8)
+    out = np.empty((b.shape[0], 20), dtype=np.uint8)
+    out[:, 0:2] = d.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 2:4] = lo.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    out[:, 4:] = q[:, :16] | (q[:, 16:] << 4)
     return out.reshape(-1)
 
 
@@ -145,9 +191,12 @@ def random_q4_1(rows: int, k: int, seed: int, scale_sigma: float = 0.005) -> np.
 def tensor_plan(shape: ModelShape):
     """(name, dims innermost first, ggml type, kind) in file order."""
     H, F, Q, KV, D = shape.hidden, shape.ffn, shape.q_width, shape.kv_width, shape.head_dim
-    plan = [("token_embd.weight", (H, shape.vocab), gguf.TYPE_Q4_0, "linear")]
+    pinned = shape.mix == "pinned"
+    embd = (gguf.TYPE_Q8_0, "q8_0") if pinned else (gguf.TYPE_Q4_0, "linear")
+    plan = [("token_embd.weight", (H, shape.vocab), embd[0], embd[1])]
     for l in range(shape.layers):
         p = f"blk.{l}."
+        down = (gguf.TYPE_Q4_1, "q4_1") if pinned and l < 3 else (gguf.TYPE_Q4_0, "linear")
         plan += [
             (p + "attn_norm.weight", (H,), gguf.TYPE_F32, "norm"),
             (p + "attn_q.weight", (H, Q), gguf.TYPE_Q4_0, "linear"),
@@ -160,7 +209,7 @@ def tensor_plan(shape: ModelShape):
             (p + "ffn_norm.weight", (H,), gguf.TYPE_F32, "norm"),
             (p + "ffn_gate.weight", (H, F), gguf.TYPE_Q4_0, "linear"),
             (p + "ffn_up.weight", (H, F), gguf.TYPE_Q4_0, "linear"),
-            (p + "ffn_down.weight", (F, H), gguf.TYPE_Q4_0, "linear"),
+            (p + "ffn_down.weight", (F, H), down[0], down[1]),
             (p + "post_ffw_norm.weight", (H,), gguf.TYPE_F32, "norm"),
         ]
     plan.append(("output_norm.weight", (H,), gguf.TYPE_F32, "norm"))
@@ -173,6 +222,10 @@ def _slice_job(args):
     if kind == "norm":
         return (np.float32(1.0) + rng.standard_normal(count, dtype=np.float32) * np.float32(0.1)).tobytes()
     x = rng.standard_normal(count, dtype=np.float32) * np.float32(0.02)
+    if kind == "q8_0":
+        return quantize_q8_0(x).tobytes()
+    if kind == "q4_1":
+        return quantize_q4_1(x).tobytes()
     return quantize_q4_0(x).tobytes()
 
 

@@ -86,6 +86,8 @@ def _declare(L):
     L.oracle_capture_slots.restype = C.c_int64
     L.oracle_step.argtypes = [P, C.c_uint32, C.c_int, U32P, P, P, P]
     L.oracle_threads.restype = C.c_int
+    L.oracle_ctx_set_types.argtypes = [P, C.c_int, P]
+    L.oracle_ctx_set_types.restype = C.c_int
     L.oracle_set_threads.argtypes = [C.c_int]
 
 
@@ -202,6 +204,13 @@ class OracleModel:
         self.ctx = lib().oracle_ctx_new(C.byref(self.cshape), self._ptr("token_embd.weight"),
                                         self._ptr("output_norm.weight"), arr, context, rollback)
         self.capture_floats = lib().oracle_capture_floats(C.byref(self.cshape))
+        # The tensors' formats (the pinned file's Q8_0 embedding, Q4_1 ffn_down).
+        embd = self.index.tensors["token_embd.weight"].ggml_type
+        downs = np.array([self.index.tensors[f"blk.{l}.ffn_down.weight"].ggml_type for l in range(s.layers)],
+                         dtype=np.int32)
+        if embd != 2 or np.any(downs != 2):
+            if lib().oracle_ctx_set_types(self.ctx, embd, downs.ctypes.data) != 0:
+                raise ValueError("a tensor format the oracle does not restate")
 
     def tensor(self, name: str) -> np.ndarray:
         a, b = self.index.tensor_range(name)

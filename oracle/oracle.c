@@ -578,7 +578,9 @@ typedef struct {
 
 typedef struct {
     oracle_shape s;
-    const uint8_t *token_embd;  /* Q4_0, tied head */
+    const uint8_t *token_embd;  /* tied head; GGUF type embd_type (Q4_0 unless set) */
+    int embd_type;
+    int *down_type;             /* each layer's ffn_down GGUF type (Q4_0 unless set) */
     const float *output_norm;
     oracle_layer *layer;
     uint32_t *slots;            /* ring slots per layer */
@@ -594,6 +596,9 @@ EXPORT oracle_ctx *oracle_ctx_new(const oracle_shape *s, const uint8_t *token_em
     oracle_ctx *c = calloc(1, sizeof(*c));
     c->s = *s;
     c->token_embd = token_embd;
+    c->embd_type = 2;
+    c->down_type = calloc(s->layers, sizeof(int));
+    for (int l = 0; l < s->layers; l++) c->down_type[l] = 2;
     c->output_norm = output_norm;
     c->layer = calloc(s->layers, sizeof(oracle_layer));
     c->slots = calloc(s->layers, sizeof(uint32_t));
@@ -625,9 +630,24 @@ EXPORT oracle_ctx *oracle_ctx_new(const oracle_shape *s, const uint8_t *token_em
 EXPORT void oracle_ctx_free(oracle_ctx *c) {
     if (!c) return;
     for (int l = 0; l < c->s.layers; l++) { free(c->kc[l]); free(c->vc[l]); }
-    free(c->kc); free(c->vc); free(c->slots); free(c->layer);
+    free(c->kc); free(c->vc); free(c->slots); free(c->layer); free(c->down_type);
     free(c->turns_global); free(c->turns_local);
     free(c);
+}
+
+/* The pinned file's mix (docs/architecture/logical-overview.md:63-64): the
+ * tied embedding's and each layer's ffn_down GGUF types (2 Q4_0, 3 Q4_1,
+ * 8 Q8_0); the reference reads every format through the one matmul and
+ * gather over the format's unpack (formats/format.h).  Returns -1 for a
+ * type not restated. */
+EXPORT int oracle_ctx_set_types(oracle_ctx *c, int embd_type, const int *down_types) {
+    unpack_fn u;
+    if (!format_of(embd_type, &u)) return -1;
+    for (int l = 0; l < c->s.layers; l++)
+        if (!format_of(down_types[l], &u)) return -1;
+    c->embd_type = embd_type;
+    for (int l = 0; l < c->s.layers; l++) c->down_type[l] = down_types[l];
+    return 0;
 }
 
 EXPORT uint32_t oracle_ctx_slots(const oracle_ctx *c, int layer) { return c->slots[layer]; }
@@ -690,10 +710,12 @@ EXPORT void oracle_step(oracle_ctx *c, uint32_t position, int tokens, const uint
     for (int l = 0; cap && l < s->layers; l++) oracle_capture_slots(s, l, slot[l], &keys[l]);
     /* embed (gather.wgsl:25-48), scale sqrt(width) in f32 (gemma3.cpp:105) */
     float scale = sqrtf((float)H);
+    unpack_fn embd_unpack;
+    const int embd_bytes = format_of(c->embd_type, &embd_unpack);
     for (int t = 0; t < T; t++) {
         float w[32];
         for (int g = 0; g < H / 32; g++) {
-            oracle_q4_0_unpack(c->token_embd + ((int64_t)ids[t] * (H / 32) + g) * 18, w);
+            embd_unpack(c->token_embd + ((int64_t)ids[t] * (H / 32) + g) * embd_bytes, w);
             for (int i = 0; i < 32; i++) hidden[(int64_t)t * H + g * 32 + i] = w[i] * scale;
         }
     }
@@ -760,14 +782,14 @@ EXPORT void oracle_step(oracle_ctx *c, uint32_t position, int tokens, const uint
         oracle_gated(L->gate, L->up, F, H, normed, T, act);
         oracle_edit_apply(edit_table, (uint32_t)l, position, T, F, act);
         if (lc) memcpy(cap + slot[l][0], act + (int64_t)(T - 1) * F, sizeof(float) * F);
-        oracle_matmul(L->down, H, F, act, T, output);
+        oracle_matmul_fmt(c->down_type[l], L->down, H, F, act, T, output);
     }
     if (logits_out) {
         float *x = hidden + (int64_t)(T - 1) * H;
         float fin[8192];
         oracle_norm_row(x, output + (int64_t)(T - 1) * H, c->layer[s->layers - 1].post_ffw_norm, c->output_norm, H,
                         s->eps, fin, cap ? cap + slot[s->layers - 1][3] : NULL);
-        oracle_matmul(c->token_embd, s->vocab, H, fin, 1, logits_out);
+        oracle_matmul_fmt(c->embd_type, c->token_embd, s->vocab, H, fin, 1, logits_out);
     }
     if (cap) {
         const int L = s->layers;
@@ -787,7 +809,7 @@ EXPORT void oracle_step(oracle_ctx *c, uint32_t position, int tokens, const uint
             float xr[8192], fin[8192];
             memcpy(xr, cap + slot[l + 1][1], sizeof(float) * H);
             oracle_norm_row(xr, NULL, NULL, c->output_norm, H, s->eps, fin, NULL);
-            oracle_matmul(c->token_embd, s->vocab, H, fin, 1, lrow);
+            oracle_matmul_fmt(c->embd_type, c->token_embd, s->vocab, H, fin, 1, lrow);
             oracle_topk64(lrow, s->vocab, (uint32_t *)(cap + slot[l][7]));
         }
         free(lrow);

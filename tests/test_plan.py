@@ -94,3 +94,20 @@ def test_refusals():
     assert plan(180 << 30, sequences=17)[0] == 1
     assert plan(180 << 30, context=S.context + 1)[0] == 1
     assert plan(0)[0] == 1   # no device: a budget is required
+
+
+def test_pinned_mix_weights():
+    # The pinned file's Q8_0 embedding takes its file bytes on the device; each
+    # Q4_1 block of ffn_down (20 bytes) becomes a Q4_0 block and a 4-byte
+    # correction (22).
+    P = synth.GEMMA3_1B_PINNED
+    head, _ = synth.model_header(P)
+    idx = gguf.read_index(head)
+    q4_1 = [t for t in idx.tensors.values() if t.ggml_type == gguf.TYPE_Q4_1]
+    assert len(q4_1) == 3 and idx.tensors["token_embd.weight"].ggml_type == gguf.TYPE_Q8_0
+    weights = sum(t.nbytes for t in idx.tensors.values()) + sum(t.nbytes // 10 for t in q4_1)
+    weights += P.layers * (P.head_dim // 2) * 4
+    st, p = plan(180 << 30, shape=P)
+    assert st == 0, _native.load().fz_last_error()
+    assert p.weight_bytes == weights
+    assert p.copy_bytes == 2_791_047_168
