@@ -153,6 +153,8 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   o += 4u * 8u;
   L.kvstate = o;
   o += 4u * 4u;
+  L.corr = o;   // the down phase's Q4_1 corrections (pointer) and its block count
+  o += 16u;
   L.total = o;
   return L;
 }
@@ -163,7 +165,7 @@ __host__ __device__ inline bool layout_aligned(const DLayout& L) {
   return L.codes % 128 == 0 && L.scales % 128 == 0 && L.full % 8 == 0 && L.empty % 8 == 0 && L.uni % 128 == 0 &&
          L.xf % 16 == 0 && L.rowbuf % 16 == 0 && L.part % 16 == 0 && L.stat % 16 == 0 && L.red % 16 == 0 &&
          L.task_rg % 4 == 0 && L.best % 8 == 0 && L.flags % 4 == 0 && L.gains % 16 == 0 && L.tags % 4 == 0 &&
-         L.uses % 4 == 0 && L.kvbar % 8 == 0 && L.kvstate % 4 == 0 && L.kvbuf % 1024 == 0;
+         L.uses % 4 == 0 && L.kvbar % 8 == 0 && L.kvstate % 4 == 0 && L.corr % 8 == 0 && L.kvbuf % 1024 == 0;
 }
 
 // ------------------------------------------------------------ primitives
@@ -915,15 +917,13 @@ __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const fl
 // thread at a time when the fragments are one row quad.
 template <int MQ>
 __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const unsigned long long* src, uint32_t K,
-                                          uint32_t kb0, uint32_t nkb, uint32_t want, float* bsum = nullptr) {
+                                          uint32_t kb0, uint32_t nkb, uint32_t want) {
   const int tid = threadIdx.x, items = (int)nkb * 8;
   uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
   const volatile uint32_t* abort = reinterpret_cast<const volatile uint32_t*>(g_smem + a.lay.flags);
   constexpr int U = MQ == 1 ? 2 : 1;
-  // (warp-uniform trips: a lane past the items runs with zeros, so that the
-  // block sums' shuffles see every lane)
 #pragma unroll 1
-  for (int i0 = tid; i0 - (tid & 31) < items; i0 += U * kCT) {
+  for (int i0 = tid; i0 < items; i0 += U * kCT) {
     float4 v[U][MQ][4];
     const uint64_t t0 = now_ns();
 #pragma unroll 1
@@ -958,25 +958,6 @@ __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const
       }
       __nanosleep(it < 4 ? 64u : 256u);
     }
-    if (bsum) {
-      // Each block's sum per row ([row][nkb]): a block's 32 values are the
-      // 8 consecutive items of 8 consecutive lanes, summed in a fixed order.
-#pragma unroll
-      for (int u = 0; u < U; u++) {
-        const int i = i0 + u * kCT;
-#pragma unroll
-        for (int q = 0; q < MQ; q++)
-#pragma unroll
-          for (int gp = 0; gp < 4; gp++) {
-            const float4 w = v[u][q][gp];
-            float p = add(add(w.x, w.y), add(w.z, w.w));
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) p = add(p, __shfl_xor_sync(0xffffffffu, p, o));
-            const int r = 4 * q + gp;
-            if ((threadIdx.x & 7) == 0 && i < items && r < (int)M) bsum[r * (int)nkb + (i >> 3)] = p;
-          }
-      }
-    }
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const int i = i0 + u * kCT;
@@ -1002,6 +983,35 @@ __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const
           dst[k] = make_uint4(col[2 * k].x, col[2 * k].y, col[2 * k + 1].x, col[2 * k + 1].y);
       }
     }
+  }
+}
+
+// Each row's sum over each block of the fragments just staged (hi + lo of
+// its 32 values, in item order), into sums[row][block] for rows < M and
+// blocks < nkb: the activation's block sums a Q4_1 product's correction
+// takes.  A thread a (row, block); the caller's barrier precedes and follows.
+template <int MQ>
+__device__ __noinline__ void block_sums(const DecodeArgs& a, uint32_t M, uint32_t nkb, float* sums) {
+  const uint4* xf = reinterpret_cast<const uint4*>(g_smem + a.lay.xf);
+#pragma unroll 1
+  for (uint32_t w = threadIdx.x; w < M * nkb; w += kCT) {
+    const uint32_t r = w / nkb, kb = w % nkb, q = r / 4, gp = r % 4;
+    float s = 0.f;
+#pragma unroll 1
+    for (uint32_t h = 0; h < 2; h++)
+#pragma unroll
+      for (uint32_t tq = 0; tq < 4; tq++) {
+        // the item's four uint4 for row quad q: (hi halves, lo halves) of row 4q + gp at [gp]
+        const uint4 v = xf[(((kb * 2 + h) * MQ + q) * 32 + tq * 8) / 2 + gp];
+        const __half2* hi = reinterpret_cast<const __half2*>(&v.x);
+        const __half2* lo = reinterpret_cast<const __half2*>(&v.z);
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+          const float2 fh = __half22float2(hi[e]), fl = __half22float2(lo[e]);
+          s = add(s, add(add(fh.x, fl.x), add(fh.y, fl.y)));
+        }
+      }
+    sums[r * nkb + kb] = s;
   }
 }
 
@@ -1647,13 +1657,37 @@ __device__ __noinline__ void attention_fragments(const DecodeArgs& a, uint32_t M
 
 // ------------------------------------------------------------ consumers
 
+// A Q4_1 down projection: each output a flush wrote, plus the correction
+// over the slice's blocks (the sum over blocks j of corr[n][j] x the row's
+// block sum j, in `part`), by the thread that wrote it (the flush's item
+// order: `pending` tasks of 16 rows x M tokens).
+__device__ __noinline__ void add_correction(const DecodeArgs& a, uint32_t M, uint32_t pending, uint32_t kb_base,
+                                            uint32_t task_d) {
+  const float* corr = *reinterpret_cast<const float* const*>(g_smem + a.lay.corr);
+  const uint32_t nkb = *reinterpret_cast<const uint32_t*>(g_smem + a.lay.corr + 8);
+  const uint32_t* task_rg = reinterpret_cast<const uint32_t*>(g_smem + a.lay.task_rg);
+  const float* part = reinterpret_cast<const float*>(g_smem + a.lay.part);
+  const int per_task = 16 * (int)M, total = (int)pending * per_task;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < total; i += kCT) {
+    const int slot = i / per_task, rest = i % per_task, tok = rest / 16, row = rest % 16;
+    const uint32_t n = task_rg[slot] * 16 + row;
+    const float* c = corr + (size_t)n * (a.ffn / 32) + kb_base;
+    const float* bs = part + tok * nkb;
+    float cv = 0.f;
+    for (uint32_t j = 0; j < nkb; j++) cv = __fmaf_rn(c[j], bs[j], cv);
+    float* y = a.y_mlp + ((size_t)task_d * M + tok) * a.hidden + n;
+    *y = add(*y, cv);
+  }
+}
+
 template <int MQ>
 struct Consumer {
   static constexpr uint32_t S = ring_slots<MQ>();
   static constexpr int R = 4 * MQ;        // rows of X the fragments carry
   static constexpr int C = 4 * MQ;        // columns of a warp's partial block
   const DecodeArgs& a;
-  uint32_t idx, kb_base, kb_count, M, pos, W, pending, pslots, task_d, ph_kind, ph_l;
+  uint32_t idx, kb_base, M, pos, W, pending, pslots, task_d, ph_kind, ph_l;
   unsigned long long wait_ns;   // thread 0: time waiting for tiles (trace)
   // Shared-memory regions (offsets from the launch, so no registers hold them).
   FZ_DEV const uint4* codes() const { return reinterpret_cast<const uint4*>(g_smem + a.lay.codes); }
@@ -1725,7 +1759,12 @@ struct Consumer {
       pg = L.post_attn_norm;
       gain = L.ffn_norm;
     } else if (kind == kPhDown) {
-      // (no counter: the activation words are polled)
+      // (no counter: the activation words are polled; a Q4_1 projection's
+      // corrections and the slice's block count go to shared memory now)
+      if (tid == 0) {
+        *reinterpret_cast<const float**>(g_smem + a.lay.corr) = L.down_corr;
+        *reinterpret_cast<uint32_t*>(g_smem + a.lay.corr + 8) = nkb;
+      }
     } else {
       ctr = sync_of(Ln - 1) + kSyncDown;
       target = active_ctas(L.down.n / 16, kDecodeDownSlices, G);
@@ -1749,7 +1788,6 @@ struct Consumer {
     if (sync_dead()) return false;
     stamp(tl, trace_phase(kind), 1);
     kb_base = kb0;
-    kb_count = nkb;
     pending = 0;
     pslots = 0;
     ph_kind = kind;
@@ -1782,11 +1820,14 @@ struct Consumer {
     } else if (kind == kPhO) {
       attention_fragments<MQ>(a, M, o_splits, kb0, nkb, phase_epoch(serial(), l, kEpAttn));
     } else {
-      // (a Q4_1 down projection: the activation's block sums for the correction, in `part`)
-      fragments_ll<MQ>(a, M, a.act_ll, a.ffn, kb0, nkb, phase_epoch(serial(), l, kPhGate),
-                       L.down_corr ? part() : nullptr);
+      fragments_ll<MQ>(a, M, a.act_ll, a.ffn, kb0, nkb, phase_epoch(serial(), l, kPhGate));
     }
     cbar();
+    if (kind == kPhDown && *reinterpret_cast<const float* const*>(g_smem + a.lay.corr)) {
+      // A Q4_1 down projection: the activation's block sums for its correction.
+      block_sums<MQ>(a, M, nkb, part());
+      cbar();
+    }
     stamp(tl, trace_phase(kind), 2);
     zero_acc();
     return true;
@@ -1915,14 +1956,6 @@ struct Consumer {
         } else if (kind == kPhO) {
           a.y_attn[((size_t)task_d * M + tok) * Hd + n] = v;
         } else if (kind == kPhDown) {
-          const float* corr = a.layers[l].down_corr;
-          if (corr) {   // the Q4_1 correction over the slice's blocks
-            const float* c = corr + (size_t)n * (a.ffn / 32) + kb_base;
-            const float* bs = part() + tok * kb_count;
-            float cv = 0.f;
-            for (uint32_t j = 0; j < kb_count; j++) cv = __fmaf_rn(c[j], bs[j], cv);
-            v = add(v, cv);
-          }
           a.y_mlp[((size_t)task_d * M + tok) * Hd + n] = v;
         } else if (kind == kPhHead) {
           a.logits[(size_t)tok * a.head.n + n] = v;
@@ -1943,6 +1976,8 @@ struct Consumer {
         if ((lane & 15) == 0 && key) atomicMax(best() + tok, key);
       }
     }
+    if (kind == kPhDown && *reinterpret_cast<const float* const*>(g_smem + a.lay.corr))
+      add_correction(a, M, pending, kb_base, task_d);
     pending = 0;
     pslots = 0;
     sync_dead();
@@ -2066,7 +2101,6 @@ __global__ void __launch_bounds__(kDT, 1) decode_kernel(const __grid_constant__ 
     Consumer<MQ> c{a};
     c.idx = 0;
     c.kb_base = 0;
-    c.kb_count = 0;
     c.M = a.m;
     c.pos = a.step->position;
     c.W = kDecodeSyncFixed + a.m * a.kv_heads;

@@ -53,7 +53,7 @@ constexpr uint32_t kDecodeFoldSplits = 8;   // up to this many, the output proje
 // Byte offsets of the decode kernel's shared-memory regions (set by the launch).
 struct DecodeLayout {
   uint32_t codes, scales, full, empty, uni, xf, rowbuf, part, stat, red, task_rg, best, flags, gains, tags, uses,
-      kvbuf, kvbar, kvstate, total;
+      kvbuf, kvbar, kvstate, corr, total;
 };
 
 struct DecodeArgs {
