@@ -622,6 +622,92 @@ __global__ void __launch_bounds__(kThreads) norm_f16_kernel(const MatvecArgs a, 
   pdl_launch_dependents();
 }
 
+// The same for rows of a width that is a multiple of 128 (up to 2048): a warp
+// a row, the row's NV float4s a lane in registers, every load of the row in
+// flight at once and each sum of squares a warp shuffle reduction, so no CTA
+// barrier sits between the loads and the stores (the one-CTA-a-row form
+// above runs two 256-invocation trees with a barrier a level).  The
+// per-element formulas are the norm's; only the order of the two sums of
+// squares differs (a few f32 roundings of the statistics).
+template <int NV>
+__global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecArgs a, __half* out_hi,
+                                                                  __half* out_lo) {
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t row = blockIdx.x * kWarps + warp;
+  if (row < a.m) {
+    const NormArgs& n = a.norm;
+    const uint32_t W = n.width;
+    const float wf = (float)W;
+    const float4* x4 = reinterpret_cast<const float4*>(n.hidden_in + (size_t)row * W);
+    float4 x[NV], y[NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) x[i] = x4[lane + 32 * i];
+    if (n.y) {
+      const float* yr = n.y + (size_t)row * W;
+#pragma unroll
+      for (int i = 0; i < NV; i++) y[i] = y_sum(n, yr, lane + 32 * i);
+    }
+    const uint32_t seq = row / a.seq_tokens;
+    const bool last = row % a.seq_tokens == a.seq_tokens - 1;
+    if (n.y) {
+      if (n.post_gain) {
+        float p = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) p = add(p, dot_self(y[i]));
+        const float s = inverse_sqrt(add(__fdiv_rn(warp_sum(p), wf), n.eps));
+        const float4* pg4 = reinterpret_cast<const float4*>(n.post_gain);
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+          const float4 g = pg4[lane + 32 * i];
+          y[i] = make_float4(mul(mul(y[i].x, s), g.x), mul(mul(y[i].y, s), g.y), mul(mul(y[i].z, s), g.z),
+                             mul(mul(y[i].w, s), g.w));
+        }
+      }
+      float4* ycap = last && n.capture_added ? reinterpret_cast<float4*>(n.capture_added + seq * a.capture_stride)
+                                             : nullptr;
+#pragma unroll
+      for (int i = 0; i < NV; i++) {
+        if (ycap) ycap[lane + 32 * i] = y[i];
+        x[i] = make_float4(add(x[i].x, y[i].x), add(x[i].y, y[i].y), add(x[i].z, y[i].z), add(x[i].w, y[i].w));
+      }
+    }
+    float4* out4 = n.hidden_out ? reinterpret_cast<float4*>(n.hidden_out + (size_t)row * W) : nullptr;
+    float4* xcap = last && n.capture_residual
+                       ? reinterpret_cast<float4*>(n.capture_residual + seq * a.capture_stride) : nullptr;
+    float p = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      if (out4) out4[lane + 32 * i] = x[i];
+      if (xcap) xcap[lane + 32 * i] = x[i];
+      p = add(p, dot_self(x[i]));
+    }
+    const float s = inverse_sqrt(add(__fdiv_rn(warp_sum(p), wf), n.eps));
+    const float4* g4 = reinterpret_cast<const float4*>(n.gain);
+    uint2* hi = reinterpret_cast<uint2*>(out_hi + (size_t)row * W);
+    uint2* lo = out_lo ? reinterpret_cast<uint2*>(out_lo + (size_t)row * W) : nullptr;
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const float4 g = g4[lane + 32 * i];
+      const float v[4] = {mul(mul(x[i].x, s), g.x), mul(mul(x[i].y, s), g.y), mul(mul(x[i].z, s), g.z),
+                          mul(mul(x[i].w, s), g.w)};
+      __half h[4], l[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        h[e] = __float2half_rn(v[e]);
+        l[e] = __float2half_rn(__fsub_rn(v[e], __half2float(h[e])));
+      }
+      __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
+      hi[lane + 32 * i] = make_uint2(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23));
+      if (lo) {
+        __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
+        lo[lane + 32 * i] = make_uint2(*reinterpret_cast<uint32_t*>(&l01), *reinterpret_cast<uint32_t*>(&l23));
+      }
+    }
+  }
+  pdl_launch_dependents();
+}
+
 // The norm prologue's rows as f32 (CTA i: the row the prologue would read for
 // slot i), for a product that takes f32 x (the Q8_0 head).
 __global__ void __launch_bounds__(kThreads) norm_f32_kernel(const MatvecArgs a, float* out) {
@@ -887,10 +973,39 @@ cudaError_t launch_plain(const void* fn, dim3 grid, dim3 block, cudaStream_t str
 }
 }  // namespace
 
+template <int NV>
+const void* norm_warp_fn() {
+  return (const void*)norm_rows_warp_kernel<NV>;
+}
+
 cudaError_t launch_norm_f16(const MatvecArgs& a, __half* out_hi, __half* out_lo, cudaStream_t stream, bool pdl) {
   if (a.norm.width > 8192 || a.norm.width % 4 || a.m == 0) return cudaErrorInvalidValue;
   MatvecArgs copy = a;
   void* args[] = {&copy, &out_hi, &out_lo};
+  // A warp a row for widths of 128 .. 2048 in 128s (both forms take rows 0 .. m - 1).
+  const void* warp_fn = nullptr;
+  if (a.norm.width % 128 == 0) {
+    switch (a.norm.width / 128) {
+      case 1: warp_fn = norm_warp_fn<1>(); break;
+      case 2: warp_fn = norm_warp_fn<2>(); break;
+      case 3: warp_fn = norm_warp_fn<3>(); break;
+      case 4: warp_fn = norm_warp_fn<4>(); break;
+      case 5: warp_fn = norm_warp_fn<5>(); break;
+      case 6: warp_fn = norm_warp_fn<6>(); break;
+      case 7: warp_fn = norm_warp_fn<7>(); break;
+      case 8: warp_fn = norm_warp_fn<8>(); break;
+      case 9: warp_fn = norm_warp_fn<9>(); break;
+      case 10: warp_fn = norm_warp_fn<10>(); break;
+      case 11: warp_fn = norm_warp_fn<11>(); break;
+      case 12: warp_fn = norm_warp_fn<12>(); break;
+      case 13: warp_fn = norm_warp_fn<13>(); break;
+      case 14: warp_fn = norm_warp_fn<14>(); break;
+      case 15: warp_fn = norm_warp_fn<15>(); break;
+      case 16: warp_fn = norm_warp_fn<16>(); break;
+      default: break;
+    }
+  }
+  if (warp_fn) return launch_plain(warp_fn, dim3((a.m + kWarps - 1) / kWarps), dim3(kThreads), stream, pdl, args);
   return launch_plain((const void*)norm_f16_kernel, dim3(a.m), dim3(kThreads), stream, pdl, args);
 }
 
