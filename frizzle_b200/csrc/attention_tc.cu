@@ -1,0 +1,497 @@
+// Attention for many query rows (prefill steps of more than 16 rows) on the
+// fifth-generation tensor cores: softmax(q.k / 16) . v over keys j in
+// [p - W + 1, p] (attention.wgsl:166-438 computes the same sums key by key;
+// here it is the flash form, tile by tile).
+//
+// A CTA takes one sequence, one KV head and QT = 128 / G tokens of each of
+// the G query heads that share it: 128 query rows, row r = head (r / QT),
+// token (r % QT), one row a TMEM lane.  Keys go 32 at a time:
+//   - warp 4 (one lane) brings each tile's keys and values by TMA from the
+//     cache (4D tensor maps, 32-slot x 64-dimension boxes, 128-byte swizzle)
+//     into a two-stage ring;
+//   - warp 5 (one lane) issues tcgen05.mma: S = Q K^T (M = 128, N = 32) into
+//     one of two TMEM score buffers, Q as f16 part and remainder (two MMAs a
+//     16-dimension step, so the products are exact and the sums f32), then
+//     O += P V (N = 256, V read MN-major straight from the tile) into a
+//     TMEM accumulator, P as f16 part and remainder;
+//   - warps 0..3 (thread = row) read their row's 32 scores (tcgen05.ld), mask
+//     them (causal, window, rows past the step), keep the online softmax
+//     (max m, sum l), write P to shared memory and, when a tile's max passes
+//     m by more than 8 (log2 units), rescale O in TMEM (tcgen05.ld/st) first;
+//     in between, the exponent base may lag the true max by up to 8, which
+//     keeps P <= 256 and leaves the result the same softmax.
+// At the end each row's O / l is written as f32 and as f16 part and
+// remainder (the output projection's operands).
+//
+// Every mbarrier wait is bounded; a wait that gives up records an error, the
+// CTA waits (bounded) for the copies and products it issued, releases its
+// tensor memory and returns.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "kernels.cuh"
+#include "q4_device.cuh"
+
+namespace fz {
+namespace {
+
+using namespace q4dev;
+
+constexpr uint32_t kD = 256;              // head dimension
+constexpr uint32_t kRows = 128;           // query rows a CTA (the MMA's M)
+constexpr uint32_t kKT = 32;              // keys a tile
+constexpr uint32_t kStages = 2;           // key/value tiles in flight
+constexpr uint32_t kQChunk = kRows * 128;                 // 64 dimensions of 128 rows, f16: 16 KB
+constexpr uint32_t kQBytes = 4 * kQChunk;                 // one of Q's two halves: 64 KB
+constexpr uint32_t kBox = kKT * 128;                      // 32 keys x 64 dimensions f16: 4 KB
+constexpr uint32_t kTileBytes = 8 * kBox;                 // keys then values: 32 KB
+constexpr uint32_t kPBytes = kRows * kKT * 2;             // P's part (or remainder): 8 KB
+constexpr uint32_t kSmem = 2 * kQBytes + kStages * kTileBytes + 2 * kPBytes + 1024;
+constexpr uint32_t kThreads = 192;
+constexpr uint32_t kTmemCols = 512;       // O [0, 256), S buffers [256, 288) and [288, 320)
+constexpr uint32_t kSpin = 1u << 22;      // polls a wait takes before it gives up
+
+FZ_DEV uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+FZ_DEV void mb_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n) : "memory");
+}
+FZ_DEV void mb_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+FZ_DEV void mb_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+FZ_DEV bool mb_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// The CTA's failure state: a flag in shared memory every wait checks.
+struct Fail {
+  volatile uint32_t* flag;
+  uint32_t* error;
+  FZ_DEV void raise(uint32_t code) const {
+    *flag = 1u;
+    if (error) atomicOr(error, code);
+  }
+};
+
+// Waits for the phase of `parity` (bounded); false when it gave up or
+// another thread of the CTA already did.
+FZ_DEV bool mb_wait(uint64_t* b, uint32_t parity, const Fail& f, uint32_t code) {
+  for (uint32_t i = 0; i < kSpin; i++) {
+    if (mb_try(b, parity)) return true;
+    if ((i & 255u) == 255u && *f.flag) return false;
+  }
+  f.raise(code);
+  return false;
+}
+
+FZ_DEV void tma_box(void* dst, const void* map, uint64_t* bar, uint32_t x, uint32_t h, uint32_t slot, uint32_t seq) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(su32(dst)),
+      "l"(map), "r"(x), "r"(h), "r"(slot), "r"(seq), "r"(su32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptors (sm_100): start >> 4, leading and stride
+// byte offsets >> 4, version 1, layout type (0: no swizzle, 2: 128-byte).
+FZ_DEV uint64_t desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)(lbo >> 4) << 16) | ((uint64_t)(sbo >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)layout << 61);
+}
+// kind::f16 with an f32 accumulator, M = 128: A K-major; B K-major or MN-major.
+constexpr uint32_t idesc(uint32_t n, bool b_mn) {
+  return (1u << 4) | ((b_mn ? 1u : 0u) << 16) | ((n >> 3) << 17) | ((kRows >> 4) << 24);
+}
+
+FZ_DEV void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(da), "l"(db), "r"(id), "r"(accumulate)
+      : "memory");
+}
+FZ_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+FZ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+FZ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+FZ_DEV void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+FZ_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+FZ_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+FZ_DEV uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+
+template <int G>
+__global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const AttentionArgs a) {
+  constexpr uint32_t QT = kRows / G;   // tokens a CTA
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t kv_full[kStages], kv_empty[kStages], s_full[2], s_empty[2];
+  __shared__ __align__(8) uint64_t q_full, p_full, pv_done, drain;
+  __shared__ uint32_t tmem_base;
+  __shared__ uint32_t fail_word;
+  unsigned char* smem = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* qhi = smem;
+  unsigned char* qlo = smem + kQBytes;
+  unsigned char* tiles = smem + 2 * kQBytes;
+  unsigned char* phi = tiles + kStages * kTileBytes;
+  unsigned char* plo = phi + kPBytes;
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t T = a.seq_tokens;
+  const uint32_t nblk = (T + QT - 1) / QT;
+  const uint32_t blk = nblk - 1 - blockIdx.x;   // the latest tokens (the most keys) first
+  const uint32_t kvh = blockIdx.y, seq = blockIdx.z, t0 = blk * QT;
+  const Fail f{reinterpret_cast<volatile uint32_t*>(&fail_word), a.error};
+
+  if (threadIdx.x == 0) {
+    fail_word = 0u;
+    for (uint32_t s = 0; s < kStages; s++) {
+      mb_init(&kv_full[s], 1);
+      mb_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mb_init(&s_full[b], 1);
+      mb_init(&s_empty[b], 128);
+    }
+    mb_init(&q_full, 128);
+    mb_init(&p_full, 128);
+    mb_init(&pv_done, 1);
+    mb_init(&drain, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 5) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  pdl_wait();   // the queries and the caches' new rows come from the previous launches
+
+  const uint32_t pos0 = (a.step ? a.step->position : a.position) + t0;
+  const uint32_t ntok = min(QT, T - t0);
+  const uint32_t p_last = pos0 + ntok - 1;
+  const uint32_t k_lo = pos0 + 1 > a.window ? pos0 + 1 - a.window : 0u;   // the earliest key any row reads
+  const uint32_t kt0 = k_lo / kKT * kKT;
+  const uint32_t ntiles = (p_last - kt0) / kKT + 1;
+
+  if (warp < 4) {
+    // ---- softmax: thread r is query row r (TMEM lane r).
+    const uint32_t r = threadIdx.x, hh = r / QT, t = r % QT;
+    const bool live = t < ntok;
+    const uint32_t head = kvh * G + hh, p = pos0 + t;
+    const size_t row_base = (((size_t)seq * T + t0 + t) * a.heads + head) * kD;
+    {
+      // The row's query times scale x log2 e, as f16 part and remainder, K-major
+      // 64-dimension chunks with 128-byte swizzle (16-byte unit u of row r at
+      // unit u ^ (r % 8)).
+      const float4* q4 = reinterpret_cast<const float4*>(a.q + row_base);
+      const float sc = a.scale_log2e;
+#pragma unroll 4
+      for (uint32_t u = 0; u < 32; u++) {
+        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+        if (live) {
+          v0 = __ldcg(q4 + 2 * u);
+          v1 = __ldcg(q4 + 2 * u + 1);
+        }
+        const float x[8] = {mul(v0.x, sc), mul(v0.y, sc), mul(v0.z, sc), mul(v0.w, sc),
+                            mul(v1.x, sc), mul(v1.y, sc), mul(v1.z, sc), mul(v1.w, sc)};
+        __half h[8], l[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) split_hi_lo(x[e], h[e], l[e]);
+        const uint32_t off = (u >> 3) * kQChunk + r * 128u + (((u & 7u) ^ (r & 7u)) << 4);
+        *reinterpret_cast<uint4*>(qhi + off) =
+            make_uint4(h2_bits(__halves2half2(h[0], h[1])), h2_bits(__halves2half2(h[2], h[3])),
+                       h2_bits(__halves2half2(h[4], h[5])), h2_bits(__halves2half2(h[6], h[7])));
+        *reinterpret_cast<uint4*>(qlo + off) =
+            make_uint4(h2_bits(__halves2half2(l[0], l[1])), h2_bits(__halves2half2(l[2], l[3])),
+                       h2_bits(__halves2half2(l[4], l[5])), h2_bits(__halves2half2(l[6], l[7])));
+      }
+      proxy_fence();
+      mb_arrive(&q_full);
+    }
+    const uint32_t lane_addr = tmem + ((warp * 32u) << 16);
+    float m = -INFINITY, l = 0.f;
+    uint32_t pv_seen = 0;
+    bool ok = true;
+#pragma unroll 1
+    for (uint32_t i = 0; i < ntiles; i++) {
+      const uint32_t sb = i & 1u;
+      // (the warp decides together: the tensor-memory loads below are warp-wide)
+      if (!__all_sync(0xffffffffu, mb_wait(&s_full[sb], (i >> 1) & 1u, f, 0x10000u))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[32];
+      tmem_ld32(lane_addr + 256u + 32u * sb, sr);
+      tc_fence_before();
+      mb_arrive(&s_empty[sb]);
+      const uint32_t j0 = kt0 + i * kKT;
+      float sv[32];
+      float mx = -INFINITY;
+#pragma unroll
+      for (uint32_t c = 0; c < 32; c++) {
+        const uint32_t j = j0 + c;
+        const bool valid = live && j <= p && p - j < a.window;
+        sv[c] = valid ? __uint_as_float(sr[c]) : -INFINITY;
+        mx = fmaxf(mx, sv[c]);
+      }
+      // The previous tile's P V is done: P's buffer is free and O may be rescaled.
+      if (i > 0) {
+        if (!__all_sync(0xffffffffu, mb_wait(&pv_done, pv_seen & 1u, f, 0x20000u))) {
+          ok = false;
+          break;
+        }
+        pv_seen++;
+        tc_fence_after();
+      }
+      // A new base when the tile's max passes it by more than 8; O is
+      // rescaled by the warp together (lanes that keep their base scale by 1).
+      const bool moved = mx > m + 8.f;
+      const bool rescale = moved && m != -INFINITY;
+      const float c = rescale ? exp2f(m - mx) : 1.f;
+      if (rescale) l = mul(l, c);
+      if (moved) m = mx;
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+        for (uint32_t c0 = 0; c0 < kD; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(lane_addr + c0, o);
+#pragma unroll
+          for (int k = 0; k < 32; k++) o[k] = __float_as_uint(mul(__uint_as_float(o[k]), c));
+          tmem_st32(lane_addr + c0, o);
+        }
+      }
+      float sum = 0.f;
+      uint32_t ph[16], pl[16];
+#pragma unroll
+      for (uint32_t c = 0; c < 32; c += 2) {
+        const float e0 = sv[c] == -INFINITY ? 0.f : exp2f(sv[c] - m);
+        const float e1 = sv[c + 1] == -INFINITY ? 0.f : exp2f(sv[c + 1] - m);
+        sum = add(add(sum, e0), e1);
+        __half h0, h1, l0, l1;
+        split_hi_lo(e0, h0, l0);
+        split_hi_lo(e1, h1, l1);
+        ph[c / 2] = h2_bits(__halves2half2(h0, h1));
+        pl[c / 2] = h2_bits(__halves2half2(l0, l1));
+      }
+      l = add(l, sum);
+      // P row r, K-major without swizzle: core matrices of 8 rows x 8 keys
+      // (128 bytes), 128 bytes apart along the keys, 512 along the rows.
+#pragma unroll
+      for (uint32_t ck = 0; ck < 4; ck++) {
+        const uint32_t off = (r >> 3) * 512u + ck * 128u + (r & 7u) * 16u;
+        *reinterpret_cast<uint4*>(phi + off) = make_uint4(ph[4 * ck], ph[4 * ck + 1], ph[4 * ck + 2], ph[4 * ck + 3]);
+        *reinterpret_cast<uint4*>(plo + off) = make_uint4(pl[4 * ck], pl[4 * ck + 1], pl[4 * ck + 2], pl[4 * ck + 3]);
+      }
+      proxy_fence();
+      tc_fence_before();
+      mb_arrive(&p_full);
+    }
+    if (ok) {
+      if (!__all_sync(0xffffffffu, mb_wait(&pv_done, pv_seen & 1u, f, 0x40000u))) ok = false;
+      tc_fence_after();
+    }
+    pdl_launch_dependents();
+    if (ok) {
+      // out = O / l, and its f16 part and remainder.
+#pragma unroll 1
+      for (uint32_t c0 = 0; c0 < kD; c0 += 32) {
+        uint32_t o[32];
+        tmem_ld32(lane_addr + c0, o);
+        if (!live) continue;   // (after the warp-wide load)
+        float v[32];
+#pragma unroll
+        for (int k = 0; k < 32; k++) v[k] = __fdiv_rn(__uint_as_float(o[k]), l);
+        float4* out4 = reinterpret_cast<float4*>(a.out + row_base + c0);
+#pragma unroll
+        for (int k = 0; k < 8; k++) out4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        if (a.out_hi) {
+          uint32_t hw[16], lw[16];
+#pragma unroll
+          for (int k = 0; k < 16; k++) {
+            __half h0, h1, l0, l1;
+            split_hi_lo(v[2 * k], h0, l0);
+            split_hi_lo(v[2 * k + 1], h1, l1);
+            hw[k] = h2_bits(__halves2half2(h0, h1));
+            lw[k] = h2_bits(__halves2half2(l0, l1));
+          }
+          uint4* oh = reinterpret_cast<uint4*>(a.out_hi + row_base + c0);
+#pragma unroll
+          for (int k = 0; k < 4; k++) oh[k] = make_uint4(hw[4 * k], hw[4 * k + 1], hw[4 * k + 2], hw[4 * k + 3]);
+          if (a.out_lo) {
+            uint4* ol = reinterpret_cast<uint4*>(a.out_lo + row_base + c0);
+#pragma unroll
+            for (int k = 0; k < 4; k++) ol[k] = make_uint4(lw[4 * k], lw[4 * k + 1], lw[4 * k + 2], lw[4 * k + 3]);
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---- the tiles' keys and values by TMA (lane 0).
+    if (lane == 0) {
+      const unsigned char* kmap = static_cast<const unsigned char*>(a.kv_maps);
+      const unsigned char* vmap = kmap + 128;
+      uint32_t issued = 0;
+#pragma unroll 1
+      for (uint32_t i = 0; i < ntiles; i++) {
+        const uint32_t s = i % kStages;
+        if (i >= kStages && !mb_wait(&kv_empty[s], ((i / kStages) + 1u) & 1u, f, 0x1000u)) break;
+        if (*f.flag) break;
+        mb_expect_tx(&kv_full[s], kTileBytes);
+        const uint32_t slot = (kt0 + i * kKT) % a.slots;
+        unsigned char* kb = tiles + s * kTileBytes;
+#pragma unroll
+        for (uint32_t q = 0; q < 4; q++) tma_box(kb + q * kBox, kmap, &kv_full[s], 64u * q, kvh, slot, seq);
+#pragma unroll
+        for (uint32_t q = 0; q < 4; q++) tma_box(kb + (4 + q) * kBox, vmap, &kv_full[s], 64u * q, kvh, slot, seq);
+        issued++;
+      }
+      // Every copy issued has landed before the CTA exits (bounded; the last
+      // tile of each stage completes after the earlier ones).
+      for (uint32_t s = 0; s < kStages && s < issued; s++) {
+        const uint32_t last = s + ((issued - 1 - s) / kStages) * kStages;
+        for (uint32_t it = 0; it < kSpin && !mb_try(&kv_full[s], (last / kStages) & 1u); it++) {
+        }
+      }
+    }
+  } else {
+    // ---- the MMA issuer (lane 0).
+    if (lane == 0) {
+      bool ok = mb_wait(&q_full, 0u, f, 0x2000u);
+      tc_fence_after();
+      constexpr uint32_t id_s = idesc(kKT, false), id_pv = idesc(kD, true);
+      const uint32_t qh = su32(qhi), ql = su32(qlo), pa = su32(phi), pb = su32(plo);
+#pragma unroll 1
+      for (uint32_t i = 0; ok && i <= ntiles; i++) {
+        if (i < ntiles) {
+          const uint32_t s = i % kStages, sb = i & 1u;
+          if (!mb_wait(&kv_full[s], (i / kStages) & 1u, f, 0x4000u) ||
+              (i >= 2 && !mb_wait(&s_empty[sb], ((i >> 1) + 1u) & 1u, f, 0x8000u)))
+            break;
+          tc_fence_after();
+          const uint32_t kb = su32(tiles + s * kTileBytes);
+          const uint32_t d = tmem + 256u + 32u * sb;
+#pragma unroll
+          for (uint32_t c = 0; c < 4; c++)
+#pragma unroll
+            for (uint32_t kk = 0; kk < 4; kk++) {
+              // 16 dimensions = 32 bytes along K within the 128-byte swizzled rows.
+              const uint64_t db = desc(kb + c * kBox + kk * 32u, 16u, 1024u, 2u);
+              umma(d, desc(qh + c * kQChunk + kk * 32u, 16u, 1024u, 2u), db, id_s, (c | kk) != 0u ? 1u : 0u);
+              umma(d, desc(ql + c * kQChunk + kk * 32u, 16u, 1024u, 2u), db, id_s, 1u);
+            }
+          umma_commit(&s_full[sb]);
+        }
+        if (i >= 1) {
+          const uint32_t j = i - 1, s = j % kStages;
+          if (!mb_wait(&p_full, j & 1u, f, 0x8000u)) break;
+          tc_fence_after();
+          const uint32_t vb = su32(tiles + s * kTileBytes + 4 * kBox);
+#pragma unroll
+          for (uint32_t kk = 0; kk < 2; kk++) {
+            // V MN-major: 64-dimension boxes kBox apart, 8-key row groups 1024 bytes apart.
+            const uint64_t dv = desc(vb + kk * 2048u, kBox, 1024u, 2u);
+            umma(tmem, desc(pa + kk * 256u, 128u, 512u, 0u), dv, id_pv, (j | kk) != 0u ? 1u : 0u);
+            umma(tmem, desc(pb + kk * 256u, 128u, 512u, 0u), dv, id_pv, 1u);
+          }
+          umma_commit(&kv_empty[s]);
+          umma_commit(&pv_done);
+        }
+      }
+      // Every product issued has completed before tensor memory is released.
+      umma_commit(&drain);
+      for (uint32_t it = 0; it < kSpin && !mb_try(&drain, 0u); it++) {
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+template <int G>
+cudaError_t launch_g(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
+  constexpr uint32_t QT = kRows / G;
+  const uint32_t seqs = a.m / a.seq_tokens;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.seq_tokens + QT - 1) / QT, a.kv_heads, seqs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  (void)cudaGetLastError();
+  return cudaLaunchKernelEx(&cfg, attention_tc_kernel<G>, a);
+}
+
+}  // namespace
+
+cudaError_t configure_attention_tc() {
+  cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_tc_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attention_tc_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
+  return e;
+}
+
+cudaError_t launch_attention_tc(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.head_dim != kD || a.kv_heads == 0 || a.heads % a.kv_heads || a.seq_tokens == 0 || a.m % a.seq_tokens ||
+      !a.kv_maps || (reinterpret_cast<uintptr_t>(a.kv_maps) & 63u) || a.slots == 0)
+    return cudaErrorInvalidValue;
+  switch (a.heads / a.kv_heads) {
+    case 1: return launch_g<1>(a, stream, pdl);
+    case 2: return launch_g<2>(a, stream, pdl);
+    case 4: return launch_g<4>(a, stream, pdl);
+    case 8: return launch_g<8>(a, stream, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace fz

@@ -27,6 +27,12 @@ struct AttentionArgs {
   float* out;                      // [m][heads][d]
   __half* out_hi;                  // [m][heads][d] f16 of out, or null
   __half* out_lo;                  // its f16 remainder, or null
+  // The tensor-core prefill form: the layer's key and value cache tensor maps
+  // (two CUtensorMaps, 4D [sequence][slot][KV head][256], 32-slot x
+  // 64-dimension boxes, 128-byte swizzle; device memory, 64-byte aligned)
+  // and a device word set nonzero when one of its bounded waits gives up.
+  const void* kv_maps;
+  uint32_t* error;
 };
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl);
@@ -38,6 +44,11 @@ cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool p
 bool attention_prefill_supported(uint32_t heads, uint32_t kv_heads, uint32_t head_dim);
 cudaError_t configure_attention_prefill();
 cudaError_t launch_attention_prefill(const AttentionArgs& a, cudaStream_t stream, bool pdl);
+// The same on tcgen05 (attention_tc.cu): 1, 2, 4 or 8 query heads a KV
+// head, head dimension 256, a.kv_maps the layer's cache tensor maps;
+// configure_attention_tc raises its shared-memory limit (outside capture).
+cudaError_t configure_attention_tc();
+cudaError_t launch_attention_tc(const AttentionArgs& a, cudaStream_t stream, bool pdl);
 
 // The embedding rows of the step's tokens (or, for a fed step, the last draw)
 // times `scale`, into hidden [m][width]; also clears the argmax slots.
