@@ -305,10 +305,14 @@ __global__ void __launch_bounds__(kThreadsG, 1)
   const uint32_t half_bn = BN / 2;
   const uint32_t cols = EPI == kGemmGated ? half_bn : BN;       // weight rows (neurons) a tile
   const uint32_t mtiles = (a.m + kBM - 1) / kBM, ntiles = (a.w[0].n + cols - 1) / cols;
-  const uint32_t tiles = mtiles * ntiles;
-  // Tile t: rows m0 = (t % mtiles) * 128 of X, weight rows n0 = (t / mtiles) * cols.
-  auto m0_of = [&](uint32_t tile) { return (tile % mtiles) * kBM; };
-  auto n0_of = [&](uint32_t tile) { return (tile / mtiles) * cols; };
+  // Work items: a tile and one of KS slices of its k-stages (KS divides nkt).
+  const uint32_t KS = a.k_split > 1 ? a.k_split : 1u, nks = nkt / KS;
+  const uint32_t tiles = mtiles * ntiles * KS;
+  // Item t: tile t / KS (rows m0 = (tile % mtiles) * 128 of X, weight rows
+  // n0 = (tile / mtiles) * cols) over k-stages (t % KS) * nks, + nks.
+  auto m0_of = [&](uint32_t item) { return ((item / KS) % mtiles) * kBM; };
+  auto n0_of = [&](uint32_t item) { return ((item / KS) / mtiles) * cols; };
+  auto k0_of = [&](uint32_t item) { return (item % KS) * nks; };
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < S; s++) {
@@ -339,8 +343,9 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     uint32_t it = 0;
     bool stop = false;
     for (uint32_t tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x) {
-      const uint32_t m0 = m0_of(tile), n0 = n0_of(tile);
-      for (uint32_t kt = 0; kt < nkt; kt++, it++) {
+      const uint32_t m0 = m0_of(tile), n0 = n0_of(tile), k0 = k0_of(tile);
+      for (uint32_t kr = 0; kr < nks; kr++, it++) {
+        const uint32_t kt = k0 + kr;
         const int s = (int)(it % S);
         const uint32_t round = it / S;
         if (!mbar_wait(&empty[s], (round + 1) & 1u, a.error, 1)) {
@@ -380,7 +385,7 @@ __global__ void __launch_bounds__(kThreadsG, 1)
       if (!mbar_wait(&acc_empty[buf], (use + 1) & 1u, a.error, 5)) break;
       fence_after_sync();
       const uint32_t acc = tmem + buf * BN;
-      for (uint32_t kt = 0; kt < nkt; kt++, it++) {
+      for (uint32_t kt = 0; kt < nks; kt++, it++) {
         const int s = (int)(it % S);
         const uint32_t round = it / S;
         if (!mbar_wait(&full[s], round & 1u, a.error, 2)) {
@@ -421,9 +426,9 @@ __global__ void __launch_bounds__(kThreadsG, 1)
     constexpr int kMine = kRgs / kProducers;       // row groups a warp, a stage
     static_assert(kRgs % kProducers == 0, "row groups split evenly over the producers");
     const uint32_t my_tiles = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    const uint32_t total = my_tiles * nkt;
+    const uint32_t total = my_tiles * nks;
     auto rg_of = [&](uint32_t q, int j) {
-      const uint32_t n0 = n0_of(blockIdx.x + (q / nkt) * gridDim.x);
+      const uint32_t n0 = n0_of(blockIdx.x + (q / nks) * gridDim.x);
       const int r = pw + j * kProducers;
       return EPI == kGemmGated ? (n0 / 16 + (uint32_t)(r % (kRgs / 2))) : (n0 / 16 + (uint32_t)r);
     };
@@ -435,7 +440,8 @@ __global__ void __launch_bounds__(kThreadsG, 1)
 #pragma unroll
       for (int j = 0; j < kMine; j++) {
         const uint32_t rg = rg_of(q, j);
-        dst[j] = load_codes(mat_of(j), rg, q % nkt, rg < mat_of(j).n / 16, lane);
+        dst[j] = load_codes(mat_of(j), rg, k0_of(blockIdx.x + (q / nks) * gridDim.x) + q % nks,
+                            rg < mat_of(j).n / 16, lane);
       }
     };
     Codes A[kMine], B[kMine], C[kMine];
@@ -497,7 +503,12 @@ __global__ void __launch_bounds__(kThreadsG, 1)
             const uint32_t n = n0 + (uint32_t)c0 + h * kStageCols + (lane & 15);
             for (int rr = lane >> 4; rr < 32; rr += 2) {
               const uint32_t orow = m0 + quarter * 32 + rr;
-              if (orow < a.m && n < N) a.out[(size_t)orow * a.out_stride + n] = stage[rr * (kStageCols + 1) + (lane & 15)];
+              if (orow < a.m && n < N) {
+                float* o = a.out + (size_t)orow * a.out_stride + n;
+                const float v = stage[rr * (kStageCols + 1) + (lane & 15)];
+                if (KS > 1) atomicAdd(o, v);   // (a reduction: the result is not read)
+                else *o = v;
+              }
             }
             __syncwarp();
           }
@@ -626,8 +637,23 @@ cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (sms <= 0) sms = 148;
   }
+  // Few tiles (few rows, or a narrow product): split K so that every SM has
+  // an item, at least two k-stages an item, the slice count dividing the
+  // stages; the partials meet in `out` by f32 reductions, so it is zeroed.
+  GemmArgs g = a;
+  g.k_split = 1;
+  const uint32_t nkt = a.w[0].k / kBK;
+  if (EPI == kGemmWrite && tiles < (uint32_t)sms) {
+    for (uint32_t d = 2; d <= nkt / 2; d++)
+      if (nkt % d == 0 && tiles * d <= (uint32_t)sms) g.k_split = d;
+    if (g.k_split > 1) {
+      const cudaError_t z = cudaMemset2DAsync(a.out, (size_t)a.out_stride * 4, 0, (size_t)a.w[0].n * 4, a.m, stream);
+      if (z != cudaSuccess) return z;
+    }
+  }
+  const uint32_t items = tiles * g.k_split;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(std::min<uint32_t>(tiles, (uint32_t)sms));
+  cfg.gridDim = dim3(std::min<uint32_t>(items, (uint32_t)sms));
   cfg.blockDim = dim3(kThreadsG);
   cfg.dynamicSmemBytes = L::kSmem;
   cfg.stream = stream;
@@ -636,7 +662,7 @@ cudaError_t launch_tiles(const GemmArgs& a, cudaStream_t stream, bool pdl) {
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, XP, WP, EPI, WT>, map_hi, map_lo, wm, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel<BN, XP, WP, EPI, WT>, map_hi, map_lo, wm, g);
   if (e != cudaSuccess) (void)cudaGetLastError();
   return e;
 }

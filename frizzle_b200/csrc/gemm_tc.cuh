@@ -37,6 +37,11 @@ struct GemmArgs {
   float* capture_neurons;     // sequence 0's capture slot, or null
   uint64_t capture_stride;
   uint32_t* error;            // set nonzero when a bounded wait gives up
+  // K split (set by launch_gemm for a Write product of few tiles): each
+  // (tile, K slice) is a work item whose partial is added into `out` with
+  // f32 reductions (out zeroed first by launch_gemm), so the slices' sums
+  // meet in no fixed order.  1 = none.
+  uint32_t k_split;
 };
 
 // Launches the product: X_hi.W (x_lo null), X_hi.W + X_lo.W (x_lo), or with
