@@ -6,9 +6,12 @@
 // A CTA takes one sequence, one KV head and QT = 128 / G tokens of each of
 // the G query heads that share it: 128 query rows, row r = head (r / QT),
 // token (r % QT), one row a TMEM lane.  Keys go 32 at a time:
-//   - warp 4 (one lane) brings each tile's keys and values by TMA from the
-//     cache (4D tensor maps, 32-slot x 64-dimension boxes, 128-byte swizzle)
-//     into a two-stage ring;
+//   - warps 4 and 6 (one lane each) bring each tile's keys, and its values,
+//     by TMA from the cache (4D tensor maps, 32-slot x 64-dimension boxes,
+//     128-byte swizzle) into a three-stage key ring, freed as each score
+//     product completes, and a two-stage value ring, freed as each P V does
+//     (the keys run a tile further ahead, so a copy's latency hides behind
+//     the products of the tiles before it);
 //   - warp 5 (one lane) issues tcgen05.mma: S = Q K^T (M = 128, N = 32) into
 //     one of two TMEM score buffers, Q as f16 part and remainder (two MMAs a
 //     16-dimension step, so the products are exact and the sums f32), then
@@ -40,14 +43,15 @@ using namespace q4dev;
 constexpr uint32_t kD = 256;              // head dimension
 constexpr uint32_t kRows = 128;           // query rows a CTA (the MMA's M)
 constexpr uint32_t kKT = 32;              // keys a tile
-constexpr uint32_t kStages = 2;           // key/value tiles in flight
+constexpr uint32_t kKStages = 3;          // key tiles in flight
+constexpr uint32_t kVStages = 2;          // value tiles in flight
 constexpr uint32_t kQChunk = kRows * 128;                 // 64 dimensions of 128 rows, f16: 16 KB
 constexpr uint32_t kQBytes = 4 * kQChunk;                 // one of Q's two halves: 64 KB
 constexpr uint32_t kBox = kKT * 128;                      // 32 keys x 64 dimensions f16: 4 KB
-constexpr uint32_t kTileBytes = 8 * kBox;                 // keys then values: 32 KB
+constexpr uint32_t kHalf = 4 * kBox;                      // a tile's keys (or values): 16 KB
 constexpr uint32_t kPBytes = kRows * kKT * 2;             // P's part (or remainder): 8 KB
-constexpr uint32_t kSmem = 2 * kQBytes + kStages * kTileBytes + 2 * kPBytes + 1024;
-constexpr uint32_t kThreads = 192;
+constexpr uint32_t kSmem = 2 * kQBytes + (kKStages + kVStages) * kHalf + 2 * kPBytes + 1024;
+constexpr uint32_t kThreads = 224;
 constexpr uint32_t kTmemCols = 512;       // O [0, 256), S buffers [256, 288) and [288, 320)
 constexpr uint32_t kSpin = 1u << 22;      // polls a wait takes before it gives up
 
@@ -157,15 +161,17 @@ template <int G>
 __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const AttentionArgs a) {
   constexpr uint32_t QT = kRows / G;   // tokens a CTA
   extern __shared__ unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t kv_full[kStages], kv_empty[kStages], s_full[2], s_empty[2];
+  __shared__ __align__(8) uint64_t k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
+  __shared__ __align__(8) uint64_t s_full[2], s_empty[2];
   __shared__ __align__(8) uint64_t q_full, p_full, pv_done, drain;
   __shared__ uint32_t tmem_base;
   __shared__ uint32_t fail_word;
   unsigned char* smem = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
   unsigned char* qhi = smem;
   unsigned char* qlo = smem + kQBytes;
-  unsigned char* tiles = smem + 2 * kQBytes;
-  unsigned char* phi = tiles + kStages * kTileBytes;
+  unsigned char* kring = smem + 2 * kQBytes;
+  unsigned char* vring = kring + kKStages * kHalf;
+  unsigned char* phi = vring + kVStages * kHalf;
   unsigned char* plo = phi + kPBytes;
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -177,9 +183,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
 
   if (threadIdx.x == 0) {
     fail_word = 0u;
-    for (uint32_t s = 0; s < kStages; s++) {
-      mb_init(&kv_full[s], 1);
-      mb_init(&kv_empty[s], 1);
+    for (uint32_t s = 0; s < kKStages; s++) {
+      mb_init(&k_full[s], 1);
+      mb_init(&k_empty[s], 1);
+    }
+    for (uint32_t s = 0; s < kVStages; s++) {
+      mb_init(&v_full[s], 1);
+      mb_init(&v_empty[s], 1);
     }
     for (int b = 0; b < 2; b++) {
       mb_init(&s_full[b], 1);
@@ -222,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       // unit u ^ (r % 8)).
       const float4* q4 = reinterpret_cast<const float4*>(a.q + row_base);
       const float sc = a.scale_log2e;
-#pragma unroll 4
+#pragma unroll 8
       for (uint32_t u = 0; u < 32; u++) {
         float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
         if (live) {
@@ -363,31 +373,35 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
         }
       }
     }
-  } else if (warp == 4) {
-    // ---- the tiles' keys and values by TMA (lane 0).
+  } else if (warp == 4 || warp == 6) {
+    // ---- the tiles' keys (warp 4) or values (warp 6) by TMA (lane 0): a
+    // ring of kKStages key tiles, freed as each score product completes, and
+    // one of kVStages value tiles, freed as each P V completes.
     if (lane == 0) {
-      const unsigned char* kmap = static_cast<const unsigned char*>(a.kv_maps);
-      const unsigned char* vmap = kmap + 128;
+      const bool keys = warp == 4;
+      const unsigned char* map = static_cast<const unsigned char*>(a.kv_maps) + (keys ? 0 : 128);
+      const uint32_t NS = keys ? kKStages : kVStages;
+      uint64_t* full = keys ? k_full : v_full;
+      uint64_t* empty = keys ? k_empty : v_empty;
+      unsigned char* ring = keys ? kring : vring;
       uint32_t issued = 0;
 #pragma unroll 1
       for (uint32_t i = 0; i < ntiles; i++) {
-        const uint32_t s = i % kStages;
-        if (i >= kStages && !mb_wait(&kv_empty[s], ((i / kStages) + 1u) & 1u, f, 0x1000u)) break;
+        const uint32_t s = i % NS;
+        if (i >= NS && !mb_wait(&empty[s], ((i / NS) + 1u) & 1u, f, keys ? 0x1000u : 0x800u)) break;
         if (*f.flag) break;
-        mb_expect_tx(&kv_full[s], kTileBytes);
+        mb_expect_tx(&full[s], kHalf);
         const uint32_t slot = (kt0 + i * kKT) % a.slots;
-        unsigned char* kb = tiles + s * kTileBytes;
+        unsigned char* dst = ring + s * kHalf;
 #pragma unroll
-        for (uint32_t q = 0; q < 4; q++) tma_box(kb + q * kBox, kmap, &kv_full[s], 64u * q, kvh, slot, seq);
-#pragma unroll
-        for (uint32_t q = 0; q < 4; q++) tma_box(kb + (4 + q) * kBox, vmap, &kv_full[s], 64u * q, kvh, slot, seq);
+        for (uint32_t q = 0; q < 4; q++) tma_box(dst + q * kBox, map, &full[s], 64u * q, kvh, slot, seq);
         issued++;
       }
       // Every copy issued has landed before the CTA exits (bounded; the last
       // tile of each stage completes after the earlier ones).
-      for (uint32_t s = 0; s < kStages && s < issued; s++) {
-        const uint32_t last = s + ((issued - 1 - s) / kStages) * kStages;
-        for (uint32_t it = 0; it < kSpin && !mb_try(&kv_full[s], (last / kStages) & 1u); it++) {
+      for (uint32_t s = 0; s < NS && s < issued; s++) {
+        const uint32_t last = s + ((issued - 1 - s) / NS) * NS;
+        for (uint32_t it = 0; it < kSpin && !mb_try(&full[s], (last / NS) & 1u); it++) {
         }
       }
     }
@@ -401,12 +415,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
 #pragma unroll 1
       for (uint32_t i = 0; ok && i <= ntiles; i++) {
         if (i < ntiles) {
-          const uint32_t s = i % kStages, sb = i & 1u;
-          if (!mb_wait(&kv_full[s], (i / kStages) & 1u, f, 0x4000u) ||
+          const uint32_t s = i % kKStages, sb = i & 1u;
+          if (!mb_wait(&k_full[s], (i / kKStages) & 1u, f, 0x4000u) ||
               (i >= 2 && !mb_wait(&s_empty[sb], ((i >> 1) + 1u) & 1u, f, 0x8000u)))
             break;
           tc_fence_after();
-          const uint32_t kb = su32(tiles + s * kTileBytes);
+          const uint32_t kb = su32(kring + s * kHalf);
           const uint32_t d = tmem + 256u + 32u * sb;
 #pragma unroll
           for (uint32_t c = 0; c < 4; c++)
@@ -418,12 +432,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
               umma(d, desc(ql + c * kQChunk + kk * 32u, 16u, 1024u, 2u), db, id_s, 1u);
             }
           umma_commit(&s_full[sb]);
+          umma_commit(&k_empty[s]);
         }
         if (i >= 1) {
-          const uint32_t j = i - 1, s = j % kStages;
-          if (!mb_wait(&p_full, j & 1u, f, 0x8000u)) break;
+          const uint32_t j = i - 1, s = j % kVStages;
+          if (!mb_wait(&v_full[s], (j / kVStages) & 1u, f, 0x4000u) || !mb_wait(&p_full, j & 1u, f, 0x8000u)) break;
           tc_fence_after();
-          const uint32_t vb = su32(tiles + s * kTileBytes + 4 * kBox);
+          const uint32_t vb = su32(vring + s * kHalf);
 #pragma unroll
           for (uint32_t kk = 0; kk < 2; kk++) {
             // V MN-major: 64-dimension boxes kBox apart, 8-key row groups 1024 bytes apart.
@@ -431,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
             umma(tmem, desc(pa + kk * 256u, 128u, 512u, 0u), dv, id_pv, (j | kk) != 0u ? 1u : 0u);
             umma(tmem, desc(pb + kk * 256u, 128u, 512u, 0u), dv, id_pv, 1u);
           }
-          umma_commit(&kv_empty[s]);
+          umma_commit(&v_empty[s]);
           umma_commit(&pv_done);
         }
       }
