@@ -23,8 +23,8 @@
 //     m by more than 8 (log2 units), rescale O in TMEM (tcgen05.ld/st) first;
 //     in between, the exponent base may lag the true max by up to 8, which
 //     keeps P <= 256 and leaves the result the same softmax.
-// At the end each row's O / l is written as f32 and as f16 part and
-// remainder (the output projection's operands).
+// At the end each row's O / l is written as f16 part and remainder (the
+// output projection's operands) and, when asked for, as f32.
 //
 // Every mbarrier wait is bounded; a wait that gives up records an error, the
 // CTA waits (bounded) for the copies and products it issued, releases its
@@ -227,30 +227,45 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
     const uint32_t head = kvh * G + hh, p = pos0 + t;
     const size_t row_base = (((size_t)seq * T + t0 + t) * a.heads + head) * kD;
     {
-      // The row's query times scale x log2 e, as f16 part and remainder, K-major
-      // 64-dimension chunks with 128-byte swizzle (16-byte unit u of row r at
-      // unit u ^ (r % 8)).
-      const float4* q4 = reinterpret_cast<const float4*>(a.q + row_base);
+      // The CTA's queries times scale x log2 e, as f16 part and remainder,
+      // K-major 64-dimension chunks with 128-byte swizzle (16-byte unit u of
+      // row r at unit u ^ (r % 8)).  Warp w reads rows 32 w .. 32 w + 31 a
+      // whole row at a time (lane l: dimensions 4 l .. 4 l + 3 and 128 + 4 l
+      // ..), eight rows' loads in flight.
       const float sc = a.scale_log2e;
-#pragma unroll 8
-      for (uint32_t u = 0; u < 32; u++) {
-        float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
-        if (live) {
-          v0 = __ldcg(q4 + 2 * u);
-          v1 = __ldcg(q4 + 2 * u + 1);
-        }
-        const float x[8] = {mul(v0.x, sc), mul(v0.y, sc), mul(v0.z, sc), mul(v0.w, sc),
-                            mul(v1.x, sc), mul(v1.y, sc), mul(v1.z, sc), mul(v1.w, sc)};
-        __half h[8], l[8];
+#pragma unroll 1
+      for (uint32_t r0 = warp * 32u; r0 < warp * 32u + 32u; r0 += 8) {
+        float4 v[8][2];
 #pragma unroll
-        for (int e = 0; e < 8; e++) split_hi_lo(x[e], h[e], l[e]);
-        const uint32_t off = (u >> 3) * kQChunk + r * 128u + (((u & 7u) ^ (r & 7u)) << 4);
-        *reinterpret_cast<uint4*>(qhi + off) =
-            make_uint4(h2_bits(__halves2half2(h[0], h[1])), h2_bits(__halves2half2(h[2], h[3])),
-                       h2_bits(__halves2half2(h[4], h[5])), h2_bits(__halves2half2(h[6], h[7])));
-        *reinterpret_cast<uint4*>(qlo + off) =
-            make_uint4(h2_bits(__halves2half2(l[0], l[1])), h2_bits(__halves2half2(l[2], l[3])),
-                       h2_bits(__halves2half2(l[4], l[5])), h2_bits(__halves2half2(l[6], l[7])));
+        for (uint32_t k = 0; k < 8; k++) {
+          const uint32_t rr = r0 + k, tt = rr % QT;
+          v[k][0] = v[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (tt < ntok) {
+            const float4* q4 = reinterpret_cast<const float4*>(
+                a.q + (((size_t)seq * T + t0 + tt) * a.heads + kvh * G + rr / QT) * kD);
+            v[k][0] = __ldcg(q4 + lane);
+            v[k][1] = __ldcg(q4 + 32 + lane);
+          }
+        }
+#pragma unroll
+        for (uint32_t k = 0; k < 8; k++) {
+          const uint32_t rr = r0 + k;
+#pragma unroll
+          for (uint32_t hsel = 0; hsel < 2; hsel++) {
+            const float4 w = v[k][hsel];
+            const float x[4] = {mul(w.x, sc), mul(w.y, sc), mul(w.z, sc), mul(w.w, sc)};
+            __half h[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) split_hi_lo(x[e], h[e], lo[e]);
+            const uint32_t dim = 128u * hsel + 4u * lane;
+            const uint32_t off = (dim >> 6) * kQChunk + rr * 128u + ((((dim & 63u) >> 3) ^ (rr & 7u)) << 4) +
+                                 (dim & 7u) * 2u;
+            *reinterpret_cast<uint2*>(qhi + off) =
+                make_uint2(h2_bits(__halves2half2(h[0], h[1])), h2_bits(__halves2half2(h[2], h[3])));
+            *reinterpret_cast<uint2*>(qlo + off) =
+                make_uint2(h2_bits(__halves2half2(lo[0], lo[1])), h2_bits(__halves2half2(lo[2], lo[3])));
+          }
+        }
       }
       proxy_fence();
       mb_arrive(&q_full);
@@ -349,9 +364,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
         float v[32];
 #pragma unroll
         for (int k = 0; k < 32; k++) v[k] = __fdiv_rn(__uint_as_float(o[k]), l);
-        float4* out4 = reinterpret_cast<float4*>(a.out + row_base + c0);
+        if (a.out) {   // (the f32 form, when the caller wants it)
+          float4* out4 = reinterpret_cast<float4*>(a.out + row_base + c0);
 #pragma unroll
-        for (int k = 0; k < 8; k++) out4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+          for (int k = 0; k < 8; k++) out4[k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+        }
         if (a.out_hi) {
           uint32_t hw[16], lw[16];
 #pragma unroll

@@ -1151,8 +1151,10 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       at.out_lo = xlo;
       at.kv_maps = b.kv_maps + l;
       at.error = b.gemm_error;
-      if (attention_tc_enabled() && fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim))
+      if (attention_tc_enabled() && fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) {
+        at.out = nullptr;   // (the output projection reads the f16 halves only)
         FZ_CUDA(fz::launch_attention_tc(at, st, pdl));
+      }
       else if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim))
         FZ_CUDA(fz::launch_attention_prefill(at, st, pdl));
       else
