@@ -502,6 +502,12 @@ cudaError_t launch_g(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
 
 }  // namespace
 
+bool attention_prefill_supported(uint32_t heads, uint32_t kv_heads, uint32_t head_dim) {
+  if (head_dim != kD || kv_heads == 0 || heads % kv_heads) return false;
+  const uint32_t g = heads / kv_heads;
+  return g == 1 || g == 2 || g == 4 || g == 8;
+}
+
 cudaError_t configure_attention_tc() {
   cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
   if (e == cudaSuccess)

@@ -817,13 +817,6 @@ bool decode_step_enabled() {
   return !(v && *v && *v != '0');
 }
 
-// The wide step's attention on tcgen05 (FRIZZLE_B200_ATTN_MMA_SYNC=1 selects
-// the mma.sync form instead, for comparison).
-bool attention_tc_enabled() {
-  const char* v = std::getenv("FRIZZLE_B200_ATTN_MMA_SYNC");
-  return !(v && *v && *v != '0');
-}
-
 fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st);
 
 // What a capture step adds after the forward pass (capture/capture.h): each
@@ -1151,13 +1144,10 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       at.out_lo = xlo;
       at.kv_maps = b.kv_maps + l;
       at.error = b.gemm_error;
-      if (attention_tc_enabled() && fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) {
+      if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) {
         at.out = nullptr;   // (the output projection reads the f16 halves only)
         FZ_CUDA(fz::launch_attention_tc(at, st, pdl));
-      }
-      else if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim))
-        FZ_CUDA(fz::launch_attention_prefill(at, st, pdl));
-      else
+      } else
         FZ_CUDA(fz::launch_attention(at, st, pdl));
       if ((stt = gemm(L.o, nullptr, b.x16_hi, xlo, b.y_attn, s.hidden, fz::kGemmWrite, l))) return stt;
       fz::MatvecArgs g = a;
@@ -1639,7 +1629,6 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
     if (fz::decode_supported(1, s.hidden, s.ffn, s.heads, s.kv_heads, s.head_dim))
       FZ_CUDA(fz::prepare_decode(s.hidden, s.ffn, s.heads, s.kv_heads));
     if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) {
-      FZ_CUDA(fz::configure_attention_prefill());
       FZ_CUDA(fz::configure_attention_tc());
     }
     FZ_CUDA(cudaMemcpy(b->dlayers, dl.data(), dl.size() * sizeof(fz::DecodeLayer), cudaMemcpyHostToDevice));

@@ -37,16 +37,12 @@ struct AttentionArgs {
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl);
 
-// The tensor-core form for steps of many rows (attention_prefill.cu): head
-// dimension 256, 1, 2 or 4 query heads a KV head; every row of a sequence at
-// consecutive positions from the step's.  configure_attention_prefill raises
-// its shared-memory limit on the current device (call outside stream capture).
+// The tensor-core form for steps of many rows (attention_tc.cu, tcgen05):
+// head dimension 256, 1, 2, 4 or 8 query heads a KV head, every row of a
+// sequence at consecutive positions from the step's, a.kv_maps the layer's
+// cache tensor maps; configure_attention_tc raises its shared-memory limit
+// on the current device (call outside stream capture).
 bool attention_prefill_supported(uint32_t heads, uint32_t kv_heads, uint32_t head_dim);
-cudaError_t configure_attention_prefill();
-cudaError_t launch_attention_prefill(const AttentionArgs& a, cudaStream_t stream, bool pdl);
-// The same on tcgen05 (attention_tc.cu): 1, 2, 4 or 8 query heads a KV
-// head, head dimension 256, a.kv_maps the layer's cache tensor maps;
-// configure_attention_tc raises its shared-memory limit (outside capture).
 cudaError_t configure_attention_tc();
 cudaError_t launch_attention_tc(const AttentionArgs& a, cudaStream_t stream, bool pdl);
 
