@@ -955,6 +955,8 @@ def run_trace(args):
         out["phases"][name] = {"handoff_us": float(np.mean([hand[0][l, ph] for l in rows]) / n),
                                "work_us": float(np.mean([hand[1][l, ph] for l in rows]) / n)}
         out["phases"][name].update({k: float(np.mean(v)) for k, v in spread[ph].items()})
+    # Each layer's phases (hand-off + work, us): the global layers stand out at long contexts.
+    out["layers"] = [[round(float((hand[0][l, ph] + hand[1][l, ph]) / n), 2) for ph in range(5)] for l in range(L)]
     print(json.dumps(out))
     batch.free()
     model.free()
