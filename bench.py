@@ -812,6 +812,8 @@ def main():
     ap.add_argument("--no-long", action="store_true", help="skip the config-5 long-context run")
     ap.add_argument("--no-c2", action="store_true", help="skip the config-2 product sweep")
     ap.add_argument("--c2-only", action="store_true", help="run only the config-2 product sweep and print it")
+    ap.add_argument("--profile-prefill-tokens", type=int, default=4096,
+                    help="the prompt length --profile-prefill steps (4096: config 3; 32: config 1's prompt)")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="run one config-3 4096-token prefill step between cudaProfilerStart/Stop (after a warm-up one)")
     ap.add_argument("--seqs", type=int, default=1, help="sequences a batch in --trace")
@@ -853,12 +855,13 @@ def main():
         dev = engine.Device(0)
         model = engine.Model.from_file(dev, synth.model_path(synth.GEMMA3_1B, 0))
         b = engine.Batch(model, 1, 8192)
-        ids = np.random.default_rng([0, 4096]).integers(2, synth.GEMMA3_1B.vocab, size=4096).astype(np.uint32)
-        b.step(0, ids, tokens=4096, logits=True)
+        n = args.profile_prefill_tokens
+        ids = np.random.default_rng([0, n]).integers(2, synth.GEMMA3_1B.vocab, size=n).astype(np.uint32)
+        b.step(0, ids, tokens=n, logits=True)
         b.wait()
         torch.cuda.synchronize()
         torch.cuda.profiler.start()
-        b.step(0, ids, tokens=4096, logits=True)
+        b.step(0, ids, tokens=n, logits=True)
         b.wait()
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()

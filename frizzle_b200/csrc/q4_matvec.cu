@@ -632,7 +632,19 @@ __global__ void __launch_bounds__(kThreads) norm_f16_kernel(const MatvecArgs a, 
 template <int NV>
 __global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecArgs a, __half* out_hi,
                                                                   __half* out_lo) {
+  // The gains are weights, not the previous launch's output: staged in
+  // shared memory before waiting for it.
+  __shared__ float4 gsm[2][NV * 32];
+  {
+    const float4* g4 = reinterpret_cast<const float4*>(a.norm.gain);
+    const float4* p4 = reinterpret_cast<const float4*>(a.norm.post_gain);
+    for (int i = threadIdx.x; i < NV * 32; i += kThreads) {
+      gsm[0][i] = g4[i];
+      if (p4) gsm[1][i] = p4[i];
+    }
+  }
   pdl_wait();
+  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t row = blockIdx.x * kWarps + warp;
   if (row < a.m) {
@@ -656,10 +668,9 @@ __global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecAr
 #pragma unroll
         for (int i = 0; i < NV; i++) p = add(p, dot_self(y[i]));
         const float s = inverse_sqrt(add(__fdiv_rn(warp_sum(p), wf), n.eps));
-        const float4* pg4 = reinterpret_cast<const float4*>(n.post_gain);
 #pragma unroll
         for (int i = 0; i < NV; i++) {
-          const float4 g = pg4[lane + 32 * i];
+          const float4 g = gsm[1][lane + 32 * i];
           y[i] = make_float4(mul(mul(y[i].x, s), g.x), mul(mul(y[i].y, s), g.y), mul(mul(y[i].z, s), g.z),
                              mul(mul(y[i].w, s), g.w));
         }
@@ -683,12 +694,11 @@ __global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecAr
       p = add(p, dot_self(x[i]));
     }
     const float s = inverse_sqrt(add(__fdiv_rn(warp_sum(p), wf), n.eps));
-    const float4* g4 = reinterpret_cast<const float4*>(n.gain);
     uint2* hi = reinterpret_cast<uint2*>(out_hi + (size_t)row * W);
     uint2* lo = out_lo ? reinterpret_cast<uint2*>(out_lo + (size_t)row * W) : nullptr;
 #pragma unroll
     for (int i = 0; i < NV; i++) {
-      const float4 g = g4[lane + 32 * i];
+      const float4 g = gsm[0][lane + 32 * i];
       const float v[4] = {mul(mul(x[i].x, s), g.x), mul(mul(x[i].y, s), g.y), mul(mul(x[i].z, s), g.z),
                           mul(mul(x[i].w, s), g.w)};
       __half h[4], l[4];
