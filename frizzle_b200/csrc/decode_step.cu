@@ -719,7 +719,10 @@ __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, con
                                       uint32_t cx, uint32_t cy) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int items = (int)a.hidden / 4;
-  const float wf = (float)a.hidden;
+  // (1 / width, rounded once: each reciprocal RMS is one multiply-add and
+  // the hardware reciprocal square root, within 2e-7 of the reference's
+  // division and inverseSqrt; the barriers before them stay the only wait)
+  const float inv_w = __frcp_rn((float)a.hidden);
   const float* gs = smem_f(a.lay.gains);   // gain [hidden], then the post gain [hidden]
   float* sums = smem_f(a.lay.part);        // [2][kCW] warp sums
   uint4* xf = reinterpret_cast<uint4*>(g_smem + a.lay.xf);
@@ -782,7 +785,7 @@ __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, con
     float s = 0.f;
 #pragma unroll
     for (int w = 0; w < kCW; w++) s = add(s, sums[w]);
-    ry = inverse_sqrt(add(__fdiv_rn(s, wf), a.eps));
+    ry = rsqrtf(__fmaf_rn(s, inv_w, a.eps));
   }
   const bool writer = blockIdx.x == 0;
   float* capbase = writer && a.capture ? a.capture : nullptr;
@@ -826,7 +829,7 @@ __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, con
   float s = 0.f;
 #pragma unroll
   for (int w = 0; w < kCW; w++) s = add(s, sums[kCW + w]);
-  const float rx = inverse_sqrt(add(__fdiv_rn(s, wf), a.eps));
+  const float rx = rsqrtf(__fmaf_rn(s, inv_w, a.eps));
   // The fragments of the row quad: row 0 the normed row, rows 1..3 zero.
   // Item i's slot of row r: uint4 (i / 4) * 16 + (i % 4) * 4 + r (part, then remainder).
 #pragma unroll
