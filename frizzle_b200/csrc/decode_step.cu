@@ -1433,10 +1433,11 @@ struct Attn {
         const float o0 = add(acc[i][0], r0), o1 = add(acc[i][1], r1);
         const uint32_t ep = phase_epoch(serial, l, kEpAttn);
         if (nsplit == 1) {
-          const float lsum = hstat()[GH + g];
+          // (times the reciprocal of the sum: within an ulp of the division)
+          const float rl = __frcp_rn(hstat()[GH + g]);
           unsigned long long* o = a.attn_ll + ((size_t)row * H + head) * kHd + dim;
-          st_ll(o, __fdiv_rn(o0, lsum), ep);
-          st_ll(o + 1, __fdiv_rn(o1, lsum), ep);
+          st_ll(o, mul(o0, rl), ep);
+          st_ll(o + 1, mul(o1, rl), ep);
         } else if (fold_in_o(nsplit, M)) {
           unsigned long long* o = a.part_o_ll + (((size_t)row * H + head) * kFoldInO + split) * kHd + dim;
           st_ll(o, o0, ep);
@@ -1640,7 +1641,8 @@ __device__ __noinline__ void fold_attention(const DecodeArgs& a, uint32_t M, uin
           m = mn;
         }
     }
-    out[i] = make_float4(__fdiv_rn(acc.x, l), __fdiv_rn(acc.y, l), __fdiv_rn(acc.z, l), __fdiv_rn(acc.w, l));
+    const float rl = __frcp_rn(l);   // (within an ulp of dividing each)
+    out[i] = make_float4(mul(acc.x, rl), mul(acc.y, rl), mul(acc.z, rl), mul(acc.w, rl));
   }
   cbar();
 }
