@@ -265,6 +265,7 @@ FZ_DEV bool cbar_or(bool p) {
 // phase, so a word left by an earlier layer, launch or step never passes.
 FZ_DEV uint32_t phase_epoch(uint32_t serial, uint32_t l, uint32_t ph) { return (serial << 8) | (l << 3) | ph; }
 constexpr uint32_t kEpAttn = 5;   // the attention's epoch phase (QKV, gate/up use their phase numbers)
+constexpr uint32_t kEpNormQkv = 6, kEpNormGate = 7;   // several rows: the normed rows before QKV, gate/up
 FZ_DEV void st_ll(unsigned long long* p, float v, uint32_t epoch) {
   const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
@@ -715,8 +716,14 @@ __device__ __noinline__ void norm_rows(const DecodeArgs& a, uint32_t M, const fl
 // sums' order is not the reference's 256-invocation tree: the difference is
 // a few f32 roundings of the statistics, far inside the 1e-3 bar.
 constexpr uint32_t kNormMaxSlices = kDecodeDownSlices > kDecodeOSlices ? kDecodeDownSlices : kDecodeOSlices;
+// Also for one row r of several (the row's X at xin, its slices ystride
+// apart, its X out at xout, the captures in sequence r's store, written by
+// this CTA when `writer`): with `words` the normed row goes out as
+// flag-in-data words words[r * hidden + c] under `epoch` instead of as this
+// CTA's fragments.
 __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, const float* y, uint32_t ny, float* xout,
-                                      uint32_t cx, uint32_t cy) {
+                                      uint32_t cx, uint32_t cy, uint32_t ystride, uint32_t row, bool writer,
+                                      unsigned long long* words, uint32_t epoch) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int items = (int)a.hidden / 4;
   // (1 / width, rounded once: each reciprocal RMS is one multiply-add and
@@ -750,7 +757,7 @@ __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, con
     for (uint32_t j = 0; j < kNormMaxSlices; j++) {
       ya[u][j] = yb[u][j] = make_float2(0.f, 0.f);
       if (y && j < ny && live[u]) {
-        const float* yj = y + (size_t)j * a.hidden + col[u];
+        const float* yj = y + (size_t)j * ystride + col[u];
         ya[u][j] = __ldcg(reinterpret_cast<const float2*>(yj));
         yb[u][j] = __ldcg(reinterpret_cast<const float2*>(yj + 16));
       }
@@ -787,8 +794,7 @@ __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, con
     for (int w = 0; w < kCW; w++) s = add(s, sums[w]);
     ry = rsqrtf(__fmaf_rn(s, inv_w, a.eps));
   }
-  const bool writer = blockIdx.x == 0;
-  float* capbase = writer && a.capture ? a.capture : nullptr;
+  float* capbase = writer && a.capture ? a.capture + (size_t)row * a.capture_stride : nullptr;
   float* xc = capbase && (cx & 3) ? capbase + cap_offset(a, cx) : nullptr;
   float* yc = capbase && (cy & 3) ? capbase + cap_offset(a, cy) : nullptr;
   float p = 0.f;
@@ -832,6 +838,18 @@ __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, con
   const float rx = rsqrtf(__fmaf_rn(s, inv_w, a.eps));
   // The fragments of the row quad: row 0 the normed row, rows 1..3 zero.
   // Item i's slot of row r: uint4 (i / 4) * 16 + (i % 4) * 4 + r (part, then remainder).
+  if (words) {
+    unsigned long long* wr = words + (size_t)row * a.hidden;
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+      if (!live[u]) continue;
+      const int cc[4] = {col[u], col[u] + 1, col[u] + 16, col[u] + 17};
+#pragma unroll
+      for (int e = 0; e < 4; e++) st_ll(wr + cc[e], mul(mul(x[u][e], rx), gs[cc[e]]), epoch);
+    }
+    cbar();
+    return;
+  }
 #pragma unroll
   for (int u = 0; u < 2; u++) {
     if (!live[u]) continue;
@@ -1776,6 +1794,14 @@ struct Consumer {
       pg = L.post_ffw_norm;
       gain = a.output_norm;
     }
+    // Several rows: CTA r < M norms row r and publishes it (the counter and
+    // the gains are its alone); every CTA then stages the normed rows.
+    const bool one = MQ == 1 && M == 1;
+    const bool split_norm = !one && (kind == kPhQkv || kind == kPhGate);
+    if (split_norm && blockIdx.x >= M) {
+      ctr = nullptr;
+      gain = nullptr;
+    }
     // The norm's gains do not depend on the step: copy them before waiting.
     if (gain) {
       const int V = (int)a.hidden / 4;
@@ -1797,27 +1823,37 @@ struct Consumer {
     pslots = 0;
     ph_kind = kind;
     ph_l = l;
-    // One row: the norm writes the fragments itself (norm_one).
-    const bool one = MQ == 1 && M == 1;
+    // One row: the norm writes the fragments itself (norm_one).  Several:
+    // row r's norm by CTA r into words, every CTA's fragments from them.
+    const uint32_t H = a.hidden, r = blockIdx.x;
     if (kind == kPhQkv) {
       const float* y = l > 0 ? a.y_mlp : nullptr;
       const uint32_t cy = l > 0 ? cap_slot(l - 1, kCapMlpAdded) : kCapNone;
       if (one) {
-        norm_one(a, a.hidden_a, y, kDecodeDownSlices, a.hidden_b, cap_slot(l, kCapResidual), cy);
+        norm_one(a, a.hidden_a, y, kDecodeDownSlices, a.hidden_b, cap_slot(l, kCapResidual), cy, H, 0,
+                 blockIdx.x == 0, nullptr, 0);
       } else {
-        norm_rows(a, M, a.hidden_a, y, kDecodeDownSlices, a.hidden_b, cap_slot(l, kCapResidual), cy);
-        fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+        const uint32_t ep = phase_epoch(serial(), l, kEpNormQkv);
+        if (r < M)
+          norm_one(a, a.hidden_a + (size_t)r * H, y ? y + (size_t)r * H : nullptr, kDecodeDownSlices,
+                   a.hidden_b + (size_t)r * H, cap_slot(l, kCapResidual), cy, M * H, r, true, a.norm_ll, ep);
+        fragments_ll<MQ>(a, M, a.norm_ll, H, kb0, nkb, ep);
       }
     } else if (kind == kPhGate) {
       if (one) {
-        norm_one(a, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, kCapNone, cap_slot(l, kCapAttnAdded));
+        norm_one(a, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, kCapNone, cap_slot(l, kCapAttnAdded), H, 0,
+                 blockIdx.x == 0, nullptr, 0);
       } else {
-        norm_rows(a, M, a.hidden_b, a.y_attn, kDecodeOSlices, a.hidden_a, kCapNone, cap_slot(l, kCapAttnAdded));
-        fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);
+        const uint32_t ep = phase_epoch(serial(), l, kEpNormGate);
+        if (r < M)
+          norm_one(a, a.hidden_b + (size_t)r * H, a.y_attn + (size_t)r * H, kDecodeOSlices, a.hidden_a + (size_t)r * H,
+                   kCapNone, cap_slot(l, kCapAttnAdded), M * H, r, true, a.norm_ll, ep);
+        fragments_ll<MQ>(a, M, a.norm_ll, H, kb0, nkb, ep);
       }
     } else if (kind == kPhHead) {
       if (one) {
-        norm_one(a, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, kCapNone, cap_slot(Ln - 1, kCapMlpAdded));
+        norm_one(a, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, kCapNone, cap_slot(Ln - 1, kCapMlpAdded), H, 0,
+                 blockIdx.x == 0, nullptr, 0);
       } else {
         norm_rows(a, M, a.hidden_a, a.y_mlp, kDecodeDownSlices, nullptr, kCapNone, cap_slot(Ln - 1, kCapMlpAdded));
         fragments<MQ, false>(a, M, rowbuf(), a.hidden, kb0, nkb);

@@ -76,6 +76,9 @@ struct DecodeArgs {
   // [rows][heads][8][2], all as flag-in-data words the output projection polls.
   unsigned long long* attn_ll;
   unsigned long long* act_ll;      // the gated activation [kDecodeMaxRows][ffn] (flag-in-data)
+  // Several rows: each norm's normed rows [kDecodeMaxRows][hidden] (flag-in-data), row r made by CTA r
+  // and read by every CTA for its fragments.
+  unsigned long long* norm_ll;
   unsigned long long* part_o_ll;
   unsigned long long* part_ml_ll;
   float* attn;                     // [m][heads 256]

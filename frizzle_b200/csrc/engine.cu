@@ -305,6 +305,7 @@ struct fz_batch {
   std::vector<uint32_t> windows;
   // The decode kernel's flag-in-data words: QKV products, attention output and
   // few-split partials, gated activation.
+  unsigned long long *norm_ll = nullptr;
   unsigned long long *qkv_ll = nullptr, *attn_ll = nullptr, *part_o_ll = nullptr, *part_ml_ll = nullptr,
                      *act_ll = nullptr;
   std::map<GraphKey, cudaGraphExec_t> graphs;
@@ -687,7 +688,7 @@ BatchBytes batch_bytes(const Shape& s, uint32_t S, uint32_t context, uint32_t ro
   const uint64_t Q = (uint64_t)s.heads * s.head_dim, KV = (uint64_t)s.kv_heads * s.head_dim;
   const uint64_t R8 = (uint64_t)fz::kDecodeMaxRows * 8, V = s.vocab, T16 = fz::kMaxTokens;
   const uint64_t tiles = fz::select_tiles(s.vocab), table_words = 2ull * s.layers + 5ull * kMaxEdits;
-  uint64_t f = R8 * (Q + 2 * KV) + R8 * Q + R8 * s.ffn + R8 * s.heads * fz::kDecodeFoldSplits * s.head_dim +
+  uint64_t f = R8 * s.hidden + R8 * (Q + 2 * KV) + R8 * Q + R8 * s.ffn + R8 * s.heads * fz::kDecodeFoldSplits * s.head_dim +
                R8 * s.heads * fz::kDecodeFoldSplits * 2;
   f += S * V * 4 + S * 8 + S * tiles * 64 * 8 + S * 128 * 4 + S * 16 + 64 + S * 8 + 16 + S * table_words * 4 +
        S * capture_layout(s).words * 4 + T16 * s.hidden * 4 + T16 * V * 4 + T16 * 8 + T16 * tiles * 64 * 8;
@@ -971,6 +972,7 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
     d.qkv_ll = b.qkv_ll;
     d.attn_ll = b.attn_ll;
     d.act_ll = b.act_ll;
+    d.norm_ll = b.norm_ll;
     d.part_o_ll = b.part_o_ll;
     d.part_ml_ll = b.part_ml_ll;
     d.attn = b.attn;
@@ -1619,7 +1621,8 @@ fz_status fz_batch_create(fz_model* m, uint32_t sequences, uint32_t context, uin
         return fail(FZ_ERR_CUDA, "cuTensorMapEncodeTiled refused the key/value cache maps");
     }
     const size_t R8 = (size_t)fz::kDecodeMaxRows * 8;   // rows x bytes a word
-    if ((st = b->alloc(&b->qkv_ll, R8 * (s.heads + 2 * s.kv_heads) * s.head_dim)) ||
+    if ((st = b->alloc(&b->norm_ll, R8 * s.hidden)) ||
+        (st = b->alloc(&b->qkv_ll, R8 * (s.heads + 2 * s.kv_heads) * s.head_dim)) ||
         (st = b->alloc(&b->attn_ll, R8 * s.heads * s.head_dim)) || (st = b->alloc(&b->act_ll, R8 * s.ffn)) ||
         (st = b->alloc(&b->part_o_ll, R8 * s.heads * fz::kDecodeFoldSplits * s.head_dim)) ||
         (st = b->alloc(&b->part_ml_ll, R8 * s.heads * fz::kDecodeFoldSplits * 2)) ||
