@@ -977,7 +977,7 @@ __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const
         if (!*abort && !error_word(a.error)) atomicOr(a.error, kErrCounter);
         break;
       }
-      __nanosleep(it < 4 ? 64u : 256u);
+      __nanosleep(it < 4 ? 32u : 64u);
     }
 #pragma unroll
     for (int u = 0; u < U; u++) {
