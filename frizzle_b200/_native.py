@@ -125,6 +125,7 @@ SIGNATURES = {
     "fz_split_f16": (C.c_int, [VP, C.c_size_t, VP, VP, VP]),
     "fz_attention": (C.c_int, [VP, VP, VP, U32, U32, U32, U32, U32, U32, U32, VP, VP, VP, VP, VP]),
     "fz_attention_splits": (U32, [U32, U32, U32]),
+    "fz_attention_wide": (C.c_int, [VP, VP, VP, U32, U32, U32, U32, U32, U32, U32, VP, VP, VP, VP, VP, VP]),
     "fz_attention_static": (C.c_int, [VP, VP, VP, U32, U32, U32, U32, U32, U32, U32, VP, VP]),
 }
 

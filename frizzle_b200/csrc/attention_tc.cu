@@ -26,6 +26,14 @@
 // At the end each row's O / l is written as f16 part and remainder (the
 // output projection's operands) and, when asked for, as f32.
 //
+// Causal blocks are uneven: block i of a long prompt has i + 1 key tiles, so
+// with one CTA a block the last block sets the launch's time.  When the
+// launch's blocks fit one wave, each block gets a pair of CTAs, and a block
+// of more than split_tiles tiles runs its two halves of keys on the two: each
+// half writes its unnormalised O with its m and l, takes a ticket, and the
+// second merges (O1 2^(m1-m) + O2 2^(m2-m)) / (l1 2^(m1-m) + l2 2^(m2-m)),
+// m = max(m1, m2), and writes the block out; nothing waits on the other CTA.
+//
 // Every mbarrier wait is bounded; a wait that gives up records an error, the
 // CTA waits (bounded) for the copies and products it issued, releases its
 // tensor memory and returns.
@@ -165,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
   __shared__ __align__(8) uint64_t s_full[2], s_empty[2];
   __shared__ __align__(8) uint64_t q_full, p_full, pv_done, drain;
   __shared__ uint32_t tmem_base;
-  __shared__ uint32_t fail_word;
+  __shared__ uint32_t fail_word, ticket_word;
   unsigned char* smem = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
   unsigned char* qhi = smem;
   unsigned char* qlo = smem + kQBytes;
@@ -177,7 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t T = a.seq_tokens;
   const uint32_t nblk = (T + QT - 1) / QT;
-  const uint32_t blk = nblk - 1 - blockIdx.x;   // the latest tokens (the most keys) first
+  const uint32_t parts = gridDim.x / nblk;   // 2 when the longest blocks' keys split in two
+  // The latest tokens (the most keys) first; a block's two halves side by side.
+  const uint32_t blk = nblk - 1 - blockIdx.x / parts, part = blockIdx.x % parts;
   const uint32_t kvh = blockIdx.y, seq = blockIdx.z, t0 = blk * QT;
   const Fail f{reinterpret_cast<volatile uint32_t*>(&fail_word), a.error};
 
@@ -217,10 +227,27 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
   const uint32_t ntok = min(QT, T - t0);
   const uint32_t p_last = pos0 + ntok - 1;
   const uint32_t k_lo = pos0 + 1 > a.window ? pos0 + 1 - a.window : 0u;   // the earliest key any row reads
-  const uint32_t kt0 = k_lo / kKT * kKT;
-  const uint32_t ntiles = (p_last - kt0) / kKT + 1;
+  uint32_t kt0 = k_lo / kKT * kKT;
+  uint32_t ntiles = (p_last - kt0) / kKT + 1;
+  // A block of more than split_tiles tiles: this CTA takes one half of its
+  // tiles (the second half holds every row's own key); otherwise the second
+  // CTA of the pair has nothing to do.
+  const bool split = parts == 2 && ntiles > a.split_tiles;
+  if (split) {
+    const uint32_t h = ntiles / 2;
+    if (part == 0)
+      ntiles = h;
+    else {
+      kt0 += h * kKT;
+      ntiles -= h;
+    }
+  } else if (part == 1)
+    ntiles = 0;
+  const uint32_t sidx = (seq * gridDim.y + kvh) * nblk + blk;   // the block's split slot and counter
 
-  if (warp < 4) {
+  if (ntiles == 0) {
+    // (the empty second CTA of a block that did not split)
+  } else if (warp < 4) {
     // ---- softmax: thread r is query row r (TMEM lane r).
     const uint32_t r = threadIdx.x, hh = r / QT, t = r % QT;
     const bool live = t < ntok;
@@ -231,13 +258,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       // K-major 64-dimension chunks with 128-byte swizzle (16-byte unit u of
       // row r at unit u ^ (r % 8)).  Warp w reads rows 32 w .. 32 w + 31 a
       // whole row at a time (lane l: dimensions 4 l .. 4 l + 3 and 128 + 4 l
-      // ..), eight rows' loads in flight.
+      // ..), sixteen rows' loads in flight.
       const float sc = a.scale_log2e;
 #pragma unroll 1
-      for (uint32_t r0 = warp * 32u; r0 < warp * 32u + 32u; r0 += 8) {
-        float4 v[8][2];
+      for (uint32_t r0 = warp * 32u; r0 < warp * 32u + 32u; r0 += 16) {
+        float4 v[16][2];
 #pragma unroll
-        for (uint32_t k = 0; k < 8; k++) {
+        for (uint32_t k = 0; k < 16; k++) {
           const uint32_t rr = r0 + k, tt = rr % QT;
           v[k][0] = v[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
           if (tt < ntok) {
@@ -248,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
           }
         }
 #pragma unroll
-        for (uint32_t k = 0; k < 8; k++) {
+        for (uint32_t k = 0; k < 16; k++) {
           const uint32_t rr = r0 + k;
 #pragma unroll
           for (uint32_t hsel = 0; hsel < 2; hsel++) {
@@ -354,16 +381,62 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       tc_fence_after();
     }
     pdl_launch_dependents();
-    if (ok) {
-      // out = O / l, and its f16 part and remainder.
+    // A split block: each half writes its O, m and l (row r at column-major
+    // offsets, so a warp's stores are consecutive) and takes a ticket; the
+    // second to take one merges the other's into its own and writes out.
+    bool write = ok;
+    const float* other = nullptr;
+    float c_own = 1.f, c_oth = 0.f;
+    if (split) {
+      float* mine = a.split_part + ((size_t)sidx * 2 + part) * kAttnSplitFloats;
+      if (ok) {
+#pragma unroll 1
+        for (uint32_t c0 = 0; c0 < kD; c0 += 32) {
+          uint32_t o[32];
+          tmem_ld32(lane_addr + c0, o);
+          if (!live) continue;   // (after the warp-wide load)
+#pragma unroll
+          for (int k = 0; k < 32; k++) __stcg(mine + (c0 + k) * kRows + r, __uint_as_float(o[k]));
+        }
+        __stcg(mine + kD * kRows + r, m);
+        __stcg(mine + (kD + 1) * kRows + r, l);
+      }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (r == 0) ticket_word = atomicAdd(a.counters + sidx, 1u);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (ticket_word == 0u)
+        write = false;   // the other half, still running, merges
+      else {
+        if (r == 0) a.counters[sidx] = 0u;   // zero again for the next launch
+        __threadfence();
+        other = a.split_part + ((size_t)sidx * 2 + (1u - part)) * kAttnSplitFloats;
+        if (write && live) {
+          const float m1 = __ldcg(other + kD * kRows + r), l1 = __ldcg(other + (kD + 1) * kRows + r);
+          const float mm = fmaxf(m, m1);
+          c_own = m == -INFINITY ? 0.f : exp2f(m - mm);
+          c_oth = m1 == -INFINITY ? 0.f : exp2f(m1 - mm);
+          l = __fmaf_rn(l1, c_oth, mul(l, c_own));
+        }
+      }
+    }
+    if (write) {
+      // out = O / l (by one reciprocal), and its f16 part and remainder.
+      const float inv = __frcp_rn(l);
 #pragma unroll 1
       for (uint32_t c0 = 0; c0 < kD; c0 += 32) {
         uint32_t o[32];
         tmem_ld32(lane_addr + c0, o);
         if (!live) continue;   // (after the warp-wide load)
         float v[32];
+        if (other) {
 #pragma unroll
-        for (int k = 0; k < 32; k++) v[k] = __fdiv_rn(__uint_as_float(o[k]), l);
+          for (int k = 0; k < 32; k++)
+            v[k] = mul(__fmaf_rn(__ldcg(other + (c0 + k) * kRows + r), c_oth, mul(__uint_as_float(o[k]), c_own)), inv);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; k++) v[k] = mul(__uint_as_float(o[k]), inv);
+        }
         if (a.out) {   // (the f32 form, when the caller wants it)
           float4* out4 = reinterpret_cast<float4*>(a.out + row_base + c0);
 #pragma unroll
@@ -485,9 +558,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
 template <int G>
 cudaError_t launch_g(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
   constexpr uint32_t QT = kRows / G;
-  const uint32_t seqs = a.m / a.seq_tokens;
+  const uint32_t seqs = a.m / a.seq_tokens, nblk = (a.seq_tokens + QT - 1) / QT;
+  // Pairs of CTAs a block when its keys may split: one wave of blocks at most
+  // (more waves balance without it) and a window past split_tiles tiles.
+  const bool pairs = a.split_part && a.counters && a.split_tiles &&
+                     (uint64_t)nblk * a.kv_heads * seqs <= kAttnSplitBlocks && a.window > a.split_tiles * kKT;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.seq_tokens + QT - 1) / QT, a.kv_heads, seqs);
+  cfg.gridDim = dim3(nblk * (pairs ? 2u : 1u), a.kv_heads, seqs);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;

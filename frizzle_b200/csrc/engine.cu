@@ -239,6 +239,7 @@ struct fz_batch {
   float *hidden_a = nullptr, *hidden_b = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr,
         *y_attn = nullptr, *y_mlp = nullptr, *act = nullptr, *logits = nullptr;
   float *partial_o = nullptr, *partial_ml = nullptr;
+  float* attn_split = nullptr;   // the tensor-core attention's split halves (kAttnSplitBlocks x 2)
   uint32_t* counters = nullptr;   // per layer: 1 QKV + M*kv attention counters
   uint32_t counters_per_layer = 0;
   uint32_t splits_max = 0;
@@ -668,6 +669,18 @@ std::vector<uint32_t> layer_windows(const Shape& s) {
   return w;
 }
 
+// The tensor-core attention splits the keys of a block longer than this many
+// 32-key tiles over two CTAs, when one wave holds all its blocks (a window
+// layer's blocks stay whole: 512 keys are at most 17 tiles).
+constexpr uint32_t kAttnSplitTiles = 40;
+static_assert(FZ_ATTENTION_WIDE_SPLIT_FLOATS == fz::kAttnSplitBlocks * 2 * fz::kAttnSplitFloats, "split scratch size");
+
+// Its split halves: wide steps (more than 16 rows) with the tensor-core form.
+uint64_t attn_split_bytes(const Shape& s, uint64_t rows) {
+  if (rows <= (uint64_t)fz::kMaxTokens || !fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) return 0;
+  return (uint64_t)fz::kAttnSplitBlocks * 2 * fz::kAttnSplitFloats * 4;
+}
+
 // The device bytes of a batch, counted with the expressions its allocations
 // use (fz_batch_create, alloc_rows): the key/value rings, and the scratch
 // for `rows` token rows a step.
@@ -696,7 +709,7 @@ BatchBytes batch_bytes(const Shape& s, uint32_t S, uint32_t context, uint32_t ro
   const uint64_t PM = fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim) ? std::min<uint64_t>(M, T16) : M;
   f += M * s.hidden * 4 * 2 + M * (Q + 2 * KV) * 4 + M * Q * 4 * 2 + M * s.hidden * 4 * 2 + M * s.ffn * 4 +
        PM * s.heads * splits_max * s.head_dim * 4 + PM * s.heads * splits_max * 2 * 4 +
-       (uint64_t)s.layers * (1 + M * s.kv_heads) * 4 + M * 4 + M * X * 2 * 2 + M * s.ffn * 2 * 2 +
+       attn_split_bytes(s, rows) + (uint64_t)s.layers * (1 + M * s.kv_heads) * 4 + M * 4 + M * X * 2 * 2 + M * s.ffn * 2 * 2 +
        (fz::kDecodeOSlices + fz::kDecodeDownSlices) * M * s.hidden * 4 +
        fz::decode_sync_words(s.layers, (uint32_t)M, s.kv_heads) * 4;
   out.scratch = f;
@@ -794,6 +807,7 @@ fz_status alloc_rows(fz_batch& b, uint32_t rows) {
       (st = b.alloc_row(&b.y_mlp, M * s.hidden * 4)) || (st = b.alloc_row(&b.act, M * s.ffn * 4)) ||
       (st = b.alloc_row(&b.partial_o, PM * s.heads * b.splits_max * s.head_dim * 4)) ||
       (st = b.alloc_row(&b.partial_ml, PM * s.heads * b.splits_max * 2 * 4)) ||
+      (st = b.alloc_row(&b.attn_split, attn_split_bytes(s, rows))) ||
       (st = b.alloc_row(&b.counters, (size_t)s.layers * b.counters_per_layer * 4)) ||
       (st = b.alloc_row(&b.dids, M * 4)) || (st = b.alloc_row(&b.x16_hi, M * X * 2)) ||
       (st = b.alloc_row(&b.x16_lo, M * X * 2)) || (st = b.alloc_row(&b.act16_hi, M * s.ffn * 2)) ||
@@ -1146,6 +1160,8 @@ fz_status enqueue_forward(fz_batch& b, const GraphKey& key, cudaStream_t st) {
       at.out_lo = xlo;
       at.kv_maps = b.kv_maps + l;
       at.error = b.gemm_error;
+      at.split_part = attn_split_bytes(s, b.rows_cap) ? b.attn_split : nullptr;
+      at.split_tiles = kAttnSplitTiles;
       if (fz::attention_prefill_supported(s.heads, s.kv_heads, s.head_dim)) {
         at.out = nullptr;   // (the output projection reads the f16 halves only)
         FZ_CUDA(fz::launch_attention_tc(at, st, pdl));
@@ -2261,6 +2277,54 @@ fz_status fz_attention(const float* q, const void* key_cache, const void* value_
   at.counters = counters;
   at.out = out;
   FZ_CUDA(fz::launch_attention(at, static_cast<cudaStream_t>(stream), false));
+  return FZ_OK;
+}
+
+fz_status fz_attention_wide(const float* q, const void* key_cache, const void* value_cache, uint32_t slots,
+                            uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t window, uint32_t position,
+                            uint32_t rows, void* maps, float* split_part, uint32_t* counters, float* out,
+                            uint32_t* error, void* stream) {
+  if (!q || !key_cache || !value_cache || !out || !maps) return fail(FZ_ERR_ARGUMENT, "null pointer");
+  if (reinterpret_cast<uintptr_t>(maps) & 63u) return fail(FZ_ERR_ARGUMENT, "maps not 64-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(key_cache) | reinterpret_cast<uintptr_t>(value_cache)) & 15u)
+    return fail(FZ_ERR_ARGUMENT, "caches not 16-byte aligned");
+  if (!fz::attention_prefill_supported(heads, kv_heads, head_dim))
+    return fail(FZ_ERR_ARGUMENT, "head dimension 256 and 1, 2, 4 or 8 heads per KV head only");
+  if (rows == 0 || window == 0 || slots == 0) return fail(FZ_ERR_ARGUMENT, "rows, window and slots must be nonzero");
+  if (slots % 32) return fail(FZ_ERR_ARGUMENT, "slots must be a multiple of 32 (whole key tiles)");
+  if ((uint64_t)position + rows > (1u << 24)) return fail(FZ_ERR_ARGUMENT, "position past 2^24");
+  if (split_part && !counters) return fail(FZ_ERR_ARGUMENT, "split scratch needs its counters");
+  fz::DecodeLayer d{};
+  d.key_cache = static_cast<uint16_t*>(const_cast<void*>(key_cache));
+  d.value_cache = static_cast<uint16_t*>(const_cast<void*>(value_cache));
+  d.slots = slots;
+  d.seq_stride = (uint64_t)slots * kv_heads * head_dim;
+  fz::DecodeKvMaps host{};
+  if (!fz::make_kv_maps(host, d, kv_heads, 1)) return fail(FZ_ERR_CUDA, "cache tensor maps refused");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  FZ_CUDA(fz::configure_attention_tc());
+  // (from pageable memory: the copy has taken `host` when the call returns)
+  FZ_CUDA(cudaMemcpyAsync(maps, &host, sizeof(host), cudaMemcpyHostToDevice, st));
+  fz::AttentionArgs at{};
+  at.position = position;
+  at.q = q;
+  at.key_cache = d.key_cache;
+  at.value_cache = d.value_cache;
+  at.slots = slots;
+  at.heads = heads;
+  at.kv_heads = kv_heads;
+  at.head_dim = head_dim;
+  at.window = window;
+  at.seq_tokens = rows;
+  at.m = rows;
+  at.scale_log2e = (float)((double)(1.0f / std::sqrt((float)head_dim)) * 1.4426950408889634);
+  at.counters = counters;
+  at.out = out;
+  at.kv_maps = maps;
+  at.error = error;
+  at.split_part = split_part;
+  at.split_tiles = split_part ? kAttnSplitTiles : 0u;
+  FZ_CUDA(fz::launch_attention_tc(at, st, false));
   return FZ_OK;
 }
 

@@ -33,7 +33,18 @@ struct AttentionArgs {
   // and a device word set nonzero when one of its bounded waits gives up.
   const void* kv_maps;
   uint32_t* error;
+  // Its key-range split: with split_part set, at most kAttnSplitBlocks
+  // (sequence, KV head, query block)s in the launch and a window longer than
+  // split_tiles 32-key tiles, a block of more than split_tiles tiles runs as
+  // two CTAs over the two halves of its keys; each writes its unnormalised O,
+  // m and l to split_part[block][half] (kAttnSplitFloats floats) and takes a
+  // ticket from counters[block], and the second merges the two.
+  float* split_part;
+  uint32_t split_tiles;
 };
+
+constexpr uint32_t kAttnSplitBlocks = 148;          // one wave of CTAs
+constexpr uint32_t kAttnSplitFloats = 258u * 128u;  // O [256][128 rows], m [128], l [128]
 
 cudaError_t launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl);
 

@@ -172,6 +172,55 @@ def test_attention_vs_oracle(rows, position, window, slots):
     assert int(cnt.abs().sum()) == 0  # the counters are left at zero for the next launch
 
 
+WIDE_CASES = [
+    # (heads, kv_heads, rows, position, window, slots)
+    (4, 1, 1600, 0, 32768, 2048),    # 50 blocks of 32 tokens: those of more than 40 key tiles split
+    (4, 1, 300, 1000, 32768, 2048),  # a later step: its blocks start past position 1000
+    (8, 1, 1400, 0, 32768, 2048),    # 16-token blocks
+    (4, 2, 1500, 0, 32768, 2048),    # two KV heads, 64-token blocks
+    (4, 1, 700, 1900, 512, 1024),    # a window layer over a ring (key j at slot j mod 1024): never split
+]
+_WIDE_WANT = {}
+
+
+@pytest.mark.parametrize("split", [False, True])
+@pytest.mark.parametrize("heads,kv,rows,position,window,slots", WIDE_CASES)
+def test_attention_wide_vs_oracle(heads, kv, rows, position, window, slots, split):
+    """The tensor-core attention (fz_attention_wide) on every row against the
+    oracle, whole blocks and, with split scratch, long blocks whose two halves
+    of keys run on two CTAs and merge."""
+    torch = torch_cuda()
+    lib = _native.load()
+    d = 256
+    rng = np.random.default_rng([heads, kv, rows, position])
+    q = rng.standard_normal((rows, heads, d)).astype(np.float32)
+    kc = (rng.standard_normal((slots, kv, d)) * 0.5).astype(np.float16).view(np.uint16)
+    vc = rng.standard_normal((slots, kv, d)).astype(np.float16).view(np.uint16)
+    scale = float(np.float32(np.float64(np.float32(1.0) / np.sqrt(np.float32(d))) * 1.4426950408889634))
+    key = (heads, kv, rows, position, window, slots)
+    if key not in _WIDE_WANT:
+        _WIDE_WANT[key] = oracle.attention(q, kc, vc, slots, kv, window, scale, position)
+    want = _WIDE_WANT[key]
+    qd, kd, vd = dev(q), dev(kc.view(np.int16)), dev(vc.view(np.int16))
+    maps = torch.zeros(64, dtype=torch.int32, device="cuda")   # 256 bytes (torch aligns to 256)
+    part = torch.empty(148 * 2 * 258 * 128, dtype=torch.float32, device="cuda") if split else None
+    cnt = torch.zeros(148, dtype=torch.int32, device="cuda")
+    err_word = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.full((rows, heads, d), float("nan"), dtype=torch.float32, device="cuda")
+    _native.check(lib.fz_attention_wide(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), slots, heads, kv, d, window,
+                                        position, rows, maps.data_ptr(), part.data_ptr() if split else None,
+                                        cnt.data_ptr(), out.data_ptr(), err_word.data_ptr(), stream()))
+    torch.cuda.synchronize()
+    assert int(err_word.item()) == 0
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    err = np.sqrt(np.mean((got.astype(np.float64) - want) ** 2)) / np.sqrt(np.mean(want.astype(np.float64) ** 2))
+    print(f"wide attention {key} split={split} rel_rms={err:.3e}")
+    assert err < 1e-4, err
+    assert np.abs(got - want).max() <= 1e-3 * np.abs(want).max()
+    assert int(cnt.abs().sum()) == 0  # the split counters are left at zero for the next launch
+
+
 def split_dev(x):
     torch = torch_cuda()
     lib = _native.load()

@@ -280,6 +280,16 @@ def test_tiny_model_chunked_wide_prefill(tiny_model_path, S):
     run_batch(tiny_model_path, s, S, 700, 6, edit_sets=edits, block=256)
 
 
+@pytest.mark.parametrize("n_prompt,block", [(2048, 2048), (2100, 1024)])
+def test_tiny_model_split_key_ranges(tiny_model_path, n_prompt, block):
+    # Long causal blocks of the global layer (5) split their keys over two CTAs
+    # of the tensor-core attention and the second to finish merges: a
+    # 2048-token step (blocks of up to 64 key tiles), and 1024-token steps
+    # whose later blocks start past position 1024 (the third step's 52 rows
+    # at position 2048, ~66 tiles each).
+    assert_parity(run_both(tiny_model_path, synth.TINY, n_prompt, 4, block=block))
+
+
 @pytest.mark.parametrize("S", [3, 6])
 def test_tiny_model_batch_decode(tiny_model_path, S):
     # 3 sequences: one column quad of the decode kernel's fragments; 6: two.
