@@ -5,24 +5,29 @@
 //
 // A CTA takes one sequence, one KV head and QT = 128 / G tokens of each of
 // the G query heads that share it: 128 query rows, row r = head (r / QT),
-// token (r % QT), one row a TMEM lane.  Keys go 32 at a time:
+// token (r % QT), one row a TMEM lane.  Keys go 64 at a time:
 //   - warps 4 and 6 (one lane each) bring each tile's keys, and its values,
 //     by TMA from the cache (4D tensor maps, 32-slot x 64-dimension boxes,
-//     128-byte swizzle) into a three-stage key ring, freed as each score
-//     product completes, and a two-stage value ring, freed as each P V does
-//     (the keys run a tile further ahead, so a copy's latency hides behind
-//     the products of the tiles before it);
-//   - warp 5 (one lane) issues tcgen05.mma: S = Q K^T (M = 128, N = 32) into
-//     one of two TMEM score buffers, Q as f16 part and remainder (two MMAs a
-//     16-dimension step, so the products are exact and the sums f32), then
-//     O += P V (N = 256, V read MN-major straight from the tile) into a
-//     TMEM accumulator, P as f16 part and remainder;
-//   - warps 0..3 (thread = row) read their row's 32 scores (tcgen05.ld), mask
+//     two a 64-dimension chunk, 128-byte swizzle) into two-stage key and
+//     value rings, freed as each score product, or P V, completes; the value
+//     ring first carries Q's f16 part on its way to tensor memory;
+//   - warp 5 (one lane) issues tcgen05.mma: S = Q K^T (M = 128, N = 64) into
+//     one of two TMEM score buffers, Q as f16 part (read from tensor memory)
+//     and remainder (from shared memory), two MMAs a 16-dimension step, so
+//     the products are exact and the sums f32; then O += P V (N = 256, V read
+//     MN-major straight from the tile) into a TMEM accumulator, P as f16 part
+//     and remainder;
+//   - warps 0..3 (thread = row) read their row's 64 scores (tcgen05.ld), mask
 //     them (causal, window, rows past the step), keep the online softmax
 //     (max m, sum l), write P to shared memory and, when a tile's max passes
 //     m by more than 8 (log2 units), rescale O in TMEM (tcgen05.ld/st) first;
 //     in between, the exponent base may lag the true max by up to 8, which
 //     keeps P <= 256 and leaves the result the same softmax.
+// A score MMA of N = 32 took ~49 cycles whether A came from shared or tensor
+// memory, so the tiles are 64 keys: half the MMAs, barriers and waits a key.
+// Every f16 part and remainder is made two values at a time (split2: one
+// paired conversion each), since single conversions ran on the slow
+// conversion pipe and bounded the query load, the softmax and the epilogue.
 // At the end each row's O / l is written as f16 part and remainder (the
 // output projection's operands) and, when asked for, as f32.
 //
@@ -50,17 +55,21 @@ using namespace q4dev;
 
 constexpr uint32_t kD = 256;              // head dimension
 constexpr uint32_t kRows = 128;           // query rows a CTA (the MMA's M)
-constexpr uint32_t kKT = 32;              // keys a tile
-constexpr uint32_t kKStages = 3;          // key tiles in flight
+constexpr uint32_t kKT = 64;              // keys a tile
+constexpr uint32_t kKStages = 2;          // key tiles in flight
 constexpr uint32_t kVStages = 2;          // value tiles in flight
 constexpr uint32_t kQChunk = kRows * 128;                 // 64 dimensions of 128 rows, f16: 16 KB
 constexpr uint32_t kQBytes = 4 * kQChunk;                 // one of Q's two halves: 64 KB
-constexpr uint32_t kBox = kKT * 128;                      // 32 keys x 64 dimensions f16: 4 KB
-constexpr uint32_t kHalf = 4 * kBox;                      // a tile's keys (or values): 16 KB
-constexpr uint32_t kPBytes = kRows * kKT * 2;             // P's part (or remainder): 8 KB
-constexpr uint32_t kSmem = 2 * kQBytes + (kKStages + kVStages) * kHalf + 2 * kPBytes + 1024;
+constexpr uint32_t kCopyKeys = 32;                        // keys a tensor copy brings (the cache maps' box)
+constexpr uint32_t kBox = kCopyKeys * 128;                // 32 keys x 64 dimensions f16: 4 KB
+constexpr uint32_t kChunk = kKT * 128;                    // a tile's 64 dimensions: 8 KB (two copies)
+constexpr uint32_t kHalf = 4 * kChunk;                    // a tile's keys (or values): 32 KB
+constexpr uint32_t kPBytes = kRows * kKT * 2;             // P's part (or remainder): 16 KB
+constexpr uint32_t kSmem = kQBytes + (kKStages + kVStages) * kHalf + 2 * kPBytes + 1024;   // 225 KB
+static_assert(kVStages * kHalf >= kQBytes, "Q's f16 part passes through the value ring");
 constexpr uint32_t kThreads = 224;
-constexpr uint32_t kTmemCols = 512;       // O [0, 256), S buffers [256, 288) and [288, 320)
+constexpr uint32_t kTmemCols = 512;       // O [0, 256), S buffers [256, 320) and [320, 384), Q's part [384, 512)
+constexpr uint32_t kQhiCol = 384;         // Q's f16 part: row r on lane r, dimensions 2c, 2c + 1 in column c
 constexpr uint32_t kSpin = 1u << 22;      // polls a wait takes before it gives up
 
 FZ_DEV uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -131,6 +140,15 @@ FZ_DEV void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_
       "l"(da), "l"(db), "r"(id), "r"(accumulate)
       : "memory");
 }
+// The same with A (M x 16, two f16 a 32-bit column, row m on lane m) read
+// from tensor memory.
+FZ_DEV void umma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t id, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "r"(tmem_a), "l"(db), "r"(id), "r"(accumulate)
+      : "memory");
+}
 FZ_DEV void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
                : "memory");
@@ -162,7 +180,6 @@ FZ_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-FZ_DEV uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 
 template <int G>
@@ -175,10 +192,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
   __shared__ uint32_t tmem_base;
   __shared__ uint32_t fail_word, ticket_word;
   unsigned char* smem = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
-  unsigned char* qhi = smem;
-  unsigned char* qlo = smem + kQBytes;
-  unsigned char* kring = smem + 2 * kQBytes;
+  unsigned char* qlo = smem;
+  unsigned char* kring = smem + kQBytes;
   unsigned char* vring = kring + kKStages * kHalf;
+  unsigned char* qhi = vring;   // Q's f16 part on its way to tensor memory, before the first value tile
   unsigned char* phi = vring + kVStages * kHalf;
   unsigned char* plo = phi + kPBytes;
 
@@ -280,21 +297,37 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
 #pragma unroll
           for (uint32_t hsel = 0; hsel < 2; hsel++) {
             const float4 w = v[k][hsel];
-            const float x[4] = {mul(w.x, sc), mul(w.y, sc), mul(w.z, sc), mul(w.w, sc)};
-            __half h[4], lo[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) split_hi_lo(x[e], h[e], lo[e]);
+            uint32_t h0, h1, l0, l1;
+            split2(mul(w.x, sc), mul(w.y, sc), h0, l0);
+            split2(mul(w.z, sc), mul(w.w, sc), h1, l1);
             const uint32_t dim = 128u * hsel + 4u * lane;
             const uint32_t off = (dim >> 6) * kQChunk + rr * 128u + ((((dim & 63u) >> 3) ^ (rr & 7u)) << 4) +
                                  (dim & 7u) * 2u;
-            *reinterpret_cast<uint2*>(qhi + off) =
-                make_uint2(h2_bits(__halves2half2(h[0], h[1])), h2_bits(__halves2half2(h[2], h[3])));
-            *reinterpret_cast<uint2*>(qlo + off) =
-                make_uint2(h2_bits(__halves2half2(lo[0], lo[1])), h2_bits(__halves2half2(lo[2], lo[3])));
+            *reinterpret_cast<uint2*>(qhi + off) = make_uint2(h0, h1);
+            *reinterpret_cast<uint2*>(qlo + off) = make_uint2(l0, l1);
           }
         }
       }
+      // Each warp wrote its own 32 rows; each thread now moves its row's f16
+      // part into tensor memory (the score MMAs read it from there, so only
+      // the remainder is read from shared memory a key tile).
+      __syncwarp();
+      const uint32_t q_lane = tmem + ((warp * 32u) << 16) + kQhiCol;
+#pragma unroll 1
+      for (uint32_t c = 0; c < 4; c++) {
+        uint32_t v[32];
+#pragma unroll
+        for (uint32_t u = 0; u < 8; u++) {
+          const uint4 w = *reinterpret_cast<const uint4*>(qhi + c * kQChunk + r * 128u + ((u ^ (r & 7u)) << 4));
+          v[4 * u] = w.x;
+          v[4 * u + 1] = w.y;
+          v[4 * u + 2] = w.z;
+          v[4 * u + 3] = w.w;
+        }
+        tmem_st32(q_lane + 32u * c, v);
+      }
       proxy_fence();
+      tc_fence_before();
       mb_arrive(&q_full);
     }
     const uint32_t lane_addr = tmem + ((warp * 32u) << 16);
@@ -310,20 +343,33 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
         break;
       }
       tc_fence_after();
-      uint32_t sr[32];
-      tmem_ld32(lane_addr + 256u + 32u * sb, sr);
+      uint32_t sr0[32], sr1[32];
+      tmem_ld32(lane_addr + 256u + kKT * sb, sr0);
+      tmem_ld32(lane_addr + 256u + kKT * sb + 32u, sr1);
       tc_fence_before();
       mb_arrive(&s_empty[sb]);
       const uint32_t j0 = kt0 + i * kKT;
-      float sv[32];
-      float mx = -INFINITY;
+      float sv[kKT];
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      // A tile every lane of the warp keeps whole (the interior of the
+      // window) needs no mask.
+      const bool whole = live && j0 + kKT - 1 <= p && p - j0 < a.window;
+      if (__all_sync(0xffffffffu, whole)) {
 #pragma unroll
-      for (uint32_t c = 0; c < 32; c++) {
-        const uint32_t j = j0 + c;
-        const bool valid = live && j <= p && p - j < a.window;
-        sv[c] = valid ? __uint_as_float(sr[c]) : -INFINITY;
-        mx = fmaxf(mx, sv[c]);
+        for (uint32_t c = 0; c < kKT; c++) {
+          sv[c] = __uint_as_float(c < 32 ? sr0[c] : sr1[c - 32]);
+          mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
+        }
+      } else {
+#pragma unroll
+        for (uint32_t c = 0; c < kKT; c++) {
+          const uint32_t j = j0 + c;
+          const bool valid = live && j <= p && p - j < a.window;
+          sv[c] = valid ? __uint_as_float(c < 32 ? sr0[c] : sr1[c - 32]) : -INFINITY;
+          mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
+        }
       }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       // The previous tile's P V is done: P's buffer is free and O may be rescaled.
       if (i > 0) {
         if (!__all_sync(0xffffffffu, mb_wait(&pv_done, pv_seen & 1u, f, 0x20000u))) {
@@ -350,25 +396,21 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
           tmem_st32(lane_addr + c0, o);
         }
       }
-      float sum = 0.f;
-      uint32_t ph[16], pl[16];
+      float sq[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t ph[kKT / 2], pl[kKT / 2];
 #pragma unroll
-      for (uint32_t c = 0; c < 32; c += 2) {
+      for (uint32_t c = 0; c < kKT; c += 2) {
         const float e0 = sv[c] == -INFINITY ? 0.f : exp2f(sv[c] - m);
         const float e1 = sv[c + 1] == -INFINITY ? 0.f : exp2f(sv[c + 1] - m);
-        sum = add(add(sum, e0), e1);
-        __half h0, h1, l0, l1;
-        split_hi_lo(e0, h0, l0);
-        split_hi_lo(e1, h1, l1);
-        ph[c / 2] = h2_bits(__halves2half2(h0, h1));
-        pl[c / 2] = h2_bits(__halves2half2(l0, l1));
+        sq[(c >> 1) & 3] = add(sq[(c >> 1) & 3], add(e0, e1));
+        split2(e0, e1, ph[c / 2], pl[c / 2]);
       }
-      l = add(l, sum);
+      l = add(l, add(add(sq[0], sq[1]), add(sq[2], sq[3])));
       // P row r, K-major without swizzle: core matrices of 8 rows x 8 keys
-      // (128 bytes), 128 bytes apart along the keys, 512 along the rows.
+      // (128 bytes), 128 bytes apart along the keys, 1024 along the rows.
 #pragma unroll
-      for (uint32_t ck = 0; ck < 4; ck++) {
-        const uint32_t off = (r >> 3) * 512u + ck * 128u + (r & 7u) * 16u;
+      for (uint32_t ck = 0; ck < kKT / 8; ck++) {
+        const uint32_t off = (r >> 3) * (kKT * 16u) + ck * 128u + (r & 7u) * 16u;
         *reinterpret_cast<uint4*>(phi + off) = make_uint4(ph[4 * ck], ph[4 * ck + 1], ph[4 * ck + 2], ph[4 * ck + 3]);
         *reinterpret_cast<uint4*>(plo + off) = make_uint4(pl[4 * ck], pl[4 * ck + 1], pl[4 * ck + 2], pl[4 * ck + 3]);
       }
@@ -445,13 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
         if (a.out_hi) {
           uint32_t hw[16], lw[16];
 #pragma unroll
-          for (int k = 0; k < 16; k++) {
-            __half h0, h1, l0, l1;
-            split_hi_lo(v[2 * k], h0, l0);
-            split_hi_lo(v[2 * k + 1], h1, l1);
-            hw[k] = h2_bits(__halves2half2(h0, h1));
-            lw[k] = h2_bits(__halves2half2(l0, l1));
-          }
+          for (int k = 0; k < 16; k++) split2(v[2 * k], v[2 * k + 1], hw[k], lw[k]);
           uint4* oh = reinterpret_cast<uint4*>(a.out_hi + row_base + c0);
 #pragma unroll
           for (int k = 0; k < 4; k++) oh[k] = make_uint4(hw[4 * k], hw[4 * k + 1], hw[4 * k + 2], hw[4 * k + 3]);
@@ -475,16 +511,23 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       uint64_t* empty = keys ? k_empty : v_empty;
       unsigned char* ring = keys ? kring : vring;
       uint32_t issued = 0;
+      // (the value ring holds Q's f16 part until it is in tensor memory)
+      const bool go = keys || mb_wait(&q_full, 0u, f, 0x400u);
 #pragma unroll 1
-      for (uint32_t i = 0; i < ntiles; i++) {
+      for (uint32_t i = 0; go && i < ntiles; i++) {
         const uint32_t s = i % NS;
         if (i >= NS && !mb_wait(&empty[s], ((i / NS) + 1u) & 1u, f, keys ? 0x1000u : 0x800u)) break;
         if (*f.flag) break;
         mb_expect_tx(&full[s], kHalf);
-        const uint32_t slot = (kt0 + i * kKT) % a.slots;
         unsigned char* dst = ring + s * kHalf;
+        // Two 32-key copies a 64-dimension chunk, rows 0..31 then 32..63 of
+        // the chunk (each wraps the ring on its own: slots hold whole copies).
 #pragma unroll
-        for (uint32_t q = 0; q < 4; q++) tma_box(dst + q * kBox, map, &full[s], 64u * q, kvh, slot, seq);
+        for (uint32_t h = 0; h < kKT / kCopyKeys; h++) {
+          const uint32_t slot = (kt0 + i * kKT + h * kCopyKeys) % a.slots;
+#pragma unroll
+          for (uint32_t q = 0; q < 4; q++) tma_box(dst + q * kChunk + h * kBox, map, &full[s], 64u * q, kvh, slot, seq);
+        }
         issued++;
       }
       // Every copy issued has landed before the CTA exits (bounded; the last
@@ -501,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       bool ok = mb_wait(&q_full, 0u, f, 0x2000u);
       tc_fence_after();
       constexpr uint32_t id_s = idesc(kKT, false), id_pv = idesc(kD, true);
-      const uint32_t qh = su32(qhi), ql = su32(qlo), pa = su32(phi), pb = su32(plo);
+      const uint32_t ql = su32(qlo), pa = su32(phi), pb = su32(plo);
 #pragma unroll 1
       for (uint32_t i = 0; ok && i <= ntiles; i++) {
         if (i < ntiles) {
@@ -511,14 +554,14 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
             break;
           tc_fence_after();
           const uint32_t kb = su32(kring + s * kHalf);
-          const uint32_t d = tmem + 256u + 32u * sb;
+          const uint32_t d = tmem + 256u + kKT * sb;
 #pragma unroll
           for (uint32_t c = 0; c < 4; c++)
 #pragma unroll
             for (uint32_t kk = 0; kk < 4; kk++) {
               // 16 dimensions = 32 bytes along K within the 128-byte swizzled rows.
-              const uint64_t db = desc(kb + c * kBox + kk * 32u, 16u, 1024u, 2u);
-              umma(d, desc(qh + c * kQChunk + kk * 32u, 16u, 1024u, 2u), db, id_s, (c | kk) != 0u ? 1u : 0u);
+              const uint64_t db = desc(kb + c * kChunk + kk * 32u, 16u, 1024u, 2u);
+              umma_ts(d, tmem + kQhiCol + 32u * c + 8u * kk, db, id_s, (c | kk) != 0u ? 1u : 0u);
               umma(d, desc(ql + c * kQChunk + kk * 32u, 16u, 1024u, 2u), db, id_s, 1u);
             }
           umma_commit(&s_full[sb]);
@@ -530,11 +573,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
           tc_fence_after();
           const uint32_t vb = su32(vring + s * kHalf);
 #pragma unroll
-          for (uint32_t kk = 0; kk < 2; kk++) {
-            // V MN-major: 64-dimension boxes kBox apart, 8-key row groups 1024 bytes apart.
-            const uint64_t dv = desc(vb + kk * 2048u, kBox, 1024u, 2u);
-            umma(tmem, desc(pa + kk * 256u, 128u, 512u, 0u), dv, id_pv, (j | kk) != 0u ? 1u : 0u);
-            umma(tmem, desc(pb + kk * 256u, 128u, 512u, 0u), dv, id_pv, 1u);
+          for (uint32_t kk = 0; kk < kKT / 16; kk++) {
+            // V MN-major: 64-dimension chunks kChunk apart, 8-key row groups 1024 bytes apart.
+            const uint64_t dv = desc(vb + kk * 2048u, kChunk, 1024u, 2u);
+            umma(tmem, desc(pa + kk * 256u, 128u, kKT * 16u, 0u), dv, id_pv, (j | kk) != 0u ? 1u : 0u);
+            umma(tmem, desc(pb + kk * 256u, 128u, kKT * 16u, 0u), dv, id_pv, 1u);
           }
           umma_commit(&v_empty[s]);
           umma_commit(&pv_done);

@@ -670,9 +670,9 @@ std::vector<uint32_t> layer_windows(const Shape& s) {
 }
 
 // The tensor-core attention splits the keys of a block longer than this many
-// 32-key tiles over two CTAs, when one wave holds all its blocks (a window
-// layer's blocks stay whole: 512 keys are at most 17 tiles).
-constexpr uint32_t kAttnSplitTiles = 40;
+// 64-key tiles (1280 keys) over two CTAs, when one wave holds all its blocks
+// (a window layer's blocks stay whole: 512 keys are at most 10 tiles).
+constexpr uint32_t kAttnSplitTiles = 20;
 static_assert(FZ_ATTENTION_WIDE_SPLIT_FLOATS == fz::kAttnSplitBlocks * 2 * fz::kAttnSplitFloats, "split scratch size");
 
 // Its split halves: wide steps (more than 16 rows) with the tensor-core form.

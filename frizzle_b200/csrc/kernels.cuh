@@ -35,7 +35,7 @@ struct AttentionArgs {
   uint32_t* error;
   // Its key-range split: with split_part set, at most kAttnSplitBlocks
   // (sequence, KV head, query block)s in the launch and a window longer than
-  // split_tiles 32-key tiles, a block of more than split_tiles tiles runs as
+  // split_tiles 64-key tiles, a block of more than split_tiles tiles runs as
   // two CTAs over the two halves of its keys; each writes its unnormalised O,
   // m and l to split_part[block][half] (kAttnSplitFloats floats) and takes a
   // ticket from counters[block], and the second merges the two.

@@ -55,6 +55,17 @@ FZ_DEV void split_hi_lo(float v, __half& hi, __half& lo) {
   lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
 }
 
+// split_hi_lo of two values at once, as packed half2 words (a the low half):
+// one paired conversion (cvt.rn.f16x2.f32) for the parts and one for the
+// remainders, the same bits as two split_hi_lo calls.
+FZ_DEV void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 back = __half22float2(h);
+  const __half2 l = __floats2half2_rn(__fsub_rn(a, back.x), __fsub_rn(b, back.y));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
 FZ_DEV uint2 pack4(__half a, __half b, __half c, __half d) {
   return make_uint2(h2_bits(__halves2half2(a, b)), h2_bits(__halves2half2(c, d)));
 }

@@ -409,7 +409,7 @@ uint32_t fz_attention_splits(uint32_t window, uint32_t position, uint32_t rows);
 
 /* fz_attention for steps of many rows, on the tensor cores (the engine's
  * attention for steps of more than 16 rows; the same sums as attention.wgsl:
- * 166-438): tiles of 32 keys by TMA, S = Q K^T and O += P V by tcgen05 with Q
+ * 166-438): tiles of 64 keys by TMA, S = Q K^T and O += P V by tcgen05 with Q
  * and P as f16 part and remainder, the online softmax a thread a row.  The
  * rows are one sequence at positions position .. position + rows - 1; q, out
  * and the caches as in fz_attention, the caches 16-byte aligned and slots a
@@ -419,7 +419,7 @@ uint32_t fz_attention_splits(uint32_t window, uint32_t position, uint32_t rows);
  * FZ_ATTENTION_WIDE_SPLIT_FLOATS floats of scratch with counters (148 words
  * that start at zero; the kernel leaves them zero): then, when the launch's
  * blocks of 128 / (heads / kv_heads) rows fit one wave of 148 CTAs and the
- * window is longer than 40 key tiles, a block of more than 40 tiles runs as
+ * window is longer than 1280 keys, a block of more than 1280 keys runs as
  * two CTAs over the halves of its keys, merged by the second to finish.
  * error: null or a device word set nonzero when a bounded wait gave up. */
 #define FZ_ATTENTION_WIDE_SPLIT_FLOATS (148u * 2u * 258u * 128u)
