@@ -855,10 +855,12 @@ __device__ __noinline__ void norm_one(const DecodeArgs& a, const float* xin, con
     if (!live[u]) continue;
     const int i = tid + u * kCT;
     const int cc[4] = {col[u], col[u] + 1, col[u] + 16, col[u] + 17};
-    __half hi[4], lo[4];
+    float y4[4];
 #pragma unroll
-    for (int e = 0; e < 4; e++) split_hi_lo(mul(mul(x[u][e], rx), gs[cc[e]]), hi[e], lo[e]);
-    const uint2 h = pack4(hi[0], hi[1], hi[2], hi[3]), l = pack4(lo[0], lo[1], lo[2], lo[3]);
+    for (int e = 0; e < 4; e++) y4[e] = mul(mul(x[u][e], rx), gs[cc[e]]);
+    uint2 h, l;
+    split2(y4[0], y4[1], h.x, l.x);
+    split2(y4[2], y4[3], h.y, l.y);
     uint4* dst = xf + (i >> 2) * 16 + (i & 3) * 4;
     dst[0] = make_uint4(h.x, h.y, l.x, l.y);
     dst[1] = dst[2] = dst[3] = make_uint4(0u, 0u, 0u, 0u);
@@ -915,13 +917,8 @@ __device__ __noinline__ void fragments(const DecodeArgs& a, uint32_t M, const fl
 #pragma unroll
         for (int gp = 0; gp < 4; gp++) {
           const float4 w = v[u][q][gp];
-          __half h0, h1, h2, h3, l0, l1, l2, l3;
-          split_hi_lo(w.x, h0, l0);
-          split_hi_lo(w.y, h1, l1);
-          split_hi_lo(w.z, h2, l2);
-          split_hi_lo(w.w, h3, l3);
-          col[2 * gp] = pack4(h0, h1, h2, h3);
-          col[2 * gp + 1] = pack4(l0, l1, l2, l3);
+          split2(w.x, w.y, col[2 * gp].x, col[2 * gp + 1].x);
+          split2(w.z, w.w, col[2 * gp].y, col[2 * gp + 1].y);
         }
         // xf_index(kb_rel, h, q, MQ, tq, g) = ((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8 + g
         uint4* dst = xf + (((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8) / 2;
@@ -990,13 +987,8 @@ __device__ __noinline__ void fragments_ll(const DecodeArgs& a, uint32_t M, const
 #pragma unroll
         for (int gp = 0; gp < 4; gp++) {
           const float4 w = v[u][q][gp];
-          __half h0, h1, h2, h3, l0, l1, l2, l3;
-          split_hi_lo(w.x, h0, l0);
-          split_hi_lo(w.y, h1, l1);
-          split_hi_lo(w.z, h2, l2);
-          split_hi_lo(w.w, h3, l3);
-          col[2 * gp] = pack4(h0, h1, h2, h3);
-          col[2 * gp + 1] = pack4(l0, l1, l2, l3);
+          split2(w.x, w.y, col[2 * gp].x, col[2 * gp + 1].x);
+          split2(w.z, w.w, col[2 * gp].y, col[2 * gp + 1].y);
         }
         uint4* dst = xf + (((kb_rel * 2 + h) * MQ + q) * 32 + tq * 8) / 2;
 #pragma unroll
@@ -1274,15 +1266,15 @@ struct Attn {
         const float s = a.scale_log2e;
         const float qv[8] = {mul(va.x, s), mul(va.y, s), mul(va.z, s), mul(va.w, s),
                              mul(vb.x, s), mul(vb.y, s), mul(vb.z, s), mul(vb.w, s)};
-        __half hi[8], lo[8];
+        uint32_t hi[4], lo[4];
 #pragma unroll
-        for (int i = 0; i < 8; i++) split_hi_lo(qv[i], hi[i], lo[i]);
+        for (int i = 0; i < 4; i++) split2(qv[2 * i], qv[2 * i + 1], hi[i], lo[i]);
         uint16_t* qa = qh() + warp * QS;
         uint16_t* qb = qh() + (GH + warp) * QS;
-        *reinterpret_cast<uint2*>(qa + 4 * lane) = pack4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint2*>(qa + kHd / 2 + 4 * lane) = pack4(hi[4], hi[5], hi[6], hi[7]);
-        *reinterpret_cast<uint2*>(qb + 4 * lane) = pack4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint2*>(qb + kHd / 2 + 4 * lane) = pack4(lo[4], lo[5], lo[6], lo[7]);
+        *reinterpret_cast<uint2*>(qa + 4 * lane) = make_uint2(hi[0], hi[1]);
+        *reinterpret_cast<uint2*>(qa + kHd / 2 + 4 * lane) = make_uint2(hi[2], hi[3]);
+        *reinterpret_cast<uint2*>(qb + 4 * lane) = make_uint2(lo[0], lo[1]);
+        *reinterpret_cast<uint2*>(qb + kHd / 2 + 4 * lane) = make_uint2(lo[2], lo[3]);
       } else if (last) {
         uint16_t* cache = (warp == GH ? L.key_cache : L.value_cache) + row * L.seq_stride +
                           ((size_t)(pos % L.slots) * KV + kvh) * kHd;

@@ -91,13 +91,8 @@ FZ_DEV void build_fragments(uint2* xf, int MQ, int row, const float* src, int kb
       const int k0 = 32 * (kb_base + kb_rel) + 8 * h + 2 * t;
       const float2 v01 = *reinterpret_cast<const float2*>(src + k0);
       const float2 v23 = *reinterpret_cast<const float2*>(src + k0 + 16);
-      __half h0, h1, h2, h3, l0, l1, l2, l3;
-      split_hi_lo(v01.x, h0, l0);
-      split_hi_lo(v01.y, h1, l1);
-      split_hi_lo(v23.x, h2, l2);
-      split_hi_lo(v23.y, h3, l3);
-      hi = pack4(h0, h1, h2, h3);
-      lo = pack4(l0, l1, l2, l3);
+      split2(v01.x, v01.y, hi.x, lo.x);
+      split2(v23.x, v23.y, hi.y, lo.y);
     }
     xf[xf_index(kb_rel, h, q, MQ, t, 2 * gp)] = hi;
     xf[xf_index(kb_rel, h, q, MQ, t, 2 * gp + 1)] = lo;
