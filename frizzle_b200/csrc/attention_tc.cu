@@ -6,21 +6,24 @@
 // A CTA takes one sequence, one KV head and QT = 128 / G tokens of each of
 // the G query heads that share it: 128 query rows, row r = head (r / QT),
 // token (r % QT), one row a TMEM lane.  Keys go 64 at a time:
-//   - warps 4 and 6 (one lane each) bring each tile's keys, and its values,
+//   - warps 8 and 10 (one lane each) bring each tile's keys, and its values,
 //     by TMA from the cache (4D tensor maps, 32-slot x 64-dimension boxes,
 //     two a 64-dimension chunk, 128-byte swizzle) into two-stage key and
 //     value rings, freed as each score product, or P V, completes; the value
 //     ring first carries Q's f16 part on its way to tensor memory;
-//   - warp 5 (one lane) issues tcgen05.mma: S = Q K^T (M = 128, N = 64) into
+//   - warp 9 (one lane) issues tcgen05.mma: S = Q K^T (M = 128, N = 64) into
 //     one of two TMEM score buffers, Q as f16 part (read from tensor memory)
 //     and remainder (from shared memory), two MMAs a 16-dimension step, so
 //     the products are exact and the sums f32; then O += P V (N = 256, V read
 //     MN-major straight from the tile) into a TMEM accumulator, P as f16 part
 //     and remainder;
-//   - warps 0..3 (thread = row) read their row's 64 scores (tcgen05.ld), mask
-//     them (causal, window, rows past the step), keep the online softmax
-//     (max m, sum l), write P to shared memory and, when a tile's max passes
-//     m by more than 8 (log2 units), rescale O in TMEM (tcgen05.ld/st) first;
+//   - warps 0..7, two threads a row (warps w and w ^ 4 share TMEM lanes
+//     32 (w % 4) ..; each takes half of a tile's keys and of O's columns),
+//     read their 32 scores (tcgen05.ld), mask them (causal, window, rows
+//     past the step), agree on the tile's max through shared memory, keep
+//     the online softmax (max m, sum l), write P to shared memory and, when
+//     a tile's max passes m by more than 8 (log2 units), rescale O in TMEM
+//     (tcgen05.ld/st) first;
 //     in between, the exponent base may lag the true max by up to 8, which
 //     keeps P <= 256 and leaves the result the same softmax.
 // A score MMA of N = 32 took ~49 cycles whether A came from shared or tensor
@@ -67,7 +70,7 @@ constexpr uint32_t kHalf = 4 * kChunk;                    // a tile's keys (or v
 constexpr uint32_t kPBytes = kRows * kKT * 2;             // P's part (or remainder): 16 KB
 constexpr uint32_t kSmem = kQBytes + (kKStages + kVStages) * kHalf + 2 * kPBytes + 1024;   // 225 KB
 static_assert(kVStages * kHalf >= kQBytes, "Q's f16 part passes through the value ring");
-constexpr uint32_t kThreads = 224;
+constexpr uint32_t kThreads = 352;
 constexpr uint32_t kTmemCols = 512;       // O [0, 256), S buffers [256, 320) and [320, 384), Q's part [384, 512)
 constexpr uint32_t kQhiCol = 384;         // Q's f16 part: row r on lane r, dimensions 2c, 2c + 1 in column c
 constexpr uint32_t kSpin = 1u << 22;      // polls a wait takes before it gives up
@@ -155,6 +158,18 @@ FZ_DEV void umma_commit(uint64_t* bar) {
 }
 FZ_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 FZ_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Named barriers of two softmax warps (64 threads); the _or form returns the
+// OR of both sides' predicates to both.
+FZ_DEV void pair_sync(uint32_t id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+FZ_DEV bool pair_sync_or(uint32_t id, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.or.pred b, %2, 64, a;\n selp.u32 %0, 1, 0, b;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)p), "r"(id)
+      : "memory");
+  return r != 0;
+}
 FZ_DEV void proxy_fence() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 FZ_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -191,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
   __shared__ __align__(8) uint64_t q_full, p_full, pv_done, drain;
   __shared__ uint32_t tmem_base;
   __shared__ uint32_t fail_word, ticket_word;
+  __shared__ float xch[2 * kRows];   // a row's two softmax threads: [half][row]
   unsigned char* smem = smem_raw + ((1024u - (su32(smem_raw) & 1023u)) & 1023u);
   unsigned char* qlo = smem;
   unsigned char* kring = smem + kQBytes;
@@ -220,15 +236,15 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
     }
     for (int b = 0; b < 2; b++) {
       mb_init(&s_full[b], 1);
-      mb_init(&s_empty[b], 128);
+      mb_init(&s_empty[b], 256);
     }
-    mb_init(&q_full, 128);
-    mb_init(&p_full, 128);
+    mb_init(&q_full, 256);
+    mb_init(&p_full, 256);
     mb_init(&pv_done, 1);
     mb_init(&drain, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 5) {
+  if (warp == 9) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_base)),
                  "r"(kTmemCols)
                  : "memory");
@@ -264,121 +280,129 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
 
   if (ntiles == 0) {
     // (the empty second CTA of a block that did not split)
-  } else if (warp < 4) {
-    // ---- softmax: thread r is query row r (TMEM lane r).
-    const uint32_t r = threadIdx.x, hh = r / QT, t = r % QT;
+  } else if (warp < 8) {
+    // ---- softmax: two threads a query row.  Warp w takes rows r = 32 (w %
+    // 4) + lane (TMEM lanes r) and half h = w / 4 of each tile's 64 keys, of
+    // O's 256 columns and of the query load; a row's two threads (warps w
+    // and w ^ 4) meet once a tile in shared memory for the tile's max, and
+    // at the end for l.
+    const uint32_t half = warp >> 2, quarter = warp & 3;
+    const uint32_t r = quarter * 32u + lane, hh = r / QT, t = r % QT;
     const bool live = t < ntok;
     const uint32_t head = kvh * G + hh, p = pos0 + t;
     const size_t row_base = (((size_t)seq * T + t0 + t) * a.heads + head) * kD;
+    const uint32_t pair = 2u + quarter;   // the named barrier of warps w and w ^ 4
+    const uint32_t lane_addr = tmem + ((quarter * 32u) << 16);
     {
       // The CTA's queries times scale x log2 e, as f16 part and remainder,
       // K-major 64-dimension chunks with 128-byte swizzle (16-byte unit u of
-      // row r at unit u ^ (r % 8)).  Warp w reads rows 32 w .. 32 w + 31 a
-      // whole row at a time (lane l: dimensions 4 l .. 4 l + 3 and 128 + 4 l
-      // ..), sixteen rows' loads in flight.
+      // row r at unit u ^ (r % 8)).  The warp reads rows 32 (w % 4) + 16 h ..
+      // + 15 a whole row at a time (lane l: dimensions 4 l .. 4 l + 3 and 128
+      // + 4 l ..), all sixteen rows' loads in flight.
       const float sc = a.scale_log2e;
-#pragma unroll 1
-      for (uint32_t r0 = warp * 32u; r0 < warp * 32u + 32u; r0 += 16) {
-        float4 v[16][2];
+      const uint32_t r0 = quarter * 32u + half * 16u;
+      float4 v[16][2];
 #pragma unroll
-        for (uint32_t k = 0; k < 16; k++) {
-          const uint32_t rr = r0 + k, tt = rr % QT;
-          v[k][0] = v[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (tt < ntok) {
-            const float4* q4 = reinterpret_cast<const float4*>(
-                a.q + (((size_t)seq * T + t0 + tt) * a.heads + kvh * G + rr / QT) * kD);
-            v[k][0] = __ldcg(q4 + lane);
-            v[k][1] = __ldcg(q4 + 32 + lane);
-          }
-        }
-#pragma unroll
-        for (uint32_t k = 0; k < 16; k++) {
-          const uint32_t rr = r0 + k;
-#pragma unroll
-          for (uint32_t hsel = 0; hsel < 2; hsel++) {
-            const float4 w = v[k][hsel];
-            uint32_t h0, h1, l0, l1;
-            split2(mul(w.x, sc), mul(w.y, sc), h0, l0);
-            split2(mul(w.z, sc), mul(w.w, sc), h1, l1);
-            const uint32_t dim = 128u * hsel + 4u * lane;
-            const uint32_t off = (dim >> 6) * kQChunk + rr * 128u + ((((dim & 63u) >> 3) ^ (rr & 7u)) << 4) +
-                                 (dim & 7u) * 2u;
-            *reinterpret_cast<uint2*>(qhi + off) = make_uint2(h0, h1);
-            *reinterpret_cast<uint2*>(qlo + off) = make_uint2(l0, l1);
-          }
+      for (uint32_t k = 0; k < 16; k++) {
+        const uint32_t rr = r0 + k, tt = rr % QT;
+        v[k][0] = v[k][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tt < ntok) {
+          const float4* q4 = reinterpret_cast<const float4*>(
+              a.q + (((size_t)seq * T + t0 + tt) * a.heads + kvh * G + rr / QT) * kD);
+          v[k][0] = __ldcg(q4 + lane);
+          v[k][1] = __ldcg(q4 + 32 + lane);
         }
       }
-      // Each warp wrote its own 32 rows; each thread now moves its row's f16
-      // part into tensor memory (the score MMAs read it from there, so only
-      // the remainder is read from shared memory a key tile).
-      __syncwarp();
-      const uint32_t q_lane = tmem + ((warp * 32u) << 16) + kQhiCol;
+#pragma unroll
+      for (uint32_t k = 0; k < 16; k++) {
+        const uint32_t rr = r0 + k;
+#pragma unroll
+        for (uint32_t hsel = 0; hsel < 2; hsel++) {
+          const float4 w = v[k][hsel];
+          uint32_t h0, h1, l0, l1;
+          split2(mul(w.x, sc), mul(w.y, sc), h0, l0);
+          split2(mul(w.z, sc), mul(w.w, sc), h1, l1);
+          const uint32_t dim = 128u * hsel + 4u * lane;
+          const uint32_t off = (dim >> 6) * kQChunk + rr * 128u + ((((dim & 63u) >> 3) ^ (rr & 7u)) << 4) +
+                               (dim & 7u) * 2u;
+          *reinterpret_cast<uint2*>(qhi + off) = make_uint2(h0, h1);
+          *reinterpret_cast<uint2*>(qlo + off) = make_uint2(l0, l1);
+        }
+      }
+      // The pair wrote the quarter's rows; each thread now moves its half of
+      // its row's f16 part (dimensions 128 h .. + 127) into tensor memory (the
+      // score MMAs read it from there, only the remainder from shared memory).
+      pair_sync(pair);
 #pragma unroll 1
-      for (uint32_t c = 0; c < 4; c++) {
-        uint32_t v[32];
+      for (uint32_t c = 2 * half; c < 2 * half + 2; c++) {
+        uint32_t qv[32];
 #pragma unroll
         for (uint32_t u = 0; u < 8; u++) {
           const uint4 w = *reinterpret_cast<const uint4*>(qhi + c * kQChunk + r * 128u + ((u ^ (r & 7u)) << 4));
-          v[4 * u] = w.x;
-          v[4 * u + 1] = w.y;
-          v[4 * u + 2] = w.z;
-          v[4 * u + 3] = w.w;
+          qv[4 * u] = w.x;
+          qv[4 * u + 1] = w.y;
+          qv[4 * u + 2] = w.z;
+          qv[4 * u + 3] = w.w;
         }
-        tmem_st32(q_lane + 32u * c, v);
+        tmem_st32(lane_addr + kQhiCol + 32u * c, qv);
       }
       proxy_fence();
       tc_fence_before();
       mb_arrive(&q_full);
     }
-    const uint32_t lane_addr = tmem + ((warp * 32u) << 16);
-    float m = -INFINITY, l = 0.f;
+    const uint32_t ocol = 128u * half;   // this thread's columns of O
+    float m = -INFINITY, l = 0.f;        // l: the sum over this thread's keys
     uint32_t pv_seen = 0;
     bool ok = true;
 #pragma unroll 1
     for (uint32_t i = 0; i < ntiles; i++) {
       const uint32_t sb = i & 1u;
       // (the warp decides together: the tensor-memory loads below are warp-wide)
-      if (!__all_sync(0xffffffffu, mb_wait(&s_full[sb], (i >> 1) & 1u, f, 0x10000u))) {
-        ok = false;
-        break;
+      bool go = __all_sync(0xffffffffu, mb_wait(&s_full[sb], (i >> 1) & 1u, f, 0x10000u));
+      uint32_t sr[32];
+      if (go) {
+        tc_fence_after();
+        tmem_ld32(lane_addr + 256u + kKT * sb + 32u * half, sr);
+        tc_fence_before();
+        mb_arrive(&s_empty[sb]);
       }
-      tc_fence_after();
-      uint32_t sr0[32], sr1[32];
-      tmem_ld32(lane_addr + 256u + kKT * sb, sr0);
-      tmem_ld32(lane_addr + 256u + kKT * sb + 32u, sr1);
-      tc_fence_before();
-      mb_arrive(&s_empty[sb]);
-      const uint32_t j0 = kt0 + i * kKT;
-      float sv[kKT];
+      const uint32_t j0 = kt0 + i * kKT + 32u * half;
+      float sv[32];
       float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      // A tile every lane of the warp keeps whole (the interior of the
+      // A half tile every lane of the warp keeps whole (the interior of the
       // window) needs no mask.
-      const bool whole = live && j0 + kKT - 1 <= p && p - j0 < a.window;
+      const bool whole = live && j0 + 31u <= p && p - j0 < a.window;
       if (__all_sync(0xffffffffu, whole)) {
 #pragma unroll
-        for (uint32_t c = 0; c < kKT; c++) {
-          sv[c] = __uint_as_float(c < 32 ? sr0[c] : sr1[c - 32]);
+        for (uint32_t c = 0; c < 32; c++) {
+          sv[c] = __uint_as_float(sr[c]);
           mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
         }
       } else {
 #pragma unroll
-        for (uint32_t c = 0; c < kKT; c++) {
+        for (uint32_t c = 0; c < 32; c++) {
           const uint32_t j = j0 + c;
           const bool valid = live && j <= p && p - j < a.window;
-          sv[c] = valid ? __uint_as_float(c < 32 ? sr0[c] : sr1[c - 32]) : -INFINITY;
+          sv[c] = valid ? __uint_as_float(sr[c]) : -INFINITY;
           mq[c & 3] = fmaxf(mq[c & 3], sv[c]);
         }
       }
-      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      // The previous tile's P V is done: P's buffer is free and O may be rescaled.
-      if (i > 0) {
-        if (!__all_sync(0xffffffffu, mb_wait(&pv_done, pv_seen & 1u, f, 0x20000u))) {
-          ok = false;
-          break;
-        }
+      const float mine = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      // The previous tile's P V is done: P's buffer is free, O may be
+      // rescaled, and the partner has read the last tile's exchange word.
+      if (go && i > 0) {
+        go = __all_sync(0xffffffffu, mb_wait(&pv_done, pv_seen & 1u, f, 0x20000u));
         pv_seen++;
         tc_fence_after();
       }
+      xch[half * kRows + r] = mine;
+      // Both threads of the row stop together (a wait that gave up, here or
+      // anywhere in the CTA), so neither waits at a barrier the other left.
+      if (pair_sync_or(pair, !go || *f.flag != 0u)) {
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(mine, xch[(half ^ 1u) * kRows + r]);
       // A new base when the tile's max passes it by more than 8; O is
       // rescaled by the warp together (lanes that keep their base scale by 1).
       const bool moved = mx > m + 8.f;
@@ -388,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       if (moved) m = mx;
       if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
-        for (uint32_t c0 = 0; c0 < kD; c0 += 32) {
+        for (uint32_t c0 = ocol; c0 < ocol + 128u; c0 += 32) {
           uint32_t o[32];
           tmem_ld32(lane_addr + c0, o);
 #pragma unroll
@@ -397,9 +421,9 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
         }
       }
       float sq[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t ph[kKT / 2], pl[kKT / 2];
+      uint32_t ph[16], pl[16];
 #pragma unroll
-      for (uint32_t c = 0; c < kKT; c += 2) {
+      for (uint32_t c = 0; c < 32; c += 2) {
         const float e0 = sv[c] == -INFINITY ? 0.f : exp2f(sv[c] - m);
         const float e1 = sv[c + 1] == -INFINITY ? 0.f : exp2f(sv[c + 1] - m);
         sq[(c >> 1) & 3] = add(sq[(c >> 1) & 3], add(e0, e1));
@@ -407,12 +431,13 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       }
       l = add(l, add(add(sq[0], sq[1]), add(sq[2], sq[3])));
       // P row r, K-major without swizzle: core matrices of 8 rows x 8 keys
-      // (128 bytes), 128 bytes apart along the keys, 1024 along the rows.
+      // (128 bytes), 128 bytes apart along the keys, 1024 along the rows;
+      // this thread's keys are core matrices 4 h .. 4 h + 3.
 #pragma unroll
-      for (uint32_t ck = 0; ck < kKT / 8; ck++) {
-        const uint32_t off = (r >> 3) * (kKT * 16u) + ck * 128u + (r & 7u) * 16u;
-        *reinterpret_cast<uint4*>(phi + off) = make_uint4(ph[4 * ck], ph[4 * ck + 1], ph[4 * ck + 2], ph[4 * ck + 3]);
-        *reinterpret_cast<uint4*>(plo + off) = make_uint4(pl[4 * ck], pl[4 * ck + 1], pl[4 * ck + 2], pl[4 * ck + 3]);
+      for (uint32_t k = 0; k < 4; k++) {
+        const uint32_t off = (r >> 3) * (kKT * 16u) + (4u * half + k) * 128u + (r & 7u) * 16u;
+        *reinterpret_cast<uint4*>(phi + off) = make_uint4(ph[4 * k], ph[4 * k + 1], ph[4 * k + 2], ph[4 * k + 3]);
+        *reinterpret_cast<uint4*>(plo + off) = make_uint4(pl[4 * k], pl[4 * k + 1], pl[4 * k + 2], pl[4 * k + 3]);
       }
       proxy_fence();
       tc_fence_before();
@@ -422,6 +447,11 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       if (!__all_sync(0xffffffffu, mb_wait(&pv_done, pv_seen & 1u, f, 0x40000u))) ok = false;
       tc_fence_after();
     }
+    // The row's l: both threads' sums, in one order (after the last P V, so
+    // the partner has read every earlier exchange word).
+    xch[half * kRows + r] = l;
+    pair_sync(pair);
+    l = add(xch[r], xch[kRows + r]);
     pdl_launch_dependents();
     // A split block: each half writes its O, m and l (row r at column-major
     // offsets, so a warp's stores are consecutive) and takes a ticket; the
@@ -433,24 +463,26 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       float* mine = a.split_part + ((size_t)sidx * 2 + part) * kAttnSplitFloats;
       if (ok) {
 #pragma unroll 1
-        for (uint32_t c0 = 0; c0 < kD; c0 += 32) {
+        for (uint32_t c0 = ocol; c0 < ocol + 128u; c0 += 32) {
           uint32_t o[32];
           tmem_ld32(lane_addr + c0, o);
           if (!live) continue;   // (after the warp-wide load)
 #pragma unroll
           for (int k = 0; k < 32; k++) __stcg(mine + (c0 + k) * kRows + r, __uint_as_float(o[k]));
         }
-        __stcg(mine + kD * kRows + r, m);
-        __stcg(mine + (kD + 1) * kRows + r, l);
+        if (half == 0) {
+          __stcg(mine + kD * kRows + r, m);
+          __stcg(mine + (kD + 1) * kRows + r, l);
+        }
       }
       __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (r == 0) ticket_word = atomicAdd(a.counters + sidx, 1u);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (threadIdx.x == 0) ticket_word = atomicAdd(a.counters + sidx, 1u);
+      asm volatile("bar.sync 1, 256;" ::: "memory");
       if (ticket_word == 0u)
         write = false;   // the other half, still running, merges
       else {
-        if (r == 0) a.counters[sidx] = 0u;   // zero again for the next launch
+        if (threadIdx.x == 0) a.counters[sidx] = 0u;   // zero again for the next launch
         __threadfence();
         other = a.split_part + ((size_t)sidx * 2 + (1u - part)) * kAttnSplitFloats;
         if (write && live) {
@@ -466,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
       // out = O / l (by one reciprocal), and its f16 part and remainder.
       const float inv = __frcp_rn(l);
 #pragma unroll 1
-      for (uint32_t c0 = 0; c0 < kD; c0 += 32) {
+      for (uint32_t c0 = ocol; c0 < ocol + 128u; c0 += 32) {
         uint32_t o[32];
         tmem_ld32(lane_addr + c0, o);
         if (!live) continue;   // (after the warp-wide load)
@@ -499,12 +531,12 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
         }
       }
     }
-  } else if (warp == 4 || warp == 6) {
-    // ---- the tiles' keys (warp 4) or values (warp 6) by TMA (lane 0): a
+  } else if (warp == 8 || warp == 10) {
+    // ---- the tiles' keys (warp 8) or values (warp 10) by TMA (lane 0): a
     // ring of kKStages key tiles, freed as each score product completes, and
     // one of kVStages value tiles, freed as each P V completes.
     if (lane == 0) {
-      const bool keys = warp == 4;
+      const bool keys = warp == 8;
       const unsigned char* map = static_cast<const unsigned char*>(a.kv_maps) + (keys ? 0 : 128);
       const uint32_t NS = keys ? kKStages : kVStages;
       uint64_t* full = keys ? k_full : v_full;
@@ -591,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_tc_kernel(const Attenti
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
