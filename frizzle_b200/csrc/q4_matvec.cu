@@ -650,7 +650,10 @@ __global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecAr
   if (row < a.m) {
     const NormArgs& n = a.norm;
     const uint32_t W = n.width;
-    const float wf = (float)W;
+    // (1 / width, rounded once: each reciprocal RMS is one multiply-add and
+    // the hardware reciprocal square root, within 2e-7 of a division and an
+    // IEEE square root)
+    const float inv_w = __frcp_rn((float)W);
     const float4* x4 = reinterpret_cast<const float4*>(n.hidden_in + (size_t)row * W);
     float4 x[NV], y[NV];
 #pragma unroll
@@ -667,7 +670,7 @@ __global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecAr
         float p = 0.f;
 #pragma unroll
         for (int i = 0; i < NV; i++) p = add(p, dot_self(y[i]));
-        const float s = inverse_sqrt(add(__fdiv_rn(warp_sum(p), wf), n.eps));
+        const float s = rsqrtf(__fmaf_rn(warp_sum(p), inv_w, n.eps));
 #pragma unroll
         for (int i = 0; i < NV; i++) {
           const float4 g = gsm[1][lane + 32 * i];
@@ -693,7 +696,7 @@ __global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecAr
       if (xcap) xcap[lane + 32 * i] = x[i];
       p = add(p, dot_self(x[i]));
     }
-    const float s = inverse_sqrt(add(__fdiv_rn(warp_sum(p), wf), n.eps));
+    const float s = rsqrtf(__fmaf_rn(warp_sum(p), inv_w, n.eps));
     uint2* hi = reinterpret_cast<uint2*>(out_hi + (size_t)row * W);
     uint2* lo = out_lo ? reinterpret_cast<uint2*>(out_lo + (size_t)row * W) : nullptr;
 #pragma unroll
@@ -701,18 +704,11 @@ __global__ void __launch_bounds__(kThreads) norm_rows_warp_kernel(const MatvecAr
       const float4 g = gsm[0][lane + 32 * i];
       const float v[4] = {mul(mul(x[i].x, s), g.x), mul(mul(x[i].y, s), g.y), mul(mul(x[i].z, s), g.z),
                           mul(mul(x[i].w, s), g.w)};
-      __half h[4], l[4];
-#pragma unroll
-      for (int e = 0; e < 4; e++) {
-        h[e] = __float2half_rn(v[e]);
-        l[e] = __float2half_rn(__fsub_rn(v[e], __half2float(h[e])));
-      }
-      __half2 h01 = __halves2half2(h[0], h[1]), h23 = __halves2half2(h[2], h[3]);
-      hi[lane + 32 * i] = make_uint2(*reinterpret_cast<uint32_t*>(&h01), *reinterpret_cast<uint32_t*>(&h23));
-      if (lo) {
-        __half2 l01 = __halves2half2(l[0], l[1]), l23 = __halves2half2(l[2], l[3]);
-        lo[lane + 32 * i] = make_uint2(*reinterpret_cast<uint32_t*>(&l01), *reinterpret_cast<uint32_t*>(&l23));
-      }
+      uint2 h, l;
+      split2(v[0], v[1], h.x, l.x);
+      split2(v[2], v[3], h.y, l.y);
+      hi[lane + 32 * i] = h;
+      if (lo) lo[lane + 32 * i] = l;
     }
   }
   pdl_launch_dependents();
