@@ -150,3 +150,28 @@ def test_gguf_reader_round_trip(tiny_model_path):
     t = idx.tensors["blk.0.ffn_gate.weight"]
     assert t.dims == (synth.TINY.hidden, synth.TINY.ffn) and t.ggml_type == gguf.TYPE_Q4_0
     assert t.offset % 32 == 0
+
+
+def test_attention_wide_refuses_bad_arguments_before_any_launch():
+    """fz_attention_wide checks its arguments on the host, before it encodes
+    tensor maps or launches anything, so these refusals need no GPU: null
+    pointers, maps not 64-byte aligned, caches not 16-byte aligned, a head
+    group other than 1, 2, 4 or 8, a slot count that is not whole 32-key
+    tiles, zero rows, and split scratch without its counters."""
+    lib = _native.load()
+    P = 0x10000          # a 64-byte-aligned stand-in address; nothing is dereferenced
+    ok = dict(q=P, k=P, v=P, slots=2048, heads=4, kv=1, d=256, window=32768, position=0, rows=64,
+              maps=P, split=None, counters=None, out=P)
+
+    def call(**kw):
+        c = dict(ok, **kw)
+        return lib.fz_attention_wide(c["q"], c["k"], c["v"], c["slots"], c["heads"], c["kv"], c["d"], c["window"],
+                                     c["position"], c["rows"], c["maps"], c["split"], c["counters"], c["out"],
+                                     None, None)
+
+    for bad in (dict(q=None), dict(out=None), dict(maps=None), dict(maps=P + 32), dict(k=P + 8),
+                dict(heads=3), dict(d=128), dict(slots=1000), dict(rows=0), dict(split=P),
+                dict(position=(1 << 24) - 10, rows=64)):
+        st = call(**bad)
+        assert st == 1, (bad, st)   # FZ_ERR_ARGUMENT
+        assert lib.fz_last_error(), bad
