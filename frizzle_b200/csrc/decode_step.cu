@@ -131,8 +131,8 @@ __host__ __device__ inline DLayout layout_for(int MQ, uint32_t slots, uint32_t h
   // Attention view: the split queries, then (1024-aligned, for the 128-byte
   // swizzle) the chunk buffers, then scores, weights and head statistics.
   L.kvbuf = (o + 8u * (kHd + 8u) * 2u + 1023u) & ~1023u;
-  const uint32_t att_end = L.kvbuf + kv_bufs(MQ) * kKvBuf + 2u * group * kAttnChunk * 4u +
-                           8u * (kAttnChunk + 8u) * 2u + 2u * group * 4u;
+  const uint32_t att_end = L.kvbuf + kv_bufs(MQ) * kKvBuf + 2u * group * 2u * kAttnChunk * 4u +
+                           8u * (2u * kAttnChunk + 8u) * 2u + 2u * group * 4u;
   o = m > att_end ? m : att_end;
   o = (o + 15u) & ~15u;
   L.stat = o;
@@ -1096,14 +1096,15 @@ struct Attn {
 
   static constexpr int C = kAttnChunk;    // keys a chunk
   static constexpr int QS = kHd + 8;      // row stride (halves) of the split queries
-  static constexpr int PS = C + 8;        // row stride (halves) of the split weights
+  static constexpr int PS = 2 * C + 8;    // row stride (halves) of the split weights (two chunks' keys)
   // Split rows: r < GH the f16 part of head r's query (or weights), GH <= r <
   // 2 GH the f16 remainder of head r - GH's, the rest zero (the mma's A rows).
   FZ_DEV uint16_t* qh() const { return reinterpret_cast<uint16_t*>(g_smem + a.lay.uni); }  // [8][QS]
   FZ_DEV unsigned char* ks(uint32_t b) const { return g_smem + a.lay.kvbuf + b * kKvBuf; }  // 4 boxes
   FZ_DEV unsigned char* vs(uint32_t b) const { return ks(b) + 4 * kKvBox; }                 // 4 boxes
-  FZ_DEV float* sc() const { return reinterpret_cast<float*>(ks(NB)); }                     // [2][GH][C] scores
-  FZ_DEV uint16_t* ph() const { return reinterpret_cast<uint16_t*>(sc() + 2 * GH * C); }    // [8][PS] weights
+  // Scores [2][GH][C] (one chunk) or [2][GH][2C] (a pair of chunks).
+  FZ_DEV float* sc() const { return reinterpret_cast<float*>(ks(NB)); }
+  FZ_DEV uint16_t* ph() const { return reinterpret_cast<uint16_t*>(sc() + 2 * GH * 2 * C); }  // [8][PS] weights
   FZ_DEV float* hstat() const { return reinterpret_cast<float*>(ph() + 8 * PS); }           // [GH] corr or m, [GH] l
   // Byte offset of (key r, dimensions d .. d + 7) in a K or V half-buffer:
   // box d / 64, row r of 128 bytes, 16-byte unit (d / 8) % 8 XOR r % 8.
@@ -1299,6 +1300,131 @@ struct Attn {
     wrote = false;
 #pragma unroll 1
     for (uint32_t jc = j0, b = 0; jc < j1; jc += C, b = b + 1 == (uint32_t)NB ? 0u : b + 1) {
+      // The split's last two chunks in one pass (both staged: the second's
+      // copies were issued when the chunk before the first was read): one
+      // round of barriers, one softmax step and one P V for 64 keys.
+      if (NB >= 2 && jc + C < j1 && j1 - jc <= 2u * C) {
+        const uint32_t b2 = b + 1 == (uint32_t)NB ? 0u : b + 1, jc2 = jc + C;
+        const uint32_t lo0 = earliest > jc ? earliest - jc : 0u, lo1 = earliest > jc2 ? earliest - jc2 : 0u;
+        const uint32_t n1 = j1 - jc2;   // the second chunk's keys (the first is whole)
+        wait_chunk(b);
+        wait_chunk(b2);
+        if (pos >= jc && pos < j1 && (warp == GH || warp == GH + 1)) {
+          const bool second = pos >= jc2;
+          const uint32_t r = pos - (second ? jc2 : jc), d = 4u * (uint32_t)lane;
+          unsigned char* half = warp == GH ? ks(second ? b2 : b) : vs(second ? b2 : b);
+          *reinterpret_cast<ushort4*>(half + at(r, d) + (d & 7u) * 2u) =
+              make_ushort4(f16_pack(va.x), f16_pack(va.y), f16_pack(va.z), f16_pack(va.w));
+          *reinterpret_cast<ushort4*>(half + at(r, d + kHd / 2) + (d & 7u) * 2u) =
+              make_ushort4(f16_pack(vb.x), f16_pack(vb.y), f16_pack(vb.z), f16_pack(vb.w));
+          wrote = true;
+        }
+        if (cbar_or(fail)) {
+          dead = true;
+          break;
+        }
+        // Scores: warp w takes keys 8 (w % 4) .. + 7 of each chunk over
+        // dimensions 128 (w / 4) .. + 127, as in the one-chunk pass.
+        {
+          const int nt = warp & 3, kh = warp >> 2;
+          const uint16_t* qrow = qh() + g * QS + 2 * t + 128 * kh;
+          const uint32_t key = 8 * nt + (lane & 7), d0 = 128 * kh + 8 * (lane >> 3);
+#pragma unroll 1
+          for (int cc = 0; cc < 2; cc++) {
+            const unsigned char* kb = ks(cc ? b2 : b);
+            uint32_t af[4][2][4], kr[4][4];
+            const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kp = 0; kp < 4; kp++) {
+              af[kp][0][0] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp);
+              af[kp][0][2] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 8);
+              af[kp][1][0] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 16);
+              af[kp][1][2] = *reinterpret_cast<const uint32_t*>(qrow + 32 * kp + 24);
+              af[kp][0][1] = af[kp][0][3] = af[kp][1][1] = af[kp][1][3] = 0u;
+              asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(kr[kp][0]), "=r"(kr[kp][1]), "=r"(kr[kp][2]), "=r"(kr[kp][3])
+                           : "r"(su32(kb + at(key, d0 + 32 * kp))));
+            }
+            float dk[4][4];
+#pragma unroll
+            for (int kp = 0; kp < 4; kp++) mma16816(dk[kp], af[kp][0], make_uint2(kr[kp][0], kr[kp][1]), zero);
+#pragma unroll
+            for (int kp = 0; kp < 4; kp++) mma16816(dk[kp], af[kp][1], make_uint2(kr[kp][2], kr[kp][3]), dk[kp]);
+            float d[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) d[e] = add(add(dk[0][e], dk[1][e]), add(dk[2][e], dk[3][e]));
+            const float r0 = __shfl_down_sync(0xffffffffu, d[0], 4 * GH);
+            const float r1 = __shfl_down_sync(0xffffffffu, d[1], 4 * GH);
+            if (g < GH) {
+              float* dst = sc() + (kh * GH + g) * (2 * C) + C * cc + 8 * nt + 2 * t;
+              dst[0] = add(d[0], r0);
+              dst[1] = add(d[1], r1);
+            }
+          }
+        }
+        cbar();
+        // Online softmax: warp h takes head h (lane l: key l of each chunk).
+        if (warp < GH) {
+          const bool ok0 = (uint32_t)lane >= lo0;
+          const bool ok1 = (uint32_t)lane >= lo1 && (uint32_t)lane < n1;
+          const float* sa = sc() + warp * (2 * C);
+          const float* sb2 = sc() + (GH + warp) * (2 * C);
+          const float s0 = ok0 ? add(sa[lane], sb2[lane]) : -INFINITY;
+          const float s1 = ok1 ? add(sa[C + lane], sb2[C + lane]) : -INFINITY;
+          const float mx = fmaxf(m_h, warp_max(fmaxf(s0, s1)));
+          const float corr = exp2f(m_h - mx);
+          const float e0 = ok0 ? exp2f(s0 - mx) : 0.f, e1 = ok1 ? exp2f(s1 - mx) : 0.f;
+          l_h = __fmaf_rn(l_h, corr, warp_sum(add(e0, e1)));
+          m_h = mx;
+          uint32_t hw, lw;
+          split2(e0, e1, hw, lw);
+          ph()[warp * PS + lane] = (uint16_t)(hw & 0xffffu);
+          ph()[warp * PS + C + lane] = (uint16_t)(hw >> 16);
+          ph()[(GH + warp) * PS + lane] = (uint16_t)(lw & 0xffffu);
+          ph()[(GH + warp) * PS + C + lane] = (uint16_t)(lw >> 16);
+          if (lane == 0) hstat()[warp] = corr;
+        }
+        cbar();
+        // Values: warp w takes dimensions 32 w .. 32 w + 31 (four n-tiles),
+        // four k-steps, two from each chunk's ldmatrix.x4.trans.
+        {
+          const float corr = g < 2 * GH ? hstat()[g < GH ? g : g - GH] : 0.f;
+          uint32_t af[4][4];
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            af[k][0] = *reinterpret_cast<const uint32_t*>(ph() + g * PS + 16 * k + 2 * t);
+            af[k][1] = 0u;
+            af[k][2] = *reinterpret_cast<const uint32_t*>(ph() + g * PS + 16 * k + 8 + 2 * t);
+            af[k][3] = 0u;
+          }
+#pragma unroll
+          for (int cc = 0; cc < 2; cc++) {
+            uint32_t vr[4][4];
+            float d[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              const uint32_t nt = 4 * warp + i;
+              asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(vr[i][0]), "=r"(vr[i][1]), "=r"(vr[i][2]), "=r"(vr[i][3])
+                           : "r"(su32(vs(cc ? b2 : b) + at((uint32_t)lane, nt * 8))));
+              d[i][0] = cc ? acc[i][0] : mul(acc[i][0], corr);
+              d[i][1] = cc ? acc[i][1] : mul(acc[i][1], corr);
+              d[i][2] = d[i][3] = 0.f;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) mma16816(d[i], af[2 * cc], make_uint2(vr[i][0], vr[i][1]), d[i]);
+#pragma unroll
+            for (int i = 0; i < 4; i++) mma16816(d[i], af[2 * cc + 1], make_uint2(vr[i][2], vr[i][3]), d[i]);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+              acc[i][0] = d[i][0];
+              acc[i][1] = d[i][1];
+            }
+          }
+        }
+        cbar();
+        break;
+      }
       // Keys lo .. n - 1 of the chunk are the split's.
       const uint32_t n = min((uint32_t)C, j1 - jc), lo = earliest > jc ? earliest - jc : 0u;
       // Chunk's copies (the next chunks' may still be in flight).
